@@ -1,0 +1,684 @@
+// Flash attention for sm_100a on tcgen05 tensor cores (head_dim 128, bf16).
+//
+// Replaces the SDPA call of avgen/models/attention.py:227-273 (self-attention of
+// every DiT block and cross-attention to the text tokens) with hand-written
+// Blackwell kernels. Bidirectional, optional key-padding mask (packed bits),
+// grouped-query attention (H query heads over Hk key/value heads).
+//
+// Forward (one CTA = one (batch, head) and 256 query rows = two 128-row tiles):
+//   warp 0      TMA: Q tiles once, then K/V blocks of 128 keys into a 2-stage ring
+//   warp 1      MMA: S_g = Q_g K^T into TMEM; O_g += P_g V with P read from TMEM
+//   warps 4..11 two softmax warpgroups, one per query tile; thread = query row
+// The two tiles ping-pong on the tensor core (S of one tile is computed while
+// the other tile's softmax runs). P overwrites S in place (bf16 packed two per
+// 32-bit column). The running max is only moved when it grows by more than 8
+// (log2 units); O in TMEM is rescaled only then, after the pending PV finished.
+// Scores use the base-2 domain: s2 = (q.k) * scale * log2(e), lse2 = m + log2(l).
+//
+// Backward (one CTA = one (batch, kv head) and 128 keys, looping over query
+// blocks of every query head that reads this kv head):
+//   S^T = K Q^T and dP^T = V dO^T into TMEM; one warpgroup (thread = key row)
+//   forms P^T = exp2(s2 - lse2) and dS^T = P^T (dP^T - delta); dV += P^T dO and
+//   dK += dS^T Q read P^T / dS^T from TMEM; dQ = dS K reads dS from shared
+//   memory and is flushed to an fp32 accumulator with vector atomics.
+#include <algorithm>
+#include <cfloat>
+
+#include "include/host_utils.h"
+#include "include/launchers.h"
+#include "include/sm100.cuh"
+
+namespace avgen {
+namespace {
+
+constexpr int kHD = 128;
+constexpr int kTile = 128;
+constexpr float kNegBig = -1.0e30f;
+constexpr float kRescaleThreshold = 8.0f;
+
+__device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
+  return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~static_cast<uintptr_t>(1023));
+}
+
+// K-major SW128 descriptor for a 128-row x 128-element tile stored as two
+// 64-element column chunks of 16 KB; k-step kk (16 elements) of 8.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int kk) {
+  return umma_desc_sw128(tile + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024);
+}
+// The same tile read MN-major (rows are the reduction axis): k-step kk covers
+// rows 16kk..16kk+15; the two 64-element MN chunks are 16 KB apart.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int kk) {
+  return umma_desc_sw128(tile + kk * 2048, 16384, 1024);
+}
+
+// =========================================================================== forward
+struct FwdSmem {
+  static constexpr int Q = 0;            // 2 tiles x 32 KB
+  static constexpr int KV = 65536;       // 2 stages x (K 32 KB + V 32 KB)
+  static constexpr int BARS = 65536 + 131072;
+  static constexpr int BYTES = BARS + 256 + 1024;
+};
+
+__global__ void __launch_bounds__(384, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const AttnFwdDesc p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + FwdSmem::BARS);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;
+  uint64_t* kv_empty = bars + 3;
+  uint64_t* s_full = bars + 5;
+  uint64_t* p_full = bars + 7;
+  uint64_t* o_done = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 11);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int qt = blockIdx.x % p.q_tiles;
+  const int bh = blockIdx.x / p.q_tiles;
+  const int h = bh % p.H;
+  const int b = bh / p.H;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qt * 256;
+  const int nkv = (p.Lk + kTile - 1) / kTile;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_done[s], 1);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_arrive_expect_tx(q_full, 65536);
+      for (int g = 0; g < 2; ++g)
+        for (int c = 0; c < 2; ++c)
+          tma_load_3d(smem + FwdSmem::Q + g * 32768 + c * 16384, &tmQ, q_full, c * 64, q0 + g * 128,
+                      b * p.H + h);
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&kv_full[s], 65536);
+        uint8_t* st = smem + FwdSmem::KV + s * 65536;
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(st + c * 16384, &tmK, &kv_full[s], c * 64, j * kTile, b * p.Hk + hk);
+          tma_load_3d(st + 32768 + c * 16384, &tmV, &kv_full[s], c * 64, j * kTile, b * p.Hk + hk);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    const uint32_t idS = idesc_bf16_f32(128, 128, false, false);
+    const uint32_t idO = idesc_bf16_f32(128, 128, false, true);
+    const uint32_t sQ = smem_u32(smem + FwdSmem::Q);
+    const uint32_t sKV = smem_u32(smem + FwdSmem::KV);
+    auto issue_S = [&](int g, int s) {
+      const uint32_t qa = sQ + g * 32768;
+      const uint32_t ka = sKV + s * 65536;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_bf16_ss(tmem + g * 128, kmajor_desc(qa, kk), kmajor_desc(ka, kk), idS, kk > 0 ? 1u : 0u);
+    };
+    auto issue_PV = [&](int g, int s, bool acc) {
+      const uint32_t va = sKV + s * 65536 + 32768;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_bf16_ts(tmem + 256 + g * 128, tmem + g * 128 + kk * 8, mnmajor_desc(va, kk), idO,
+                    (acc || kk > 0) ? 1u : 0u);
+    };
+    bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutMma) &&
+              mbar_wait(&kv_full[0], 0, abort_flag, p.err, kErrTimeoutMma);
+    if (ok) {
+      tc_fence_after();
+      if (lane == 0) {
+        issue_S(0, 0);
+        mma_commit(&s_full[0]);
+        issue_S(1, 0);
+        mma_commit(&s_full[1]);
+      }
+      __syncwarp();
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j & 1;
+        const int s2 = (j + 1) & 1;
+        if (!mbar_wait(&p_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          issue_PV(0, s, j > 0);
+          mma_commit(&o_done[0]);
+        }
+        __syncwarp();
+        const bool more = j + 1 < nkv;
+        if (more) {
+          if (!mbar_wait(&kv_full[s2], ((j + 1) >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+          tc_fence_after();
+          if (lane == 0) {
+            issue_S(0, s2);
+            mma_commit(&s_full[0]);
+          }
+          __syncwarp();
+        }
+        if (!mbar_wait(&p_full[1], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          issue_PV(1, s, j > 0);
+          mma_commit(&o_done[1]);
+          mma_commit(&kv_empty[s]);
+          if (more) {
+            issue_S(1, s2);
+            mma_commit(&s_full[1]);
+          }
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ softmax
+    const int g = (warp - 4) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int q = q0 + g * 128 + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_base + g * 128;
+    const uint32_t tO = tmem + lane_base + 256 + g * 128;
+    const float sl = p.scale_log2;
+    float m = kNegBig;
+    float l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait(&s_full[g], j & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]);
+        tmem_ld32(tS + 32 * c, chunk);
+      }
+      tmem_wait_ld();
+      const int kbase = j * kTile;
+      if (kbase + kTile > p.Lk || p.kmask != nullptr) {
+        uint32_t words[4];
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          const int key0 = kbase + 32 * w;
+          uint32_t bits = 0xffffffffu;
+          if (p.kmask != nullptr && key0 < p.Lk) bits = p.kmask[static_cast<long>(b) * p.kmask_words + (key0 >> 5)];
+          const int left = p.Lk - key0;
+          if (left < 32) bits &= (left <= 0) ? 0u : ((1u << left) - 1u);
+          words[w] = bits;
+        }
+#pragma unroll
+        for (int c = 0; c < 128; ++c)
+          if (!((words[c >> 5] >> (c & 31)) & 1u)) sr[c] = __float_as_uint(-INFINITY);
+      }
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
+      const float m_new = fmaxf(m, mx * sl);
+      if (j == 0) {
+        m = m_new;
+      } else {
+        const bool need = m_new > m + kRescaleThreshold;
+        if (__any_sync(0xffffffffu, need)) {
+          if (!mbar_wait(&o_done[g], (j - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float f = need ? fast_exp2(m - m_new) : 1.f;
+          if (need) {
+            l *= f;
+            m = m_new;
+          }
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + 32 * c, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+            tmem_st32(tO + 32 * c, o);
+          }
+          tmem_wait_st();
+        }
+      }
+      float sum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; ++c) {
+        const float p0 = fast_exp2(fmaf(__uint_as_float(sr[2 * c]), sl, -m));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(sr[2 * c + 1]), sl, -m));
+        sum += p0 + p1;
+        sr[c] = pack_bf16(p0, p1);
+      }
+      l += sum;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint32_t (&chunk)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&sr[16 * c]);
+        tmem_st16(tS + 16 * c, chunk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&p_full[g]);
+    }
+    if (ok && mbar_wait(&o_done[g], (nkv - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* dst = p.out + static_cast<long>(b) * p.o_sb + static_cast<long>(q) * p.o_sl +
+                           static_cast<long>(h) * p.o_sh;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + 32 * c, o);
+        tmem_wait_ld();
+        if (q < p.Lq) {
+          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+            w.y = pack_bf16(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+            w.z = pack_bf16(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+            w.w = pack_bf16(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+            d4[v] = w;
+          }
+        }
+      }
+      if (q < p.Lq && p.lse != nullptr)
+        p.lse[(static_cast<long>(b) * p.H + h) * p.Lq + q] = l > 0.f ? m + __log2f(l) : -INFINITY;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// =========================================================================== backward
+// delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]; one warp per (b, q, h) row.
+__global__ void attn_bwd_delta_kernel(const __nv_bfloat16* o, const __nv_bfloat16* dout, float* delta,
+                                      int B, int H, int L, long sb, long sl, long sh) {
+  const long rows = static_cast<long>(B) * H * L;
+  const int lane = threadIdx.x & 31;
+  for (long r = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
+       r += static_cast<long>(gridDim.x) * (blockDim.x >> 5)) {
+    const long q = r % L;
+    const long bh = r / L;
+    const long h = bh % H;
+    const long b = bh / H;
+    const long off = b * sb + q * sl + h * sh + lane * 4;
+    const uint2 a = *reinterpret_cast<const uint2*>(o + off);
+    const uint2 c = *reinterpret_cast<const uint2*>(dout + off);
+    float s = bf16_lo(a.x) * bf16_lo(c.x) + bf16_hi(a.x) * bf16_hi(c.x) + bf16_lo(a.y) * bf16_lo(c.y) +
+              bf16_hi(a.y) * bf16_hi(c.y);
+#pragma unroll
+    for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
+    if (lane == 0) delta[r] = s;
+  }
+}
+
+struct BwdSmem {
+  static constexpr int K = 0;                // 32 KB
+  static constexpr int V = 32768;            // 32 KB
+  static constexpr int STAGE = 65536;        // 2 stages x (Q 32 KB, dO 32 KB, lse 512 B, delta 512 B)
+  static constexpr int STAGE_BYTES = 65536 + 1024;
+  static constexpr int DS = STAGE + 2 * STAGE_BYTES;  // 32 KB dS tile (MN-major, SW128)
+  static constexpr int BARS = DS + 32768;
+  static constexpr int BYTES = BARS + 256;
+};
+
+__global__ void __launch_bounds__(256, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                    const __grid_constant__ CUtensorMap tmLse, const __grid_constant__ CUtensorMap tmDelta,
+                    const AttnBwdDesc p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BwdSmem::BARS);
+  uint64_t* kv_full = bars;        // 1
+  uint64_t* st_full = bars + 1;    // 2
+  uint64_t* st_empty = bars + 3;   // 2
+  uint64_t* sdp_full = bars + 5;   // 1
+  uint64_t* p_full = bars + 6;     // 1 (128 arrivals)
+  uint64_t* dq_full = bars + 7;    // 1
+  uint64_t* dq_free = bars + 8;    // 1 (128 arrivals)
+  uint64_t* acc_done = bars + 9;   // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int kt = blockIdx.x % p.k_tiles;
+  const int bhk = blockIdx.x / p.k_tiles;
+  const int hk = bhk % p.Hk;
+  const int b = bhk / p.Hk;
+  const int k0 = kt * kTile;
+  const int group = p.H / p.Hk;
+  const int nq = (p.Lq + kTile - 1) / kTile;
+  const int iters = nq * group;
+
+  if (threadIdx.x == 0) {
+    if ((smem_u32(smem) & 1023u) != 0) record_error(p.err, kErrBadArgument);
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&st_full[s], 1);
+      mbar_init(&st_empty[s], 1);
+    }
+    mbar_init(sdp_full, 1);
+    mbar_init(p_full, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(acc_done, 1);
+    *abort_flag = (smem_u32(smem) & 1023u) != 0 ? 1 : 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  // TMEM columns: [0,128) S^T then dQ, [128,256) dP^T, [256,384) dV, [384,512) dK
+  const uint32_t tS = tmem, tP = tmem + 128, tDV = tmem + 256, tDK = tmem + 384;
+
+  if (warp == 0) {
+    if (lane == 0 && !*abort_flag) {
+      mbar_arrive_expect_tx(kv_full, 65536);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_3d(smem + BwdSmem::K + c * 16384, &tmK, kv_full, c * 64, k0, b * p.Hk + hk);
+        tma_load_3d(smem + BwdSmem::V + c * 16384, &tmV, kv_full, c * 64, k0, b * p.Hk + hk);
+      }
+      for (int i = 0; i < iters; ++i) {
+        const int s = i & 1;
+        const int h = hk * group + i / nq;
+        const int qb = (i % nq) * kTile;
+        if (!mbar_wait(&st_empty[s], ((i >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        uint8_t* st = smem + BwdSmem::STAGE + s * BwdSmem::STAGE_BYTES;
+        mbar_arrive_expect_tx(&st_full[s], 65536 + 1024);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(st + c * 16384, &tmQ, &st_full[s], c * 64, qb, b * p.H + h);
+          tma_load_4d(st + 32768 + c * 16384, &tmdO, &st_full[s], c * 64, h, qb, b);
+        }
+        tma_load_2d(st + 65536, &tmLse, &st_full[s], qb, b * p.H + h);
+        tma_load_2d(st + 65536 + 512, &tmDelta, &st_full[s], qb, b * p.H + h);
+      }
+    }
+  } else if (warp == 1) {
+    const uint32_t idT = idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
+    const uint32_t idA = idesc_bf16_f32(128, 128, false, true);   // dV, dK (A from TMEM)
+    const uint32_t idQ = idesc_bf16_f32(128, 128, true, true);    // dQ = dS K
+    const uint32_t sK = smem_u32(smem + BwdSmem::K);
+    const uint32_t sV = smem_u32(smem + BwdSmem::V);
+    const uint32_t sDS = smem_u32(smem + BwdSmem::DS);
+    bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
+    for (int i = 0; i < iters && ok; ++i) {
+      const int s = i & 1;
+      const uint32_t sQ = smem_u32(smem + BwdSmem::STAGE + s * BwdSmem::STAGE_BYTES);
+      const uint32_t sdO = sQ + 32768;
+      if (!mbar_wait(&st_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+      if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+      tc_fence_after();
+      if (lane == 0) {
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_bf16_ss(tS, kmajor_desc(sK, kk), kmajor_desc(sQ, kk), idT, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          mma_bf16_ss(tP, kmajor_desc(sV, kk), kmajor_desc(sdO, kk), idT, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(sdp_full);
+      }
+      __syncwarp();
+      if (!mbar_wait(p_full, i & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        // dV += P^T dO ; dK += dS^T Q   (A from TMEM, B = MN-major views of dO / Q)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ts(tDV, tS + kk * 8, mnmajor_desc(sdO, kk), idA, (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ts(tDK, tP + kk * 8, mnmajor_desc(sQ, kk), idA, (i > 0 || kk > 0) ? 1u : 0u);
+        // dQ = dS K : A = dS (smem, MN-major: q contiguous), B = K viewed MN-major
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_bf16_ss(tS, mnmajor_desc(sDS, kk), mnmajor_desc(sK, kk), idQ, kk > 0 ? 1u : 0u);
+        mma_commit(dq_full);
+        mma_commit(&st_empty[s]);
+        if (i == iters - 1) mma_commit(acc_done);
+      }
+      __syncwarp();
+    }
+  } else if (warp >= 4) {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;  // key row for S^T / dP^T / dK / dV; query row for dQ
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl = p.scale_log2;
+    const int key = k0 + row;
+    bool key_ok = key < p.Lk;
+    if (key_ok && p.kmask != nullptr)
+      key_ok = (p.kmask[static_cast<long>(b) * p.kmask_words + (key >> 5)] >> (key & 31)) & 1u;
+    uint8_t* ds_tile = smem + BwdSmem::DS;
+    bool ok = true;
+    for (int i = 0; i < iters; ++i) {
+      const int s = i & 1;
+      const int h = hk * group + i / nq;
+      const int qb = (i % nq) * kTile;
+      const float* lse = reinterpret_cast<const float*>(smem + BwdSmem::STAGE + s * BwdSmem::STAGE_BYTES + 65536);
+      const float* dlt = lse + 128;
+      if (!mbar_wait(sdp_full, i & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      // Process 32 query columns at a time: P^T, dS^T into TMEM (bf16 packed) and dS into smem.
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + lane_base + 32 * c, sv);
+        tmem_ld32(tP + lane_base + 32 * c, dv);
+        tmem_wait_ld();
+        uint32_t pp[16], dd[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int qa = 32 * c + 2 * e;
+          float p0 = 0.f, p1 = 0.f;
+          if (key_ok) {
+            const float l0 = lse[qa], l1 = lse[qa + 1];
+            p0 = (qb + qa < p.Lq && l0 != -INFINITY) ? fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -l0)) : 0.f;
+            p1 = (qb + qa + 1 < p.Lq && l1 != -INFINITY) ? fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -l1)) : 0.f;
+          }
+          const float d0 = p0 * (__uint_as_float(dv[2 * e]) - dlt[qa]);
+          const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - dlt[qa + 1]);
+          pp[e] = pack_bf16(p0, p1);
+          dd[e] = pack_bf16(d0, d1);
+        }
+        tmem_st16(tS + lane_base + 16 * c, pp);
+        tmem_st16(tP + lane_base + 16 * c, dd);
+        // dS tile, MN-major (q contiguous): chunk = q / 64, key row `row` at 128 B,
+        // 16-byte unit u (8 queries) stored at unit u ^ (row & 7).
+        const int chunk = c >> 1;
+        const int unit0 = (c & 1) * 4;
+        uint8_t* rowp = ds_tile + chunk * 16384 + row * 128;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int unit = (unit0 + u) ^ (row & 7);
+          *reinterpret_cast<uint4*>(rowp + unit * 16) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
+        }
+      }
+      tmem_wait_st();
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(p_full);
+      // dQ readout: TMEM lane = query row of this block.
+      if (!mbar_wait(dq_full, i & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      const int q = qb + row;
+      float* dq = p.dq_acc + ((static_cast<long>(b) * p.H + h) * p.Lq + q) * kHD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS + lane_base + 32 * c, v);
+        tmem_wait_ld();
+        if (q < p.Lq) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            atomicAdd(reinterpret_cast<float4*>(dq + 32 * c) + e,
+                      make_float4(__uint_as_float(v[4 * e]) * p.scale, __uint_as_float(v[4 * e + 1]) * p.scale,
+                                  __uint_as_float(v[4 * e + 2]) * p.scale, __uint_as_float(v[4 * e + 3]) * p.scale));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    if (ok && mbar_wait(acc_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
+      tc_fence_after();
+      if (key < p.Lk) {
+        __nv_bfloat16* dk = p.dk + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+        __nv_bfloat16* dv = p.dv + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t a[32], d[32];
+          tmem_ld32(tDK + lane_base + 32 * c, a);
+          tmem_ld32(tDV + lane_base + 32 * c, d);
+          tmem_wait_ld();
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 wk, wv;
+            wk.x = pack_bf16(__uint_as_float(a[8 * v + 0]) * p.scale, __uint_as_float(a[8 * v + 1]) * p.scale);
+            wk.y = pack_bf16(__uint_as_float(a[8 * v + 2]) * p.scale, __uint_as_float(a[8 * v + 3]) * p.scale);
+            wk.z = pack_bf16(__uint_as_float(a[8 * v + 4]) * p.scale, __uint_as_float(a[8 * v + 5]) * p.scale);
+            wk.w = pack_bf16(__uint_as_float(a[8 * v + 6]) * p.scale, __uint_as_float(a[8 * v + 7]) * p.scale);
+            wv.x = pack_bf16(__uint_as_float(d[8 * v + 0]), __uint_as_float(d[8 * v + 1]));
+            wv.y = pack_bf16(__uint_as_float(d[8 * v + 2]), __uint_as_float(d[8 * v + 3]));
+            wv.z = pack_bf16(__uint_as_float(d[8 * v + 4]), __uint_as_float(d[8 * v + 5]));
+            wv.w = pack_bf16(__uint_as_float(d[8 * v + 6]), __uint_as_float(d[8 * v + 7]));
+            reinterpret_cast<uint4*>(dk + 32 * c)[v] = wk;
+            reinterpret_cast<uint4*>(dv + 32 * c)[v] = wv;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+}  // namespace
+
+void attn_fwd_launch(const AttnFwdDesc& d_in, cudaStream_t stream) {
+  AttnFwdDesc d = d_in;
+  AVGEN_CHECK(d.D == kHD, "attention: head_dim must be 128, got ", d.D);
+  AVGEN_CHECK(d.H % d.Hk == 0, "attention: H must be a multiple of Hk");
+  if (d.B == 0 || d.Lq == 0) return;
+  d.q_tiles = (d.Lq + 255) / 256;
+  // Q, K, V head-major [B*H, L, D] with rows of D elements.
+  const CUtensorMap tq = make_tmap_3d_bf16(d.q, kHD, d.Lq, static_cast<long>(d.B) * d.H, kHD,
+                                           static_cast<long>(d.Lq) * kHD, 64, 128, 1);
+  const CUtensorMap tk = make_tmap_3d_bf16(d.k, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
+                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
+  const CUtensorMap tv = make_tmap_3d_bf16(d.v, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
+                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
+  static bool attr = false;
+  if (!attr) {
+    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          FwdSmem::BYTES));
+    attr = true;
+  }
+  const long grid = static_cast<long>(d.B) * d.H * d.q_tiles;
+  attn_fwd_kernel<<<grid, 384, FwdSmem::BYTES, stream>>>(tq, tk, tv, d);
+  AVGEN_CUDA_CHECK(cudaGetLastError());
+}
+
+void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
+  AttnBwdDesc d = d_in;
+  AVGEN_CHECK(d.D == kHD, "attention bwd: head_dim must be 128");
+  if (d.B == 0 || d.Lk == 0) return;
+  d.k_tiles = (d.Lk + kTile - 1) / kTile;
+  // delta = rowsum(dO * O)
+  {
+    const long rows = static_cast<long>(d.B) * d.H * d.Lq;
+    const long blocks = std::min<long>((rows + 7) / 8, 16L * num_sms(d.device));
+    attn_bwd_delta_kernel<<<blocks, 256, 0, stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(d.o), reinterpret_cast<const __nv_bfloat16*>(d.dout),
+        d.delta, d.B, d.H, d.Lq, d.o_sb, d.o_sl, d.o_sh);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
+  }
+  const CUtensorMap tq = make_tmap_3d_bf16(d.q, kHD, d.Lq, static_cast<long>(d.B) * d.H, kHD,
+                                           static_cast<long>(d.Lq) * kHD, 64, 128, 1);
+  const CUtensorMap tk = make_tmap_3d_bf16(d.k, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
+                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
+  const CUtensorMap tv = make_tmap_3d_bf16(d.v, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
+                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
+  // O / dO must be dense token-major [B, L, H, D].
+  AVGEN_CHECK(d.o_sh == kHD && d.o_sl == static_cast<long>(d.H) * kHD && d.o_sb == static_cast<long>(d.Lq) * d.H * kHD,
+              "attention bwd: dO / O must be dense [B, L, H, 128]");
+  auto f32_rows = [&](const float* ptr) {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(d.B) * d.H};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.Lq) * 4};
+    cuuint32_t box[2] = {128, 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: row-stat tensor map failed (", static_cast<int>(r), ")");
+    return m;
+  };
+  AVGEN_CHECK(d.Lq % 4 == 0, "attention bwd: Lq must be a multiple of 4");
+  const CUtensorMap tl = f32_rows(d.lse);
+  const CUtensorMap tdl = f32_rows(d.delta);
+  // dO token-major dense [B, L, H, D]: 4-D map (d, h, l, b), box (64, 1, 128, 1).
+  CUtensorMap tdo3;
+  {
+    cuuint64_t dims[4] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(d.H),
+                          static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(d.B)};
+    cuuint64_t strides[3] = {static_cast<cuuint64_t>(kHD) * 2, static_cast<cuuint64_t>(d.H) * kHD * 2,
+                             static_cast<cuuint64_t>(d.Lq) * d.H * kHD * 2};
+    cuuint32_t box[4] = {64, 1, 128, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = tensor_map_encoder()(&tdo3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(d.dout), dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: dO tensor map failed (", static_cast<int>(r), ")");
+  }
+  static bool attr = false;
+  if (!attr) {
+    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          BwdSmem::BYTES));
+    attr = true;
+  }
+  const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
+  attn_bwd_kernel<<<grid, 256, BwdSmem::BYTES, stream>>>(tq, tk, tv, tdo3, tl, tdl, d);
+  AVGEN_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace avgen

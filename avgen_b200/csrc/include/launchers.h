@@ -1,0 +1,233 @@
+// Torch-free launcher interfaces of the avgen_b200 kernels. The .cu files
+// implement them; bindings.cpp validates torch tensors and calls them.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace avgen {
+
+enum GemmEpilogue : int {
+  kEpiStore = 0,
+  kEpiGateResid = 1,
+  kEpiSwiGLU = 2,
+  kEpiGelu = 3,
+  kEpiAtomicF32 = 4,
+};
+
+struct GemmDesc {
+  int device = 0;
+  int M = 0, N = 0, K = 0;
+  const void* a = nullptr;  // bf16, [M, K] (a_mn=false) or [K, M] (a_mn=true)
+  long lda = 0;
+  bool a_mn = false;
+  const void* b = nullptr;  // bf16, [N, K] (b_mn=false) or [K, N] (b_mn=true)
+  long ldb = 0;
+  bool b_mn = false;
+  void* out = nullptr;
+  long ldo = 0;
+  bool out_f32 = false;
+  int epilogue = kEpiStore;
+  const float* bias = nullptr;
+  const void* resid = nullptr;  // bf16 [M, N]
+  long ldr = 0;
+  const float* gate = nullptr;  // fp32 [B, gate_stride]
+  long gate_stride = 0;
+  int rows_per_batch = 1;
+  void* aux = nullptr;  // bf16 [M, N]
+  long ldaux = 0;
+  int k_splits = 1;
+  int* err = nullptr;
+};
+
+void gemm_launch(const GemmDesc& d, cudaStream_t stream);
+
+// adaLN RMSNorm. y = rmsnorm(x) * w * (1 + scale[b]) + shift[b] (each optional).
+struct NormDesc {
+  int device = 0;
+  long rows = 0;
+  int W = 0;
+  long rows_per_batch = 1;
+  float eps = 1e-6f;
+  const void* x = nullptr;  // bf16 [rows, W]
+  long ldx = 0;
+  void* y = nullptr;  // bf16 [rows, W]
+  long ldy = 0;
+  float* rstd = nullptr;  // fp32 [rows]
+  const float* w = nullptr;
+  const float* scale = nullptr;  // fp32 [B, mod_stride]
+  const float* shift = nullptr;
+  long mod_stride = 0;
+  // backward
+  const void* dy = nullptr;
+  long lddy = 0;
+  void* dx = nullptr;
+  long lddx = 0;
+  const void* dres = nullptr;  // optional incoming residual gradient added to dx
+  long lddres = 0;
+  float* dw = nullptr;
+  float* dscale = nullptr;
+  float* dshift = nullptr;
+  long dmod_stride = 0;
+};
+void rmsnorm_mod_fwd_launch(const NormDesc& d, cudaStream_t stream);
+void rmsnorm_mod_bwd_launch(const NormDesc& d, cudaStream_t stream);
+
+struct GateBwdDesc {
+  int device = 0;
+  long rows = 0;
+  int W = 0;
+  long rows_per_batch = 1;
+  const void* dx = nullptr;  // bf16 [rows, W]
+  long lddx = 0;
+  const void* a = nullptr;  // bf16 [rows, W], the un-gated branch output
+  long lda = 0;
+  const float* gate = nullptr;  // fp32 [B, gate_stride]
+  long gate_stride = 0;
+  void* da = nullptr;  // bf16 [rows, W]
+  long ldda = 0;
+  float* dgate = nullptr;  // fp32 [B, dgate_stride], accumulated
+  long dgate_stride = 0;
+};
+void gate_bwd_launch(const GateBwdDesc& d, cudaStream_t stream);
+
+// QK-RMSNorm + 3-D RoPE + head-major relayout of a fused QKV projection.
+struct QkvRopeDesc {
+  int device = 0;
+  int B = 0, L = 0, H = 0, Hk = 0, D = 0;
+  float eps = 1e-6f;
+  const void* qkv = nullptr;  // bf16 [B*L, (H + 2Hk) * D]
+  long ldqkv = 0;
+  const float* q_w = nullptr;  // fp32 [D] or null (no QK norm)
+  const float* k_w = nullptr;
+  const float* coords = nullptr;  // fp32 [B*L, 3] or null (no rotary)
+  const float* freq = nullptr;    // fp32 [D/2]
+  const int* axis = nullptr;      // int32 [D/2]
+  void* q = nullptr;  // bf16 [B, H, L, D]
+  void* k = nullptr;  // bf16 [B, Hk, L, D]
+  void* v = nullptr;  // bf16 [B, Hk, L, D]
+  // backward
+  const void* dq = nullptr;
+  const void* dk = nullptr;
+  const void* dv = nullptr;
+  void* dqkv = nullptr;  // bf16 [B*L, (H + 2Hk) * D]
+  long lddqkv = 0;
+  float* dq_w = nullptr;
+  float* dk_w = nullptr;
+};
+void qkv_rope_fwd_launch(const QkvRopeDesc& d, cudaStream_t stream);
+void qkv_rope_bwd_launch(const QkvRopeDesc& d, cudaStream_t stream);
+
+// Elementwise activations.
+void swiglu_bwd_launch(int device, long rows, int F, const void* dh, long lddh, const void* gu,
+                       long ldgu, void* dgu, long lddgu, cudaStream_t stream);
+void gelu_bwd_launch(int device, long rows, int F, const void* dh, long lddh, const void* pre,
+                     long ldpre, void* dpre, long lddpre, cudaStream_t stream);
+
+// Flow-matching loss partials: stats[0] += sum(w_b * mse_tok * m), stats[1] += sum(mse_tok * m),
+// stats[2] += sum(m) with mse_tok the mean over the P features of (pred - target)^2.
+struct FlowLossDesc {
+  int device = 0;
+  long rows = 0;
+  int P = 0;
+  long rows_per_batch = 1;
+  const void* pred = nullptr;
+  bool pred_f32 = false;
+  const void* target = nullptr;
+  bool target_f32 = true;
+  const uint8_t* mask = nullptr;  // [rows] loss mask
+  const float* weight = nullptr;  // [B]
+  float* stats = nullptr;         // [3]
+  // backward: dpred = scale[0] * 2 (pred - target) / P * w_b * m
+  const float* scale = nullptr;
+  void* dpred = nullptr;
+  bool dpred_f32 = false;
+};
+void flow_loss_fwd_launch(const FlowLossDesc& d, cudaStream_t stream);
+void flow_loss_bwd_launch(const FlowLossDesc& d, cudaStream_t stream);
+
+// Counter-based Gaussian noise (Philox-4x32-10 + Box-Muller) keyed by the global
+// element index, and the rectified-flow interpolation
+//   noisy = x + t (eps - x),  target = eps - x.
+struct NoiseDesc {
+  int device = 0;
+  long rows = 0;
+  int P = 0;
+  uint64_t seed = 0;
+  uint64_t offset = 0;
+  long row_base = 0;        // global index of local row 0 (CP shard start)
+  long rows_per_sample = 1; // local rows per sample
+  long global_rows_per_sample = 1;
+  const void* clean = nullptr;
+  bool clean_f32 = true;
+  const float* t = nullptr;  // [rows] per-token noise level
+  void* noisy = nullptr;     // fp32 [rows, P]
+  void* target = nullptr;    // fp32 [rows, P]
+  void* noise = nullptr;     // optional fp32 [rows, P]
+};
+void noise_interp_launch(const NoiseDesc& d, cudaStream_t stream);
+
+// Fused AdamW over a flat fp32 parameter range, with optional bf16 copy-out.
+struct AdamWDesc {
+  int device = 0;
+  long n = 0;
+  float* param = nullptr;
+  const float* grad = nullptr;
+  float* exp_avg = nullptr;
+  float* exp_avg_sq = nullptr;
+  void* param_bf16 = nullptr;  // optional bf16 compute copy
+  float lr = 1e-4f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
+  float bias_correction1 = 1.f, bias_correction2_sqrt = 1.f;
+  const float* grad_scale = nullptr;  // device scalar multiplying grads (clip); may be null
+  const int* skip = nullptr;          // device flag: non-zero skips the update
+};
+// Flash attention (head_dim 128). q: [B, H, Lq, D]; k, v: [B, Hk, Lk, D] (dense,
+// head-major); out: token-major with strides (o_sb, o_sl, o_sh); lse: fp32
+// [B, H, Lq] in the base-2 domain of the scaled scores.
+struct AttnFwdDesc {
+  int device = 0;
+  int B = 0, H = 0, Hk = 0, Lq = 0, Lk = 0, D = 128;
+  int q_tiles = 0;
+  float scale_log2 = 0.f;
+  const void* q = nullptr;
+  const void* k = nullptr;
+  const void* v = nullptr;
+  const uint32_t* kmask = nullptr;  // packed key-valid bits [B, kmask_words] or null
+  int kmask_words = 0;
+  __nv_bfloat16* out = nullptr;
+  long o_sb = 0, o_sl = 0, o_sh = 0;
+  float* lse = nullptr;
+  int* err = nullptr;
+};
+void attn_fwd_launch(const AttnFwdDesc& d, cudaStream_t stream);
+
+struct AttnBwdDesc {
+  int device = 0;
+  int B = 0, H = 0, Hk = 0, Lq = 0, Lk = 0, D = 128;
+  int k_tiles = 0;
+  float scale = 0.f;       // softmax scale (dK and dQ are multiplied by it)
+  float scale_log2 = 0.f;  // scale * log2(e)
+  const void* q = nullptr;
+  const void* k = nullptr;
+  const void* v = nullptr;
+  const void* o = nullptr;     // forward output, token-major dense [B, Lq, H, D]
+  const void* dout = nullptr;  // same layout
+  long o_sb = 0, o_sl = 0, o_sh = 0;
+  const float* lse = nullptr;  // [B, H, Lq]
+  float* delta = nullptr;      // scratch [B, H, Lq]
+  const uint32_t* kmask = nullptr;
+  int kmask_words = 0;
+  float* dq_acc = nullptr;     // fp32 [B, H, Lq, D], zeroed by the caller
+  __nv_bfloat16* dk = nullptr; // [B, Hk, Lk, D]
+  __nv_bfloat16* dv = nullptr;
+  int* err = nullptr;
+};
+void attn_bwd_launch(const AttnBwdDesc& d, cudaStream_t stream);
+
+void adamw_launch(const AdamWDesc& d, cudaStream_t stream);
+void sq_norm_launch(int device, const float* x, long n, float* out, cudaStream_t stream);
+void ema_launch(int device, long n, const float* param, void* shadow, bool shadow_bf16, float decay,
+                cudaStream_t stream);
+
+}  // namespace avgen

@@ -1,0 +1,378 @@
+"""Functional wrappers over the sm_100a kernels of ``avgen_b200._C``.
+
+Every function here launches a hand-written kernel on the current CUDA stream;
+outputs are allocated by the caller or here with ``torch.empty``. Shapes follow
+the conventions of the kernels:
+
+* GEMM: ``D[M, N] = A[M, K] . B[N, K]^T``; ``a_mn`` / ``b_mn`` say an operand is
+  given transposed (``[K, M]`` / ``[K, N]``) so backward GEMMs need no copies.
+* attention: ``q`` ``[B, H, Lq, D]``, ``k``/``v`` ``[B, Hk, Lk, D]`` (head-major),
+  output token-major ``[B, Lq, H, D]``, ``lse`` fp32 ``[B, H, Lq]`` in the base-2
+  domain of the scaled scores.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from avgen_b200.ops._ext import load
+
+EPILOGUES = {"store": 0, "gate_resid": 1, "swiglu": 2, "gelu": 3, "atomic": 4}
+
+_BF16 = torch.bfloat16
+_F32 = torch.float32
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    epilogue: str = "store",
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype = _BF16,
+    bias: torch.Tensor | None = None,
+    resid: torch.Tensor | None = None,
+    gate: torch.Tensor | None = None,
+    rows_per_batch: int = 1,
+    aux: torch.Tensor | None = None,
+    k_splits: int = 1,
+) -> torch.Tensor:
+    """tcgen05 GEMM with a fused epilogue (see ``csrc/gemm.cu``)."""
+    m = a.shape[1] if a_mn else a.shape[0]
+    n = b.shape[1] if b_mn else b.shape[0]
+    if out is None:
+        cols = n // 2 if epilogue == "swiglu" else n
+        if epilogue == "atomic":
+            out = torch.zeros((m, cols), device=a.device, dtype=_F32)
+        else:
+            out = torch.empty((m, cols), device=a.device, dtype=out_dtype)
+    load().gemm(
+        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits
+    )
+    return out
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """``x[M, K] @ w[N, K]^T (+ bias)`` in bf16 with fp32 accumulation."""
+    return gemm(x, w, bias=bias)
+
+
+def linear_dx(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = _BF16) -> torch.Tensor:
+    """Input gradient ``dy[M, N] @ w[N, K]``."""
+    return gemm(dy, w, b_mn=True, out_dtype=out_dtype)
+
+
+def linear_dw(dy: torch.Tensor, x: torch.Tensor, grad: torch.Tensor, *, k_splits: int = 0) -> torch.Tensor:
+    """Accumulate the weight gradient ``grad[N, K] += dy[M, N]^T @ x[M, K]`` (fp32)."""
+    n, k = grad.shape
+    if k_splits <= 0:
+        tiles = -(-n // 128) * -(-k // 256)
+        sms = torch.cuda.get_device_properties(dy.device).multi_processor_count
+        k_splits = max(1, min(8, (2 * sms) // max(1, tiles)))
+    return gemm(dy, x, a_mn=True, b_mn=True, epilogue="atomic", out=grad, k_splits=k_splits)
+
+
+def rmsnorm_mod(
+    x: torch.Tensor,
+    weight: torch.Tensor | None,
+    scale: torch.Tensor | None = None,
+    shift: torch.Tensor | None = None,
+    *,
+    rows_per_batch: int = 1,
+    eps: float = 1e-6,
+    out: torch.Tensor | None = None,
+    want_rstd: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """``rmsnorm(x) * weight * (1 + scale[b]) + shift[b]`` over rows of ``x[R, W]``."""
+    y = out if out is not None else torch.empty_like(x)
+    rstd = torch.empty(x.shape[0], device=x.device, dtype=_F32) if want_rstd else None
+    load().rmsnorm_mod_fwd(x, y, rstd, weight, scale, shift, rows_per_batch, eps)
+    return y, rstd
+
+
+def rmsnorm_mod_bwd(
+    x: torch.Tensor,
+    rstd: torch.Tensor,
+    dy: torch.Tensor,
+    weight: torch.Tensor | None,
+    scale: torch.Tensor | None = None,
+    shift: torch.Tensor | None = None,
+    *,
+    dres: torch.Tensor | None = None,
+    dweight: torch.Tensor | None = None,
+    dscale: torch.Tensor | None = None,
+    dshift: torch.Tensor | None = None,
+    rows_per_batch: int = 1,
+    dx: torch.Tensor | None = None,
+) -> torch.Tensor:
+    """Backward of :func:`rmsnorm_mod`; parameter grads accumulate (fp32)."""
+    dx = dx if dx is not None else torch.empty_like(x)
+    load().rmsnorm_mod_bwd(
+        x, rstd, dy, dx, dres, weight, scale, shift, dweight, dscale, dshift, rows_per_batch
+    )
+    return dx
+
+
+def gate_bwd(
+    dx: torch.Tensor, a: torch.Tensor, gate: torch.Tensor, dgate: torch.Tensor, *, rows_per_batch: int
+) -> torch.Tensor:
+    """``da = dx * gate[b]`` and ``dgate[b] += sum_rows(dx * a)``."""
+    da = torch.empty_like(dx)
+    load().gate_bwd(dx, a, gate, da, dgate, rows_per_batch)
+    return da
+
+
+def rope_frequencies(
+    head_dim: int,
+    *,
+    theta: float = 10000.0,
+    time_scale: float = 1.0,
+    mode: str = "none",
+    time_factor: float = 1.0,
+    spatial_factor: float = 1.0,
+    device: torch.device | str = "cpu",
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-pair angular frequency and coordinate axis for 3-D axial RoPE.
+
+    Pairs are split over (time, row, column) as ``(P - 2 floor(P/3), floor(P/3),
+    floor(P/3))`` (reference: avgen/models/rope.py:128-157); time scaling and
+    linear / NTK scaling fold into the frequencies so the kernel computes
+    ``angle = coords[axis] * freq`` (reference: avgen/models/rope.py:218-294).
+    """
+    pairs = head_dim // 2
+    spatial = pairs // 3
+    budgets = (pairs - 2 * spatial, spatial, spatial)
+    factors = (time_factor, spatial_factor, spatial_factor)
+    freqs: list[torch.Tensor] = []
+    axes: list[torch.Tensor] = []
+    for axis, (count, factor) in enumerate(zip(budgets, factors, strict=True)):
+        axis_theta = theta
+        mult = 1.0
+        if axis == 0 and time_scale != 1.0:
+            mult *= time_scale
+        if mode == "linear" and factor != 1.0:
+            mult /= factor
+        elif mode == "ntk" and factor != 1.0:
+            dim = 2 * count
+            if dim > 2:
+                axis_theta = theta * factor ** (dim / (dim - 2))
+        exponent = torch.arange(count, dtype=_F32) / count
+        inv = torch.pow(torch.tensor(axis_theta, dtype=_F32), -exponent) * mult
+        freqs.append(inv)
+        axes.append(torch.full((count,), axis, dtype=torch.int32))
+    return torch.cat(freqs).to(device), torch.cat(axes).to(device)
+
+
+def qkv_rope(
+    qkv: torch.Tensor,
+    *,
+    batch: int,
+    length: int,
+    heads: int,
+    kv_heads: int,
+    head_dim: int,
+    q_weight: torch.Tensor | None,
+    k_weight: torch.Tensor | None,
+    coords: torch.Tensor | None,
+    freq: torch.Tensor | None,
+    axis: torch.Tensor | None,
+    eps: float = 1e-6,
+) -> tuple[torch.Tensor | None, torch.Tensor | None, torch.Tensor | None]:
+    """QK-RMSNorm + RoPE + relayout of ``qkv[B*L, (H + 2Hk) * D]`` into head-major q, k, v."""
+    dev = qkv.device
+    q = torch.empty((batch, heads, length, head_dim), device=dev, dtype=_BF16) if heads else None
+    k = torch.empty((batch, kv_heads, length, head_dim), device=dev, dtype=_BF16) if kv_heads else None
+    v = torch.empty_like(k) if kv_heads else None
+    load().qkv_rope_fwd(
+        qkv, batch, length, heads, kv_heads, head_dim, eps, q_weight, k_weight, coords, freq, axis, q, k, v
+    )
+    return q, k, v
+
+
+def qkv_rope_bwd(
+    qkv: torch.Tensor,
+    dq: torch.Tensor | None,
+    dk: torch.Tensor | None,
+    dv: torch.Tensor | None,
+    *,
+    batch: int,
+    length: int,
+    heads: int,
+    kv_heads: int,
+    head_dim: int,
+    q_weight: torch.Tensor | None,
+    k_weight: torch.Tensor | None,
+    coords: torch.Tensor | None,
+    freq: torch.Tensor | None,
+    axis: torch.Tensor | None,
+    dq_weight: torch.Tensor | None = None,
+    dk_weight: torch.Tensor | None = None,
+    eps: float = 1e-6,
+) -> torch.Tensor:
+    """Backward of :func:`qkv_rope`: returns ``dqkv`` in the GEMM layout."""
+    dqkv = torch.empty_like(qkv)
+    load().qkv_rope_bwd(
+        qkv, dqkv, batch, length, heads, kv_heads, head_dim, eps, q_weight, k_weight, coords, freq, axis,
+        dq, dk, dv, dq_weight, dk_weight,
+    )
+    return dqkv
+
+
+def pack_key_mask(mask: torch.Tensor | None) -> torch.Tensor | None:
+    """Pack a boolean key mask ``[B, L]`` into int32 bit words ``[B, ceil(L/32)]``."""
+    if mask is None:
+        return None
+    b, length = mask.shape
+    words = -(-length // 32)
+    padded = torch.zeros((b, words * 32), device=mask.device, dtype=torch.int64)
+    padded[:, :length] = mask.to(torch.int64)
+    weights = torch.bitwise_left_shift(torch.ones(32, device=mask.device, dtype=torch.int64),
+                                       torch.arange(32, device=mask.device, dtype=torch.int64))
+    packed = (padded.view(b, words, 32) * weights).sum(-1)
+    packed = torch.where(packed >= 2**31, packed - 2**32, packed)
+    return packed.to(torch.int32).contiguous()
+
+
+def attention_fwd(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    *,
+    kmask: torch.Tensor | None = None,
+    scale: float | None = None,
+    out: torch.Tensor | None = None,
+    want_lse: bool = True,
+) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Flash attention forward. Returns ``(out [B, Lq, H, D], lse [B, H, Lq])``."""
+    b, h, lq, d = q.shape
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    if out is None:
+        out = torch.empty((b, lq, h, d), device=q.device, dtype=_BF16)
+    lse = torch.empty((b, h, lq), device=q.device, dtype=_F32) if want_lse else None
+    load().attn_fwd(q, k, v, out, lse, kmask, scale)
+    return out, lse
+
+
+def attention_bwd(
+    q: torch.Tensor,
+    k: torch.Tensor,
+    v: torch.Tensor,
+    o: torch.Tensor,
+    dout: torch.Tensor,
+    lse: torch.Tensor,
+    *,
+    kmask: torch.Tensor | None = None,
+    scale: float | None = None,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Flash attention backward. Returns ``(dq fp32 [B,H,Lq,D], dk, dv)``."""
+    d = q.shape[-1]
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    delta = torch.empty_like(lse)
+    dq = torch.zeros(q.shape, device=q.device, dtype=_F32)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    load().attn_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, kmask, scale)
+    return dq, dk, dv
+
+
+def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
+    """Backward of the interleaved SwiGLU epilogue: returns ``dgu`` like ``gu``."""
+    dgu = torch.empty_like(gu)
+    load().swiglu_bwd(dh, gu, dgu)
+    return dgu
+
+
+def gelu_bwd(dh: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
+    """Backward of GELU(tanh): returns the gradient w.r.t. the pre-activation."""
+    dpre = torch.empty_like(pre)
+    load().gelu_bwd(dh, pre, dpre)
+    return dpre
+
+
+def flow_loss_stats(
+    pred: torch.Tensor,
+    target: torch.Tensor,
+    loss_mask: torch.Tensor,
+    weight: torch.Tensor | None,
+    *,
+    rows_per_batch: int,
+) -> torch.Tensor:
+    """``[sum(w*mse*m), sum(mse*m), sum(m)]`` over token rows (fp32, device)."""
+    stats = torch.zeros(3, device=pred.device, dtype=_F32)
+    load().flow_loss_fwd(pred.contiguous(), target.contiguous(), loss_mask.contiguous(), weight, rows_per_batch, stats)
+    return stats
+
+
+def flow_loss_grad(
+    pred: torch.Tensor,
+    target: torch.Tensor,
+    loss_mask: torch.Tensor,
+    weight: torch.Tensor | None,
+    scale: torch.Tensor,
+    *,
+    rows_per_batch: int,
+    out_dtype: torch.dtype | None = None,
+) -> torch.Tensor:
+    """Gradient of ``scale * sum(w * mse * m)`` w.r.t. ``pred``."""
+    dpred = torch.empty(pred.shape, device=pred.device, dtype=out_dtype or pred.dtype)
+    load().flow_loss_bwd(pred.contiguous(), target.contiguous(), loss_mask.contiguous(), weight, rows_per_batch,
+                         scale, dpred)
+    return dpred
+
+
+def noise_interp(
+    clean: torch.Tensor,
+    t: torch.Tensor,
+    *,
+    seed: int,
+    offset: int = 0,
+    row_base: int = 0,
+    rows_per_sample: int | None = None,
+    global_rows_per_sample: int | None = None,
+    want_noise: bool = False,
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor | None]:
+    """Counter-based noise and ``noisy = x + t(eps - x)``, ``target = eps - x``."""
+    rows = clean.numel() // clean.shape[-1]
+    rps = rows_per_sample or clean.shape[-2]
+    grps = global_rows_per_sample or rps
+    noisy = torch.empty(clean.shape, device=clean.device, dtype=_F32)
+    target = torch.empty_like(noisy)
+    noise = torch.empty_like(noisy) if want_noise else None
+    del rows
+    load().noise_interp(clean.contiguous(), t.contiguous(), seed & ((1 << 63) - 1), offset, row_base, rps, grps,
+                        noisy, target, noise)
+    return noisy, target, noise
+
+
+def adamw_step(
+    param: torch.Tensor,
+    grad: torch.Tensor,
+    exp_avg: torch.Tensor,
+    exp_avg_sq: torch.Tensor,
+    *,
+    lr: float,
+    betas: tuple[float, float],
+    eps: float,
+    weight_decay: float,
+    step: int,
+    param_bf16: torch.Tensor | None = None,
+    grad_scale: torch.Tensor | None = None,
+    skip: torch.Tensor | None = None,
+) -> None:
+    """Fused AdamW over flat fp32 buffers (optionally writing a bf16 copy)."""
+    load().adamw(param, grad, exp_avg, exp_avg_sq, lr, betas[0], betas[1], eps, weight_decay, step, param_bf16,
+                 grad_scale, skip)
+
+
+def sq_norm_(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """``out += sum(x ** 2)`` for a flat fp32 buffer."""
+    load().sq_norm(x, out)
+    return out
+
+
+def ema_(param: torch.Tensor, shadow: torch.Tensor, decay: float) -> None:
+    """``shadow += (1 - decay) * (param - shadow)``."""
+    load().ema(param, shadow, decay)

@@ -1,0 +1,257 @@
+"""Numerics of the sm_100a kernels against plain PyTorch fp32 references."""
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ops():
+    from avgen_b200.ops import kernels
+
+    return kernels
+
+
+def _close(got: torch.Tensor, ref: torch.Tensor, rtol: float = 2e-2, atol: float = 2e-2) -> None:
+    got = got.float()
+    ref = ref.float()
+    err = (got - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= atol + rtol * scale, f"max err {err:.4g} vs scale {scale:.4g}"
+
+
+def _errors_clear() -> None:
+    from avgen_b200.ops._ext import check_errors
+
+    assert check_errors() == 0, "a kernel recorded a timed-out wait"
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 128), (300, 264, 200), (1024, 2560, 2560), (129, 8, 64)])
+def test_gemm_store(m: int, n: int, k: int) -> None:
+    ops = _ops()
+    torch.manual_seed(0)
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    b = torch.randn(n, k, device=DEV).bfloat16()
+    bias = torch.randn(n, device=DEV)
+    ref = a.float() @ b.float().t() + bias
+    got = ops.gemm(a, b, bias=bias)
+    _close(got, ref)
+    got32 = ops.gemm(a, b, out_dtype=torch.float32)
+    _close(got32, a.float() @ b.float().t(), rtol=1e-3, atol=1e-2)
+    _errors_clear()
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 384, 256), (200, 136, 72)])
+def test_gemm_transposed_operands(m: int, n: int, k: int) -> None:
+    ops = _ops()
+    torch.manual_seed(1)
+    dy = torch.randn(m, n, device=DEV).bfloat16()
+    w = torch.randn(n, k, device=DEV).bfloat16()
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    # dX = dY . W  (B given as [K_red, N_out])
+    _close(ops.linear_dx(dy, w), dy.float() @ w.float())
+    # dW += dY^T . X (both operands MN-major), split-K atomics, accumulating
+    grad = torch.ones(n, k, device=DEV)
+    ops.linear_dw(dy, x, grad, k_splits=3)
+    _close(grad, 1.0 + dy.float().t() @ x.float(), rtol=1e-3, atol=5e-2)
+    _errors_clear()
+
+
+def test_gemm_fused_epilogues() -> None:
+    ops = _ops()
+    torch.manual_seed(2)
+    bsz, rows, k, n = 2, 192, 256, 512
+    m = bsz * rows
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    w = torch.randn(n, k, device=DEV).bfloat16() * 0.1
+    acc = a.float() @ w.float().t()
+    resid = torch.randn(m, n, device=DEV).bfloat16()
+    gate = torch.randn(bsz, n, device=DEV)
+    aux = torch.empty(m, n, device=DEV, dtype=torch.bfloat16)
+    got = ops.gemm(a, w, epilogue="gate_resid", resid=resid, gate=gate, rows_per_batch=rows, aux=aux)
+    ref = resid.float() + gate.repeat_interleave(rows, 0) * acc
+    _close(got, ref)
+    _close(aux, acc)
+    sw = ops.gemm(a, w, epilogue="swiglu")
+    g, u = acc[:, 0::2], acc[:, 1::2]
+    _close(sw, F.silu(g) * u)
+    ge = ops.gemm(a, w, epilogue="gelu")
+    _close(ge, F.gelu(acc, approximate="tanh"))
+    _errors_clear()
+
+
+def test_rmsnorm_mod_fwd_bwd() -> None:
+    ops = _ops()
+    torch.manual_seed(3)
+    bsz, rows, w_ = 2, 100, 2560
+    x = torch.randn(bsz * rows, w_, device=DEV).bfloat16()
+    weight = torch.rand(w_, device=DEV) + 0.5
+    scale = torch.randn(bsz, w_, device=DEV) * 0.1
+    shift = torch.randn(bsz, w_, device=DEV) * 0.1
+    y, rstd = ops.rmsnorm_mod(x, weight, scale, shift, rows_per_batch=rows)
+    xr = x.float().requires_grad_()
+    wr, sr, tr = (t.clone().requires_grad_() for t in (weight, scale, shift))
+    ref = F.rms_norm(xr, (w_,), wr, 1e-6) * (1 + sr.repeat_interleave(rows, 0)) + tr.repeat_interleave(rows, 0)
+    _close(y, ref)
+    dy = torch.randn_like(ref).bfloat16()
+    ref.backward(dy.float())
+    dw = torch.zeros(w_, device=DEV)
+    ds = torch.zeros(bsz, w_, device=DEV)
+    dt = torch.zeros(bsz, w_, device=DEV)
+    dx = ops.rmsnorm_mod_bwd(x, rstd, dy, weight, scale, shift, dweight=dw, dscale=ds, dshift=dt, rows_per_batch=rows)
+    _close(dx, xr.grad)
+    _close(dw, wr.grad, rtol=1e-2, atol=1e-2)
+    _close(ds, sr.grad, rtol=1e-2, atol=1e-2)
+    _close(dt, tr.grad, rtol=1e-2, atol=1e-2)
+    _errors_clear()
+
+
+def test_gate_bwd() -> None:
+    ops = _ops()
+    torch.manual_seed(4)
+    bsz, rows, w_ = 2, 64, 256
+    dx = torch.randn(bsz * rows, w_, device=DEV).bfloat16()
+    a = torch.randn_like(dx)
+    gate = torch.randn(bsz, w_, device=DEV)
+    dgate = torch.zeros(bsz, w_, device=DEV)
+    da = ops.gate_bwd(dx, a, gate, dgate, rows_per_batch=rows)
+    _close(da, dx.float() * gate.repeat_interleave(rows, 0))
+    _close(dgate, (dx.float() * a.float()).view(bsz, rows, w_).sum(1), rtol=1e-2, atol=1e-2)
+
+
+def _rope_ref(x: torch.Tensor, coords: torch.Tensor, freq: torch.Tensor, axis: torch.Tensor) -> torch.Tensor:
+    # x [B, H, L, D] fp32, coords [B, L, 3]
+    ang = coords[..., axis.long()] * freq  # [B, L, D/2]
+    cos, sin = torch.cos(ang)[:, None], torch.sin(ang)[:, None]
+    pairs = x.unflatten(-1, (-1, 2))
+    e, o = pairs[..., 0], pairs[..., 1]
+    return torch.stack((e * cos - o * sin, e * sin + o * cos), -1).flatten(-2)
+
+
+def test_qkv_rope_fwd_bwd() -> None:
+    ops = _ops()
+    torch.manual_seed(5)
+    bsz, length, h, d = 2, 40, 3, 128
+    qkv = torch.randn(bsz * length, 3 * h * d, device=DEV).bfloat16()
+    qw = torch.rand(d, device=DEV) + 0.5
+    kw = torch.rand(d, device=DEV) + 0.5
+    coords = torch.rand(bsz, length, 3, device=DEV) * 10
+    freq, axis = ops.rope_frequencies(d, device=DEV)
+    q, k, v = ops.qkv_rope(qkv, batch=bsz, length=length, heads=h, kv_heads=h, head_dim=d, q_weight=qw,
+                           k_weight=kw, coords=coords, freq=freq, axis=axis)
+    xr = qkv.float().view(bsz, length, 3, h, d).permute(2, 0, 3, 1, 4).requires_grad_()
+    qr = _rope_ref(F.rms_norm(xr[0], (d,), qw, 1e-6), coords, freq, axis)
+    kr = _rope_ref(F.rms_norm(xr[1], (d,), kw, 1e-6), coords, freq, axis)
+    vr = xr[2]
+    _close(q, qr)
+    _close(k, kr)
+    _close(v, vr)
+    dq, dk, dv = (torch.randn_like(t).bfloat16() for t in (qr, kr, vr))
+    (qr * dq.float()).sum().add((kr * dk.float()).sum()).add((vr * dv.float()).sum()).backward()
+    dqw = torch.zeros(d, device=DEV)
+    dkw = torch.zeros(d, device=DEV)
+    dqkv = ops.qkv_rope_bwd(qkv, dq, dk, dv, batch=bsz, length=length, heads=h, kv_heads=h, head_dim=d,
+                            q_weight=qw, k_weight=kw, coords=coords, freq=freq, axis=axis, dq_weight=dqw,
+                            dk_weight=dkw)
+    ref_grad = xr.grad.permute(1, 3, 0, 2, 4).reshape(bsz * length, 3 * h * d)
+    _close(dqkv, ref_grad)
+    _errors_clear()
+
+
+def _attn_ref(q, k, v, kmask, scale):
+    qf, kf, vf = q.float(), k.float(), v.float()
+    rep = q.shape[1] // k.shape[1]
+    kf = kf.repeat_interleave(rep, 1)
+    vf = vf.repeat_interleave(rep, 1)
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    if kmask is not None:
+        s = s.masked_fill(~kmask[:, None, None, :], float("-inf"))
+    p = torch.softmax(s, -1)
+    return (p @ vf).transpose(1, 2)  # [B, Lq, H, D]
+
+
+@pytest.mark.parametrize("b,h,hk,lq,lk,masked", [(1, 2, 2, 256, 256, False), (2, 2, 1, 300, 333, True),
+                                                   (1, 1, 1, 1024, 2048, False)])
+def test_attention_fwd_bwd(b: int, h: int, hk: int, lq: int, lk: int, masked: bool) -> None:
+    ops = _ops()
+    torch.manual_seed(6)
+    d = 128
+    scale = 1.0 / math.sqrt(d)
+    q = torch.randn(b, h, lq, d, device=DEV).bfloat16()
+    k = torch.randn(b, hk, lk, d, device=DEV).bfloat16()
+    v = torch.randn(b, hk, lk, d, device=DEV).bfloat16()
+    kmask = None
+    if masked:
+        kmask = torch.rand(b, lk, device=DEV) > 0.3
+        kmask[:, 0] = True
+    packed = ops.pack_key_mask(kmask)
+    out, lse = ops.attention_fwd(q, k, v, kmask=packed)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    ref = _attn_ref(qr, kr, vr, kmask, scale)
+    _close(out, ref, rtol=2e-2, atol=2e-2)
+    dout = torch.randn_like(ref).bfloat16()
+    ref.backward(dout.float())
+    dq, dk, dv = ops.attention_bwd(q, k, v, out, dout.contiguous(), lse, kmask=packed)
+    _close(dq, qr.grad, rtol=3e-2, atol=3e-2)
+    _close(dk, kr.grad, rtol=3e-2, atol=3e-2)
+    _close(dv, vr.grad, rtol=3e-2, atol=3e-2)
+    _errors_clear()
+
+
+def test_flow_loss_and_noise() -> None:
+    ops = _ops()
+    torch.manual_seed(7)
+    bsz, length, p = 2, 50, 64
+    pred = torch.randn(bsz, length, p, device=DEV)
+    target = torch.randn(bsz, length, p, device=DEV)
+    mask = torch.rand(bsz, length, device=DEV) > 0.2
+    weight = torch.rand(bsz, device=DEV)
+    stats = ops.flow_loss_stats(pred, target, mask, weight, rows_per_batch=length)
+    mse = (pred - target).pow(2).mean(-1)
+    m = mask.float()
+    ref = torch.stack(((mse * m * weight[:, None]).sum(), (mse * m).sum(), m.sum()))
+    _close(stats, ref, rtol=1e-4, atol=1e-3)
+    scale = torch.tensor([0.5], device=DEV)
+    grad = ops.flow_loss_grad(pred, target, mask, weight, scale, rows_per_batch=length)
+    pr = pred.clone().requires_grad_()
+    (0.5 * ((pr - target).pow(2).mean(-1) * m * weight[:, None]).sum()).backward()
+    _close(grad, pr.grad, rtol=1e-4, atol=1e-5)
+    clean = torch.randn(bsz, length, p, device=DEV)
+    t = torch.rand(bsz, length, device=DEV)
+    noisy, tgt, noise = ops.noise_interp(clean, t, seed=123, want_noise=True)
+    assert abs(noise.mean().item()) < 0.05 and abs(noise.std().item() - 1) < 0.05
+    _close(noisy, clean + t[..., None] * (noise - clean), rtol=1e-5, atol=1e-5)
+    _close(tgt, noise - clean, rtol=1e-5, atol=1e-5)
+    # a shard drawn with its global row base equals the slice of the full draw
+    half = length // 2
+    _, _, shard = ops.noise_interp(clean[:, half:].contiguous(), t[:, half:].contiguous(), seed=123, row_base=half,
+                                   rows_per_sample=length - half, global_rows_per_sample=length, want_noise=True)
+    torch.testing.assert_close(shard, noise[:, half:])
+
+
+def test_adamw_matches_torch() -> None:
+    ops = _ops()
+    torch.manual_seed(8)
+    n = 1000
+    p = torch.randn(n, device=DEV)
+    ref = p.clone().requires_grad_()
+    opt = torch.optim.AdamW([ref], lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    m = torch.zeros_like(p)
+    v = torch.zeros_like(p)
+    pb = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    for step in range(1, 4):
+        g = torch.randn(n, device=DEV)
+        ref.grad = g.clone()
+        opt.step()
+        ops.adamw_step(p, g, m, v, lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, step=step, param_bf16=pb)
+    torch.testing.assert_close(p, ref.detach(), rtol=1e-5, atol=1e-6)
+    _close(pb, p, rtol=1e-2, atol=1e-2)
+    out = torch.zeros(1, device=DEV)
+    ops.sq_norm_(p, out)
+    torch.testing.assert_close(out[0], p.pow(2).sum(), rtol=1e-4, atol=1e-4)

@@ -180,7 +180,7 @@ struct AdamWDesc {
   float lr = 1e-4f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
   float bias_correction1 = 1.f, bias_correction2_sqrt = 1.f;
   const float* grad_scale = nullptr;  // device scalar multiplying grads (clip); may be null
-  const int* skip = nullptr;          // device flag: non-zero skips the update
+  const int* skip = nullptr;          // device flag: non-zero treats all gradients as zero
 };
 // Flash attention (head_dim 128). q: [B, H, Lq, D]; k, v: [B, Hk, Lk, D] (dense,
 // head-major); out: token-major with strides (o_sb, o_sl, o_sh); lse: fp32

@@ -17,8 +17,9 @@ namespace avgen {
 namespace {
 
 __global__ void adamw_kernel(AdamWDesc d) {
-  if (d.skip != nullptr && *d.skip != 0) return;
-  const float gscale = d.grad_scale ? *d.grad_scale : 1.f;
+  // A non-finite step treats every gradient as zero (moments still decay).
+  const bool zero_grads = d.skip != nullptr && *d.skip != 0;
+  const float gscale = zero_grads ? 0.f : (d.grad_scale ? *d.grad_scale : 1.f);
   const float step_lr = d.lr / d.bias_correction1;
   const float decay = 1.f - d.lr * d.weight_decay;
   const long n4 = d.n / 4;
@@ -32,7 +33,7 @@ __global__ void adamw_kernel(AdamWDesc d) {
     float mv[4] = {m.x, m.y, m.z, m.w}, vv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      const float gr = gv[e] * gscale;
+      const float gr = zero_grads ? 0.f : gv[e] * gscale;
       mv[e] = d.beta1 * mv[e] + (1.f - d.beta1) * gr;
       vv[e] = d.beta2 * vv[e] + (1.f - d.beta2) * gr * gr;
       const float denom = sqrtf(vv[e]) / d.bias_correction2_sqrt + d.eps;
@@ -50,7 +51,7 @@ __global__ void adamw_kernel(AdamWDesc d) {
   }
   // scalar tail
   for (long i = n4 * 4 + static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < d.n; i += stride) {
-    const float gr = d.grad[i] * gscale;
+    const float gr = zero_grads ? 0.f : d.grad[i] * gscale;
     const float mv = d.beta1 * d.exp_avg[i] + (1.f - d.beta1) * gr;
     const float vv = d.beta2 * d.exp_avg_sq[i] + (1.f - d.beta2) * gr * gr;
     const float denom = sqrtf(vv) / d.bias_correction2_sqrt + d.eps;

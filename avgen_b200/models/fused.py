@@ -1,0 +1,410 @@
+"""The fused DiT block: one autograd node per block driving the sm_100a kernels.
+
+Forward of one block (reference semantics: avgen/models/blocks.py:173-227):
+
+    n1  = rmsnorm(x) * w_a * (1 + scale_a) + shift_a              rmsnorm_mod kernel
+    qkv = n1 @ Wqkv^T                                              tcgen05 GEMM
+    q,k,v = rope(qknorm(qkv))  (head-major)                        qkv_rope kernel
+    O   = flash_attention(q, k, v)                                 tcgen05 attention
+    x1  = x + gate_a * (O @ Wo^T)                                  GEMM, gated-residual epilogue
+    x2  = x1 + cross_attention(rmsnorm(x1), text)                  norm + GEMMs + attention + residual epilogue
+    x3  = x2 + gate_f * down(silu(gate(n3)) * up(n3)),             GEMM with SwiGLU epilogue, then
+          n3 = rmsnorm(x2) * w_f * (1 + scale_f) + shift_f          GEMM with gated-residual epilogue
+
+Only ``x``, the self-attention output ``O`` and its log-sum-exp are saved
+(about 2 x B*L*W bf16 per block). Backward recomputes every GEMM and the cheap
+cross-attention but never the self-attention forward, then runs the backward
+kernels; weight gradients accumulate in fp32 through the GEMM's atomic
+epilogue. This is the "selective" activation-checkpoint policy of the
+reference (avgen/parallel/activation.py:72-160: keep attention outputs,
+recompute the rest) built into the block.
+
+Self-attention can be swapped for a context-parallel implementation through
+``BlockSpec.attention`` (see :mod:`avgen_b200.parallel.context`).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any, Protocol
+
+import torch
+from torch import nn
+
+__all__ = ["AttentionImpl", "BlockSpec", "LocalAttention", "fused_block_forward", "packed_weights"]
+
+_BF16 = torch.bfloat16
+
+
+class AttentionImpl(Protocol):
+    """Self-attention implementation used inside the fused block."""
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, kmask: torch.Tensor | None,
+                scale: float) -> tuple[torch.Tensor, torch.Tensor, Any]: ...
+
+    def backward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, o: torch.Tensor, do: torch.Tensor,
+                 lse: torch.Tensor, kmask: torch.Tensor | None, scale: float,
+                 state: Any) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]: ...
+
+
+class LocalAttention:
+    """Single-device flash attention (tcgen05 kernels)."""
+
+    def forward(self, q, k, v, kmask, scale):  # noqa: ANN001, ANN201
+        from avgen_b200.ops import kernels as K
+
+        out, lse = K.attention_fwd(q, k, v, kmask=kmask, scale=scale)
+        return out, lse, None
+
+    def backward(self, q, k, v, o, do, lse, kmask, scale, state):  # noqa: ANN001, ANN201
+        from avgen_b200.ops import kernels as K
+
+        dq, dk, dv = K.attention_bwd(q, k, v, o, do, lse, kmask=kmask, scale=scale)
+        return dq, dk, dv
+
+
+@dataclass
+class BlockSpec:
+    """Static description of one fused block call."""
+
+    batch: int
+    length: int
+    width: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    hidden: int
+    ffn: str  # "swiglu" | "gelu"
+    eps: float
+    qk_norm: bool
+    cross: bool
+    ctx_heads: int = 0
+    ctx_kv_heads: int = 0
+    text_length: int = 0
+    attention: AttentionImpl | None = None
+
+
+def _packed(module: nn.Module, key: str, params: list[torch.Tensor], build) -> torch.Tensor:  # noqa: ANN001
+    from avgen_b200.models.linear import weight_epoch
+
+    cache = module.__dict__.setdefault("_avgen_packed", {})
+    version = (weight_epoch(), *((p._version, p.data_ptr()) for p in params))
+    hit = cache.get(key)
+    if hit is not None and hit[0] == version:
+        return hit[1]
+    with torch.no_grad():
+        value = build(*[p.detach() for p in params]).to(_BF16).contiguous()
+    cache[key] = (version, value)
+    return value
+
+
+def packed_weights(block: nn.Module) -> dict[str, torch.Tensor]:
+    """bf16 kernel-layout weights of a DiT block, rebuilt only after parameter updates."""
+    att = block.attention
+    ff = block.feed_forward
+    out = {
+        "qkv": _packed(block, "qkv", [att.q_proj.weight, att.k_proj.weight, att.v_proj.weight],
+                       lambda q, k, v: torch.cat((q, k, v), 0)),
+        "o": _packed(block, "o", [att.out_proj.weight], lambda w: w),
+        "down": _packed(block, "down", [ff.down_proj.weight], lambda w: w),
+    }
+    if hasattr(ff, "gate_proj"):
+        out["gu"] = _packed(block, "gu", [ff.gate_proj.weight, ff.up_proj.weight],
+                            lambda g, u: torch.stack((g, u), 1).reshape(2 * g.shape[0], g.shape[1]))
+    else:
+        out["up"] = _packed(block, "up", [ff.up_proj.weight], lambda w: w)
+    if block.cross_attention is not None:
+        ca = block.cross_attention
+        out["cq"] = _packed(block, "cq", [ca.q_proj.weight], lambda w: w)
+        out["ckv"] = _packed(block, "ckv", [ca.k_proj.weight, ca.v_proj.weight], lambda k, v: torch.cat((k, v), 0))
+        out["co"] = _packed(block, "co", [ca.out_proj.weight], lambda w: w)
+    return out
+
+
+def _f32(t: torch.Tensor | None) -> torch.Tensor | None:
+    return None if t is None else t.detach().float().contiguous()
+
+
+def _attn_impl(spec: BlockSpec) -> AttentionImpl:
+    return spec.attention if spec.attention is not None else LocalAttention()
+
+
+def _norm_weight(norm: nn.Module) -> torch.Tensor | None:
+    w = getattr(norm, "weight", None)
+    return _f32(w) if isinstance(w, torch.Tensor) else None
+
+
+def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, *, save):  # noqa: ANN001, ANN202
+    """Run the block forward; returns (x3, (O, lse, attn_state)) and, when
+    ``save`` is False, also the intermediates the backward needs."""
+    from avgen_b200.ops import kernels as K
+
+    b, length, w = spec.batch, spec.length, spec.width
+    h, hk, d = spec.heads, spec.kv_heads, spec.head_dim
+    eps = spec.eps
+    shift_a, scale_a, gate_a = modf[:, 0], modf[:, 1], modf[:, 2]
+    shift_f, scale_f, gate_f = modf[:, 3], modf[:, 4], modf[:, 5]
+    att = block.attention
+    n1, rstd1 = K.rmsnorm_mod(xb, _norm_weight(block.attention_norm), scale_a, shift_a, rows_per_batch=length,
+                              eps=block.attention_norm.eps or eps)
+    qkv = K.gemm(n1, pw["qkv"])
+    qw = _norm_weight(att.q_norm) if spec.qk_norm else None
+    kw = _norm_weight(att.k_norm) if spec.qk_norm else None
+    q, k, v = K.qkv_rope(qkv, batch=b, length=length, heads=h, kv_heads=hk, head_dim=d, q_weight=qw, k_weight=kw,
+                         coords=coords, freq=freq, axis=axis, eps=eps)
+    scale = 1.0 / math.sqrt(d)
+    impl = _attn_impl(spec)
+    if save:
+        o, lse, attn_state = impl.forward(q, k, v, kmask, scale)
+    else:
+        o = lse = attn_state = None
+    return_o = o
+    inter: dict[str, Any] = {}
+    if not save:
+        inter.update(n1=n1, rstd1=rstd1, qkv=qkv, q=q, k=k, v=v)
+    return inter, return_o, lse, attn_state
+
+
+def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep):  # noqa: ANN001, ANN202
+    """Everything after the self-attention kernel. Returns x3 and (if keep) the
+    intermediates needed for backward."""
+    from avgen_b200.ops import kernels as K
+
+    b, length, w = spec.batch, spec.length, spec.width
+    m = b * length
+    eps = spec.eps
+    gate_a = modf[:, 2]
+    shift_f, scale_f, gate_f = modf[:, 3], modf[:, 4], modf[:, 5]
+    keep_d: dict[str, Any] = {}
+    a_o = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
+    x1 = K.gemm(o.view(m, -1), pw["o"], epilogue="gate_resid", resid=xb, gate=gate_a, rows_per_batch=length,
+                aux=a_o)
+    x2 = x1
+    if spec.cross and ctxb is not None:
+        ca = block.cross_attention
+        n2, rstd2 = K.rmsnorm_mod(x1, _norm_weight(block.cross_norm), eps=block.cross_norm.eps or eps)
+        qc = K.gemm(n2, pw["cq"])
+        t = ctxb.shape[1]
+        kvc = K.gemm(ctxb.view(b * t, -1), pw["ckv"])
+        cqw = _norm_weight(ca.q_norm) if spec.qk_norm else None
+        ckw = _norm_weight(ca.k_norm) if spec.qk_norm else None
+        qh, _, _ = K.qkv_rope(qc, batch=b, length=length, heads=spec.ctx_heads, kv_heads=0, head_dim=spec.head_dim,
+                              q_weight=cqw, k_weight=None, coords=None, freq=None, axis=None, eps=eps)
+        _, kc, vc = K.qkv_rope(kvc, batch=b, length=t, heads=0, kv_heads=spec.ctx_kv_heads, head_dim=spec.head_dim,
+                               q_weight=None, k_weight=ckw, coords=None, freq=None, axis=None, eps=eps)
+        oc, lsec = K.attention_fwd(qh, kc, vc, kmask=cmask, scale=1.0 / math.sqrt(spec.head_dim))
+        x2 = K.gemm(oc.view(m, -1), pw["co"], epilogue="gate_resid", resid=x1, gate=None)
+        if keep:
+            keep_d.update(x1=x1, n2=n2, rstd2=rstd2, qc=qc, kvc=kvc, qh=qh, kc=kc, vc=vc, oc=oc, lsec=lsec)
+    elif keep:
+        keep_d.update(x1=x1)
+    n3, rstd3 = K.rmsnorm_mod(x2, _norm_weight(block.ffn_norm), scale_f, shift_f, rows_per_batch=length,
+                              eps=block.ffn_norm.eps or eps)
+    if spec.ffn == "swiglu":
+        gu = torch.empty((m, 2 * spec.hidden), device=xb.device, dtype=_BF16) if keep else None
+        hdn = K.gemm(n3, pw["gu"], epilogue="swiglu", aux=gu)
+    else:
+        gu = torch.empty((m, spec.hidden), device=xb.device, dtype=_BF16) if keep else None
+        hdn = K.gemm(n3, pw["up"], epilogue="gelu", aux=gu)
+    if keep:
+        f = K.gemm(hdn, pw["down"])
+        keep_d.update(a_o=a_o, x2=x2, n3=n3, rstd3=rstd3, gu=gu, h=hdn, f=f)
+        return None, keep_d
+    x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, rows_per_batch=length)
+    return x3, keep_d
+
+
+def _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask):  # noqa: ANN001, ANN202
+    _, o, lse, attn_state = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask,
+                                          save=True)
+    x3, _ = _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, keep=False)
+    return x3, (o, lse, attn_state)
+
+
+def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask, o, lse, attn_state, dout):  # noqa: ANN001, ANN202
+    from avgen_b200.ops import kernels as K
+
+    b, length, w = spec.batch, spec.length, spec.width
+    m = b * length
+    h, hk, d = spec.heads, spec.kv_heads, spec.head_dim
+    eps = spec.eps
+    dev = xb.device
+    pw = packed_weights(block)
+    att = block.attention
+    ff = block.feed_forward
+    # ---------------------------------------------------------------- recompute
+    inter, _, _, _ = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, save=False)
+    _, keep = _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, keep=True)
+    dmod = torch.zeros_like(modf)  # [B, 6, W]
+    gate_a, gate_f = modf[:, 2], modf[:, 5]
+    dx3 = dout.reshape(m, w).to(_BF16).contiguous()
+
+    def zeros_like_param(p: torch.Tensor) -> torch.Tensor:
+        return torch.zeros(p.shape, device=dev, dtype=torch.float32)
+
+    # ---------------------------------------------------------------- FFN
+    df = K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], rows_per_batch=length)
+    dh = K.linear_dx(df, pw["down"])
+    g_down = zeros_like_param(ff.down_proj.weight)
+    K.linear_dw(df, keep["h"], g_down)
+    if spec.ffn == "swiglu":
+        dgu = K.swiglu_bwd(dh, keep["gu"])
+        dn3 = K.linear_dx(dgu, pw["gu"])
+        g_gu = torch.zeros((2 * spec.hidden, w), device=dev, dtype=torch.float32)
+        K.linear_dw(dgu, keep["n3"], g_gu)
+        g_gate = g_gu[0::2].contiguous()
+        g_up = g_gu[1::2].contiguous()
+    else:
+        dpre = K.gelu_bwd(dh, keep["gu"])
+        dn3 = K.linear_dx(dpre, pw["up"])
+        g_up = zeros_like_param(ff.up_proj.weight)
+        K.linear_dw(dpre, keep["n3"], g_up)
+        g_gate = None
+    g_ffn_norm = zeros_like_param(block.ffn_norm.weight) if block.ffn_norm.weight is not None else None
+    dx2 = K.rmsnorm_mod_bwd(keep["x2"], keep["rstd3"], dn3, _norm_weight(block.ffn_norm), modf[:, 4], modf[:, 3],
+                            dres=dx3, dweight=g_ffn_norm, dscale=dmod[:, 4], dshift=dmod[:, 3],
+                            rows_per_batch=length)
+    # ---------------------------------------------------------------- cross attention
+    dctx = None
+    cross_grads: list[torch.Tensor | None] = []
+    if spec.cross and ctxb is not None:
+        ca = block.cross_attention
+        t = ctxb.shape[1]
+        doc = K.linear_dx(dx2, pw["co"])
+        g_co = zeros_like_param(ca.out_proj.weight)
+        K.linear_dw(dx2, keep["oc"].view(m, -1), g_co)
+        dqh, dkc, dvc = K.attention_bwd(keep["qh"], keep["kc"], keep["vc"], keep["oc"],
+                                        doc.view(b, length, spec.ctx_heads, d), keep["lsec"], kmask=cmask,
+                                        scale=1.0 / math.sqrt(d))
+        cqw = _norm_weight(ca.q_norm) if spec.qk_norm else None
+        ckw = _norm_weight(ca.k_norm) if spec.qk_norm else None
+        g_cqn = zeros_like_param(ca.q_norm.weight) if cqw is not None else None
+        g_ckn = zeros_like_param(ca.k_norm.weight) if ckw is not None else None
+        dqc = K.qkv_rope_bwd(keep["qc"], dqh.to(_BF16), None, None, batch=b, length=length, heads=spec.ctx_heads,
+                             kv_heads=0, head_dim=d, q_weight=cqw, k_weight=None, coords=None, freq=None, axis=None,
+                             dq_weight=g_cqn, eps=eps)
+        dkvc = K.qkv_rope_bwd(keep["kvc"], None, dkc, dvc, batch=b, length=t, heads=0, kv_heads=spec.ctx_kv_heads,
+                              head_dim=d, q_weight=None, k_weight=ckw, coords=None, freq=None, axis=None,
+                              dk_weight=g_ckn, eps=eps)
+        dn2 = K.linear_dx(dqc, pw["cq"])
+        g_cq = zeros_like_param(ca.q_proj.weight)
+        K.linear_dw(dqc, keep["n2"], g_cq)
+        g_ckv = torch.zeros((pw["ckv"].shape[0], pw["ckv"].shape[1]), device=dev, dtype=torch.float32)
+        K.linear_dw(dkvc, ctxb.view(b * t, -1), g_ckv)
+        dctx = K.linear_dx(dkvc, pw["ckv"]).view(b, t, -1)
+        kv_rows = ca.k_proj.weight.shape[0]
+        g_cross_norm = zeros_like_param(block.cross_norm.weight) if block.cross_norm.weight is not None else None
+        dx1 = K.rmsnorm_mod_bwd(keep["x1"], keep["rstd2"], dn2, _norm_weight(block.cross_norm), dres=dx2,
+                                dweight=g_cross_norm)
+        cross_grads = [g_cross_norm, g_cq, g_ckv[:kv_rows].contiguous(), g_ckv[kv_rows:].contiguous(), g_co,
+                       g_cqn, g_ckn]
+    else:
+        dx1 = dx2
+    # ---------------------------------------------------------------- self attention
+    da = K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], rows_per_batch=length)
+    do = K.linear_dx(da, pw["o"])
+    g_o = zeros_like_param(att.out_proj.weight)
+    K.linear_dw(da, o.view(m, -1), g_o)
+    impl = _attn_impl(spec)
+    dq, dk, dv = impl.backward(inter["q"], inter["k"], inter["v"], o, do.view(b, length, h, d), lse, kmask,
+                               1.0 / math.sqrt(d), attn_state)
+    qw = _norm_weight(att.q_norm) if spec.qk_norm else None
+    kw = _norm_weight(att.k_norm) if spec.qk_norm else None
+    g_qn = zeros_like_param(att.q_norm.weight) if qw is not None else None
+    g_kn = zeros_like_param(att.k_norm.weight) if kw is not None else None
+    dqkv = K.qkv_rope_bwd(inter["qkv"], dq.to(_BF16), dk, dv, batch=b, length=length, heads=h, kv_heads=hk,
+                          head_dim=d, q_weight=qw, k_weight=kw, coords=coords, freq=freq, axis=axis, dq_weight=g_qn,
+                          dk_weight=g_kn, eps=eps)
+    dn1 = K.linear_dx(dqkv, pw["qkv"])
+    g_qkv = torch.zeros((pw["qkv"].shape[0], w), device=dev, dtype=torch.float32)
+    K.linear_dw(dqkv, inter["n1"], g_qkv)
+    g_attn_norm = zeros_like_param(block.attention_norm.weight) if block.attention_norm.weight is not None else None
+    dx = K.rmsnorm_mod_bwd(xb, inter["rstd1"], dn1, _norm_weight(block.attention_norm), modf[:, 1], modf[:, 0],
+                           dres=dx1, dweight=g_attn_norm, dscale=dmod[:, 1], dshift=dmod[:, 0],
+                           rows_per_batch=length)
+    qr, kr = h * d, hk * d
+    pgrads = {
+        "attention_norm.weight": g_attn_norm,
+        "attention.q_proj.weight": g_qkv[:qr].contiguous(),
+        "attention.k_proj.weight": g_qkv[qr:qr + kr].contiguous(),
+        "attention.v_proj.weight": g_qkv[qr + kr:].contiguous(),
+        "attention.out_proj.weight": g_o,
+        "attention.q_norm.weight": g_qn,
+        "attention.k_norm.weight": g_kn,
+        "ffn_norm.weight": g_ffn_norm,
+        "feed_forward.down_proj.weight": g_down,
+        "feed_forward.up_proj.weight": g_up,
+    }
+    if g_gate is not None:
+        pgrads["feed_forward.gate_proj.weight"] = g_gate
+    if cross_grads:
+        names = ["cross_norm.weight", "cross_attention.q_proj.weight", "cross_attention.k_proj.weight",
+                 "cross_attention.v_proj.weight", "cross_attention.out_proj.weight", "cross_attention.q_norm.weight",
+                 "cross_attention.k_norm.weight"]
+        pgrads.update(dict(zip(names, cross_grads)))
+    ordered = [pgrads.get(name) for name in block_param_names(block)]
+    return dx, dmod, dctx, ordered
+
+
+def block_param_names(block: nn.Module) -> list[str]:
+    """Parameter names the fused function takes (excludes the modulation table)."""
+    return [n for n, _ in block.named_parameters() if n != "scale_shift_table"]
+
+
+class FusedBlockFn(torch.autograd.Function):
+    """Autograd node for a whole DiT block."""
+
+    @staticmethod
+    def forward(ctx, spec, block, coords, freq, axis, kmask, cmask, x, mod, context, *params):  # noqa: ANN001, ANN205
+        b, length, w = spec.batch, spec.length, spec.width
+        m = b * length
+        xb = x.reshape(m, w).to(_BF16).contiguous()
+        modf = mod.detach().float().contiguous()
+        ctxb = context.detach().to(_BF16).contiguous() if context is not None else None
+        pw = packed_weights(block)
+        x3, (o, lse, attn_state) = _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask)
+        ctx.spec = spec
+        ctx.block = block
+        ctx.attn_state = attn_state
+        ctx.flags = (coords is not None, kmask is not None, cmask is not None, ctxb is not None)
+        empty = torch.empty(0)
+        ctx.save_for_backward(xb, modf, ctxb if ctxb is not None else empty, o, lse,
+                              coords if coords is not None else empty, freq if freq is not None else empty,
+                              axis if axis is not None else empty, kmask if kmask is not None else empty,
+                              cmask if cmask is not None else empty)
+        ctx.x_dtype = x.dtype
+        ctx.ctx_dtype = context.dtype if context is not None else None
+        return x3.view(b, length, w).to(x.dtype)
+
+    @staticmethod
+    def backward(ctx, dout):  # noqa: ANN001, ANN205
+        xb, modf, ctxb, o, lse, coords, freq, axis, kmask, cmask = ctx.saved_tensors
+        has_coords, has_kmask, has_cmask, has_ctx = ctx.flags
+        dx, dmod, dctx, pgrads = _backward_impl(
+            ctx.spec, ctx.block, xb, modf, ctxb if has_ctx else None, coords if has_coords else None,
+            freq if has_coords else None, axis if has_coords else None, kmask if has_kmask else None,
+            cmask if has_cmask else None, o, lse, ctx.attn_state, dout)
+        if dctx is not None and ctx.ctx_dtype is not None:
+            dctx = dctx.to(ctx.ctx_dtype)
+        return (None, None, None, None, None, None, None, dx.view_as(dout).to(ctx.x_dtype), dmod, dctx, *pgrads)
+
+
+def fused_block_forward(block: nn.Module, hidden: torch.Tensor, combined_mod: torch.Tensor, *,
+                        coords: torch.Tensor | None, freq: torch.Tensor | None, axis: torch.Tensor | None,
+                        kmask: torch.Tensor | None, context: torch.Tensor | None, cmask: torch.Tensor | None,
+                        attention_impl: AttentionImpl | None = None) -> torch.Tensor:
+    """Run ``block`` through :class:`FusedBlockFn` (CUDA only)."""
+    b, length, w = hidden.shape
+    att = block.attention
+    ff = block.feed_forward
+    ffn = "swiglu" if hasattr(ff, "gate_proj") else "gelu"
+    hidden_dim = ff.down_proj.weight.shape[1]
+    ca = block.cross_attention
+    spec = BlockSpec(batch=b, length=length, width=w, heads=att.num_heads, kv_heads=att.num_kv_heads,
+                     head_dim=att.head_dim, hidden=hidden_dim, ffn=ffn, eps=block.attention_norm.eps or 1e-6,
+                     qk_norm=isinstance(att.q_norm, nn.RMSNorm), cross=ca is not None and context is not None,
+                     ctx_heads=ca.num_heads if ca is not None else 0,
+                     ctx_kv_heads=ca.num_kv_heads if ca is not None else 0,
+                     text_length=context.shape[1] if context is not None else 0, attention=attention_impl)
+    params = [p for n, p in block.named_parameters() if n != "scale_shift_table"]
+    return FusedBlockFn.apply(spec, block, coords, freq, axis, kmask, cmask, hidden, combined_mod, context, *params)

@@ -1,0 +1,113 @@
+"""Linear layers on the tcgen05 GEMM.
+
+``linear(x, layer)`` runs ``x @ W^T + b`` through the sm_100a GEMM kernel on CUDA
+(bf16 operands, fp32 accumulation, fp32 master weights cast once per optimizer
+step through :func:`bf16_weight`), and through ``F.linear`` on the CPU (the fp32
+oracle). Weight gradients accumulate in fp32 with the GEMM's atomic epilogue.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+from torch import nn
+
+__all__ = ["KernelLinear", "bf16_weight", "bump_weight_epoch", "linear", "weight_epoch"]
+
+_CACHE_ATTR = "_avgen_bf16_cache"
+_EPOCH = [0]
+
+
+def bump_weight_epoch() -> None:
+    """Invalidate every cached bf16 weight copy (called after optimizer kernels
+    update parameters through raw pointers, which does not bump version counters)."""
+    _EPOCH[0] += 1
+
+
+def weight_epoch() -> int:
+    return _EPOCH[0]
+
+
+def bf16_weight(param: torch.Tensor, *, key: str = "w", build=None) -> torch.Tensor:  # noqa: ANN001
+    """A bf16 copy of ``param`` (or of ``build(param)``), rebuilt only when it changes.
+
+    The cache is keyed on the parameter's version counter, which in-place
+    optimizer updates bump, so the cast costs one pass per optimizer step rather
+    than one per forward / recompute.
+    """
+    cache = getattr(param, _CACHE_ATTR, None)
+    if cache is None:
+        cache = {}
+        try:
+            setattr(param, _CACHE_ATTR, cache)
+        except (AttributeError, RuntimeError):
+            pass
+    version = (param._version, param.data_ptr(), tuple(param.shape), _EPOCH[0])
+    hit = cache.get(key)
+    if hit is not None and hit[0] == version:
+        return hit[1]
+    with torch.no_grad():
+        value = build(param) if build is not None else param.detach().to(torch.bfloat16).contiguous()
+    cache[key] = (version, value)
+    return value
+
+
+def _weight_grad_buffer(weight: torch.Tensor) -> torch.Tensor:
+    return torch.zeros(weight.shape, device=weight.device, dtype=torch.float32)
+
+
+class KernelLinear(torch.autograd.Function):
+    """``y = x W^T + b`` on the tcgen05 GEMM with fp32 weight-gradient accumulation."""
+
+    @staticmethod
+    def forward(ctx, x, weight, bias):  # noqa: ANN001, ANN205
+        from avgen_b200.ops import kernels as K
+
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        w = bf16_weight(weight)
+        b = bias.detach().float().contiguous() if bias is not None else None
+        y = K.gemm(x2, w, bias=b)
+        ctx.save_for_backward(x2, weight)
+        ctx.has_bias = bias is not None
+        ctx.in_dtype = x.dtype
+        ctx.shape = shape
+        return y.view(*shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        from avgen_b200.ops import kernels as K
+
+        x2, weight = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1]).to(torch.bfloat16).contiguous()
+        dx = dw = db = None
+        if ctx.needs_input_grad[0]:
+            dx = K.linear_dx(dy2, bf16_weight(weight)).view(*ctx.shape).to(ctx.in_dtype)
+        if ctx.needs_input_grad[1]:
+            dw = _weight_grad_buffer(weight)
+            K.linear_dw(dy2, x2, dw)
+            dw = dw.to(weight.dtype)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = dy2.float().sum(0)
+        return dx, dw, db
+
+
+def _kernel_ok(x: torch.Tensor, layer: nn.Linear) -> bool:
+    return (x.device.type == "cuda" and layer.in_features % 8 == 0 and layer.out_features % 8 == 0
+            and x.numel() > 0)
+
+
+def linear(x: torch.Tensor, layer: nn.Linear) -> torch.Tensor:
+    """Apply ``layer`` with the sm_100a GEMM on CUDA (bf16 output), ``F.linear`` on CPU."""
+    if _kernel_ok(x, layer):
+        return KernelLinear.apply(x, layer.weight, layer.bias)
+    if x.device.type == "cuda":
+        raise NotImplementedError(
+            f"linear {layer.in_features}->{layer.out_features}: the GEMM kernel needs feature sizes that are "
+            "multiples of 8"
+        )
+    w = layer.weight
+    b = layer.bias
+    if w.dtype != x.dtype:
+        w = w.to(x.dtype)
+        b = b.to(x.dtype) if b is not None else None
+    return F.linear(x, w, b)

@@ -20,6 +20,18 @@ from avgen_b200.ops._ext import load
 
 EPILOGUES = {"store": 0, "gate_resid": 1, "swiglu": 2, "gelu": 3, "atomic": 4}
 
+# Running count of kernel launches issued through this module (benchmarks read it).
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
+
+def launch_count() -> int:
+    """Kernels launched through :mod:`avgen_b200.ops.kernels` so far in this process."""
+    return LAUNCHES[0]
+
 _BF16 = torch.bfloat16
 _F32 = torch.float32
 
@@ -52,6 +64,7 @@ def gemm(
     load().gemm(
         a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits
     )
+    _count()
     return out
 
 
@@ -90,6 +103,7 @@ def rmsnorm_mod(
     y = out if out is not None else torch.empty_like(x)
     rstd = torch.empty(x.shape[0], device=x.device, dtype=_F32) if want_rstd else None
     load().rmsnorm_mod_fwd(x, y, rstd, weight, scale, shift, rows_per_batch, eps)
+    _count()
     return y, rstd
 
 
@@ -113,6 +127,7 @@ def rmsnorm_mod_bwd(
     load().rmsnorm_mod_bwd(
         x, rstd, dy, dx, dres, weight, scale, shift, dweight, dscale, dshift, rows_per_batch
     )
+    _count(2 if (dweight is not None or dscale is not None or dshift is not None) else 1)
     return dx
 
 
@@ -122,6 +137,7 @@ def gate_bwd(
     """``da = dx * gate[b]`` and ``dgate[b] += sum_rows(dx * a)``."""
     da = torch.empty_like(dx)
     load().gate_bwd(dx, a, gate, da, dgate, rows_per_batch)
+    _count()
     return da
 
 
@@ -189,6 +205,7 @@ def qkv_rope(
     load().qkv_rope_fwd(
         qkv, batch, length, heads, kv_heads, head_dim, eps, q_weight, k_weight, coords, freq, axis, q, k, v
     )
+    _count()
     return q, k, v
 
 
@@ -218,6 +235,7 @@ def qkv_rope_bwd(
         qkv, dqkv, batch, length, heads, kv_heads, head_dim, eps, q_weight, k_weight, coords, freq, axis,
         dq, dk, dv, dq_weight, dk_weight,
     )
+    _count()
     return dqkv
 
 
@@ -253,6 +271,7 @@ def attention_fwd(
         out = torch.empty((b, lq, h, d), device=q.device, dtype=_BF16)
     lse = torch.empty((b, h, lq), device=q.device, dtype=_F32) if want_lse else None
     load().attn_fwd(q, k, v, out, lse, kmask, scale)
+    _count()
     return out, lse
 
 
@@ -275,6 +294,7 @@ def attention_bwd(
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     load().attn_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, kmask, scale)
+    _count(2)
     return dq, dk, dv
 
 
@@ -282,6 +302,7 @@ def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
     """Backward of the interleaved SwiGLU epilogue: returns ``dgu`` like ``gu``."""
     dgu = torch.empty_like(gu)
     load().swiglu_bwd(dh, gu, dgu)
+    _count()
     return dgu
 
 
@@ -289,6 +310,7 @@ def gelu_bwd(dh: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
     """Backward of GELU(tanh): returns the gradient w.r.t. the pre-activation."""
     dpre = torch.empty_like(pre)
     load().gelu_bwd(dh, pre, dpre)
+    _count()
     return dpre
 
 
@@ -303,6 +325,7 @@ def flow_loss_stats(
     """``[sum(w*mse*m), sum(mse*m), sum(m)]`` over token rows (fp32, device)."""
     stats = torch.zeros(3, device=pred.device, dtype=_F32)
     load().flow_loss_fwd(pred.contiguous(), target.contiguous(), loss_mask.contiguous(), weight, rows_per_batch, stats)
+    _count()
     return stats
 
 
@@ -320,6 +343,7 @@ def flow_loss_grad(
     dpred = torch.empty(pred.shape, device=pred.device, dtype=out_dtype or pred.dtype)
     load().flow_loss_bwd(pred.contiguous(), target.contiguous(), loss_mask.contiguous(), weight, rows_per_batch,
                          scale, dpred)
+    _count()
     return dpred
 
 
@@ -344,6 +368,7 @@ def noise_interp(
     del rows
     load().noise_interp(clean.contiguous(), t.contiguous(), seed & ((1 << 63) - 1), offset, row_base, rps, grps,
                         noisy, target, noise)
+    _count()
     return noisy, target, noise
 
 
@@ -365,14 +390,17 @@ def adamw_step(
     """Fused AdamW over flat fp32 buffers (optionally writing a bf16 copy)."""
     load().adamw(param, grad, exp_avg, exp_avg_sq, lr, betas[0], betas[1], eps, weight_decay, step, param_bf16,
                  grad_scale, skip)
+    _count()
 
 
 def sq_norm_(x: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
     """``out += sum(x ** 2)`` for a flat fp32 buffer."""
     load().sq_norm(x, out)
+    _count()
     return out
 
 
 def ema_(param: torch.Tensor, shadow: torch.Tensor, decay: float) -> None:
     """``shadow += (1 - decay) * (param - shadow)``."""
     load().ema(param, shadow, decay)
+    _count()

@@ -1,0 +1,233 @@
+"""Context parallelism: contiguous sequence sharding and global attention over shards.
+
+Sharding (avgen/parallel/context.py:58-229): the token axis is split into
+contiguous equal shards (balanced because attention is bidirectional);
+``pad_to_multiple`` makes padding explicit and masked; ``gather_stream`` /
+``gather_tokens`` reassemble.
+
+Unlike the reference, whose ``context_parallel_region`` is never entered (each
+rank attends only within its shard), attention here is global:
+
+* :class:`ContextParallelAttention` is the fused-block implementation on
+  B200s: every rank's K/V shard is exchanged over NVLink and the local queries
+  attend to the whole sequence with the tcgen05 flash kernels; backward
+  reduce-scatters dK/dV back to their owners.
+* :func:`cp_attention` is the eager / CPU path (gloo): K/V all-gathered with
+  autograd, then the reference attention; it is the oracle for the fused path.
+"""
+from __future__ import annotations
+
+from collections.abc import Iterator, Sequence
+from contextlib import contextmanager, nullcontext
+from dataclasses import replace
+
+import torch
+import torch.distributed as dist
+from torch.distributed.device_mesh import DeviceMesh
+
+from avgen_b200.core.tokens import TokenStream
+
+__all__ = ["ContextParallelAttention", "context_parallel_region", "cp_attention", "gather_stream", "gather_tokens",
+           "maybe_context_parallel", "pad_to_multiple", "shard_bounds", "shard_stream", "sharded_length"]
+
+
+def sharded_length(total: int, shards: int) -> int:
+    if total % shards:
+        raise ValueError(f"sequence length {total} is not divisible by context-parallel degree {shards}; pad with "
+                         "pad_to_multiple() at the data boundary so the padding is explicit and masked")
+    return total // shards
+
+
+def shard_bounds(total: int, shards: int, index: int) -> tuple[int, int]:
+    local = sharded_length(total, shards)
+    return index * local, (index + 1) * local
+
+
+def pad_to_multiple(stream: TokenStream, multiple: int) -> TokenStream:
+    """Pad the token axis with masked, unconditioned, zero tokens to a multiple."""
+    if multiple < 1:
+        raise ValueError(f"multiple must be positive; got {multiple!r}")
+    rem = stream.length % multiple
+    if rem == 0:
+        return stream
+    pad = multiple - rem
+    b = stream.batch_size
+
+    def padt(t: torch.Tensor) -> torch.Tensor:
+        shape = list(t.shape)
+        shape[1] = pad
+        return torch.cat((t, torch.zeros(shape, dtype=t.dtype, device=t.device)), 1)
+
+    noise = padt(stream.noise_level) if stream.per_token_noise else stream.noise_level
+    return TokenStream(tokens=padt(stream.tokens), coords=padt(stream.coords), mask=padt(stream.mask),
+                       noise_level=noise, layout=stream.layout, conditioned=padt(stream.conditioned))
+
+
+def _cp(mesh: DeviceMesh | None) -> tuple[int, int]:
+    if mesh is None or mesh.size() == 1:
+        return 0, 1
+    return mesh.get_local_rank(), mesh.size()
+
+
+def shard_stream(stream: TokenStream, mesh: DeviceMesh | None) -> TokenStream:
+    """This rank's contiguous shard of a stream."""
+    index, shards = _cp(mesh)
+    if shards == 1:
+        return stream
+    lo, hi = shard_bounds(stream.length, shards, index)
+    noise = stream.noise_level[:, lo:hi] if stream.per_token_noise else stream.noise_level
+    return replace(stream, tokens=stream.tokens[:, lo:hi], coords=stream.coords[:, lo:hi], mask=stream.mask[:, lo:hi],
+                   noise_level=noise, conditioned=stream.conditioned[:, lo:hi])
+
+
+def _gather_dim1(t: torch.Tensor, mesh: DeviceMesh) -> torch.Tensor:
+    parts = [torch.empty_like(t) for _ in range(mesh.size())]
+    dist.all_gather(parts, t.contiguous(), group=mesh.get_group())
+    return torch.cat(parts, 1)
+
+
+def gather_stream(stream: TokenStream, mesh: DeviceMesh | None) -> TokenStream:
+    if mesh is None or mesh.size() == 1 or not (dist.is_available() and dist.is_initialized()):
+        return stream
+    noise = _gather_dim1(stream.noise_level, mesh) if stream.per_token_noise else stream.noise_level
+    return replace(stream, tokens=_gather_dim1(stream.tokens, mesh), coords=_gather_dim1(stream.coords, mesh),
+                   mask=_gather_dim1(stream.mask, mesh), noise_level=noise,
+                   conditioned=_gather_dim1(stream.conditioned, mesh))
+
+
+def gather_tokens(tensor: torch.Tensor, mesh: DeviceMesh | None) -> torch.Tensor:
+    if mesh is None or mesh.size() == 1 or not (dist.is_available() and dist.is_initialized()):
+        return tensor
+    return _gather_dim1(tensor, mesh)
+
+
+class _AllGatherSeq(torch.autograd.Function):
+    """All-gather along the sequence axis (dim 2 of [B, H, L, D]); backward reduce-scatters."""
+
+    @staticmethod
+    def forward(ctx, x: torch.Tensor, group) -> torch.Tensor:  # noqa: ANN001, ANN205
+        world = dist.get_world_size(group)
+        parts = [torch.empty_like(x) for _ in range(world)]
+        dist.all_gather(parts, x.contiguous(), group=group)
+        ctx.group = group
+        ctx.world = world
+        ctx.rank = dist.get_rank(group)
+        return torch.cat(parts, 2)
+
+    @staticmethod
+    def backward(ctx, grad: torch.Tensor):  # noqa: ANN205
+        chunks = [c.contiguous() for c in grad.chunk(ctx.world, 2)]
+        out = torch.empty_like(chunks[0])
+        if grad.device.type == "cpu":
+            # gloo has no reduce_scatter: all-reduce then slice.
+            full = grad.contiguous().clone()
+            dist.all_reduce(full, group=ctx.group)
+            out = full.chunk(ctx.world, 2)[ctx.rank].contiguous()
+        else:
+            dist.reduce_scatter(out, chunks, group=ctx.group)
+        return out, None
+
+
+def cp_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, mesh: DeviceMesh | None,
+                 key_mask: torch.Tensor | None = None, scale: float | None = None) -> torch.Tensor:
+    """Global attention for sequence-sharded q/k/v ``[B, H, L_local, D]`` (returns ``[B, H, L_local, D]``).
+
+    ``key_mask`` is the *global* ``(B, L_global)`` key validity (or ``None``).
+    """
+    from avgen_b200.models.attention import attention
+
+    if mesh is None or mesh.size() == 1:
+        return attention(q, k, v, key_mask=key_mask, scale=scale)
+    group = mesh.get_group()
+    kf = _AllGatherSeq.apply(k, group)
+    vf = _AllGatherSeq.apply(v, group)
+    return attention(q, kf, vf, key_mask=key_mask, scale=scale)
+
+
+class ContextParallelAttention:
+    """Fused-block self-attention over a context-parallel group.
+
+    Forward exchanges K/V shards over NVLink (NCCL all-gather into one
+    ``[B, Hk, L_global, D]`` buffer) and runs the tcgen05 flash kernel with the
+    local queries against the whole sequence; backward runs the flash backward
+    against the same buffer and reduce-scatters dK/dV to their owners.
+    """
+
+    def __init__(self, mesh: DeviceMesh) -> None:
+        self.mesh = mesh
+        self.group = mesh.get_group()
+        self.world = mesh.size()
+
+    def _gather(self, t: torch.Tensor) -> torch.Tensor:
+        b, h, length, d = t.shape
+        buf = torch.empty((self.world, b, h, length, d), device=t.device, dtype=t.dtype)
+        dist.all_gather_into_tensor(buf, t.contiguous(), group=self.group)
+        return buf.permute(1, 2, 0, 3, 4).reshape(b, h, self.world * length, d)
+
+    def forward(self, q, k, v, kmask, scale):  # noqa: ANN001, ANN201
+        from avgen_b200.ops import kernels as K
+
+        kf = self._gather(k)
+        vf = self._gather(v)
+        out, lse = K.attention_fwd(q, kf, vf, kmask=kmask, scale=scale)
+        return out, lse, (kf, vf)
+
+    def backward(self, q, k, v, o, do, lse, kmask, scale, state):  # noqa: ANN001, ANN201
+        from avgen_b200.ops import kernels as K
+
+        kf, vf = state
+        dq, dkf, dvf = K.attention_bwd(q, kf, vf, o, do, lse, kmask=kmask, scale=scale)
+        b, h, length, d = k.shape
+
+        def scatter(full: torch.Tensor) -> torch.Tensor:
+            parts = full.view(b, h, self.world, length, d).permute(2, 0, 1, 3, 4).contiguous()
+            out = torch.empty((b, h, length, d), device=full.device, dtype=full.dtype)
+            dist.reduce_scatter_tensor(out, parts, group=self.group)
+            return out
+
+        return dq, scatter(dkf), scatter(dvf)
+
+
+@contextmanager
+def context_parallel_region(mesh: DeviceMesh | None, *, buffers: Sequence[torch.Tensor] | None = None,
+                            buffer_seq_dims: Sequence[int] | None = None) -> Iterator[None]:
+    """Compatibility region: attention in this framework is always global under CP,
+    so entering the region only validates its arguments."""
+    if buffers is not None and buffer_seq_dims is not None and len(buffers) != len(buffer_seq_dims):
+        raise ValueError("buffers and buffer_seq_dims must have the same length")
+    del mesh
+    yield
+
+
+def maybe_context_parallel(mesh: DeviceMesh | None, **kwargs: object):  # noqa: ANN201
+    if mesh is None or mesh.size() == 1:
+        return nullcontext()
+    return context_parallel_region(mesh, **kwargs)
+
+
+def apply_context_parallel(model: torch.nn.Module, mesh: DeviceMesh | None) -> torch.nn.Module:
+    """Make every self-attention of ``model`` global over the CP group ``mesh``.
+
+    Fused DiT blocks get :class:`ContextParallelAttention`; eager
+    ``SelfAttention`` modules get the all-gather attention; the model gathers
+    key masks across shards.
+    """
+    if mesh is None or mesh.size() == 1:
+        return model
+    from avgen_b200.models.blocks import DiTBlock
+    from avgen_b200.models.layers import SelfAttention
+
+    impl = ContextParallelAttention(mesh)
+    for module in model.modules():
+        if isinstance(module, DiTBlock):
+            module.attention_impl = impl
+        if isinstance(module, SelfAttention):
+            module.cp_mesh = mesh
+    model.cp_mesh = mesh
+    # text-refiner self-attention runs on replicated text tokens: keep it local
+    for refiner in getattr(model, "text_refiner", []):
+        refiner.attention.cp_mesh = None
+    return model
+
+
+__all__ += ["apply_context_parallel"]

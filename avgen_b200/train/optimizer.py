@@ -1,0 +1,255 @@
+"""Optimizers: AdamW on flat fp32 buffers (sm_100a kernel), plus the reference set.
+
+``build_optimizer`` keeps the reference contract (avgen/train/optimizer.py:68-222):
+decay / no-decay groups (ndim <= 1 or a name containing norm / bias /
+scale_shift / embed), names ``adamw`` / ``adamw_8bit`` / ``adafactor``.
+
+On CUDA, ``adamw`` is :class:`FusedAdamW`: each parameter group's parameters and
+gradients are re-homed into one contiguous fp32 buffer (parameters become views,
+so ``state_dict`` / DCP see ordinary per-parameter tensors), and a step is
+
+1. an optional average of the flat gradients over the data-parallel group
+   (one NCCL all-reduce per group),
+2. one squared-norm kernel per group, the clip coefficient and the non-finite
+   flag computed on the device (no host sync),
+3. one fused AdamW kernel per group that also treats a non-finite step's
+   gradients as zero (the reference's ``_neutralise_nonfinite`` semantics).
+"""
+from __future__ import annotations
+
+import math
+from collections.abc import Iterable, Sequence
+from typing import Any
+
+import torch
+import torch.distributed as dist
+from torch import nn
+from torch.optim import Optimizer
+
+__all__ = ["DEFAULT_NO_DECAY_PATTERNS", "FusedAdamW", "build_optimizer", "build_param_groups", "list_optimizers"]
+
+DEFAULT_NO_DECAY_PATTERNS: tuple[str, ...] = ("norm", "bias", "scale_shift", "embed")
+_OPTIMIZERS = ("adafactor", "adamw", "adamw_8bit")
+_ALIGN = 4  # fp32 elements: keeps every view 16-byte aligned for the vector kernels
+
+
+def list_optimizers() -> tuple[str, ...]:
+    return _OPTIMIZERS
+
+
+def build_param_groups(model: nn.Module, *, weight_decay: float,
+                       no_decay_patterns: Sequence[str] = DEFAULT_NO_DECAY_PATTERNS) -> list[dict[str, Any]]:
+    patterns = tuple(p.lower() for p in no_decay_patterns)
+    decayed: list[nn.Parameter] = []
+    undecayed: list[nn.Parameter] = []
+    for name, p in model.named_parameters():
+        if not p.requires_grad:
+            continue
+        if p.ndim <= 1 or any(pat in name.lower() for pat in patterns):
+            undecayed.append(p)
+        else:
+            decayed.append(p)
+    if not decayed and not undecayed:
+        raise ValueError("model has no trainable parameters")
+    groups = []
+    if decayed:
+        groups.append({"params": decayed, "weight_decay": weight_decay})
+    if undecayed:
+        groups.append({"params": undecayed, "weight_decay": 0.0})
+    return groups
+
+
+class FusedAdamW(Optimizer):
+    """AdamW over per-group flat fp32 buffers with the sm_100a fused kernel."""
+
+    def __init__(self, params: Iterable[Any], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.95),
+                 eps: float = 1e-8, weight_decay: float = 0.0, *, dp_group: Any = None) -> None:
+        defaults = {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay}
+        super().__init__(params, defaults)
+        self.dp_group = dp_group
+        self.max_grad_norm: float | None = None
+        self._flat: list[dict[str, torch.Tensor]] = []
+        self._step = 0
+        self.last_grad_norm: torch.Tensor | None = None
+        self.last_nonfinite: torch.Tensor | None = None
+        for group in self.param_groups:
+            self._flat.append(self._flatten(group))
+
+    # ------------------------------------------------------------------ layout
+    @staticmethod
+    def _flatten(group: dict[str, Any]) -> dict[str, torch.Tensor]:
+        params: list[torch.Tensor] = group["params"]
+        if not params:
+            raise ValueError("empty parameter group")
+        dev = params[0].device
+        offsets = []
+        total = 0
+        for p in params:
+            if p.device != dev:
+                raise ValueError("all parameters of a group must share a device")
+            offsets.append(total)
+            total += -(-p.numel() // _ALIGN) * _ALIGN
+        flat_p = torch.zeros(total, device=dev, dtype=torch.float32)
+        flat_g = torch.zeros(total, device=dev, dtype=torch.float32)
+        with torch.no_grad():
+            for p, off in zip(params, offsets):
+                n = p.numel()
+                flat_p[off:off + n].copy_(p.detach().reshape(-1).float())
+                p.data = flat_p[off:off + n].view(p.shape)
+                p.grad = flat_g[off:off + n].view(p.shape)
+        return {"param": flat_p, "grad": flat_g, "exp_avg": torch.zeros_like(flat_p),
+                "exp_avg_sq": torch.zeros_like(flat_p), "offsets": torch.tensor(offsets)}
+
+    def flat_buffers(self) -> list[dict[str, torch.Tensor]]:
+        """Per-group flat buffers (``param``, ``grad``, ``exp_avg``, ``exp_avg_sq``)."""
+        return self._flat
+
+    @property
+    def state(self) -> dict:  # type: ignore[override]
+        """Per-parameter views of the flat moments (torch AdamW state layout)."""
+        out: dict = {}
+        for group, flat in zip(self.param_groups, getattr(self, "_flat", [])):
+            for p, off in zip(group["params"], flat["offsets"].tolist()):
+                n = p.numel()
+                out[p] = {"step": torch.tensor(float(self._step)),
+                          "exp_avg": flat["exp_avg"][off:off + n].view(p.shape),
+                          "exp_avg_sq": flat["exp_avg_sq"][off:off + n].view(p.shape)}
+        return out
+
+    @state.setter
+    def state(self, value: dict) -> None:  # torch.optim.Optimizer.__init__ assigns a defaultdict
+        if not getattr(self, "_flat", None):
+            return
+        for group, flat in zip(self.param_groups, self._flat):
+            for p, off in zip(group["params"], flat["offsets"].tolist()):
+                st = value.get(p)
+                if not st:
+                    continue
+                n = p.numel()
+                with torch.no_grad():
+                    flat["exp_avg"][off:off + n].copy_(st["exp_avg"].reshape(-1))
+                    flat["exp_avg_sq"][off:off + n].copy_(st["exp_avg_sq"].reshape(-1))
+                self._step = int(float(st.get("step", self._step)))
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        """Load torch-AdamW-format state into the flat buffers."""
+        groups = state_dict["param_groups"]
+        if len(groups) != len(self.param_groups):
+            raise ValueError("loaded state has a different number of parameter groups")
+        index = {}
+        for g_saved, g in zip(groups, self.param_groups):
+            for pid, p in zip(g_saved["params"], g["params"]):
+                index[pid] = p
+            for key in ("lr", "betas", "eps", "weight_decay"):
+                if key in g_saved:
+                    g[key] = g_saved[key]
+        mapped = {index[k]: v for k, v in state_dict["state"].items() if k in index}
+        self.state = mapped
+
+    # ------------------------------------------------------------------ step
+    def zero_grad(self, set_to_none: bool = True) -> None:  # noqa: ARG002 - the flat views must persist
+        for flat in self._flat:
+            flat["grad"].zero_()
+        for group, flat in zip(self.param_groups, self._flat):
+            for p, off in zip(group["params"], flat["offsets"].tolist()):
+                if p.grad is None or p.grad.data_ptr() != flat["grad"][off:].data_ptr():
+                    p.grad = flat["grad"][off:off + p.numel()].view(p.shape)
+
+    def grad_norm(self) -> torch.Tensor:
+        """Global L2 norm of all gradients (device scalar, no host sync)."""
+        from avgen_b200.ops import kernels as K
+
+        acc = torch.zeros(1, device=self._flat[0]["grad"].device, dtype=torch.float32)
+        for flat in self._flat:
+            if flat["grad"].device.type == "cuda":
+                K.sq_norm_(flat["grad"], acc)
+            else:
+                acc += flat["grad"].pow(2).sum()
+        return acc.sqrt()[0]
+
+    def sync_gradients(self) -> None:
+        """Average flat gradients over the data-parallel group (if any)."""
+        if self.dp_group is None or not dist.is_initialized() or dist.get_world_size(self.dp_group) == 1:
+            return
+        world = dist.get_world_size(self.dp_group)
+        for flat in self._flat:
+            g = flat["grad"]
+            if g.device.type == "cuda":
+                dist.all_reduce(g, op=dist.ReduceOp.AVG, group=self.dp_group)
+            else:
+                dist.all_reduce(g, group=self.dp_group)
+                g.div_(world)
+
+    @torch.no_grad()
+    def step(self, closure: Any = None, *, max_grad_norm: float | None = None) -> Any:
+        """One AdamW step; clips by ``max_grad_norm`` (argument or attribute) on the device."""
+        loss = closure() if closure is not None else None
+        from avgen_b200.models.linear import bump_weight_epoch
+
+        self.sync_gradients()
+        self._step += 1
+        norm = self.grad_norm()
+        nonfinite = ~torch.isfinite(norm)
+        clip = max_grad_norm if max_grad_norm is not None else self.max_grad_norm
+        if clip is not None:
+            scale = torch.clamp(clip / (norm + 1e-6), max=1.0)
+        else:
+            scale = torch.ones_like(norm)
+        scale = torch.where(nonfinite, torch.zeros_like(scale), scale).reshape(1)
+        skip = nonfinite.to(torch.int32).reshape(1)
+        self.last_grad_norm = norm
+        self.last_nonfinite = nonfinite
+        for group, flat in zip(self.param_groups, self._flat):
+            beta1, beta2 = group["betas"]
+            if flat["param"].device.type == "cuda":
+                from avgen_b200.ops import kernels as K
+
+                K.adamw_step(flat["param"], flat["grad"], flat["exp_avg"], flat["exp_avg_sq"], lr=group["lr"],
+                             betas=(beta1, beta2), eps=group["eps"], weight_decay=group["weight_decay"],
+                             step=self._step, grad_scale=scale, skip=skip)
+            else:
+                _adamw_reference(flat, lr=group["lr"], beta1=beta1, beta2=beta2, eps=group["eps"],
+                                 weight_decay=group["weight_decay"], step=self._step, scale=scale, nonfinite=nonfinite)
+        bump_weight_epoch()
+        return loss
+
+
+def _adamw_reference(flat: dict[str, torch.Tensor], *, lr: float, beta1: float, beta2: float, eps: float,
+                     weight_decay: float, step: int, scale: torch.Tensor, nonfinite: torch.Tensor) -> None:
+    """CPU fp32 AdamW over a flat buffer (same maths as the kernel)."""
+    g = torch.where(nonfinite, torch.zeros_like(flat["grad"]), flat["grad"] * scale)
+    flat["exp_avg"].mul_(beta1).add_(g, alpha=1 - beta1)
+    flat["exp_avg_sq"].mul_(beta2).addcmul_(g, g, value=1 - beta2)
+    bc1 = 1 - beta1 ** step
+    bc2 = math.sqrt(1 - beta2 ** step)
+    denom = flat["exp_avg_sq"].sqrt() / bc2 + eps
+    flat["param"].mul_(1 - lr * weight_decay).addcdiv_(flat["exp_avg"], denom, value=-lr / bc1)
+
+
+def build_optimizer(model: nn.Module, *, name: str = "adamw", lr: float, weight_decay: float = 0.0,
+                    betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8, fused: bool | None = None,
+                    no_decay_patterns: Sequence[str] = DEFAULT_NO_DECAY_PATTERNS, dp_group: Any = None) -> Optimizer:
+    if lr <= 0.0:
+        raise ValueError(f"lr must be positive; got {lr!r}")
+    if weight_decay < 0.0:
+        raise ValueError("weight_decay must be non-negative")
+    if not all(0.0 <= b < 1.0 for b in betas):
+        raise ValueError(f"betas must lie in [0, 1); got {betas!r}")
+    if eps <= 0.0:
+        raise ValueError("eps must be positive")
+    groups = build_param_groups(model, weight_decay=weight_decay, no_decay_patterns=no_decay_patterns)
+    if name == "adamw":
+        on_cuda = all(p.device.type == "cuda" for g in groups for p in g["params"])
+        use_fused = on_cuda if fused is None else fused
+        if use_fused:
+            return FusedAdamW(groups, lr=lr, betas=betas, eps=eps, dp_group=dp_group)
+        return torch.optim.AdamW(groups, lr=lr, betas=betas, eps=eps)
+    if name == "adamw_8bit":
+        try:
+            import bitsandbytes
+        except ImportError as exc:
+            raise RuntimeError("the 'adamw_8bit' optimizer requires bitsandbytes") from exc
+        return bitsandbytes.optim.AdamW8bit(list(groups), lr=lr, betas=betas, eps=eps)
+    if name == "adafactor":
+        return torch.optim.Adafactor(groups, lr=lr, beta2_decay=-0.8, eps=(None, eps), weight_decay=weight_decay)
+    raise ValueError(f"unknown optimizer {name!r}; available: {', '.join(_OPTIMIZERS)}")

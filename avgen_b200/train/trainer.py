@@ -1,0 +1,299 @@
+"""Functional train step and the Trainer loop (avgen/train/trainer.py:169-683).
+
+``train_step``: zero grads on the first micro-step, gradient sync only on the
+last, loss / accumulation backward, then on the last micro-step clip by the
+global norm, neutralise a non-finite step without any collective (its
+gradients count as zero, so ranks never desync or deadlock), optimizer,
+schedule and EMA steps, progress counters. With :class:`FusedAdamW` the norm,
+clip coefficient and non-finite flag never leave the device.
+"""
+from __future__ import annotations
+
+import logging
+from collections.abc import Iterable, Iterator, Sequence
+from contextlib import nullcontext
+from dataclasses import dataclass, field
+from typing import Any, Protocol, runtime_checkable
+
+import torch
+from torch.distributed.device_mesh import DeviceMesh
+
+from avgen_b200.core._validate import require_name, require_positive
+from avgen_b200.core.batch import MediaBatch
+from avgen_b200.core.metrics import StepMetrics
+from avgen_b200.core.patchify import GridPatchifier, Patchifier
+from avgen_b200.core.state import TrainState
+from avgen_b200.train.objective import Objective, ObjectiveOutput
+from avgen_b200.train.optimizer import FusedAdamW
+
+__all__ = ["Curriculum", "CurriculumStage", "MetricSink", "ResolutionBucket", "Trainer", "TrainerCallback",
+           "TrainerConfig", "train_step"]
+
+_LOG = logging.getLogger("avgen_b200.train")
+
+
+@runtime_checkable
+class MetricSink(Protocol):
+    def log_metrics(self, metrics: dict[str, float], step: int) -> None: ...
+
+
+@runtime_checkable
+class TrainerCallback(Protocol):
+    def on_step_end(self, trainer: Trainer, state: TrainState, metrics: StepMetrics) -> None: ...
+
+    def on_checkpoint(self, trainer: Trainer, state: TrainState) -> None: ...
+
+    def on_eval(self, trainer: Trainer, state: TrainState) -> None: ...
+
+
+@dataclass(frozen=True, slots=True)
+class ResolutionBucket:
+    name: str
+    frames: int
+    height: int
+    width: int
+
+    def __post_init__(self) -> None:
+        require_name("name", self.name)
+        for f in ("frames", "height", "width"):
+            require_positive(f, getattr(self, f))
+
+    @property
+    def latents(self) -> int:
+        return self.frames * self.height * self.width
+
+
+@dataclass(frozen=True, slots=True)
+class CurriculumStage:
+    name: str
+    until_step: int
+    buckets: tuple[tuple[ResolutionBucket, float], ...]
+
+    def __post_init__(self) -> None:
+        require_name("name", self.name)
+        require_positive("until_step", self.until_step)
+        if not self.buckets:
+            raise ValueError(f"stage {self.name!r} must declare at least one bucket")
+        if sum(w for _, w in self.buckets) <= 0.0:
+            raise ValueError(f"stage {self.name!r} must have a positive total weight")
+        if any(w < 0 for _, w in self.buckets):
+            raise ValueError(f"stage {self.name!r} has a negative weight")
+
+
+@dataclass(frozen=True, slots=True)
+class Curriculum:
+    stages: tuple[CurriculumStage, ...] = ()
+
+    def __post_init__(self) -> None:
+        bounds = [s.until_step for s in self.stages]
+        if bounds != sorted(set(bounds)):
+            raise ValueError(f"curriculum stages must have strictly increasing until_step; got {bounds}")
+
+    @property
+    def is_empty(self) -> bool:
+        return not self.stages
+
+    def stage_for(self, step: int) -> CurriculumStage | None:
+        if not self.stages:
+            return None
+        for s in self.stages:
+            if step < s.until_step:
+                return s
+        return self.stages[-1]
+
+
+@dataclass(frozen=True, slots=True)
+class TrainerConfig:
+    gradient_accumulation_steps: int = 1
+    max_grad_norm: float | None = 1.0
+    log_every: int = 10
+    eval_every: int = 0
+    checkpoint_every: int = 0
+    autocast_dtype: str = "bfloat16"
+    curriculum: Curriculum = field(default_factory=Curriculum)
+    data_world: int = 1
+
+    def __post_init__(self) -> None:
+        require_positive("gradient_accumulation_steps", self.gradient_accumulation_steps)
+        require_positive("log_every", self.log_every)
+        require_positive("data_world", self.data_world)
+        for name in ("eval_every", "checkpoint_every"):
+            v = getattr(self, name)
+            if isinstance(v, bool) or v < 0:
+                raise ValueError(f"{name} must be non-negative")
+        if self.max_grad_norm is not None and self.max_grad_norm <= 0.0:
+            raise ValueError("max_grad_norm must be positive or None")
+        if not isinstance(getattr(torch, self.autocast_dtype, None), torch.dtype):
+            raise ValueError(f"unknown autocast dtype {self.autocast_dtype!r}")
+
+    @property
+    def torch_autocast_dtype(self) -> torch.dtype:
+        return getattr(torch, self.autocast_dtype)
+
+
+def _native(model: torch.nn.Module) -> bool:
+    from avgen_b200.models.dit import VideoDiT
+
+    inner = getattr(model, "module", model)
+    return isinstance(inner, VideoDiT)
+
+
+def _autocast(model: torch.nn.Module, device: torch.device, dtype: torch.dtype) -> Any:
+    # Native models pick bf16 per op themselves (fp32 coords and statistics stay fp32).
+    if device.type != "cuda" or _native(model):
+        return nullcontext()
+    return torch.autocast(device_type="cuda", dtype=dtype)
+
+
+def _set_gradient_sync(model: torch.nn.Module, enabled: bool) -> None:
+    setter = getattr(model, "set_requires_gradient_sync", None)
+    if callable(setter):
+        setter(enabled)
+
+
+def _neutralise_nonfinite(grads: Sequence[torch.Tensor], finite: torch.Tensor) -> None:
+    with torch.no_grad():
+        for g in grads:
+            torch.where(finite, g, torch.zeros((), dtype=g.dtype, device=g.device), out=g)
+
+
+def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, patchifier: Patchifier,
+               gradient_accumulation_steps: int = 1, microbatch_index: int = 0, max_grad_norm: float | None = None,
+               cp_mesh: DeviceMesh | None = None, pp_mesh: DeviceMesh | None = None,
+               autocast_dtype: torch.dtype = torch.bfloat16, data_world: int = 1) -> tuple[TrainState, StepMetrics]:
+    """One micro-step (and the optimizer step on the last micro-step)."""
+    if not 0 <= microbatch_index < gradient_accumulation_steps:
+        raise ValueError(f"microbatch_index={microbatch_index} must lie in [0, {gradient_accumulation_steps})")
+    dev = batch.device
+    first = microbatch_index == 0
+    last = microbatch_index == gradient_accumulation_steps - 1
+    opt = state.optimizer
+    if first:
+        opt.zero_grad(set_to_none=not isinstance(opt, FusedAdamW))
+    _set_gradient_sync(state.model, last)
+    with _autocast(state.model, dev, autocast_dtype):
+        out: ObjectiveOutput = objective(state.model, batch, state.rng, patchifier=patchifier, cp_mesh=cp_mesh)
+    (out.loss / gradient_accumulation_steps).backward()
+    grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
+    finite = torch.isfinite(out.loss.detach())
+    if last:
+        if isinstance(opt, FusedAdamW):
+            opt.step(max_grad_norm=max_grad_norm)
+            grad_norm = opt.last_grad_norm.to(torch.float32).to(dev)
+            finite = finite & ~opt.last_nonfinite.to(dev)
+        else:
+            from avgen_b200.parallel.comm import clip_grad_norm
+
+            params = [p for p in state.model.parameters() if p.grad is not None]
+            if max_grad_norm is not None and params:
+                grad_norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh).to(torch.float32)
+            elif params:
+                grad_norm = torch.nn.utils.get_total_norm([p.grad for p in params], norm_type=2.0,
+                                                          error_if_nonfinite=False).to(torch.float32)
+            finite = finite & torch.isfinite(grad_norm)
+            _neutralise_nonfinite([p.grad for p in params], finite)
+            opt.step()
+        if state.schedule is not None:
+            state.schedule.step()
+        if state.ema is not None:
+            state.ema.update(state.model)
+        state.step += 1
+    state.samples_seen += batch.spec.batch_size * data_world
+    state.tokens_seen += batch.spec.batch_size * batch.spec.sequence_length * data_world
+    skipped = ~finite if last else torch.zeros((), dtype=torch.bool, device=dev)
+    metrics = StepMetrics(loss=out.loss.detach().to(torch.float32), video_loss=out.video_loss.to(torch.float32),
+                          audio_loss=out.audio_loss.to(torch.float32), valid_video_tokens=out.valid_video_tokens,
+                          valid_audio_tokens=out.valid_audio_tokens, grad_norm=grad_norm.reshape(()),
+                          nonfinite=(~finite).reshape(()), skipped=skipped.reshape(()))
+    return state, metrics
+
+
+class Trainer:
+    """The fit loop: cadence callbacks, logging, curriculum stage announcements."""
+
+    def __init__(self, state: TrainState, objective: Objective, parallel: Any, config: TrainerConfig, *,
+                 patchifier: Patchifier | None = None, callbacks: Sequence[TrainerCallback] = (),
+                 logger: MetricSink | None = None) -> None:
+        self.state = state
+        self.objective = objective
+        self.parallel = parallel
+        self.config = config
+        self.patchifier = patchifier or _model_patchifier(state.model)
+        self.callbacks = tuple(callbacks)
+        self.logger = logger
+        self._stage_name: str | None = None
+
+    @property
+    def device(self) -> torch.device:
+        for p in self.state.model.parameters():
+            return p.device
+        return torch.device("cpu")
+
+    def train_step(self, batch: MediaBatch, *, microbatch_index: int = 0, accumulation: int | None = None,
+                   ) -> StepMetrics:
+        _, metrics = train_step(
+            self.state, batch, self.objective, patchifier=self.patchifier,
+            gradient_accumulation_steps=accumulation or self.config.gradient_accumulation_steps,
+            microbatch_index=microbatch_index, max_grad_norm=self.config.max_grad_norm,
+            cp_mesh=getattr(self.parallel, "cp_mesh", None), pp_mesh=getattr(self.parallel, "pp_mesh", None),
+            autocast_dtype=self.config.torch_autocast_dtype, data_world=self.config.data_world)
+        return metrics
+
+    def fit(self, loader: Iterable[MediaBatch], total_steps: int | None = None) -> None:
+        if total_steps is not None and (isinstance(total_steps, bool) or total_steps < 1):
+            raise ValueError(f"total_steps must be positive; got {total_steps!r}")
+        acc = self.config.gradient_accumulation_steps
+        self._announce_stage(loader)
+        for index, batch in enumerate(_iterate(loader, self.device)):
+            metrics = self.train_step(batch, microbatch_index=index % acc, accumulation=acc)
+            if index % acc != acc - 1:
+                continue
+            self._on_step_end(metrics)
+            self._announce_stage(loader)
+            if total_steps is not None and self.state.step >= total_steps:
+                return
+
+    def _on_step_end(self, metrics: StepMetrics) -> None:
+        step = self.state.step
+        _dispatch(self.callbacks, "on_step_end", self, self.state, metrics)
+        if step % self.config.log_every == 0:
+            snap = metrics.to_mapping()
+            snap.update({f"progress/{k}": float(v) for k, v in self.state.progress().items()})
+            if self.state.schedule is not None:
+                snap["lr"] = self.state.schedule.get_last_lr()[0]
+            if self.logger is not None:
+                self.logger.log_metrics(snap, step)
+            else:
+                _LOG.info("step %d %s", step, snap)
+        if self.config.eval_every and step % self.config.eval_every == 0:
+            _dispatch(self.callbacks, "on_eval", self, self.state)
+        if self.config.checkpoint_every and step % self.config.checkpoint_every == 0:
+            _dispatch(self.callbacks, "on_checkpoint", self, self.state)
+
+    def _announce_stage(self, loader: object) -> None:
+        stage = self.config.curriculum.stage_for(self.state.step)
+        if stage is None or stage.name == self._stage_name:
+            return
+        self._stage_name = stage.name
+        setter = getattr(loader, "set_curriculum", None)
+        if callable(setter):
+            setter(stage)
+        _LOG.info("curriculum stage %r active at step %d", stage.name, self.state.step)
+
+
+def _iterate(loader: Iterable[MediaBatch], device: torch.device) -> Iterator[MediaBatch]:
+    for batch in loader:
+        yield batch if batch.device == device else batch.to(device)
+
+
+def _dispatch(callbacks: Sequence[Any], hook: str, *args: object) -> None:
+    for cb in callbacks:
+        method = getattr(cb, hook, None)
+        if callable(method):
+            method(*args)
+
+
+def _model_patchifier(model: torch.nn.Module) -> Patchifier:
+    inner = getattr(model, "module", model)
+    cand = getattr(inner, "patchifier", None)
+    return cand if isinstance(cand, Patchifier) else GridPatchifier()

@@ -1,0 +1,441 @@
+#!/usr/bin/env python
+"""Headline benchmark: training throughput of the 2B video DiT at 65,536 tokens/sample.
+
+Metric: samples/s (+ MFU) of full training steps of the
+32 x 2560 (20 heads of 128, SwiGLU MLP 4x, QK-RMSNorm, 3-D RoPE, cross-attention
+to 512 x 4096 text tokens) video DiT on 65,536 tokens per sample (latents
+16 x 16 x 128 x 128, patch 1 x 2 x 2), flow-matching loss, AdamW, bf16 compute,
+synthetic N(0, 1) latents and text, random-init weights.
+
+Weak scaling: every GPU processes 65,536 tokens per step. With N GPUs the job
+runs context parallelism cp = min(N, 4) and data parallelism dp = N / cp, and
+the global batch is N samples (each data-parallel group accumulates cp
+micro-batches of one sample sharded over its cp ranks). N = 8 is the named
+config: FSDP-style data parallel dp = 2 x cp = 4, global batch 8.
+
+    python bench.py --gpus N --steps K --warmup W [--impl avgen_b200|reference]
+
+For N > 1 launch with torchrun (one rank per GPU); rank 0 prints one JSON line.
+``value`` is device-timed (CUDA events, barrier + synchronize on both sides, max
+over ranks); ``e2e`` times the same steps through the public Trainer API with a
+pinned host->device copy of every micro-batch and a device->host read of the
+loss every step.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+WIDTH, DEPTH, HEADS, TEXT_TOKENS, TEXT_WIDTH, CHANNELS = 2560, 32, 20, 512, 4096, 16
+FRAMES, HEIGHT, WIDTH_PX = 16, 128, 128  # 65,536 tokens after 1x2x2 patching
+PEAK_NOMINAL = 2.25e15
+
+
+def parse_args() -> argparse.Namespace:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=4)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--e2e-steps", type=int, default=2)
+    p.add_argument("--impl", choices=("avgen_b200", "reference"), default="avgen_b200")
+    p.add_argument("--ref-variant", choices=("ring", "shipped"), default="ring",
+                   help="reference CP attention: its own context_parallel_region (ring) or as shipped (block-local)")
+    p.add_argument("--depth", type=int, default=DEPTH, help="override for quick local checks (not a valid bench)")
+    p.add_argument("--frames", type=int, default=FRAMES)
+    return p.parse_args()
+
+
+# --------------------------------------------------------------------------- helpers
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms in the background."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self) -> None:
+        self.rows: list[list[str]] = []
+        self.proc: subprocess.Popen | None = None
+        self.thread: threading.Thread | None = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+
+        def pump() -> None:
+            assert self.proc is not None and self.proc.stdout is not None
+            for line in self.proc.stdout:
+                self.rows.append([c.strip() for c in line.split(",")])
+
+        self.thread = threading.Thread(target=pump, daemon=True)
+        self.thread.start()
+
+    def stop(self, devices: list[int]) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for row in self.rows:
+            if len(row) < 9:
+                continue
+            try:
+                idx = int(row[0])
+            except ValueError:
+                continue
+            if devices and idx not in devices:
+                continue
+            try:
+                sm.append(float(row[1]))
+                mx.append(float(row[2]))
+            except ValueError:
+                pass
+            for name, flag in zip(names, row[5:9]):
+                if flag.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def model_flops_per_sample(tokens: int, depth: int) -> float:
+    """Training FLOPs of one sample (3 x forward; recompute not counted)."""
+    w, f, t = WIDTH, 4 * WIDTH, TEXT_TOKENS
+    per_block_linear = 2 * tokens * (6 * w * w + 3 * w * f) + 2 * t * 2 * w * w
+    per_block_attn = 4 * tokens * tokens * w + 4 * tokens * t * w
+    root = 2 * tokens * (64 * w + w * 64) + 2 * t * TEXT_WIDTH * w
+    return 3.0 * (depth * (per_block_linear + per_block_attn) + root)
+
+
+def dist_setup() -> tuple[int, int, int]:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1 and not dist.is_initialized():
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(minutes=10),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def barrier() -> None:
+    if dist.is_initialized():
+        dist.barrier(device_ids=[torch.cuda.current_device()])
+
+
+def max_over_ranks(value: float) -> float:
+    if not dist.is_initialized():
+        return value
+    t = torch.tensor([value], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def layout(world: int) -> tuple[int, int]:
+    cp = 1
+    for c in (4, 2, 1):
+        if world % c == 0 and c <= world:
+            cp = c
+            break
+    return cp, world // cp
+
+
+# --------------------------------------------------------------------------- our arm
+def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dict:
+    sys.path.insert(0, HERE)
+    from avgen_b200.core.rng import RNGStreams
+    from avgen_b200.core.state import TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.models import build_model
+    from avgen_b200.ops import kernels as K
+    from avgen_b200.parallel.context import apply_context_parallel
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, Trainer,
+                                  TrainerConfig, build_optimizer, build_timestep_sampler, train_step)
+
+    dev = torch.device("cuda", local)
+    cp, dp = layout(world)
+    mesh = cp_mesh = None
+    if world > 1:
+        from torch.distributed.device_mesh import init_device_mesh
+
+        mesh = init_device_mesh("cuda", (dp, cp), mesh_dim_names=("dp", "cp"))
+        cp_mesh = mesh["cp"] if cp > 1 else None
+        data_rank = mesh["dp"].get_local_rank() if dp > 1 else 0
+    else:
+        data_rank = 0
+    torch.manual_seed(1234)
+    with torch.device("meta"):
+        model = build_model("video_dit", {"width": WIDTH, "depth": args.depth, "num_heads": HEADS,
+                                          "text_width": TEXT_WIDTH, "text_context_length": TEXT_TOKENS,
+                                          "in_channels": CHANNELS})
+    model = model.to_empty(device=dev)
+    model.init_weights()
+    apply_context_parallel(model, cp_mesh)
+    optimizer = build_optimizer(model, lr=1e-4, weight_decay=0.0, dp_group=dist.group.WORLD if world > 1 else None)
+    state = TrainState(model=model, optimizer=optimizer, rng=RNGStreams.for_rank(0, data_rank=data_rank))
+    objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("shifted_logit_normal"),
+                                      MultiTaskConditioning())
+    patchifier = model.patchifier
+    micro = cp
+    gen = torch.Generator().manual_seed(1000 + data_rank)
+    shape = dict(batch=1, channels=CHANNELS, frames=args.frames, height=HEIGHT, width=WIDTH_PX,
+                 text_tokens=TEXT_TOKENS, text_width=TEXT_WIDTH)
+    dev_batches = [random_batch(**shape, generator=gen, device=dev) for _ in range(micro)]
+    tokens = dev_batches[0].spec.video_tokens
+
+    def step(batches) -> object:
+        metrics = None
+        for m, b in enumerate(batches):
+            _, metrics = train_step(state, b, objective, patchifier=patchifier, gradient_accumulation_steps=micro,
+                                    microbatch_index=m, max_grad_norm=1.0, cp_mesh=cp_mesh, data_world=dp)
+        return metrics
+
+    for _ in range(args.warmup):
+        step(dev_batches)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    launches0 = K.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    barrier()
+    ev0.record()
+    for _ in range(args.steps):
+        metrics = step(dev_batches)
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = (K.launch_count() - launches0)
+    clock_info = clocks.stop(list(range(world))) if rank == 0 else {}
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    loss_val = float(metrics.loss.item())
+    from avgen_b200.ops._ext import check_errors
+
+    err = check_errors(local)
+
+    # ------------------------------------------------------------------ end to end through the Trainer
+    trainer = Trainer(state, objective, type("P", (), {"cp_mesh": cp_mesh, "pp_mesh": None})(),
+                      TrainerConfig(gradient_accumulation_steps=micro, max_grad_norm=1.0, data_world=dp))
+    host = [random_batch(**shape, generator=gen, pin=True) for _ in range(micro)]
+    h2d = sum(b.nbytes() for b in host)
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        for m, hb in enumerate(host):
+            metrics = trainer.train_step(hb.to(dev, non_blocking=True), microbatch_index=m, accumulation=micro)
+        _ = metrics.loss.item()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0) / max(1, args.e2e_steps)
+
+    samples_per_step = world  # global batch (dp groups x cp micro-batches of one sample)
+    value = samples_per_step / (ms / 1000.0)
+    flops = model_flops_per_sample(tokens, args.depth)
+    mfu = flops * value / (world * PEAK_NOMINAL)
+    return {
+        "value": value, "ms_per_step": ms, "mfu": mfu, "loss": loss_val, "kernel_errors": err,
+        "gpu_launches": launches // max(1, args.steps), "gpu_launches_total": launches,
+        "e2e": {"value": samples_per_step / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
+        "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro,
+        "params": sum(p.numel() for p in model.parameters()),
+    }
+
+
+# --------------------------------------------------------------------------- reference arm
+def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -> dict:
+    ref = os.path.join(HERE, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "avgen")):
+        return {"unavailable": "reference not installed in baseline/_ref"}
+    sys.path.insert(0, ref)
+    import avgen
+    from avgen import RNGStreams, TrainState, build_model, train_step
+    from avgen.core.batch import MediaBatch, MediaBatchSpec
+    from avgen.core.patchify import GridPatchifier
+    from avgen.parallel import ParallelDims, parallelize
+    from avgen.parallel.activation import ActivationCheckpointConfig
+    from avgen.parallel.apply import ParallelConfig
+    from avgen.parallel.context import context_parallel_region
+    from avgen.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                             build_timestep_sampler)
+
+    del avgen
+    dev = torch.device("cuda", local)
+    cp, dp = layout(world)
+    torch.manual_seed(1234)
+    with torch.device("meta"):
+        model = build_model("video_dit", {"width": WIDTH, "depth": args.depth, "num_heads": HEADS,
+                                          "text_width": TEXT_WIDTH, "text_context_length": TEXT_TOKENS,
+                                          "in_channels": CHANNELS})
+    model = model.to_empty(device=dev)
+    model.init_weights()
+    tokens_local = (args.frames * HEIGHT * WIDTH_PX // 4) // cp
+    ac_mode = "selective_op" if tokens_local <= 16384 else "full"
+    dims = ParallelDims(world_size=world, dp_shard=dp, context=cp)
+    parallel = parallelize(model, dims, config=ParallelConfig(
+        activation_checkpoint=ActivationCheckpointConfig(mode=ac_mode)))
+    data_rank = dims.data_coordinates(parallel.mesh)[0] if parallel.mesh is not None else 0
+    optimizer = build_optimizer(parallel.model, lr=1e-4, weight_decay=0.0)
+    state = TrainState(model=parallel.model, optimizer=optimizer, rng=RNGStreams.for_rank(0, data_rank=data_rank))
+    objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("shifted_logit_normal"),
+                                      MultiTaskConditioning())
+    patchifier = GridPatchifier()
+    micro = cp
+    gen = torch.Generator().manual_seed(1000 + data_rank)
+
+    def make(pin: bool) -> MediaBatch:
+        spec = MediaBatchSpec(schema_version=1, bucket_id=0, video_shape=(1, CHANNELS, args.frames, HEIGHT, WIDTH_PX),
+                              audio_shape=(1, 1, 0), text_shape=(1, TEXT_TOKENS, TEXT_WIDTH), video_timebase_num=24000,
+                              video_timebase_den=1000, audio_timebase_num=1, audio_timebase_den=1,
+                              video_codec_id="synthetic", audio_codec_id="none")
+        t = {
+            "video": torch.randn((1, CHANNELS, args.frames, HEIGHT, WIDTH_PX), generator=gen),
+            "audio": torch.zeros((1, 1, 0)), "text": torch.randn((1, TEXT_TOKENS, TEXT_WIDTH), generator=gen),
+            "video_mask": torch.ones((1, args.frames, HEIGHT, WIDTH_PX), dtype=torch.bool),
+            "audio_mask": torch.zeros((1, 0), dtype=torch.bool),
+            "video_positions": (torch.arange(args.frames, dtype=torch.float32) / 24.0)[None].contiguous(),
+            "audio_positions": torch.zeros((1, 0)),
+            "text_mask": torch.ones((1, TEXT_TOKENS), dtype=torch.bool),
+        }
+        if pin:
+            t = {k: v.pin_memory() for k, v in t.items()}
+        return MediaBatch(sample_ids=torch.zeros(1, dtype=torch.int64), spec=spec, **t)
+
+    host = [make(True) for _ in range(micro)]
+    dev_batches = [b.to(dev) for b in host]
+    use_ring = cp > 1 and args.ref_variant == "ring"
+
+    def step(batches, *, copy: bool) -> object:
+        metrics = None
+        for m, b in enumerate(batches):
+            if copy:
+                b = b.to(dev, non_blocking=True)
+            region = context_parallel_region(parallel.cp_mesh) if use_ring else _null()
+            with region:
+                _, metrics = train_step(state, b, objective, patchifier=patchifier, gradient_accumulation_steps=micro,
+                                        microbatch_index=m, max_grad_norm=1.0, cp_mesh=parallel.cp_mesh,
+                                        autocast_dtype=torch.bfloat16, data_world=dp)
+        return metrics
+
+    for _ in range(args.warmup):
+        step(dev_batches, copy=False)
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        metrics = step(dev_batches, copy=False)
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clock_info = clocks.stop(list(range(world))) if rank == 0 else {}
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    loss_val = float(metrics.loss.item())
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        metrics = step(host, copy=True)
+        _ = metrics.loss.item()
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0) / max(1, args.e2e_steps)
+    h2d = sum(sum(t.numel() * t.element_size() for t in (b.video, b.audio, b.text, b.video_mask, b.audio_mask,
+                                                         b.video_positions, b.audio_positions, b.text_mask))
+              for b in host)
+    tokens = args.frames * HEIGHT * WIDTH_PX // 4
+    value = world / (ms / 1000.0)
+    return {
+        "value": value, "ms_per_step": ms, "mfu": model_flops_per_sample(tokens, args.depth) * value / (world * PEAK_NOMINAL),
+        "loss": loss_val, "e2e": {"value": world / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
+                                  "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
+        "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro, "ac_mode": ac_mode,
+        "ref_variant": ("ring (context_parallel_region)" if use_ring else "shipped") if cp > 1 else "n/a (cp=1)",
+        "applied": list(parallel.applied),
+    }
+
+
+class _null:
+    def __enter__(self) -> None:
+        return None
+
+    def __exit__(self, *exc: object) -> None:
+        return None
+
+
+def main() -> None:
+    args = parse_args()
+    rank, world, local = dist_setup()
+    if args.gpus != world:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun --nproc-per-node {args.gpus}")
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    out = run_reference(args, rank, world, local) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if rank == 0:
+        if "unavailable" in out:
+            print(json.dumps({"impl": "reference", "unavailable": out["unavailable"]}), flush=True)
+        else:
+            cp, dp = out["cp"], out["dp"]
+            line = {
+                "metric": "samples/s + MFU, 2B video DiT @64k tok, 1/2/4/8 B200; ring-attn exposed comm",
+                "value": out["value"], "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+                "warmup": args.warmup, "ms_per_step": out["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+                "data": "synthetic N(0,1) latents [1,16,16,128,128] and text [1,512,4096]; random-init weights",
+                "config": {"model": f"video_dit {args.depth}x{WIDTH}, {HEADS} heads x 128, SwiGLU mlp_ratio 4, "
+                                    f"QK-RMSNorm, 3-D RoPE, cross-attn 512x4096",
+                           "global_batch": world, "seq_len": out["tokens"],
+                           "parallelism": (f"dp{dp}xcp{cp}" if world > 1 else "single"),
+                           "micro_batches_per_step": out["micro"],
+                           "l2": "inputs larger than L2 (each block activation is 335 MB)"},
+                "mfu": out["mfu"], "loss": out["loss"], "e2e": out["e2e"], "clocks": out["clocks"],
+            }
+            if args.impl == "reference":
+                line["impl"] = "reference"
+                line["config"]["activation_checkpoint"] = out["ac_mode"]
+                line["config"]["ref_variant"] = out["ref_variant"]
+                line["config"]["applied"] = out["applied"]
+            else:
+                line["impl"] = "avgen_b200"
+                line["gpu_launches"] = out["gpu_launches"]
+                line["kernel_errors"] = out["kernel_errors"]
+                line["params"] = out["params"]
+            if args.depth != DEPTH or args.frames != FRAMES:
+                line["note"] = "reduced model/config: not a valid benchmark line"
+            print(json.dumps(line), flush=True)
+    if dist.is_initialized():
+        barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

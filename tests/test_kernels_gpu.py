@@ -152,7 +152,7 @@ def test_qkv_rope_fwd_bwd() -> None:
     _close(q, qr)
     _close(k, kr)
     _close(v, vr)
-    dq, dk, dv = (torch.randn_like(t).bfloat16() for t in (qr, kr, vr))
+    dq, dk, dv = (torch.randn(t.shape, device=DEV).bfloat16() for t in (qr, kr, vr))
     (qr * dq.float()).sum().add((kr * dk.float()).sum()).add((vr * dv.float()).sum()).backward()
     dqw = torch.zeros(d, device=DEV)
     dkw = torch.zeros(d, device=DEV)

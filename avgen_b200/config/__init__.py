@@ -1,0 +1,12 @@
+"""Configuration: frozen schema, YAML loader with composition and overrides, resolution, diff."""
+from avgen_b200.config.diff import config_diff, config_to_dict, render_diff, save_config
+from avgen_b200.config.loader import ConfigError, apply_overrides, load_config, load_mapping, parse_override
+from avgen_b200.config.schema import (ActivationSpec, BucketConfig, CheckpointConfig, DataConfig, EvalConfig,
+                                      FinetuneConfig, FSDPSpec, InferenceConfig, ModelConfig, ParallelConfigSpec,
+                                      PipelineSpec, PrecisionSpec, RLConfig, RunConfig, TelemetryConfig, TrainConfig)
+
+__all__ = ["ActivationSpec", "BucketConfig", "CheckpointConfig", "ConfigError", "DataConfig", "EvalConfig",
+           "FSDPSpec", "FinetuneConfig", "InferenceConfig", "ModelConfig", "ParallelConfigSpec", "PipelineSpec",
+           "PrecisionSpec", "RLConfig", "RunConfig", "TelemetryConfig", "TrainConfig", "apply_overrides",
+           "config_diff", "config_to_dict", "load_config", "load_mapping", "parse_override", "render_diff",
+           "save_config"]

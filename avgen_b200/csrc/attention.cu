@@ -340,32 +340,56 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* o, const __nv_bfloat1
   }
 }
 
-struct BwdSmem {
-  static constexpr int K = 0;                // 32 KB
-  static constexpr int V = 32768;            // 32 KB
-  static constexpr int STAGE = 65536;        // 2 stages x (Q 32 KB, dO 32 KB, lse 512 B, delta 512 B)
-  static constexpr int STAGE_BYTES = 65536 + 1024;
-  static constexpr int DS = STAGE + 2 * STAGE_BYTES;  // 32 KB dS tile (MN-major, SW128)
-  static constexpr int BARS = DS + 32768;
+// Descriptors for tiles whose 64-element column chunks are `chunk` bytes apart
+// (rows x 128 B): K-major k-step kk (16 elements), MN-major k-step kk (16 rows).
+__device__ __forceinline__ uint64_t kdesc(uint32_t tile, int kk, uint32_t chunk) {
+  return umma_desc_sw128(tile + (kk >> 2) * chunk + (kk & 3) * 32, 16, 1024);
+}
+__device__ __forceinline__ uint64_t mndesc(uint32_t tile, int kk, uint32_t chunk) {
+  return umma_desc_sw128(tile + kk * 2048, chunk, 1024);
+}
+
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_t (&v)[32], float scale) {
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = pack_bf16(__uint_as_float(v[8 * j + 0]) * scale, __uint_as_float(v[8 * j + 1]) * scale);
+    w.y = pack_bf16(__uint_as_float(v[8 * j + 2]) * scale, __uint_as_float(v[8 * j + 3]) * scale);
+    w.z = pack_bf16(__uint_as_float(v[8 * j + 4]) * scale, __uint_as_float(v[8 * j + 5]) * scale);
+    w.w = pack_bf16(__uint_as_float(v[8 * j + 6]) * scale, __uint_as_float(v[8 * j + 7]) * scale);
+    d4[j] = w;
+  }
+}
+
+// ------------------------------------------------------------------ dK / dV
+// CTA = (batch, kv head, 128 keys); loops over 64-query tiles of every query head
+// of the group. TMEM: S^T[2] (64 cols each), dP^T[2] (64), dV (128), dK (128).
+struct DkvSmem {
+  static constexpr int K = 0;           // 32 KB (2 chunks x 16 KB)
+  static constexpr int V = 32768;       // 32 KB
+  static constexpr int STAGES = 4;
+  static constexpr int STAGE = 65536;   // per stage: Q 16 KB, dO 16 KB, lse 256 B, delta 256 B
+  static constexpr int STAGE_BYTES = 33280;
+  static constexpr int BARS = STAGE + STAGES * STAGE_BYTES;
   static constexpr int BYTES = BARS + 256;
 };
+constexpr int kQT = 64;  // query tile of the dK/dV kernel
 
 __global__ void __launch_bounds__(256, 1)
-    attn_bwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
-                    const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
-                    const __grid_constant__ CUtensorMap tmLse, const __grid_constant__ CUtensorMap tmDelta,
-                    const AttnBwdDesc p) {
+    attn_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                        const __grid_constant__ CUtensorMap tmLse, const __grid_constant__ CUtensorMap tmDelta,
+                        const AttnBwdDesc p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + BwdSmem::BARS);
-  uint64_t* kv_full = bars;        // 1
-  uint64_t* st_full = bars + 1;    // 2
-  uint64_t* st_empty = bars + 3;   // 2
-  uint64_t* sdp_full = bars + 5;   // 1
-  uint64_t* p_full = bars + 6;     // 1 (128 arrivals)
-  uint64_t* dq_full = bars + 7;    // 1
-  uint64_t* dq_free = bars + 8;    // 1 (128 arrivals)
-  uint64_t* acc_done = bars + 9;   // 1
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DkvSmem::BARS);
+  uint64_t* kv_full = bars;                          // 1
+  uint64_t* st_full = bars + 1;                      // STAGES
+  uint64_t* st_empty = st_full + DkvSmem::STAGES;    // STAGES
+  uint64_t* sdp_full = st_empty + DkvSmem::STAGES;   // 2
+  uint64_t* p_full = sdp_full + 2;                   // 2 (128 arrivals)
+  uint64_t* acc_done = p_full + 2;                   // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = warp_id();
@@ -376,22 +400,23 @@ __global__ void __launch_bounds__(256, 1)
   const int b = bhk / p.Hk;
   const int k0 = kt * kTile;
   const int group = p.H / p.Hk;
-  const int nq = (p.Lq + kTile - 1) / kTile;
+  const int nq = (p.Lq + kQT - 1) / kQT;
   const int iters = nq * group;
 
   if (threadIdx.x == 0) {
-    if ((smem_u32(smem) & 1023u) != 0) record_error(p.err, kErrBadArgument);
+    const bool misaligned = (smem_u32(smem) & 1023u) != 0;
+    if (misaligned) record_error(p.err, kErrBadArgument);
     mbar_init(kv_full, 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < DkvSmem::STAGES; ++s) {
       mbar_init(&st_full[s], 1);
       mbar_init(&st_empty[s], 1);
     }
-    mbar_init(sdp_full, 1);
-    mbar_init(p_full, 128);
-    mbar_init(dq_full, 1);
-    mbar_init(dq_free, 128);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&p_full[i], 128);
+    }
     mbar_init(acc_done, 1);
-    *abort_flag = (smem_u32(smem) & 1023u) != 0 ? 1 : 0;
+    *abort_flag = misaligned ? 1 : 0;
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -402,183 +427,351 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: [0,128) S^T then dQ, [128,256) dP^T, [256,384) dV, [384,512) dK
-  const uint32_t tS = tmem, tP = tmem + 128, tDV = tmem + 256, tDK = tmem + 384;
+  // TMEM columns: S^T[b] at 64*b, dP^T[b] at 128 + 64*b, dV at 256, dK at 384.
+  const uint32_t tDV = tmem + 256, tDK = tmem + 384;
 
   if (warp == 0) {
     if (lane == 0 && !*abort_flag) {
       mbar_arrive_expect_tx(kv_full, 65536);
       for (int c = 0; c < 2; ++c) {
-        tma_load_3d(smem + BwdSmem::K + c * 16384, &tmK, kv_full, c * 64, k0, b * p.Hk + hk);
-        tma_load_3d(smem + BwdSmem::V + c * 16384, &tmV, kv_full, c * 64, k0, b * p.Hk + hk);
+        tma_load_3d(smem + DkvSmem::K + c * 16384, &tmK, kv_full, c * 64, k0, b * p.Hk + hk);
+        tma_load_3d(smem + DkvSmem::V + c * 16384, &tmV, kv_full, c * 64, k0, b * p.Hk + hk);
       }
       for (int i = 0; i < iters; ++i) {
-        const int s = i & 1;
+        const int s = i % DkvSmem::STAGES;
         const int h = hk * group + i / nq;
-        const int qb = (i % nq) * kTile;
-        if (!mbar_wait(&st_empty[s], ((i >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
-        uint8_t* st = smem + BwdSmem::STAGE + s * BwdSmem::STAGE_BYTES;
-        mbar_arrive_expect_tx(&st_full[s], 65536 + 1024);
+        const int qb = (i % nq) * kQT;
+        if (!mbar_wait(&st_empty[s], ((i / DkvSmem::STAGES) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        uint8_t* st = smem + DkvSmem::STAGE + s * DkvSmem::STAGE_BYTES;
+        mbar_arrive_expect_tx(&st_full[s], DkvSmem::STAGE_BYTES);
         for (int c = 0; c < 2; ++c) {
-          tma_load_3d(st + c * 16384, &tmQ, &st_full[s], c * 64, qb, b * p.H + h);
-          tma_load_4d(st + 32768 + c * 16384, &tmdO, &st_full[s], c * 64, h, qb, b);
+          tma_load_3d(st + c * 8192, &tmQ, &st_full[s], c * 64, qb, b * p.H + h);
+          tma_load_4d(st + 16384 + c * 8192, &tmdO, &st_full[s], c * 64, h, qb, b);
         }
-        tma_load_2d(st + 65536, &tmLse, &st_full[s], qb, b * p.H + h);
-        tma_load_2d(st + 65536 + 512, &tmDelta, &st_full[s], qb, b * p.H + h);
+        tma_load_2d(st + 32768, &tmLse, &st_full[s], qb, b * p.H + h);
+        tma_load_2d(st + 32768 + 256, &tmDelta, &st_full[s], qb, b * p.H + h);
       }
     }
   } else if (warp == 1) {
-    const uint32_t idT = idesc_bf16_f32(128, 128, false, false);  // S^T, dP^T
-    const uint32_t idA = idesc_bf16_f32(128, 128, false, true);   // dV, dK (A from TMEM)
-    const uint32_t idQ = idesc_bf16_f32(128, 128, true, true);    // dQ = dS K
-    const uint32_t sK = smem_u32(smem + BwdSmem::K);
-    const uint32_t sV = smem_u32(smem + BwdSmem::V);
-    const uint32_t sDS = smem_u32(smem + BwdSmem::DS);
+    const uint32_t idS = idesc_bf16_f32(128, kQT, false, false);
+    const uint32_t idA = idesc_bf16_f32(128, 128, false, true);
+    const uint32_t sK = smem_u32(smem + DkvSmem::K);
+    const uint32_t sV = smem_u32(smem + DkvSmem::V);
+    auto stage_addr = [&](int i) { return smem_u32(smem + DkvSmem::STAGE + (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES); };
+    auto issue_sdp = [&](int i) {
+      const uint32_t sQ = stage_addr(i), sdO = sQ + 16384;
+      const uint32_t bufS = tmem + 64 * (i & 1), bufP = tmem + 128 + 64 * (i & 1);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(bufS, kdesc(sK, kk, 16384), kdesc(sQ, kk, 8192), idS, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(bufP, kdesc(sV, kk, 16384), kdesc(sdO, kk, 8192), idS, kk > 0);
+      mma_commit(&sdp_full[i & 1]);
+    };
     bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
-    for (int i = 0; i < iters && ok; ++i) {
-      const int s = i & 1;
-      const uint32_t sQ = smem_u32(smem + BwdSmem::STAGE + s * BwdSmem::STAGE_BYTES);
-      const uint32_t sdO = sQ + 32768;
-      if (!mbar_wait(&st_full[s], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
-      if (i > 0 && !mbar_wait(dq_free, (i - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+    for (int i = 0; i < 2 && i < iters && ok; ++i) {
+      ok = mbar_wait(&st_full[i % DkvSmem::STAGES], (i / DkvSmem::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma);
+      if (!ok) break;
       tc_fence_after();
-      if (lane == 0) {
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_bf16_ss(tS, kmajor_desc(sK, kk), kmajor_desc(sQ, kk), idT, kk > 0 ? 1u : 0u);
-        }
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          mma_bf16_ss(tP, kmajor_desc(sV, kk), kmajor_desc(sdO, kk), idT, kk > 0 ? 1u : 0u);
-        }
-        mma_commit(sdp_full);
-      }
+      if (lane == 0) issue_sdp(i);
       __syncwarp();
-      if (!mbar_wait(p_full, i & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+    }
+    for (int i = 0; i < iters && ok; ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait(&p_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
       tc_fence_after();
       if (lane == 0) {
-        // dV += P^T dO ; dK += dS^T Q   (A from TMEM, B = MN-major views of dO / Q)
+        const uint32_t sQ = stage_addr(i), sdO = sQ + 16384;
+        const uint32_t bufS = tmem + 64 * buf, bufP = tmem + 128 + 64 * buf;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(tDV, tS + kk * 8, mnmajor_desc(sdO, kk), idA, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_bf16_ts(tDV, bufS + kk * 8, mndesc(sdO, kk, 8192), idA, (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ts(tDK, tP + kk * 8, mnmajor_desc(sQ, kk), idA, (i > 0 || kk > 0) ? 1u : 0u);
-        // dQ = dS K : A = dS (smem, MN-major: q contiguous), B = K viewed MN-major
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_bf16_ss(tS, mnmajor_desc(sDS, kk), mnmajor_desc(sK, kk), idQ, kk > 0 ? 1u : 0u);
-        mma_commit(dq_full);
-        mma_commit(&st_empty[s]);
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_bf16_ts(tDK, bufP + kk * 8, mndesc(sQ, kk, 8192), idA, (i > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(&st_empty[i % DkvSmem::STAGES]);
         if (i == iters - 1) mma_commit(acc_done);
       }
       __syncwarp();
+      if (i + 2 < iters) {
+        if (!mbar_wait(&st_full[(i + 2) % DkvSmem::STAGES], ((i + 2) / DkvSmem::STAGES) & 1, abort_flag, p.err,
+                       kErrTimeoutMma))
+          break;
+        tc_fence_after();
+        if (lane == 0) issue_sdp(i + 2);
+        __syncwarp();
+      }
     }
   } else if (warp >= 4) {
     const int quad = warp & 3;
-    const int row = quad * 32 + lane;  // key row for S^T / dP^T / dK / dV; query row for dQ
+    const int row = quad * 32 + lane;  // key row
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const float sl = p.scale_log2;
     const int key = k0 + row;
     bool key_ok = key < p.Lk;
     if (key_ok && p.kmask != nullptr)
       key_ok = (p.kmask[static_cast<long>(b) * p.kmask_words + (key >> 5)] >> (key & 31)) & 1u;
-    uint8_t* ds_tile = smem + BwdSmem::DS;
     bool ok = true;
     for (int i = 0; i < iters; ++i) {
-      const int s = i & 1;
-      const int h = hk * group + i / nq;
-      const int qb = (i % nq) * kTile;
-      const float* lse = reinterpret_cast<const float*>(smem + BwdSmem::STAGE + s * BwdSmem::STAGE_BYTES + 65536);
-      const float* dlt = lse + 128;
-      if (!mbar_wait(sdp_full, i & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
+      const int buf = i & 1;
+      const int qb = (i % nq) * kQT;
+      const float* lse = reinterpret_cast<const float*>(smem + DkvSmem::STAGE +
+                                                        (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES + 32768);
+      const float* dlt = lse + 64;
+      if (!mbar_wait(&sdp_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
-      // Process 32 query columns at a time: P^T, dS^T into TMEM (bf16 packed) and dS into smem.
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      const uint32_t tS = tmem + lane_base + 64 * buf, tP = tmem + lane_base + 128 + 64 * buf;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
         uint32_t sv[32], dv[32];
-        tmem_ld32(tS + lane_base + 32 * c, sv);
-        tmem_ld32(tP + lane_base + 32 * c, dv);
+        tmem_ld32(tS + 32 * c, sv);
+        tmem_ld32(tP + 32 * c, dv);
         tmem_wait_ld();
         uint32_t pp[16], dd[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           const int qa = 32 * c + 2 * e;
+          const float l0 = lse[qa], l1 = lse[qa + 1];
           float p0 = 0.f, p1 = 0.f;
           if (key_ok) {
-            const float l0 = lse[qa], l1 = lse[qa + 1];
-            p0 = (qb + qa < p.Lq && l0 != -INFINITY) ? fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -l0)) : 0.f;
-            p1 = (qb + qa + 1 < p.Lq && l1 != -INFINITY) ? fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -l1)) : 0.f;
+            if (qb + qa < p.Lq && l0 != -INFINITY) p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -l0));
+            if (qb + qa + 1 < p.Lq && l1 != -INFINITY) p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -l1));
           }
-          const float d0 = p0 * (__uint_as_float(dv[2 * e]) - dlt[qa]);
-          const float d1 = p1 * (__uint_as_float(dv[2 * e + 1]) - dlt[qa + 1]);
           pp[e] = pack_bf16(p0, p1);
-          dd[e] = pack_bf16(d0, d1);
+          dd[e] = pack_bf16(p0 * (__uint_as_float(dv[2 * e]) - dlt[qa]), p1 * (__uint_as_float(dv[2 * e + 1]) - dlt[qa + 1]));
         }
-        tmem_st16(tS + lane_base + 16 * c, pp);
-        tmem_st16(tP + lane_base + 16 * c, dd);
-        // dS tile, MN-major (q contiguous): chunk = q / 64, key row `row` at 128 B,
-        // 16-byte unit u (8 queries) stored at unit u ^ (row & 7).
-        const int chunk = c >> 1;
-        const int unit0 = (c & 1) * 4;
-        uint8_t* rowp = ds_tile + chunk * 16384 + row * 128;
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int unit = (unit0 + u) ^ (row & 7);
-          *reinterpret_cast<uint4*>(rowp + unit * 16) = make_uint4(dd[4 * u], dd[4 * u + 1], dd[4 * u + 2], dd[4 * u + 3]);
-        }
+        tmem_st16(tS + 16 * c, pp);
+        tmem_st16(tP + 16 * c, dd);
       }
       tmem_wait_st();
-      fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(p_full);
-      // dQ readout: TMEM lane = query row of this block.
-      if (!mbar_wait(dq_full, i & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
-      tc_fence_after();
-      const int q = qb + row;
-      float* dq = p.dq_acc + ((static_cast<long>(b) * p.H + h) * p.Lq + q) * kHD;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        tmem_ld32(tS + lane_base + 32 * c, v);
-        tmem_wait_ld();
-        if (q < p.Lq) {
-#pragma unroll
-          for (int e = 0; e < 8; ++e)
-            atomicAdd(reinterpret_cast<float4*>(dq + 32 * c) + e,
-                      make_float4(__uint_as_float(v[4 * e]) * p.scale, __uint_as_float(v[4 * e + 1]) * p.scale,
-                                  __uint_as_float(v[4 * e + 2]) * p.scale, __uint_as_float(v[4 * e + 3]) * p.scale));
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(dq_free);
+      mbar_arrive(&p_full[buf]);
     }
     if (ok && mbar_wait(acc_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
       tc_fence_after();
-      if (key < p.Lk) {
-        __nv_bfloat16* dk = p.dk + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
-        __nv_bfloat16* dv = p.dv + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+      __nv_bfloat16* dk = p.dk + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+      __nv_bfloat16* dv = p.dv + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t a[32], d[32];
-          tmem_ld32(tDK + lane_base + 32 * c, a);
-          tmem_ld32(tDV + lane_base + 32 * c, d);
-          tmem_wait_ld();
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            uint4 wk, wv;
-            wk.x = pack_bf16(__uint_as_float(a[8 * v + 0]) * p.scale, __uint_as_float(a[8 * v + 1]) * p.scale);
-            wk.y = pack_bf16(__uint_as_float(a[8 * v + 2]) * p.scale, __uint_as_float(a[8 * v + 3]) * p.scale);
-            wk.z = pack_bf16(__uint_as_float(a[8 * v + 4]) * p.scale, __uint_as_float(a[8 * v + 5]) * p.scale);
-            wk.w = pack_bf16(__uint_as_float(a[8 * v + 6]) * p.scale, __uint_as_float(a[8 * v + 7]) * p.scale);
-            wv.x = pack_bf16(__uint_as_float(d[8 * v + 0]), __uint_as_float(d[8 * v + 1]));
-            wv.y = pack_bf16(__uint_as_float(d[8 * v + 2]), __uint_as_float(d[8 * v + 3]));
-            wv.z = pack_bf16(__uint_as_float(d[8 * v + 4]), __uint_as_float(d[8 * v + 5]));
-            wv.w = pack_bf16(__uint_as_float(d[8 * v + 6]), __uint_as_float(d[8 * v + 7]));
-            reinterpret_cast<uint4*>(dk + 32 * c)[v] = wk;
-            reinterpret_cast<uint4*>(dv + 32 * c)[v] = wv;
-          }
+      for (int c = 0; c < 4; ++c) {
+        uint32_t a[32], v[32];
+        tmem_ld32(tDK + lane_base + 32 * c, a);
+        tmem_ld32(tDV + lane_base + 32 * c, v);
+        tmem_wait_ld();
+        if (key < p.Lk) {
+          store_row_bf16(dk + 32 * c, a, p.scale);
+          store_row_bf16(dv + 32 * c, v, 1.0f);
         }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ dQ
+// CTA = (batch, head, 256 queries as two 128-row tiles); loops over 64-key blocks.
+// TMEM per tile g: S (64 cols) at 128g, dP (64) at 128g + 64, dQ (128) at 256 + 128g.
+struct DqSmem {
+  static constexpr int Q = 0;          // 2 x 32 KB
+  static constexpr int DO = 65536;     // 2 x 32 KB
+  static constexpr int STAGES = 3;
+  static constexpr int KV = 131072;    // per stage: K 16 KB, V 16 KB
+  static constexpr int STAGE_BYTES = 32768;
+  static constexpr int BARS = KV + STAGES * STAGE_BYTES;
+  static constexpr int BYTES = BARS + 256;
+};
+constexpr int kKT = 64;  // key block of the dQ kernel
+
+__global__ void __launch_bounds__(384, 1)
+    attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                       const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                       const AttnBwdDesc p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + DqSmem::BARS);
+  uint64_t* q_full = bars;                          // 1
+  uint64_t* kv_full = bars + 1;                     // STAGES
+  uint64_t* kv_empty = kv_full + DqSmem::STAGES;    // STAGES
+  uint64_t* sdp_full = kv_empty + DqSmem::STAGES;   // 2
+  uint64_t* ds_full = sdp_full + 2;                 // 2 (128 arrivals)
+  uint64_t* dq_done = ds_full + 2;                  // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(dq_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int qt = blockIdx.x % p.q_tiles;
+  const int bh = blockIdx.x / p.q_tiles;
+  const int h = bh % p.H;
+  const int b = bh / p.H;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qt * 256;
+  const int nkv = (p.Lk + kKT - 1) / kKT;
+
+  if (threadIdx.x == 0) {
+    const bool misaligned = (smem_u32(smem) & 1023u) != 0;
+    if (misaligned) record_error(p.err, kErrBadArgument);
+    mbar_init(q_full, 1);
+    for (int s = 0; s < DqSmem::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&sdp_full[g], 1);
+      mbar_init(&ds_full[g], 128);
+    }
+    mbar_init(dq_done, 1);
+    *abort_flag = misaligned ? 1 : 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && !*abort_flag) {
+      mbar_arrive_expect_tx(q_full, 131072);
+      for (int g = 0; g < 2; ++g)
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(smem + DqSmem::Q + g * 32768 + c * 16384, &tmQ, q_full, c * 64, q0 + 128 * g, b * p.H + h);
+          tma_load_4d(smem + DqSmem::DO + g * 32768 + c * 16384, &tmdO, q_full, c * 64, h, q0 + 128 * g, b);
+        }
+      for (int j = 0; j < nkv; ++j) {
+        const int s = j % DqSmem::STAGES;
+        if (!mbar_wait(&kv_empty[s], ((j / DqSmem::STAGES) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        uint8_t* st = smem + DqSmem::KV + s * DqSmem::STAGE_BYTES;
+        mbar_arrive_expect_tx(&kv_full[s], DqSmem::STAGE_BYTES);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(st + c * 8192, &tmK, &kv_full[s], c * 64, j * kKT, b * p.Hk + hk);
+          tma_load_3d(st + 16384 + c * 8192, &tmV, &kv_full[s], c * 64, j * kKT, b * p.Hk + hk);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    const uint32_t idS = idesc_bf16_f32(128, kKT, false, false);
+    const uint32_t idQ = idesc_bf16_f32(128, 128, false, true);
+    const uint32_t sQ = smem_u32(smem + DqSmem::Q), sdO = smem_u32(smem + DqSmem::DO);
+    auto kv_addr = [&](int j) { return smem_u32(smem + DqSmem::KV + (j % DqSmem::STAGES) * DqSmem::STAGE_BYTES); };
+    auto issue_sdp = [&](int g, int j) {
+      const uint32_t sK = kv_addr(j), sV = sK + 16384;
+      const uint32_t tS = tmem + 128 * g, tP = tS + 64;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_bf16_ss(tS, kdesc(sQ + g * 32768, kk, 16384), kdesc(sK, kk, 8192), idS, kk > 0);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_bf16_ss(tP, kdesc(sdO + g * 32768, kk, 16384), kdesc(sV, kk, 8192), idS, kk > 0);
+      mma_commit(&sdp_full[g]);
+    };
+    auto issue_dq = [&](int g, int j) {
+      const uint32_t sK = kv_addr(j);
+#pragma unroll
+      for (int kk = 0; kk < kKT / 16; ++kk)
+        mma_bf16_ts(tmem + 256 + 128 * g, tmem + 128 * g + kk * 8, mndesc(sK, kk, 8192), idQ,
+                    (j > 0 || kk > 0) ? 1u : 0u);
+    };
+    bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutMma) &&
+              mbar_wait(&kv_full[0], 0, abort_flag, p.err, kErrTimeoutMma);
+    if (ok) {
+      tc_fence_after();
+      if (lane == 0) {
+        issue_sdp(0, 0);
+        issue_sdp(1, 0);
+      }
+      __syncwarp();
+    }
+    for (int j = 0; j < nkv && ok; ++j) {
+      const bool more = j + 1 < nkv;
+      if (!mbar_wait(&ds_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+      tc_fence_after();
+      if (lane == 0) issue_dq(0, j);
+      __syncwarp();
+      if (more) {
+        if (!mbar_wait(&kv_full[(j + 1) % DqSmem::STAGES], ((j + 1) / DqSmem::STAGES) & 1, abort_flag, p.err,
+                       kErrTimeoutMma))
+          break;
+        tc_fence_after();
+        if (lane == 0) issue_sdp(0, j + 1);
+        __syncwarp();
+      }
+      if (!mbar_wait(&ds_full[1], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        issue_dq(1, j);
+        mma_commit(&kv_empty[j % DqSmem::STAGES]);
+        if (more) issue_sdp(1, j + 1);
+        if (!more) mma_commit(dq_done);
+      }
+      __syncwarp();
+    }
+  } else if (warp >= 4) {
+    const int g = (warp - 4) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int q = q0 + 128 * g + row;
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_base + 128 * g, tP = tS + 64;
+    const float sl = p.scale_log2;
+    const bool q_ok = q < p.Lq;
+    const float lse_q = q_ok ? p.lse[(static_cast<long>(b) * p.H + h) * p.Lq + q] : -INFINITY;
+    const float dlt_q = q_ok ? p.delta[(static_cast<long>(b) * p.H + h) * p.Lq + q] : 0.f;
+    const bool row_live = q_ok && lse_q != -INFINITY;
+    bool ok = true;
+    for (int j = 0; j < nkv; ++j) {
+      if (!mbar_wait(&sdp_full[g], j & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
+      tc_fence_after();
+      const int kbase = j * kKT;
+      uint32_t words[2];
+#pragma unroll
+      for (int w = 0; w < 2; ++w) {
+        const int key0 = kbase + 32 * w;
+        uint32_t bits = 0xffffffffu;
+        if (p.kmask != nullptr && key0 < p.Lk) bits = p.kmask[static_cast<long>(b) * p.kmask_words + (key0 >> 5)];
+        const int left = p.Lk - key0;
+        if (left < 32) bits &= (left <= 0) ? 0u : ((1u << left) - 1u);
+        words[w] = bits;
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tS + 32 * c, sv);
+        tmem_ld32(tP + 32 * c, dv);
+        tmem_wait_ld();
+        uint32_t dd[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          const int ka = 32 * c + 2 * e;
+          float p0 = 0.f, p1 = 0.f;
+          if (row_live) {
+            if ((words[c] >> (2 * e)) & 1u) p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -lse_q));
+            if ((words[c] >> (2 * e + 1)) & 1u) p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -lse_q));
+          }
+          (void)ka;
+          dd[e] = pack_bf16(p0 * (__uint_as_float(dv[2 * e]) - dlt_q), p1 * (__uint_as_float(dv[2 * e + 1]) - dlt_q));
+        }
+        tmem_st16(tS + 16 * c, dd);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&ds_full[g]);
+    }
+    if (ok && mbar_wait(dq_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
+      tc_fence_after();
+      __nv_bfloat16* dst = p.dq + ((static_cast<long>(b) * p.H + h) * p.Lq + q) * kHD;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + 256 + 128 * g + 32 * c, v);
+        tmem_wait_ld();
+        if (q_ok) store_row_bf16(dst + 32 * c, v, p.scale);
       }
     }
   }
@@ -620,8 +813,12 @@ void attn_fwd_launch(const AttnFwdDesc& d_in, cudaStream_t stream) {
 void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
   AttnBwdDesc d = d_in;
   AVGEN_CHECK(d.D == kHD, "attention bwd: head_dim must be 128");
-  if (d.B == 0 || d.Lk == 0) return;
-  d.k_tiles = (d.Lk + kTile - 1) / kTile;
+  AVGEN_CHECK(d.H % d.Hk == 0, "attention bwd: H must be a multiple of Hk");
+  if (d.B == 0 || d.Lk == 0 || d.Lq == 0) return;
+  AVGEN_CHECK(d.o_sh == kHD && d.o_sl == static_cast<long>(d.H) * kHD &&
+                  d.o_sb == static_cast<long>(d.Lq) * d.H * kHD,
+              "attention bwd: O / dO must be dense [B, Lq, H, 128]");
+  AVGEN_CHECK(d.Lq % 4 == 0, "attention bwd: Lq must be a multiple of 4");
   // delta = rowsum(dO * O)
   {
     const long rows = static_cast<long>(d.B) * d.H * d.Lq;
@@ -631,54 +828,72 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
         d.delta, d.B, d.H, d.Lq, d.o_sb, d.o_sl, d.o_sh);
     AVGEN_CUDA_CHECK(cudaGetLastError());
   }
-  const CUtensorMap tq = make_tmap_3d_bf16(d.q, kHD, d.Lq, static_cast<long>(d.B) * d.H, kHD,
-                                           static_cast<long>(d.Lq) * kHD, 64, 128, 1);
-  const CUtensorMap tk = make_tmap_3d_bf16(d.k, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
-                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
-  const CUtensorMap tv = make_tmap_3d_bf16(d.v, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
-                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
-  // O / dO must be dense token-major [B, L, H, D].
-  AVGEN_CHECK(d.o_sh == kHD && d.o_sl == static_cast<long>(d.H) * kHD && d.o_sb == static_cast<long>(d.Lq) * d.H * kHD,
-              "attention bwd: dO / O must be dense [B, L, H, 128]");
-  auto f32_rows = [&](const float* ptr) {
-    CUtensorMap m;
-    cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(d.B) * d.H};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.Lq) * 4};
-    cuuint32_t box[2] = {128, 1};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims,
-                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: row-stat tensor map failed (", static_cast<int>(r), ")");
-    return m;
+  auto head_major = [&](const void* ptr, int heads, int len, int rows) {
+    return make_tmap_3d_bf16(ptr, kHD, len, static_cast<long>(d.B) * heads, kHD, static_cast<long>(len) * kHD, 64,
+                             rows, 1);
   };
-  AVGEN_CHECK(d.Lq % 4 == 0, "attention bwd: Lq must be a multiple of 4");
-  const CUtensorMap tl = f32_rows(d.lse);
-  const CUtensorMap tdl = f32_rows(d.delta);
-  // dO token-major dense [B, L, H, D]: 4-D map (d, h, l, b), box (64, 1, 128, 1).
-  CUtensorMap tdo3;
-  {
+  auto dout_map = [&](int rows) {
+    CUtensorMap m;
     cuuint64_t dims[4] = {static_cast<cuuint64_t>(kHD), static_cast<cuuint64_t>(d.H),
                           static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(d.B)};
     cuuint64_t strides[3] = {static_cast<cuuint64_t>(kHD) * 2, static_cast<cuuint64_t>(d.H) * kHD * 2,
                              static_cast<cuuint64_t>(d.Lq) * d.H * kHD * 2};
-    cuuint32_t box[4] = {64, 1, 128, 1};
+    cuuint32_t box[4] = {64, 1, static_cast<cuuint32_t>(rows), 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = tensor_map_encoder()(&tdo3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(d.dout), dims,
-                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(d.dout), dims,
+                                      strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: dO tensor map failed (", static_cast<int>(r), ")");
+    return m;
+  };
+  auto f32_rows = [&](const float* ptr, int box_len) {
+    CUtensorMap m;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(d.B) * d.H};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.Lq) * 4};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(box_len), 1};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides,
+                                      box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                                      CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: row-stat tensor map failed (", static_cast<int>(r), ")");
+    return m;
+  };
+  // ---- dK / dV
+  {
+    d.k_tiles = (d.Lk + kTile - 1) / kTile;
+    const CUtensorMap tq = head_major(d.q, d.H, d.Lq, kQT);
+    const CUtensorMap tk = head_major(d.k, d.Hk, d.Lk, kTile);
+    const CUtensorMap tv = head_major(d.v, d.Hk, d.Lk, kTile);
+    const CUtensorMap tdo = dout_map(kQT);
+    const CUtensorMap tl = f32_rows(d.lse, kQT);
+    const CUtensorMap tdl = f32_rows(d.delta, kQT);
+    static bool attr = false;
+    if (!attr) {
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            DkvSmem::BYTES));
+      attr = true;
+    }
+    const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
+    attn_bwd_dkv_kernel<<<grid, 256, DkvSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, d);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
   }
-  static bool attr = false;
-  if (!attr) {
-    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          BwdSmem::BYTES));
-    attr = true;
+  // ---- dQ
+  {
+    d.q_tiles = (d.Lq + 255) / 256;
+    const CUtensorMap tq = head_major(d.q, d.H, d.Lq, 128);
+    const CUtensorMap tk = head_major(d.k, d.Hk, d.Lk, kKT);
+    const CUtensorMap tv = head_major(d.v, d.Hk, d.Lk, kKT);
+    const CUtensorMap tdo = dout_map(128);
+    static bool attr = false;
+    if (!attr) {
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            DqSmem::BYTES));
+      attr = true;
+    }
+    const long grid = static_cast<long>(d.B) * d.H * d.q_tiles;
+    attn_bwd_dq_kernel<<<grid, 384, DqSmem::BYTES, stream>>>(tq, tk, tv, tdo, d);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
   }
-  const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
-  attn_bwd_kernel<<<grid, 256, BwdSmem::BYTES, stream>>>(tq, tk, tv, tdo3, tl, tdl, d);
-  AVGEN_CUDA_CHECK(cudaGetLastError());
 }
 
 }  // namespace avgen

@@ -507,13 +507,13 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 }
 
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
-              const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dk,
+              const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
               at::Tensor& dv, const OptT& kmask, double scale) {
   c10::cuda::CUDAGuard guard(q.device());
   for (const at::Tensor* t : {&q, &k, &v, &o, &dout, static_cast<const at::Tensor*>(&dk), static_cast<const at::Tensor*>(&dv)}) check_bf16(*t, "attention bwd tensor");
   check_f32(lse, "lse");
   check_f32(delta, "delta");
-  check_f32(dq_acc, "dq_acc");
+  check_bf16(dq, "dq");
   AttnBwdDesc d;
   d.device = q.device().index();
   d.B = static_cast<int>(q.size(0));
@@ -526,7 +526,7 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   TORCH_CHECK(o.is_contiguous() && dout.is_contiguous() && o.dim() == 4 && o.size(1) == d.Lq && o.size(2) == d.H,
               "attention bwd: o / dout must be dense [B, Lq, H, D]");
   TORCH_CHECK(dout.sizes() == o.sizes(), "attention bwd: dout must match o");
-  TORCH_CHECK(dq_acc.is_contiguous() && dq_acc.numel() == q.numel(), "attention bwd: dq_acc [B, H, Lq, D] fp32");
+  TORCH_CHECK(dq.is_contiguous() && dq.sizes() == q.sizes(), "attention bwd: dq must match q");
   TORCH_CHECK(dk.is_contiguous() && dv.is_contiguous() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(),
               "attention bwd: dk/dv must match k/v");
   TORCH_CHECK(lse.numel() == static_cast<long>(d.B) * d.H * d.Lq && delta.numel() == lse.numel(),
@@ -541,7 +541,7 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   d.o_sh = o.stride(2);
   d.lse = lse.data_ptr<float>();
   d.delta = delta.data_ptr<float>();
-  d.dq_acc = dq_acc.data_ptr<float>();
+  d.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
   d.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   d.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   if (has(kmask)) {
@@ -605,7 +605,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("attn_fwd", &a::attn_fwd, arg("q"), arg("k"), arg("v"), arg("out"), arg("lse") = none, arg("kmask") = none,
         arg("scale") = 0.0);
   m.def("attn_bwd", &a::attn_bwd, arg("q"), arg("k"), arg("v"), arg("o"), arg("dout"), arg("lse"), arg("delta"),
-        arg("dq_acc"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0);
+        arg("dq"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0);
   m.def("read_error", &a::read_error);
   m.def("clear_error", &a::clear_error);
 }

@@ -218,7 +218,8 @@ struct AttnBwdDesc {
   float* delta = nullptr;      // scratch [B, H, Lq]
   const uint32_t* kmask = nullptr;
   int kmask_words = 0;
-  float* dq_acc = nullptr;     // fp32 [B, H, Lq, D], zeroed by the caller
+  __nv_bfloat16* dq = nullptr; // [B, H, Lq, D]
+  int q_tiles = 0;
   __nv_bfloat16* dk = nullptr; // [B, Hk, Lk, D]
   __nv_bfloat16* dv = nullptr;
   int* err = nullptr;

@@ -286,15 +286,15 @@ def attention_bwd(
     kmask: torch.Tensor | None = None,
     scale: float | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Flash attention backward. Returns ``(dq fp32 [B,H,Lq,D], dk, dv)``."""
+    """Flash attention backward. Returns ``(dq, dk, dv)`` (bf16, shapes of q, k, v)."""
     d = q.shape[-1]
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     delta = torch.empty_like(lse)
-    dq = torch.zeros(q.shape, device=q.device, dtype=_F32)
+    dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     load().attn_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, kmask, scale)
-    _count(2)
+    _count(3)
     return dq, dk, dv
 
 

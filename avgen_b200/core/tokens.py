@@ -91,6 +91,12 @@ class TokenStream:
         noise_level: ``(B,)`` per-sample or ``(B, L)`` per-token, fp32 in [0, 1].
         layout: static geometry.
         conditioned: ``(B, L)`` clean anchors (attended, excluded from the loss).
+        level_values: optional ``(B, G)`` fp32 distinct noise levels of each sample.
+        level_index: optional ``(B, L)`` int32 with ``noise_level[b, l] ==
+            level_values[b, level_index[b, l]]``. Producers that know their per-token
+            levels take few values (clean conditioning frames at 0, the rest at
+            ``t``) set both, so the model computes adaLN modulation once per level
+            instead of once per token. Empty when absent.
     """
 
     tokens: torch.Tensor
@@ -99,6 +105,8 @@ class TokenStream:
     noise_level: torch.Tensor
     layout: PatchLayout
     conditioned: torch.Tensor = field(default_factory=_empty_bool)
+    level_values: torch.Tensor = field(default_factory=lambda: torch.empty(0))
+    level_index: torch.Tensor = field(default_factory=lambda: torch.empty(0, dtype=torch.int32))
 
     def __post_init__(self) -> None:
         if self.conditioned.numel() == 0:
@@ -130,6 +138,10 @@ class TokenStream:
     @property
     def per_token_noise(self) -> bool:
         return self.noise_level.ndim == 2
+
+    @property
+    def has_level_groups(self) -> bool:
+        return self.level_values.numel() > 0
 
     def expanded_noise(self) -> torch.Tensor:
         """Noise level broadcast to ``(B, L)``."""
@@ -166,6 +178,15 @@ class TokenStream:
         for name in ("coords", "mask", "conditioned", "noise_level"):
             if getattr(self, name).device != self.tokens.device:
                 raise ValueError(f"{name} must be on tokens device {self.tokens.device}")
+        if self.level_index.numel():
+            require_shape("level_index", self.level_index, (batch, length))
+            require_dtype("level_index", self.level_index, torch.int32)
+            require_dtype("level_values", self.level_values, torch.float32)
+            if self.level_values.ndim != 2 or self.level_values.shape[0] != batch:
+                raise ValueError(f"level_values must be ({batch}, G); got {tuple(self.level_values.shape)}")
+            expanded = self.level_values.gather(1, self.level_index.long())
+            if not torch.equal(expanded, self.expanded_noise()):
+                raise ValueError("level_values[level_index] must equal noise_level")
 
     @classmethod
     def empty_like(cls, batch: int, width: int, *, device: torch.device | str = "cpu",
@@ -215,12 +236,14 @@ class TextContext:
 
 
 def _flatten_stream(stream: TokenStream) -> tuple[list[torch.Tensor], PatchLayout]:
-    return [stream.tokens, stream.coords, stream.mask, stream.noise_level, stream.conditioned], stream.layout
+    return [stream.tokens, stream.coords, stream.mask, stream.noise_level, stream.conditioned, stream.level_values,
+            stream.level_index], stream.layout
 
 
 def _unflatten_stream(values: list[torch.Tensor], layout: PatchLayout) -> TokenStream:
-    tokens, coords, mask, noise, cond = values
-    return TokenStream(tokens=tokens, coords=coords, mask=mask, noise_level=noise, layout=layout, conditioned=cond)
+    tokens, coords, mask, noise, cond, lv, li = values
+    return TokenStream(tokens=tokens, coords=coords, mask=mask, noise_level=noise, layout=layout, conditioned=cond,
+                       level_values=lv, level_index=li)
 
 
 _pytree.register_pytree_node(TokenStream, _flatten_stream, _unflatten_stream,

@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       if (q < p.Lq && p.lse != nullptr)
-        p.lse[(static_cast<long>(b) * p.H + h) * p.Lq + q] = l > 0.f ? m + __log2f(l) : -INFINITY;
+        p.lse[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] = l > 0.f ? m + __log2f(l) : -INFINITY;
     }
   }
 
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(384, 1)
 // =========================================================================== backward
 // delta[b, h, q] = sum_d dO[b, q, h, d] * O[b, q, h, d]; one warp per (b, q, h) row.
 __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* o, const __nv_bfloat16* dout, float* delta,
-                                      int B, int H, int L, long sb, long sl, long sh) {
+                                      int B, int H, int L, long sb, long sl, long sh, long ld) {
   const long rows = static_cast<long>(B) * H * L;
   const int lane = threadIdx.x & 31;
   for (long r = static_cast<long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows;
@@ -336,7 +336,7 @@ __global__ void attn_bwd_delta_kernel(const __nv_bfloat16* o, const __nv_bfloat1
               bf16_hi(a.y) * bf16_hi(c.y);
 #pragma unroll
     for (int k = 16; k > 0; k >>= 1) s += __shfl_xor_sync(0xffffffffu, s, k);
-    if (lane == 0) delta[r] = s;
+    if (lane == 0) delta[bh * ld + q] = s;
   }
 }
 
@@ -517,7 +517,13 @@ __global__ void __launch_bounds__(256, 1)
       const float* lse = reinterpret_cast<const float*>(smem + DkvSmem::STAGE +
                                                         (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES + 32768);
       const float* dlt = lse + 64;
-      if (!mbar_wait(&sdp_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
+      // lse / delta of this stage were written by TMA: observe its barrier too
+      if (!mbar_wait(&st_full[i % DkvSmem::STAGES], (i / DkvSmem::STAGES) & 1, abort_flag, p.err,
+                     kErrTimeoutSoftmax) ||
+          !mbar_wait(&sdp_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
       tc_fence_after();
       const uint32_t tS = tmem + lane_base + 64 * buf, tP = tmem + lane_base + 128 + 64 * buf;
 #pragma unroll
@@ -721,8 +727,8 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tS = tmem + lane_base + 128 * g, tP = tS + 64;
     const float sl = p.scale_log2;
     const bool q_ok = q < p.Lq;
-    const float lse_q = q_ok ? p.lse[(static_cast<long>(b) * p.H + h) * p.Lq + q] : -INFINITY;
-    const float dlt_q = q_ok ? p.delta[(static_cast<long>(b) * p.H + h) * p.Lq + q] : 0.f;
+    const float lse_q = q_ok ? p.lse[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] : -INFINITY;
+    const float dlt_q = q_ok ? p.delta[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] : 0.f;
     const bool row_live = q_ok && lse_q != -INFINITY;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
@@ -818,14 +824,14 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
   AVGEN_CHECK(d.o_sh == kHD && d.o_sl == static_cast<long>(d.H) * kHD &&
                   d.o_sb == static_cast<long>(d.Lq) * d.H * kHD,
               "attention bwd: O / dO must be dense [B, Lq, H, 128]");
-  AVGEN_CHECK(d.Lq % 4 == 0, "attention bwd: Lq must be a multiple of 4");
+  AVGEN_CHECK(d.stat_ld >= d.Lq && d.stat_ld % 4 == 0, "attention bwd: lse/delta row stride must be >= Lq and a multiple of 4");
   // delta = rowsum(dO * O)
   {
     const long rows = static_cast<long>(d.B) * d.H * d.Lq;
     const long blocks = std::min<long>((rows + 7) / 8, 16L * num_sms(d.device));
     attn_bwd_delta_kernel<<<blocks, 256, 0, stream>>>(
         reinterpret_cast<const __nv_bfloat16*>(d.o), reinterpret_cast<const __nv_bfloat16*>(d.dout),
-        d.delta, d.B, d.H, d.Lq, d.o_sb, d.o_sl, d.o_sh);
+        d.delta, d.B, d.H, d.Lq, d.o_sb, d.o_sl, d.o_sh, d.stat_ld);
     AVGEN_CUDA_CHECK(cudaGetLastError());
   }
   auto head_major = [&](const void* ptr, int heads, int len, int rows) {
@@ -849,7 +855,7 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
   auto f32_rows = [&](const float* ptr, int box_len) {
     CUtensorMap m;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(d.B) * d.H};
-    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.Lq) * 4};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d.stat_ld) * 4};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(box_len), 1};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = tensor_map_encoder()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(ptr), dims, strides,

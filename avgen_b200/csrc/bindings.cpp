@@ -42,10 +42,18 @@ const float* f32_or_null(const OptT& t, const char* name) {
   return t->data_ptr<float>();
 }
 
+// Optional per-row modulation group index: contiguous int32 with one entry per row.
+const int* groups_or_null(const OptT& g, long rows, const char* what) {
+  if (!has(g)) return nullptr;
+  TORCH_CHECK(g->scalar_type() == at::kInt && g->is_cuda() && g->is_contiguous() && g->numel() >= rows, what,
+              ": groups must be a contiguous int32 device tensor with one entry per row");
+  return g->data_ptr<int>();
+}
+
 // --------------------------------------------------------------------- GEMM
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epilogue,
           const OptT& bias, const OptT& resid, const OptT& gate, int64_t rows_per_batch, const OptT& aux,
-          int64_t k_splits) {
+          int64_t k_splits, const OptT& groups) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_cuda(out, "out");
@@ -94,7 +102,9 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     if (has(gate)) {
       check_f32(*gate, "gate");
       TORCH_CHECK(gate->dim() == 2 && gate->size(1) == d.N && gate->stride(1) == 1, "gemm: gate must be fp32 [B, N]");
-      TORCH_CHECK(gate->size(0) * d.rows_per_batch >= d.M, "gemm: gate rows do not cover M");
+      d.groups = groups_or_null(groups, d.M, "gemm");
+      d.num_groups = static_cast<int>(gate->size(0));
+      TORCH_CHECK(d.groups != nullptr || gate->size(0) * d.rows_per_batch >= d.M, "gemm: gate rows do not cover M");
       d.gate = gate->data_ptr<float>();
       d.gate_stride = gate->stride(0);
     }
@@ -113,7 +123,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
 
 // --------------------------------------------------------------------- norms
 NormDesc norm_common(const at::Tensor& x, int64_t rows_per_batch, double eps, const OptT& w, const OptT& scale,
-                     const OptT& shift) {
+                     const OptT& shift, const OptT& groups) {
   check_bf16(x, "x");
   check_rows(x, "x");
   NormDesc d;
@@ -128,7 +138,9 @@ NormDesc norm_common(const at::Tensor& x, int64_t rows_per_batch, double eps, co
   if (has(scale) || has(shift)) {
     const at::Tensor& ref = has(scale) ? *scale : *shift;
     TORCH_CHECK(ref.dim() == 2 && ref.size(1) >= d.W && ref.stride(1) == 1, "norm: modulation must be [B, >=W]");
-    TORCH_CHECK(ref.size(0) * d.rows_per_batch >= d.rows, "norm: modulation rows do not cover x");
+    d.groups = groups_or_null(groups, d.rows, "norm");
+    d.num_groups = static_cast<int>(ref.size(0));
+    TORCH_CHECK(d.groups != nullptr || ref.size(0) * d.rows_per_batch >= d.rows, "norm: modulation rows do not cover x");
     d.mod_stride = ref.stride(0);
     if (has(scale)) {
       check_f32(*scale, "scale");
@@ -145,9 +157,9 @@ NormDesc norm_common(const at::Tensor& x, int64_t rows_per_batch, double eps, co
 }
 
 void rmsnorm_mod_fwd(const at::Tensor& x, at::Tensor& y, const OptT& rstd, const OptT& w, const OptT& scale,
-                     const OptT& shift, int64_t rows_per_batch, double eps) {
+                     const OptT& shift, int64_t rows_per_batch, double eps, const OptT& groups) {
   c10::cuda::CUDAGuard guard(x.device());
-  NormDesc d = norm_common(x, rows_per_batch, eps, w, scale, shift);
+  NormDesc d = norm_common(x, rows_per_batch, eps, w, scale, shift, groups);
   check_bf16(y, "y");
   check_rows(y, "y");
   TORCH_CHECK(y.size(0) == d.rows && y.size(1) == d.W, "norm: y shape");
@@ -163,9 +175,10 @@ void rmsnorm_mod_fwd(const at::Tensor& x, at::Tensor& y, const OptT& rstd, const
 
 void rmsnorm_mod_bwd(const at::Tensor& x, const at::Tensor& rstd, const at::Tensor& dy, const OptT& dx,
                      const OptT& dres, const OptT& w, const OptT& scale, const OptT& shift, const OptT& dw,
-                     const OptT& dscale, const OptT& dshift, int64_t rows_per_batch) {
+                     const OptT& dscale, const OptT& dshift, int64_t rows_per_batch, const OptT& groups) {
   c10::cuda::CUDAGuard guard(x.device());
-  NormDesc d = norm_common(x, rows_per_batch, 0.0, w, scale, shift);
+  NormDesc d = norm_common(x, rows_per_batch, 0.0, w, scale, shift, groups);
+  TORCH_CHECK(d.groups != nullptr || !has(groups), "norm bwd: groups need scale or shift");
   check_f32(rstd, "rstd");
   TORCH_CHECK(rstd.numel() == d.rows, "norm bwd: rstd must be [rows]");
   d.rstd = rstd.data_ptr<float>();
@@ -196,7 +209,7 @@ void rmsnorm_mod_bwd(const at::Tensor& x, const at::Tensor& rstd, const at::Tens
 }
 
 void gate_bwd(const at::Tensor& dx, const at::Tensor& a, const at::Tensor& gate, at::Tensor& da, at::Tensor& dgate,
-              int64_t rows_per_batch) {
+              int64_t rows_per_batch, const OptT& groups) {
   c10::cuda::CUDAGuard guard(dx.device());
   check_bf16(dx, "dx");
   check_bf16(a, "a");
@@ -208,6 +221,8 @@ void gate_bwd(const at::Tensor& dx, const at::Tensor& a, const at::Tensor& gate,
   d.rows = dx.size(0);
   d.W = static_cast<int>(dx.size(1));
   d.rows_per_batch = std::max<int64_t>(1, rows_per_batch);
+  d.groups = groups_or_null(groups, d.rows, "gate_bwd");
+  d.num_groups = static_cast<int>(gate.size(0));
   d.dx = dx.data_ptr();
   d.lddx = dx.stride(0);
   d.a = a.data_ptr();
@@ -459,6 +474,15 @@ void ema(const at::Tensor& param, at::Tensor& shadow, double decay) {
 }
 
 // --------------------------------------------------------------------- attention
+// Row stride (in floats) of a [B, H, Lq] row-statistics tensor whose (b, h) rows
+// may be padded: the backward reads them with TMA, which needs 16-byte rows.
+long stat_row_stride(const at::Tensor& t, int B, int H, int Lq, const char* what) {
+  TORCH_CHECK(t.dim() == 3 && t.size(0) == B && t.size(1) == H && t.size(2) == Lq && t.stride(2) == 1 &&
+                  t.stride(1) >= Lq && t.stride(0) == t.stride(1) * H,
+              what, " must be [B, H, Lq] with unit last stride and (b, h) rows laid out densely");
+  return t.stride(1);
+}
+
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, const OptT& lse,
               const OptT& kmask, double scale) {
   c10::cuda::CUDAGuard guard(q.device());
@@ -492,7 +516,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   d.o_sh = out.stride(2);
   if (has(lse)) {
     check_f32(*lse, "lse");
-    TORCH_CHECK(lse->is_contiguous() && lse->numel() == static_cast<long>(d.B) * d.H * d.Lq, "attention: lse [B,H,Lq]");
+    d.stat_ld = stat_row_stride(*lse, d.B, d.H, d.Lq, "attention: lse");
     d.lse = lse->data_ptr<float>();
   }
   if (has(kmask)) {
@@ -529,8 +553,9 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   TORCH_CHECK(dq.is_contiguous() && dq.sizes() == q.sizes(), "attention bwd: dq must match q");
   TORCH_CHECK(dk.is_contiguous() && dv.is_contiguous() && dk.sizes() == k.sizes() && dv.sizes() == v.sizes(),
               "attention bwd: dk/dv must match k/v");
-  TORCH_CHECK(lse.numel() == static_cast<long>(d.B) * d.H * d.Lq && delta.numel() == lse.numel(),
-              "attention bwd: lse/delta [B, H, Lq]");
+  d.stat_ld = stat_row_stride(lse, d.B, d.H, d.Lq, "attention bwd: lse");
+  TORCH_CHECK(delta.strides() == lse.strides() && delta.sizes() == lse.sizes(),
+              "attention bwd: delta must have the shape and strides of lse");
   d.q = q.data_ptr();
   d.k = k.data_ptr();
   d.v = v.data_ptr();
@@ -577,13 +602,15 @@ PYBIND11_MODULE(_C, m) {
   m.doc() = "avgen_b200 sm_100a kernels";
   m.def("gemm", &a::gemm, arg("a"), arg("b"), arg("out"), arg("a_mn"), arg("b_mn"), arg("epilogue"),
         arg("bias") = none, arg("resid") = none, arg("gate") = none, arg("rows_per_batch") = 1, arg("aux") = none,
-        arg("k_splits") = 1);
+        arg("k_splits") = 1, arg("groups") = none);
   m.def("rmsnorm_mod_fwd", &a::rmsnorm_mod_fwd, arg("x"), arg("y"), arg("rstd") = none, arg("w") = none,
-        arg("scale") = none, arg("shift") = none, arg("rows_per_batch") = 1, arg("eps") = 1e-6);
+        arg("scale") = none, arg("shift") = none, arg("rows_per_batch") = 1, arg("eps") = 1e-6,
+        arg("groups") = none);
   m.def("rmsnorm_mod_bwd", &a::rmsnorm_mod_bwd, arg("x"), arg("rstd"), arg("dy"), arg("dx") = none,
         arg("dres") = none, arg("w") = none, arg("scale") = none, arg("shift") = none, arg("dw") = none,
-        arg("dscale") = none, arg("dshift") = none, arg("rows_per_batch") = 1);
-  m.def("gate_bwd", &a::gate_bwd, arg("dx"), arg("a"), arg("gate"), arg("da"), arg("dgate"), arg("rows_per_batch"));
+        arg("dscale") = none, arg("dshift") = none, arg("rows_per_batch") = 1, arg("groups") = none);
+  m.def("gate_bwd", &a::gate_bwd, arg("dx"), arg("a"), arg("gate"), arg("da"), arg("dgate"), arg("rows_per_batch"),
+        arg("groups") = none);
   m.def("qkv_rope_fwd", &a::qkv_rope_fwd, arg("qkv"), arg("B"), arg("L"), arg("H"), arg("Hk"), arg("D"), arg("eps"),
         arg("q_w") = none, arg("k_w") = none, arg("coords") = none, arg("freq") = none, arg("axis") = none,
         arg("q") = none, arg("k") = none, arg("v") = none);

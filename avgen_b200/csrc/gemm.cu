@@ -49,6 +49,8 @@ struct GemmArgs {
   const float* gate;
   long gate_stride;
   int rows_per_batch;
+  const int* groups;
+  int num_groups;
   __nv_bfloat16* aux;
   long ldaux;
   int* err;
@@ -150,7 +152,7 @@ __device__ __forceinline__ void epilogue_row(const GemmArgs& a, int row, int col
   } else if constexpr (EPI == kEpiGateResid) {
     if (a.aux != nullptr) store_bf16x32(a.aux + row * a.ldaux + col0, v, valid);
     const float* g = (a.gate != nullptr)
-                         ? a.gate + static_cast<long>(row / a.rows_per_batch) * a.gate_stride + col0
+                         ? a.gate + mod_row(a.groups, a.num_groups, row, a.rows_per_batch) * a.gate_stride + col0
                          : nullptr;
     const __nv_bfloat16* res = a.resid + row * a.ldr + col0;
     float o[32];
@@ -444,6 +446,8 @@ void gemm_launch(const GemmDesc& d, cudaStream_t stream) {
   args.gate = d.gate;
   args.gate_stride = d.gate_stride;
   args.rows_per_batch = std::max(1, d.rows_per_batch);
+  args.groups = d.groups;
+  args.num_groups = d.num_groups;
   args.aux = reinterpret_cast<__nv_bfloat16*>(d.aux);
   args.ldaux = d.ldaux;
   args.err = d.err;

@@ -35,6 +35,8 @@ struct GemmDesc {
   const float* gate = nullptr;  // fp32 [B, gate_stride]
   long gate_stride = 0;
   int rows_per_batch = 1;
+  const int* groups = nullptr;  // int32 [M]: gate row of each output row (overrides rows_per_batch)
+  int num_groups = 0;           // gate rows; group indices are clamped to [0, num_groups)
   void* aux = nullptr;  // bf16 [M, N]
   long ldaux = 0;
   int k_splits = 1;
@@ -49,6 +51,8 @@ struct NormDesc {
   long rows = 0;
   int W = 0;
   long rows_per_batch = 1;
+  const int* groups = nullptr;  // int32 [rows]: modulation row of each row (overrides rows_per_batch)
+  int num_groups = 0;           // modulation rows; indices are clamped to [0, num_groups)
   float eps = 1e-6f;
   const void* x = nullptr;  // bf16 [rows, W]
   long ldx = 0;
@@ -79,6 +83,8 @@ struct GateBwdDesc {
   long rows = 0;
   int W = 0;
   long rows_per_batch = 1;
+  const int* groups = nullptr;  // int32 [rows]: gate row of each row (overrides rows_per_batch)
+  int num_groups = 0;
   const void* dx = nullptr;  // bf16 [rows, W]
   long lddx = 0;
   const void* a = nullptr;  // bf16 [rows, W], the un-gated branch output
@@ -197,7 +203,8 @@ struct AttnFwdDesc {
   int kmask_words = 0;
   __nv_bfloat16* out = nullptr;
   long o_sb = 0, o_sl = 0, o_sh = 0;
-  float* lse = nullptr;
+  float* lse = nullptr;  // [B, H, Lq] with row stride stat_ld
+  long stat_ld = 0;      // floats between (b, h) rows of lse; a multiple of 4
   int* err = nullptr;
 };
 void attn_fwd_launch(const AttnFwdDesc& d, cudaStream_t stream);
@@ -214,8 +221,9 @@ struct AttnBwdDesc {
   const void* o = nullptr;     // forward output, token-major dense [B, Lq, H, D]
   const void* dout = nullptr;  // same layout
   long o_sb = 0, o_sl = 0, o_sh = 0;
-  const float* lse = nullptr;  // [B, H, Lq]
-  float* delta = nullptr;      // scratch [B, H, Lq]
+  const float* lse = nullptr;  // [B, H, Lq], row stride stat_ld
+  float* delta = nullptr;      // scratch [B, H, Lq], row stride stat_ld
+  long stat_ld = 0;            // floats between (b, h) rows; a multiple of 4 (16-byte TMA rows)
   const uint32_t* kmask = nullptr;
   int kmask_words = 0;
   __nv_bfloat16* dq = nullptr; // [B, H, Lq, D]

@@ -32,6 +32,14 @@ enum ErrorCode : int {
   kErrBadArgument = 6,
 };
 
+// Modulation (adaLN) row of activation row `row`: its entry of `groups`, clamped
+// into [0, num_groups), when a per-row group index is given; else row / rows_per_batch.
+__device__ __forceinline__ long mod_row(const int* groups, int num_groups, long row, long rows_per_batch) {
+  if (groups == nullptr) return row / rows_per_batch;
+  const int g = __ldg(groups + row);
+  return g < 0 ? 0 : (g >= num_groups ? num_groups - 1 : g);
+}
+
 __device__ __forceinline__ uint64_t globaltimer() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -73,7 +73,7 @@ __global__ void __launch_bounds__(256) rmsnorm_mod_fwd_kernel(NormDesc d) {
   }
   ss = warp_sum(ss);
   const float r = rsqrtf(ss / static_cast<float>(d.W) + d.eps);
-  const long b = row / d.rows_per_batch;
+  const long b = mod_row(d.groups, d.num_groups, row, d.rows_per_batch);
   __nv_bfloat16* yr = reinterpret_cast<__nv_bfloat16*>(d.y) + row * d.ldy;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) {
@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(256) rmsnorm_mod_bwd_rows_kernel(NormDesc d) {
   const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(d.x) + row * d.ldx;
   const __nv_bfloat16* dyr = reinterpret_cast<const __nv_bfloat16*>(d.dy) + row * d.lddy;
   const float r = d.rstd[row];
-  const long b = row / d.rows_per_batch;
+  const long b = mod_row(d.groups, d.num_groups, row, d.rows_per_batch);
   float n[VPL][8], g[VPL][8];
   float dot = 0.f;
 #pragma unroll
@@ -213,6 +213,61 @@ __global__ void __launch_bounds__(256) rmsnorm_mod_bwd_cols_kernel(NormDesc d, i
   }
 }
 
+// Column pass when each row names its own modulation row (`groups`). A CTA's row
+// range may then cross several groups: every thread keeps running sums for the
+// group of its current row and adds them to global memory when the group changes
+// or the range ends. Groups are piecewise constant along rows (a sample's clean
+// and noisy frames), so flushes are rare. Grid = (ceil(W/64), 1, row splits).
+__global__ void __launch_bounds__(256) rmsnorm_mod_bwd_cols_grouped_kernel(NormDesc d, int splits) {
+  const int tx = threadIdx.x & 31;
+  const int ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 64 + tx * 2;
+  if (c >= d.W) return;  // no block-wide barrier below
+  const long chunk = (d.rows + splits - 1) / splits;
+  const long r0 = blockIdx.z * chunk;
+  const long r1 = min(r0 + chunk, static_cast<long>(d.rows));
+  float w0 = 1.f, w1 = 1.f;
+  if (d.w != nullptr) { w0 = d.w[c]; w1 = d.w[c + 1]; }
+  float acc_w[2] = {0.f, 0.f}, acc_s[2] = {0.f, 0.f}, acc_t[2] = {0.f, 0.f};
+  long g = -1;
+  float s0 = 0.f, s1 = 0.f;
+  auto flush = [&]() {
+    if (g < 0) return;
+    if (d.dscale != nullptr) {
+      atomicAdd(d.dscale + g * d.dmod_stride + c, acc_s[0]);
+      atomicAdd(d.dscale + g * d.dmod_stride + c + 1, acc_s[1]);
+    }
+    if (d.dshift != nullptr) {
+      atomicAdd(d.dshift + g * d.dmod_stride + c, acc_t[0]);
+      atomicAdd(d.dshift + g * d.dmod_stride + c + 1, acc_t[1]);
+    }
+    acc_s[0] = acc_s[1] = acc_t[0] = acc_t[1] = 0.f;
+  };
+  for (long row = r0 + ty; row < r1; row += 8) {
+    const long gr = mod_row(d.groups, d.num_groups, row, 1);
+    if (gr != g) {
+      flush();
+      g = gr;
+      if (d.scale != nullptr) { s0 = d.scale[g * d.mod_stride + c]; s1 = d.scale[g * d.mod_stride + c + 1]; }
+    }
+    const uint32_t xv = *reinterpret_cast<const uint32_t*>(
+        reinterpret_cast<const __nv_bfloat16*>(d.x) + row * d.ldx + c);
+    const uint32_t gv = *reinterpret_cast<const uint32_t*>(
+        reinterpret_cast<const __nv_bfloat16*>(d.dy) + row * d.lddy + c);
+    const float r = d.rstd[row];
+    const float n0 = bf16_lo(xv) * r, n1 = bf16_hi(xv) * r;
+    const float g0 = bf16_lo(gv), g1 = bf16_hi(gv);
+    acc_t[0] += g0; acc_t[1] += g1;
+    acc_s[0] += g0 * n0 * w0; acc_s[1] += g1 * n1 * w1;
+    acc_w[0] += g0 * n0 * (1.f + s0); acc_w[1] += g1 * n1 * (1.f + s1);
+  }
+  flush();
+  if (d.dw != nullptr) {
+    atomicAdd(d.dw + c, acc_w[0]);
+    atomicAdd(d.dw + c + 1, acc_w[1]);
+  }
+}
+
 // da = dx * gate[b];  dgate[b] += sum_rows dx * a.   Same tiling as above.
 __global__ void __launch_bounds__(256) gate_bwd_kernel(GateBwdDesc d, int splits) {
   const int tx = threadIdx.x & 31;
@@ -251,8 +306,50 @@ __global__ void __launch_bounds__(256) gate_bwd_kernel(GateBwdDesc d, int splits
   }
 }
 
-template <template <int> class K>
-struct VplDispatch;
+// Grouped variant of gate_bwd_kernel (see rmsnorm_mod_bwd_cols_grouped_kernel).
+__global__ void __launch_bounds__(256) gate_bwd_grouped_kernel(GateBwdDesc d, int splits) {
+  const int tx = threadIdx.x & 31;
+  const int ty = threadIdx.x >> 5;
+  const int c = blockIdx.x * 64 + tx * 2;
+  if (c >= d.W) return;
+  const long chunk = (d.rows + splits - 1) / splits;
+  const long r0 = blockIdx.z * chunk;
+  const long r1 = min(r0 + chunk, static_cast<long>(d.rows));
+  float acc[2] = {0.f, 0.f};
+  long g = -1;
+  float g0 = 0.f, g1 = 0.f;
+  for (long row = r0 + ty; row < r1; row += 8) {
+    const long gr = mod_row(d.groups, d.num_groups, row, 1);
+    if (gr != g) {
+      if (g >= 0) {
+        atomicAdd(d.dgate + g * d.dgate_stride + c, acc[0]);
+        atomicAdd(d.dgate + g * d.dgate_stride + c + 1, acc[1]);
+      }
+      acc[0] = acc[1] = 0.f;
+      g = gr;
+      g0 = d.gate[g * d.gate_stride + c];
+      g1 = d.gate[g * d.gate_stride + c + 1];
+    }
+    const uint32_t dv = *reinterpret_cast<const uint32_t*>(
+        reinterpret_cast<const __nv_bfloat16*>(d.dx) + row * d.lddx + c);
+    const uint32_t av = *reinterpret_cast<const uint32_t*>(
+        reinterpret_cast<const __nv_bfloat16*>(d.a) + row * d.lda + c);
+    const float d0 = bf16_lo(dv), d1 = bf16_hi(dv);
+    acc[0] += d0 * bf16_lo(av);
+    acc[1] += d1 * bf16_hi(av);
+    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(d.da) + row * d.ldda + c) =
+        pack_bf16(d0 * g0, d1 * g1);
+  }
+  if (g >= 0) {
+    atomicAdd(d.dgate + g * d.dgate_stride + c, acc[0]);
+    atomicAdd(d.dgate + g * d.dgate_stride + c + 1, acc[1]);
+  }
+}
+
+int grouped_splits(long rows, int col_tiles, int sms) {
+  long s = (4L * sms) / std::max(1, col_tiles);
+  return static_cast<int>(std::max(1L, std::min(s, (rows + 63) / 64)));
+}
 
 int pick_vpl(int W) {
   const int need = (W + 255) / 256;
@@ -303,7 +400,12 @@ void rmsnorm_mod_bwd_launch(const NormDesc& d, cudaStream_t stream) {
     AVGEN_VPL_SWITCH(vpl, rmsnorm_mod_bwd_rows_kernel<V><<<blocks, 256, 0, stream>>>(d));
     AVGEN_CUDA_CHECK(cudaGetLastError());
   }
-  if (d.dw != nullptr || d.dscale != nullptr || d.dshift != nullptr) {
+  if (d.groups != nullptr && (d.dw != nullptr || d.dscale != nullptr || d.dshift != nullptr)) {
+    const int col_tiles = (d.W + 63) / 64;
+    const int splits = grouped_splits(d.rows, col_tiles, num_sms(d.device));
+    rmsnorm_mod_bwd_cols_grouped_kernel<<<dim3(col_tiles, 1, splits), 256, 0, stream>>>(d, splits);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
+  } else if (d.dw != nullptr || d.dscale != nullptr || d.dshift != nullptr) {
     const int col_tiles = (d.W + 63) / 64;
     const int batches = static_cast<int>((d.rows + d.rows_per_batch - 1) / d.rows_per_batch);
     const int splits = column_splits(d.rows_per_batch, col_tiles, batches, num_sms(d.device));
@@ -317,6 +419,12 @@ void gate_bwd_launch(const GateBwdDesc& d, cudaStream_t stream) {
   AVGEN_CHECK(d.W % 2 == 0, "gate_bwd: width must be even");
   if (d.rows == 0) return;
   const int col_tiles = (d.W + 63) / 64;
+  if (d.groups != nullptr) {
+    const int splits = grouped_splits(d.rows, col_tiles, num_sms(d.device));
+    gate_bwd_grouped_kernel<<<dim3(col_tiles, 1, splits), 256, 0, stream>>>(d, splits);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int batches = static_cast<int>((d.rows + d.rows_per_batch - 1) / d.rows_per_batch);
   const int splits = column_splits(d.rows_per_batch, col_tiles, batches, num_sms(d.device));
   dim3 grid(col_tiles, batches, splits);

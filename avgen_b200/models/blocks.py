@@ -101,17 +101,25 @@ class DiTBlock(nn.Module):
 
     def forward(self, hidden: torch.Tensor, *, modulation: torch.Tensor, rope: RotaryTables | RopeInputs | None = None,
                 key_mask: torch.Tensor | None = None, context: torch.Tensor | None = None,
-                context_mask: torch.Tensor | None = None) -> torch.Tensor:
+                context_mask: torch.Tensor | None = None,
+                modulation_index: torch.Tensor | None = None) -> torch.Tensor:
+        """One block. ``modulation`` is ``(B, 6, W)`` per sample, ``(B, L, 6, W)`` per
+        token, or ``(R, 6, W)`` shared rows picked per token by ``modulation_index``
+        ``(B, L)`` (integer row numbers)."""
         if modulation.ndim not in (3, 4):
             raise ValueError(f"modulation must be (batch, 6, width) or (batch, length, 6, width); got "
                              f"{tuple(modulation.shape)}")
+        if modulation_index is not None and modulation.ndim != 3:
+            raise ValueError("modulation_index selects rows of a (rows, 6, width) modulation")
         combined = modulation + self.scale_shift_table
-        if (self.use_fused and combined.ndim == 3 and _fused_eligible(self, hidden)
+        if (self.use_fused and _fused_eligible(self, hidden)
                 and (rope is None or isinstance(rope, RopeInputs))):
-            return self._fused(hidden, combined, rope, key_mask, context, context_mask)
+            return self._fused(hidden, combined, rope, key_mask, context, context_mask, modulation_index)
+        if modulation_index is not None:
+            combined = combined[modulation_index.long()]
         return self._eager(hidden, combined, rope, key_mask, context, context_mask)
 
-    def _fused(self, hidden, combined, rope, key_mask, context, context_mask):  # noqa: ANN001, ANN202
+    def _fused(self, hidden, combined, rope, key_mask, context, context_mask, mod_index=None):  # noqa: ANN001, ANN202
         from avgen_b200.models.fused import fused_block_forward
         from avgen_b200.ops.kernels import pack_key_mask
 
@@ -123,7 +131,8 @@ class DiTBlock(nn.Module):
         if self.cross_attention is None:
             context = None
         return fused_block_forward(self, hidden, combined, coords=coords, freq=freq, axis=axis, kmask=kmask,
-                                   context=context, cmask=cmask, attention_impl=self.attention_impl)
+                                   context=context, cmask=cmask, attention_impl=self.attention_impl,
+                                   mod_index=mod_index)
 
     def _eager(self, hidden, combined, rope, key_mask, context, context_mask):  # noqa: ANN001, ANN202
         parts = combined.unbind(-2)

@@ -186,8 +186,26 @@ class VideoDiT(nn.Module):
         return feats, mask
 
     def _stream_conditioning(self, stream: TokenStream, *, embed: TimestepEmbedding,
-                             modulation: AdaLNModulation) -> torch.Tensor:
-        return modulation(embed(stream.noise_level))
+                             modulation: AdaLNModulation) -> tuple[torch.Tensor, torch.Tensor | None]:
+        """adaLN modulation rows of a stream and the per-token row index.
+
+        Per-sample levels give ``(B, 6, W)`` and no index. Grouped per-token levels
+        (``level_values`` / ``level_index``) give one row per distinct level,
+        ``(B*G, 6, W)``, and the ``(B, L)`` row of every token; plain per-token
+        levels give one row per token. The reference computes the per-token form
+        ``(B, L, 6, W)`` (avgen/models/dit.py:330-352); the rows are identical.
+        """
+        if stream.has_level_groups:
+            b, g = stream.level_values.shape
+            rows = modulation(embed(stream.level_values.reshape(-1)))
+            base = torch.arange(b, device=stream.level_index.device, dtype=torch.int32)[:, None] * g
+            return rows, stream.level_index + base
+        if stream.per_token_noise:
+            b, length = stream.noise_level.shape
+            rows = modulation(embed(stream.noise_level.reshape(-1)))
+            index = torch.arange(b * length, device=rows.device, dtype=torch.int32).view(b, length)
+            return rows, index
+        return modulation(embed(stream.noise_level)), None
 
     def _global_mask(self, mask: torch.Tensor) -> torch.Tensor:
         """Key validity over the whole sequence (gathered across context-parallel shards)."""
@@ -203,10 +221,10 @@ class VideoDiT(nn.Module):
 
     def _denoise(self, hidden: torch.Tensor, *, modulation: torch.Tensor, rope: RopeInputs | None,
                  key_mask: torch.Tensor | None, context: torch.Tensor | None,
-                 context_mask: torch.Tensor | None) -> torch.Tensor:
+                 context_mask: torch.Tensor | None, modulation_index: torch.Tensor | None = None) -> torch.Tensor:
         for block in self.blocks:
             hidden = block(hidden, modulation=modulation, rope=rope, key_mask=key_mask, context=context,
-                           context_mask=context_mask)
+                           context_mask=context_mask, modulation_index=modulation_index)
         return hidden
 
     def _video_head(self, hidden: torch.Tensor, stream: TokenStream) -> torch.Tensor:
@@ -225,11 +243,11 @@ class VideoDiT(nn.Module):
         if tokens.device.type == "cuda":
             tokens = tokens.to(torch.bfloat16)
         hidden = linear(match_dtype(tokens, self.patch_embed), self.patch_embed)
-        modulation = self._stream_conditioning(video, embed=self.time_embed, modulation=self.modulation)
+        modulation, mod_index = self._stream_conditioning(video, embed=self.time_embed, modulation=self.modulation)
         rope = self._rope_inputs(video.coords)
         key_mask = key_padding_mask(self._global_mask(video.mask), assume_dense=self.config.assume_dense_mask)
         hidden = self._denoise(hidden, modulation=modulation, rope=rope, key_mask=key_mask, context=context,
-                               context_mask=context_mask)
+                               context_mask=context_mask, modulation_index=mod_index)
         predicted = self._video_head(hidden, video)
         return ModelOutput(video=predicted, audio=self._null_audio(inputs, predicted))
 
@@ -375,13 +393,16 @@ class AVDiT(VideoDiT):
         context, context_mask = self.encode_text(inputs.text)
         hidden = torch.cat((self._embed(video, self.patch_embed),
                             linear(self._embed(audio, self.audio_patch_embed), self.audio_in_proj)), 1)
-        vmod = self.modulation(self.time_embed(video.noise_level))
-        amod = self.audio_modulation(self.audio_time_embed(audio.noise_level))
-        modulation = torch.cat((_expand_modulation(vmod, video.length), _expand_modulation(amod, audio.length)), 1)
+        vrows, vidx = self._stream_conditioning(video, embed=self.time_embed, modulation=self.modulation)
+        arows, aidx = self._stream_conditioning(audio, embed=self.audio_time_embed, modulation=self.audio_modulation)
+        vidx = _row_index(vrows, vidx, video.batch_size, video.length)
+        aidx = _row_index(arows, aidx, audio.batch_size, audio.length)
+        modulation = torch.cat((vrows, arows), 0)
+        mod_index = torch.cat((vidx, aidx + vrows.shape[0]), 1)
         rope = self._rope_inputs(torch.cat((video.coords, audio.coords), 1))
         key_mask = key_padding_mask(torch.cat((video.mask, audio.mask), 1), assume_dense=self.config.assume_dense_mask)
         hidden = self._denoise(hidden, modulation=modulation, rope=rope, key_mask=key_mask, context=context,
-                               context_mask=context_mask)
+                               context_mask=context_mask, modulation_index=mod_index)
         vh, ah = hidden.split((video.length, audio.length), 1)
         pa = linear(self.audio_final_norm(linear(ah, self.audio_out_proj)), self.audio_final_proj)
         pa = pa * audio.mask.unsqueeze(-1).to(pa.dtype)
@@ -394,8 +415,8 @@ class AVDiT(VideoDiT):
         actx, actx_mask = self._audio_context(inputs.text)
         vh = self._embed(video, self.patch_embed)
         ah = self._embed(audio, self.audio_patch_embed)
-        vmod = self.modulation(self.time_embed(video.noise_level))
-        amod = self.audio_modulation(self.audio_time_embed(audio.noise_level))
+        vmod, vidx = self._stream_conditioning(video, embed=self.time_embed, modulation=self.modulation)
+        amod, aidx = self._stream_conditioning(audio, embed=self.audio_time_embed, modulation=self.audio_modulation)
         vrope = self._rope_inputs(video.coords)
         arope = self._rope_inputs(audio.coords, self.audio_rope)
         vkm = key_padding_mask(video.mask, assume_dense=c.assume_dense_mask)
@@ -406,9 +427,10 @@ class AVDiT(VideoDiT):
                                       key_mask=video.mask)
         fusion_at = {p: i for i, p in enumerate(c.fusion_points)}
         for i in range(c.depth):
-            vh = self.blocks[i](vh, modulation=vmod, rope=vrope, key_mask=vkm, context=context, context_mask=context_mask)
+            vh = self.blocks[i](vh, modulation=vmod, rope=vrope, key_mask=vkm, context=context, context_mask=context_mask,
+                                modulation_index=vidx)
             ah = self.audio_blocks[i](ah, modulation=amod, rope=arope, key_mask=akm, context=actx,
-                                      context_mask=actx_mask)
+                                      context_mask=actx_mask, modulation_index=aidx)
             fi = fusion_at.get(i)
             if fi is not None:
                 vh, ah = self.fusion_blocks[fi](vh, ah, video_to_audio=v2a, audio_to_video=a2v)
@@ -424,12 +446,11 @@ class AVDiT(VideoDiT):
         return self._forward_two_tower(inputs)
 
 
-def _expand_modulation(mod: torch.Tensor, length: int) -> torch.Tensor:
-    if mod.ndim == 4:
-        if mod.shape[1] != length:
-            raise ValueError("per-token modulation length mismatch")
-        return mod
-    return mod[:, None].expand(-1, length, -1, -1)
+def _row_index(rows: torch.Tensor, index: torch.Tensor | None, batch: int, length: int) -> torch.Tensor:
+    """Per-token modulation row numbers; per-sample rows become ``b`` for every token of sample ``b``."""
+    if index is not None:
+        return index
+    return torch.arange(batch, device=rows.device, dtype=torch.int32)[:, None].expand(batch, length)
 
 
 # Identity module in AVDiT joint mode goes through `linear` only for nn.Linear.

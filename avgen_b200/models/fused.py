@@ -82,6 +82,12 @@ class BlockSpec:
     ctx_kv_heads: int = 0
     text_length: int = 0
     attention: AttentionImpl | None = None
+    mod_rows_per_batch: int = 0   # rows sharing one modulation row (0: ``length``)
+    groups: torch.Tensor | None = None  # int32 [B*L] modulation row per token (overrides the above)
+
+    def mod_rows(self) -> dict[str, Any]:
+        """Keyword arguments selecting each token's modulation row in the kernels."""
+        return {"rows_per_batch": self.mod_rows_per_batch or self.length, "groups": self.groups}
 
 
 def _packed(module: nn.Module, key: str, params: list[torch.Tensor], build) -> torch.Tensor:  # noqa: ANN001
@@ -145,7 +151,7 @@ def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     shift_a, scale_a, gate_a = modf[:, 0], modf[:, 1], modf[:, 2]
     shift_f, scale_f, gate_f = modf[:, 3], modf[:, 4], modf[:, 5]
     att = block.attention
-    n1, rstd1 = K.rmsnorm_mod(xb, _norm_weight(block.attention_norm), scale_a, shift_a, rows_per_batch=length,
+    n1, rstd1 = K.rmsnorm_mod(xb, _norm_weight(block.attention_norm), scale_a, shift_a, **spec.mod_rows(),
                               eps=block.attention_norm.eps or eps)
     qkv = K.gemm(n1, pw["qkv"])
     qw = _norm_weight(att.q_norm) if spec.qk_norm else None
@@ -177,7 +183,7 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep):  # noqa: AN
     shift_f, scale_f, gate_f = modf[:, 3], modf[:, 4], modf[:, 5]
     keep_d: dict[str, Any] = {}
     a_o = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
-    x1 = K.gemm(o.view(m, -1), pw["o"], epilogue="gate_resid", resid=xb, gate=gate_a, rows_per_batch=length,
+    x1 = K.gemm(o.view(m, -1), pw["o"], epilogue="gate_resid", resid=xb, gate=gate_a, **spec.mod_rows(),
                 aux=a_o)
     x2 = x1
     if spec.cross and ctxb is not None:
@@ -198,7 +204,7 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep):  # noqa: AN
             keep_d.update(x1=x1, n2=n2, rstd2=rstd2, qc=qc, kvc=kvc, qh=qh, kc=kc, vc=vc, oc=oc, lsec=lsec)
     elif keep:
         keep_d.update(x1=x1)
-    n3, rstd3 = K.rmsnorm_mod(x2, _norm_weight(block.ffn_norm), scale_f, shift_f, rows_per_batch=length,
+    n3, rstd3 = K.rmsnorm_mod(x2, _norm_weight(block.ffn_norm), scale_f, shift_f, **spec.mod_rows(),
                               eps=block.ffn_norm.eps or eps)
     if spec.ffn == "swiglu":
         gu = torch.empty((m, 2 * spec.hidden), device=xb.device, dtype=_BF16) if keep else None
@@ -210,7 +216,7 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep):  # noqa: AN
         f = K.gemm(hdn, pw["down"])
         keep_d.update(a_o=a_o, x2=x2, n3=n3, rstd3=rstd3, gu=gu, h=hdn, f=f)
         return None, keep_d
-    x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, rows_per_batch=length)
+    x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, **spec.mod_rows())
     return x3, keep_d
 
 
@@ -235,7 +241,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     # ---------------------------------------------------------------- recompute
     inter, _, _, _ = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, save=False)
     _, keep = _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, keep=True)
-    dmod = torch.zeros_like(modf)  # [B, 6, W]
+    dmod = torch.zeros_like(modf)  # [modulation rows, 6, W]
     gate_a, gate_f = modf[:, 2], modf[:, 5]
     dx3 = dout.reshape(m, w).to(_BF16).contiguous()
 
@@ -243,7 +249,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
         return torch.zeros(p.shape, device=dev, dtype=torch.float32)
 
     # ---------------------------------------------------------------- FFN
-    df = K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], rows_per_batch=length)
+    df = K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], **spec.mod_rows())
     dh = K.linear_dx(df, pw["down"])
     g_down = zeros_like_param(ff.down_proj.weight)
     K.linear_dw(df, keep["h"], g_down)
@@ -263,7 +269,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     g_ffn_norm = zeros_like_param(block.ffn_norm.weight) if block.ffn_norm.weight is not None else None
     dx2 = K.rmsnorm_mod_bwd(keep["x2"], keep["rstd3"], dn3, _norm_weight(block.ffn_norm), modf[:, 4], modf[:, 3],
                             dres=dx3, dweight=g_ffn_norm, dscale=dmod[:, 4], dshift=dmod[:, 3],
-                            rows_per_batch=length)
+                            **spec.mod_rows())
     # ---------------------------------------------------------------- cross attention
     dctx = None
     cross_grads: list[torch.Tensor | None] = []
@@ -301,7 +307,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     else:
         dx1 = dx2
     # ---------------------------------------------------------------- self attention
-    da = K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], rows_per_batch=length)
+    da = K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], **spec.mod_rows())
     do = K.linear_dx(da, pw["o"])
     g_o = zeros_like_param(att.out_proj.weight)
     K.linear_dw(da, o.view(m, -1), g_o)
@@ -321,7 +327,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     g_attn_norm = zeros_like_param(block.attention_norm.weight) if block.attention_norm.weight is not None else None
     dx = K.rmsnorm_mod_bwd(xb, inter["rstd1"], dn1, _norm_weight(block.attention_norm), modf[:, 1], modf[:, 0],
                            dres=dx1, dweight=g_attn_norm, dscale=dmod[:, 1], dshift=dmod[:, 0],
-                           rows_per_batch=length)
+                           **spec.mod_rows())
     qr, kr = h * d, hk * d
     pgrads = {
         "attention_norm.weight": g_attn_norm,
@@ -392,9 +398,25 @@ class FusedBlockFn(torch.autograd.Function):
 def fused_block_forward(block: nn.Module, hidden: torch.Tensor, combined_mod: torch.Tensor, *,
                         coords: torch.Tensor | None, freq: torch.Tensor | None, axis: torch.Tensor | None,
                         kmask: torch.Tensor | None, context: torch.Tensor | None, cmask: torch.Tensor | None,
-                        attention_impl: AttentionImpl | None = None) -> torch.Tensor:
-    """Run ``block`` through :class:`FusedBlockFn` (CUDA only)."""
+                        attention_impl: AttentionImpl | None = None,
+                        mod_index: torch.Tensor | None = None) -> torch.Tensor:
+    """Run ``block`` through :class:`FusedBlockFn` (CUDA only).
+
+    ``combined_mod`` is the block's adaLN modulation (shared rows plus its table):
+    ``(B, 6, W)`` per sample, ``(B, L, 6, W)`` per token, or ``(R, 6, W)`` rows that
+    ``mod_index`` ``(B, L)`` selects for each token. The last form is how per-token
+    noise levels with few distinct values (clean conditioning frames vs. noisy ones)
+    stay cheap: the kernels read each token's row through the index instead of a
+    materialised per-token tensor.
+    """
     b, length, w = hidden.shape
+    rpb = 0
+    groups = None
+    if mod_index is not None:
+        groups = mod_index.reshape(-1).to(torch.int32).contiguous()
+    elif combined_mod.ndim == 4:
+        combined_mod = combined_mod.reshape(b * length, *combined_mod.shape[2:])
+        rpb = 1
     att = block.attention
     ff = block.feed_forward
     ffn = "swiglu" if hasattr(ff, "gate_proj") else "gelu"
@@ -405,6 +427,7 @@ def fused_block_forward(block: nn.Module, hidden: torch.Tensor, combined_mod: to
                      qk_norm=isinstance(att.q_norm, nn.RMSNorm), cross=ca is not None and context is not None,
                      ctx_heads=ca.num_heads if ca is not None else 0,
                      ctx_kv_heads=ca.num_kv_heads if ca is not None else 0,
-                     text_length=context.shape[1] if context is not None else 0, attention=attention_impl)
+                     text_length=context.shape[1] if context is not None else 0, attention=attention_impl,
+                     mod_rows_per_batch=rpb, groups=groups)
     params = [p for n, p in block.named_parameters() if n != "scale_shift_table"]
     return FusedBlockFn.apply(spec, block, coords, freq, axis, kmask, cmask, hidden, combined_mod, context, *params)

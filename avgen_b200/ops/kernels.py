@@ -13,6 +13,9 @@ the conventions of the kernels:
 from __future__ import annotations
 
 import math
+import os
+import sys
+import time
 
 import torch
 
@@ -22,10 +25,28 @@ EPILOGUES = {"store": 0, "gate_resid": 1, "swiglu": 2, "gelu": 3, "atomic": 4}
 
 # Running count of kernel launches issued through this module (benchmarks read it).
 LAUNCHES = [0]
+# AVGEN_KERNEL_DEBUG=1: synchronise after every wrapper call, report its device time
+# and stop at the first call that leaves a timed-out wait in the device error word.
+_DEBUG = os.environ.get("AVGEN_KERNEL_DEBUG") == "1"
 
 
 def _count(n: int = 1) -> None:
     LAUNCHES[0] += n
+    if _DEBUG:
+        _debug_check(sys._getframe(1).f_code.co_name)
+
+
+def _debug_check(name: str) -> None:
+    from avgen_b200.ops._ext import check_errors
+
+    t0 = time.perf_counter()
+    torch.cuda.synchronize()
+    dt = time.perf_counter() - t0
+    code = check_errors(clear=False)
+    if dt > 0.5 or code:
+        print(f"[avgen kernel debug] {name}: {dt * 1e3:.1f} ms after launch, error word {code}", flush=True)
+    if code:
+        raise RuntimeError(f"kernel wrapper {name} left error code {code}")
 
 
 def launch_count() -> int:
@@ -51,8 +72,13 @@ def gemm(
     rows_per_batch: int = 1,
     aux: torch.Tensor | None = None,
     k_splits: int = 1,
+    groups: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """tcgen05 GEMM with a fused epilogue (see ``csrc/gemm.cu``)."""
+    """tcgen05 GEMM with a fused epilogue (see ``csrc/gemm.cu``).
+
+    ``gate`` rows are picked per output row by ``groups`` (int32, one entry per
+    row) when given, else by ``row // rows_per_batch``.
+    """
     m = a.shape[1] if a_mn else a.shape[0]
     n = b.shape[1] if b_mn else b.shape[0]
     if out is None:
@@ -62,7 +88,7 @@ def gemm(
         else:
             out = torch.empty((m, cols), device=a.device, dtype=out_dtype)
     load().gemm(
-        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits
+        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits, groups
     )
     _count()
     return out
@@ -98,11 +124,13 @@ def rmsnorm_mod(
     eps: float = 1e-6,
     out: torch.Tensor | None = None,
     want_rstd: bool = True,
+    groups: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
-    """``rmsnorm(x) * weight * (1 + scale[b]) + shift[b]`` over rows of ``x[R, W]``."""
+    """``rmsnorm(x) * weight * (1 + scale[g]) + shift[g]`` over rows of ``x[R, W]``, with
+    ``g = groups[row]`` when a per-row group index is given, else ``row // rows_per_batch``."""
     y = out if out is not None else torch.empty_like(x)
     rstd = torch.empty(x.shape[0], device=x.device, dtype=_F32) if want_rstd else None
-    load().rmsnorm_mod_fwd(x, y, rstd, weight, scale, shift, rows_per_batch, eps)
+    load().rmsnorm_mod_fwd(x, y, rstd, weight, scale, shift, rows_per_batch, eps, groups)
     _count()
     return y, rstd
 
@@ -121,22 +149,24 @@ def rmsnorm_mod_bwd(
     dshift: torch.Tensor | None = None,
     rows_per_batch: int = 1,
     dx: torch.Tensor | None = None,
+    groups: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """Backward of :func:`rmsnorm_mod`; parameter grads accumulate (fp32)."""
     dx = dx if dx is not None else torch.empty_like(x)
     load().rmsnorm_mod_bwd(
-        x, rstd, dy, dx, dres, weight, scale, shift, dweight, dscale, dshift, rows_per_batch
+        x, rstd, dy, dx, dres, weight, scale, shift, dweight, dscale, dshift, rows_per_batch, groups
     )
     _count(2 if (dweight is not None or dscale is not None or dshift is not None) else 1)
     return dx
 
 
 def gate_bwd(
-    dx: torch.Tensor, a: torch.Tensor, gate: torch.Tensor, dgate: torch.Tensor, *, rows_per_batch: int
+    dx: torch.Tensor, a: torch.Tensor, gate: torch.Tensor, dgate: torch.Tensor, *, rows_per_batch: int,
+    groups: torch.Tensor | None = None,
 ) -> torch.Tensor:
-    """``da = dx * gate[b]`` and ``dgate[b] += sum_rows(dx * a)``."""
+    """``da = dx * gate[g]`` and ``dgate[g] += sum_rows(dx * a)`` (``g`` as in :func:`rmsnorm_mod`)."""
     da = torch.empty_like(dx)
-    load().gate_bwd(dx, a, gate, da, dgate, rows_per_batch)
+    load().gate_bwd(dx, a, gate, da, dgate, rows_per_batch, groups)
     _count()
     return da
 
@@ -254,6 +284,13 @@ def pack_key_mask(mask: torch.Tensor | None) -> torch.Tensor | None:
     return packed.to(torch.int32).contiguous()
 
 
+def row_stats(b: int, h: int, length: int, device: torch.device) -> torch.Tensor:
+    """An fp32 ``[b, h, length]`` tensor whose ``(b, h)`` rows are padded to 16 bytes
+    (the attention backward streams these rows with TMA)."""
+    padded = -(-length // 4) * 4
+    return torch.empty((b, h, padded), device=device, dtype=_F32)[..., :length]
+
+
 def attention_fwd(
     q: torch.Tensor,
     k: torch.Tensor,
@@ -269,7 +306,7 @@ def attention_fwd(
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     if out is None:
         out = torch.empty((b, lq, h, d), device=q.device, dtype=_BF16)
-    lse = torch.empty((b, h, lq), device=q.device, dtype=_F32) if want_lse else None
+    lse = row_stats(b, h, lq, q.device) if want_lse else None
     load().attn_fwd(q, k, v, out, lse, kmask, scale)
     _count()
     return out, lse
@@ -289,7 +326,7 @@ def attention_bwd(
     """Flash attention backward. Returns ``(dq, dk, dv)`` (bf16, shapes of q, k, v)."""
     d = q.shape[-1]
     scale = 1.0 / math.sqrt(d) if scale is None else scale
-    delta = torch.empty_like(lse)
+    delta = torch.empty_strided(lse.shape, lse.stride(), device=lse.device, dtype=_F32)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)

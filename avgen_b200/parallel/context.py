@@ -59,8 +59,14 @@ def pad_to_multiple(stream: TokenStream, multiple: int) -> TokenStream:
         return torch.cat((t, torch.zeros(shape, dtype=t.dtype, device=t.device)), 1)
 
     noise = padt(stream.noise_level) if stream.per_token_noise else stream.noise_level
+    values, index = stream.level_values, stream.level_index
+    if stream.has_level_groups:  # padding tokens sit at level 0: give them a group of their own
+        g = values.shape[1]
+        values = torch.cat((values, torch.zeros((b, 1), dtype=values.dtype, device=values.device)), 1)
+        index = torch.cat((index, torch.full((b, pad), g, dtype=index.dtype, device=index.device)), 1)
     return TokenStream(tokens=padt(stream.tokens), coords=padt(stream.coords), mask=padt(stream.mask),
-                       noise_level=noise, layout=stream.layout, conditioned=padt(stream.conditioned))
+                       noise_level=noise, layout=stream.layout, conditioned=padt(stream.conditioned),
+                       level_values=values, level_index=index)
 
 
 def _cp(mesh: DeviceMesh | None) -> tuple[int, int]:
@@ -76,8 +82,9 @@ def shard_stream(stream: TokenStream, mesh: DeviceMesh | None) -> TokenStream:
         return stream
     lo, hi = shard_bounds(stream.length, shards, index)
     noise = stream.noise_level[:, lo:hi] if stream.per_token_noise else stream.noise_level
+    index = stream.level_index[:, lo:hi] if stream.has_level_groups else stream.level_index
     return replace(stream, tokens=stream.tokens[:, lo:hi], coords=stream.coords[:, lo:hi], mask=stream.mask[:, lo:hi],
-                   noise_level=noise, conditioned=stream.conditioned[:, lo:hi])
+                   noise_level=noise, conditioned=stream.conditioned[:, lo:hi], level_index=index)
 
 
 def _gather_dim1(t: torch.Tensor, mesh: DeviceMesh) -> torch.Tensor:
@@ -90,9 +97,10 @@ def gather_stream(stream: TokenStream, mesh: DeviceMesh | None) -> TokenStream:
     if mesh is None or mesh.size() == 1 or not (dist.is_available() and dist.is_initialized()):
         return stream
     noise = _gather_dim1(stream.noise_level, mesh) if stream.per_token_noise else stream.noise_level
+    index = _gather_dim1(stream.level_index, mesh) if stream.has_level_groups else stream.level_index
     return replace(stream, tokens=_gather_dim1(stream.tokens, mesh), coords=_gather_dim1(stream.coords, mesh),
                    mask=_gather_dim1(stream.mask, mesh), noise_level=noise,
-                   conditioned=_gather_dim1(stream.conditioned, mesh))
+                   conditioned=_gather_dim1(stream.conditioned, mesh), level_index=index)
 
 
 def gather_tokens(tensor: torch.Tensor, mesh: DeviceMesh | None) -> torch.Tensor:

@@ -193,6 +193,9 @@ class FlowMatchingObjective:
         clean = patchifier.to_tokens(grid, positions=positions, mask=mask, noise_level=timesteps,
                                      conditioned=conditioned)
         per_token = clean.noise_level[:, None] * (~clean.conditioned).to(torch.float32)
+        # two levels per sample: t for noisy tokens, 0 for clean conditioning anchors
+        clean = replace(clean, level_values=torch.stack((clean.noise_level, torch.zeros_like(clean.noise_level)), 1),
+                        level_index=clean.conditioned.to(torch.int32))
         if clean.tokens.device.type == "cuda":
             from avgen_b200.ops import kernels as K
 

@@ -204,7 +204,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     shape = dict(batch=1, channels=CHANNELS, frames=args.frames, height=HEIGHT, width=WIDTH_PX,
                  text_tokens=TEXT_TOKENS, text_width=TEXT_WIDTH)
     dev_batches = [random_batch(**shape, generator=gen, device=dev) for _ in range(micro)]
-    tokens = dev_batches[0].spec.video_tokens
+    pt, ph, pw = model.config.patch_frames, model.config.patch_height, model.config.patch_width
+    tokens = dev_batches[0].spec.video_tokens // (pt * ph * pw)  # transformer tokens (patches)
 
     def step(batches) -> object:
         metrics = None

@@ -17,8 +17,9 @@ def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
     return float((a - b).norm() / (b.norm() + 1e-12))
 
 
-@pytest.mark.parametrize("ffn,masked", [("swiglu", False), ("gelu", True)])
-def test_fused_block_matches_eager(ffn: str, masked: bool) -> None:
+@pytest.mark.parametrize("ffn,masked,grouped", [("swiglu", False, False), ("gelu", True, False),
+                                                 ("swiglu", True, True)])
+def test_fused_block_matches_eager(ffn: str, masked: bool, grouped: bool) -> None:
     torch.manual_seed(0)
     width, heads, hidden, b, length, t = 256, 2, 512, 2, 384, 24
     block = DiTBlock(width, heads, hidden=hidden, ffn=ffn)
@@ -28,7 +29,12 @@ def test_fused_block_matches_eager(ffn: str, masked: bool) -> None:
             p.add_(0.02 * torch.randn_like(p))
     rope = RotaryEmbedding(128)
     x = torch.randn(b, length, width)
-    mod = 0.1 * torch.randn(b, 6, width)
+    mod_index = None
+    if grouped:  # two modulation rows per sample: clean first frame (row 2b+1), noisy rest (row 2b)
+        mod = 0.1 * torch.randn(2 * b, 6, width)
+        mod_index = (torch.arange(b)[:, None] * 2 + (torch.arange(length) < 96).long()[None]).int()
+    else:
+        mod = 0.1 * torch.randn(b, 6, width)
     ctx = torch.randn(b, t, width)
     coords = torch.rand(b, length, 3) * 8
     kmask = None
@@ -41,7 +47,7 @@ def test_fused_block_matches_eager(ffn: str, masked: bool) -> None:
     ref_block = copy.deepcopy(block)
     xr, modr, ctxr = (v.clone().requires_grad_() for v in (x, mod, ctx))
     out_ref = ref_block(xr, modulation=modr, rope=RopeInputs(coords, rope), key_mask=kmask, context=ctxr,
-                        context_mask=cmask)
+                        context_mask=cmask, modulation_index=mod_index)
     g = torch.randn_like(out_ref)
     out_ref.backward(g)
     # fused on the GPU
@@ -50,7 +56,7 @@ def test_fused_block_matches_eager(ffn: str, masked: bool) -> None:
     modg = mod.cuda().requires_grad_()
     ctxg = ctx.cuda().bfloat16().requires_grad_()
     out = gb(xg, modulation=modg, rope=RopeInputs(coords.cuda(), rope), key_mask=None if kmask is None else kmask.cuda(),
-             context=ctxg, context_mask=cmask.cuda())
+             context=ctxg, context_mask=cmask.cuda(), modulation_index=None if mod_index is None else mod_index.cuda())
     out.backward(g.cuda().bfloat16())
     assert _rel(out, out_ref) < 3e-2
     assert _rel(xg.grad, xr.grad) < 5e-2

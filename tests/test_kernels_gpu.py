@@ -255,3 +255,75 @@ def test_adamw_matches_torch() -> None:
     out = torch.zeros(1, device=DEV)
     ops.sq_norm_(p, out)
     torch.testing.assert_close(out[0], p.pow(2).sum(), rtol=1e-4, atol=1e-4)
+
+
+def _piecewise_groups(rows: int, groups: int, gen: torch.Generator) -> torch.Tensor:
+    """Row -> modulation row, constant over random runs (like clean / noisy frames)."""
+    cuts = torch.sort(torch.randint(0, rows, (groups * 2,), generator=gen)).values.tolist()
+    out = torch.zeros(rows, dtype=torch.int32)
+    g = 0
+    for i, c in enumerate(cuts):
+        out[c:] = (g + i) % groups
+    return out
+
+
+def test_grouped_modulation_kernels() -> None:
+    ops = _ops()
+    gen = torch.Generator().manual_seed(11)
+    rows, w_, ng = 777, 384, 5
+    groups_cpu = _piecewise_groups(rows, ng, gen)
+    groups = groups_cpu.to(DEV)
+    gl = groups_cpu.long().to(DEV)
+    x = torch.randn(rows, w_, generator=gen).to(DEV).bfloat16()
+    weight = (torch.rand(w_, generator=gen) + 0.5).to(DEV)
+    mod = (torch.randn(ng, 3, w_, generator=gen) * 0.1).to(DEV)
+    scale, shift, gate = mod[:, 0], mod[:, 1], mod[:, 2]
+    y, rstd = ops.rmsnorm_mod(x, weight, scale, shift, groups=groups)
+    xr = x.float().requires_grad_()
+    modr = mod.clone().requires_grad_()
+    wr = weight.clone().requires_grad_()
+    ref = F.rms_norm(xr, (w_,), wr, 1e-6) * (1 + modr[:, 0][gl]) + modr[:, 1][gl]
+    _close(y, ref)
+    dy = torch.randn(rows, w_, generator=gen).to(DEV).bfloat16()
+    ref.backward(dy.float())
+    dmod = torch.zeros_like(mod)
+    dw = torch.zeros(w_, device=DEV)
+    dx = ops.rmsnorm_mod_bwd(x, rstd, dy, weight, scale, shift, dweight=dw, dscale=dmod[:, 0], dshift=dmod[:, 1],
+                             groups=groups)
+    _close(dx, xr.grad)
+    _close(dw, wr.grad, rtol=1e-2, atol=1e-2)
+    _close(dmod[:, :2], modr.grad[:, :2], rtol=1e-2, atol=1e-2)
+    # gate backward and the gated-residual GEMM epilogue with the same groups
+    a = torch.randn(rows, w_, generator=gen).to(DEV).bfloat16()
+    da = ops.gate_bwd(dy, a, gate, dmod[:, 2], rows_per_batch=1, groups=groups)
+    _close(da, dy.float() * gate[gl])
+    ref_dg = torch.zeros(ng, w_, device=DEV).index_add_(0, gl, dy.float() * a.float())
+    _close(dmod[:, 2], ref_dg, rtol=1e-2, atol=1e-2)
+    wt = (torch.randn(w_, 256, generator=gen) * 0.05).to(DEV).bfloat16()
+    resid = torch.randn(rows, w_, generator=gen).to(DEV).bfloat16()
+    inp = torch.randn(rows, 256, generator=gen).to(DEV).bfloat16()
+    got = ops.gemm(inp, wt, epilogue="gate_resid", resid=resid, gate=gate, groups=groups)
+    _close(got, resid.float() + gate[gl] * (inp.float() @ wt.float().t()))
+    _errors_clear()
+
+
+@pytest.mark.parametrize("lq,lk", [(77, 16), (5, 130)])
+def test_attention_odd_lengths(lq: int, lk: int) -> None:
+    """Short and unaligned sequence lengths (text tokens): padded row statistics."""
+    ops = _ops()
+    torch.manual_seed(12)
+    b, h, d = 2, 2, 128
+    q = torch.randn(b, h, lq, d, device=DEV).bfloat16()
+    k = torch.randn(b, h, lk, d, device=DEV).bfloat16()
+    v = torch.randn(b, h, lk, d, device=DEV).bfloat16()
+    out, lse = ops.attention_fwd(q, k, v)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    ref = _attn_ref(qr, kr, vr, None, 1.0 / math.sqrt(d))
+    _close(out, ref)
+    dout = torch.randn_like(ref).bfloat16()
+    ref.backward(dout.float())
+    dq, dk, dv = ops.attention_bwd(q, k, v, out, dout.contiguous(), lse)
+    _close(dq, qr.grad, rtol=3e-2, atol=3e-2)
+    _close(dk, kr.grad, rtol=3e-2, atol=3e-2)
+    _close(dv, vr.grad, rtol=3e-2, atol=3e-2)
+    _errors_clear()

@@ -305,7 +305,7 @@ __global__ void __launch_bounds__(384, 1)
         }
       }
       if (q < p.Lq && p.lse != nullptr)
-        p.lse[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] = l > 0.f ? m + __log2f(l) : -INFINITY;
+        p.lse[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] = l > 0.f ? m + __log2f(l) : INFINITY;
     }
   }
 
@@ -364,7 +364,20 @@ __device__ __forceinline__ void store_row_bf16(__nv_bfloat16* dst, const uint32_
 
 // ------------------------------------------------------------------ dK / dV
 // CTA = (batch, kv head, 128 keys); loops over 64-query tiles of every query head
-// of the group. TMEM: S^T[2] (64 cols each), dP^T[2] (64), dV (128), dK (128).
+// of the group. S^T = K Q^T and dP^T = V dO^T land in TMEM (double-buffered);
+// eight softmax warps (two per TMEM lane quadrant, one per 32-query half) turn
+// them into P^T and dS^T in place, which the tensor core then consumes directly
+// from TMEM: dV += P^T dO, dK += dS^T Q.
+//
+// Elementwise work per score is one FFMA, one EX2, one FADD and one FMUL. No
+// bounds tests are needed: rows of Q / dO / lse / delta past Lq arrive as TMA
+// zero fill, and dP^T = 0, delta = 0 there, so they add nothing to dK or dV.
+// Queries whose every key is masked carry lse = +inf (P = 0). Keys that are
+// masked or past Lk only touch their own dK / dV rows, which are stored as 0.
+//
+// TMEM columns: S^T[b] at 64*b, dP^T[b] at 128 + 64*b, dV at 256, dK at 384.
+// Half h of a buffer writes its bf16 pairs to columns [32h, 32h + 16), inside
+// the 32 columns only it reads, so the two halves never race.
 struct DkvSmem {
   static constexpr int K = 0;           // 32 KB (2 chunks x 16 KB)
   static constexpr int V = 32768;       // 32 KB
@@ -376,7 +389,10 @@ struct DkvSmem {
 };
 constexpr int kQT = 64;  // query tile of the dK/dV kernel
 
-__global__ void __launch_bounds__(256, 1)
+// TMEM column of k-step kk (16 queries) of a P^T / dS^T buffer written as above.
+__device__ __forceinline__ uint32_t half_packed_col(int kk) { return static_cast<uint32_t>(kk * 8 + (kk >= 2 ? 16 : 0)); }
+
+__global__ void __launch_bounds__(384, 1)
     attn_bwd_dkv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                         const __grid_constant__ CUtensorMap tmLse, const __grid_constant__ CUtensorMap tmDelta,
@@ -387,7 +403,7 @@ __global__ void __launch_bounds__(256, 1)
   uint64_t* st_full = bars + 1;                      // STAGES
   uint64_t* st_empty = st_full + DkvSmem::STAGES;    // STAGES
   uint64_t* sdp_full = st_empty + DkvSmem::STAGES;   // 2
-  uint64_t* p_full = sdp_full + 2;                   // 2 (128 arrivals)
+  uint64_t* p_full = sdp_full + 2;                   // 2 (256 arrivals)
   uint64_t* acc_done = p_full + 2;                   // 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -413,7 +429,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&sdp_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      mbar_init(&p_full[i], 256);
     }
     mbar_init(acc_done, 1);
     *abort_flag = misaligned ? 1 : 0;
@@ -427,11 +443,12 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  // TMEM columns: S^T[b] at 64*b, dP^T[b] at 128 + 64*b, dV at 256, dK at 384.
   const uint32_t tDV = tmem + 256, tDK = tmem + 384;
 
   if (warp == 0) {
     if (lane == 0 && !*abort_flag) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmdO);
       mbar_arrive_expect_tx(kv_full, 65536);
       for (int c = 0; c < 2; ++c) {
         tma_load_3d(smem + DkvSmem::K + c * 16384, &tmK, kv_full, c * 64, k0, b * p.Hk + hk);
@@ -455,16 +472,21 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     const uint32_t idS = idesc_bf16_f32(128, kQT, false, false);
     const uint32_t idA = idesc_bf16_f32(128, 128, false, true);
-    const uint32_t sK = smem_u32(smem + DkvSmem::K);
-    const uint32_t sV = smem_u32(smem + DkvSmem::V);
-    auto stage_addr = [&](int i) { return smem_u32(smem + DkvSmem::STAGE + (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES); };
+    // Descriptors of k-step 0; k-step kk adds (byte offset >> 4) to the start-address field.
+    const uint64_t dK0 = kdesc(smem_u32(smem + DkvSmem::K), 0, 16384);
+    const uint64_t dV0 = kdesc(smem_u32(smem + DkvSmem::V), 0, 16384);
+    auto stage_base = [&](int i) {
+      return smem_u32(smem + DkvSmem::STAGE + (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES);
+    };
+    auto kstep = [](int kk, uint32_t chunk) -> uint64_t { return ((kk >> 2) * chunk + (kk & 3) * 32) >> 4; };
     auto issue_sdp = [&](int i) {
-      const uint32_t sQ = stage_addr(i), sdO = sQ + 16384;
+      const uint32_t sQ = stage_base(i);
+      const uint64_t q0 = kdesc(sQ, 0, 8192), o0 = kdesc(sQ + 16384, 0, 8192);
       const uint32_t bufS = tmem + 64 * (i & 1), bufP = tmem + 128 + 64 * (i & 1);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(bufS, kdesc(sK, kk, 16384), kdesc(sQ, kk, 8192), idS, kk > 0);
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(bufS, dK0 + kstep(kk, 16384), q0 + kstep(kk, 8192), idS, kk > 0);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(bufP, kdesc(sV, kk, 16384), kdesc(sdO, kk, 8192), idS, kk > 0);
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(bufP, dV0 + kstep(kk, 16384), o0 + kstep(kk, 8192), idS, kk > 0);
       mma_commit(&sdp_full[i & 1]);
     };
     bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
@@ -480,14 +502,17 @@ __global__ void __launch_bounds__(256, 1)
       if (!mbar_wait(&p_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t sQ = stage_addr(i), sdO = sQ + 16384;
+        const uint32_t sQ = stage_base(i);
+        const uint64_t q0 = mndesc(sQ, 0, 8192), o0 = mndesc(sQ + 16384, 0, 8192);
         const uint32_t bufS = tmem + 64 * buf, bufP = tmem + 128 + 64 * buf;
 #pragma unroll
         for (int kk = 0; kk < kQT / 16; ++kk)
-          mma_bf16_ts(tDV, bufS + kk * 8, mndesc(sdO, kk, 8192), idA, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tDV, bufS + half_packed_col(kk), o0 + static_cast<uint64_t>(kk * 128), idA,
+                      (i > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
         for (int kk = 0; kk < kQT / 16; ++kk)
-          mma_bf16_ts(tDK, bufP + kk * 8, mndesc(sQ, kk, 8192), idA, (i > 0 || kk > 0) ? 1u : 0u);
+          mma_bf16_ts(tDK, bufP + half_packed_col(kk), q0 + static_cast<uint64_t>(kk * 128), idA,
+                      (i > 0 || kk > 0) ? 1u : 0u);
         mma_commit(&st_empty[i % DkvSmem::STAGES]);
         if (i == iters - 1) mma_commit(acc_done);
       }
@@ -503,6 +528,7 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp >= 4) {
     const int quad = warp & 3;
+    const int half = (warp - 4) >> 2;  // which 32 queries of the 64-query tile
     const int row = quad * 32 + lane;  // key row
     const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
     const float sl = p.scale_log2;
@@ -513,10 +539,8 @@ __global__ void __launch_bounds__(256, 1)
     bool ok = true;
     for (int i = 0; i < iters; ++i) {
       const int buf = i & 1;
-      const int qb = (i % nq) * kQT;
-      const float* lse = reinterpret_cast<const float*>(smem + DkvSmem::STAGE +
-                                                        (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES + 32768);
-      const float* dlt = lse + 64;
+      const float* stats = reinterpret_cast<const float*>(smem + DkvSmem::STAGE +
+                                                          (i % DkvSmem::STAGES) * DkvSmem::STAGE_BYTES + 32768);
       // lse / delta of this stage were written by TMA: observe its barrier too
       if (!mbar_wait(&st_full[i % DkvSmem::STAGES], (i / DkvSmem::STAGES) & 1, abort_flag, p.err,
                      kErrTimeoutSoftmax) ||
@@ -525,46 +549,51 @@ __global__ void __launch_bounds__(256, 1)
         break;
       }
       tc_fence_after();
-      const uint32_t tS = tmem + lane_base + 64 * buf, tP = tmem + lane_base + 128 + 64 * buf;
+      const uint32_t tS = tmem + lane_base + 64 * buf + 32 * half;
+      const uint32_t tP = tmem + lane_base + 128 + 64 * buf + 32 * half;
+      uint32_t sv[32], dv[32];
+      tmem_ld32(tS, sv);
+      tmem_ld32(tP, dv);
+      const float4* l4 = reinterpret_cast<const float4*>(stats + 32 * half);
+      const float4* d4 = reinterpret_cast<const float4*>(stats + 64 + 32 * half);
+      tmem_wait_ld();
+      uint32_t pp[16], dd[16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tS + 32 * c, sv);
-        tmem_ld32(tP + 32 * c, dv);
-        tmem_wait_ld();
-        uint32_t pp[16], dd[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          const int qa = 32 * c + 2 * e;
-          const float l0 = lse[qa], l1 = lse[qa + 1];
-          float p0 = 0.f, p1 = 0.f;
-          if (key_ok) {
-            if (qb + qa < p.Lq && l0 != -INFINITY) p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -l0));
-            if (qb + qa + 1 < p.Lq && l1 != -INFINITY) p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -l1));
-          }
-          pp[e] = pack_bf16(p0, p1);
-          dd[e] = pack_bf16(p0 * (__uint_as_float(dv[2 * e]) - dlt[qa]), p1 * (__uint_as_float(dv[2 * e + 1]) - dlt[qa + 1]));
-        }
-        tmem_st16(tS + 16 * c, pp);
-        tmem_st16(tP + 16 * c, dd);
+      for (int e = 0; e < 8; ++e) {
+        const float4 l = l4[e], dl = d4[e];
+        const float p0 = fast_exp2(fmaf(__uint_as_float(sv[4 * e + 0]), sl, -l.x));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(sv[4 * e + 1]), sl, -l.y));
+        const float p2 = fast_exp2(fmaf(__uint_as_float(sv[4 * e + 2]), sl, -l.z));
+        const float p3 = fast_exp2(fmaf(__uint_as_float(sv[4 * e + 3]), sl, -l.w));
+        pp[2 * e] = pack_bf16(p0, p1);
+        pp[2 * e + 1] = pack_bf16(p2, p3);
+        dd[2 * e] = pack_bf16(p0 * (__uint_as_float(dv[4 * e + 0]) - dl.x), p1 * (__uint_as_float(dv[4 * e + 1]) - dl.y));
+        dd[2 * e + 1] =
+            pack_bf16(p2 * (__uint_as_float(dv[4 * e + 2]) - dl.z), p3 * (__uint_as_float(dv[4 * e + 3]) - dl.w));
       }
+      tmem_st16(tS, pp);
+      tmem_st16(tP, dd);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&p_full[buf]);
     }
     if (ok && mbar_wait(acc_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
       tc_fence_after();
-      __nv_bfloat16* dk = p.dk + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
-      __nv_bfloat16* dv = p.dv + ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+      const long off = ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+      // each half stores 64 of the 128 columns of its key row
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t a[32], v[32];
         tmem_ld32(tDK + lane_base + 32 * c, a);
         tmem_ld32(tDV + lane_base + 32 * c, v);
         tmem_wait_ld();
         if (key < p.Lk) {
-          store_row_bf16(dk + 32 * c, a, p.scale);
-          store_row_bf16(dv + 32 * c, v, 1.0f);
+          if (!key_ok) {  // a masked key's rows hold unnormalised garbage: write zeros, not 0 * garbage
+#pragma unroll
+            for (int e = 0; e < 32; ++e) a[e] = v[e] = 0u;
+          }
+          store_row_bf16(p.dk + off + 32 * c, a, p.scale);
+          store_row_bf16(p.dv + off + 32 * c, v, 1.f);
         }
       }
     }
@@ -581,6 +610,9 @@ __global__ void __launch_bounds__(256, 1)
 // ------------------------------------------------------------------ dQ
 // CTA = (batch, head, 256 queries as two 128-row tiles); loops over 64-key blocks.
 // TMEM per tile g: S (64 cols) at 128g, dP (64) at 128g + 64, dQ (128) at 256 + 128g.
+// Masked keys (HAS_MASK) and keys past Lk in the last block get P = 0: a key row
+// of TMA zero fill scores 0, and exp2(0 - lse) can overflow when every valid
+// score of the row is very negative.
 struct DqSmem {
   static constexpr int Q = 0;          // 2 x 32 KB
   static constexpr int DO = 65536;     // 2 x 32 KB
@@ -592,6 +624,7 @@ struct DqSmem {
 };
 constexpr int kKT = 64;  // key block of the dQ kernel
 
+template <bool HAS_MASK>
 __global__ void __launch_bounds__(384, 1)
     attn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -644,6 +677,8 @@ __global__ void __launch_bounds__(384, 1)
 
   if (warp == 0) {
     if (lane == 0 && !*abort_flag) {
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
       mbar_arrive_expect_tx(q_full, 131072);
       for (int g = 0; g < 2; ++g)
         for (int c = 0; c < 2; ++c) {
@@ -664,24 +699,27 @@ __global__ void __launch_bounds__(384, 1)
   } else if (warp == 1) {
     const uint32_t idS = idesc_bf16_f32(128, kKT, false, false);
     const uint32_t idQ = idesc_bf16_f32(128, 128, false, true);
-    const uint32_t sQ = smem_u32(smem + DqSmem::Q), sdO = smem_u32(smem + DqSmem::DO);
+    const uint64_t dQ0[2] = {kdesc(smem_u32(smem + DqSmem::Q), 0, 16384),
+                             kdesc(smem_u32(smem + DqSmem::Q + 32768), 0, 16384)};
+    const uint64_t dO0[2] = {kdesc(smem_u32(smem + DqSmem::DO), 0, 16384),
+                             kdesc(smem_u32(smem + DqSmem::DO + 32768), 0, 16384)};
     auto kv_addr = [&](int j) { return smem_u32(smem + DqSmem::KV + (j % DqSmem::STAGES) * DqSmem::STAGE_BYTES); };
+    auto kstep = [](int kk, uint32_t chunk) -> uint64_t { return ((kk >> 2) * chunk + (kk & 3) * 32) >> 4; };
     auto issue_sdp = [&](int g, int j) {
-      const uint32_t sK = kv_addr(j), sV = sK + 16384;
+      const uint32_t sK = kv_addr(j);
+      const uint64_t k0d = kdesc(sK, 0, 8192), v0d = kdesc(sK + 16384, 0, 8192);
       const uint32_t tS = tmem + 128 * g, tP = tS + 64;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_bf16_ss(tS, kdesc(sQ + g * 32768, kk, 16384), kdesc(sK, kk, 8192), idS, kk > 0);
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tS, dQ0[g] + kstep(kk, 16384), k0d + kstep(kk, 8192), idS, kk > 0);
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk)
-        mma_bf16_ss(tP, kdesc(sdO + g * 32768, kk, 16384), kdesc(sV, kk, 8192), idS, kk > 0);
+      for (int kk = 0; kk < 8; ++kk) mma_bf16_ss(tP, dO0[g] + kstep(kk, 16384), v0d + kstep(kk, 8192), idS, kk > 0);
       mma_commit(&sdp_full[g]);
     };
     auto issue_dq = [&](int g, int j) {
-      const uint32_t sK = kv_addr(j);
+      const uint64_t km = mndesc(kv_addr(j), 0, 8192);
 #pragma unroll
       for (int kk = 0; kk < kKT / 16; ++kk)
-        mma_bf16_ts(tmem + 256 + 128 * g, tmem + 128 * g + kk * 8, mndesc(sK, kk, 8192), idQ,
+        mma_bf16_ts(tmem + 256 + 128 * g, tmem + 128 * g + kk * 8, km + static_cast<uint64_t>(kk * 128), idQ,
                     (j > 0 || kk > 0) ? 1u : 0u);
     };
     bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutMma) &&
@@ -727,24 +765,28 @@ __global__ void __launch_bounds__(384, 1)
     const uint32_t tS = tmem + lane_base + 128 * g, tP = tS + 64;
     const float sl = p.scale_log2;
     const bool q_ok = q < p.Lq;
-    const float lse_q = q_ok ? p.lse[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] : -INFINITY;
+    // rows past Lq or with no valid key: lse = +inf makes every P zero
+    const float lse_q = q_ok ? p.lse[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] : INFINITY;
     const float dlt_q = q_ok ? p.delta[(static_cast<long>(b) * p.H + h) * p.stat_ld + q] : 0.f;
-    const bool row_live = q_ok && lse_q != -INFINITY;
     bool ok = true;
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait(&sdp_full[g], j & 1, abort_flag, p.err, kErrTimeoutSoftmax)) { ok = false; break; }
       tc_fence_after();
-      const int kbase = j * kKT;
-      uint32_t words[2];
+      uint32_t words[2] = {0xffffffffu, 0xffffffffu};
+      const int key0 = j * kKT;
+      const bool tail = key0 + kKT > p.Lk;
+      if (HAS_MASK || tail) {
 #pragma unroll
-      for (int w = 0; w < 2; ++w) {
-        const int key0 = kbase + 32 * w;
-        uint32_t bits = 0xffffffffu;
-        if (p.kmask != nullptr && key0 < p.Lk) bits = p.kmask[static_cast<long>(b) * p.kmask_words + (key0 >> 5)];
-        const int left = p.Lk - key0;
-        if (left < 32) bits &= (left <= 0) ? 0u : ((1u << left) - 1u);
-        words[w] = bits;
+        for (int w = 0; w < 2; ++w) {
+          const int k32 = key0 + 32 * w;
+          uint32_t bits = 0xffffffffu;
+          if (HAS_MASK && k32 < p.Lk) bits = p.kmask[static_cast<long>(b) * p.kmask_words + (k32 >> 5)];
+          const int left = p.Lk - k32;
+          if (left < 32) bits &= (left <= 0) ? 0u : ((1u << left) - 1u);
+          words[w] = bits;
+        }
       }
+      const bool masked = HAS_MASK || tail;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t sv[32], dv[32];
@@ -754,13 +796,12 @@ __global__ void __launch_bounds__(384, 1)
         uint32_t dd[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
-          const int ka = 32 * c + 2 * e;
-          float p0 = 0.f, p1 = 0.f;
-          if (row_live) {
-            if ((words[c] >> (2 * e)) & 1u) p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -lse_q));
-            if ((words[c] >> (2 * e + 1)) & 1u) p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -lse_q));
+          float p0 = fast_exp2(fmaf(__uint_as_float(sv[2 * e]), sl, -lse_q));
+          float p1 = fast_exp2(fmaf(__uint_as_float(sv[2 * e + 1]), sl, -lse_q));
+          if (masked) {
+            p0 = ((words[c] >> (2 * e)) & 1u) ? p0 : 0.f;
+            p1 = ((words[c] >> (2 * e + 1)) & 1u) ? p1 : 0.f;
           }
-          (void)ka;
           dd[e] = pack_bf16(p0 * (__uint_as_float(dv[2 * e]) - dlt_q), p1 * (__uint_as_float(dv[2 * e + 1]) - dlt_q));
         }
         tmem_st16(tS + 16 * c, dd);
@@ -787,6 +828,364 @@ __global__ void __launch_bounds__(384, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------ fused backward
+// One pass over (query tile, key tile) pairs with five GEMM-shaped products per
+// pair (the minimum): S^T = K Q^T, dP^T = V dO^T, dV += P^T dO, dK += dS^T Q and
+// dQ^T = K^T dS^T. CTA = (batch, kv head, 128 keys); it walks the 64-query tiles
+// of every query head of its group.
+//
+//  * S^T, dP^T: TMEM, double-buffered. Eight softmax warps (two per TMEM lane
+//    quadrant, one per 32-query half) form P^T and dS^T in place in TMEM (bf16
+//    pairs) and also write dS^T to shared memory as a 128 x 64 SW128 tile.
+//  * dV and dK read P^T / dS^T from TMEM (the TS form: no shared-memory traffic
+//    for A); the shared dS^T tile is the MN-major B operand of dQ^T, whose A
+//    operand is the K tile read MN-major.
+//  * dQ^T of a pair (128 d x 64 q, fp32) lands in the dP^T buffer after dK has
+//    read it. Four epilogue warps drain it through shared memory and add it into
+//    a global fp32 dQ^T accumulator [B*H, 128, ld] with TMA bulk reduce-add, two
+//    32 x 32 swizzled boxes per warp (measured faster than per-thread
+//    red.global.add, whose load/store-pipe traffic slows the MMA operand reads).
+//    A final kernel scales and transposes it to bf16 dQ.
+//
+// No bounds tests sit in the elementwise loop: query rows past Lq arrive as TMA
+// zero fill (they add nothing and are dropped by the reduce), rows whose every
+// key is masked carry lse = +inf (P = 0), and masked keys or keys past Lk get
+// P = dS = 0 through a per-thread select (their dS^T would otherwise reach dQ).
+//
+// TMEM columns: dV [0,128), dK [128,256), S^T[b] at 256 + 64b, dP^T / dQ^T[b] at 384 + 64b.
+struct FusedBwdSmem {
+  static constexpr int K = 0;            // 2 chunks x 16 KB (128 keys x 64 d, SW128)
+  static constexpr int V = 32768;
+  static constexpr int STAGES = 3;
+  static constexpr int STAGE = 65536;    // per stage: Q 16 KB, dO 16 KB
+  static constexpr int STAGE_BYTES = 32768;
+  static constexpr int DST = STAGE + STAGES * STAGE_BYTES;   // 2 x 16 KB dS^T (128 keys x 64 q)
+  static constexpr int STG = DST + 2 * 16384;                 // 4 x 8 KB fp32 dQ^T slabs
+  static constexpr int STATS = STG + 4 * 8192;                // STAGES x (lse 256 B, delta 256 B)
+  static constexpr int BARS = STATS + STAGES * 512;
+  static constexpr int BYTES = BARS + 256;
+};
+static_assert(FusedBwdSmem::BYTES <= 232448, "fused attention backward exceeds shared memory");
+
+__global__ void __launch_bounds__(512, 1)
+    attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                          const __grid_constant__ CUtensorMap tmLse, const __grid_constant__ CUtensorMap tmDelta,
+                          const __grid_constant__ CUtensorMap tmAcc, const AttnBwdDesc p) {
+  using S = FusedBwdSmem;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S::BARS);
+  uint64_t* kv_full = bars;                      // 1
+  uint64_t* st_full = bars + 1;                  // STAGES
+  uint64_t* st_empty = st_full + S::STAGES;      // STAGES
+  uint64_t* sdp_full = st_empty + S::STAGES;     // 2
+  uint64_t* p_full = sdp_full + 2;               // 2 (256 arrivals)
+  uint64_t* dq_full = p_full + 2;                // 2
+  uint64_t* dq_empty = dq_full + 2;              // 2 (128 arrivals)
+  uint64_t* acc_done = dq_empty + 2;             // 1
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  const int kt = blockIdx.x % p.k_tiles;
+  const int bhk = blockIdx.x / p.k_tiles;
+  const int hk = bhk % p.Hk;
+  const int b = bhk / p.Hk;
+  const int k0 = kt * kTile;
+  const int group = p.H / p.Hk;
+  const int nq = (p.Lq + kQT - 1) / kQT;
+  const int iters = nq * group;
+  // diagnostics: SM clock stamps of CTA 0, 24 per iteration, first 64 iterations
+  long long* trace = (p.trace != nullptr && blockIdx.x == 0) ? p.trace : nullptr;
+  auto stamp = [&](int i, int slot) {
+    if (trace != nullptr && i < 64) trace[i * 24 + slot] = clock64();
+  };
+
+  if (threadIdx.x == 0) {
+    const bool misaligned = (smem_u32(smem) & 1023u) != 0;
+    if (misaligned) record_error(p.err, kErrBadArgument);
+    mbar_init(kv_full, 1);
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(&st_full[s], 1);
+      mbar_init(&st_empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&sdp_full[i], 1);
+      mbar_init(&p_full[i], 256);
+      mbar_init(&dq_full[i], 1);
+      mbar_init(&dq_empty[i], 128);
+    }
+    mbar_init(acc_done, 1);
+    *abort_flag = misaligned ? 1 : 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tDV = tmem, tDK = tmem + 128;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0 && !*abort_flag) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmdO);
+      mbar_arrive_expect_tx(kv_full, 65536);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_3d(smem + S::K + c * 16384, &tmK, kv_full, c * 64, k0, b * p.Hk + hk);
+        tma_load_3d(smem + S::V + c * 16384, &tmV, kv_full, c * 64, k0, b * p.Hk + hk);
+      }
+      for (int i = 0; i < iters; ++i) {
+        const int s = i % S::STAGES;
+        const int h = hk * group + i / nq;
+        const int qb = (i % nq) * kQT;
+        if (!mbar_wait(&st_empty[s], ((i / S::STAGES) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        uint8_t* st = smem + S::STAGE + s * S::STAGE_BYTES;
+        mbar_arrive_expect_tx(&st_full[s], S::STAGE_BYTES + 512);
+        for (int c = 0; c < 2; ++c) {
+          tma_load_3d(st + c * 8192, &tmQ, &st_full[s], c * 64, qb, b * p.H + h);
+          tma_load_4d(st + 16384 + c * 8192, &tmdO, &st_full[s], c * 64, h, qb, b);
+        }
+        tma_load_2d(smem + S::STATS + s * 512, &tmLse, &st_full[s], qb, b * p.H + h);
+        tma_load_2d(smem + S::STATS + s * 512 + 256, &tmDelta, &st_full[s], qb, b * p.H + h);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    const uint32_t idS = idesc_bf16_f32(128, kQT, false, false);  // S^T, dP^T: 128 keys x 64 q
+    const uint32_t idA = idesc_bf16_f32(128, 128, false, true);   // dV, dK: 128 keys x 128 d
+    const uint32_t idQ = idesc_bf16_f32(128, kQT, true, true);    // dQ^T: 128 d x 64 q
+    const uint64_t dK0 = kdesc(smem_u32(smem + S::K), 0, 16384);
+    const uint64_t dV0 = kdesc(smem_u32(smem + S::V), 0, 16384);
+    const uint64_t dKt = mndesc(smem_u32(smem + S::K), 0, 16384);  // K as the MN-major A of dQ^T
+    auto stage_base = [&](int i) { return smem_u32(smem + S::STAGE + (i % S::STAGES) * S::STAGE_BYTES); };
+    auto kstep = [](int kk, uint32_t chunk) -> uint64_t { return ((kk >> 2) * chunk + (kk & 3) * 32) >> 4; };
+    auto issue_s = [&](int i) {
+      const uint64_t q0 = kdesc(stage_base(i), 0, 8192);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_bf16_ss(tmem + 256 + 64 * (i & 1), dK0 + kstep(kk, 16384), q0 + kstep(kk, 8192), idS, kk > 0);
+    };
+    auto issue_dp = [&](int i) {
+      const uint64_t o0 = kdesc(stage_base(i) + 16384, 0, 8192);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        mma_bf16_ss(tmem + 384 + 64 * (i & 1), dV0 + kstep(kk, 16384), o0 + kstep(kk, 8192), idS, kk > 0);
+    };
+    bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
+    for (int i = 0; i < 2 && i < iters && ok; ++i) {
+      ok = mbar_wait(&st_full[i % S::STAGES], (i / S::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        issue_s(i);
+        issue_dp(i);
+        mma_commit(&sdp_full[i & 1]);
+      }
+      __syncwarp();
+    }
+    for (int i = 0; i < iters && ok; ++i) {
+      const int buf = i & 1;
+      if (!mbar_wait(&p_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+      tc_fence_after();
+      if (lane == 0) {
+        stamp(i, 0);
+        const uint32_t sQ = stage_base(i);
+        const uint64_t qmn = mndesc(sQ, 0, 8192), omn = mndesc(sQ + 16384, 0, 8192);
+        const uint32_t dst = smem_u32(smem + S::DST + buf * 16384);
+        const uint64_t dsM = mndesc(dst, 0, 16384);  // dS^T as MN-major B (k = keys, n = queries)
+#pragma unroll
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_bf16_ts(tDV, tmem + 256 + 64 * buf + half_packed_col(kk), omn + static_cast<uint64_t>(kk * 128), idA,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kQT / 16; ++kk)
+          mma_bf16_ts(tDK, tmem + 384 + 64 * buf + half_packed_col(kk), qmn + static_cast<uint64_t>(kk * 128), idA,
+                      (i > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < kTile / 16; ++kk)
+          mma_bf16_ss(tmem + 384 + 64 * buf, dKt + static_cast<uint64_t>(kk * 128),
+                      dsM + static_cast<uint64_t>(kk * 128), idQ, kk > 0 ? 1u : 0u);
+        mma_commit(&dq_full[buf]);
+        mma_commit(&st_empty[i % S::STAGES]);
+        if (i == iters - 1) mma_commit(acc_done);
+      }
+      __syncwarp();
+      if (i + 2 < iters) {
+        if (!mbar_wait(&st_full[(i + 2) % S::STAGES], ((i + 2) / S::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma))
+          break;
+        tc_fence_after();
+        if (lane == 0) issue_s(i + 2);  // S^T buffer: in order after dV(i) read P^T(i)
+        __syncwarp();
+        // dP^T buffer holds dQ^T(i) until the epilogue has read it
+        if (!mbar_wait(&dq_empty[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        if (lane == 0) {
+          stamp(i, 1);
+          issue_dp(i + 2);
+          mma_commit(&sdp_full[buf]);
+        }
+        __syncwarp();
+      }
+    }
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------ softmax: P^T, dS^T
+    const int quad = warp & 3;
+    const int half = (warp - 4) >> 2;
+    const int row = quad * 32 + lane;  // key row
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    const float sl = p.scale_log2;
+    const int key = k0 + row;
+    bool key_ok = key < p.Lk;
+    if (key_ok && p.kmask != nullptr)
+      key_ok = (p.kmask[static_cast<long>(b) * p.kmask_words + (key >> 5)] >> (key & 31)) & 1u;
+    bool ok = true;
+    for (int i = 0; i < iters; ++i) {
+      const int buf = i & 1;
+      const float* stats = reinterpret_cast<const float*>(smem + S::STATS + (i % S::STAGES) * 512);
+      if (!mbar_wait(&st_full[i % S::STAGES], (i / S::STAGES) & 1, abort_flag, p.err, kErrTimeoutSoftmax) ||
+          !mbar_wait(&sdp_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      if (warp == 4 && lane == 0) stamp(i, 2);
+      const uint32_t tS = tmem + lane_base + 256 + 64 * buf + 32 * half;
+      const uint32_t tP = tmem + lane_base + 384 + 64 * buf + 32 * half;
+      uint32_t sv[32], dv[32];
+      tmem_ld32(tS, sv);
+      tmem_ld32(tP, dv);
+      const float4* l4 = reinterpret_cast<const float4*>(stats + 32 * half);
+      const float4* d4 = reinterpret_cast<const float4*>(stats + 64 + 32 * half);
+      tmem_wait_ld();
+      uint32_t pp[16], dd[16];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float4 l = l4[e], dl = d4[e];
+        // select, not multiply: a masked key's score may overflow exp2 and 0 * inf is NaN
+        const float p0 = key_ok ? fast_exp2(fmaf(__uint_as_float(sv[4 * e + 0]), sl, -l.x)) : 0.f;
+        const float p1 = key_ok ? fast_exp2(fmaf(__uint_as_float(sv[4 * e + 1]), sl, -l.y)) : 0.f;
+        const float p2 = key_ok ? fast_exp2(fmaf(__uint_as_float(sv[4 * e + 2]), sl, -l.z)) : 0.f;
+        const float p3 = key_ok ? fast_exp2(fmaf(__uint_as_float(sv[4 * e + 3]), sl, -l.w)) : 0.f;
+        pp[2 * e] = pack_bf16(p0, p1);
+        pp[2 * e + 1] = pack_bf16(p2, p3);
+        dd[2 * e] = pack_bf16(p0 * (__uint_as_float(dv[4 * e + 0]) - dl.x), p1 * (__uint_as_float(dv[4 * e + 1]) - dl.y));
+        dd[2 * e + 1] =
+            pack_bf16(p2 * (__uint_as_float(dv[4 * e + 2]) - dl.z), p3 * (__uint_as_float(dv[4 * e + 3]) - dl.w));
+      }
+      tmem_st16(tS, pp);
+      tmem_st16(tP, dd);
+      // dS^T row `row`, queries [32 half, 32 half + 32): 16-byte chunks 4 half .. 4 half + 3 of
+      // the 128-byte row, XOR-swizzled by row & 7 (SW128).
+      uint8_t* drow = smem + S::DST + buf * 16384 + row * 128;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int chunk = (4 * half + j) ^ (row & 7);
+        *reinterpret_cast<uint4*>(drow + chunk * 16) = make_uint4(dd[4 * j], dd[4 * j + 1], dd[4 * j + 2], dd[4 * j + 3]);
+      }
+      tmem_wait_st();
+      fence_proxy_async();
+      tc_fence_before();
+      if (warp == 4 && lane == 0) stamp(i, 3);
+      if (lane == 0) stamp(i, 8 + (warp - 4));
+      mbar_arrive(&p_full[buf]);
+    }
+    if (ok && mbar_wait(acc_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
+      tc_fence_after();
+      const long off = ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+#pragma unroll 1
+      for (int c = 2 * half; c < 2 * half + 2; ++c) {
+        uint32_t a[32], v[32];
+        tmem_ld32(tDK + lane_base + 32 * c, a);
+        tmem_ld32(tDV + lane_base + 32 * c, v);
+        tmem_wait_ld();
+        if (key < p.Lk) {
+          store_row_bf16(p.dk + off + 32 * c, a, p.scale);
+          store_row_bf16(p.dv + off + 32 * c, v, 1.f);
+        }
+      }
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------ dQ^T drain + TMA reduce-add
+    const int quad = warp & 3;  // d rows [32 quad, 32 quad + 32)
+    const uint32_t lane_base = static_cast<uint32_t>(quad * 32) << 16;
+    // two SW128 sub-tiles of 32 d x 32 q (4 KB each) per warp: queries [0,32) and [32,64)
+    uint8_t* slab = smem + S::STG + quad * 8192;
+    for (int i = 0; i < iters; ++i) {
+      const int buf = i & 1;
+      const int h = hk * group + i / nq;
+      const int qb = (i % nq) * kQT;
+      if (!mbar_wait(&dq_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      if (warp == 12 && lane == 0) stamp(i, 4);
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tmem + lane_base + 384 + 64 * buf, v0);
+      tmem_ld32(tmem + lane_base + 384 + 64 * buf + 32, v1);
+      tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(&dq_empty[buf]);
+      if (lane == 0) stamp(i, 16 + (warp - 12));
+      if (lane == 0 && i > 0) bulk_wait_group_read0();  // the previous reduce has read the slab
+      __syncwarp();
+      // row `lane` of each sub-tile: 16-byte chunk j at j ^ (lane & 7) (SW128), so the
+      // eight lanes of a store phase hit eight different bank groups
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = (j ^ (lane & 7)) * 16 + lane * 128;
+        *reinterpret_cast<uint4*>(slab + c) = make_uint4(v0[4 * j], v0[4 * j + 1], v0[4 * j + 2], v0[4 * j + 3]);
+        *reinterpret_cast<uint4*>(slab + 4096 + c) =
+            make_uint4(v1[4 * j], v1[4 * j + 1], v1[4 * j + 2], v1[4 * j + 3]);
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_3d(&tmAcc, slab, qb, 32 * quad, b * p.H + h);
+        tma_reduce_add_3d(&tmAcc, slab + 4096, qb + 32, 32 * quad, b * p.H + h);
+        bulk_commit_group();
+      }
+    }
+    if (lane == 0) bulk_wait_group0();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// dq[b, h, q, :] = scale * acc[b*H + h, :, q] (fp32 [B*H, 128, ld] -> bf16 [B, H, Lq, 128]).
+// CTA = 64 queries of one (b, h): coalesced row reads, a shared-memory transpose, 256-byte row writes.
+__global__ void __launch_bounds__(256) attn_dq_convert_kernel(const float* __restrict__ acc, long ld, int Lq,
+                                                              float scale, __nv_bfloat16* __restrict__ dq) {
+  __shared__ float tile[128][65];
+  const long bh = blockIdx.y;
+  const int q0 = blockIdx.x * 64;
+  const float* src = acc + bh * 128 * ld;
+  for (int idx = threadIdx.x; idx < 128 * 64; idx += 256) {
+    const int d = idx >> 6, q = idx & 63;
+    tile[d][q] = (q0 + q < Lq) ? src[d * ld + q0 + q] : 0.f;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 64 * 16; idx += 256) {
+    const int q = idx >> 4, d0 = (idx & 15) * 8;
+    if (q0 + q >= Lq) continue;
+    uint4 w;
+    w.x = pack_bf16(tile[d0 + 0][q] * scale, tile[d0 + 1][q] * scale);
+    w.y = pack_bf16(tile[d0 + 2][q] * scale, tile[d0 + 3][q] * scale);
+    w.z = pack_bf16(tile[d0 + 4][q] * scale, tile[d0 + 5][q] * scale);
+    w.w = pack_bf16(tile[d0 + 6][q] * scale, tile[d0 + 7][q] * scale);
+    *reinterpret_cast<uint4*>(dq + (bh * Lq + q0 + q) * kHD + d0) = w;
   }
 }
 
@@ -864,6 +1263,43 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
     AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: row-stat tensor map failed (", static_cast<int>(r), ")");
     return m;
   };
+  if (d.dq_acc != nullptr) {
+    // ---- fused: dK, dV and dQ^T partials in one pass, then dQ = scale * acc^T
+    const long ld = (d.Lq + 3) / 4 * 4;  // 16-byte rows for the TMA reduce
+    AVGEN_CUDA_CHECK(cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * ld * kHD * d.B * d.H, stream));
+    d.k_tiles = (d.Lk + kTile - 1) / kTile;
+    const CUtensorMap tq = head_major(d.q, d.H, d.Lq, kQT);
+    const CUtensorMap tk = head_major(d.k, d.Hk, d.Lk, kTile);
+    const CUtensorMap tv = head_major(d.v, d.Hk, d.Lk, kTile);
+    const CUtensorMap tdo = dout_map(kQT);
+    const CUtensorMap tl = f32_rows(d.lse, kQT);
+    const CUtensorMap tdl = f32_rows(d.delta, kQT);
+    CUtensorMap tacc;
+    {
+      cuuint64_t dims[3] = {static_cast<cuuint64_t>(d.Lq), static_cast<cuuint64_t>(kHD),
+                            static_cast<cuuint64_t>(d.B) * d.H};
+      cuuint64_t strides[2] = {static_cast<cuuint64_t>(ld) * 4, static_cast<cuuint64_t>(ld) * kHD * 4};
+      cuuint32_t box[3] = {32, 32, 1};  // 32 q (128 B, the SW128 span) x 32 d
+      cuuint32_t estr[3] = {1, 1, 1};
+      CUresult r = tensor_map_encoder()(&tacc, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, d.dq_acc, dims, strides, box, estr,
+                                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: dQ accumulator tensor map failed (", static_cast<int>(r), ")");
+    }
+    static bool attr = false;
+    if (!attr) {
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            FusedBwdSmem::BYTES));
+      attr = true;
+    }
+    const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
+    attn_bwd_fused_kernel<<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
+    dim3 cgrid((d.Lq + 63) / 64, d.B * d.H);
+    attn_dq_convert_kernel<<<cgrid, 256, 0, stream>>>(d.dq_acc, ld, d.Lq, d.scale, d.dq);
+    AVGEN_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   // ---- dK / dV
   {
     d.k_tiles = (d.Lk + kTile - 1) / kTile;
@@ -880,7 +1316,7 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
       attr = true;
     }
     const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
-    attn_bwd_dkv_kernel<<<grid, 256, DkvSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, d);
+    attn_bwd_dkv_kernel<<<grid, 384, DkvSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, d);
     AVGEN_CUDA_CHECK(cudaGetLastError());
   }
   // ---- dQ
@@ -892,12 +1328,18 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
     const CUtensorMap tdo = dout_map(128);
     static bool attr = false;
     if (!attr) {
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            DqSmem::BYTES));
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             DqSmem::BYTES));
       attr = true;
     }
     const long grid = static_cast<long>(d.B) * d.H * d.q_tiles;
-    attn_bwd_dq_kernel<<<grid, 384, DqSmem::BYTES, stream>>>(tq, tk, tv, tdo, d);
+    if (d.kmask != nullptr) {
+      attn_bwd_dq_kernel<true><<<grid, 384, DqSmem::BYTES, stream>>>(tq, tk, tv, tdo, d);
+    } else {
+      attn_bwd_dq_kernel<false><<<grid, 384, DqSmem::BYTES, stream>>>(tq, tk, tv, tdo, d);
+    }
     AVGEN_CUDA_CHECK(cudaGetLastError());
   }
 }

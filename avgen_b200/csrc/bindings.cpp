@@ -532,7 +532,7 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
               const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
-              at::Tensor& dv, const OptT& kmask, double scale) {
+              at::Tensor& dv, const OptT& kmask, double scale, const OptT& dq_acc, const OptT& trace) {
   c10::cuda::CUDAGuard guard(q.device());
   for (const at::Tensor* t : {&q, &k, &v, &o, &dout, static_cast<const at::Tensor*>(&dk), static_cast<const at::Tensor*>(&dv)}) check_bf16(*t, "attention bwd tensor");
   check_f32(lse, "lse");
@@ -569,6 +569,17 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   d.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
   d.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   d.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  if (has(dq_acc)) {
+    check_f32(*dq_acc, "dq_acc");
+    TORCH_CHECK(dq_acc->numel() >= static_cast<long>(d.B) * d.H * ((d.Lq + 3) / 4 * 4) * d.D && dq_acc->is_contiguous(),
+                "attention bwd: dq_acc must be contiguous fp32 with B*H*128*ceil4(Lq) elements");
+    d.dq_acc = dq_acc->data_ptr<float>();
+  }
+  if (has(trace)) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda() && trace->numel() >= 64 * 24,
+                "attention bwd: trace must be an int64 device tensor of at least 1536 entries");
+    d.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   if (has(kmask)) {
     TORCH_CHECK(kmask->scalar_type() == at::kInt && kmask->is_cuda() && kmask->dim() == 2 && kmask->size(0) == d.B,
                 "attention bwd: kmask must be packed int32 [B, words]");
@@ -632,7 +643,8 @@ PYBIND11_MODULE(_C, m) {
   m.def("attn_fwd", &a::attn_fwd, arg("q"), arg("k"), arg("v"), arg("out"), arg("lse") = none, arg("kmask") = none,
         arg("scale") = 0.0);
   m.def("attn_bwd", &a::attn_bwd, arg("q"), arg("k"), arg("v"), arg("o"), arg("dout"), arg("lse"), arg("delta"),
-        arg("dq"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0);
+        arg("dq"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0, arg("dq_acc") = none,
+        arg("trace") = none);
   m.def("read_error", &a::read_error);
   m.def("clear_error", &a::clear_error);
 }

@@ -230,6 +230,8 @@ struct AttnBwdDesc {
   int q_tiles = 0;
   __nv_bfloat16* dk = nullptr; // [B, Hk, Lk, D]
   __nv_bfloat16* dv = nullptr;
+  float* dq_acc = nullptr;     // optional fp32 scratch of B*H*128*ld floats, ld = Lq rounded up to 4: selects the fused one-pass kernel
+  long long* trace = nullptr;  // optional int64 [64 * 24]: per-warp SM clock stamps of CTA 0 (diagnostics)
   int* err = nullptr;
 };
 void attn_bwd_launch(const AttnBwdDesc& d, cudaStream_t stream);

@@ -28,6 +28,7 @@ LAUNCHES = [0]
 # AVGEN_KERNEL_DEBUG=1: synchronise after every wrapper call, report its device time
 # and stop at the first call that leaves a timed-out wait in the device error word.
 _DEBUG = os.environ.get("AVGEN_KERNEL_DEBUG") == "1"
+_ATTN_BWD = os.environ.get("AVGEN_ATTN_BWD", "fused")
 
 
 def _count(n: int = 1) -> None:
@@ -322,16 +323,29 @@ def attention_bwd(
     *,
     kmask: torch.Tensor | None = None,
     scale: float | None = None,
+    trace: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """Flash attention backward. Returns ``(dq, dk, dv)`` (bf16, shapes of q, k, v)."""
+    """Flash attention backward. Returns ``(dq, dk, dv)`` (bf16, shapes of q, k, v).
+
+    ``trace`` (int64, >= 1536 entries, diagnostics) receives per-role SM clock
+    stamps of the first CTA of the one-pass kernel.
+
+    The default is the one-pass kernel (five GEMM-shaped products per tile pair,
+    dQ summed in an fp32 scratch by TMA reduce-add); ``AVGEN_ATTN_BWD=split``
+    selects the two-kernel variant (dK/dV and dQ passes, no reduction, two extra
+    products per tile pair).
+    """
     d = q.shape[-1]
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     delta = torch.empty_strided(lse.shape, lse.stride(), device=lse.device, dtype=_F32)
     dq = torch.empty_like(q)
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
-    load().attn_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, kmask, scale)
-    _count(3)
+    acc = None
+    if _ATTN_BWD != "split":
+        acc = torch.empty(q.shape[0] * q.shape[1] * d * (-(-q.shape[2] // 4) * 4), device=q.device, dtype=_F32)
+    load().attn_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, kmask, scale, acc, trace)
+    _count(4 if acc is not None else 3)
     return dq, dk, dv
 
 

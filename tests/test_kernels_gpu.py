@@ -327,3 +327,30 @@ def test_attention_odd_lengths(lq: int, lk: int) -> None:
     _close(dk, kr.grad, rtol=3e-2, atol=3e-2)
     _close(dv, vr.grad, rtol=3e-2, atol=3e-2)
     _errors_clear()
+
+
+@pytest.mark.parametrize("mode", ["fused", "split"])
+def test_attention_bwd_variants_agree(mode: str, monkeypatch: pytest.MonkeyPatch) -> None:
+    """Both backward variants (one-pass with dQ reduce-add, and two-pass) against fp32."""
+    ops = _ops()
+    monkeypatch.setattr(ops, "_ATTN_BWD", mode)
+    torch.manual_seed(13)
+    b, h, hk, lq, lk, d = 2, 4, 2, 517, 389, 128
+    q = torch.randn(b, h, lq, d, device=DEV).bfloat16()
+    k = torch.randn(b, hk, lk, d, device=DEV).bfloat16()
+    v = torch.randn(b, hk, lk, d, device=DEV).bfloat16()
+    kmask = torch.rand(b, lk, device=DEV) > 0.25
+    kmask[1] = False  # a sample with no valid key: its rows attend to nothing
+    packed = ops.pack_key_mask(kmask)
+    out, lse = ops.attention_fwd(q, k, v, kmask=packed)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, k, v))
+    ref = _attn_ref(qr, kr, vr, kmask, 1.0 / math.sqrt(d))
+    ref = torch.where(kmask.any(-1)[:, None, None, None], ref, torch.zeros_like(ref))
+    _close(out, ref)
+    dout = torch.randn_like(ref).bfloat16()
+    ref.backward(dout.float())
+    dq, dk, dv = ops.attention_bwd(q, k, v, out, dout.contiguous(), lse, kmask=packed)
+    for got, want in ((dq, qr.grad), (dk, kr.grad), (dv, vr.grad)):
+        assert torch.isfinite(got.float()).all()
+        _close(got, torch.nan_to_num(want), rtol=3e-2, atol=3e-2)
+    _errors_clear()

@@ -213,8 +213,8 @@ __global__ void __launch_bounds__(256) rmsnorm_mod_bwd_cols_kernel(NormDesc d, i
   }
 }
 
-// Column pass when each row names its own modulation row (`groups`). A CTA's row
-// range may then cross several groups: every thread keeps running sums for the
+// Column pass when rows map to modulation rows by `groups` (or by row /
+// rows_per_batch with small batches). A CTA's row range may then cross several groups: every thread keeps running sums for the
 // group of its current row and adds them to global memory when the group changes
 // or the range ends. Groups are piecewise constant along rows (a sample's clean
 // and noisy frames), so flushes are rare. Grid = (ceil(W/64), 1, row splits).
@@ -244,7 +244,7 @@ __global__ void __launch_bounds__(256) rmsnorm_mod_bwd_cols_grouped_kernel(NormD
     acc_s[0] = acc_s[1] = acc_t[0] = acc_t[1] = 0.f;
   };
   for (long row = r0 + ty; row < r1; row += 8) {
-    const long gr = mod_row(d.groups, d.num_groups, row, 1);
+    const long gr = mod_row(d.groups, d.num_groups, row, d.rows_per_batch);
     if (gr != g) {
       flush();
       g = gr;
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(256) gate_bwd_grouped_kernel(GateBwdDesc d, in
   long g = -1;
   float g0 = 0.f, g1 = 0.f;
   for (long row = r0 + ty; row < r1; row += 8) {
-    const long gr = mod_row(d.groups, d.num_groups, row, 1);
+    const long gr = mod_row(d.groups, d.num_groups, row, d.rows_per_batch);
     if (gr != g) {
       if (g >= 0) {
         atomicAdd(d.dgate + g * d.dgate_stride + c, acc[0]);
@@ -391,7 +391,14 @@ void rmsnorm_mod_fwd_launch(const NormDesc& d, cudaStream_t stream) {
   AVGEN_CUDA_CHECK(cudaGetLastError());
 }
 
-void rmsnorm_mod_bwd_launch(const NormDesc& d, cudaStream_t stream) {
+// The per-batch column kernels put one batch per grid row (y <= 65535) and want
+// many rows per batch; otherwise the run-flushing kernels take over.
+constexpr long kMinRowsPerBatch = 256;
+
+void rmsnorm_mod_bwd_launch(const NormDesc& d_in, cudaStream_t stream) {
+  NormDesc d = d_in;
+  // without modulation only dw is reduced: one batch spanning every row
+  if (d.scale == nullptr && d.shift == nullptr && d.groups == nullptr) d.rows_per_batch = d.rows;
   AVGEN_CHECK(d.W % 8 == 0, "norm: width must be a multiple of 8");
   if (d.rows == 0) return;
   const int vpl = pick_vpl(d.W);
@@ -400,7 +407,8 @@ void rmsnorm_mod_bwd_launch(const NormDesc& d, cudaStream_t stream) {
     AVGEN_VPL_SWITCH(vpl, rmsnorm_mod_bwd_rows_kernel<V><<<blocks, 256, 0, stream>>>(d));
     AVGEN_CUDA_CHECK(cudaGetLastError());
   }
-  if (d.groups != nullptr && (d.dw != nullptr || d.dscale != nullptr || d.dshift != nullptr)) {
+  const bool irregular = d.groups != nullptr || d.rows_per_batch < kMinRowsPerBatch;
+  if (irregular && (d.dw != nullptr || d.dscale != nullptr || d.dshift != nullptr)) {
     const int col_tiles = (d.W + 63) / 64;
     const int splits = grouped_splits(d.rows, col_tiles, num_sms(d.device));
     rmsnorm_mod_bwd_cols_grouped_kernel<<<dim3(col_tiles, 1, splits), 256, 0, stream>>>(d, splits);
@@ -419,7 +427,7 @@ void gate_bwd_launch(const GateBwdDesc& d, cudaStream_t stream) {
   AVGEN_CHECK(d.W % 2 == 0, "gate_bwd: width must be even");
   if (d.rows == 0) return;
   const int col_tiles = (d.W + 63) / 64;
-  if (d.groups != nullptr) {
+  if (d.groups != nullptr || d.rows_per_batch < kMinRowsPerBatch) {
     const int splits = grouped_splits(d.rows, col_tiles, num_sms(d.device));
     gate_bwd_grouped_kernel<<<dim3(col_tiles, 1, splits), 256, 0, stream>>>(d, splits);
     AVGEN_CUDA_CHECK(cudaGetLastError());

@@ -1,0 +1,108 @@
+"""Device-timed microbenchmarks of the sm_100a kernels.
+
+    python -m avgen_b200.ops.bench attention --L 16384 --H 20 [--bwd split]
+    python -m avgen_b200.ops.bench gemm --m 16384 --n 7680 --k 2560
+    python -m avgen_b200.ops.bench attention --L 4096 --H 37 --once   # one call each (for ncu -k/-c)
+
+Times come from CUDA events on the launching stream after warm-up, with a
+synchronize on both sides; each line also reports the library equivalent
+(cuBLAS through ``torch.matmul``, cuDNN/flash SDPA) on the same inputs.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+from collections.abc import Callable
+
+import torch
+
+
+def _time(fn: Callable[[], object], iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(iters):
+        fn()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters
+
+
+def bench_attention(length: int, heads: int, iters: int, once: bool) -> None:
+    from avgen_b200.ops import kernels as K
+
+    q = torch.randn(1, heads, length, 128, device="cuda").bfloat16()
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    out, lse = K.attention_fwd(q, k, v)
+    dout = torch.randn_like(out)
+    if once:
+        K.attention_fwd(q, k, v)
+        K.attention_bwd(q, k, v, out, dout, lse)
+        torch.cuda.synchronize()
+        return
+    flops = 4.0 * heads * length * length * 128
+    t_fwd = _time(lambda: K.attention_fwd(q, k, v), iters)
+    t_bwd = _time(lambda: K.attention_bwd(q, k, v, out, dout, lse), iters)
+    qt, kt, vt = (t.requires_grad_() for t in (q.clone(), k.clone(), v.clone()))
+    ref = torch.nn.functional.scaled_dot_product_attention
+    t_lf = _time(lambda: ref(qt, kt, vt), iters)
+    o = ref(qt, kt, vt)
+    g = torch.randn_like(o)
+    t_lb = _time(lambda: torch.autograd.grad(o, (qt, kt, vt), g, retain_graph=True), iters)
+    print(f"attention L={length} H={heads}: fwd {t_fwd:.3f} ms ({flops / t_fwd / 1e9:.0f} TF/s) | "
+          f"bwd {t_bwd:.3f} ms ({2.5 * flops / t_bwd / 1e9:.0f} TF/s counted) | "
+          f"torch SDPA fwd {t_lf:.3f} ms, bwd {t_lb:.3f} ms")
+
+
+def bench_gemm(m: int, n: int, k: int, iters: int) -> None:
+    from avgen_b200.ops import kernels as K
+
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    b = torch.randn(n, k, device="cuda").bfloat16()
+    dy = torch.randn(m, n, device="cuda").bfloat16()
+    grad = torch.zeros(n, k, device="cuda")
+    flops = 2.0 * m * n * k
+    rows = [("fwd", lambda: K.gemm(a, b), lambda: a @ b.t()),
+            ("dx", lambda: K.linear_dx(dy, b), lambda: dy @ b),
+            ("dw", lambda: K.linear_dw(dy, a, grad), lambda: dy.t() @ a)]
+    for name, ours, lib in rows:
+        t_o, t_l = _time(ours, iters), _time(lib, iters)
+        print(f"gemm {m}x{n}x{k} {name}: {t_o:.3f} ms ({flops / t_o / 1e9:.0f} TF/s) | "
+              f"cuBLAS {t_l:.3f} ms ({flops / t_l / 1e9:.0f} TF/s)")
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    sub = p.add_subparsers(dest="op", required=True)
+    a = sub.add_parser("attention")
+    a.add_argument("--L", type=int, default=16384)
+    a.add_argument("--H", type=int, default=20)
+    a.add_argument("--bwd", choices=("fused", "split"), default=None)
+    a.add_argument("--once", action="store_true")
+    g = sub.add_parser("gemm")
+    g.add_argument("--m", type=int, default=16384)
+    g.add_argument("--n", type=int, default=7680)
+    g.add_argument("--k", type=int, default=2560)
+    for s in (a, g):
+        s.add_argument("--iters", type=int, default=10)
+    args = p.parse_args()
+    if getattr(args, "bwd", None):
+        os.environ["AVGEN_ATTN_BWD"] = args.bwd
+        from avgen_b200.ops import kernels as K
+
+        K._ATTN_BWD = args.bwd
+    if args.op == "attention":
+        bench_attention(args.L, args.H, args.iters, args.once)
+    else:
+        bench_gemm(args.m, args.n, args.k, args.iters)
+    from avgen_b200.ops._ext import check_errors
+
+    code = check_errors()
+    if code:
+        raise SystemExit(f"a kernel recorded error code {code}")
+
+
+if __name__ == "__main__":
+    main()

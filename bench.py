@@ -54,6 +54,8 @@ def parse_args() -> argparse.Namespace:
                    help="reference CP attention: its own context_parallel_region (ring) or as shipped (block-local)")
     p.add_argument("--depth", type=int, default=DEPTH, help="override for quick local checks (not a valid bench)")
     p.add_argument("--frames", type=int, default=FRAMES)
+    p.add_argument("--profile-step", action="store_true",
+                   help="after the timed region, print the device-time breakdown of one step (stderr)")
     return p.parse_args()
 
 
@@ -233,6 +235,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     barrier()
     launches = (K.launch_count() - launches0)
     clock_info = clocks.stop(list(range(world))) if rank == 0 else {}
+    if args.profile_step:
+        _profile_one_step(lambda: step(dev_batches), rank)
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
     loss_val = float(metrics.loss.item())
     from avgen_b200.ops._ext import check_errors
@@ -261,12 +265,29 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     mfu = flops * value / (world * PEAK_NOMINAL)
     return {
         "value": value, "ms_per_step": ms, "mfu": mfu, "loss": loss_val, "kernel_errors": err,
-        "gpu_launches": launches // max(1, args.steps), "gpu_launches_total": launches,
+        "gpu_launches": launches, "gpu_launches_per_step": launches // max(1, args.steps),
         "e2e": {"value": samples_per_step / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
         "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro,
         "params": sum(p.numel() for p in model.parameters()),
     }
+
+
+def _profile_one_step(fn, rank: int) -> None:  # noqa: ANN001
+    """Kernel-time shares of one step (torch.profiler CUDA activity); never a bench value."""
+    from torch.profiler import ProfilerActivity, profile
+
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    if rank != 0:
+        return
+    rows = [(e.device_time_total, e.count, e.key) for e in prof.key_averages() if e.device_time_total > 0]
+    total = sum(r[0] for r in rows)
+    print(f"[profile] one step: {total / 1e3:.1f} ms of kernel time", file=sys.stderr)
+    for t, n, key in sorted(rows, reverse=True)[:30]:
+        print(f"[profile] {t / 1e3:9.2f} ms {100 * t / total:5.1f}%  n={n:5d}  {key[:90]}", file=sys.stderr)
 
 
 # --------------------------------------------------------------------------- reference arm

@@ -354,3 +354,32 @@ def test_attention_bwd_variants_agree(mode: str, monkeypatch: pytest.MonkeyPatch
         assert torch.isfinite(got.float()).all()
         _close(got, torch.nan_to_num(want), rtol=3e-2, atol=3e-2)
     _errors_clear()
+
+
+def test_norm_column_reductions_many_rows() -> None:
+    """More rows than a grid dimension holds, with and without modulation (per-token rows)."""
+    ops = _ops()
+    torch.manual_seed(14)
+    rows, w_ = 70000, 256
+    x = torch.randn(rows, w_, device=DEV).bfloat16()
+    weight = torch.rand(w_, device=DEV) + 0.5
+    y, rstd = ops.rmsnorm_mod(x, weight)
+    dy = torch.randn(rows, w_, device=DEV).bfloat16()
+    dw = torch.zeros(w_, device=DEV)
+    dx = ops.rmsnorm_mod_bwd(x, rstd, dy, weight, dweight=dw)
+    xr, wr = x.float().requires_grad_(), weight.clone().requires_grad_()
+    ref = F.rms_norm(xr, (w_,), wr, 1e-6)
+    ref.backward(dy.float())
+    _close(y, ref)
+    _close(dx, xr.grad)
+    _close(dw, wr.grad, rtol=1e-2, atol=1e-2)
+    # per-token modulation rows (rows_per_batch = 1)
+    scale = torch.randn(rows, w_, device=DEV) * 0.1
+    gate = torch.randn(rows, w_, device=DEV)
+    ds = torch.zeros_like(scale)
+    ops.rmsnorm_mod_bwd(x, rstd, dy, weight, scale, None, dscale=ds, rows_per_batch=1)
+    _close(ds, dy.float() * F.rms_norm(x.float(), (w_,), weight, 1e-6), rtol=2e-2, atol=2e-2)
+    dg = torch.zeros_like(gate)
+    ops.gate_bwd(dy, x, gate, dg, rows_per_batch=1)
+    _close(dg, dy.float() * x.float(), rtol=1e-2, atol=1e-2)
+    _errors_clear()

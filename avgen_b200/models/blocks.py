@@ -70,6 +70,10 @@ def _fused_eligible(block: DiTBlock, hidden: torch.Tensor) -> bool:
         linears += [ca.q_proj, ca.k_proj, ca.v_proj, ca.out_proj]
         if ca.head_dim != 128:
             return False
+    from torch.distributed.tensor import DTensor
+
+    if any(isinstance(m.weight, DTensor) for m in linears if isinstance(m, nn.Linear)):
+        return False  # tensor-parallel shards run the module path
     return all(getattr(m, "bias", None) is None for m in linears if isinstance(m, nn.Linear))
 
 

@@ -256,7 +256,8 @@ class VideoDiT(nn.Module):
 
         block = standard_block_plan(sequence_parallel=sequence_parallel,
                                     cross_attention_prefix="cross_attention" if self.config.cross_attention else None,
-                                    ffn=self.config.ffn)
+                                    ffn_projections=("gate_proj", "up_proj") if self.config.ffn == "swiglu"
+                                    else ("up_proj",))
         return standard_root_plan(sequence_parallel=sequence_parallel), block
 
 

@@ -93,15 +93,26 @@ class BlockSpec:
 def _packed(module: nn.Module, key: str, params: list[torch.Tensor], build) -> torch.Tensor:  # noqa: ANN001
     from avgen_b200.models.linear import weight_epoch
 
-    cache = module.__dict__.setdefault("_avgen_packed", {})
-    version = (weight_epoch(), *((p._version, p.data_ptr()) for p in params))
-    hit = cache.get(key)
-    if hit is not None and hit[0] == version:
-        return hit[1]
     with torch.no_grad():
-        value = build(*[p.detach() for p in params]).to(_BF16).contiguous()
-    cache[key] = (version, value)
-    return value
+        fresh = lambda: build(*[p.detach() for p in params]).to(_BF16).contiguous()  # noqa: E731
+        if _fsdp_managed(module):
+            return fresh()  # FSDP re-gathers the parameters every forward: never serve a cached copy
+        cache = module.__dict__.setdefault("_avgen_packed", {})
+        version = (weight_epoch(), *((p._version, p.data_ptr()) for p in params))
+        hit = cache.get(key)
+        if hit is not None and hit[0] == version:
+            return hit[1]
+        value = fresh()
+        cache[key] = (version, value)
+        return value
+
+
+def _fsdp_managed(module: nn.Module) -> bool:
+    try:
+        from torch.distributed.fsdp import FSDPModule
+    except ImportError:
+        return False
+    return isinstance(module, FSDPModule)
 
 
 def packed_weights(block: nn.Module) -> dict[str, torch.Tensor]:

@@ -96,8 +96,20 @@ def _kernel_ok(x: torch.Tensor, layer: nn.Linear) -> bool:
             and x.numel() > 0)
 
 
+def _is_dtensor(t: torch.Tensor) -> bool:
+    from torch.distributed.tensor import DTensor
+
+    return isinstance(t, DTensor)
+
+
 def linear(x: torch.Tensor, layer: nn.Linear) -> torch.Tensor:
-    """Apply ``layer`` with the sm_100a GEMM on CUDA (bf16 output), ``F.linear`` on CPU."""
+    """Apply ``layer`` with the sm_100a GEMM on CUDA (bf16 output), ``F.linear`` on CPU.
+
+    A tensor-parallel layer (DTensor weight) runs its own forward so its parallel
+    style's hooks move activations between local shards and DTensors.
+    """
+    if _is_dtensor(layer.weight):
+        return layer(x)
     if _kernel_ok(x, layer):
         return KernelLinear.apply(x, layer.weight, layer.bias)
     if x.device.type == "cuda":

@@ -1,0 +1,134 @@
+"""``parallelize``: apply a parallel plan to a model (avgen/parallel/apply.py:49-259 API).
+
+Order: float8 conversion -> tensor parallel -> ``adapt`` hook (LoRA, control
+branches) -> activation checkpointing -> FSDP2/HSDP over the data (and
+context) dimensions, or replicated data parallelism.
+
+Replicated data parallelism (``dp_replicate`` and/or ``cp`` without sharding)
+is native by default: the model stays an ordinary module and the fused AdamW
+all-reduces its flat fp32 gradient buffer once per step over
+``ParallelModel.data_group`` (one collective, no per-bucket hooks). ``ParallelConfig(native_data_parallel=False)``
+wraps the model in ``DistributedDataParallel`` instead.
+"""
+from __future__ import annotations
+
+import warnings
+from collections.abc import Callable
+from dataclasses import dataclass, field
+from typing import Any
+
+from torch import nn
+
+from avgen_b200.parallel.activation import ActivationCheckpointConfig, apply_activation_checkpointing
+from avgen_b200.parallel.dims import ParallelDims, submesh
+from avgen_b200.parallel.fsdp import FSDPConfig, apply_fsdp
+from avgen_b200.parallel.precision import PrecisionConfig, convert_to_float8
+from avgen_b200.parallel.tensor import apply_tensor_parallel
+
+__all__ = ["ParallelConfig", "ParallelModel", "parallelize"]
+
+
+@dataclass(frozen=True, slots=True)
+class ParallelConfig:
+    precision: PrecisionConfig = field(default_factory=PrecisionConfig)
+    activation_checkpoint: ActivationCheckpointConfig = field(default_factory=ActivationCheckpointConfig)
+    fsdp: FSDPConfig = field(default_factory=FSDPConfig)
+    compile_blocks: bool = False
+    compile_mode: str = "default"
+    block_attribute: str = "blocks"
+    sequence_parallel: bool = False
+    native_data_parallel: bool = True
+
+
+@dataclass(frozen=True, slots=True)
+class ParallelModel:
+    model: nn.Module
+    dims: ParallelDims
+    mesh: Any
+    applied: tuple[str, ...]
+
+    def submesh(self, name: str) -> Any:
+        return submesh(self.mesh, name)
+
+    @property
+    def cp_mesh(self) -> Any:
+        return self.submesh("cp")
+
+    @property
+    def pp_mesh(self) -> Any:
+        return self.submesh("pp")
+
+    @property
+    def data_group(self) -> Any:
+        """Process group the optimizer averages gradients over (native data parallelism): the
+        replicated data ranks and the context-parallel ranks, which hold identical parameters."""
+        if self.mesh is None or not any(a.startswith("native_dp") for a in self.applied):
+            return None
+        for name in ("dp_cp", "dp_replicate", "cp"):
+            m = submesh(self.mesh, name)
+            if m is not None:
+                return m.get_group()
+        return None
+
+
+def _fsdp_mesh(dims: ParallelDims, mesh: Any) -> Any:
+    if dims.dp_replicate_enabled:
+        hsdp = submesh(mesh, "hsdp")
+        if hsdp is not None:
+            return hsdp
+    for name in ("dp_shard_cp", "dp_shard", "cp"):
+        m = submesh(mesh, name)
+        if m is not None:
+            return m
+    return None
+
+
+def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, config: ParallelConfig | None = None,
+                adapt: Callable[[nn.Module], nn.Module] | None = None) -> ParallelModel:
+    cfg = config or ParallelConfig()
+    applied: list[str] = []
+    if mesh is None and dims.world_size > 1:
+        mesh = dims.build_mesh()
+    n8 = convert_to_float8(model, cfg.precision)
+    if n8:
+        applied.append(f"float8({n8} linears)")
+    if dims.tp_enabled and mesh is not None:
+        apply_tensor_parallel(model, mesh["tp"], sequence_parallel=cfg.sequence_parallel,
+                              block_attribute=cfg.block_attribute)
+        applied.append(f"tensor_parallel(tp={dims.tensor})")
+    if adapt is not None:
+        model = adapt(model)
+        applied.append("adapt")
+    if cfg.activation_checkpoint.enabled:
+        apply_activation_checkpointing(model, cfg.activation_checkpoint, block_attribute=cfg.block_attribute)
+        applied.append(f"activation_checkpoint({cfg.activation_checkpoint.mode})")
+    if cfg.compile_blocks:
+        warnings.warn("compile_blocks is ignored: blocks already run as fused sm_100a kernels", RuntimeWarning,
+                      stacklevel=2)
+    if mesh is not None and dims.dp_shard_enabled:
+        target = _fsdp_mesh(dims, mesh)
+        if target is not None:
+            apply_fsdp(model, target, precision=cfg.precision, config=cfg.fsdp)
+            if dims.dp_replicate_enabled:
+                applied.append(f"hsdp(dp_replicate={dims.dp_replicate}, dp_shard={dims.dp_shard})")
+            else:
+                applied.append(f"fsdp(dp_shard={dims.dp_shard}" + (f", cp={dims.context})" if dims.cp_enabled
+                                                                   else ")"))
+    elif mesh is not None and (dims.dp_replicate_enabled or dims.cp_enabled):
+        if cfg.native_data_parallel:
+            applied.append(f"native_dp(dp_replicate={dims.dp_replicate}, cp={dims.context})")
+        else:
+            from torch.nn.parallel import DistributedDataParallel
+
+            name = "dp_cp" if submesh(mesh, "dp_cp") is not None else (
+                "dp_replicate" if dims.dp_replicate_enabled else "cp")
+            model = DistributedDataParallel(model, device_mesh=submesh(mesh, name), gradient_as_bucket_view=True)
+            applied.append(f"ddp({name})")
+    if dims.cp_enabled and mesh is not None:
+        from avgen_b200.parallel.context import apply_context_parallel
+
+        apply_context_parallel(model, submesh(mesh, "cp"))
+        applied.append(f"context_parallel(cp={dims.context})")
+    if not applied:
+        applied.append("single-device")
+    return ParallelModel(model=model, dims=dims, mesh=mesh, applied=tuple(applied))

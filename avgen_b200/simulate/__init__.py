@@ -11,7 +11,7 @@ from avgen_b200.simulate.memory import (OPTIMIZER_BYTES, MemoryEstimate, ModelSh
                                         estimate_memory, measure_memory)
 from avgen_b200.simulate.plan import PlanCandidate, SearchSpace, render_plan_table, search_parallel_plan
 from avgen_b200.simulate.report import SimulationReport, simulate_config
-from avgen_b200.simulate.world import FakeWorld, fake_tensors, fake_world, meta_init, simulate_rank, summarize_sharding
+from avgen_b200.simulate.world import FakeWorld, fake_tensors, fake_world, meta_init, simulate_rank
 
 __all__ = ["A100_80GB", "ACCELERATORS", "B200", "ETHERNET_200G", "H100_SXM", "H200_SXM", "INFINIBAND_NDR", "NVLINK4",
            "NVLINK5", "OPTIMIZER_BYTES", "Accelerator", "CollectiveCost", "CommunicationEstimate", "ComputeEstimate",
@@ -20,4 +20,4 @@ __all__ = ["A100_80GB", "ACCELERATORS", "B200", "ETHERNET_200G", "H100_SXM", "H2
            "capture_execution_trace", "capture_with_timing", "count_collectives", "estimate_compute",
            "estimate_memory", "estimate_step_communication", "fake_tensors", "fake_world", "measure_memory",
            "measure_runtime", "meta_init", "render_plan_table", "search_parallel_plan", "simulate_config",
-           "simulate_rank", "suggest_activation_policy", "summarize_sharding", "transformer_flops"]
+           "simulate_rank", "suggest_activation_policy", "transformer_flops"]

@@ -20,7 +20,7 @@ from torch.distributed.device_mesh import DeviceMesh
 
 from avgen_b200.parallel.dims import ParallelDims
 
-__all__ = ["FakeWorld", "fake_tensors", "fake_world", "meta_init", "simulate_rank", "summarize_sharding"]
+__all__ = ["FakeWorld", "fake_tensors", "fake_world", "meta_init", "simulate_rank"]
 
 _ENV = ("RANK", "WORLD_SIZE", "LOCAL_RANK", "LOCAL_WORLD_SIZE")
 
@@ -107,25 +107,6 @@ def fake_tensors(allow_fallback: bool = True) -> Iterator[Any]:
         yield mode
 
 
-def summarize_sharding(model: nn.Module) -> dict[str, Any]:
-    """Local vs. global element counts of a (possibly DTensor-sharded) model."""
-    from torch.distributed.tensor import DTensor
-
-    local = total = sharded = 0
-    placements: dict[str, int] = {}
-    for p in model.parameters():
-        total += p.numel()
-        if isinstance(p, DTensor):
-            local += p.to_local().numel()
-            sharded += 1
-            key = ",".join(str(pl) for pl in p.placements)
-            placements[key] = placements.get(key, 0) + 1
-        else:
-            local += p.numel()
-    return {"local_elements": local, "global_elements": total, "sharded_parameters": sharded,
-            "placements": placements}
-
-
 def simulate_rank(dims: ParallelDims, build: Callable[[], nn.Module],
                   apply_plan: Callable[[nn.Module, ParallelDims, DeviceMesh], nn.Module], *, rank: int = 0,
                   device_type: str | None = None) -> dict[str, Any]:
@@ -138,6 +119,8 @@ def simulate_rank(dims: ParallelDims, build: Callable[[], nn.Module],
         model = apply_plan(model, dims, mesh)
         report = world.describe()
         report["global_parameters"] = params
+        from avgen_b200.parallel.fsdp import summarize_sharding
+
         report.update(summarize_sharding(model))
         report["parameters_per_rank"] = report.pop("local_elements")
         per_rank = report["parameters_per_rank"]

@@ -239,7 +239,12 @@ def build_optimizer(model: nn.Module, *, name: str = "adamw", lr: float, weight_
         raise ValueError("eps must be positive")
     groups = build_param_groups(model, weight_decay=weight_decay, no_decay_patterns=no_decay_patterns)
     if name == "adamw":
+        from torch.distributed.tensor import DTensor
+
         on_cuda = all(p.device.type == "cuda" for g in groups for p in g["params"])
+        if any(isinstance(p, DTensor) for g in groups for p in g["params"]):
+            # FSDP / tensor-parallel shards: per-shard updates; the flat-buffer kernel needs plain tensors
+            return torch.optim.AdamW(groups, lr=lr, betas=betas, eps=eps, fused=on_cuda or None)
         use_fused = on_cuda if fused is None else fused
         if use_fused:
             return FusedAdamW(groups, lr=lr, betas=betas, eps=eps, dp_group=dp_group)

@@ -151,6 +151,17 @@ def _set_gradient_sync(model: torch.nn.Module, enabled: bool) -> None:
         setter(enabled)
 
 
+def _average_gradients(params: Sequence[torch.Tensor], group: Any) -> None:
+    import torch.distributed as dist
+
+    if group is None or not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return
+    world = dist.get_world_size(group)
+    for p in params:
+        dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=group)
+        p.grad.div_(world)
+
+
 def _neutralise_nonfinite(grads: Sequence[torch.Tensor], finite: torch.Tensor) -> None:
     with torch.no_grad():
         for g in grads:
@@ -160,8 +171,14 @@ def _neutralise_nonfinite(grads: Sequence[torch.Tensor], finite: torch.Tensor) -
 def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, patchifier: Patchifier,
                gradient_accumulation_steps: int = 1, microbatch_index: int = 0, max_grad_norm: float | None = None,
                cp_mesh: DeviceMesh | None = None, pp_mesh: DeviceMesh | None = None,
-               autocast_dtype: torch.dtype = torch.bfloat16, data_world: int = 1) -> tuple[TrainState, StepMetrics]:
-    """One micro-step (and the optimizer step on the last micro-step)."""
+               autocast_dtype: torch.dtype = torch.bfloat16, data_world: int = 1,
+               data_group: Any = None) -> tuple[TrainState, StepMetrics]:
+    """One micro-step (and the optimizer step on the last micro-step).
+
+    ``data_group`` (native data parallelism, see ``ParallelModel.data_group``):
+    ranks whose gradients are averaged before the optimizer step. The fused
+    AdamW averages its flat buffer over its own ``dp_group`` instead.
+    """
     if not 0 <= microbatch_index < gradient_accumulation_steps:
         raise ValueError(f"microbatch_index={microbatch_index} must lie in [0, {gradient_accumulation_steps})")
     dev = batch.device
@@ -185,6 +202,7 @@ def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, pa
             from avgen_b200.parallel.comm import clip_grad_norm
 
             params = [p for p in state.model.parameters() if p.grad is not None]
+            _average_gradients(params, data_group)
             if max_grad_norm is not None and params:
                 grad_norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh).to(torch.float32)
             elif params:
@@ -236,7 +254,8 @@ class Trainer:
             gradient_accumulation_steps=accumulation or self.config.gradient_accumulation_steps,
             microbatch_index=microbatch_index, max_grad_norm=self.config.max_grad_norm,
             cp_mesh=getattr(self.parallel, "cp_mesh", None), pp_mesh=getattr(self.parallel, "pp_mesh", None),
-            autocast_dtype=self.config.torch_autocast_dtype, data_world=self.config.data_world)
+            autocast_dtype=self.config.torch_autocast_dtype, data_world=self.config.data_world,
+            data_group=getattr(self.parallel, "data_group", None))
         return metrics
 
     def fit(self, loader: Iterable[MediaBatch], total_steps: int | None = None) -> None:

@@ -1,0 +1,196 @@
+"""Multi-process parallelism on CPU (gloo, world size 2): FSDP2, tensor parallel and context
+parallel each reproduce single-process forward and gradients; a rank with a non-finite loss
+makes every rank skip the same step; data shards are disjoint."""
+from __future__ import annotations
+
+import os
+import socket
+from dataclasses import asdict
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _spawn(fn, world: int = 2, *args) -> None:  # noqa: ANN001
+    mp.spawn(_entry, args=(world, _free_port(), fn, args), nprocs=world, join=True)
+
+
+def _entry(rank: int, world: int, port: int, fn, args) -> None:  # noqa: ANN001
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    from datetime import timedelta
+
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        fn(rank, world, *args)
+    finally:
+        dist.destroy_process_group()
+
+
+def _model(seed: int = 0):  # noqa: ANN202
+    from avgen_b200.models import build_model, preset
+
+    torch.manual_seed(seed)
+    cfg = {k: v for k, v in asdict(preset("tiny")).items() if k != "rope_scaling"}
+    m = build_model("video_dit", cfg)
+    m.init_weights()
+    with torch.no_grad():
+        for p in m.parameters():
+            p.add_(0.02 * torch.randn_like(p))
+    return m
+
+
+def _inputs(seed: int, model):  # noqa: ANN001, ANN202
+    """A ModelInput with per-token levels (a clean first frame) from a synthetic batch."""
+    from avgen_b200.codecs import ReferenceTextEncoder  # noqa: F401 (import check)
+    from avgen_b200.core.tokens import TextContext
+    from avgen_b200.infer.conditioning import StreamState, condition_first_frame
+
+    g = torch.Generator().manual_seed(seed)
+    c = model.config
+    lat = torch.randn(1, c.in_channels, 4, 8, 8, generator=g)
+    text = TextContext(features=torch.randn(1, 6, c.text_width, generator=g), mask=torch.ones(1, 6, dtype=torch.bool))
+    return condition_first_frame(StreamState(lat, fps=8.0), lat[:, :, 0], sigma=0.6, text=text,
+                                 patchifier=model.patchifier)
+
+
+def _loss(out) -> torch.Tensor:  # noqa: ANN001
+    w = torch.linspace(-1.0, 1.0, out.video.shape[-1])
+    return (out.video * w).sum()
+
+
+def _reference_grads(seeds: list[int]) -> tuple[list[torch.Tensor], dict[str, torch.Tensor]]:
+    model = _model()
+    outs, grads = [], {}
+    for s in seeds:
+        model.zero_grad()
+        out = model(_inputs(s, model))
+        _loss(out).backward()
+        outs.append(out.video.detach())
+        for n, p in model.named_parameters():
+            grads[n] = grads.get(n, 0) + p.grad.detach() / len(seeds)
+    return outs, grads
+
+
+def _fsdp_worker(rank: int, world: int) -> None:
+    from torch.distributed.tensor import DTensor
+
+    from avgen_b200.parallel import ParallelDims, parallelize
+
+    ref_outs, ref_grads = _reference_grads([10, 11])
+    from avgen_b200.parallel import ParallelConfig, PrecisionConfig
+
+    model = _model()
+    dims = ParallelDims(world_size=world, dp_shard=world)
+    fp32 = ParallelConfig(precision=PrecisionConfig(param_dtype="float32"))  # exact comparison with fp32 reference
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"), config=fp32)
+    assert pm.applied[0].startswith("fsdp")
+    out = pm.model(_inputs(10 + rank, model))
+    torch.testing.assert_close(out.video.detach(), ref_outs[rank], rtol=1e-4, atol=1e-5)
+    _loss(out).backward()
+    for n, p in pm.model.named_parameters():
+        g = p.grad.full_tensor() if isinstance(p.grad, DTensor) else p.grad
+        torch.testing.assert_close(g, ref_grads[n], rtol=1e-3, atol=1e-5, msg=n)
+
+
+def _tp_worker(rank: int, world: int) -> None:
+    from torch.distributed.tensor import DTensor
+
+    from avgen_b200.parallel import ParallelDims, parallelize
+
+    ref_outs, ref_grads = _reference_grads([21])
+    model = _model()
+    dims = ParallelDims(world_size=world, tensor=world)
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"))
+    assert any(isinstance(p, DTensor) for p in pm.model.parameters())
+    out = pm.model(_inputs(21, model))
+    torch.testing.assert_close(out.video.detach(), ref_outs[0], rtol=1e-4, atol=1e-5)
+    _loss(out).backward()
+    for n, p in pm.model.named_parameters():
+        g = p.grad.full_tensor() if isinstance(p.grad, DTensor) else p.grad
+        torch.testing.assert_close(g, ref_grads[n], rtol=1e-3, atol=1e-5, msg=n)
+
+
+def _cp_worker(rank: int, world: int) -> None:
+    from avgen_b200.core.model_input import ModelOutput  # noqa: F401
+    from avgen_b200.parallel import ParallelDims, gather_tokens, parallelize, shard_stream
+
+    ref_outs, ref_grads = _reference_grads([31])
+    model = _model()
+    dims = ParallelDims(world_size=world, context=world)
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"))
+    inputs = _inputs(31, model)
+    local = inputs.replace_streams(video=shard_stream(inputs.video, pm.cp_mesh))
+    out = pm.model(local)
+    full = gather_tokens(out.video.detach(), pm.cp_mesh)
+    torch.testing.assert_close(full, ref_outs[0], rtol=1e-4, atol=1e-5)
+    _loss(out).backward()  # per-shard partial loss: the full gradient is the sum over shards
+    for n, p in pm.model.named_parameters():
+        g = p.grad.clone()
+        dist.all_reduce(g)
+        torch.testing.assert_close(g, ref_grads[n], rtol=1e-3, atol=1e-5, msg=n)
+
+
+def _nonfinite_worker(rank: int, world: int) -> None:
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.parallel import ParallelDims, parallelize
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                                  build_timestep_sampler, train_step)
+
+    model = _model()
+    dims = ParallelDims(world_size=world, dp_replicate=world)
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"))
+    assert pm.data_group is not None
+    opt = build_optimizer(pm.model, lr=1e-2)
+    state = TrainState(model=pm.model, optimizer=opt, rng=RNGStreams.for_rank(0, data_rank=rank))
+    obj = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("uniform"), MultiTaskConditioning())
+    c = model.config
+    batch = random_batch(batch=1, channels=c.in_channels, frames=2, height=8, width=8, text_tokens=4,
+                         text_width=c.text_width, generator=torch.Generator().manual_seed(rank))
+    if rank == 1:
+        batch.video.view(-1)[0] = float("nan")
+    before = {n: p.detach().clone() for n, p in pm.model.named_parameters()}
+    _, metrics = train_step(state, batch, obj, patchifier=model.patchifier, max_grad_norm=1.0,
+                            data_group=pm.data_group)
+    assert bool(metrics.skipped), "every rank must skip the step when one rank's gradients are non-finite"
+    for n, p in pm.model.named_parameters():
+        assert torch.equal(p.detach(), before[n]), n
+    # a clean step moves the parameters identically on both ranks
+    batch.video.nan_to_num_(0.0)
+    _, metrics = train_step(state, batch, obj, patchifier=model.patchifier, max_grad_norm=1.0,
+                            data_group=pm.data_group)
+    assert not bool(metrics.skipped)
+    flat = torch.cat([p.detach().reshape(-1) for p in pm.model.parameters()])
+    other = flat.clone()
+    dist.broadcast(other, src=0)
+    torch.testing.assert_close(flat, other)
+
+
+def _shards_worker(rank: int, world: int) -> None:
+    from avgen_b200.data.synthetic import SyntheticConfig, SyntheticSource
+
+    src = SyntheticSource(SyntheticConfig(num_samples=37), data_rank=rank, data_world=world)
+    it = iter(src)
+    ids = [int(i) for _ in range(len(src)) for i in next(it).sample_ids]
+    gathered: list = [None] * world
+    dist.all_gather_object(gathered, ids)
+    allids = [i for part in gathered for i in part]
+    assert len(allids) == len(set(allids)) == 37
+
+
+@pytest.mark.parametrize("worker", [_fsdp_worker, _tp_worker, _cp_worker, _nonfinite_worker],
+                         ids=["fsdp", "tensor_parallel", "context_parallel", "nonfinite_skip"])
+def test_two_rank_parallelism(worker) -> None:  # noqa: ANN001
+    _spawn(worker)
+
+
+def test_data_shards_disjoint() -> None:
+    _spawn(_shards_worker)

@@ -17,7 +17,7 @@ __all__ = ["ActivationSpec", "BucketConfig", "CheckpointConfig", "DataConfig", "
 
 SCHEMA_VERSION = 1
 DTYPE_NAMES = ("float32", "bfloat16", "float16")
-AC_MODES = ("none", "full", "selective_op", "selective_layer")
+AC_MODES = ("fused", "none", "full", "selective_op", "selective_layer")
 OPTIMIZER_NAMES = ("adamw", "adamw_8bit", "adafactor", "adamw_bf16_state", "sgd_momentum", "muon")
 SCHEDULE_NAMES = ("constant", "cosine", "linear", "wsd")
 TIMESTEP_SAMPLERS = ("uniform", "logit_normal", "shifted_logit_normal", "mode")
@@ -284,7 +284,8 @@ class PrecisionSpec:
 
 @dataclass(frozen=True, slots=True)
 class ActivationSpec:
-    mode: str = "selective_op"
+    # "fused": the sm_100a block's built-in recompute (saves x, O, lse); the others are the eager policies
+    mode: str = "fused"
     layer_interval: int = 2
     save_op_frequency: int = 1
 

@@ -6,6 +6,7 @@ Exit codes: 0 success, 1 runtime error, 2 usage error, 3 configuration error,
 from __future__ import annotations
 
 import argparse
+import re
 import sys
 from collections.abc import Sequence
 
@@ -41,10 +42,27 @@ def build_parser() -> argparse.ArgumentParser:
     return parser
 
 
+_OVERRIDE = re.compile(r"^[A-Za-z_][\w.\[\]-]*=")
+
+
+def _overrides_last(argv: list[str]) -> list[str]:
+    """Move ``key=value`` overrides behind the options so they may appear anywhere on the line
+    (argparse only collects one contiguous run of positionals)."""
+    moved, kept = [], []
+    for i, tok in enumerate(argv):
+        prev = argv[i - 1] if i else ""
+        if _OVERRIDE.match(tok) and not prev.startswith("-"):
+            moved.append(tok)
+        else:
+            kept.append(tok)
+    return kept + moved
+
+
 def main(argv: Sequence[str] | None = None) -> int:
     parser = build_parser()
+    raw = list(argv) if argv is not None else sys.argv[1:]
     try:
-        args = parser.parse_args(list(argv) if argv is not None else None)
+        args = parser.parse_args(_overrides_last(raw))
     except SystemExit as exc:  # argparse: --help (0) or a usage error (2)
         return int(exc.code or 0)
     if args.version:

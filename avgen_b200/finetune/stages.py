@@ -1,0 +1,184 @@
+"""Staged fine-tuning recipes (avgen/finetune/stages.py:262-683 API).
+
+A :class:`FinetuneStage` bundles what to train (patterns, a LoRA or control
+adapter, or distillation), optimizer settings, a timestep plan and a
+conditioning-mode mix. Registered stages: ``full``, ``lora``, ``control``,
+``resolution_adaptation``, ``duration_extension`` and ``distillation``.
+"""
+from __future__ import annotations
+
+import math
+from collections.abc import Mapping, Sequence
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from avgen_b200.finetune.adapters import ControlAdapterConfig
+from avgen_b200.finetune.lora import LoRAConfig
+
+__all__ = ["DistillationConfig", "FinetuneStage", "TimestepPlan", "apply_stage", "get_stage", "list_stages",
+           "register_stage", "resolution_shift", "shift_timesteps", "stage_names_for", "standard_stages"]
+
+_MODES = ("JOINT", "VIDEO_TO_AUDIO", "AUDIO_TO_VIDEO", "VIDEO_ONLY", "CONTINUATION", "INPAINT", "IMAGE_TO_VIDEO",
+          "VIDEO_TO_VIDEO")
+
+
+def resolution_shift(sequence_length: int, *, base_length: int = 4096, base_shift: float = 1.0,
+                     max_length: int = 65536, max_shift: float = 3.0) -> float:
+    """Timestep shift growing linearly in the token count, clamped to its end points."""
+    if base_length >= max_length:
+        raise ValueError("base_length must be below max_length")
+    t = (sequence_length - base_length) / (max_length - base_length)
+    return min(max(base_shift + t * (max_shift - base_shift), min(base_shift, max_shift)), max(base_shift, max_shift))
+
+
+def shift_timesteps(noise_level: torch.Tensor, shift: float) -> torch.Tensor:
+    if not shift > 0:
+        raise ValueError(f"shift must be positive; got {shift!r}")
+    return shift * noise_level / (1.0 + (shift - 1.0) * noise_level)
+
+
+@dataclass(frozen=True, slots=True)
+class TimestepPlan:
+    sampler: str = "logit_normal"
+    options: tuple[tuple[str, float], ...] = ()
+    shift: float | None = None
+    base_length: int = 4096
+    base_shift: float = 1.0
+    max_length: int = 65536
+    max_shift: float = 3.0
+
+    def shift_for(self, sequence_length: int) -> float:
+        if self.shift is not None:
+            return self.shift
+        return resolution_shift(sequence_length, base_length=self.base_length, base_shift=self.base_shift,
+                                max_length=self.max_length, max_shift=self.max_shift)
+
+    def as_kwargs(self) -> dict[str, float]:
+        return {k: float(v) for k, v in self.options}
+
+
+@dataclass(frozen=True, slots=True)
+class DistillationConfig:
+    method: str = "progressive"
+    teacher_checkpoint: str | None = None
+    student_steps: int = 4
+    distill_guidance: bool = True
+    teacher_steps: int = 50
+
+    def __post_init__(self) -> None:
+        if self.method not in ("progressive", "consistency", "guidance"):
+            raise ValueError(f"unknown distillation method {self.method!r}")
+        if self.student_steps < 1 or self.teacher_steps < self.student_steps:
+            raise ValueError("need 1 <= student_steps <= teacher_steps")
+
+
+@dataclass(frozen=True, slots=True)
+class FinetuneStage:
+    name: str
+    description: str
+    trainable_patterns: tuple[str, ...] = ()
+    frozen_patterns: tuple[str, ...] = ()
+    lora: LoRAConfig | None = None
+    control: ControlAdapterConfig | None = None
+    distillation: DistillationConfig | None = None
+    learning_rate: float = 1e-4
+    weight_decay: float = 0.0
+    warmup_steps: int = 500
+    schedule: str = "constant"
+    max_grad_norm: float = 1.0
+    ema_decay: float | None = None
+    timesteps: TimestepPlan = field(default_factory=TimestepPlan)
+    conditioning_mix: tuple[tuple[str, float], ...] = (("JOINT", 1.0),)
+    batch_size: int | None = None
+    total_steps: int | None = None
+    notes: str = ""
+
+    def __post_init__(self) -> None:
+        if not self.name:
+            raise ValueError("stage name must be non-empty")
+        if not (math.isfinite(self.learning_rate) and self.learning_rate > 0):
+            raise ValueError("learning_rate must be positive")
+        if self.lora is not None and self.control is not None:
+            raise ValueError("a stage trains either a LoRA or a control adapter, not both")
+        for mode, w in self.conditioning_mix:
+            if mode not in _MODES or w < 0:
+                raise ValueError(f"bad conditioning mix entry {(mode, w)!r}")
+        if sum(w for _, w in self.conditioning_mix) <= 0:
+            raise ValueError("conditioning_mix weights must sum to a positive value")
+
+    @property
+    def uses_adapter(self) -> bool:
+        return self.lora is not None or self.control is not None
+
+    def normalized_mix(self) -> dict[str, float]:
+        total = sum(w for _, w in self.conditioning_mix)
+        return {m: w / total for m, w in self.conditioning_mix if w > 0}
+
+
+_STAGES: dict[str, FinetuneStage] = {}
+
+
+def register_stage(stage: FinetuneStage, *, overwrite: bool = False) -> FinetuneStage:
+    if stage.name in _STAGES and not overwrite:
+        raise KeyError(f"stage {stage.name!r} already registered (overwrite=True replaces it)")
+    _STAGES[stage.name] = stage
+    return stage
+
+
+def get_stage(name: str) -> FinetuneStage:
+    if name not in _STAGES:
+        raise KeyError(f"unknown stage {name!r}; registered: {list_stages()}")
+    return _STAGES[name]
+
+
+def list_stages() -> tuple[str, ...]:
+    return tuple(sorted(_STAGES))
+
+
+def standard_stages() -> Mapping[str, FinetuneStage]:
+    return dict(_STAGES)
+
+
+def stage_names_for(modes: Sequence[str]) -> tuple[str, ...]:
+    """Stages whose conditioning mix covers every mode in ``modes``."""
+    return tuple(sorted(n for n, s in _STAGES.items() if all(m in s.normalized_mix() for m in modes)))
+
+
+def apply_stage(model: Any, stage: FinetuneStage) -> Any:
+    from avgen_b200.finetune.freeze import freeze_except, freeze_matching
+    from avgen_b200.finetune.lora import apply_lora, mark_only_lora_trainable
+
+    if stage.lora is not None:
+        apply_lora(model, stage.lora)
+        mark_only_lora_trainable(model, extra_trainable=stage.trainable_patterns)
+    elif stage.trainable_patterns:
+        freeze_except(model, stage.trainable_patterns)
+    if stage.frozen_patterns:
+        freeze_matching(model, stage.frozen_patterns)
+    return model
+
+
+_LN = TimestepPlan(sampler="logit_normal", options=(("mean", 0.0), ("std", 1.0)))
+for _s in (
+    FinetuneStage("full", "every weight trainable at a low rate with EMA", learning_rate=1e-5, warmup_steps=1000,
+                  ema_decay=0.9999, timesteps=_LN),
+    FinetuneStage("lora", "rank-32 LoRA on attention and FFN projections", lora=LoRAConfig(rank=32, alpha=64.0),
+                  learning_rate=1e-4, warmup_steps=200, timesteps=_LN),
+    FinetuneStage("control", "control branch over the first six blocks; base frozen",
+                  control=ControlAdapterConfig(control_width=16, num_blocks=6),
+                  frozen_patterns=("patch_embed", "time_embed", "text_proj", "modulation", "blocks", "final"),
+                  learning_rate=1e-4, warmup_steps=500, ema_decay=0.999, timesteps=TimestepPlan(sampler="uniform")),
+    FinetuneStage("resolution_adaptation", "adapt to a larger spatial size with a length-dependent shift",
+                  learning_rate=2e-5, warmup_steps=500, ema_decay=0.9999,
+                  timesteps=TimestepPlan(sampler="shifted_logit_normal", base_shift=1.0, max_shift=3.0)),
+    FinetuneStage("duration_extension", "longer clips, with continuation and inpainting in the mix",
+                  learning_rate=2e-5, warmup_steps=500, ema_decay=0.9999,
+                  timesteps=TimestepPlan(sampler="shifted_logit_normal", max_shift=3.0),
+                  conditioning_mix=(("JOINT", 0.5), ("CONTINUATION", 0.35), ("INPAINT", 0.15))),
+    FinetuneStage("distillation", "few-step student from a many-step teacher",
+                  distillation=DistillationConfig(method="progressive", student_steps=4, teacher_steps=50),
+                  learning_rate=5e-6, warmup_steps=100, ema_decay=0.999, timesteps=TimestepPlan(sampler="uniform")),
+):
+    register_stage(_s)

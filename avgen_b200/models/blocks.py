@@ -72,8 +72,9 @@ def _fused_eligible(block: DiTBlock, hidden: torch.Tensor) -> bool:
             return False
     from torch.distributed.tensor import DTensor
 
-    if any(isinstance(m.weight, DTensor) for m in linears if isinstance(m, nn.Linear)):
-        return False  # tensor-parallel shards run the module path
+    if any(isinstance(m.weight, DTensor) or hasattr(m, "adapted_weight") for m in linears
+           if isinstance(m, nn.Linear)):
+        return False  # tensor-parallel shards and adapters run the per-layer path
     return all(getattr(m, "bias", None) is None for m in linears if isinstance(m, nn.Linear))
 
 

@@ -110,6 +110,11 @@ def linear(x: torch.Tensor, layer: nn.Linear) -> torch.Tensor:
     """
     if _is_dtensor(layer.weight):
         return layer(x)
+    adapted = getattr(layer, "adapted_weight", None)
+    if callable(adapted):  # LoRA / DoRA: one GEMM on the effective weight, autograd reaches the adapters
+        if _kernel_ok(x, layer):
+            return KernelLinear.apply(x, adapted(), layer.bias)
+        return layer(x)
     if _kernel_ok(x, layer):
         return KernelLinear.apply(x, layer.weight, layer.bias)
     if x.device.type == "cuda":

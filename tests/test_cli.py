@@ -69,3 +69,22 @@ def test_data_commands(tmp_path: Path, capsys: pytest.CaptureFixture[str]) -> No
 def test_info(capsys: pytest.CaptureFixture[str]) -> None:
     assert main(["info"]) == 0
     assert "torch" in capsys.readouterr().out
+
+
+def test_finetune_lora_from_exported_base(tmp_path: Path) -> None:
+    base = tmp_path / "base"
+    assert main(["train", *TINY, "train.steps=1", "checkpoint.save_every=1", f"output_dir={base}"]) == 0
+    export = tmp_path / "export"
+    assert main(["checkpoint", "export", str(base / "checkpoints" / "step_0000000001"), str(export)]) == 0
+    out = tmp_path / "ft"
+    assert main(["finetune", *TINY, "train.steps=2", "--base", str(export), f"output_dir={out}",
+                 "finetune.lora_rank=4"]) == 0
+    from avgen_b200.finetune import LoRAConfig, apply_lora, load_adapter
+
+    from avgen_b200.config import load_config
+    from avgen_b200.config.resolve import build_model
+
+    model = build_model(load_config(out / "config.yaml"))
+    apply_lora(model, LoRAConfig(rank=4, alpha=32.0))
+    meta = load_adapter(out / "adapter.safetensors", model)
+    assert meta["base_checkpoint"] == str(export)

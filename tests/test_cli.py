@@ -73,9 +73,9 @@ def test_info(capsys: pytest.CaptureFixture[str]) -> None:
 
 def test_finetune_lora_from_exported_base(tmp_path: Path) -> None:
     base = tmp_path / "base"
-    assert main(["train", *TINY, "train.steps=1", "checkpoint.save_every=1", f"output_dir={base}"]) == 0
+    assert main(["train", *TINY, "train.steps=2", "checkpoint.save_every=2", f"output_dir={base}"]) == 0
     export = tmp_path / "export"
-    assert main(["checkpoint", "export", str(base / "checkpoints" / "step_0000000001"), str(export)]) == 0
+    assert main(["checkpoint", "export", str(base / "checkpoints" / "step_0000000002"), str(export)]) == 0
     out = tmp_path / "ft"
     assert main(["finetune", *TINY, "train.steps=2", "--base", str(export), f"output_dir={out}",
                  "finetune.lora_rank=4"]) == 0

@@ -149,7 +149,7 @@ __global__ void __launch_bounds__(384, 1)
               mbar_wait(&kv_full[0], 0, abort_flag, p.err, kErrTimeoutMma);
     if (ok) {
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         issue_S(0, 0);
         mma_commit(&s_full[0]);
         issue_S(1, 0);
@@ -161,7 +161,7 @@ __global__ void __launch_bounds__(384, 1)
         const int s2 = (j + 1) & 1;
         if (!mbar_wait(&p_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (elect_one()) {
           issue_PV(0, s, j > 0);
           mma_commit(&o_done[0]);
         }
@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(384, 1)
         if (more) {
           if (!mbar_wait(&kv_full[s2], ((j + 1) >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
           tc_fence_after();
-          if (lane == 0) {
+          if (elect_one()) {
             issue_S(0, s2);
             mma_commit(&s_full[0]);
           }
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (!mbar_wait(&p_full[1], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (elect_one()) {
           issue_PV(1, s, j > 0);
           mma_commit(&o_done[1]);
           mma_commit(&kv_empty[s]);
@@ -494,14 +494,14 @@ __global__ void __launch_bounds__(384, 1)
       ok = mbar_wait(&st_full[i % DkvSmem::STAGES], (i / DkvSmem::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma);
       if (!ok) break;
       tc_fence_after();
-      if (lane == 0) issue_sdp(i);
+      if (elect_one()) issue_sdp(i);
       __syncwarp();
     }
     for (int i = 0; i < iters && ok; ++i) {
       const int buf = i & 1;
       if (!mbar_wait(&p_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         const uint32_t sQ = stage_base(i);
         const uint64_t q0 = mndesc(sQ, 0, 8192), o0 = mndesc(sQ + 16384, 0, 8192);
         const uint32_t bufS = tmem + 64 * buf, bufP = tmem + 128 + 64 * buf;
@@ -522,7 +522,7 @@ __global__ void __launch_bounds__(384, 1)
                        kErrTimeoutMma))
           break;
         tc_fence_after();
-        if (lane == 0) issue_sdp(i + 2);
+        if (elect_one()) issue_sdp(i + 2);
         __syncwarp();
       }
     }
@@ -726,7 +726,7 @@ __global__ void __launch_bounds__(384, 1)
               mbar_wait(&kv_full[0], 0, abort_flag, p.err, kErrTimeoutMma);
     if (ok) {
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         issue_sdp(0, 0);
         issue_sdp(1, 0);
       }
@@ -736,19 +736,19 @@ __global__ void __launch_bounds__(384, 1)
       const bool more = j + 1 < nkv;
       if (!mbar_wait(&ds_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
       tc_fence_after();
-      if (lane == 0) issue_dq(0, j);
+      if (elect_one()) issue_dq(0, j);
       __syncwarp();
       if (more) {
         if (!mbar_wait(&kv_full[(j + 1) % DqSmem::STAGES], ((j + 1) / DqSmem::STAGES) & 1, abort_flag, p.err,
                        kErrTimeoutMma))
           break;
         tc_fence_after();
-        if (lane == 0) issue_sdp(0, j + 1);
+        if (elect_one()) issue_sdp(0, j + 1);
         __syncwarp();
       }
       if (!mbar_wait(&ds_full[1], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         issue_dq(1, j);
         mma_commit(&kv_empty[j % DqSmem::STAGES]);
         if (more) issue_sdp(1, j + 1);
@@ -985,7 +985,7 @@ __global__ void __launch_bounds__(512, 1)
       ok = mbar_wait(&st_full[i % S::STAGES], (i / S::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma);
       if (!ok) break;
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         issue_s(i);
         issue_dp(i);
         mma_commit(&sdp_full[i & 1]);
@@ -996,7 +996,7 @@ __global__ void __launch_bounds__(512, 1)
       const int buf = i & 1;
       if (!mbar_wait(&p_full[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
       tc_fence_after();
-      if (lane == 0) {
+      if (elect_one()) {
         stamp(i, 0);
         const uint32_t sQ = stage_base(i);
         const uint64_t qmn = mndesc(sQ, 0, 8192), omn = mndesc(sQ + 16384, 0, 8192);
@@ -1023,12 +1023,12 @@ __global__ void __launch_bounds__(512, 1)
         if (!mbar_wait(&st_full[(i + 2) % S::STAGES], ((i + 2) / S::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma))
           break;
         tc_fence_after();
-        if (lane == 0) issue_s(i + 2);  // S^T buffer: in order after dV(i) read P^T(i)
+        if (elect_one()) issue_s(i + 2);  // S^T buffer: in order after dV(i) read P^T(i)
         __syncwarp();
         // dP^T buffer holds dQ^T(i) until the epilogue has read it
         if (!mbar_wait(&dq_empty[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
-        if (lane == 0) {
+        if (elect_one()) {
           stamp(i, 1);
           issue_dp(i + 2);
           mma_commit(&sdp_full[buf]);

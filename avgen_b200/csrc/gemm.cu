@@ -336,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        if (lane == 0) {
+        if (elect_one()) {
           const uint32_t a_base = smem_u32(smem + stage * Cfg::STAGE_BYTES);
           const uint32_t b_base = a_base + Cfg::A_BYTES;
 #pragma unroll
@@ -356,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       if (aborted) break;
-      if (lane == 0) mma_commit(&tfull[acc]);
+      if (elect_one()) mma_commit(&tfull[acc]);
       __syncwarp();
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;

@@ -59,6 +59,8 @@ struct FwdSmem {
   static constexpr int BYTES = BARS + 256 + 1024;
 };
 
+// kTrace compiles the diagnostic clock stamps in; the production instance has none of them.
+template <bool kTrace>
 __global__ void __launch_bounds__(384, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                     const __grid_constant__ CUtensorMap tmV, const AttnFwdDesc p) {
@@ -83,6 +85,14 @@ __global__ void __launch_bounds__(384, 1)
   const int hk = h / (p.H / p.Hk);
   const int q0 = qt * 256;
   const int nkv = (p.Lk + kTile - 1) / kTile;
+  // diagnostics: SM clock stamps of CTA 0, 24 per key tile, first 64 tiles. Slots: 0/1/2 MMA
+  // thread passes p_full[0] / kv_full(j+1) / p_full[1]; 3-8 softmax group 0 (S seen, loaded,
+  // max, rescaled, exponentials, arrive), 9-14 the same for group 1; 15/16 S/PV of group 0
+  // complete, 17/18 of group 1 (the tracer waits in order, so 15 can lag).
+  long long* trace = (kTrace && blockIdx.x == 0) ? p.trace : nullptr;
+  auto stamp = [&](int j, int slot) {
+    if (trace != nullptr && j < 64) trace[j * 24 + slot] = clock64();
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -161,6 +171,7 @@ __global__ void __launch_bounds__(384, 1)
         const int s2 = (j + 1) & 1;
         if (!mbar_wait(&p_full[0], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
+        if (lane == 0) stamp(j, 0);
         if (elect_one()) {
           issue_PV(0, s, j > 0);
           mma_commit(&o_done[0]);
@@ -170,6 +181,7 @@ __global__ void __launch_bounds__(384, 1)
         if (more) {
           if (!mbar_wait(&kv_full[s2], ((j + 1) >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
           tc_fence_after();
+          if (lane == 0) stamp(j, 1);
           if (elect_one()) {
             issue_S(0, s2);
             mma_commit(&s_full[0]);
@@ -178,6 +190,7 @@ __global__ void __launch_bounds__(384, 1)
         }
         if (!mbar_wait(&p_full[1], j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
+        if (lane == 0) stamp(j, 2);
         if (elect_one()) {
           issue_PV(1, s, j > 0);
           mma_commit(&o_done[1]);
@@ -188,6 +201,21 @@ __global__ void __launch_bounds__(384, 1)
           }
         }
         __syncwarp();
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ diagnostics: MMA completion stamps
+    if (trace != nullptr && lane == 0) {
+      for (int j = 0; j < nkv && j < 64; ++j) {
+        const uint32_t ph = j & 1;
+        if (!mbar_wait(&s_full[0], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(j, 15);
+        if (!mbar_wait(&s_full[1], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(j, 17);
+        if (!mbar_wait(&o_done[0], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(j, 16);
+        if (!mbar_wait(&o_done[1], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(j, 18);
       }
     }
   } else if (warp >= 4) {
@@ -203,12 +231,15 @@ __global__ void __launch_bounds__(384, 1)
     float m = kNegBig;
     float l = 0.f;
     bool ok = true;
+    const bool tr = kTrace && (warp & 3) == 0 && lane == 0;  // warps 4 and 8 stamp for their group
+    const int ts = 3 + 6 * g;
     for (int j = 0; j < nkv; ++j) {
       if (!mbar_wait(&s_full[g], j & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
         ok = false;
         break;
       }
       tc_fence_after();
+      if (tr) stamp(j, ts);
       uint32_t sr[128];
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -216,6 +247,7 @@ __global__ void __launch_bounds__(384, 1)
         tmem_ld32(tS + 32 * c, chunk);
       }
       tmem_wait_ld();
+      if (tr) stamp(j, ts + 1);
       const int kbase = j * kTile;
       if (kbase + kTile > p.Lk || p.kmask != nullptr) {
         uint32_t words[4];
@@ -236,6 +268,7 @@ __global__ void __launch_bounds__(384, 1)
 #pragma unroll
       for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(sr[c]));
       const float m_new = fmaxf(m, mx * sl);
+      if (tr) stamp(j, ts + 2);
       if (j == 0) {
         m = m_new;
       } else {
@@ -263,6 +296,7 @@ __global__ void __launch_bounds__(384, 1)
           tmem_wait_st();
         }
       }
+      if (tr) stamp(j, ts + 3);
       float sum = 0.f;
 #pragma unroll
       for (int c = 0; c < 64; ++c) {
@@ -272,6 +306,7 @@ __global__ void __launch_bounds__(384, 1)
         sr[c] = pack_bf16(p0, p1);
       }
       l += sum;
+      if (tr) stamp(j, ts + 4);
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const uint32_t (&chunk)[16] = *reinterpret_cast<const uint32_t(*)[16]>(&sr[16 * c]);
@@ -279,6 +314,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       tmem_wait_st();
       tc_fence_before();
+      if (tr) stamp(j, ts + 5);
       mbar_arrive(&p_full[g]);
     }
     if (ok && mbar_wait(&o_done[g], (nkv - 1) & 1, abort_flag, p.err, kErrTimeoutSoftmax)) {
@@ -870,6 +906,7 @@ struct FusedBwdSmem {
 };
 static_assert(FusedBwdSmem::BYTES <= 232448, "fused attention backward exceeds shared memory");
 
+template <bool kTrace>
 __global__ void __launch_bounds__(512, 1)
     attn_bwd_fused_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
@@ -888,6 +925,7 @@ __global__ void __launch_bounds__(512, 1)
   uint64_t* acc_done = dq_empty + 2;             // 1
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_done + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint64_t* trace_bar = bars + 20;               // 5, diagnostics only: per-GEMM completion
 
   const int warp = warp_id();
   const int lane = lane_id();
@@ -899,8 +937,11 @@ __global__ void __launch_bounds__(512, 1)
   const int group = p.H / p.Hk;
   const int nq = (p.Lq + kQT - 1) / kQT;
   const int iters = nq * group;
-  // diagnostics: SM clock stamps of CTA 0, 24 per iteration, first 64 iterations
-  long long* trace = (p.trace != nullptr && blockIdx.x == 0) ? p.trace : nullptr;
+  // diagnostics: SM clock stamps of CTA 0, 24 per iteration, first 64 iterations. Slots:
+  // 0 MMA thread passes p_full(i), 1 it passes dq_empty, 2 softmax starts, 3 warp 4 arrives,
+  // 4 drain sees dq_full, 5/6/7 dV/dK/dQ^T(i) complete, 8-15 softmax warps arrive,
+  // 16-19 drain warps release dQ^T, 20/21 S^T/dP^T(i+2) complete.
+  long long* trace = (kTrace && blockIdx.x == 0) ? p.trace : nullptr;
   auto stamp = [&](int i, int slot) {
     if (trace != nullptr && i < 64) trace[i * 24 + slot] = clock64();
   };
@@ -920,6 +961,7 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(&dq_empty[i], 128);
     }
     mbar_init(acc_done, 1);
+    for (int j = 0; j < 5; ++j) mbar_init(&trace_bar[j], 1);
     *abort_flag = misaligned ? 1 : 0;
     fence_barrier_init();
   }
@@ -1006,15 +1048,18 @@ __global__ void __launch_bounds__(512, 1)
         for (int kk = 0; kk < kQT / 16; ++kk)
           mma_bf16_ts(tDV, tmem + 256 + 64 * buf + half_packed_col(kk), omn + static_cast<uint64_t>(kk * 128), idA,
                       (i > 0 || kk > 0) ? 1u : 0u);
+        if (trace != nullptr) mma_commit(&trace_bar[0]);
 #pragma unroll
         for (int kk = 0; kk < kQT / 16; ++kk)
           mma_bf16_ts(tDK, tmem + 384 + 64 * buf + half_packed_col(kk), qmn + static_cast<uint64_t>(kk * 128), idA,
                       (i > 0 || kk > 0) ? 1u : 0u);
+        if (trace != nullptr) mma_commit(&trace_bar[1]);
 #pragma unroll
         for (int kk = 0; kk < kTile / 16; ++kk)
           mma_bf16_ss(tmem + 384 + 64 * buf, dKt + static_cast<uint64_t>(kk * 128),
                       dsM + static_cast<uint64_t>(kk * 128), idQ, kk > 0 ? 1u : 0u);
         mma_commit(&dq_full[buf]);
+        if (trace != nullptr) mma_commit(&trace_bar[2]);
         mma_commit(&st_empty[i % S::STAGES]);
         if (i == iters - 1) mma_commit(acc_done);
       }
@@ -1023,7 +1068,10 @@ __global__ void __launch_bounds__(512, 1)
         if (!mbar_wait(&st_full[(i + 2) % S::STAGES], ((i + 2) / S::STAGES) & 1, abort_flag, p.err, kErrTimeoutMma))
           break;
         tc_fence_after();
-        if (elect_one()) issue_s(i + 2);  // S^T buffer: in order after dV(i) read P^T(i)
+        if (elect_one()) {
+          issue_s(i + 2);  // S^T buffer: in order after dV(i) read P^T(i)
+          if (trace != nullptr) mma_commit(&trace_bar[3]);
+        }
         __syncwarp();
         // dP^T buffer holds dQ^T(i) until the epilogue has read it
         if (!mbar_wait(&dq_empty[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
@@ -1032,8 +1080,27 @@ __global__ void __launch_bounds__(512, 1)
           stamp(i, 1);
           issue_dp(i + 2);
           mma_commit(&sdp_full[buf]);
+          if (trace != nullptr) mma_commit(&trace_bar[4]);
         }
         __syncwarp();
+      }
+    }
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ diagnostics: GEMM completion stamps
+    if (trace != nullptr && lane == 0) {
+      for (int i = 0; i < iters && i < 64; ++i) {
+        const uint32_t ph = i & 1;
+        if (!mbar_wait(&trace_bar[0], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(i, 5);
+        if (!mbar_wait(&trace_bar[1], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(i, 6);
+        if (!mbar_wait(&trace_bar[2], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(i, 7);
+        if (i + 2 >= iters) continue;
+        if (!mbar_wait(&trace_bar[3], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(i, 20);
+        if (!mbar_wait(&trace_bar[4], ph, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+        stamp(i, 21);
       }
     }
   } else if (warp >= 4 && warp < 12) {
@@ -1206,12 +1273,17 @@ void attn_fwd_launch(const AttnFwdDesc& d_in, cudaStream_t stream) {
                                            static_cast<long>(d.Lk) * kHD, 64, 128, 1);
   static bool attr = false;
   if (!attr) {
-    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          FwdSmem::BYTES));
+    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           FwdSmem::BYTES));
     attr = true;
   }
   const long grid = static_cast<long>(d.B) * d.H * d.q_tiles;
-  attn_fwd_kernel<<<grid, 384, FwdSmem::BYTES, stream>>>(tq, tk, tv, d);
+  if (d.trace != nullptr)
+    attn_fwd_kernel<true><<<grid, 384, FwdSmem::BYTES, stream>>>(tq, tk, tv, d);
+  else
+    attn_fwd_kernel<false><<<grid, 384, FwdSmem::BYTES, stream>>>(tq, tk, tv, d);
   AVGEN_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -1288,12 +1360,17 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
     }
     static bool attr = false;
     if (!attr) {
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_fused_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            FusedBwdSmem::BYTES));
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_fused_kernel<false>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, FusedBwdSmem::BYTES));
+      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_fused_kernel<true>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, FusedBwdSmem::BYTES));
       attr = true;
     }
     const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
-    attn_bwd_fused_kernel<<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
+    if (d.trace != nullptr)
+      attn_bwd_fused_kernel<true><<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
+    else
+      attn_bwd_fused_kernel<false><<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
     AVGEN_CUDA_CHECK(cudaGetLastError());
     dim3 cgrid((d.Lq + 63) / 64, d.B * d.H);
     attn_dq_convert_kernel<<<cgrid, 256, 0, stream>>>(d.dq_acc, ld, d.Lq, d.scale, d.dq);

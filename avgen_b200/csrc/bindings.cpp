@@ -484,7 +484,7 @@ long stat_row_stride(const at::Tensor& t, int B, int H, int Lq, const char* what
 }
 
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, const OptT& lse,
-              const OptT& kmask, double scale) {
+              const OptT& kmask, double scale, const OptT& trace) {
   c10::cuda::CUDAGuard guard(q.device());
   check_bf16(q, "q");
   check_bf16(k, "k");
@@ -527,6 +527,11 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
   }
   d.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   d.err = error_word(d.device);
+  if (has(trace)) {
+    TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda() && trace->numel() >= 64 * 24,
+                "attention fwd: trace must be an int64 device tensor of at least 1536 entries");
+    d.trace = reinterpret_cast<long long*>(trace->data_ptr<int64_t>());
+  }
   attn_fwd_launch(d, cur_stream());
 }
 
@@ -641,7 +646,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("sq_norm", &a::sq_norm);
   m.def("ema", &a::ema);
   m.def("attn_fwd", &a::attn_fwd, arg("q"), arg("k"), arg("v"), arg("out"), arg("lse") = none, arg("kmask") = none,
-        arg("scale") = 0.0);
+        arg("scale") = 0.0, arg("trace") = none);
   m.def("attn_bwd", &a::attn_bwd, arg("q"), arg("k"), arg("v"), arg("o"), arg("dout"), arg("lse"), arg("delta"),
         arg("dq"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0, arg("dq_acc") = none,
         arg("trace") = none);

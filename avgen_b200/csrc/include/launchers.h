@@ -206,6 +206,7 @@ struct AttnFwdDesc {
   float* lse = nullptr;  // [B, H, Lq] with row stride stat_ld
   long stat_ld = 0;      // floats between (b, h) rows of lse; a multiple of 4
   int* err = nullptr;
+  long long* trace = nullptr;  // diagnostics: SM clock stamps of CTA 0 (64 iterations x 24 slots)
 };
 void attn_fwd_launch(const AttnFwdDesc& d, cudaStream_t stream);
 

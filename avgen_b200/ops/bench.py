@@ -3,6 +3,7 @@
     python -m avgen_b200.ops.bench attention --L 16384 --H 20 [--bwd split]
     python -m avgen_b200.ops.bench gemm --m 16384 --n 7680 --k 2560
     python -m avgen_b200.ops.bench attention --L 4096 --H 37 --once   # one call each (for ncu -k/-c)
+    python -m avgen_b200.ops.bench trace --L 16384 --H 20 --pass bwd   # SM-clock timeline of CTA 0
 
 Times come from CUDA events on the launching stream after warm-up, with a
 synchronize on both sides; each line also reports the library equivalent
@@ -56,6 +57,45 @@ def bench_attention(length: int, heads: int, iters: int, once: bool) -> None:
           f"torch SDPA fwd {t_lf:.3f} ms, bwd {t_lb:.3f} ms")
 
 
+def trace_attention(length: int, heads: int, which: str) -> None:
+    """Print the SM-clock timeline of CTA 0 (one row per tile), from the kernels' ``trace`` slots."""
+    from avgen_b200.ops import kernels as K
+
+    q = torch.randn(1, heads, length, 128, device="cuda").bfloat16()
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    tr = torch.zeros(64 * 24, dtype=torch.int64, device="cuda")
+    if which == "fwd":
+        for _ in range(3):
+            K.attention_fwd(q, k, v, trace=tr)
+    else:
+        out, lse = K.attention_fwd(q, k, v)
+        dout = torch.randn_like(out)
+        for _ in range(3):
+            K.attention_bwd(q, k, v, out, dout, lse, trace=tr)
+    torch.cuda.synchronize()
+    t = tr.view(64, 24).cpu().tolist()
+    rows = range(4, 24)
+    if which == "fwd":
+        print("cycles relative to the MMA thread passing p_full[0] of tile j")
+        print("tile period | g0: S seen  loaded  max  rescaled  exp  arrive | PV0 done | g1: S seen  loaded  max  "
+              "rescaled  exp  arrive | MMA passes p_full[1] | PV1 done")
+        for j in rows:
+            b = t[j][0]
+            g0 = " ".join(f"{t[j][s] - b:6d}" for s in range(3, 9))
+            g1 = " ".join(f"{t[j][s] - b:6d}" for s in range(9, 15))
+            print(f"{j:4d} {b - t[j - 1][0]:6d} | {g0} | {t[j][16] - b:6d} | {g1} | {t[j][2] - b:6d} | {t[j][18] - b:6d}")
+    else:
+        print("cycles relative to the MMA thread passing p_full(i)")
+        print("iter period | dV dK dQ^T S(i+2) dP(i+2) complete | MMA passes dq_empty | softmax start, last arrive "
+              "(of i) | drain sees dQ^T, releases it")
+        for i in rows:
+            b = t[i][0]
+            ends = max(t[i][s] for s in range(8, 16))
+            mma = " ".join(f"{t[i][s] - b:6d}" for s in (5, 6, 7, 20, 21))
+            print(f"{i:4d} {b - t[i - 1][0]:6d} | {mma} | {t[i][1] - b:6d} | {t[i][2] - b:6d} {ends - b:6d} | "
+                  f"{t[i][4] - b:6d} {max(t[i][s] for s in range(16, 20)) - b:6d}")
+
+
 def bench_gemm(m: int, n: int, k: int, iters: int) -> None:
     from avgen_b200.ops import kernels as K
 
@@ -81,6 +121,10 @@ def main() -> None:
     a.add_argument("--H", type=int, default=20)
     a.add_argument("--bwd", choices=("fused", "split"), default=None)
     a.add_argument("--once", action="store_true")
+    t = sub.add_parser("trace")
+    t.add_argument("--L", type=int, default=16384)
+    t.add_argument("--H", type=int, default=20)
+    t.add_argument("--pass", dest="which", choices=("fwd", "bwd"), default="bwd")
     g = sub.add_parser("gemm")
     g.add_argument("--m", type=int, default=16384)
     g.add_argument("--n", type=int, default=7680)
@@ -95,6 +139,8 @@ def main() -> None:
         K._ATTN_BWD = args.bwd
     if args.op == "attention":
         bench_attention(args.L, args.H, args.iters, args.once)
+    elif args.op == "trace":
+        trace_attention(args.L, args.H, args.which)
     else:
         bench_gemm(args.m, args.n, args.k, args.iters)
     from avgen_b200.ops._ext import check_errors

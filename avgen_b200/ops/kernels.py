@@ -301,14 +301,20 @@ def attention_fwd(
     scale: float | None = None,
     out: torch.Tensor | None = None,
     want_lse: bool = True,
+    trace: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
-    """Flash attention forward. Returns ``(out [B, Lq, H, D], lse [B, H, Lq])``."""
+    """Flash attention forward. Returns ``(out [B, Lq, H, D], lse [B, H, Lq])``.
+
+    ``trace`` (int64, >= 1536 entries, diagnostics) receives SM clock stamps of
+    CTA 0 per key tile: the MMA thread's waits, each softmax group's phases and
+    the completion of its S and PV products (slot map in ``attention.cu``).
+    """
     b, h, lq, d = q.shape
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     if out is None:
         out = torch.empty((b, lq, h, d), device=q.device, dtype=_BF16)
     lse = row_stats(b, h, lq, q.device) if want_lse else None
-    load().attn_fwd(q, k, v, out, lse, kmask, scale)
+    load().attn_fwd(q, k, v, out, lse, kmask, scale, trace)
     _count()
     return out, lse
 

@@ -383,3 +383,26 @@ def test_norm_column_reductions_many_rows() -> None:
     ops.gate_bwd(dy, x, gate, dg, rows_per_batch=1)
     _close(dg, dy.float() * x.float(), rtol=1e-2, atol=1e-2)
     _errors_clear()
+
+
+def test_attention_trace_diagnostics_leave_results_unchanged() -> None:
+    """The ``trace`` diagnostics only add clock stamps: outputs match an untraced call bit for bit."""
+    ops = _ops()
+    torch.manual_seed(0)
+    q = torch.randn(1, 2, 512, 128, device=DEV).bfloat16()
+    k, v = torch.randn_like(q), torch.randn_like(q)
+    out, lse = ops.attention_fwd(q, k, v)
+    tr = torch.zeros(64 * 24, dtype=torch.int64, device=DEV)
+    out_t, lse_t = ops.attention_fwd(q, k, v, trace=tr)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out_t) and torch.equal(lse, lse_t)
+    assert int(tr.view(64, 24)[:4, 0].min()) > 0, "forward stamps missing"
+    dout = torch.randn_like(out)
+    ref = ops.attention_bwd(q, k, v, out, dout, lse)
+    tr.zero_()
+    got = ops.attention_bwd(q, k, v, out, dout, lse, trace=tr)
+    torch.cuda.synchronize()
+    for a, b in zip(ref, got):
+        _close(b, a, rtol=1e-3, atol=1e-3)
+    assert int(tr.view(64, 24)[:4, 0].min()) > 0, "backward stamps missing"
+    _errors_clear()

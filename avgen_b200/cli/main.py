@@ -10,7 +10,7 @@ import re
 import sys
 from collections.abc import Sequence
 
-from avgen_b200.cli import checkpoint, data, generate, info, plan, simulate, train
+from avgen_b200.cli import checkpoint, data, evaluate, generate, info, plan, simulate, train
 from avgen_b200.cli._common import EXIT_CONFIG, EXIT_ERROR, EXIT_INTERRUPT, EXIT_USAGE, fail, version
 
 __all__ = ["build_parser", "main"]
@@ -31,14 +31,8 @@ def build_parser() -> argparse.ArgumentParser:
     parser.add_argument("--version", action="store_true", help="print the version and exit")
     parser.add_argument("--traceback", action="store_true", help="show full tracebacks")
     sub = parser.add_subparsers(dest="command", metavar="COMMAND")
-    for module in (train, generate, simulate, plan, checkpoint, data, info):
+    for module in (train, generate, evaluate, simulate, plan, checkpoint, data, info):
         module.add_parser(sub)
-    try:
-        from avgen_b200.cli import evaluate
-
-        evaluate.add_parser(sub)
-    except ImportError:
-        pass
     return parser
 
 

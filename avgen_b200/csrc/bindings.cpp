@@ -415,6 +415,88 @@ void noise_interp(const at::Tensor& clean, const at::Tensor& t, int64_t seed, in
   noise_interp_launch(d, cur_stream());
 }
 
+// --------------------------------------------------------------------- sampling
+void guided_euler(const at::Tensor& cond, const OptT& uncond, const at::Tensor& x, const at::Tensor& sigma,
+                  const at::Tensor& sigma_next, double scale, at::Tensor& out) {
+  c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(cond, "cond");
+  check_cuda(x, "x");
+  check_f32(sigma, "sigma");
+  check_f32(sigma_next, "sigma_next");
+  TORCH_CHECK(cond.is_contiguous() && x.is_contiguous() && out.is_contiguous(), "guided_euler: contiguous tensors");
+  TORCH_CHECK(cond.numel() == x.numel() && out.numel() == x.numel(), "guided_euler: shape mismatch");
+  GuidedEulerDesc d;
+  d.device = x.device().index();
+  d.batch = static_cast<int>(x.size(0));
+  d.per_sample = x.numel() / std::max<int64_t>(1, x.size(0));
+  TORCH_CHECK(sigma.numel() == d.batch && sigma_next.numel() == d.batch, "guided_euler: sigma must be [batch]");
+  d.cond = cond.data_ptr();
+  d.vel_f32 = cond.scalar_type() == at::kFloat;
+  if (has(uncond)) {
+    TORCH_CHECK(uncond->is_contiguous() && uncond->numel() == x.numel() &&
+                uncond->scalar_type() == cond.scalar_type(), "guided_euler: uncond must match cond");
+    d.uncond = uncond->data_ptr();
+  }
+  d.x = x.data_ptr();
+  d.x_f32 = x.scalar_type() == at::kFloat;
+  d.out = out.data_ptr();
+  d.out_f32 = out.scalar_type() == at::kFloat;
+  d.sigma = sigma.data_ptr<float>();
+  d.sigma_next = sigma_next.data_ptr<float>();
+  d.scale = static_cast<float>(scale);
+  guided_euler_launch(d, cur_stream());
+}
+
+void sde_step(const at::Tensor& v, const at::Tensor& x, const at::Tensor& sigma, const at::Tensor& sigma_next,
+              const at::Tensor& g, double floor, at::Tensor& mean, at::Tensor& log_prob, const OptT& noise,
+              const OptT& prev, const OptT& mask, const OptT& sample) {
+  c10::cuda::CUDAGuard guard(x.device());
+  check_cuda(v, "v");
+  check_f32(x, "x");
+  check_f32(sigma, "sigma");
+  check_f32(sigma_next, "sigma_next");
+  check_f32(g, "g");
+  check_f32(mean, "mean");
+  check_f32(log_prob, "log_prob");
+  TORCH_CHECK(v.is_contiguous() && x.is_contiguous() && mean.is_contiguous(), "sde_step: contiguous tensors");
+  SDEStepDesc d;
+  d.device = x.device().index();
+  d.batch = static_cast<int>(x.size(0));
+  d.per_sample = x.numel() / std::max<int64_t>(1, x.size(0));
+  TORCH_CHECK(v.numel() == x.numel() && mean.numel() == x.numel(), "sde_step: shape mismatch");
+  TORCH_CHECK(sigma.numel() == d.batch && sigma_next.numel() == d.batch && g.numel() == d.batch &&
+              log_prob.numel() == d.batch, "sde_step: per-sample tensors must be [batch]");
+  TORCH_CHECK(has(noise) != has(prev), "sde_step: give exactly one of noise (rollout) or prev (update)");
+  d.v = v.data_ptr();
+  d.v_f32 = v.scalar_type() == at::kFloat;
+  d.x = x.data_ptr<float>();
+  d.sigma = sigma.data_ptr<float>();
+  d.sigma_next = sigma_next.data_ptr<float>();
+  d.g = g.data_ptr<float>();
+  d.floor = static_cast<float>(floor);
+  if (has(noise)) {
+    check_f32(*noise, "noise");
+    TORCH_CHECK(noise->is_contiguous() && noise->numel() == x.numel(), "sde_step: noise shape");
+    TORCH_CHECK(has(sample), "sde_step: rollout needs a sample output");
+    check_f32(*sample, "sample");
+    TORCH_CHECK(sample->is_contiguous() && sample->numel() == x.numel(), "sde_step: sample shape");
+    d.noise = noise->data_ptr<float>();
+    d.sample = sample->data_ptr<float>();
+  } else {
+    check_f32(*prev, "prev");
+    TORCH_CHECK(prev->is_contiguous() && prev->numel() == x.numel(), "sde_step: prev shape");
+    d.prev = prev->data_ptr<float>();
+  }
+  if (has(mask)) {
+    TORCH_CHECK(mask->scalar_type() == at::kBool && mask->is_contiguous() && mask->numel() == x.numel(),
+                "sde_step: mask must be a contiguous bool tensor shaped like x");
+    d.mask = mask->data_ptr<bool>();
+  }
+  d.mean = mean.data_ptr<float>();
+  d.log_prob = log_prob.data_ptr<float>();
+  sde_step_launch(d, cur_stream());
+}
+
 // --------------------------------------------------------------------- optimizer
 void adamw(at::Tensor& param, const at::Tensor& grad, at::Tensor& exp_avg, at::Tensor& exp_avg_sq, double lr,
            double beta1, double beta2, double eps, double weight_decay, int64_t step, const OptT& param_bf16,
@@ -640,6 +722,11 @@ PYBIND11_MODULE(_C, m) {
   m.def("flow_loss_bwd", &a::flow_loss_bwd);
   m.def("noise_interp", &a::noise_interp, arg("clean"), arg("t"), arg("seed"), arg("offset"), arg("row_base"),
         arg("rows_per_sample"), arg("global_rows_per_sample"), arg("noisy"), arg("target"), arg("noise") = none);
+  m.def("guided_euler", &a::guided_euler, arg("cond"), arg("uncond"), arg("x"), arg("sigma"), arg("sigma_next"),
+        arg("scale"), arg("out"));
+  m.def("sde_step", &a::sde_step, arg("v"), arg("x"), arg("sigma"), arg("sigma_next"), arg("g"), arg("floor"),
+        arg("mean"), arg("log_prob"), arg("noise") = none, arg("prev") = none, arg("mask") = none,
+        arg("sample") = none);
   m.def("adamw", &a::adamw, arg("param"), arg("grad"), arg("exp_avg"), arg("exp_avg_sq"), arg("lr"), arg("beta1"),
         arg("beta2"), arg("eps"), arg("weight_decay"), arg("step"), arg("param_bf16") = none,
         arg("grad_scale") = none, arg("skip") = none);

@@ -242,4 +242,45 @@ void sq_norm_launch(int device, const float* x, long n, float* out, cudaStream_t
 void ema_launch(int device, long n, const float* param, void* shadow, bool shadow_bf16, float decay,
                 cudaStream_t stream);
 
+// Guided Euler step over [batch, per_sample] latents: out = x + (sigma_next - sigma) *
+// (uncond + scale (cond - uncond)); uncond may be null (plain Euler).
+struct GuidedEulerDesc {
+  int device = 0;
+  int batch = 0;
+  long per_sample = 0;
+  const void* cond = nullptr;
+  const void* uncond = nullptr;
+  bool vel_f32 = true;
+  const void* x = nullptr;
+  bool x_f32 = true;
+  void* out = nullptr;
+  bool out_f32 = true;
+  const float* sigma = nullptr;       // [batch]
+  const float* sigma_next = nullptr;  // [batch]
+  float scale = 1.f;
+};
+void guided_euler_launch(const GuidedEulerDesc& d, cudaStream_t stream);
+
+// Flow-GRPO SDE transition over fp32 [batch, per_sample] states; log_prob [batch]
+// is accumulated into (zero it first).
+struct SDEStepDesc {
+  int device = 0;
+  int batch = 0;
+  long per_sample = 0;
+  const void* v = nullptr;
+  bool v_f32 = true;
+  const float* x = nullptr;
+  const float* sigma = nullptr;
+  const float* sigma_next = nullptr;
+  const float* g = nullptr;      // diffusion coefficient per sample
+  float floor = 1e-3f;
+  const float* noise = nullptr;  // rollout: standard normal draw
+  const float* prev = nullptr;   // update: stored next state
+  const bool* mask = nullptr;    // optional element validity
+  float* mean = nullptr;
+  float* sample = nullptr;       // rollout output
+  float* log_prob = nullptr;
+};
+void sde_step_launch(const SDEStepDesc& d, cudaStream_t stream);
+
 }  // namespace avgen

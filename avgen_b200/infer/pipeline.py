@@ -29,7 +29,7 @@ from avgen_b200.core.rng import RNGStreams
 from avgen_b200.core.tokens import TextContext, TokenStream
 from avgen_b200.infer.conditioning import StreamState, build_model_input, default_audio_patchifier
 from avgen_b200.infer.guidance import GuidanceConfig, apply_guidance
-from avgen_b200.infer.sampler import Sampler, SamplerConfig, build_sampler
+from avgen_b200.infer.sampler import EulerSampler, Sampler, SamplerConfig, build_sampler
 from avgen_b200.infer.schedule import ScheduleConfig, SigmaSchedule, build_sigma_schedule
 
 __all__ = ["GeneratedMedia", "GenerationConfig", "GenerationPipeline", "LatentCallback", "ProgressCallback"]
@@ -303,6 +303,8 @@ class GenerationPipeline:
                  audio_solver: Sampler | None, config: GenerationConfig,
                  rng: RNGStreams) -> tuple[StreamState, StreamState | None]:
         audio_lat = audio_state.latents if audio_state is not None else None
+        if audio_state is None and self._fusable_euler(solver, config, video_state):
+            return self._guided_euler(video_state, text, null_text, sigma, sigma_next, progress, config), None
 
         def velocity(v_lat: torch.Tensor, a_lat: torch.Tensor | None, at: float):  # noqa: ANN202
             a_st = audio_state.with_latents(a_lat) if audio_state is not None and a_lat is not None else None
@@ -317,6 +319,28 @@ class GenerationPipeline:
             next_audio = audio_state.with_latents(audio_solver.step(a_vel, audio_state.latents, sigma, sigma_next,
                                                                     generator=rng.sampler))
         return next_video, next_audio
+
+    def _fusable_euler(self, solver: Sampler, config: GenerationConfig, video_state: StreamState) -> bool:
+        """Plain Euler with plain CFG on a B200: the guidance combine and the
+        update run as one fused kernel over the batched forward's two halves."""
+        g = config.guidance
+        return (isinstance(solver, EulerSampler) and video_state.latents.is_cuda and self.batch_guidance
+                and g.is_enabled and g.rescale == 0.0 and not g.projection)
+
+    def _guided_euler(self, video_state: StreamState, text: TextContext, null_text: TextContext, sigma: float,
+                      sigma_next: float, progress: float, config: GenerationConfig) -> StreamState:
+        from avgen_b200.ops import kernels as K
+
+        inputs = build_model_input(video=video_state, sigma=sigma, text=text, patchifier=self.patchifier)
+        both = self._forward(_doubled(inputs, null_text))
+        b = inputs.batch_size
+        cond = unpatchify_grid(both.video[:b], inputs.video.layout)
+        uncond = unpatchify_grid(both.video[b:], inputs.video.layout)
+        lat = video_state.latents
+        s = torch.full((b,), sigma, device=lat.device, dtype=torch.float32)
+        sn = torch.full((b,), sigma_next, device=lat.device, dtype=torch.float32)
+        scale = config.guidance.modality_scale("text", progress)
+        return video_state.with_latents(K.guided_euler(cond, uncond, lat, s, sn, scale=scale))
 
     def _velocity(self, video_state: StreamState, audio_state: StreamState | None, text: TextContext,
                   null_text: TextContext, sigma: float, config: GenerationConfig,

@@ -461,3 +461,33 @@ def ema_(param: torch.Tensor, shadow: torch.Tensor, decay: float) -> None:
     """``shadow += (1 - decay) * (param - shadow)``."""
     load().ema(param, shadow, decay)
     _count()
+
+
+def guided_euler(cond: torch.Tensor, uncond: torch.Tensor | None, x: torch.Tensor, sigma: torch.Tensor,
+                 sigma_next: torch.Tensor, *, scale: float = 1.0, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """One Euler step with classifier-free guidance fused in:
+    ``x + (sigma_next - sigma) * (uncond + scale * (cond - uncond))`` per sample
+    (``uncond=None``: plain Euler). ``sigma``/``sigma_next`` are fp32 ``[batch]``."""
+    out = torch.empty(x.shape, device=x.device, dtype=out_dtype or x.dtype)
+    load().guided_euler(cond.contiguous(), None if uncond is None else uncond.contiguous(), x.contiguous(),
+                        sigma.to(_F32).contiguous(), sigma_next.to(_F32).contiguous(), float(scale), out)
+    _count()
+    return out
+
+
+def sde_step(v: torch.Tensor, x: torch.Tensor, sigma: torch.Tensor, sigma_next: torch.Tensor, g: torch.Tensor, *,
+             floor: float, noise: torch.Tensor | None = None, prev: torch.Tensor | None = None,
+             mask: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Flow-GRPO SDE transition: returns ``(sample, mean, log_prob)``. Rollout mode takes
+    a standard-normal ``noise``; update mode scores the stored ``prev`` instead."""
+    xf = x.to(_F32).contiguous()
+    mean = torch.empty_like(xf)
+    log_prob = torch.zeros(x.shape[0], device=x.device, dtype=_F32)
+    sample = torch.empty_like(xf) if prev is None else None
+    load().sde_step(v.contiguous(), xf, sigma.to(_F32).contiguous(), sigma_next.to(_F32).contiguous(),
+                    g.to(_F32).contiguous(), float(floor), mean, log_prob,
+                    None if noise is None else noise.to(_F32).contiguous(),
+                    None if prev is None else prev.to(_F32).contiguous(),
+                    None if mask is None else mask.to(torch.bool).contiguous(), sample)
+    _count()
+    return (sample if prev is None else prev), mean, log_prob

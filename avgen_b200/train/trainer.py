@@ -27,7 +27,7 @@ from avgen_b200.train.objective import Objective, ObjectiveOutput
 from avgen_b200.train.optimizer import FusedAdamW
 
 __all__ = ["Curriculum", "CurriculumStage", "MetricSink", "ResolutionBucket", "Trainer", "TrainerCallback",
-           "TrainerConfig", "train_step"]
+           "TrainerConfig", "optimizer_update", "train_step"]
 
 _LOG = logging.getLogger("avgen_b200.train")
 
@@ -168,6 +168,42 @@ def _neutralise_nonfinite(grads: Sequence[torch.Tensor], finite: torch.Tensor) -
             torch.where(finite, g, torch.zeros((), dtype=g.dtype, device=g.device), out=g)
 
 
+def optimizer_update(state: TrainState, *, max_grad_norm: float | None = None, pp_mesh: DeviceMesh | None = None,
+                     data_group: Any = None, finite: torch.Tensor | None = None,
+                     ) -> tuple[torch.Tensor, torch.Tensor]:
+    """The end of an optimizer step after ``backward``: clip by the global norm,
+    neutralise a non-finite step on device (no collective), optimizer, schedule
+    and EMA steps, ``state.step += 1``. Returns ``(grad_norm, finite)``.
+    Shared by :func:`train_step` and the RL trainers."""
+    opt = state.optimizer
+    dev = next((p.device for p in state.model.parameters()), torch.device("cpu"))
+    finite = torch.ones((), dtype=torch.bool, device=dev) if finite is None else finite
+    grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
+    if isinstance(opt, FusedAdamW):
+        opt.step(max_grad_norm=max_grad_norm)
+        grad_norm = opt.last_grad_norm.to(torch.float32).to(dev)
+        finite = finite & ~opt.last_nonfinite.to(dev)
+    else:
+        from avgen_b200.parallel.comm import clip_grad_norm
+
+        params = [p for p in state.model.parameters() if p.grad is not None]
+        _average_gradients(params, data_group)
+        if max_grad_norm is not None and params:
+            grad_norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh).to(torch.float32)
+        elif params:
+            grad_norm = torch.nn.utils.get_total_norm([p.grad for p in params], norm_type=2.0,
+                                                      error_if_nonfinite=False).to(torch.float32)
+        finite = finite & torch.isfinite(grad_norm)
+        _neutralise_nonfinite([p.grad for p in params], finite)
+        opt.step()
+    if state.schedule is not None:
+        state.schedule.step()
+    if state.ema is not None:
+        state.ema.update(state.model)
+    state.step += 1
+    return grad_norm, finite
+
+
 def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, patchifier: Patchifier,
                gradient_accumulation_steps: int = 1, microbatch_index: int = 0, max_grad_norm: float | None = None,
                cp_mesh: DeviceMesh | None = None, pp_mesh: DeviceMesh | None = None,
@@ -194,28 +230,8 @@ def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, pa
     grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
     finite = torch.isfinite(out.loss.detach())
     if last:
-        if isinstance(opt, FusedAdamW):
-            opt.step(max_grad_norm=max_grad_norm)
-            grad_norm = opt.last_grad_norm.to(torch.float32).to(dev)
-            finite = finite & ~opt.last_nonfinite.to(dev)
-        else:
-            from avgen_b200.parallel.comm import clip_grad_norm
-
-            params = [p for p in state.model.parameters() if p.grad is not None]
-            _average_gradients(params, data_group)
-            if max_grad_norm is not None and params:
-                grad_norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh).to(torch.float32)
-            elif params:
-                grad_norm = torch.nn.utils.get_total_norm([p.grad for p in params], norm_type=2.0,
-                                                          error_if_nonfinite=False).to(torch.float32)
-            finite = finite & torch.isfinite(grad_norm)
-            _neutralise_nonfinite([p.grad for p in params], finite)
-            opt.step()
-        if state.schedule is not None:
-            state.schedule.step()
-        if state.ema is not None:
-            state.ema.update(state.model)
-        state.step += 1
+        grad_norm, finite = optimizer_update(state, max_grad_norm=max_grad_norm, pp_mesh=pp_mesh,
+                                             data_group=data_group, finite=finite)
     state.samples_seen += batch.spec.batch_size * data_world
     state.tokens_seen += batch.spec.batch_size * batch.spec.sequence_length * data_world
     skipped = ~finite if last else torch.zeros((), dtype=torch.bool, device=dev)

@@ -94,3 +94,34 @@ def test_tiny_gpu_model_trains() -> None:
         losses.append(m.to_mapping())
     assert all(torch.isfinite(torch.tensor([l["loss"] for l in losses])))
     assert losses[-1]["grad_norm"] > 0
+
+
+def test_generation_fused_guided_euler_matches_unfused(monkeypatch: pytest.MonkeyPatch) -> None:
+    """The fused CFG + Euler kernel step reproduces guidance followed by the Euler update."""
+    from dataclasses import asdict
+
+    from avgen_b200.codecs import ReferenceTextEncoder, ReferenceVideoCodec
+    from avgen_b200.infer import GenerationPipeline, GuidanceConfig
+    from avgen_b200.models import build_model, preset
+    from avgen_b200.ops import kernels as K
+
+    torch.manual_seed(0)
+    cfg = {k: v for k, v in asdict(preset("tiny_gpu")).items() if k != "rope_scaling"}
+    codec = ReferenceVideoCodec(channels=1, spatial_compression=2)
+    cfg["in_channels"] = codec.latent_channels
+    model = build_model("video_dit", cfg).to("cuda")
+    model.init_weights()
+    with torch.no_grad():
+        for p in model.parameters():
+            p.add_(0.02 * torch.randn_like(p))
+    model.eval()
+    pipe = GenerationPipeline(model, video_codec=codec, text_encoder=ReferenceTextEncoder(width=cfg["text_width"]),
+                              device="cuda")
+    kw = dict(steps=3, guidance=GuidanceConfig(scale=4.0), height=32, width=64, num_frames=4, seed=3,
+              return_latents=True)
+    n0 = K.launch_count()
+    fused = pipe(["a cat"], **kw)
+    assert K.launch_count() > n0
+    monkeypatch.setattr(GenerationPipeline, "_fusable_euler", lambda *a, **k: False)
+    plain = pipe(["a cat"], **kw)
+    assert _rel(fused.latents, plain.latents) < 1e-3

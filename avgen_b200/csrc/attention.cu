@@ -85,6 +85,9 @@ __global__ void __launch_bounds__(384, 1)
   const int hk = h / (p.H / p.Hk);
   const int q0 = qt * 256;
   const int nkv = (p.Lk + kTile - 1) / kTile;
+  const bool ring = p.ring_world > 1;
+  const int ring_tiles = ring ? p.ring_len / kTile : nkv;  // key tiles per rank's chunk
+  const int ring_start = ring ? p.ring_rank * ring_tiles : 0;
   // diagnostics: SM clock stamps of CTA 0, 24 per key tile, first 64 tiles. Slots: 0/1/2 MMA
   // thread passes p_full[0] / kv_full(j+1) / p_full[1]; 3-8 softmax group 0 (S seen, loaded,
   // max, rescaled, exponentials, arrive), 9-14 the same for group 1; 15/16 S/PV of group 0
@@ -128,11 +131,21 @@ __global__ void __launch_bounds__(384, 1)
       for (int j = 0; j < nkv; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        int row = j * kTile, slab = b * p.Hk + hk;
+        if (ring) {
+          const int g = (j + ring_start) % nkv;  // global key tile
+          const int r = g / ring_tiles;
+          row = (g - r * ring_tiles) * kTile;
+          slab += r * p.B * p.Hk;
+          if (r != p.ring_rank && row == 0 &&
+              !flag_wait_geq(p.ring_flags + r, p.ring_epoch, abort_flag, p.err, kErrTimeoutPeer))
+            break;
+        }
         mbar_arrive_expect_tx(&kv_full[s], 65536);
         uint8_t* st = smem + FwdSmem::KV + s * 65536;
         for (int c = 0; c < 2; ++c) {
-          tma_load_3d(st + c * 16384, &tmK, &kv_full[s], c * 64, j * kTile, b * p.Hk + hk);
-          tma_load_3d(st + 32768 + c * 16384, &tmV, &kv_full[s], c * 64, j * kTile, b * p.Hk + hk);
+          tma_load_3d(st + c * 16384, &tmK, &kv_full[s], c * 64, row, slab);
+          tma_load_3d(st + 32768 + c * 16384, &tmV, &kv_full[s], c * 64, row, slab);
         }
       }
     }
@@ -248,7 +261,7 @@ __global__ void __launch_bounds__(384, 1)
       }
       tmem_wait_ld();
       if (tr) stamp(j, ts + 1);
-      const int kbase = j * kTile;
+      const int kbase = (ring ? (j + ring_start) % nkv : j) * kTile;
       if (kbase + kTile > p.Lk || p.kmask != nullptr) {
         uint32_t words[4];
 #pragma unroll
@@ -451,6 +464,12 @@ __global__ void __launch_bounds__(384, 1)
   const int hk = bhk % p.Hk;
   const int b = bhk / p.Hk;
   const int k0 = kt * kTile;
+  // ring layout [world][B * Hk][ring_len][D]: this tile's chunk, row within it and slab
+  const int ring_tiles = p.ring_world > 1 ? p.ring_len / kTile : p.k_tiles;
+  const int chunk = kt / ring_tiles;
+  const int kv_row = (kt - chunk * ring_tiles) * kTile;
+  const int kv_slab = chunk * p.B * p.Hk + b * p.Hk + hk;
+  const long kv_len = p.ring_world > 1 ? p.ring_len : p.Lk;
   const int group = p.H / p.Hk;
   const int nq = (p.Lq + kQT - 1) / kQT;
   const int iters = nq * group;
@@ -615,7 +634,7 @@ __global__ void __launch_bounds__(384, 1)
     }
     if (ok && mbar_wait(acc_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
       tc_fence_after();
-      const long off = ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+      const long off = (static_cast<long>(kv_slab) * kv_len + kv_row + row) * kHD;
       // each half stores 64 of the 128 columns of its key row
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
@@ -934,6 +953,12 @@ __global__ void __launch_bounds__(512, 1)
   const int hk = bhk % p.Hk;
   const int b = bhk / p.Hk;
   const int k0 = kt * kTile;
+  // ring layout [world][B * Hk][ring_len][D]: this tile's chunk, row within it and slab
+  const int ring_tiles = p.ring_world > 1 ? p.ring_len / kTile : p.k_tiles;
+  const int chunk = kt / ring_tiles;
+  const int kv_row = (kt - chunk * ring_tiles) * kTile;
+  const int kv_slab = chunk * p.B * p.Hk + b * p.Hk + hk;
+  const long kv_len = p.ring_world > 1 ? p.ring_len : p.Lk;
   const int group = p.H / p.Hk;
   const int nq = (p.Lq + kQT - 1) / kQT;
   const int iters = nq * group;
@@ -982,8 +1007,8 @@ __global__ void __launch_bounds__(512, 1)
       prefetch_tmap(&tmdO);
       mbar_arrive_expect_tx(kv_full, 65536);
       for (int c = 0; c < 2; ++c) {
-        tma_load_3d(smem + S::K + c * 16384, &tmK, kv_full, c * 64, k0, b * p.Hk + hk);
-        tma_load_3d(smem + S::V + c * 16384, &tmV, kv_full, c * 64, k0, b * p.Hk + hk);
+        tma_load_3d(smem + S::K + c * 16384, &tmK, kv_full, c * 64, kv_row, kv_slab);
+        tma_load_3d(smem + S::V + c * 16384, &tmV, kv_full, c * 64, kv_row, kv_slab);
       }
       for (int i = 0; i < iters; ++i) {
         const int s = i % S::STAGES;
@@ -1167,7 +1192,7 @@ __global__ void __launch_bounds__(512, 1)
     }
     if (ok && mbar_wait(acc_done, 0, abort_flag, p.err, kErrTimeoutSoftmax)) {
       tc_fence_after();
-      const long off = ((static_cast<long>(b) * p.Hk + hk) * p.Lk + key) * kHD;
+      const long off = (static_cast<long>(kv_slab) * kv_len + kv_row + row) * kHD;
 #pragma unroll 1
       for (int c = 2 * half; c < 2 * half + 2; ++c) {
         uint32_t a[32], v[32];
@@ -1267,10 +1292,18 @@ void attn_fwd_launch(const AttnFwdDesc& d_in, cudaStream_t stream) {
   // Q, K, V head-major [B*H, L, D] with rows of D elements.
   const CUtensorMap tq = make_tmap_3d_bf16(d.q, kHD, d.Lq, static_cast<long>(d.B) * d.H, kHD,
                                            static_cast<long>(d.Lq) * kHD, 64, 128, 1);
-  const CUtensorMap tk = make_tmap_3d_bf16(d.k, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
-                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
-  const CUtensorMap tv = make_tmap_3d_bf16(d.v, kHD, d.Lk, static_cast<long>(d.B) * d.Hk, kHD,
-                                           static_cast<long>(d.Lk) * kHD, 64, 128, 1);
+  const bool ring = d.ring_world > 1;
+  if (ring) {
+    AVGEN_CHECK(d.ring_len % kTile == 0 && d.ring_len > 0 && d.Lk == d.ring_world * d.ring_len,
+                "attention ring: keys per rank must be a positive multiple of 128 and Lk = world * that");
+    AVGEN_CHECK(d.ring_rank >= 0 && d.ring_rank < d.ring_world && d.ring_flags != nullptr,
+                "attention ring: bad rank or missing flags");
+  }
+  // ring: [world * B * Hk, ring_len, D]; else [B * Hk, Lk, D]
+  const long kv_len = ring ? d.ring_len : d.Lk;
+  const long kv_slabs = static_cast<long>(d.B) * d.Hk * (ring ? d.ring_world : 1);
+  const CUtensorMap tk = make_tmap_3d_bf16(d.k, kHD, kv_len, kv_slabs, kHD, kv_len * kHD, 64, 128, 1);
+  const CUtensorMap tv = make_tmap_3d_bf16(d.v, kHD, kv_len, kv_slabs, kHD, kv_len * kHD, 64, 128, 1);
   static bool attr = false;
   if (!attr) {
     AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -1296,6 +1329,7 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
                   d.o_sb == static_cast<long>(d.Lq) * d.H * kHD,
               "attention bwd: O / dO must be dense [B, Lq, H, 128]");
   AVGEN_CHECK(d.stat_ld >= d.Lq && d.stat_ld % 4 == 0, "attention bwd: lse/delta row stride must be >= Lq and a multiple of 4");
+  AVGEN_CHECK(d.ring_world <= 1 || d.dq_acc != nullptr, "attention bwd: the ring layout needs the fused kernel");
   // delta = rowsum(dO * O)
   {
     const long rows = static_cast<long>(d.B) * d.H * d.Lq;
@@ -1340,9 +1374,15 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
     const long ld = (d.Lq + 3) / 4 * 4;  // 16-byte rows for the TMA reduce
     AVGEN_CUDA_CHECK(cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * ld * kHD * d.B * d.H, stream));
     d.k_tiles = (d.Lk + kTile - 1) / kTile;
+    const bool ring = d.ring_world > 1;
+    if (ring)
+      AVGEN_CHECK(d.ring_len % kTile == 0 && d.ring_len > 0 && d.Lk == d.ring_world * d.ring_len,
+                  "attention bwd ring: keys per rank must be a positive multiple of 128 and Lk = world * that");
     const CUtensorMap tq = head_major(d.q, d.H, d.Lq, kQT);
-    const CUtensorMap tk = head_major(d.k, d.Hk, d.Lk, kTile);
-    const CUtensorMap tv = head_major(d.v, d.Hk, d.Lk, kTile);
+    const CUtensorMap tk = ring ? head_major(d.k, d.Hk * d.ring_world, d.ring_len, kTile)
+                                : head_major(d.k, d.Hk, d.Lk, kTile);
+    const CUtensorMap tv = ring ? head_major(d.v, d.Hk * d.ring_world, d.ring_len, kTile)
+                                : head_major(d.v, d.Hk, d.Lk, kTile);
     const CUtensorMap tdo = dout_map(kQT);
     const CUtensorMap tl = f32_rows(d.lse, kQT);
     const CUtensorMap tdl = f32_rows(d.delta, kQT);

@@ -565,25 +565,41 @@ long stat_row_stride(const at::Tensor& t, int B, int H, int Lq, const char* what
   return t.stride(1);
 }
 
+// k, v: [B, Hk, Lk, D], or the context-parallel ring layout [world, B, Hk, L, D]
+// (keys of rank r in slab r; Lk = world * L) together with ring_flags.
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, const OptT& lse,
-              const OptT& kmask, double scale, const OptT& trace) {
+              const OptT& kmask, double scale, const OptT& trace, int64_t ring_rank, const OptT& ring_flags,
+              int64_t ring_epoch) {
   c10::cuda::CUDAGuard guard(q.device());
   check_bf16(q, "q");
   check_bf16(k, "k");
   check_bf16(v, "v");
   check_bf16(out, "out");
-  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention: q, k, v must be [B, H, L, D]");
+  const bool ring = k.dim() == 5;
+  TORCH_CHECK(q.dim() == 4 && (k.dim() == 4 || ring) && v.dim() == k.dim(),
+              "attention: q must be [B, H, L, D]; k, v [B, Hk, L, D] or [world, B, Hk, L, D]");
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "attention: dense q, k, v");
   TORCH_CHECK(k.sizes() == v.sizes(), "attention: k and v shapes differ");
+  const int o5 = ring ? 1 : 0;
   AttnFwdDesc d;
   d.device = q.device().index();
   d.B = static_cast<int>(q.size(0));
   d.H = static_cast<int>(q.size(1));
   d.Lq = static_cast<int>(q.size(2));
   d.D = static_cast<int>(q.size(3));
-  d.Hk = static_cast<int>(k.size(1));
-  d.Lk = static_cast<int>(k.size(2));
-  TORCH_CHECK(k.size(0) == d.B && k.size(3) == d.D, "attention: k batch/dim mismatch");
+  d.Hk = static_cast<int>(k.size(1 + o5));
+  d.Lk = static_cast<int>(k.size(2 + o5) * (ring ? k.size(0) : 1));
+  TORCH_CHECK(k.size(o5) == d.B && k.size(3 + o5) == d.D, "attention: k batch/dim mismatch");
+  if (ring) {
+    TORCH_CHECK(has(ring_flags) && ring_flags->scalar_type() == at::kInt && ring_flags->is_cuda() &&
+                    ring_flags->numel() >= k.size(0),
+                "attention ring: ring_flags must be an int32 device tensor with one word per rank");
+    d.ring_world = static_cast<int>(k.size(0));
+    d.ring_rank = static_cast<int>(ring_rank);
+    d.ring_len = static_cast<int>(k.size(3));
+    d.ring_flags = reinterpret_cast<const unsigned*>(ring_flags->data_ptr<int>());
+    d.ring_epoch = static_cast<unsigned>(ring_epoch);
+  }
   // out: token-major [B, Lq, H, D] (any strides with a contiguous last dim)
   TORCH_CHECK(out.dim() == 4 && out.size(0) == d.B && out.size(1) == d.Lq && out.size(2) == d.H &&
                   out.size(3) == d.D && out.stride(3) == 1,
@@ -631,8 +647,14 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   d.H = static_cast<int>(q.size(1));
   d.Lq = static_cast<int>(q.size(2));
   d.D = static_cast<int>(q.size(3));
-  d.Hk = static_cast<int>(k.size(1));
-  d.Lk = static_cast<int>(k.size(2));
+  const bool ring = k.dim() == 5;  // [world, B, Hk, L, D] (dk, dv likewise)
+  const int o5 = ring ? 1 : 0;
+  d.Hk = static_cast<int>(k.size(1 + o5));
+  d.Lk = static_cast<int>(k.size(2 + o5) * (ring ? k.size(0) : 1));
+  if (ring) {
+    d.ring_world = static_cast<int>(k.size(0));
+    d.ring_len = static_cast<int>(k.size(3));
+  }
   TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(), "attention bwd: dense q, k, v");
   TORCH_CHECK(o.is_contiguous() && dout.is_contiguous() && o.dim() == 4 && o.size(1) == d.Lq && o.size(2) == d.H,
               "attention bwd: o / dout must be dense [B, Lq, H, D]");
@@ -677,6 +699,34 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   d.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   d.err = error_word(d.device);
   attn_bwd_launch(d, cur_stream());
+}
+
+// --------------------------------------------------------------------- peer memory
+int64_t p2p_alloc_py(int64_t bytes, int64_t device) {
+  return reinterpret_cast<int64_t>(p2p_alloc(static_cast<size_t>(bytes), static_cast<int>(device)));
+}
+void p2p_free_py(int64_t ptr) { p2p_free(reinterpret_cast<void*>(ptr)); }
+py::bytes p2p_export_py(int64_t ptr) {
+  char h[64];
+  p2p_export(reinterpret_cast<void*>(ptr), h);
+  return py::bytes(h, 64);
+}
+int64_t p2p_open_py(const py::bytes& handle, int64_t device) {
+  const std::string h = handle;
+  TORCH_CHECK(h.size() == 64, "p2p_open: a CUDA IPC handle is 64 bytes");
+  return reinterpret_cast<int64_t>(p2p_open(h.data(), static_cast<int>(device)));
+}
+void p2p_close_py(int64_t ptr) { p2p_close(reinterpret_cast<void*>(ptr)); }
+// A tensor viewing device memory this library manages (no ownership, no deleter).
+at::Tensor tensor_at(int64_t ptr, const std::vector<int64_t>& sizes, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, static_cast<int>(device));
+  return at::from_blob(reinterpret_cast<void*>(ptr), sizes, opts);
+}
+void stream_write_py(int64_t flag, int64_t value) {
+  stream_write(cur_stream(), reinterpret_cast<void*>(flag), static_cast<unsigned>(value));
+}
+void p2p_copy_py(int64_t dst, int64_t src, int64_t bytes) {
+  p2p_copy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), static_cast<size_t>(bytes), cur_stream());
 }
 
 int64_t read_error(int64_t device) {
@@ -733,7 +783,16 @@ PYBIND11_MODULE(_C, m) {
   m.def("sq_norm", &a::sq_norm);
   m.def("ema", &a::ema);
   m.def("attn_fwd", &a::attn_fwd, arg("q"), arg("k"), arg("v"), arg("out"), arg("lse") = none, arg("kmask") = none,
-        arg("scale") = 0.0, arg("trace") = none);
+        arg("scale") = 0.0, arg("trace") = none, arg("ring_rank") = 0, arg("ring_flags") = none,
+        arg("ring_epoch") = 0);
+  m.def("p2p_alloc", &a::p2p_alloc_py, arg("bytes"), arg("device"));
+  m.def("p2p_free", &a::p2p_free_py);
+  m.def("p2p_export", &a::p2p_export_py);
+  m.def("p2p_open", &a::p2p_open_py, arg("handle"), arg("device"));
+  m.def("p2p_close", &a::p2p_close_py);
+  m.def("tensor_at", &a::tensor_at, arg("ptr"), arg("sizes"), arg("dtype"), arg("device"));
+  m.def("stream_write", &a::stream_write_py, arg("flag"), arg("value"));
+  m.def("p2p_copy", &a::p2p_copy_py, arg("dst"), arg("src"), arg("bytes"));
   m.def("attn_bwd", &a::attn_bwd, arg("q"), arg("k"), arg("v"), arg("o"), arg("dout"), arg("lse"), arg("delta"),
         arg("dq"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0, arg("dq_acc") = none,
         arg("trace") = none);

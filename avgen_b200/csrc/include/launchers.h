@@ -207,6 +207,15 @@ struct AttnFwdDesc {
   long stat_ld = 0;      // floats between (b, h) rows of lse; a multiple of 4
   int* err = nullptr;
   long long* trace = nullptr;  // diagnostics: SM clock stamps of CTA 0 (64 iterations x 24 slots)
+  // Context-parallel ring (ring_world > 1): k and v are [ring_world][B * Hk][ring_len][D]
+  // with Lk = ring_world * ring_len (ring_len a multiple of 128). Each CTA visits key
+  // tiles starting at this rank's own chunk; the first tile of chunk r != ring_rank is
+  // loaded only after ring_flags[r] has reached ring_epoch (bounded wait).
+  int ring_world = 0;
+  int ring_rank = 0;
+  int ring_len = 0;
+  const unsigned* ring_flags = nullptr;
+  unsigned ring_epoch = 0;
 };
 void attn_fwd_launch(const AttnFwdDesc& d, cudaStream_t stream);
 
@@ -232,6 +241,11 @@ struct AttnBwdDesc {
   __nv_bfloat16* dk = nullptr; // [B, Hk, Lk, D]
   __nv_bfloat16* dv = nullptr;
   float* dq_acc = nullptr;     // optional fp32 scratch of B*H*128*ld floats, ld = Lq rounded up to 4: selects the fused one-pass kernel
+  // Context-parallel ring (ring_world > 1, fused kernel only): k, v, dk and dv are
+  // [ring_world][B * Hk][ring_len][D] with Lk = ring_world * ring_len; dk/dv hold this
+  // rank's partial gradients for every rank's keys, chunk r contiguous.
+  int ring_world = 0;
+  int ring_len = 0;
   long long* trace = nullptr;  // optional int64 [64 * 24]: per-warp SM clock stamps of CTA 0 (diagnostics)
   int* err = nullptr;
 };
@@ -282,5 +296,14 @@ struct SDEStepDesc {
   float* log_prob = nullptr;
 };
 void sde_step_launch(const SDEStepDesc& d, cudaStream_t stream);
+
+// Peer-memory runtime (p2p.cu).
+void* p2p_alloc(size_t bytes, int device);
+void p2p_free(void* ptr);
+void p2p_export(void* ptr, char* handle64);
+void* p2p_open(const char* handle64, int device);
+void p2p_close(void* ptr);
+void stream_write(cudaStream_t stream, void* flag, unsigned value);
+void p2p_copy(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 
 }  // namespace avgen

@@ -123,6 +123,31 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Bounded wait until a 32-bit flag in global memory, written by another agent (a
+// copy engine's stream write, a peer GPU's store over NVLink), reaches `target`
+// (wrapping compare, so epochs may overflow). Acquire at system scope, then a
+// proxy fence so TMA loads issued afterwards see the data the flag publishes.
+__device__ __forceinline__ bool flag_wait_geq(const unsigned* flag, unsigned target, volatile int* abort_flag,
+                                              int* err, int code) {
+  auto load = [flag]() {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    return v;
+  };
+  const uint64_t t0 = globaltimer();
+  while (static_cast<int>(load() - target) < 0) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > kWaitTimeoutNs) {
+      *abort_flag = 1;
+      record_error(err, code);
+      return false;
+    }
+    __nanosleep(128);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 // ---------------------------------------------------------------- TMA (local, no multicast)
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {

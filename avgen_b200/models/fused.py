@@ -167,10 +167,13 @@ def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     qkv = K.gemm(n1, pw["qkv"])
     qw = _norm_weight(att.q_norm) if spec.qk_norm else None
     kw = _norm_weight(att.k_norm) if spec.qk_norm else None
-    q, k, v = K.qkv_rope(qkv, batch=b, length=length, heads=h, kv_heads=hk, head_dim=d, q_weight=qw, k_weight=kw,
-                         coords=coords, freq=freq, axis=axis, eps=eps)
-    scale = 1.0 / math.sqrt(d)
     impl = _attn_impl(spec)
+    kv_out = getattr(impl, "kv_out", None) if save else None  # ring CP: write K/V into the shared buffer
+    bufs = kv_out(b, hk, length, d, xb.device) if kv_out is not None else None
+    q, k, v = K.qkv_rope(qkv, batch=b, length=length, heads=h, kv_heads=hk, head_dim=d, q_weight=qw, k_weight=kw,
+                         coords=coords, freq=freq, axis=axis, eps=eps, k_out=bufs[0] if bufs else None,
+                         v_out=bufs[1] if bufs else None)
+    scale = 1.0 / math.sqrt(d)
     if save:
         o, lse, attn_state = impl.forward(q, k, v, kmask, scale)
     else:

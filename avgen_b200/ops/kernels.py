@@ -227,12 +227,21 @@ def qkv_rope(
     freq: torch.Tensor | None,
     axis: torch.Tensor | None,
     eps: float = 1e-6,
+    k_out: torch.Tensor | None = None,
+    v_out: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor | None, torch.Tensor | None, torch.Tensor | None]:
-    """QK-RMSNorm + RoPE + relayout of ``qkv[B*L, (H + 2Hk) * D]`` into head-major q, k, v."""
+    """QK-RMSNorm + RoPE + relayout of ``qkv[B*L, (H + 2Hk) * D]`` into head-major q, k, v.
+
+    ``k_out``/``v_out`` (dense ``[B, Hk, L, D]`` bf16) receive k and v in place,
+    e.g. this rank's slab of a context-parallel ring buffer."""
     dev = qkv.device
     q = torch.empty((batch, heads, length, head_dim), device=dev, dtype=_BF16) if heads else None
-    k = torch.empty((batch, kv_heads, length, head_dim), device=dev, dtype=_BF16) if kv_heads else None
-    v = torch.empty_like(k) if kv_heads else None
+    shape = (batch, kv_heads, length, head_dim)
+    for t in (k_out, v_out):
+        if t is not None and (tuple(t.shape) != shape or t.dtype != _BF16 or not t.is_contiguous()):
+            raise ValueError(f"k_out/v_out must be dense bf16 {shape}")
+    k = (k_out if k_out is not None else torch.empty(shape, device=dev, dtype=_BF16)) if kv_heads else None
+    v = (v_out if v_out is not None else torch.empty(shape, device=dev, dtype=_BF16)) if kv_heads else None
     load().qkv_rope_fwd(
         qkv, batch, length, heads, kv_heads, head_dim, eps, q_weight, k_weight, coords, freq, axis, q, k, v
     )
@@ -302,19 +311,27 @@ def attention_fwd(
     out: torch.Tensor | None = None,
     want_lse: bool = True,
     trace: torch.Tensor | None = None,
+    ring_rank: int = 0,
+    ring_flags: torch.Tensor | None = None,
+    ring_epoch: int = 0,
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
     """Flash attention forward. Returns ``(out [B, Lq, H, D], lse [B, H, Lq])``.
 
     ``trace`` (int64, >= 1536 entries, diagnostics) receives SM clock stamps of
     CTA 0 per key tile: the MMA thread's waits, each softmax group's phases and
     the completion of its S and PV products (slot map in ``attention.cu``).
+
+    Context-parallel ring: ``k``/``v`` given as ``[world, B, Hk, L, D]`` (rank r's
+    keys in slab r, ``L`` a multiple of 128). Every CTA starts at slab
+    ``ring_rank`` and reads slab r only after ``ring_flags[r]`` (int32, written
+    by a copy stream or a peer) has reached ``ring_epoch``.
     """
     b, h, lq, d = q.shape
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     if out is None:
         out = torch.empty((b, lq, h, d), device=q.device, dtype=_BF16)
     lse = row_stats(b, h, lq, q.device) if want_lse else None
-    load().attn_fwd(q, k, v, out, lse, kmask, scale, trace)
+    load().attn_fwd(q, k, v, out, lse, kmask, scale, trace, ring_rank, ring_flags, ring_epoch & 0xFFFFFFFF)
     _count()
     return out, lse
 
@@ -333,6 +350,9 @@ def attention_bwd(
 ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
     """Flash attention backward. Returns ``(dq, dk, dv)`` (bf16, shapes of q, k, v).
 
+    With ``k``/``v`` in the ring layout ``[world, B, Hk, L, D]``, ``dk``/``dv``
+    come back in it too: slab r holds this rank's partial gradients for rank r's keys.
+
     ``trace`` (int64, >= 1536 entries, diagnostics) receives per-role SM clock
     stamps of the first CTA of the one-pass kernel.
 
@@ -348,7 +368,7 @@ def attention_bwd(
     dk = torch.empty_like(k)
     dv = torch.empty_like(v)
     acc = None
-    if _ATTN_BWD != "split":
+    if _ATTN_BWD != "split" or k.dim() == 5:  # the ring layout [world, B, Hk, L, D] needs the one-pass kernel
         acc = torch.empty(q.shape[0] * q.shape[1] * d * (-(-q.shape[2] // 4) * 4), device=q.device, dtype=_F32)
     load().attn_bwd(q, k, v, o, dout, lse, delta, dq, dk, dv, kmask, scale, acc, trace)
     _count(4 if acc is not None else 3)

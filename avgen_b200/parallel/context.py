@@ -20,6 +20,7 @@ from __future__ import annotations
 from collections.abc import Iterator, Sequence
 from contextlib import contextmanager, nullcontext
 from dataclasses import replace
+from typing import Any
 
 import torch
 import torch.distributed as dist
@@ -27,7 +28,7 @@ from torch.distributed.device_mesh import DeviceMesh
 
 from avgen_b200.core.tokens import TokenStream
 
-__all__ = ["ContextParallelAttention", "context_parallel_region", "cp_attention", "gather_stream", "gather_tokens",
+__all__ = ["ContextParallelAttention", "RingAttention", "context_parallel_region", "cp_attention", "gather_stream", "gather_tokens",
            "maybe_context_parallel", "pad_to_multiple", "shard_bounds", "shard_stream", "sharded_length"]
 
 
@@ -196,6 +197,130 @@ class ContextParallelAttention:
         return dq, scatter(dkf), scatter(dvf)
 
 
+class RingAttention:
+    """Fused context-parallel self-attention over NVLink peer memory, for one DiT block.
+
+    Every rank keeps, per block, a persistent symmetric buffer holding K and V
+    of the whole sequence in the ring layout ``[world, B, Hk, L_local, D]``
+    (slab r = rank r's keys), mapped into every peer with CUDA IPC. Forward:
+
+    1. the block's QK-norm + RoPE kernel writes this rank's K/V straight into
+       its own slab (:meth:`kv_out`);
+    2. a one-word all-reduce over the CP group marks every rank's slab as
+       written (the only synchronisation; the streams never wait on flags);
+    3. a copy stream pulls each peer's slab over NVLink with the copy engines,
+       nearest-next rank first, and after each slab writes ``arrived[r]`` with a
+       stream memory operation (GPU front end, no SM);
+    4. meanwhile the tcgen05 flash kernel runs the local queries against the
+       local slab first and gates each remote slab on ``arrived[r]`` with a
+       bounded wait, so the transfer of slab r overlaps the softmax/MMA work on
+       the slabs before it.
+
+    Backward runs the one-pass flash backward on the same buffer; the kernel
+    writes this rank's partial dK/dV for every slab in the ring layout, and the
+    slabs are reduce-scattered to their owners. That reduce-scatter also orders
+    the next step's overwrite of a slab after every peer's copy of it.
+    """
+
+    def __init__(self, mesh: DeviceMesh, index: int) -> None:
+        self.mesh = mesh
+        self.group = mesh.get_group()
+        self.world = mesh.size()
+        self.rank = mesh.get_local_rank()
+        self.index = index
+        self.epoch = 0
+        self.kv: Any = None      # SymmetricBuffer: K then V, ring layout
+        self.flags: torch.Tensor | None = None  # int32 arrived[world], written by this rank's copy stream
+        self.shape: tuple[int, ...] | None = None
+        self._token: torch.Tensor | None = None
+        self._copy_stream: torch.cuda.Stream | None = None
+        self._nccl = ContextParallelAttention(mesh)  # shapes the ring kernels do not take
+
+    @staticmethod
+    def supported(k_shape: tuple[int, ...]) -> bool:
+        return k_shape[2] % 128 == 0 and k_shape[3] == 128
+
+    def _ensure(self, b: int, hk: int, length: int, d: int, device: torch.device) -> None:
+        from avgen_b200.parallel.symmetric import SymmetricBuffer
+
+        shape = (self.world, b, hk, length, d)
+        if self.shape == shape:
+            return
+        if self.kv is not None:  # shape changed: every rank reallocates at the same call
+            torch.cuda.synchronize(device)
+            dist.barrier(group=self.group, device_ids=[device.index])
+            self.kv.close()
+        self.kv = SymmetricBuffer(2 * self.world * b * hk * length * d * 2, self.group, device)
+        self.flags = torch.zeros(self.world, dtype=torch.int32, device=device)
+        self._token = torch.zeros(1, dtype=torch.float32, device=device)
+        self._copy_stream = torch.cuda.Stream(device=device)
+        self.shape = shape
+        self.epoch = 0
+
+    def _slabs(self, rank: int) -> tuple[torch.Tensor, torch.Tensor]:
+        assert self.shape is not None
+        half = self.kv.nbytes // 2
+        return (self.kv.view(rank, 0, self.shape, torch.bfloat16), self.kv.view(rank, half, self.shape, torch.bfloat16))
+
+    def kv_out(self, b: int, hk: int, length: int, d: int, device: torch.device,
+               ) -> tuple[torch.Tensor, torch.Tensor] | None:
+        """This rank's slabs, for the QK-norm + RoPE kernel to write K and V into."""
+        if not self.supported((b, hk, length, d)):
+            return None
+        self._ensure(b, hk, length, d, device)
+        k_all, v_all = self._slabs(self.rank)
+        return k_all[self.rank], v_all[self.rank]
+
+    def forward(self, q, k, v, kmask, scale):  # noqa: ANN001, ANN201
+        from avgen_b200.ops import kernels as K
+        from avgen_b200.ops._ext import load
+
+        if not self.supported(tuple(k.shape)):
+            return self._nccl.forward(q, k, v, kmask, scale)
+        b, hk, length, d = k.shape
+        self._ensure(b, hk, length, d, k.device)
+        ext = load()
+        k_all, v_all = self._slabs(self.rank)
+        if k.data_ptr() != k_all[self.rank].data_ptr():
+            k_all[self.rank].copy_(k)
+        if v.data_ptr() != v_all[self.rank].data_ptr():
+            v_all[self.rank].copy_(v)
+        self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
+        epoch = self.epoch
+        main = torch.cuda.current_stream(k.device)
+        assert self._token is not None and self.flags is not None
+        dist.all_reduce(self._token, group=self.group)  # every rank's slab is written
+        copy = self._copy_stream
+        assert copy is not None
+        copy.wait_stream(main)
+        slab_bytes = k_all[0].numel() * k_all.element_size()
+        flag0 = self.flags.data_ptr()
+        with torch.cuda.stream(copy):
+            for step in range(1, self.world):
+                r = (self.rank + step) % self.world
+                pk, pv = self._slabs(r)
+                ext.p2p_copy(k_all[r].data_ptr(), pk[r].data_ptr(), slab_bytes)
+                ext.p2p_copy(v_all[r].data_ptr(), pv[r].data_ptr(), slab_bytes)
+                ext.stream_write(flag0 + 4 * r, epoch)
+        out, lse = K.attention_fwd(q, k_all, v_all, kmask=kmask, scale=scale, ring_rank=self.rank,
+                                   ring_flags=self.flags, ring_epoch=epoch)
+        main.wait_stream(copy)
+        return out, lse, (k_all, v_all)
+
+    def backward(self, q, k, v, o, do, lse, kmask, scale, state):  # noqa: ANN001, ANN201
+        from avgen_b200.ops import kernels as K
+
+        if not isinstance(state, tuple) or state[0].dim() != 5:
+            return self._nccl.backward(q, k, v, o, do, lse, kmask, scale, state)
+        k_all, v_all = state
+        dq, dk_all, dv_all = K.attention_bwd(q, k_all, v_all, o, do, lse, kmask=kmask, scale=scale)
+        dk = torch.empty_like(dk_all[0])
+        dv = torch.empty_like(dv_all[0])
+        dist.reduce_scatter_tensor(dk, dk_all, group=self.group)
+        dist.reduce_scatter_tensor(dv, dv_all, group=self.group)
+        return dq, dk, dv
+
+
 @contextmanager
 def context_parallel_region(mesh: DeviceMesh | None, *, buffers: Sequence[torch.Tensor] | None = None,
                             buffer_seq_dims: Sequence[int] | None = None) -> Iterator[None]:
@@ -213,22 +338,46 @@ def maybe_context_parallel(mesh: DeviceMesh | None, **kwargs: object):  # noqa: 
     return context_parallel_region(mesh, **kwargs)
 
 
-def apply_context_parallel(model: torch.nn.Module, mesh: DeviceMesh | None) -> torch.nn.Module:
+def ring_attention_available(mesh: DeviceMesh | None) -> bool:
+    """The fused NVLink ring needs CUDA ranks in one node with peer access to each other."""
+    import os
+
+    if mesh is None or mesh.size() == 1 or not torch.cuda.is_available():
+        return False
+    if os.environ.get("AVGEN_CP_RING", "1") == "0":
+        return False
+    if mesh.device_type != "cuda":
+        return False
+    local = torch.cuda.device_count()
+    ranks = mesh.mesh.flatten().tolist()
+    world_local = int(os.environ.get("LOCAL_WORLD_SIZE", local))
+    # every rank of the group on this node (same node index)
+    nodes = {r // max(1, world_local) for r in ranks}
+    return len(nodes) == 1
+
+
+def apply_context_parallel(model: torch.nn.Module, mesh: DeviceMesh | None, *, ring: bool | None = None,
+                           ) -> torch.nn.Module:
     """Make every self-attention of ``model`` global over the CP group ``mesh``.
 
-    Fused DiT blocks get :class:`ContextParallelAttention`; eager
-    ``SelfAttention`` modules get the all-gather attention; the model gathers
-    key masks across shards.
+    Fused DiT blocks get :class:`RingAttention` (one per block: K/V exchanged
+    over NVLink peer memory inside the attention kernel's schedule) when the
+    group lives on one NVSwitch node, else :class:`ContextParallelAttention`
+    (NCCL all-gather / reduce-scatter). Eager ``SelfAttention`` modules get the
+    all-gather attention; the model gathers key masks across shards.
     """
     if mesh is None or mesh.size() == 1:
         return model
     from avgen_b200.models.blocks import DiTBlock
     from avgen_b200.models.layers import SelfAttention
 
-    impl = ContextParallelAttention(mesh)
+    use_ring = ring_attention_available(mesh) if ring is None else ring
+    shared = ContextParallelAttention(mesh)
+    count = 0
     for module in model.modules():
         if isinstance(module, DiTBlock):
-            module.attention_impl = impl
+            module.attention_impl = RingAttention(mesh, count) if use_ring else shared
+            count += 1
         if isinstance(module, SelfAttention):
             module.cp_mesh = mesh
     model.cp_mesh = mesh
@@ -238,4 +387,4 @@ def apply_context_parallel(model: torch.nn.Module, mesh: DeviceMesh | None) -> t
     return model
 
 
-__all__ += ["apply_context_parallel"]
+__all__ += ["apply_context_parallel", "ring_attention_available"]

@@ -352,13 +352,18 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
     host = [make(True) for _ in range(micro)]
     dev_batches = [b.to(dev) for b in host]
     use_ring = cp > 1 and args.ref_variant == "ring"
+    cp_buffer = torch.zeros(cp * 128, device=dev)
 
     def step(batches, *, copy: bool) -> object:
         metrics = None
         for m, b in enumerate(batches):
             if copy:
                 b = b.to(dev, non_blocking=True)
-            region = context_parallel_region(parallel.cp_mesh) if use_ring else _null()
+            # torch's context_parallel indexes buffers[0], so hand the region one
+            # small sequence buffer to shard (and restore); the model's own streams
+            # are sharded by the reference's objective as shipped.
+            region = context_parallel_region(parallel.cp_mesh, buffers=[cp_buffer], buffer_seq_dims=[0]) \
+                if use_ring else _null()
             with region:
                 _, metrics = train_step(state, b, objective, patchifier=patchifier, gradient_accumulation_steps=micro,
                                         microbatch_index=m, max_grad_norm=1.0, cp_mesh=parallel.cp_mesh,

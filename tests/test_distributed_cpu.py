@@ -194,3 +194,51 @@ def test_two_rank_parallelism(worker) -> None:  # noqa: ANN001
 
 def test_data_shards_disjoint() -> None:
     _spawn(_shards_worker)
+
+
+class _FakePeerMemory:
+    """Stands in for the CUDA IPC calls: a 'handle' names the owning rank's allocation."""
+
+    def __init__(self, rank: int) -> None:
+        self.rank = rank
+        self.opened: list[bytes] = []
+        self.closed: list[int] = []
+        self.freed: list[int] = []
+
+    def p2p_alloc(self, nbytes: int, device: int) -> int:
+        return (self.rank + 1) << 40
+
+    def p2p_export(self, ptr: int) -> bytes:
+        return ptr.to_bytes(8, "little") * 8
+
+    def p2p_open(self, handle: bytes, device: int) -> int:
+        self.opened.append(handle)
+        return int.from_bytes(handle[:8], "little") + (1 << 20)  # a different address for the mapping
+
+    def p2p_close(self, ptr: int) -> None:
+        self.closed.append(ptr)
+
+    def p2p_free(self, ptr: int) -> None:
+        self.freed.append(ptr)
+
+
+def _symmetric_worker(rank: int, world: int) -> None:
+    from avgen_b200.parallel.symmetric import SymmetricBuffer
+
+    fake = _FakePeerMemory(rank)
+    buf = SymmetricBuffer(4096, dist.group.WORLD, torch.device("cpu"), backend=fake)
+    assert buf.ptrs[rank] == (rank + 1) << 40
+    for r in range(world):
+        if r != rank:
+            assert buf.ptrs[r] == ((r + 1) << 40) + (1 << 20)
+    assert len(fake.opened) == world - 1
+    assert buf.address(1 - rank, 8) == buf.ptrs[1 - rank] + 8
+    buf.close()
+    assert fake.freed == [(rank + 1) << 40] and len(fake.closed) == world - 1
+    # sizes that disagree across ranks are refused on every rank
+    with pytest.raises(RuntimeError):
+        SymmetricBuffer(4096 + 16 * rank, dist.group.WORLD, torch.device("cpu"), backend=_FakePeerMemory(rank))
+
+
+def test_symmetric_buffer_handle_exchange() -> None:
+    _spawn(_symmetric_worker)

@@ -457,3 +457,93 @@ def test_sde_step_matches_torch_oracle() -> None:
         - 0.5 * math.log(2 * math.pi)
     torch.testing.assert_close(logp2.double(), (per * mask).flatten(1).sum(1).double(), rtol=1e-4, atol=1.0)
     _errors_clear()
+
+
+def _ring_reference(q, k_all, v_all, kmask, scale):  # noqa: ANN001, ANN202
+    """Plain fp32 attention over the concatenated ring slabs ([world, B, Hk, L, D] -> [B, Hk, world*L, D])."""
+    world, b, hk, length, d = k_all.shape
+    kf = k_all.permute(1, 2, 0, 3, 4).reshape(b, hk, world * length, d).float()
+    vf = v_all.permute(1, 2, 0, 3, 4).reshape(b, hk, world * length, d).float()
+    rep = q.shape[1] // hk
+    kf, vf = kf.repeat_interleave(rep, 1), vf.repeat_interleave(rep, 1)
+    s = torch.einsum("bhqd,bhkd->bhqk", q.float(), kf) * scale
+    if kmask is not None:
+        s = s.masked_fill(~kmask[:, None, None, :], float("-inf"))
+    return torch.einsum("bhqk,bhkd->bhqd", s.softmax(-1), vf)
+
+
+@pytest.mark.parametrize("masked", [False, True])
+def test_ring_attention_gates_on_copied_slabs(masked: bool) -> None:
+    """World 3 emulated on one GPU: slabs 1 and 2 arrive by copy engine behind a
+    large unrelated copy on the copy stream, each followed by a front-end flag
+    write, while the kernel (launched at once) gates each slab on its flag;
+    results match attention over the whole sequence, forward and backward
+    (dK/dV come back per slab). No stream waits on a flag."""
+    from avgen_b200.ops._ext import load
+
+    ops, ext = _ops(), load()
+    torch.manual_seed(0)
+    world, b, h, hk, length, d = 3, 1, 4, 2, 256, 128
+    me = 0
+    q = torch.randn(b, h, length, d, device=DEV).bfloat16()
+    src_k = torch.randn(world, b, hk, length, d, device=DEV).bfloat16()
+    src_v = torch.randn(world, b, hk, length, d, device=DEV).bfloat16()
+    k_all = torch.zeros_like(src_k)
+    v_all = torch.zeros_like(src_v)
+    k_all[me].copy_(src_k[me])
+    v_all[me].copy_(src_v[me])
+    flags = torch.zeros(world, dtype=torch.int32, device=DEV)
+    kmask = packed = None
+    if masked:
+        kmask = torch.ones(b, world * length, dtype=torch.bool, device=DEV)
+        kmask[:, 300:400] = False
+        packed = ops.pack_key_mask(kmask)
+    ballast = torch.empty(1 << 28, dtype=torch.uint8, device=DEV)  # 256 MB: delays the slab copies
+    ballast2 = torch.empty_like(ballast)
+    torch.cuda.synchronize()
+    epoch = 7
+    copy = torch.cuda.Stream()
+    slab = src_k[0].numel() * 2
+    with torch.cuda.stream(copy):
+        ext.p2p_copy(ballast2.data_ptr(), ballast.data_ptr(), ballast.numel())
+        for r in (1, 2):
+            ext.p2p_copy(k_all[r].data_ptr(), src_k[r].data_ptr(), slab)
+            ext.p2p_copy(v_all[r].data_ptr(), src_v[r].data_ptr(), slab)
+            ext.stream_write(flags.data_ptr() + 4 * r, epoch)
+    scale = 1.0 / math.sqrt(d)
+    out, lse = ops.attention_fwd(q, k_all, v_all, kmask=packed, scale=scale, ring_rank=me, ring_flags=flags,
+                                 ring_epoch=epoch)
+    torch.cuda.synchronize()
+    _errors_clear()
+    ref = _ring_reference(q, src_k, src_v, kmask, scale)
+    _close(out.permute(0, 2, 1, 3), ref)
+    # backward against autograd on the fp32 reference
+    do = torch.randn(b, length, h, d, device=DEV).bfloat16()
+    dq, dk_all, dv_all = ops.attention_bwd(q, k_all, v_all, out, do, lse, kmask=packed, scale=scale)
+    qr, kr, vr = (t.float().requires_grad_() for t in (q, src_k, src_v))
+    ref2 = _ring_reference(qr, kr, vr, kmask, scale)
+    ref2.backward(do.permute(0, 2, 1, 3).float())
+    _close(dq, qr.grad, rtol=3e-2, atol=3e-2)
+    assert dk_all.shape == src_k.shape
+    _close(dk_all, kr.grad, rtol=3e-2, atol=3e-2)
+    _close(dv_all, vr.grad, rtol=3e-2, atol=3e-2)
+    _errors_clear()
+
+
+def test_ring_attention_times_out_without_its_slab() -> None:
+    """A slab whose flag never arrives makes the kernel give up after its bounded
+    wait and report it in the error word; the context stays usable."""
+    from avgen_b200.ops._ext import check_errors
+
+    ops = _ops()
+    world, b, h, length, d = 2, 1, 2, 128, 128
+    q = torch.randn(b, h, length, d, device=DEV).bfloat16()
+    k_all = torch.randn(world, b, h, length, d, device=DEV).bfloat16()
+    flags = torch.zeros(world, dtype=torch.int32, device=DEV)
+    ops.attention_fwd(q, k_all, k_all.clone(), ring_rank=0, ring_flags=flags, ring_epoch=1)
+    torch.cuda.synchronize()
+    assert check_errors(clear=True) == 5  # timed out waiting on a peer's slab
+    out, _ = ops.attention_fwd(q, k_all[0], k_all[0])  # the device still works
+    torch.cuda.synchronize()
+    assert torch.isfinite(out.float()).all()
+    _errors_clear()

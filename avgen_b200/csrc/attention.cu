@@ -948,8 +948,9 @@ __global__ void __launch_bounds__(512, 1)
 
   const int warp = warp_id();
   const int lane = lane_id();
-  const int kt = blockIdx.x % p.k_tiles;
-  const int bhk = blockIdx.x / p.k_tiles;
+  const int kt_span = p.kt_count > 0 ? p.kt_count : p.k_tiles;
+  const int kt = p.kt_begin + static_cast<int>(blockIdx.x % kt_span);
+  const int bhk = blockIdx.x / kt_span;
   const int hk = bhk % p.Hk;
   const int b = bhk / p.Hk;
   const int k0 = kt * kTile;
@@ -1330,8 +1331,9 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
               "attention bwd: O / dO must be dense [B, Lq, H, 128]");
   AVGEN_CHECK(d.stat_ld >= d.Lq && d.stat_ld % 4 == 0, "attention bwd: lse/delta row stride must be >= Lq and a multiple of 4");
   AVGEN_CHECK(d.ring_world <= 1 || d.dq_acc != nullptr, "attention bwd: the ring layout needs the fused kernel");
+  AVGEN_CHECK(d.kt_count == 0 || d.dq_acc != nullptr, "attention bwd: key-tile ranges need the fused kernel");
   // delta = rowsum(dO * O)
-  {
+  if (!d.skip_prologue) {
     const long rows = static_cast<long>(d.B) * d.H * d.Lq;
     const long blocks = std::min<long>((rows + 7) / 8, 16L * num_sms(d.device));
     attn_bwd_delta_kernel<<<blocks, 256, 0, stream>>>(
@@ -1372,8 +1374,11 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
   if (d.dq_acc != nullptr) {
     // ---- fused: dK, dV and dQ^T partials in one pass, then dQ = scale * acc^T
     const long ld = (d.Lq + 3) / 4 * 4;  // 16-byte rows for the TMA reduce
-    AVGEN_CUDA_CHECK(cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * ld * kHD * d.B * d.H, stream));
+    if (!d.skip_prologue)
+      AVGEN_CUDA_CHECK(cudaMemsetAsync(d.dq_acc, 0, sizeof(float) * ld * kHD * d.B * d.H, stream));
     d.k_tiles = (d.Lk + kTile - 1) / kTile;
+    AVGEN_CHECK(d.kt_begin >= 0 && d.kt_count >= 0 && d.kt_begin + d.kt_count <= d.k_tiles,
+                "attention bwd: key-tile range outside [0, ", d.k_tiles, ")");
     const bool ring = d.ring_world > 1;
     if (ring)
       AVGEN_CHECK(d.ring_len % kTile == 0 && d.ring_len > 0 && d.Lk == d.ring_world * d.ring_len,
@@ -1406,15 +1411,17 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, FusedBwdSmem::BYTES));
       attr = true;
     }
-    const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
+    const long grid = static_cast<long>(d.B) * d.Hk * (d.kt_count > 0 ? d.kt_count : d.k_tiles);
     if (d.trace != nullptr)
       attn_bwd_fused_kernel<true><<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
     else
       attn_bwd_fused_kernel<false><<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
     AVGEN_CUDA_CHECK(cudaGetLastError());
-    dim3 cgrid((d.Lq + 63) / 64, d.B * d.H);
-    attn_dq_convert_kernel<<<cgrid, 256, 0, stream>>>(d.dq_acc, ld, d.Lq, d.scale, d.dq);
-    AVGEN_CUDA_CHECK(cudaGetLastError());
+    if (!d.skip_epilogue) {
+      dim3 cgrid((d.Lq + 63) / 64, d.B * d.H);
+      attn_dq_convert_kernel<<<cgrid, 256, 0, stream>>>(d.dq_acc, ld, d.Lq, d.scale, d.dq);
+      AVGEN_CUDA_CHECK(cudaGetLastError());
+    }
     return;
   }
   // ---- dK / dV

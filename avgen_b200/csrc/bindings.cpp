@@ -635,7 +635,8 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
 
 void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& o,
               const at::Tensor& dout, const at::Tensor& lse, at::Tensor& delta, at::Tensor& dq, at::Tensor& dk,
-              at::Tensor& dv, const OptT& kmask, double scale, const OptT& dq_acc, const OptT& trace) {
+              at::Tensor& dv, const OptT& kmask, double scale, const OptT& dq_acc, const OptT& trace,
+              int64_t kt_begin, int64_t kt_count, bool skip_prologue, bool skip_epilogue) {
   c10::cuda::CUDAGuard guard(q.device());
   for (const at::Tensor* t : {&q, &k, &v, &o, &dout, static_cast<const at::Tensor*>(&dk), static_cast<const at::Tensor*>(&dv)}) check_bf16(*t, "attention bwd tensor");
   check_f32(lse, "lse");
@@ -698,6 +699,10 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   d.scale = static_cast<float>(scale);
   d.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
   d.err = error_word(d.device);
+  d.kt_begin = static_cast<int>(kt_begin);
+  d.kt_count = static_cast<int>(kt_count);
+  d.skip_prologue = skip_prologue;
+  d.skip_epilogue = skip_epilogue;
   attn_bwd_launch(d, cur_stream());
 }
 
@@ -725,6 +730,18 @@ at::Tensor tensor_at(int64_t ptr, const std::vector<int64_t>& sizes, at::ScalarT
 void stream_write_py(int64_t flag, int64_t value) {
   stream_write(cur_stream(), reinterpret_cast<void*>(flag), static_cast<unsigned>(value));
 }
+// dst = sum of the bf16 tensors whose device addresses `srcs` (int64 device tensor) holds,
+// each with dst's element count.
+void slab_sum(const at::Tensor& srcs, at::Tensor& dst) {
+  c10::cuda::CUDAGuard guard(dst.device());
+  check_bf16(dst, "slab_sum dst");
+  TORCH_CHECK(dst.is_contiguous(), "slab_sum: dst must be contiguous");
+  TORCH_CHECK(srcs.is_cuda() && srcs.scalar_type() == at::kLong && srcs.is_contiguous() && srcs.numel() > 0,
+              "slab_sum: srcs must be a non-empty int64 device tensor of addresses");
+  slab_sum_launch(reinterpret_cast<const void* const*>(srcs.data_ptr<int64_t>()), static_cast<int>(srcs.numel()),
+                  dst.data_ptr(), dst.numel(), dst.device().index(), cur_stream());
+}
+
 void p2p_copy_py(int64_t dst, int64_t src, int64_t bytes) {
   p2p_copy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), static_cast<size_t>(bytes), cur_stream());
 }
@@ -795,7 +812,9 @@ PYBIND11_MODULE(_C, m) {
   m.def("p2p_copy", &a::p2p_copy_py, arg("dst"), arg("src"), arg("bytes"));
   m.def("attn_bwd", &a::attn_bwd, arg("q"), arg("k"), arg("v"), arg("o"), arg("dout"), arg("lse"), arg("delta"),
         arg("dq"), arg("dk"), arg("dv"), arg("kmask") = none, arg("scale") = 0.0, arg("dq_acc") = none,
-        arg("trace") = none);
+        arg("trace") = none, arg("kt_begin") = 0, arg("kt_count") = 0, arg("skip_prologue") = false,
+        arg("skip_epilogue") = false);
+  m.def("slab_sum", &a::slab_sum, arg("srcs"), arg("dst"));
   m.def("read_error", &a::read_error);
   m.def("clear_error", &a::clear_error);
 }

@@ -246,6 +246,14 @@ struct AttnBwdDesc {
   // rank's partial gradients for every rank's keys, chunk r contiguous.
   int ring_world = 0;
   int ring_len = 0;
+  // Key-tile range of one launch of the fused kernel (kt_count 0 = every tile). A
+  // backward split over several launches runs the prologue (delta, dQ scratch
+  // reset) only in the first (skip_prologue false) and the dQ conversion only in
+  // the last (skip_epilogue false).
+  int kt_begin = 0;
+  int kt_count = 0;
+  bool skip_prologue = false;
+  bool skip_epilogue = false;
   long long* trace = nullptr;  // optional int64 [64 * 24]: per-warp SM clock stamps of CTA 0 (diagnostics)
   int* err = nullptr;
 };
@@ -305,5 +313,6 @@ void* p2p_open(const char* handle64, int device);
 void p2p_close(void* ptr);
 void stream_write(cudaStream_t stream, void* flag, unsigned value);
 void p2p_copy(void* dst, const void* src, size_t bytes, cudaStream_t stream);
+void slab_sum_launch(const void* const* srcs_dev, int nsrc, void* dst, long n, int device, cudaStream_t stream);
 
 }  // namespace avgen

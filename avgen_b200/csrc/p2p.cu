@@ -11,6 +11,7 @@
 //     copies, never by SMs, so a kernel that occupies every SM can wait on them
 //     (boundedly) without starving them. Streams themselves never wait on flags:
 //     an unbounded stream-side wait could deadlock against implicit ordering.
+#include <algorithm>
 #include <mutex>
 
 #include "include/host_utils.h"
@@ -38,7 +39,41 @@ WriteValueFn write_value_fn() {
   return fn;
 }
 
+// dst = sum of nsrc bf16 tensors of n8 * 8 elements each (fp32 accumulation):
+// the owner-side reduction of context-parallel dK/dV partials pushed by peers.
+__global__ void slab_sum_kernel(const __nv_bfloat16* const* srcs, int nsrc, __nv_bfloat16* dst, long n8) {
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n8;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int s = 0; s < nsrc; ++s) {
+      const uint4 v = reinterpret_cast<const uint4*>(srcs[s])[i];
+      const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        acc[2 * e] += bf16_lo(w[e]);
+        acc[2 * e + 1] += bf16_hi(w[e]);
+      }
+    }
+    uint4 o;
+    o.x = pack_bf16(acc[0], acc[1]);
+    o.y = pack_bf16(acc[2], acc[3]);
+    o.z = pack_bf16(acc[4], acc[5]);
+    o.w = pack_bf16(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(dst)[i] = o;
+  }
+}
+
 }  // namespace
+
+void slab_sum_launch(const void* const* srcs_dev, int nsrc, void* dst, long n, int device, cudaStream_t stream) {
+  AVGEN_CHECK(n % 8 == 0, "slab_sum: element count must be a multiple of 8");
+  if (n == 0) return;
+  const long n8 = n / 8;
+  const long blocks = std::max<long>(1, std::min<long>((n8 + 255) / 256, 8L * num_sms(device)));
+  slab_sum_kernel<<<blocks, 256, 0, stream>>>(reinterpret_cast<const __nv_bfloat16* const*>(srcs_dev), nsrc,
+                                               reinterpret_cast<__nv_bfloat16*>(dst), n8);
+  AVGEN_CUDA_CHECK(cudaGetLastError());
+}
 
 void* p2p_alloc(size_t bytes, int device) {
   int prev = 0;

@@ -375,6 +375,55 @@ def attention_bwd(
     return dq, dk, dv
 
 
+def attention_bwd_slabs(
+    q: torch.Tensor,
+    k_all: torch.Tensor,
+    v_all: torch.Tensor,
+    o: torch.Tensor,
+    dout: torch.Tensor,
+    lse: torch.Tensor,
+    *,
+    order: list[int],
+    kmask: torch.Tensor | None = None,
+    scale: float | None = None,
+    on_slab=None,  # noqa: ANN001
+) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """Ring-layout backward launched once per key slab, in ``order``.
+
+    ``k_all``/``v_all`` are ``[world, B, Hk, L, D]``; slab r's partial dK/dV land
+    in ``dk_all[r]``/``dv_all[r]`` when its launch completes, and ``on_slab(r,
+    dk_all, dv_all)`` runs right after that launch is enqueued (to start moving
+    the slab while the next one computes). dQ accumulates across the launches
+    and is converted after the last.
+    """
+    world, _, _, length, d = k_all.shape
+    if length % 128:
+        raise ValueError("ring slabs must hold a multiple of 128 keys")
+    scale = 1.0 / math.sqrt(d) if scale is None else scale
+    tiles = length // 128
+    delta = torch.empty_strided(lse.shape, lse.stride(), device=lse.device, dtype=_F32)
+    dq = torch.empty_like(q)
+    dk_all = torch.empty_like(k_all)
+    dv_all = torch.empty_like(v_all)
+    acc = torch.empty(q.shape[0] * q.shape[1] * d * (-(-q.shape[2] // 4) * 4), device=q.device, dtype=_F32)
+    ext = load()
+    for i, r in enumerate(order):
+        ext.attn_bwd(q, k_all, v_all, o, dout, lse, delta, dq, dk_all, dv_all, kmask, scale, acc, None,
+                     r * tiles, tiles, i > 0, i < len(order) - 1)
+        _count(1 + (i == 0) + (i == len(order) - 1))
+        if on_slab is not None:
+            on_slab(r, dk_all, dv_all)
+    return dq, dk_all, dv_all
+
+
+def slab_sum(sources: list[torch.Tensor], out: torch.Tensor) -> torch.Tensor:
+    """``out = sum(sources)`` for bf16 tensors shaped like ``out`` (fp32 accumulation)."""
+    ptrs = torch.tensor([t.data_ptr() for t in sources], dtype=torch.int64, device=out.device)
+    load().slab_sum(ptrs, out)
+    _count()
+    return out
+
+
 def swiglu_bwd(dh: torch.Tensor, gu: torch.Tensor) -> torch.Tensor:
     """Backward of the interleaved SwiGLU epilogue: returns ``dgu`` like ``gu``."""
     dgu = torch.empty_like(gu)

@@ -216,10 +216,14 @@ class RingAttention:
        bounded wait, so the transfer of slab r overlaps the softmax/MMA work on
        the slabs before it.
 
-    Backward runs the one-pass flash backward on the same buffer; the kernel
-    writes this rank's partial dK/dV for every slab in the ring layout, and the
-    slabs are reduce-scattered to their owners. That reduce-scatter also orders
-    the next step's overwrite of a slab after every peer's copy of it.
+    Backward runs the one-pass flash backward on the same buffer, launched once
+    per slab with the remote slabs first and this rank's own slab last. As each
+    remote slab's partial dK/dV completes, the copy engines push it into the
+    owner's receive buffer (one per CP group, double-buffered across
+    backward calls) while the next slab computes; one word all-reduce then
+    marks every push landed and a summing kernel forms this rank's dK/dV from
+    its own partial and the pushed ones. That barrier also orders the next
+    step's overwrite of a K/V slab after every peer's copy of it.
     """
 
     def __init__(self, mesh: DeviceMesh, index: int) -> None:
@@ -307,18 +311,68 @@ class RingAttention:
         main.wait_stream(copy)
         return out, lse, (k_all, v_all)
 
+    # receive buffers for dK/dV partials pushed by peers: one pair per (group, shape),
+    # shared by every block, double-buffered by backward parity
+    _recv_pool: dict[tuple[int, tuple[int, ...]], Any] = {}
+
+    def _recv(self, device: torch.device) -> Any:
+        from avgen_b200.parallel.symmetric import SymmetricBuffer
+
+        assert self.shape is not None
+        key = (id(self.group), self.shape)
+        buf = RingAttention._recv_pool.get(key)
+        if buf is None:
+            n = 1
+            for s_ in self.shape:
+                n *= s_
+            buf = SymmetricBuffer(2 * 2 * n * 2, self.group, device)  # parity x (dK, dV) x ring layout, bf16
+            RingAttention._recv_pool[key] = buf
+        return buf
+
     def backward(self, q, k, v, o, do, lse, kmask, scale, state):  # noqa: ANN001, ANN201
         from avgen_b200.ops import kernels as K
+        from avgen_b200.ops._ext import load
 
         if not isinstance(state, tuple) or state[0].dim() != 5:
             return self._nccl.backward(q, k, v, o, do, lse, kmask, scale, state)
         k_all, v_all = state
-        dq, dk_all, dv_all = K.attention_bwd(q, k_all, v_all, o, do, lse, kmask=kmask, scale=scale)
-        dk = torch.empty_like(dk_all[0])
-        dv = torch.empty_like(dv_all[0])
-        dist.reduce_scatter_tensor(dk, dk_all, group=self.group)
-        dist.reduce_scatter_tensor(dv, dv_all, group=self.group)
+        ext = load()
+        recv = self._recv(q.device)
+        assert self.shape is not None and self._copy_stream is not None and self._token is not None
+        parity = RingAttention._bwd_calls % 2
+        RingAttention._bwd_calls += 1
+        part = recv.nbytes // 4  # bytes of one ring-layout tensor
+        slab = part // self.world
+
+        def base(rank: int, which: int) -> int:  # which: 0 = dK, 1 = dV
+            return recv.address(rank, (2 * parity + which) * part)
+
+        main = torch.cuda.current_stream(q.device)
+        copy = self._copy_stream
+
+        def push(r: int, dk_all: torch.Tensor, dv_all: torch.Tensor) -> None:
+            if r == self.rank:
+                return
+            copy.wait_stream(main)  # slab r's partials are complete
+            with torch.cuda.stream(copy):
+                ext.p2p_copy(base(r, 0) + self.rank * slab, dk_all[r].data_ptr(), slab)
+                ext.p2p_copy(base(r, 1) + self.rank * slab, dv_all[r].data_ptr(), slab)
+
+        order = [(self.rank + s_) % self.world for s_ in range(1, self.world)] + [self.rank]
+        dq, dk_all, dv_all = K.attention_bwd_slabs(q, k_all, v_all, o, do, lse, order=order, kmask=kmask,
+                                                   scale=scale, on_slab=push)
+        main.wait_stream(copy)
+        dist.all_reduce(self._token, group=self.group)  # every peer's pushes into this rank have landed
+        shape = self.shape[1:]
+        sources_k = [dk_all[self.rank]] + [recv.view(self.rank, (2 * parity) * part + s_ * slab, shape, torch.bfloat16)
+                                           for s_ in range(self.world) if s_ != self.rank]
+        sources_v = [dv_all[self.rank]] + [recv.view(self.rank, (2 * parity + 1) * part + s_ * slab, shape,
+                                                     torch.bfloat16) for s_ in range(self.world) if s_ != self.rank]
+        dk = K.slab_sum(sources_k, torch.empty(shape, device=q.device, dtype=torch.bfloat16))
+        dv = K.slab_sum(sources_v, torch.empty(shape, device=q.device, dtype=torch.bfloat16))
         return dq, dk, dv
+
+    _bwd_calls = 0
 
 
 @contextmanager

@@ -353,6 +353,12 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
     dev_batches = [b.to(dev) for b in host]
     use_ring = cp > 1 and args.ref_variant == "ring"
     cp_buffer = torch.zeros(cp * 128, device=dev)
+    if use_ring:
+        # torch's ring SDPA enables its head-tail load balancer by default and then
+        # refuses non-causal attention; the DiT's attention is bidirectional.
+        from torch.distributed.tensor.experimental._context_parallel import _attention as _cp_attention
+
+        _cp_attention._cp_options.enable_load_balance = False
 
     def step(batches, *, copy: bool) -> object:
         metrics = None

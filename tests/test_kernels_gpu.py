@@ -527,7 +527,24 @@ def test_ring_attention_gates_on_copied_slabs(masked: bool) -> None:
     assert dk_all.shape == src_k.shape
     _close(dk_all, kr.grad, rtol=3e-2, atol=3e-2)
     _close(dv_all, vr.grad, rtol=3e-2, atol=3e-2)
+    # the same backward split into one launch per slab (remote slabs first)
+    seen = []
+    dq2, dk2, dv2 = ops.attention_bwd_slabs(q, k_all, v_all, out, do, lse, order=[1, 2, 0], kmask=packed,
+                                            scale=scale, on_slab=lambda r, a, b_: seen.append(r))
+    torch.cuda.synchronize()
+    assert seen == [1, 2, 0]
+    _close(dq2, dq, rtol=1e-2, atol=1e-2)
+    _close(dk2, dk_all, rtol=1e-2, atol=1e-2)
+    _close(dv2, dv_all, rtol=1e-2, atol=1e-2)
     _errors_clear()
+
+
+def test_slab_sum_matches_fp32() -> None:
+    ops = _ops()
+    torch.manual_seed(0)
+    parts = [torch.randn(2, 3, 256, 128, device=DEV).bfloat16() for _ in range(4)]
+    out = ops.slab_sum(parts, torch.empty_like(parts[0]))
+    _close(out, sum(p.float() for p in parts), rtol=1e-2, atol=1e-2)
 
 
 def test_ring_attention_times_out_without_its_slab() -> None:

@@ -25,6 +25,7 @@ Self-attention can be swapped for a context-parallel implementation through
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 from typing import Any, Protocol
 
@@ -151,9 +152,11 @@ def _norm_weight(norm: nn.Module) -> torch.Tensor | None:
     return _f32(w) if isinstance(w, torch.Tensor) else None
 
 
-def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, *, save):  # noqa: ANN001, ANN202
-    """Run the block forward; returns (x3, (O, lse, attn_state)) and, when
-    ``save`` is False, also the intermediates the backward needs."""
+def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, *, save,  # noqa: ANN001, ANN202
+                  keep_inter=False):
+    """Run the block head; returns (intermediates, O, lse, attn_state). The
+    intermediates the backward needs come back when ``save`` is False (the
+    backward's recompute) or ``keep_inter`` is True (forward that keeps them)."""
     from avgen_b200.ops import kernels as K
 
     b, length, w = spec.batch, spec.length, spec.width
@@ -180,14 +183,17 @@ def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
         o = lse = attn_state = None
     return_o = o
     inter: dict[str, Any] = {}
-    if not save:
+    if not save or keep_inter:
         inter.update(n1=n1, rstd1=rstd1, qkv=qkv, q=q, k=k, v=v)
     return inter, return_o, lse, attn_state
 
 
-def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep):  # noqa: ANN001, ANN202
-    """Everything after the self-attention kernel. Returns x3 and (if keep) the
-    intermediates needed for backward."""
+def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep, want_out=False,  # noqa: ANN001, ANN202
+                keep_mlp=True):
+    """Everything after the self-attention kernel. Returns x3 (None when only
+    the intermediates are wanted: ``keep`` without ``want_out``) and, if keep,
+    the intermediates needed for backward (without the MLP activations gu and h
+    when ``keep_mlp`` is False)."""
     from avgen_b200.ops import kernels as K
 
     b, length, w = spec.batch, spec.length, spec.width
@@ -220,18 +226,30 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep):  # noqa: AN
         keep_d.update(x1=x1)
     n3, rstd3 = K.rmsnorm_mod(x2, _norm_weight(block.ffn_norm), scale_f, shift_f, **spec.mod_rows(),
                               eps=block.ffn_norm.eps or eps)
-    if spec.ffn == "swiglu":
-        gu = torch.empty((m, 2 * spec.hidden), device=xb.device, dtype=_BF16) if keep else None
-        hdn = K.gemm(n3, pw["gu"], epilogue="swiglu", aux=gu)
-    else:
-        gu = torch.empty((m, spec.hidden), device=xb.device, dtype=_BF16) if keep else None
-        hdn = K.gemm(n3, pw["up"], epilogue="gelu", aux=gu)
-    if keep:
+    gu, hdn = _mlp_up(spec, pw, n3, keep=keep and keep_mlp)
+    if keep and not want_out:
         f = K.gemm(hdn, pw["down"])
         keep_d.update(a_o=a_o, x2=x2, n3=n3, rstd3=rstd3, gu=gu, h=hdn, f=f)
         return None, keep_d
-    x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, **spec.mod_rows())
+    f = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
+    x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, **spec.mod_rows(), aux=f)
+    if keep:
+        keep_d.update(a_o=a_o, x2=x2, n3=n3, rstd3=rstd3, f=f)
+        if keep_mlp:
+            keep_d.update(gu=gu, h=hdn)
     return x3, keep_d
+
+
+def _mlp_up(spec, pw, n3, *, keep):  # noqa: ANN001, ANN202
+    """MLP up-projection with its activation epilogue: (pre-activation or None, h)."""
+    from avgen_b200.ops import kernels as K
+
+    m = n3.shape[0]
+    if spec.ffn == "swiglu":
+        gu = torch.empty((m, 2 * spec.hidden), device=n3.device, dtype=_BF16) if keep else None
+        return gu, K.gemm(n3, pw["gu"], epilogue="swiglu", aux=gu)
+    gu = torch.empty((m, spec.hidden), device=n3.device, dtype=_BF16) if keep else None
+    return gu, K.gemm(n3, pw["up"], epilogue="gelu", aux=gu)
 
 
 def _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask):  # noqa: ANN001, ANN202
@@ -241,7 +259,8 @@ def _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     return x3, (o, lse, attn_state)
 
 
-def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask, o, lse, attn_state, dout):  # noqa: ANN001, ANN202
+def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask, o, lse, attn_state, dout,  # noqa: ANN001, ANN202
+                   saved=None):
     from avgen_b200.ops import kernels as K
 
     b, length, w = spec.batch, spec.length, spec.width
@@ -252,9 +271,16 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     pw = packed_weights(block)
     att = block.attention
     ff = block.feed_forward
-    # ---------------------------------------------------------------- recompute
-    inter, _, _, _ = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, save=False)
-    _, keep = _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, keep=True)
+    # ---------------------------------------------------------------- recompute (unless kept in forward)
+    if saved is not None:
+        inter, keep = saved
+        if "gu" not in keep:  # the MLP activations were not kept: rebuild them from n3
+            keep = dict(keep)
+            keep["gu"], keep["h"] = _mlp_up(spec, pw, keep["n3"], keep=True)
+    else:
+        inter, _, _, _ = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask,
+                                       save=False)
+        _, keep = _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, keep=True)
     dmod = torch.zeros_like(modf)  # [modulation rows, 6, W]
     gate_a, gate_f = modf[:, 2], modf[:, 5]
     dx3 = dout.reshape(m, w).to(_BF16).contiguous()
@@ -371,6 +397,48 @@ def block_param_names(block: nn.Module) -> list[str]:
     return [n for n, _ in block.named_parameters() if n != "scale_shift_table"]
 
 
+# Bytes per token kept by the forward when it skips the backward's recompute, by
+# mode: everything ("all"), everything but the MLP activations ("no_mlp"). Filled
+# from the first block that keeps them; the first guess is conservative.
+_KEEP_BYTES: dict[str, float] = {}
+_KEEP_MARGIN = float(os.environ.get("AVGEN_KEEP_MARGIN_GB", "20")) * 2**30
+
+
+def _keep_mode(spec: BlockSpec, xb: torch.Tensor) -> str:
+    """Whether this block's forward keeps its intermediates for the backward
+    (skipping the recompute) given the device memory free right now.
+
+    ``AVGEN_KEEP_ACTIVATIONS``: ``auto`` (default) picks per block the most that
+    fits while leaving room for what the rest of the forward must hold (later
+    blocks' saved inputs and outputs, ring buffers still to be allocated) plus a
+    margin (``AVGEN_KEEP_MARGIN_GB``, 20) for the backward's transients;
+    ``all`` / ``no_mlp`` / ``none`` force a mode.
+    """
+    policy = os.environ.get("AVGEN_KEEP_ACTIVATIONS", "auto")
+    if policy in ("all", "no_mlp", "none"):
+        return policy
+    if not xb.is_cuda:
+        return "none"
+    free, _ = torch.cuda.mem_get_info(xb.device)
+    free += torch.cuda.memory_reserved(xb.device) - torch.cuda.memory_allocated(xb.device)
+    tokens = spec.batch * spec.length
+    w, f = spec.width, spec.hidden
+    # reserve what the rest of the forward must still hold: every later block's saved
+    # input and attention output (up to 40 blocks) and ring buffers not yet allocated
+    margin = _KEEP_MARGIN + 40 * tokens * (4 * w + 4 * spec.heads)
+    if hasattr(spec.attention, "kv_out"):
+        from avgen_b200.parallel.context import ring_buffers_pending
+
+        margin += ring_buffers_pending(spec.batch, spec.kv_heads, spec.length, spec.head_dim)
+    guess_no_mlp = tokens * (18 * w * 2 + 64)
+    per = {"all": max(_KEEP_BYTES.get("all", 0.0) * tokens, guess_no_mlp + tokens * 3 * f * 2),
+           "no_mlp": max(_KEEP_BYTES.get("no_mlp", 0.0) * tokens, guess_no_mlp)}
+    for mode in ("all", "no_mlp"):
+        if free - per[mode] > margin:
+            return mode
+    return "none"
+
+
 class FusedBlockFn(torch.autograd.Function):
     """Autograd node for a whole DiT block."""
 
@@ -382,7 +450,25 @@ class FusedBlockFn(torch.autograd.Function):
         modf = mod.detach().float().contiguous()
         ctxb = context.detach().to(_BF16).contiguous() if context is not None else None
         pw = packed_weights(block)
-        x3, (o, lse, attn_state) = _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask)
+        mode = _keep_mode(spec, xb) if any(ctx.needs_input_grad) else "none"
+        ctx.saved = None
+        if mode == "none":
+            x3, (o, lse, attn_state) = _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask,
+                                                     cmask)
+        else:
+            inter, o, lse, attn_state = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask,
+                                                      cmask, save=True, keep_inter=True)
+            x3, keep = _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, keep=True, want_out=True,
+                                   keep_mlp=mode == "all")
+            ctx.saved = (inter, keep)
+            if mode not in _KEEP_BYTES:
+                seen: set[int] = set()
+                total = 0
+                for t in (*inter.values(), *keep.values()):
+                    if isinstance(t, torch.Tensor) and t.data_ptr() not in seen:
+                        seen.add(t.data_ptr())
+                        total += t.numel() * t.element_size()
+                _KEEP_BYTES[mode] = total * 1.05 / max(1, spec.batch * spec.length)  # bytes per token
         ctx.spec = spec
         ctx.block = block
         ctx.attn_state = attn_state
@@ -403,7 +489,8 @@ class FusedBlockFn(torch.autograd.Function):
         dx, dmod, dctx, pgrads = _backward_impl(
             ctx.spec, ctx.block, xb, modf, ctxb if has_ctx else None, coords if has_coords else None,
             freq if has_coords else None, axis if has_coords else None, kmask if has_kmask else None,
-            cmask if has_cmask else None, o, lse, ctx.attn_state, dout)
+            cmask if has_cmask else None, o, lse, ctx.attn_state, dout, saved=ctx.saved)
+        ctx.saved = None
         if dctx is not None and ctx.ctx_dtype is not None:
             dctx = dctx.to(ctx.ctx_dtype)
         return (None, None, None, None, None, None, None, dx.view_as(dout).to(ctx.x_dtype), dmod, dctx, *pgrads)

@@ -20,6 +20,7 @@ from __future__ import annotations
 from collections.abc import Iterator, Sequence
 from contextlib import contextmanager, nullcontext
 from dataclasses import replace
+import weakref
 from typing import Any
 
 import torch
@@ -197,6 +198,20 @@ class ContextParallelAttention:
         return dq, scatter(dkf), scatter(dvf)
 
 
+_RING_INSTANCES: "weakref.WeakSet[RingAttention]" = weakref.WeakSet()
+
+
+def ring_buffers_pending(b: int, hk: int, length: int, d: int) -> int:
+    """Bytes of ring K/V buffers that live :class:`RingAttention` instances have yet to
+    allocate for this shape (they allocate lazily, on their block's first forward)."""
+    total = 0
+    for inst in list(_RING_INSTANCES):
+        shape = (inst.world, b, hk, length, d)
+        if inst.shape != shape and RingAttention.supported((b, hk, length, d)):
+            total += 2 * inst.world * b * hk * length * d * 2
+    return total
+
+
 class RingAttention:
     """Fused context-parallel self-attention over NVLink peer memory, for one DiT block.
 
@@ -239,6 +254,7 @@ class RingAttention:
         self._token: torch.Tensor | None = None
         self._copy_stream: torch.cuda.Stream | None = None
         self._nccl = ContextParallelAttention(mesh)  # shapes the ring kernels do not take
+        _RING_INSTANCES.add(self)
 
     @staticmethod
     def supported(k_shape: tuple[int, ...]) -> bool:

@@ -270,6 +270,7 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
                 "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
         "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro,
         "params": sum(p.numel() for p in model.parameters()),
+        "peak_mem_gib": torch.cuda.max_memory_allocated(dev) / 2**30,
     }
 
 
@@ -462,6 +463,7 @@ def main() -> None:
                 line["gpu_launches"] = out["gpu_launches"]
                 line["kernel_errors"] = out["kernel_errors"]
                 line["params"] = out["params"]
+                line["peak_mem_gib"] = round(out["peak_mem_gib"], 1)
             if args.depth != DEPTH or args.frames != FRAMES:
                 line["note"] = "reduced model/config: not a valid benchmark line"
             print(json.dumps(line), flush=True)

@@ -17,9 +17,14 @@ def _rel(a: torch.Tensor, b: torch.Tensor) -> float:
     return float((a - b).norm() / (b.norm() + 1e-12))
 
 
-@pytest.mark.parametrize("ffn,masked,grouped", [("swiglu", False, False), ("gelu", True, False),
-                                                 ("swiglu", True, True)])
-def test_fused_block_matches_eager(ffn: str, masked: bool, grouped: bool) -> None:
+@pytest.mark.parametrize("ffn,masked,grouped,keep", [("swiglu", False, False, "none"), ("gelu", True, False, "none"),
+                                                      ("swiglu", True, True, "none"), ("swiglu", False, False, "all"),
+                                                      ("swiglu", True, True, "no_mlp"), ("gelu", True, False, "all")])
+def test_fused_block_matches_eager(ffn: str, masked: bool, grouped: bool, keep: str,
+                                   monkeypatch: pytest.MonkeyPatch) -> None:
+    """Forward and gradients against the CPU oracle, with the backward recomputing
+    the block ("none") or using what the forward kept ("all", "no_mlp")."""
+    monkeypatch.setenv("AVGEN_KEEP_ACTIVATIONS", keep)
     torch.manual_seed(0)
     width, heads, hidden, b, length, t = 256, 2, 512, 2, 384, 24
     block = DiTBlock(width, heads, hidden=hidden, ffn=ffn)

@@ -91,10 +91,10 @@ def _worker(rank: int, world: int, port: int, masked: bool) -> None:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("masked", [False, True])
-def test_ring_attention_two_gpus(masked: bool) -> None:
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs two GPUs")
+@pytest.mark.parametrize("world,masked", [(2, False), (2, True), (4, True)])
+def test_ring_attention_multi_gpu(world: int, masked: bool) -> None:
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(2, _free_port(), masked), nprocs=2, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), masked), nprocs=world, join=True)

@@ -1,7 +1,8 @@
-"""Fused ring attention over real NVLink peer memory: 2 ranks, one GPU each,
-CUDA IPC buffers, copy-engine pulls gated by stream memory operations, and the
-flash kernel gating each remote slab on its flag. Forward and backward must
-match attention over the whole sequence computed on one device."""
+"""Fused ring attention over real NVLink peer memory: 2 and 4 ranks, one GPU
+each, CUDA IPC buffers, copy-engine pulls (forward) and pushes (backward) with
+front-end flag writes, and the flash kernel gating each remote slab on its flag.
+Forward and backward must match attention over the whole sequence computed on
+one device, over three repeated steps (epochs, double-buffered receive buffers)."""
 from __future__ import annotations
 
 import math

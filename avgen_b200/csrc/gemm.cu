@@ -29,6 +29,7 @@
 // The accumulator is double buffered in TMEM (2 x BN fp32 columns) so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 #include "include/host_utils.h"
@@ -60,7 +61,9 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+// Epilogue warps per CTA: 4 (one per TMEM lane quadrant) or 8 (two per quadrant,
+// each taking half of a tile's columns); see epi_warps_setting.
+constexpr int threads_for(int epi_warps) { return 64 + 32 * epi_warps; }
 
 template <int BN>
 struct GemmCfg {
@@ -210,8 +213,8 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32, int EW>
+__global__ void __launch_bounds__(threads_for(EW), 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
@@ -241,7 +244,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 128);
+      mbar_init(&tempty[b], 32 * EW);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -363,7 +366,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    // Warps 2..: warp w reads TMEM lane quadrant w % 4 (the only lanes it may
+    // access) and the part (w - 2) / 4 of the tile's columns. The next 32-column
+    // chunk is loaded from TMEM while the current one is converted and stored.
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    constexpr int HALF = BN / (EW / 4);
     const int row_in_tile = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
@@ -374,15 +382,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       const int row = tm * kBM + row_in_tile;
-      const uint32_t t_row =
-          tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c, r);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                             static_cast<uint32_t>(acc * BN + half * HALF);
+      const int col_base = tn * BN + half * HALF;
+      uint32_t r[2][32];
+      tmem_ld32(t_row, r[0]);
+#pragma unroll
+      for (int c = 0; c < HALF / 32; ++c) {
         tmem_wait_ld();
-        if (row < args.M) epilogue_row<EPI, OUT_F32>(args, row, tn * BN + c, r);
+        if (c + 1 < HALF / 32) tmem_ld32(t_row + 32 * (c + 1), r[(c + 1) & 1]);
+        if (row < args.M) epilogue_row<EPI, OUT_F32>(args, row, col_base + 32 * c, r[c & 1]);
       }
+      tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
@@ -398,11 +409,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32>
-void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
-                 cudaStream_t stream, int num_sms) {
+// Epilogue warps. In isolation on B200 (65536-row GEMMs) eight warps cut the
+// SwiGLU-epilogue GEMM from 9.17 to 7.02 ms (N=20480, K=2560) and the fp32
+// atomic weight-gradient epilogue by ~5%, while the gated-residual epilogue
+// (per-row residual loads) ran 12% slower (0.894 -> 1.005 ms, N=2560, K=2560).
+// Inside the full training step, which runs at the 1 kW power cap, eight warps
+// measured 1-2% slower per step at equal clocks, so four is the default;
+// AVGEN_GEMM_EPI_WARPS=8 selects eight.
+inline int epi_warps_setting(int /*epi*/) {
+  static const int forced = [] {
+    const char* e = std::getenv("AVGEN_GEMM_EPI_WARPS");
+    return e == nullptr ? 0 : std::atoi(e);
+  }();
+  return forced == 8 ? 8 : 4;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32, int EW>
+void launch_gemm_ew(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+                    cudaStream_t stream, int num_sms) {
   using Cfg = GemmCfg<BN>;
-  auto kernel = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, OUT_F32>;
+  auto kernel = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, OUT_F32, EW>;
   static std::once_flag once;
   std::call_once(once, [&] {
     AVGEN_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -412,8 +438,17 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a
   const int num_n = (args.N + BN - 1) / BN;
   const int tiles = num_m * num_n * args.k_splits;
   const int grid = std::max(1, std::min(tiles, num_sms));
-  kernel<<<grid, kThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+  kernel<<<grid, threads_for(EW), Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
   AVGEN_CUDA_CHECK(cudaGetLastError());
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32>
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
+                 cudaStream_t stream, int num_sms) {
+  if (epi_warps_setting(EPI) == 4)
+    launch_gemm_ew<BN, A_MN, B_MN, EPI, OUT_F32, 4>(ta, tb, args, stream, num_sms);
+  else
+    launch_gemm_ew<BN, A_MN, B_MN, EPI, OUT_F32, 8>(ta, tb, args, stream, num_sms);
 }
 
 }  // namespace

@@ -4,6 +4,7 @@
     python -m avgen_b200.ops.bench gemm --m 16384 --n 7680 --k 2560
     python -m avgen_b200.ops.bench attention --L 4096 --H 37 --once   # one call each (for ncu -k/-c)
     python -m avgen_b200.ops.bench trace --L 16384 --H 20 --pass bwd   # SM-clock timeline of CTA 0
+    python -m avgen_b200.ops.bench ring --L 16384 --world 4          # one CP rank's ring attention, emulated
 
 Times come from CUDA events on the launching stream after warm-up, with a
 synchronize on both sides; each line also reports the library equivalent
@@ -96,7 +97,7 @@ def trace_attention(length: int, heads: int, which: str) -> None:
                   f"{t[i][4] - b:6d} {max(t[i][s] for s in range(16, 20)) - b:6d}")
 
 
-def bench_gemm(m: int, n: int, k: int, iters: int) -> None:
+def bench_gemm(m: int, n: int, k: int, iters: int, once: bool = False) -> None:
     from avgen_b200.ops import kernels as K
 
     a = torch.randn(m, k, device="cuda").bfloat16()
@@ -104,13 +105,72 @@ def bench_gemm(m: int, n: int, k: int, iters: int) -> None:
     dy = torch.randn(m, n, device="cuda").bfloat16()
     grad = torch.zeros(n, k, device="cuda")
     flops = 2.0 * m * n * k
+    if once:  # one launch of each (SwiGLU-epilogue forward, dX, dW) for a profiler
+        K.gemm(a, b, epilogue="swiglu", aux=torch.empty(m, n, device="cuda", dtype=torch.bfloat16))
+        K.linear_dx(dy, b)
+        K.linear_dw(dy, a, grad)
+        torch.cuda.synchronize()
+        return
+    aux = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+    resid = torch.randn(m, n, device="cuda").bfloat16()
+    gate = torch.randn(1, n, device="cuda")
     rows = [("fwd", lambda: K.gemm(a, b), lambda: a @ b.t()),
+            ("fwd+swiglu", lambda: K.gemm(a, b, epilogue="swiglu", aux=aux), lambda: a @ b.t()),
+            ("fwd+gate_resid", lambda: K.gemm(a, b, epilogue="gate_resid", resid=resid, gate=gate, rows_per_batch=m),
+             lambda: a @ b.t()),
             ("dx", lambda: K.linear_dx(dy, b), lambda: dy @ b),
             ("dw", lambda: K.linear_dw(dy, a, grad), lambda: dy.t() @ a)]
     for name, ours, lib in rows:
         t_o, t_l = _time(ours, iters), _time(lib, iters)
         print(f"gemm {m}x{n}x{k} {name}: {t_o:.3f} ms ({flops / t_o / 1e9:.0f} TF/s) | "
               f"cuBLAS {t_l:.3f} ms ({flops / t_l / 1e9:.0f} TF/s)")
+
+
+def bench_ring(length: int, heads: int, world: int, iters: int, once: bool) -> None:
+    """Ring-layout attention as one rank of a ``world``-way context-parallel group
+    sees it, emulated on one GPU: the kernels in ring mode (rotated slab order,
+    per-slab flag checks, per-slab backward launches) with every slab already
+    resident and its flag set. On one GPU the slab copies would be same-device
+    copies, which the driver may run as kernels that cannot start while the
+    attention kernel holds every SM; across GPUs they run on copy engines."""
+    from avgen_b200.ops import kernels as K
+    from avgen_b200.ops._ext import load
+
+    ext = load()
+    q = torch.randn(1, heads, length, 128, device="cuda").bfloat16()
+    src = torch.randn(2, world, 1, heads, length, 128, device="cuda").bfloat16()
+    k_all, v_all = torch.zeros_like(src[0]), torch.zeros_like(src[1])
+    flags = torch.zeros(world, dtype=torch.int32, device="cuda")
+    copy = torch.cuda.Stream()
+    slab = src[0, 0].numel() * 2
+    epoch = [0]
+
+    for r in range(world):
+        ext.p2p_copy(k_all[r].data_ptr(), src[0, r].data_ptr(), slab)
+        ext.p2p_copy(v_all[r].data_ptr(), src[1, r].data_ptr(), slab)
+    flags.fill_(1)
+    torch.cuda.synchronize()
+    del copy, epoch
+
+    def forward() -> tuple[torch.Tensor, torch.Tensor]:
+        return K.attention_fwd(q, k_all, v_all, ring_rank=0, ring_flags=flags, ring_epoch=1)
+
+    out, lse = forward()
+    dout = torch.randn_like(out)
+    order = list(range(1, world)) + [0]
+
+    def backward() -> object:
+        return K.attention_bwd_slabs(q, k_all, v_all, out, dout, lse, order=order)
+
+    if once:
+        forward()
+        backward()
+        torch.cuda.synchronize()
+        return
+    flops = 4.0 * heads * length * world * length * 128
+    t_f, t_b = _time(forward, iters), _time(backward, iters)
+    print(f"ring attention Lq={length} Lk={world}x{length} H={heads}: fwd {t_f:.3f} ms ({flops / t_f / 1e9:.0f} TF/s) "
+          f"| bwd ({world} launches) {t_b:.3f} ms ({2.5 * flops / t_b / 1e9:.0f} TF/s counted)")
 
 
 def main() -> None:
@@ -129,7 +189,13 @@ def main() -> None:
     g.add_argument("--m", type=int, default=16384)
     g.add_argument("--n", type=int, default=7680)
     g.add_argument("--k", type=int, default=2560)
-    for s in (a, g):
+    g.add_argument("--once", action="store_true")
+    r = sub.add_parser("ring")
+    r.add_argument("--L", type=int, default=4096, help="keys and queries per rank")
+    r.add_argument("--H", type=int, default=20)
+    r.add_argument("--world", type=int, default=4)
+    r.add_argument("--once", action="store_true")
+    for s in (a, g, r):
         s.add_argument("--iters", type=int, default=10)
     args = p.parse_args()
     if getattr(args, "bwd", None):
@@ -141,8 +207,10 @@ def main() -> None:
         bench_attention(args.L, args.H, args.iters, args.once)
     elif args.op == "trace":
         trace_attention(args.L, args.H, args.which)
+    elif args.op == "ring":
+        bench_ring(args.L, args.H, args.world, args.iters, args.once)
     else:
-        bench_gemm(args.m, args.n, args.k, args.iters)
+        bench_gemm(args.m, args.n, args.k, args.iters, args.once)
     from avgen_b200.ops._ext import check_errors
 
     code = check_errors()

@@ -706,6 +706,59 @@ void attn_bwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, con
   attn_bwd_launch(d, cur_stream());
 }
 
+// --------------------------------------------------------------------- sharded AdamW
+std::vector<const float*> addr_list(const std::vector<int64_t>& addrs) {
+  std::vector<const float*> out;
+  out.reserve(addrs.size());
+  for (int64_t a : addrs) out.push_back(reinterpret_cast<const float*>(a));
+  return out;
+}
+
+void shard_reduce(const std::vector<int64_t>& grads, int64_t lo, at::Tensor& out, at::Tensor& sq_acc) {
+  c10::cuda::CUDAGuard guard(out.device());
+  check_f32(out, "out");
+  check_f32(sq_acc, "sq_acc");
+  TORCH_CHECK(out.is_contiguous(), "shard_reduce: out must be contiguous");
+  const auto p = addr_list(grads);
+  shard_reduce_launch(p.data(), static_cast<int>(p.size()), lo, out.numel(), out.data_ptr<float>(),
+                      sq_acc.data_ptr<float>(), out.device().index(), cur_stream());
+}
+
+void shard_adamw_push(const std::vector<int64_t>& params, int64_t rank, int64_t lo, const at::Tensor& grad,
+                      at::Tensor& exp_avg, at::Tensor& exp_avg_sq, double lr, double beta1, double beta2, double eps,
+                      double weight_decay, int64_t step, const OptT& grad_scale, const OptT& skip) {
+  c10::cuda::CUDAGuard guard(grad.device());
+  check_f32(grad, "grad");
+  check_f32(exp_avg, "exp_avg");
+  check_f32(exp_avg_sq, "exp_avg_sq");
+  TORCH_CHECK(grad.numel() == exp_avg.numel() && grad.numel() == exp_avg_sq.numel() && grad.numel() % 4 == 0,
+              "shard_adamw_push: shard tensors must match and hold a multiple of 4 elements");
+  ShardAdamWDesc d;
+  d.device = grad.device().index();
+  d.rank = static_cast<int>(rank);
+  d.world = static_cast<int>(params.size());
+  TORCH_CHECK(d.rank >= 0 && d.rank < d.world, "shard_adamw_push: rank outside the parameter list");
+  d.lo = lo;
+  d.n4 = grad.numel() / 4;
+  d.grad = grad.data_ptr<float>();
+  d.exp_avg = exp_avg.data_ptr<float>();
+  d.exp_avg_sq = exp_avg_sq.data_ptr<float>();
+  d.lr = static_cast<float>(lr);
+  d.beta1 = static_cast<float>(beta1);
+  d.beta2 = static_cast<float>(beta2);
+  d.eps = static_cast<float>(eps);
+  d.weight_decay = static_cast<float>(weight_decay);
+  d.bias_correction1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  d.bias_correction2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  d.grad_scale = f32_or_null(grad_scale, "grad_scale");
+  if (has(skip)) {
+    TORCH_CHECK(skip->scalar_type() == at::kInt && skip->is_cuda(), "shard_adamw_push: skip must be int32 on device");
+    d.skip = skip->data_ptr<int>();
+  }
+  const auto p = addr_list(params);
+  shard_adamw_push_launch(d, p.data(), cur_stream());
+}
+
 // --------------------------------------------------------------------- peer memory
 int64_t p2p_alloc_py(int64_t bytes, int64_t device) {
   return reinterpret_cast<int64_t>(p2p_alloc(static_cast<size_t>(bytes), static_cast<int>(device)));
@@ -802,6 +855,10 @@ PYBIND11_MODULE(_C, m) {
   m.def("attn_fwd", &a::attn_fwd, arg("q"), arg("k"), arg("v"), arg("out"), arg("lse") = none, arg("kmask") = none,
         arg("scale") = 0.0, arg("trace") = none, arg("ring_rank") = 0, arg("ring_flags") = none,
         arg("ring_epoch") = 0);
+  m.def("shard_reduce", &a::shard_reduce, arg("grads"), arg("lo"), arg("out"), arg("sq_acc"));
+  m.def("shard_adamw_push", &a::shard_adamw_push, arg("params"), arg("rank"), arg("lo"), arg("grad"),
+        arg("exp_avg"), arg("exp_avg_sq"), arg("lr"), arg("beta1"), arg("beta2"), arg("eps"), arg("weight_decay"),
+        arg("step"), arg("grad_scale") = none, arg("skip") = none);
   m.def("p2p_alloc", &a::p2p_alloc_py, arg("bytes"), arg("device"));
   m.def("p2p_free", &a::p2p_free_py);
   m.def("p2p_export", &a::p2p_export_py);

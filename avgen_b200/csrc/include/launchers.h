@@ -315,4 +315,23 @@ void stream_write(cudaStream_t stream, void* flag, unsigned value);
 void p2p_copy(void* dst, const void* src, size_t bytes, cudaStream_t stream);
 void slab_sum_launch(const void* const* srcs_dev, int nsrc, void* dst, long n, int device, cudaStream_t stream);
 
+// Sharded AdamW over NVLink (zero.cu). grads / params: one flat fp32 buffer
+// address per rank (this rank's own included), valid on this device.
+void shard_reduce_launch(const float* const* grads, int world, long lo, long n, float* out, float* sq_acc, int device,
+                         cudaStream_t stream);
+struct ShardAdamWDesc {
+  int device = 0;
+  int rank = 0, world = 1;
+  long lo = 0;    // shard start (elements, multiple of 4)
+  long n4 = 0;    // shard length / 4
+  const float* grad = nullptr;  // reduced shard gradient [n]
+  float* exp_avg = nullptr;     // shard moments [n]
+  float* exp_avg_sq = nullptr;
+  float lr = 1e-4f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
+  float bias_correction1 = 1.f, bias_correction2_sqrt = 1.f;
+  const float* grad_scale = nullptr;
+  const int* skip = nullptr;
+};
+void shard_adamw_push_launch(const ShardAdamWDesc& d, const float* const* params, cudaStream_t stream);
+
 }  // namespace avgen

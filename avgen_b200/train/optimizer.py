@@ -26,7 +26,8 @@ import torch.distributed as dist
 from torch import nn
 from torch.optim import Optimizer
 
-__all__ = ["DEFAULT_NO_DECAY_PATTERNS", "FusedAdamW", "build_optimizer", "build_param_groups", "list_optimizers"]
+__all__ = ["DEFAULT_NO_DECAY_PATTERNS", "FusedAdamW", "ShardedAdamW", "build_optimizer", "build_param_groups",
+           "list_optimizers"]
 
 DEFAULT_NO_DECAY_PATTERNS: tuple[str, ...] = ("norm", "bias", "scale_shift", "embed")
 _OPTIMIZERS = ("adafactor", "adamw", "adamw_8bit")
@@ -214,6 +215,181 @@ class FusedAdamW(Optimizer):
         return loss
 
 
+class ShardedAdamW(FusedAdamW):
+    """AdamW with its moments sharded over a one-node data-parallel group, the
+    gradient reduce-scatter and the parameter all-gather done over NVLink peer
+    memory inside the optimizer kernels (ZeRO-style; the reference runs an NCCL
+    gradient reduction and a replicated AdamW, avgen/train/optimizer.py:198-205).
+
+    Every rank keeps the full fp32 parameters and gradients as flat buffers
+    mapped into every peer (CUDA IPC) and owns the contiguous shard
+    ``[rank * shard, (rank + 1) * shard)`` of each group's buffer. A step is:
+
+    1. a one-word all-reduce: every rank's gradients are complete;
+    2. ``shard_reduce``: this rank sums its shard of every peer's gradients over
+       NVLink (averaged) and accumulates the squared norm of the result;
+    3. an all-reduce of that scalar: the global gradient norm, and every pull done;
+    4. ``shard_adamw_push``: AdamW on the shard (clip coefficient and non-finite
+       skip on the device) storing each updated parameter into every rank's
+       buffer;
+    5. a one-word all-reduce: every push landed before the next forward.
+
+    Adam moments take ``1 / world`` of the memory of the replicated optimizer.
+    On CPU (gloo) the same steps run with collectives instead of peer memory.
+    """
+
+    def __init__(self, params: Iterable[Any], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.95),
+                 eps: float = 1e-8, weight_decay: float = 0.0, *, group: Any = None) -> None:
+        if not dist.is_initialized():
+            raise RuntimeError("ShardedAdamW needs an initialised process group")
+        self.shard_group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(self.shard_group)
+        self.rank = dist.get_rank(self.shard_group)
+        self._full_state: list[tuple[torch.Tensor, torch.Tensor]] | None = None
+        super().__init__(params, lr=lr, betas=betas, eps=eps, weight_decay=weight_decay, dp_group=None)
+
+    def _flatten(self, group: dict[str, Any]) -> dict[str, Any]:  # type: ignore[override]
+        params: list[torch.Tensor] = group["params"]
+        if not params:
+            raise ValueError("empty parameter group")
+        dev = params[0].device
+        offsets, total = [], 0
+        for p in params:
+            if p.device != dev:
+                raise ValueError("all parameters of a group must share a device")
+            offsets.append(total)
+            total += -(-p.numel() // _ALIGN) * _ALIGN
+        unit = self.world * _ALIGN
+        total = -(-total // unit) * unit
+        shard = total // self.world
+        out: dict[str, Any] = {"offsets": torch.tensor(offsets), "lo": self.rank * shard, "shard": shard}
+        if dev.type == "cuda":
+            from avgen_b200.parallel.symmetric import SymmetricBuffer
+
+            out["pbuf"] = SymmetricBuffer(total * 4, self.shard_group, dev)
+            out["gbuf"] = SymmetricBuffer(total * 4, self.shard_group, dev)
+            flat_p = out["pbuf"].view(self.rank, 0, (total,), torch.float32)
+            flat_g = out["gbuf"].view(self.rank, 0, (total,), torch.float32)
+        else:
+            flat_p = torch.zeros(total, dtype=torch.float32)
+            flat_g = torch.zeros(total, dtype=torch.float32)
+        with torch.no_grad():
+            for p, off in zip(params, offsets):
+                n = p.numel()
+                flat_p[off:off + n].copy_(p.detach().reshape(-1).float())
+                p.data = flat_p[off:off + n].view(p.shape)
+                p.grad = flat_g[off:off + n].view(p.shape)
+        out.update(param=flat_p, grad=flat_g, exp_avg=torch.zeros(shard, device=dev),
+                   exp_avg_sq=torch.zeros(shard, device=dev), reduced=torch.zeros(shard, device=dev))
+        return out
+
+    # ------------------------------------------------------------------ state (gathered for checkpoints)
+    def _gathered(self) -> list[tuple[torch.Tensor, torch.Tensor]]:
+        full = []
+        for flat in self._flat:
+            ms = []
+            for key in ("exp_avg", "exp_avg_sq"):
+                t = torch.empty(flat["shard"] * self.world, device=flat[key].device)
+                dist.all_gather_into_tensor(t, flat[key], group=self.shard_group)
+                ms.append(t)
+            full.append((ms[0], ms[1]))
+        return full
+
+    @property
+    def state(self) -> dict:  # type: ignore[override]
+        """Per-parameter views of the full moments, gathered over the group
+        (collective: every rank of the group reads it, e.g. through state_dict)."""
+        if not getattr(self, "_flat", None):
+            return {}
+        full = self._gathered()
+        out: dict = {}
+        for group, flat, (m, v) in zip(self.param_groups, self._flat, full):
+            for p, off in zip(group["params"], flat["offsets"].tolist()):
+                n = p.numel()
+                out[p] = {"step": torch.tensor(float(self._step)), "exp_avg": m[off:off + n].view(p.shape),
+                          "exp_avg_sq": v[off:off + n].view(p.shape)}
+        return out
+
+    @state.setter
+    def state(self, value: dict) -> None:
+        if not getattr(self, "_flat", None):
+            return
+        for group, flat in zip(self.param_groups, self._flat):
+            lo, hi = flat["lo"], flat["lo"] + flat["shard"]
+            for p, off in zip(group["params"], flat["offsets"].tolist()):
+                st = value.get(p)
+                if not st:
+                    continue
+                n = p.numel()
+                a, b = max(off, lo), min(off + n, hi)
+                if a < b:
+                    with torch.no_grad():
+                        flat["exp_avg"][a - lo:b - lo].copy_(st["exp_avg"].reshape(-1)[a - off:b - off])
+                        flat["exp_avg_sq"][a - lo:b - lo].copy_(st["exp_avg_sq"].reshape(-1)[a - off:b - off])
+                self._step = int(float(st.get("step", self._step)))
+
+    def sync_gradients(self) -> None:  # the reduction is part of the step
+        return
+
+    def _barrier(self, dev: torch.device) -> None:
+        token = torch.zeros(1, device=dev)
+        dist.all_reduce(token, group=self.shard_group)
+
+    @torch.no_grad()
+    def step(self, closure: Any = None, *, max_grad_norm: float | None = None) -> Any:
+        loss = closure() if closure is not None else None
+        from avgen_b200.models.linear import bump_weight_epoch
+
+        self._step += 1
+        dev = self._flat[0]["param"].device
+        cuda = dev.type == "cuda"
+        acc = torch.zeros(1, device=dev, dtype=torch.float32)
+        if cuda:
+            from avgen_b200.ops import kernels as K
+            from avgen_b200.ops._ext import load
+
+            ext = load()
+            self._barrier(dev)  # 1. every rank's gradients are complete
+            for flat in self._flat:  # 2. pull-reduce this rank's shard over NVLink
+                ext.shard_reduce(flat["gbuf"].ptrs, flat["lo"], flat["reduced"], acc)
+                K._count()
+        else:
+            for flat in self._flat:
+                full = flat["grad"].clone()
+                dist.all_reduce(full, group=self.shard_group)
+                flat["reduced"].copy_(full[flat["lo"]:flat["lo"] + flat["shard"]] / self.world)
+                acc += flat["reduced"].pow(2).sum()
+        dist.all_reduce(acc, group=self.shard_group)  # 3. global norm; every pull is done
+        norm = acc.sqrt()[0]
+        nonfinite = ~torch.isfinite(norm)
+        clip = max_grad_norm if max_grad_norm is not None else self.max_grad_norm
+        scale = torch.clamp(clip / (norm + 1e-6), max=1.0) if clip is not None else torch.ones_like(norm)
+        scale = torch.where(nonfinite, torch.zeros_like(scale), scale).reshape(1)
+        skip = nonfinite.to(torch.int32).reshape(1)
+        self.last_grad_norm = norm
+        self.last_nonfinite = nonfinite
+        for group, flat in zip(self.param_groups, self._flat):
+            b1, b2 = group["betas"]
+            if cuda:  # 4. AdamW on the shard, stored into every rank's parameters
+                ext.shard_adamw_push(flat["pbuf"].ptrs, self.rank, flat["lo"], flat["reduced"], flat["exp_avg"],
+                                     flat["exp_avg_sq"], group["lr"], b1, b2, group["eps"], group["weight_decay"],
+                                     self._step, scale, skip)
+                K._count()
+            else:
+                lo, n = flat["lo"], flat["shard"]
+                view = {"param": flat["param"][lo:lo + n], "grad": flat["reduced"], "exp_avg": flat["exp_avg"],
+                        "exp_avg_sq": flat["exp_avg_sq"]}
+                _adamw_reference(view, lr=group["lr"], beta1=b1, beta2=b2, eps=group["eps"],
+                                 weight_decay=group["weight_decay"], step=self._step, scale=scale,
+                                 nonfinite=nonfinite)
+                parts = list(flat["param"].view(self.world, n).unbind(0))
+                dist.all_gather(parts, flat["param"][lo:lo + n].clone(), group=self.shard_group)
+        if cuda:
+            self._barrier(dev)  # 5. every push landed
+        bump_weight_epoch()
+        return loss
+
+
 def _adamw_reference(flat: dict[str, torch.Tensor], *, lr: float, beta1: float, beta2: float, eps: float,
                      weight_decay: float, step: int, scale: torch.Tensor, nonfinite: torch.Tensor) -> None:
     """CPU fp32 AdamW over a flat buffer (same maths as the kernel)."""
@@ -228,7 +404,11 @@ def _adamw_reference(flat: dict[str, torch.Tensor], *, lr: float, beta1: float, 
 
 def build_optimizer(model: nn.Module, *, name: str = "adamw", lr: float, weight_decay: float = 0.0,
                     betas: tuple[float, float] = (0.9, 0.95), eps: float = 1e-8, fused: bool | None = None,
-                    no_decay_patterns: Sequence[str] = DEFAULT_NO_DECAY_PATTERNS, dp_group: Any = None) -> Optimizer:
+                    no_decay_patterns: Sequence[str] = DEFAULT_NO_DECAY_PATTERNS, dp_group: Any = None,
+                    shard_group: Any = None) -> Optimizer:
+    """``shard_group`` (a one-node process group): AdamW with moments sharded over
+    it and the gradient reduction / parameter all-gather over NVLink
+    (:class:`ShardedAdamW`) instead of ``dp_group``'s all-reduce."""
     if lr <= 0.0:
         raise ValueError(f"lr must be positive; got {lr!r}")
     if weight_decay < 0.0:
@@ -246,6 +426,8 @@ def build_optimizer(model: nn.Module, *, name: str = "adamw", lr: float, weight_
             # FSDP / tensor-parallel shards: per-shard updates; the flat-buffer kernel needs plain tensors
             return torch.optim.AdamW(groups, lr=lr, betas=betas, eps=eps, fused=on_cuda or None)
         use_fused = on_cuda if fused is None else fused
+        if shard_group is not None:
+            return ShardedAdamW(groups, lr=lr, betas=betas, eps=eps, group=shard_group)
         if use_fused:
             return FusedAdamW(groups, lr=lr, betas=betas, eps=eps, dp_group=dp_group)
         return torch.optim.AdamW(groups, lr=lr, betas=betas, eps=eps)

@@ -53,7 +53,7 @@ const int* groups_or_null(const OptT& g, long rows, const char* what) {
 // --------------------------------------------------------------------- GEMM
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epilogue,
           const OptT& bias, const OptT& resid, const OptT& gate, int64_t rows_per_batch, const OptT& aux,
-          int64_t k_splits, const OptT& groups) {
+          int64_t k_splits, const OptT& groups, const OptT& a2, const OptT& b2) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_cuda(out, "out");
@@ -115,6 +115,25 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     TORCH_CHECK(aux->size(0) == d.M && aux->size(1) == d.N, "gemm: aux must be bf16 [M, N]");
     d.aux = aux->data_ptr();
     d.ldaux = aux->stride(0);
+  }
+  if (has(a2) || has(b2)) {
+    // Appended reduction pair with the majorness of (a, b): D = [a | a2] . [b | b2]^T.
+    TORCH_CHECK(has(a2) && has(b2), "gemm: a2 and b2 go together");
+    check_bf16(*a2, "a2");
+    check_bf16(*b2, "b2");
+    check_rows(*a2, "a2");
+    check_rows(*b2, "b2");
+    const long m2 = a_mn ? a2->size(1) : a2->size(0);
+    const long k2a = a_mn ? a2->size(0) : a2->size(1);
+    const long n2 = b_mn ? b2->size(1) : b2->size(0);
+    const long k2b = b_mn ? b2->size(0) : b2->size(1);
+    TORCH_CHECK(m2 == d.M && n2 == d.N && k2a == k2b && k2a > 0, "gemm: appended pair must be a2 [M, K2] and b2 [N, K2]",
+                " in the majorness of a and b; got M=", m2, " N=", n2, " K2=", k2a, "/", k2b);
+    d.a2 = a2->data_ptr();
+    d.lda2 = a2->stride(0);
+    d.b2 = b2->data_ptr();
+    d.ldb2 = b2->stride(0);
+    d.K2 = static_cast<int>(k2a);
   }
   d.k_splits = static_cast<int>(std::max<int64_t>(1, k_splits));
   d.err = error_word(d.device);
@@ -820,7 +839,7 @@ PYBIND11_MODULE(_C, m) {
   m.doc() = "avgen_b200 sm_100a kernels";
   m.def("gemm", &a::gemm, arg("a"), arg("b"), arg("out"), arg("a_mn"), arg("b_mn"), arg("epilogue"),
         arg("bias") = none, arg("resid") = none, arg("gate") = none, arg("rows_per_batch") = 1, arg("aux") = none,
-        arg("k_splits") = 1, arg("groups") = none);
+        arg("k_splits") = 1, arg("groups") = none, arg("a2") = none, arg("b2") = none);
   m.def("rmsnorm_mod_fwd", &a::rmsnorm_mod_fwd, arg("x"), arg("y"), arg("rstd") = none, arg("w") = none,
         arg("scale") = none, arg("shift") = none, arg("rows_per_batch") = 1, arg("eps") = 1e-6,
         arg("groups") = none);

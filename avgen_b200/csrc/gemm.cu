@@ -28,6 +28,14 @@
 //               row), fused math, vector stores to global memory
 // The accumulator is double buffered in TMEM (2 x BN fp32 columns) so the
 // epilogue of tile i overlaps the MMAs of tile i+1.
+//
+// Appended reduction pair: an optional second operand pair (A2[M, K2], B2[N, K2],
+// same majorness as A and B) extends the reduction, D = [A | A2] . [B | B2]^T,
+// so a low-rank update accumulates into the same TMEM tile as the dense product.
+// This is how LoRA runs without a second pass over the output: forward
+// y = x W^T + (x A^T s) B^T and input gradient dx = dy W + (dy B) (s A), the
+// rank-r factors riding as K2 = r extra reduction columns (the reference adds
+// the two products in eager PyTorch, avgen/finetune/lora.py:692-715).
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -42,6 +50,7 @@ struct GemmArgs {
   int M, N, K;
   int k_splits;
   int kb_per_split;
+  int kb2;  // k-blocks of the appended pair, issued by the last split only
   void* out;
   long ldo;
   const float* bias;
@@ -216,7 +225,9 @@ __device__ __forceinline__ void drain_wait(uint64_t* bar, uint32_t parity) {
 template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32, int EW>
 __global__ void __launch_bounds__(threads_for(EW), 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmA2,
+                      const __grid_constant__ CUtensorMap tmB2, const GemmArgs args) {
   using Cfg = GemmCfg<BN>;
   constexpr int STAGES = Cfg::STAGES;
   extern __shared__ uint8_t smem_raw[];
@@ -252,6 +263,10 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
   if (warp == 0 && lane == 0) {
     prefetch_tmap(&tmA);
     prefetch_tmap(&tmB);
+    if (args.kb2 > 0) {
+      prefetch_tmap(&tmA2);
+      prefetch_tmap(&tmB2);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
@@ -275,7 +290,8 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
         tile_coords(t - split * tiles_mn, num_m, num_n, tm, tn);
         const int kb0 = split * args.kb_per_split;
         const int kb1 = min(num_kb, kb0 + args.kb_per_split);
-        for (int kb = kb0; kb < kb1; ++kb) {
+        const int kend = kb1 + (split == args.k_splits - 1 ? args.kb2 : 0);
+        for (int kb = kb0; kb < kend; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, args.err, kErrTimeoutProducer)) {
             aborted = true;
             break;
@@ -283,19 +299,24 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
           uint8_t* sa = smem + stage * Cfg::STAGE_BYTES;
           uint8_t* sb = sa + Cfg::A_BYTES;
           mbar_arrive_expect_tx(&full[stage], Cfg::STAGE_BYTES);
-          const int k0 = kb * kBK;
+          // Blocks past the first pair's reduction come from the appended pair
+          // (out-of-range K2 columns are zero-filled by TMA and count in full).
+          const bool second = kb >= num_kb;
+          const CUtensorMap* mapA = second ? &tmA2 : &tmA;
+          const CUtensorMap* mapB = second ? &tmB2 : &tmB;
+          const int k0 = (second ? kb - num_kb : kb) * kBK;
           if constexpr (!A_MN) {
-            tma_load_2d(sa, &tmA, &full[stage], k0, tm * kBM);
+            tma_load_2d(sa, mapA, &full[stage], k0, tm * kBM);
           } else {
-            tma_load_2d(sa, &tmA, &full[stage], tm * kBM, k0);
-            tma_load_2d(sa + 8192, &tmA, &full[stage], tm * kBM + 64, k0);
+            tma_load_2d(sa, mapA, &full[stage], tm * kBM, k0);
+            tma_load_2d(sa + 8192, mapA, &full[stage], tm * kBM + 64, k0);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(sb, &tmB, &full[stage], k0, tn * BN);
+            tma_load_2d(sb, mapB, &full[stage], k0, tn * BN);
           } else {
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j) {
-              tma_load_2d(sb + j * 8192, &tmB, &full[stage], tn * BN + 64 * j, k0);
+              tma_load_2d(sb + j * 8192, mapB, &full[stage], tn * BN + 64 * j, k0);
             }
           }
           ++issued;
@@ -330,10 +351,11 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
       const int split = t / tiles_mn;
       const int kb0 = split * args.kb_per_split;
       const int kb1 = min(num_kb, kb0 + args.kb_per_split);
+      const int kend = kb1 + (split == args.k_splits - 1 ? args.kb2 : 0);
       if (!mbar_wait(&tempty[acc], acc_phase ^ 1, abort_flag, args.err, kErrTimeoutMma)) break;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-      for (int kb = kb0; kb < kb1; ++kb) {
+      for (int kb = kb0; kb < kend; ++kb) {
         if (!mbar_wait(&full[stage], phase, abort_flag, args.err, kErrTimeoutMma)) {
           aborted = true;
           break;
@@ -425,8 +447,8 @@ inline int epi_warps_setting(int /*epi*/) {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32, int EW>
-void launch_gemm_ew(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
-                    cudaStream_t stream, int num_sms) {
+void launch_gemm_ew(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
+                    const CUtensorMap& tb2, const GemmArgs& args, cudaStream_t stream, int num_sms) {
   using Cfg = GemmCfg<BN>;
   auto kernel = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, OUT_F32, EW>;
   static std::once_flag once;
@@ -438,17 +460,17 @@ void launch_gemm_ew(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs
   const int num_n = (args.N + BN - 1) / BN;
   const int tiles = num_m * num_n * args.k_splits;
   const int grid = std::max(1, std::min(tiles, num_sms));
-  kernel<<<grid, threads_for(EW), Cfg::SMEM_BYTES, stream>>>(ta, tb, args);
+  kernel<<<grid, threads_for(EW), Cfg::SMEM_BYTES, stream>>>(ta, tb, ta2, tb2, args);
   AVGEN_CUDA_CHECK(cudaGetLastError());
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool OUT_F32>
-void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& args,
-                 cudaStream_t stream, int num_sms) {
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& ta2,
+                 const CUtensorMap& tb2, const GemmArgs& args, cudaStream_t stream, int num_sms) {
   if (epi_warps_setting(EPI) == 4)
-    launch_gemm_ew<BN, A_MN, B_MN, EPI, OUT_F32, 4>(ta, tb, args, stream, num_sms);
+    launch_gemm_ew<BN, A_MN, B_MN, EPI, OUT_F32, 4>(ta, tb, ta2, tb2, args, stream, num_sms);
   else
-    launch_gemm_ew<BN, A_MN, B_MN, EPI, OUT_F32, 8>(ta, tb, args, stream, num_sms);
+    launch_gemm_ew<BN, A_MN, B_MN, EPI, OUT_F32, 8>(ta, tb, ta2, tb2, args, stream, num_sms);
 }
 
 }  // namespace
@@ -499,13 +521,28 @@ void gemm_launch(const GemmDesc& d, cudaStream_t stream) {
   } else {
     tb = make_tmap_2d_bf16(d.b, N, K, d.ldb, 64, kBK);
   }
+  // Appended pair: same majorness as (A, B), reduction length K2.
+  CUtensorMap ta2 = ta, tb2 = tb;
+  args.kb2 = 0;
+  if (d.a2 != nullptr || d.b2 != nullptr) {
+    const int K2 = d.K2;
+    AVGEN_CHECK(d.a2 != nullptr && d.b2 != nullptr && K2 > 0, "gemm: the appended pair needs a2, b2 and K2 > 0");
+    AVGEN_CHECK((d.lda2 * 2) % 16 == 0 && (d.ldb2 * 2) % 16 == 0,
+                "gemm: appended operand row strides must be 16-byte aligned");
+    AVGEN_CHECK(reinterpret_cast<uintptr_t>(d.a2) % 16 == 0 && reinterpret_cast<uintptr_t>(d.b2) % 16 == 0,
+                "gemm: appended operands must be 16-byte aligned");
+    AVGEN_CHECK(a_mn || K2 % 8 == 0, "gemm: K2 of a K-major appended A must be a multiple of 8");
+    ta2 = !a_mn ? make_tmap_2d_bf16(d.a2, K2, M, d.lda2, kBK, kBM) : make_tmap_2d_bf16(d.a2, M, K2, d.lda2, 64, kBK);
+    tb2 = !b_mn ? make_tmap_2d_bf16(d.b2, K2, N, d.ldb2, kBK, BN) : make_tmap_2d_bf16(d.b2, N, K2, d.ldb2, 64, kBK);
+    args.kb2 = (K2 + kBK - 1) / kBK;
+  }
   const int sms = num_sms(d.device);
   const int epilogue = d.epilogue;
   const bool out_f32 = d.out_f32;
 
 #define AVGEN_GEMM_CASE(AMN, BMN, EPI, F32)                                  \
   if (a_mn == AMN && b_mn == BMN && epilogue == EPI && out_f32 == F32) {    \
-    launch_gemm<BN, AMN, BMN, EPI, F32>(ta, tb, args, stream, sms);         \
+    launch_gemm<BN, AMN, BMN, EPI, F32>(ta, tb, ta2, tb2, args, stream, sms); \
     return;                                                                  \
   }
   AVGEN_GEMM_CASE(false, false, kEpiStore, false)

@@ -41,6 +41,13 @@ struct GemmDesc {
   long ldaux = 0;
   int k_splits = 1;
   int* err = nullptr;
+  // Optional appended reduction pair: D = [A | a2] . [B | b2]^T, a2 [M, K2] and
+  // b2 [N, K2] with the majorness of a and b (K2 columns, row strides lda2/ldb2).
+  const void* a2 = nullptr;
+  long lda2 = 0;
+  const void* b2 = nullptr;
+  long ldb2 = 0;
+  int K2 = 0;
 };
 
 void gemm_launch(const GemmDesc& d, cudaStream_t stream);

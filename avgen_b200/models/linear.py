@@ -4,6 +4,10 @@
 (bf16 operands, fp32 accumulation, fp32 master weights cast once per optimizer
 step through :func:`bf16_weight`), and through ``F.linear`` on the CPU (the fp32
 oracle). Weight gradients accumulate in fp32 with the GEMM's atomic epilogue.
+
+A plain LoRA layer (no DoRA, not merged, no adapter dropout, rank a multiple of
+8) runs as one GEMM with an appended rank-r reduction pair instead of
+materialising ``W + s B A`` (see :class:`LoRAKernelLinear`).
 """
 from __future__ import annotations
 
@@ -11,7 +15,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
-__all__ = ["KernelLinear", "bf16_weight", "bump_weight_epoch", "linear", "weight_epoch"]
+__all__ = ["KernelLinear", "LoRAKernelLinear", "bf16_weight", "bump_weight_epoch", "linear", "weight_epoch"]
 
 _CACHE_ATTR = "_avgen_bf16_cache"
 _EPOCH = [0]
@@ -91,6 +95,71 @@ class KernelLinear(torch.autograd.Function):
         return dx, dw, db
 
 
+class LoRAKernelLinear(torch.autograd.Function):
+    """``y = x W^T + b + s (x A^T) B^T`` with the low-rank term appended to the dense GEMM.
+
+    Forward: ``t = x (s A)^T`` ([M, r]), then one GEMM over ``[x | t] . [W | B]^T``.
+    Backward: ``u = dy B`` ([M, r]); ``dx = [dy | u] . [W ; s A]`` in one GEMM;
+    ``dA = s u^T x`` and ``dB = dy^T t`` through the fp32 atomic epilogue; ``dW``
+    only when the base weight trains. The reference computes the base and adapter
+    products separately in eager PyTorch (avgen/finetune/lora.py:692-715).
+    """
+
+    @staticmethod
+    def forward(ctx, x, weight, bias, lora_a, lora_b, scaling):  # noqa: ANN001, ANN205
+        from avgen_b200.ops import kernels as K
+
+        shape = x.shape
+        x2 = x.reshape(-1, shape[-1]).to(torch.bfloat16).contiguous()
+        w = bf16_weight(weight)
+        sa = (lora_a.detach().float() * scaling).to(torch.bfloat16).contiguous()
+        bb = lora_b.detach().to(torch.bfloat16).contiguous()
+        t = K.gemm(x2, sa)
+        b = bias.detach().float().contiguous() if bias is not None else None
+        y = K.gemm(x2, w, bias=b, a2=t, b2=bb)
+        ctx.save_for_backward(x2, weight, t, sa, bb)
+        ctx.has_bias = bias is not None
+        ctx.in_dtype = x.dtype
+        ctx.shape = shape
+        ctx.scaling = scaling
+        ctx.ab_dtypes = (lora_a.dtype, lora_b.dtype)
+        return y.view(*shape[:-1], w.shape[0])
+
+    @staticmethod
+    def backward(ctx, dy):  # noqa: ANN001, ANN205
+        from avgen_b200.ops import kernels as K
+
+        x2, weight, t, sa, bb = ctx.saved_tensors
+        dy2 = dy.reshape(-1, dy.shape[-1]).to(torch.bfloat16).contiguous()
+        dx = dw = db = da = dbb = None
+        u = K.gemm(dy2, bb, b_mn=True)  # [M, r] = dy B
+        if ctx.needs_input_grad[0]:
+            dx = K.linear_dx(dy2, bf16_weight(weight), a2=u, b2=sa).view(*ctx.shape).to(ctx.in_dtype)
+        if ctx.needs_input_grad[1]:
+            dw = _weight_grad_buffer(weight)
+            K.linear_dw(dy2, x2, dw)
+            dw = dw.to(weight.dtype)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            db = dy2.float().sum(0)
+        if ctx.needs_input_grad[3]:
+            da = torch.zeros(sa.shape, device=dy.device, dtype=torch.float32)
+            K.linear_dw(u, x2, da)
+            da = (da * ctx.scaling).to(ctx.ab_dtypes[0])
+        if ctx.needs_input_grad[4]:
+            dbb = torch.zeros(bb.shape, device=dy.device, dtype=torch.float32)
+            K.linear_dw(dy2, t, dbb)
+            dbb = dbb.to(ctx.ab_dtypes[1])
+        return dx, dw, db, da, dbb, None
+
+
+def _lora_fusable(layer: nn.Module) -> bool:
+    """A plain LoRA adapter the appended-pair GEMM covers exactly."""
+    a = getattr(layer, "lora_a", None)
+    return (a is not None and getattr(layer, "lora_magnitude", None) is None and not getattr(layer, "merged", True)
+            and isinstance(getattr(layer, "lora_dropout", None), nn.Identity) and a.shape[0] % 8 == 0
+            and not _is_dtensor(a) and not _is_dtensor(layer.lora_b))
+
+
 def _kernel_ok(x: torch.Tensor, layer: nn.Linear) -> bool:
     return (x.device.type == "cuda" and layer.in_features % 8 == 0 and layer.out_features % 8 == 0
             and x.numel() > 0)
@@ -111,7 +180,10 @@ def linear(x: torch.Tensor, layer: nn.Linear) -> torch.Tensor:
     if _is_dtensor(layer.weight):
         return layer(x)
     adapted = getattr(layer, "adapted_weight", None)
-    if callable(adapted):  # LoRA / DoRA: one GEMM on the effective weight, autograd reaches the adapters
+    if callable(adapted):
+        if _kernel_ok(x, layer) and _lora_fusable(layer):  # plain LoRA: rank-r pair appended to the GEMM
+            return LoRAKernelLinear.apply(x, layer.weight, layer.bias, layer.lora_a, layer.lora_b, layer.scaling)
+        # DoRA, merged or dropout adapters: one GEMM on the effective weight, autograd reaches the adapters
         if _kernel_ok(x, layer):
             return KernelLinear.apply(x, adapted(), layer.bias)
         return layer(x)

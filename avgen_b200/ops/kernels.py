@@ -74,11 +74,15 @@ def gemm(
     aux: torch.Tensor | None = None,
     k_splits: int = 1,
     groups: torch.Tensor | None = None,
+    a2: torch.Tensor | None = None,
+    b2: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """tcgen05 GEMM with a fused epilogue (see ``csrc/gemm.cu``).
 
     ``gate`` rows are picked per output row by ``groups`` (int32, one entry per
-    row) when given, else by ``row // rows_per_batch``.
+    row) when given, else by ``row // rows_per_batch``. An appended pair
+    ``(a2, b2)``, laid out like ``(a, b)``, extends the reduction:
+    ``D = [a | a2] . [b | b2]^T`` in one accumulator.
     """
     m = a.shape[1] if a_mn else a.shape[0]
     n = b.shape[1] if b_mn else b.shape[0]
@@ -89,7 +93,7 @@ def gemm(
         else:
             out = torch.empty((m, cols), device=a.device, dtype=out_dtype)
     load().gemm(
-        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits, groups
+        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits, groups, a2, b2
     )
     _count()
     return out
@@ -100,9 +104,10 @@ def linear(x: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -
     return gemm(x, w, bias=bias)
 
 
-def linear_dx(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = _BF16) -> torch.Tensor:
-    """Input gradient ``dy[M, N] @ w[N, K]``."""
-    return gemm(dy, w, b_mn=True, out_dtype=out_dtype)
+def linear_dx(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = _BF16, *,
+              a2: torch.Tensor | None = None, b2: torch.Tensor | None = None) -> torch.Tensor:
+    """Input gradient ``dy[M, N] @ w[N, K]`` (``+ a2[M, R] @ b2[R, K]`` when given)."""
+    return gemm(dy, w, b_mn=True, out_dtype=out_dtype, a2=a2, b2=b2)
 
 
 def linear_dw(dy: torch.Tensor, x: torch.Tensor, grad: torch.Tensor, *, k_splits: int = 0) -> torch.Tensor:

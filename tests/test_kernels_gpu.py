@@ -564,3 +564,50 @@ def test_ring_attention_times_out_without_its_slab() -> None:
     torch.cuda.synchronize()
     assert torch.isfinite(out.float()).all()
     _errors_clear()
+
+
+@pytest.mark.parametrize("m,n,k,r", [(384, 512, 256, 16), (200, 264, 136, 8), (256, 256, 128, 72)])
+def test_gemm_appended_pair_and_fused_lora_linear(m: int, n: int, k: int, r: int) -> None:
+    """``[a | a2] . [b | b2]^T`` in one accumulator (K-major and dX layouts), and a
+    LoRA layer on that path matching the fp32 eager adapter, forward and backward."""
+    ops = _ops()
+    torch.manual_seed(11)
+    a = torch.randn(m, k, device=DEV).bfloat16()
+    b = torch.randn(n, k, device=DEV).bfloat16() * 0.1
+    a2 = torch.randn(m, r, device=DEV).bfloat16()
+    b2 = torch.randn(n, r, device=DEV).bfloat16() * 0.1
+    bias = torch.randn(n, device=DEV)
+    ref = a.float() @ b.float().t() + a2.float() @ b2.float().t() + bias
+    _close(ops.gemm(a, b, bias=bias, a2=a2, b2=b2), ref)
+    dy = torch.randn(m, n, device=DEV).bfloat16()
+    u = torch.randn(m, r, device=DEV).bfloat16()
+    sa = torch.randn(r, k, device=DEV).bfloat16() * 0.1
+    _close(ops.linear_dx(dy, b, a2=u, b2=sa), dy.float() @ b.float() + u.float() @ sa.float())
+    with pytest.raises(RuntimeError):
+        ops.gemm(a, b, a2=a2)  # a2 without b2
+
+    from avgen_b200.finetune.lora import LoRALinear
+    from avgen_b200.models.linear import _lora_fusable, linear
+
+    base = torch.nn.Linear(k, n, device=DEV)
+    layer = LoRALinear.from_linear(base, rank=r, alpha=2.0 * r)
+    with torch.no_grad():
+        layer.lora_b.normal_(0, 0.05)
+    layer.weight.requires_grad_(False)
+    assert _lora_fusable(layer)
+    x = torch.randn(2, m // 2, k, device=DEV, requires_grad=True)
+    g = torch.randn(2, m // 2, n, device=DEV)
+    y = linear(x.bfloat16(), layer)
+    y.float().backward(g)
+    got = (y.detach(), x.grad.clone(), layer.lora_a.grad.clone(), layer.lora_b.grad.clone())
+    xr = x.detach().clone().requires_grad_()
+    ar = layer.lora_a.detach().clone().requires_grad_()
+    br = layer.lora_b.detach().clone().requires_grad_()
+    yr = xr @ layer.weight.t() + layer.bias + (xr @ ar.t()) @ br.t() * layer.scaling
+    yr.backward(g)
+    _close(got[0], yr)
+    _close(got[1], xr.grad)
+    _close(got[2], ar.grad, rtol=3e-2, atol=3e-2)
+    _close(got[3], br.grad, rtol=3e-2, atol=3e-2)
+    assert layer.weight.grad is None
+    _errors_clear()

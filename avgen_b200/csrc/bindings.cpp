@@ -53,7 +53,8 @@ const int* groups_or_null(const OptT& g, long rows, const char* what) {
 // --------------------------------------------------------------------- GEMM
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, bool b_mn, int64_t epilogue,
           const OptT& bias, const OptT& resid, const OptT& gate, int64_t rows_per_batch, const OptT& aux,
-          int64_t k_splits, const OptT& groups, const OptT& a2, const OptT& b2) {
+          int64_t k_splits, const OptT& groups, const OptT& a2, const OptT& b2, const OptT& gate_flags,
+          int64_t gate_epoch, int64_t gate_operand, int64_t gate_chunk, int64_t gate_rank) {
   check_bf16(a, "a");
   check_bf16(b, "b");
   check_cuda(out, "out");
@@ -134,6 +135,19 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool a_mn, 
     d.b2 = b2->data_ptr();
     d.ldb2 = b2->stride(0);
     d.K2 = static_cast<int>(k2a);
+  }
+  if (has(gate_flags)) {
+    TORCH_CHECK(gate_flags->scalar_type() == at::kInt && gate_flags->is_cuda() && gate_flags->is_contiguous() &&
+                    gate_flags->device() == a.device(),
+                "gemm: gate_flags must be a contiguous int32 tensor on the GEMM's device");
+    const long extent = gate_operand == 1 ? d.M : d.N;
+    TORCH_CHECK(gate_chunk > 0 && gate_flags->numel() * gate_chunk >= extent,
+                "gemm: gate_flags needs one word per chunk of ", gate_chunk, " rows");
+    d.gate_flags = reinterpret_cast<const unsigned*>(gate_flags->data_ptr<int>());
+    d.gate_epoch = static_cast<unsigned>(gate_epoch);
+    d.gate_operand = static_cast<int>(gate_operand);
+    d.gate_chunk = static_cast<int>(gate_chunk);
+    d.gate_rank = static_cast<int>(gate_rank);
   }
   d.k_splits = static_cast<int>(std::max<int64_t>(1, k_splits));
   d.err = error_word(d.device);
@@ -839,7 +853,8 @@ PYBIND11_MODULE(_C, m) {
   m.doc() = "avgen_b200 sm_100a kernels";
   m.def("gemm", &a::gemm, arg("a"), arg("b"), arg("out"), arg("a_mn"), arg("b_mn"), arg("epilogue"),
         arg("bias") = none, arg("resid") = none, arg("gate") = none, arg("rows_per_batch") = 1, arg("aux") = none,
-        arg("k_splits") = 1, arg("groups") = none, arg("a2") = none, arg("b2") = none);
+        arg("k_splits") = 1, arg("groups") = none, arg("a2") = none, arg("b2") = none, arg("gate_flags") = none,
+        arg("gate_epoch") = 0, arg("gate_operand") = 0, arg("gate_chunk") = 0, arg("gate_rank") = 0);
   m.def("rmsnorm_mod_fwd", &a::rmsnorm_mod_fwd, arg("x"), arg("y"), arg("rstd") = none, arg("w") = none,
         arg("scale") = none, arg("shift") = none, arg("rows_per_batch") = 1, arg("eps") = 1e-6,
         arg("groups") = none);

@@ -36,6 +36,18 @@
 // y = x W^T + (x A^T s) B^T and input gradient dx = dy W + (dy B) (s A), the
 // rank-r factors riding as K2 = r extra reduction columns (the reference adds
 // the two products in eager PyTorch, avgen/finetune/lora.py:692-715).
+//
+// Gated operand (all-gather fused into the GEMM): the rows of A (M) or of B (N)
+// are split into equal chunks, chunk r arriving from rank r over NVLink while the
+// kernel runs. Before its first k-block of a tile, the producer waits (bounded,
+// acquire at system scope) until every chunk the tile touches has its flag at the
+// call's epoch; the copy stream writes that flag after the chunk's copy lands.
+// Tiles are rotated so this rank's own chunk is computed first, and peer chunks
+// follow in the order they are pulled, so each transfer hides behind the MMAs of
+// the chunks before it. This replaces the NCCL all-gather that precedes the
+// FSDP weight GEMM (avgen/parallel/fsdp.py:75-124) and the sequence-parallel
+// activation GEMM of tensor parallelism (avgen/parallel/tensor.py:112-128) in the
+// reference.
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -51,6 +63,12 @@ struct GemmArgs {
   int k_splits;
   int kb_per_split;
   int kb2;  // k-blocks of the appended pair, issued by the last split only
+  const unsigned* gate_flags;  // arrival word per chunk (nullptr: no gating)
+  unsigned gate_epoch;
+  int gate_operand;  // 1: chunks of A's rows (M), 2: chunks of B's rows (N)
+  int gate_chunk;    // rows per chunk
+  int gate_rank;     // this rank's chunk (never waited on)
+  int rot_m, rot_n;  // tile rotation that puts the own chunk first
   void* out;
   long ldo;
   const float* bias;
@@ -95,6 +113,12 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
   const int r = t - group * per_group;
   tm = first_m + r % gsize;
   tn = r / gsize;
+}
+
+__device__ __forceinline__ void rotated_coords(const GemmArgs& a, int t, int num_m, int num_n, int& tm, int& tn) {
+  tile_coords(t, num_m, num_n, tm, tn);
+  tm = (tm + a.rot_m) % num_m;
+  tn = (tn + a.rot_n) % num_n;
 }
 
 __device__ __forceinline__ float gelu_tanh(float x) {
@@ -284,10 +308,26 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
       uint32_t phase = 0;
       int issued = 0;
       bool aborted = false;
+      uint32_t ready = 0;  // chunks already seen at the epoch
       for (int t = blockIdx.x; t < num_tiles && !aborted; t += gridDim.x) {
         const int split = t / tiles_mn;
         int tm, tn;
-        tile_coords(t - split * tiles_mn, num_m, num_n, tm, tn);
+        rotated_coords(args, t - split * tiles_mn, num_m, num_n, tm, tn);
+        if (args.gate_flags != nullptr) {
+          // Wait for every chunk this tile reads (at most two for chunk >= tile).
+          const bool on_m = args.gate_operand == 1;
+          const int lo = on_m ? tm * kBM : tn * BN;
+          const int hi = min(on_m ? args.M : args.N, lo + (on_m ? kBM : BN)) - 1;
+          for (int c = lo / args.gate_chunk; c <= hi / args.gate_chunk && !aborted; ++c) {
+            if (c == args.gate_rank || ((ready >> c) & 1u)) continue;
+            if (!flag_wait_geq(args.gate_flags + c, args.gate_epoch, abort_flag, args.err, kErrTimeoutPeer)) {
+              aborted = true;
+            } else {
+              ready |= 1u << c;
+            }
+          }
+          if (aborted) break;
+        }
         const int kb0 = split * args.kb_per_split;
         const int kb1 = min(num_kb, kb0 + args.kb_per_split);
         const int kend = kb1 + (split == args.k_splits - 1 ? args.kb2 : 0);
@@ -400,7 +440,7 @@ __global__ void __launch_bounds__(threads_for(EW), 1)
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x) {
       const int split = t / tiles_mn;
       int tm, tn;
-      tile_coords(t - split * tiles_mn, num_m, num_n, tm, tn);
+      rotated_coords(args, t - split * tiles_mn, num_m, num_n, tm, tn);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, args.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
       const int row = tm * kBM + row_in_tile;
@@ -535,6 +575,22 @@ void gemm_launch(const GemmDesc& d, cudaStream_t stream) {
     ta2 = !a_mn ? make_tmap_2d_bf16(d.a2, K2, M, d.lda2, kBK, kBM) : make_tmap_2d_bf16(d.a2, M, K2, d.lda2, 64, kBK);
     tb2 = !b_mn ? make_tmap_2d_bf16(d.b2, K2, N, d.ldb2, kBK, BN) : make_tmap_2d_bf16(d.b2, N, K2, d.ldb2, 64, kBK);
     args.kb2 = (K2 + kBK - 1) / kBK;
+  }
+  args.gate_flags = nullptr;
+  args.rot_m = args.rot_n = 0;
+  if (d.gate_flags != nullptr) {
+    AVGEN_CHECK(d.gate_operand == 1 || d.gate_operand == 2, "gemm: gate_operand must be 1 (A rows) or 2 (B rows)");
+    const int extent = d.gate_operand == 1 ? M : N;
+    AVGEN_CHECK(d.gate_chunk > 0 && (extent + d.gate_chunk - 1) / d.gate_chunk <= 32,
+                "gemm: gated operand needs 1..32 chunks, got chunk ", d.gate_chunk, " of ", extent, " rows");
+    AVGEN_CHECK(d.gate_rank >= 0 && d.gate_rank * d.gate_chunk < extent, "gemm: gate_rank out of range");
+    args.gate_flags = d.gate_flags;
+    args.gate_epoch = d.gate_epoch;
+    args.gate_operand = d.gate_operand;
+    args.gate_chunk = d.gate_chunk;
+    args.gate_rank = d.gate_rank;
+    if (d.gate_operand == 1) args.rot_m = d.gate_rank * d.gate_chunk / kBM;
+    else args.rot_n = d.gate_rank * d.gate_chunk / BN;
   }
   const int sms = num_sms(d.device);
   const int epilogue = d.epilogue;

@@ -48,6 +48,13 @@ struct GemmDesc {
   const void* b2 = nullptr;
   long ldb2 = 0;
   int K2 = 0;
+  // Optional gated operand: rows of A (gate_operand 1) or of B (2) in chunks of
+  // gate_chunk; a tile touching chunk c != gate_rank waits for gate_flags[c] >= gate_epoch.
+  const unsigned* gate_flags = nullptr;
+  unsigned gate_epoch = 0;
+  int gate_operand = 0;
+  int gate_chunk = 0;
+  int gate_rank = 0;
 };
 
 void gemm_launch(const GemmDesc& d, cudaStream_t stream);

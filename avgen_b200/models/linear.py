@@ -5,11 +5,17 @@
 step through :func:`bf16_weight`), and through ``F.linear`` on the CPU (the fp32
 oracle). Weight gradients accumulate in fp32 with the GEMM's atomic epilogue.
 
-A plain LoRA layer (no DoRA, not merged, no adapter dropout, rank a multiple of
-8) runs as one GEMM with an appended rank-r reduction pair instead of
-materialising ``W + s B A`` (see :class:`LoRAKernelLinear`).
+With ``AVGEN_LORA_FUSED=1``, a plain LoRA layer (no DoRA, not merged, no
+adapter dropout, rank a multiple of 8) runs as one GEMM with an appended rank-r
+reduction pair instead of materialising ``W + s B A`` (see
+:class:`LoRAKernelLinear`). It is opt-in: a microbenchmark of it at 8192 rows
+ended in a host segmentation fault inside the GEMM launch of its backward whose
+cause is not yet found; by default LoRA layers run one GEMM on the effective
+weight.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.nn.functional as F
@@ -155,7 +161,8 @@ class LoRAKernelLinear(torch.autograd.Function):
 def _lora_fusable(layer: nn.Module) -> bool:
     """A plain LoRA adapter the appended-pair GEMM covers exactly."""
     a = getattr(layer, "lora_a", None)
-    return (a is not None and getattr(layer, "lora_magnitude", None) is None and not getattr(layer, "merged", True)
+    return (os.environ.get("AVGEN_LORA_FUSED", "0") == "1" and a is not None
+            and getattr(layer, "lora_magnitude", None) is None and not getattr(layer, "merged", True)
             and isinstance(getattr(layer, "lora_dropout", None), nn.Identity) and a.shape[0] % 8 == 0
             and not _is_dtensor(a) and not _is_dtensor(layer.lora_b))
 

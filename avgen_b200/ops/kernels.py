@@ -76,6 +76,11 @@ def gemm(
     groups: torch.Tensor | None = None,
     a2: torch.Tensor | None = None,
     b2: torch.Tensor | None = None,
+    gate_flags: torch.Tensor | None = None,
+    gate_epoch: int = 0,
+    gate_operand: str = "",
+    gate_chunk: int = 0,
+    gate_rank: int = 0,
 ) -> torch.Tensor:
     """tcgen05 GEMM with a fused epilogue (see ``csrc/gemm.cu``).
 
@@ -83,6 +88,12 @@ def gemm(
     row) when given, else by ``row // rows_per_batch``. An appended pair
     ``(a2, b2)``, laid out like ``(a, b)``, extends the reduction:
     ``D = [a | a2] . [b | b2]^T`` in one accumulator.
+
+    Gated operand (an all-gather fused into the GEMM): with ``gate_flags``, the
+    rows of ``a`` (``gate_operand="a"``, the M axis) or of ``b`` (``"b"``, the N
+    axis) form chunks of ``gate_chunk`` rows; a tile that reads chunk ``c`` other
+    than ``gate_rank`` first waits (bounded; error code 5 on timeout) until
+    ``gate_flags[c] >= gate_epoch``. Tiles of the own chunk run first.
     """
     m = a.shape[1] if a_mn else a.shape[0]
     n = b.shape[1] if b_mn else b.shape[0]
@@ -93,7 +104,8 @@ def gemm(
         else:
             out = torch.empty((m, cols), device=a.device, dtype=out_dtype)
     load().gemm(
-        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits, groups, a2, b2
+        a, b, out, a_mn, b_mn, EPILOGUES[epilogue], bias, resid, gate, rows_per_batch, aux, k_splits, groups, a2, b2,
+        gate_flags, gate_epoch, {"": 0, "a": 1, "b": 2}[gate_operand], gate_chunk, gate_rank,
     )
     _count()
     return out

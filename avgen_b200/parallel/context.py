@@ -268,8 +268,9 @@ class RingAttention:
             return
         if self.kv is not None:  # shape changed: every rank reallocates at the same call
             torch.cuda.synchronize(device)
-            dist.barrier(group=self.group, device_ids=[device.index])
-            self.kv.close()
+            bar = lambda: dist.barrier(group=self.group, device_ids=[device.index])  # noqa: E731
+            bar()
+            self.kv.close(barrier=bar)
         self.kv = SymmetricBuffer(2 * self.world * b * hk * length * d * 2, self.group, device)
         self.flags = torch.zeros(self.world, dtype=torch.int32, device=device)
         self._token = torch.zeros(1, dtype=torch.float32, device=device)

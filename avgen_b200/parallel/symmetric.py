@@ -73,13 +73,17 @@ class SymmetricBuffer:
     def address(self, rank: int, offset: int = 0) -> int:
         return self.ptrs[rank] + offset
 
-    def close(self) -> None:
+    def close(self, barrier: Any = None) -> None:
         """Unmap the peers and free this rank's buffer. Callers synchronise first so
-        that no peer still reads or writes it."""
+        that no peer still reads or writes it. With ``barrier`` (a callable run by
+        every rank), this rank frees its buffer only after every peer has unmapped
+        it, as CUDA IPC requires of an exported allocation."""
         if self._closed:
             return
         for r, p in enumerate(self.ptrs):
             if r != self.rank:
                 self.backend.p2p_close(p)
+        if barrier is not None:
+            barrier()
         self.backend.p2p_free(self.local)
         self._closed = True

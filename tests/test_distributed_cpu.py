@@ -273,3 +273,30 @@ def _sharded_optim_worker(rank: int, world: int) -> None:
 
 def test_sharded_adamw_matches_replicated() -> None:
     _spawn(_sharded_optim_worker)
+
+
+def _collective_gemm_worker(rank: int, world: int) -> None:
+    from avgen_b200.parallel.collective_gemm import AllGatherGemm, GemmReduceScatter
+
+    g = torch.Generator().manual_seed(3)
+    rows, cols, m, n = 4, 16, 6, 8
+    w_all = torch.randn(world * rows, cols, generator=g)
+    x = torch.randn(m, cols, generator=g)
+    ag = AllGatherGemm(dist.group.WORLD, rows, cols, "cpu", operand="b")
+    y, full = ag(w_all[rank * rows:(rank + 1) * rows], x)
+    torch.testing.assert_close(full, w_all)
+    torch.testing.assert_close(y, x @ w_all.t())
+    w = torch.randn(n, cols, generator=g)
+    sp = AllGatherGemm(dist.group.WORLD, rows, cols, "cpu", operand="a")
+    y, _ = sp(w_all[rank * rows:(rank + 1) * rows], w)
+    torch.testing.assert_close(y, w_all @ w.t())
+    # row-parallel: rank r holds columns [r*c, (r+1)*c) of the reduction axis
+    xs = torch.randn(world * rows, world * cols, generator=g)
+    ws = torch.randn(n, world * cols, generator=g)
+    rs = GemmReduceScatter(dist.group.WORLD, world * rows, n, "cpu")
+    part = rs(xs[:, rank * cols:(rank + 1) * cols], ws[:, rank * cols:(rank + 1) * cols])
+    torch.testing.assert_close(part, (xs @ ws.t())[rank * rows:(rank + 1) * rows], rtol=1e-4, atol=1e-4)
+
+
+def test_collective_gemms_match_unsharded() -> None:
+    _spawn(_collective_gemm_worker)

@@ -102,6 +102,8 @@ def _worker(rank: int, world: int, port: int) -> None:
             print(f"\n[collective-gemm world={world} M={m} N={n} K={k}] ms (max over ranks): "
                   f"fused AG+GEMM {times[0]:.3f}  NCCL AG + GEMM {times[1]:.3f}  GEMM alone {times[2]:.3f}  "
                   f"fused GEMM+RS {times[3]:.3f}  GEMM + NCCL RS {times[4]:.3f}", flush=True)
+        for prim in (ag, sp, rs):  # no write ran past a symmetric buffer's bounds
+            assert not prim.buf.check_guards(), f"rank {rank}: guard bytes changed"
         ag.close()
         sp.close()
         rs.close()

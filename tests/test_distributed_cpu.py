@@ -300,3 +300,41 @@ def _collective_gemm_worker(rank: int, world: int) -> None:
 
 def test_collective_gemms_match_unsharded() -> None:
     _spawn(_collective_gemm_worker)
+
+
+class _ViewablePeerMemory(_FakePeerMemory):
+    """The fake backend with ``tensor_at`` over host bytes, so guard regions exist."""
+
+    def __init__(self, rank: int) -> None:
+        super().__init__(rank)
+        self.store = torch.zeros(1 << 16, dtype=torch.uint8)
+
+    def tensor_at(self, ptr: int, sizes: list[int], dtype: torch.dtype, device: int) -> torch.Tensor:
+        off = ptr - ((self.rank + 1) << 40)
+        n = 1
+        for s_ in sizes:
+            n *= s_
+        item = torch.empty((), dtype=dtype).element_size()
+        return self.store[off:off + n * item].view(dtype).view(sizes)
+
+
+def _guard_worker(rank: int, world: int) -> None:
+    from avgen_b200.parallel.symmetric import GUARD_PATTERN, SymmetricBuffer
+
+    fake = _ViewablePeerMemory(rank)
+    buf = SymmetricBuffer(1024, dist.group.WORLD, torch.device("cpu"), backend=fake, guard=256)
+    assert buf.ptrs[rank] == ((rank + 1) << 40) + 256  # the usable region follows the head guard
+    assert int(fake.store[0]) == GUARD_PATTERN and int(fake.store[256 + 1024 + 255]) == GUARD_PATTERN
+    buf.view(rank, 0, (256,), torch.float32).fill_(1.0)  # a full in-bounds write leaves the guards intact
+    assert buf.check_guards() == []
+    fake.store[256 + 1024 + 3] = 0  # one byte past the end
+    fake.store[255] = 7  # one byte before the start
+    assert buf.check_guards() == [("head", 255), ("tail", 3)]
+    buf.close()
+    peer = 1 - rank
+    assert fake.freed == [(rank + 1) << 40]  # the allocation base, guards included
+    assert fake.closed == [((peer + 1) << 40) + (1 << 20)]  # the peer's mapping base, not its usable start
+
+
+def test_symmetric_buffer_guards_catch_out_of_bounds_writes() -> None:
+    _spawn(_guard_worker)

@@ -62,6 +62,9 @@ def _worker(rank: int, world: int, port: int, masked: bool) -> None:
             dq, dk, dv = impl.backward(q, kb, vb, out, do_all[rank].to(dev), lse, packed, scale, state)
             torch.cuda.synchronize()
             assert check_errors(dev) == 0, "a bounded wait timed out"
+        assert not impl.kv.check_guards(), f"rank {rank}: K/V buffer guard bytes changed"
+        for buf in RingAttention._recv_pool.values():  # pushed dK/dV partials stayed in bounds
+            assert not buf.check_guards(), f"rank {rank}: receive buffer guard bytes changed"
         # reference on this device: the whole sequence
         kf = k_all.permute(1, 2, 0, 3, 4).reshape(b, hk, world * length, d).float().to(dev).requires_grad_()
         vf = v_all.permute(1, 2, 0, 3, 4).reshape(b, hk, world * length, d).float().to(dev).requires_grad_()

@@ -52,6 +52,8 @@ def _worker(rank: int, world: int, port: int) -> None:
         for a, b in zip(ref.parameters(), sharded.parameters()):
             torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(o_ref.last_grad_norm, o_sh.last_grad_norm, rtol=1e-4, atol=1e-6)
+        for flat in o_sh._flat:  # the peer pulls and pushes stayed inside the symmetric buffers
+            assert not flat["pbuf"].check_guards() and not flat["gbuf"].check_guards()
         st_ref, st_sh = o_ref.state, o_sh.state
         for p_ref, p_sh in zip(ref.parameters(), sharded.parameters()):
             torch.testing.assert_close(st_ref[p_ref]["exp_avg"], st_sh[p_sh]["exp_avg"], rtol=1e-5, atol=1e-8)

@@ -119,3 +119,68 @@ def test_collective_gemms_multi_gpu(world: int) -> None:
     import torch.multiprocessing as mp
 
     mp.spawn(_worker, args=(world, _free_port()), nprocs=world, join=True)
+
+
+def _sp_worker(rank: int, world: int, port: int) -> None:
+    """A sequence-parallel MLP (column-parallel up with the token all-gather fused,
+    row-parallel down with the reduce-scatter fused) against the unsharded MLP."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        import torch.nn.functional as F
+
+        from avgen_b200.ops._ext import check_errors
+        from avgen_b200.parallel.sequence import _POOL, sp_column_linear, sp_row_linear
+
+        g = torch.Generator().manual_seed(1)
+        t, k, f = 4096, 1024, 2048
+        x = torch.randn(t, k, generator=g).to(dev)
+        w1 = (torch.randn(f, k, generator=g) * 0.03).to(dev)
+        w2 = (torch.randn(k, f, generator=g) * 0.03).to(dev)
+        up = torch.randn(t, k, generator=g).to(dev)
+        ref = [p.clone().requires_grad_() for p in (x, w1, w2)]
+        y_ref = F.linear(F.gelu(F.linear(ref[0], ref[1])), ref[2])
+        (y_ref * up).sum().backward()
+        tl, fl = t // world, f // world
+        rows, cols = slice(rank * tl, (rank + 1) * tl), slice(rank * fl, (rank + 1) * fl)
+        xs = x[rows].clone().requires_grad_()
+        w1s = w1[cols].clone().requires_grad_()
+        w2s = w2[:, cols].contiguous().requires_grad_()
+        for _ in range(2):  # repeated steps reuse the pooled symmetric buffers
+            for p in (xs, w1s, w2s):
+                p.grad = None
+            y = sp_row_linear(F.gelu(sp_column_linear(xs, w1s, None, dist.group.WORLD).float()), w2s, None,
+                              dist.group.WORLD)
+            (y.float() * up[rows]).sum().backward()
+        torch.cuda.synchronize()
+        assert check_errors(dev) == 0
+
+        def close(a: torch.Tensor, r: torch.Tensor, tol: float = 3e-2) -> None:
+            err = (a.float() - r.float()).abs().max().item()
+            assert err <= tol * (1 + r.abs().max().item()), f"rank {rank}: max err {err}"
+
+        close(y, y_ref[rows])
+        close(xs.grad, ref[0].grad[rows])
+        close(w1s.grad, ref[1].grad[cols])
+        close(w2s.grad, ref[2].grad[:, cols])
+        for prim in _POOL.values():
+            assert not prim.buf.check_guards()
+            prim.close()
+    finally:
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+
+
+def test_sequence_parallel_mlp_multi_gpu() -> None:
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+
+    mp.spawn(_sp_worker, args=(2, _free_port()), nprocs=2, join=True)

@@ -338,3 +338,41 @@ def _guard_worker(rank: int, world: int) -> None:
 
 def test_symmetric_buffer_guards_catch_out_of_bounds_writes() -> None:
     _spawn(_guard_worker)
+
+
+def _sequence_parallel_worker(rank: int, world: int) -> None:
+    from avgen_b200.parallel.sequence import sp_column_linear, sp_row_linear
+
+    g = torch.Generator().manual_seed(7)
+    t, k, f = 8, 16, 12
+    x = torch.randn(t, k, generator=g)
+    w1, b1 = torch.randn(f, k, generator=g) * 0.3, torch.randn(f, generator=g)
+    w2, b2 = torch.randn(k, f, generator=g) * 0.3, torch.randn(k, generator=g)
+    up = torch.randn(t, k, generator=g)
+    # unsharded reference MLP
+    ref = [p.clone().requires_grad_() for p in (x, w1, b1, w2, b2)]
+    y_ref = torch.nn.functional.linear(torch.nn.functional.gelu(torch.nn.functional.linear(ref[0], ref[1], ref[2])),
+                                       ref[3], ref[4])
+    (y_ref * up).sum().backward()
+    # sequence parallel: tokens sharded, first weight by rows, second by columns
+    tl, fl = t // world, f // world
+    rows, cols = slice(rank * tl, (rank + 1) * tl), slice(rank * fl, (rank + 1) * fl)
+    xs = x[rows].clone().requires_grad_()
+    w1s, b1s = w1[cols].clone().requires_grad_(), b1[cols].clone().requires_grad_()
+    w2s, b2s = w2[:, cols].clone().requires_grad_(), b2.clone().requires_grad_()
+    h = sp_column_linear(xs, w1s, b1s, dist.group.WORLD)
+    assert h.shape == (t, fl)
+    y = sp_row_linear(torch.nn.functional.gelu(h), w2s, b2s, dist.group.WORLD)
+    assert y.shape == (tl, k)
+    (y * up[rows]).sum().backward()
+    close = dict(rtol=1e-4, atol=1e-5)
+    torch.testing.assert_close(y, y_ref[rows].detach(), **close)
+    torch.testing.assert_close(xs.grad, ref[0].grad[rows], **close)
+    torch.testing.assert_close(w1s.grad, ref[1].grad[cols], **close)
+    torch.testing.assert_close(b1s.grad, ref[2].grad[cols], **close)
+    torch.testing.assert_close(w2s.grad, ref[3].grad[:, cols], **close)
+    torch.testing.assert_close(b2s.grad, ref[4].grad, **close)
+
+
+def test_sequence_parallel_mlp_matches_unsharded() -> None:
+    _spawn(_sequence_parallel_worker)

@@ -2,6 +2,7 @@
 
     python -m avgen_b200.ops.bench attention --L 16384 --H 20 [--bwd split]
     python -m avgen_b200.ops.bench gemm --m 16384 --n 7680 --k 2560
+    python -m avgen_b200.ops.bench gemm --m 16384 --n 7680 --k 2560 --gated 4   # all-gather gating on, flags set
     python -m avgen_b200.ops.bench attention --L 4096 --H 37 --once   # one call each (for ncu -k/-c)
     python -m avgen_b200.ops.bench trace --L 16384 --H 20 --pass bwd   # SM-clock timeline of CTA 0
     python -m avgen_b200.ops.bench ring --L 16384 --world 4          # one CP rank's ring attention, emulated
@@ -97,8 +98,12 @@ def trace_attention(length: int, heads: int, which: str) -> None:
                   f"{t[i][4] - b:6d} {max(t[i][s] for s in range(16, 20)) - b:6d}")
 
 
-def bench_gemm(m: int, n: int, k: int, iters: int, once: bool = False) -> None:
+def bench_gemm(m: int, n: int, k: int, iters: int, once: bool = False, gated: int = 0) -> None:
     from avgen_b200.ops import kernels as K
+
+    if gated:
+        bench_gemm_gated(m, n, k, iters, once, gated)
+        return
 
     a = torch.randn(m, k, device="cuda").bfloat16()
     b = torch.randn(n, k, device="cuda").bfloat16()
@@ -124,6 +129,26 @@ def bench_gemm(m: int, n: int, k: int, iters: int, once: bool = False) -> None:
         t_o, t_l = _time(ours, iters), _time(lib, iters)
         print(f"gemm {m}x{n}x{k} {name}: {t_o:.3f} ms ({flops / t_o / 1e9:.0f} TF/s) | "
               f"cuBLAS {t_l:.3f} ms ({flops / t_l / 1e9:.0f} TF/s)")
+
+
+def bench_gemm_gated(m: int, n: int, k: int, iters: int, once: bool, world: int) -> None:
+    """The GEMM in gated-operand mode as one rank of a ``world``-way all-gather:
+    B's rows in ``world`` chunks whose arrival flags are already set, so the
+    difference to the plain GEMM is the cost of the rotation and the flag checks."""
+    from avgen_b200.ops import kernels as K
+
+    a = torch.randn(m, k, device="cuda").bfloat16()
+    b = torch.randn(n, k, device="cuda").bfloat16()
+    flags = torch.ones(world, dtype=torch.int32, device="cuda")
+    gated = dict(gate_flags=flags, gate_epoch=1, gate_operand="b", gate_chunk=-(-n // world), gate_rank=world // 2)
+    if once:
+        K.gemm(a, b, **gated)
+        torch.cuda.synchronize()
+        return
+    flops = 2.0 * m * n * k
+    for name, fn in (("fwd", lambda: K.gemm(a, b)), (f"fwd gated {world} chunks", lambda: K.gemm(a, b, **gated))):
+        t = _time(fn, iters)
+        print(f"gemm {m}x{n}x{k} {name}: {t:.3f} ms ({flops / t / 1e9:.0f} TF/s)")
 
 
 def bench_ring(length: int, heads: int, world: int, iters: int, once: bool) -> None:
@@ -190,6 +215,7 @@ def main() -> None:
     g.add_argument("--n", type=int, default=7680)
     g.add_argument("--k", type=int, default=2560)
     g.add_argument("--once", action="store_true")
+    g.add_argument("--gated", type=int, default=0, help="chunks of a gated (all-gathered) B operand")
     r = sub.add_parser("ring")
     r.add_argument("--L", type=int, default=4096, help="keys and queries per rank")
     r.add_argument("--H", type=int, default=20)
@@ -210,7 +236,7 @@ def main() -> None:
     elif args.op == "ring":
         bench_ring(args.L, args.H, args.world, args.iters, args.once)
     else:
-        bench_gemm(args.m, args.n, args.k, args.iters, args.once)
+        bench_gemm(args.m, args.n, args.k, args.iters, args.once, args.gated)
     from avgen_b200.ops._ext import check_errors
 
     code = check_errors()

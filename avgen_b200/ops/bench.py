@@ -6,6 +6,7 @@
     python -m avgen_b200.ops.bench attention --L 4096 --H 37 --once   # one call each (for ncu -k/-c)
     python -m avgen_b200.ops.bench trace --L 16384 --H 20 --pass bwd   # SM-clock timeline of CTA 0
     python -m avgen_b200.ops.bench ring --L 16384 --world 4          # one CP rank's ring attention, emulated
+    python -m avgen_b200.ops.bench zero --numel 268435456            # sharded AdamW step on a one-rank group
 
 Times come from CUDA events on the launching stream after warm-up, with a
 synchronize on both sides; each line also reports the library equivalent
@@ -151,6 +152,44 @@ def bench_gemm_gated(m: int, n: int, k: int, iters: int, once: bool, world: int)
         print(f"gemm {m}x{n}x{k} {name}: {t:.3f} ms ({flops / t / 1e9:.0f} TF/s)")
 
 
+def bench_zero(numel: int, iters: int, once: bool) -> None:
+    """One optimizer step over ``numel`` fp32 parameters: :class:`ShardedAdamW` on a
+    one-rank NCCL group (the gradient pull-reduce kernel, the norm all-reduce and
+    the AdamW-with-push kernel, with no peer traffic) against the replicated
+    :class:`FusedAdamW`. Bandwidth counts the bytes each must move: 36 B per
+    parameter sharded (gradient read, reduced shard written and read, parameter
+    and both moments read and written), 32 B replicated (gradient read by the norm
+    and the update, parameter and both moments read and written)."""
+    import socket
+
+    import torch.distributed as dist
+
+    from avgen_b200.train.optimizer import FusedAdamW, ShardedAdamW
+
+    if not dist.is_initialized():
+        with socket.socket() as sock:
+            sock.bind(("127.0.0.1", 0))
+            port = sock.getsockname()[1]
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        os.environ.setdefault("MASTER_PORT", str(port))
+        dist.init_process_group("nccl", rank=0, world_size=1, device_id=torch.device("cuda", 0))
+    p = torch.nn.Parameter(torch.randn(numel, device="cuda"))
+    o_sh = ShardedAdamW([p], lr=1e-4, weight_decay=0.1)
+    p.grad.normal_()
+    if once:
+        o_sh.step(max_grad_norm=1.0)
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+        return
+    q = torch.nn.Parameter(p.detach().clone())
+    o_f = FusedAdamW([q], lr=1e-4, weight_decay=0.1)
+    q.grad.normal_()
+    for name, opt, per in (("sharded (1 rank)", o_sh, 36), ("replicated", o_f, 32)):
+        t = _time(lambda opt=opt: opt.step(max_grad_norm=1.0), iters)
+        print(f"adamw step {numel} params {name}: {t:.3f} ms ({per * numel / t / 1e9:.0f} GB/s)")
+    dist.destroy_process_group()
+
+
 def bench_ring(length: int, heads: int, world: int, iters: int, once: bool) -> None:
     """Ring-layout attention as one rank of a ``world``-way context-parallel group
     sees it, emulated on one GPU: the kernels in ring mode (rotated slab order,
@@ -221,7 +260,10 @@ def main() -> None:
     r.add_argument("--H", type=int, default=20)
     r.add_argument("--world", type=int, default=4)
     r.add_argument("--once", action="store_true")
-    for s in (a, g, r):
+    z = sub.add_parser("zero")
+    z.add_argument("--numel", type=int, default=268435456)
+    z.add_argument("--once", action="store_true")
+    for s in (a, g, r, z):
         s.add_argument("--iters", type=int, default=10)
     args = p.parse_args()
     if getattr(args, "bwd", None):
@@ -235,6 +277,8 @@ def main() -> None:
         trace_attention(args.L, args.H, args.which)
     elif args.op == "ring":
         bench_ring(args.L, args.H, args.world, args.iters, args.once)
+    elif args.op == "zero":
+        bench_zero(args.numel, args.iters, args.once)
     else:
         bench_gemm(args.m, args.n, args.k, args.iters, args.once, args.gated)
     from avgen_b200.ops._ext import check_errors

@@ -186,7 +186,7 @@ def bench_zero(numel: int, iters: int, once: bool) -> None:
     q.grad.normal_()
     for name, opt, per in (("sharded (1 rank)", o_sh, 36), ("replicated", o_f, 32)):
         t = _time(lambda opt=opt: opt.step(max_grad_norm=1.0), iters)
-        print(f"adamw step {numel} params {name}: {t:.3f} ms ({per * numel / t / 1e9:.0f} GB/s)")
+        print(f"adamw step {numel} params {name}: {t:.3f} ms ({per * numel / (t * 1e-3) / 1e9:.0f} GB/s)")
     dist.destroy_process_group()
 
 

@@ -376,3 +376,27 @@ def _sequence_parallel_worker(rank: int, world: int) -> None:
 
 def test_sequence_parallel_mlp_matches_unsharded() -> None:
     _spawn(_sequence_parallel_worker)
+
+
+def _sp_validation_worker(rank: int, world: int) -> None:
+    from avgen_b200.parallel.collective_gemm import AllGatherGemm, GemmReduceScatter
+    from avgen_b200.parallel.sequence import sp_column_linear, sp_row_linear
+
+    g = dist.group.WORLD
+    with pytest.raises(ValueError):
+        sp_column_linear(torch.zeros(1, 4, 8), torch.zeros(8, 8), None, g)  # needs [tokens, features]
+    with pytest.raises(ValueError):
+        sp_row_linear(torch.zeros(3, 8), torch.zeros(8, 8), None, g)  # 3 tokens do not split over 2 ranks
+    with pytest.raises(ValueError):
+        AllGatherGemm(g, 4, 12, "cpu")  # feature count must be a multiple of 8
+    with pytest.raises(ValueError):
+        AllGatherGemm(g, 4, 16, "cpu", operand="c")
+    with pytest.raises(ValueError):
+        GemmReduceScatter(g, 5, 16, "cpu")  # rows must split evenly
+    ag = AllGatherGemm(g, 4, 16, "cpu")
+    with pytest.raises(ValueError):
+        ag.gather(torch.zeros(3, 16))  # wrong shard shape
+
+
+def test_sequence_parallel_argument_checks() -> None:
+    _spawn(_sp_validation_worker)

@@ -12,7 +12,7 @@ import importlib
 from typing import Any
 
 from avgen_b200.core import (ConditionMode, GridPatchifier, MediaBatch, MediaBatchSpec, ModelInput, ModelOutput,
-                             PatchLayout, RNGStreams, StepMetrics, TextContext, TokenStream, TrainState)
+                             PatchLayout, Patchifier, RNGStreams, StepMetrics, TextContext, TokenStream, TrainState)
 
 __version__ = "0.1.0"
 
@@ -26,8 +26,15 @@ _LAZY: dict[str, str] = {
     "AVDiTConfig": "avgen_b200.models",
     "ParallelDims": "avgen_b200.parallel",
     "init_distributed": "avgen_b200.parallel",
+    "shutdown_distributed": "avgen_b200.parallel",
+    "DistributedEnv": "avgen_b200.parallel",
     "parallelize": "avgen_b200.parallel",
     "ParallelConfig": "avgen_b200.parallel",
+    "ParallelModel": "avgen_b200.parallel",
+    "ActivationCheckpointConfig": "avgen_b200.parallel",
+    "FSDPConfig": "avgen_b200.parallel",
+    "PrecisionConfig": "avgen_b200.parallel",
+    "PipelineConfig": "avgen_b200.parallel",
     "load_config": "avgen_b200.config",
     "RunConfig": "avgen_b200.config",
     "FlowMatchingObjective": "avgen_b200.train",
@@ -38,15 +45,19 @@ _LAZY: dict[str, str] = {
     "build_sampler": "avgen_b200.infer",
     "CheckpointManager": "avgen_b200.checkpoint",
     "simulate_config": "avgen_b200.simulate",
+    "SimulationReport": "avgen_b200.simulate",
+    "ModelShape": "avgen_b200.simulate",
     "search_parallel_plan": "avgen_b200.simulate",
     "apply_lora": "avgen_b200.finetune",
     "GRPOTrainer": "avgen_b200.rl",
     "SyntheticSource": "avgen_b200.data",
+    "build_loader": "avgen_b200.data",
     "run_eval_suite": "avgen_b200.eval",
+    "EvalReport": "avgen_b200.eval",
 }
 
 __all__ = ["ConditionMode", "GridPatchifier", "MediaBatch", "MediaBatchSpec", "ModelInput", "ModelOutput",
-           "PatchLayout", "RNGStreams", "StepMetrics", "TextContext", "TokenStream", "TrainState", "__version__",
+           "PatchLayout", "Patchifier", "RNGStreams", "StepMetrics", "TextContext", "TokenStream", "TrainState", "__version__",
            *sorted(_LAZY)]
 
 

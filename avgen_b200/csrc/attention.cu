@@ -1305,14 +1305,9 @@ void attn_fwd_launch(const AttnFwdDesc& d_in, cudaStream_t stream) {
   const long kv_slabs = static_cast<long>(d.B) * d.Hk * (ring ? d.ring_world : 1);
   const CUtensorMap tk = make_tmap_3d_bf16(d.k, kHD, kv_len, kv_slabs, kHD, kv_len * kHD, 64, 128, 1);
   const CUtensorMap tv = make_tmap_3d_bf16(d.v, kHD, kv_len, kv_slabs, kHD, kv_len * kHD, 64, 128, 1);
-  static bool attr = false;
-  if (!attr) {
-    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          FwdSmem::BYTES));
-    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          FwdSmem::BYTES));
-    attr = true;
-  }
+  static PerDeviceOnce once_plain, once_trace;
+  raise_smem_limit(once_plain, attn_fwd_kernel<false>, FwdSmem::BYTES);
+  raise_smem_limit(once_trace, attn_fwd_kernel<true>, FwdSmem::BYTES);
   const long grid = static_cast<long>(d.B) * d.H * d.q_tiles;
   if (d.trace != nullptr)
     attn_fwd_kernel<true><<<grid, 384, FwdSmem::BYTES, stream>>>(tq, tk, tv, d);
@@ -1403,14 +1398,9 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
                                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       AVGEN_CHECK(r == CUDA_SUCCESS, "attention bwd: dQ accumulator tensor map failed (", static_cast<int>(r), ")");
     }
-    static bool attr = false;
-    if (!attr) {
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_fused_kernel<false>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, FusedBwdSmem::BYTES));
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_fused_kernel<true>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize, FusedBwdSmem::BYTES));
-      attr = true;
-    }
+    static PerDeviceOnce once_plain, once_trace;
+    raise_smem_limit(once_plain, attn_bwd_fused_kernel<false>, FusedBwdSmem::BYTES);
+    raise_smem_limit(once_trace, attn_bwd_fused_kernel<true>, FusedBwdSmem::BYTES);
     const long grid = static_cast<long>(d.B) * d.Hk * (d.kt_count > 0 ? d.kt_count : d.k_tiles);
     if (d.trace != nullptr)
       attn_bwd_fused_kernel<true><<<grid, 512, FusedBwdSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, tacc, d);
@@ -1433,12 +1423,8 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
     const CUtensorMap tdo = dout_map(kQT);
     const CUtensorMap tl = f32_rows(d.lse, kQT);
     const CUtensorMap tdl = f32_rows(d.delta, kQT);
-    static bool attr = false;
-    if (!attr) {
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            DkvSmem::BYTES));
-      attr = true;
-    }
+    static PerDeviceOnce once;
+    raise_smem_limit(once, attn_bwd_dkv_kernel, DkvSmem::BYTES);
     const long grid = static_cast<long>(d.B) * d.Hk * d.k_tiles;
     attn_bwd_dkv_kernel<<<grid, 384, DkvSmem::BYTES, stream>>>(tq, tk, tv, tdo, tl, tdl, d);
     AVGEN_CUDA_CHECK(cudaGetLastError());
@@ -1450,14 +1436,9 @@ void attn_bwd_launch(const AttnBwdDesc& d_in, cudaStream_t stream) {
     const CUtensorMap tk = head_major(d.k, d.Hk, d.Lk, kKT);
     const CUtensorMap tv = head_major(d.v, d.Hk, d.Lk, kKT);
     const CUtensorMap tdo = dout_map(128);
-    static bool attr = false;
-    if (!attr) {
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            DqSmem::BYTES));
-      AVGEN_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_dq_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            DqSmem::BYTES));
-      attr = true;
-    }
+    static PerDeviceOnce once_masked, once_dense;
+    raise_smem_limit(once_masked, attn_bwd_dq_kernel<true>, DqSmem::BYTES);
+    raise_smem_limit(once_dense, attn_bwd_dq_kernel<false>, DqSmem::BYTES);
     const long grid = static_cast<long>(d.B) * d.H * d.q_tiles;
     if (d.kmask != nullptr) {
       attn_bwd_dq_kernel<true><<<grid, 384, DqSmem::BYTES, stream>>>(tq, tk, tv, tdo, d);

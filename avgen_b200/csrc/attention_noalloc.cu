@@ -1,27 +1,8 @@
-// Allocation-free C entry point for the attention backward.
-//
-// This entry point has no counterpart in the reference framework (avgen ships
-// no native code). It exists for callers that must not allocate device memory
-// per call (a runtime that captures calls into CUDA graphs or budgets memory
-// up front): it runs the two-pass attention backward, whose only scratch is the
-// per-row statistic delta = rowsum(dO * O), with that scratch held in a
-// file-scope device array instead of a fresh allocation.
-//
-// Contract:
-//  * scratch limit: B * H * lse_ld floats <= kNoAllocScratchFloats (4 MiB of
-//    fp32, e.g. 20 heads x 52,428 queries); larger problems are rejected with
-//    status 2 and nothing is launched;
-//  * the scratch is one array per device shared by every call: calls whose
-//    work overlaps on the GPU (two streams, two host threads) race on it, so
-//    serialise them on one stream;
-//  * its contents persist between calls (they hold the last call's delta);
-//  * nothing here allocates: the scratch and the kernel error word are static
-//    device arrays whose addresses are fetched once per device with
-//    cudaGetSymbolAddress.
-//
-// Status codes: 0 ok, 1 invalid argument, 2 scratch limit exceeded, 3 CUDA
-// error while resolving the scratch address, 4 launch error (message kept for
-// avgen_attn_bwd_noalloc_last_error).
+// Allocation-free C entry point for the attention backward: the definitions
+// of include/attention_noalloc.h, whose comment states the contract (scratch
+// limit, the shared array and the race between overlapping calls, status
+// codes). No counterpart exists in the reference framework, which ships no
+// native code.
 
 #include <cuda_runtime.h>
 
@@ -30,6 +11,7 @@
 #include <exception>
 #include <mutex>
 
+#include "include/attention_noalloc.h"
 #include "include/launchers.h"
 
 namespace {
@@ -75,11 +57,7 @@ cudaError_t resolve(int device, DeviceSlots& out) {
 
 extern "C" {
 
-// Attention backward without device allocation (two-pass kernels, delta scratch
-// in a static device array). q [B, H, Lq, 128], k / v [B, Hk, Lk, 128], o / dout
-// [B, Lq, H, 128] dense bf16; lse fp32 [B, H, Lq] with row stride lse_ld (a
-// multiple of 4, >= Lq); dq / dk / dv bf16 outputs shaped like q / k / v; kmask
-// packed key-valid bits [B, kmask_words] or null; stream is a cudaStream_t.
+// Declared (with the argument layout) in include/attention_noalloc.h.
 __attribute__((visibility("default"))) int avgen_attn_bwd_noalloc(
     const void* q, const void* k, const void* v, const void* o, const void* dout, const float* lse, long lse_ld,
     void* dq, void* dk, void* dv, const unsigned int* kmask, int kmask_words, int B, int H, int Hk, int Lq, int Lk,
@@ -98,6 +76,14 @@ __attribute__((visibility("default"))) int avgen_attn_bwd_noalloc(
   if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
     set_error("avgen_attn_bwd_noalloc: no current CUDA device");
     return 3;
+  }
+  if (stream != nullptr) {  // the scratch address is per device: the stream must run on this one
+    int stream_device = -1;
+    if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &stream_device) != cudaSuccess ||
+        stream_device != device) {
+      set_error("avgen_attn_bwd_noalloc: the stream does not belong to the current device");
+      return 1;
+    }
   }
   DeviceSlots slots;
   if (resolve(device, slots) != cudaSuccess) {
@@ -141,7 +127,33 @@ __attribute__((visibility("default"))) int avgen_attn_bwd_noalloc(
   return 0;
 }
 
-// Message of the last failing call on this host thread ("" if none).
-__attribute__((visibility("default"))) const char* avgen_attn_bwd_noalloc_last_error() { return g_last_error; }
+__attribute__((visibility("default"))) const char* avgen_attn_bwd_noalloc_last_error(void) { return g_last_error; }
+
+__attribute__((visibility("default"))) int avgen_attn_bwd_noalloc_device_error(int* out, int clear) {
+  if (out == nullptr) {
+    set_error("avgen_attn_bwd_noalloc_device_error: null output");
+    return 1;
+  }
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= kMaxDevices) {
+    set_error("avgen_attn_bwd_noalloc_device_error: no current CUDA device");
+    return 3;
+  }
+  DeviceSlots slots;
+  if (resolve(device, slots) != cudaSuccess) {
+    set_error("avgen_attn_bwd_noalloc_device_error: cudaGetSymbolAddress failed");
+    return 3;
+  }
+  int word = 0;
+  if (cudaDeviceSynchronize() != cudaSuccess ||
+      cudaMemcpy(&word, slots.err, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess ||
+      (clear != 0 && cudaMemset(slots.err, 0, sizeof(int)) != cudaSuccess) ||
+      (clear != 0 && cudaDeviceSynchronize() != cudaSuccess)) {
+    set_error("avgen_attn_bwd_noalloc_device_error: CUDA error while reading the error word");
+    return 3;
+  }
+  *out = word;
+  return 0;
+}
 
 }  // extern "C"

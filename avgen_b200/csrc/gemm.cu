@@ -491,11 +491,8 @@ void launch_gemm_ew(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensor
                     const CUtensorMap& tb2, const GemmArgs& args, cudaStream_t stream, int num_sms) {
   using Cfg = GemmCfg<BN>;
   auto kernel = gemm_sm100_kernel<BN, A_MN, B_MN, EPI, OUT_F32, EW>;
-  static std::once_flag once;
-  std::call_once(once, [&] {
-    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Cfg::SMEM_BYTES));
-  });
+  static PerDeviceOnce once;
+  raise_smem_limit(once, kernel, Cfg::SMEM_BYTES);
   const int num_m = (args.M + kBM - 1) / kBM;
   const int num_n = (args.N + BN - 1) / BN;
   const int tiles = num_m * num_n * args.k_splits;

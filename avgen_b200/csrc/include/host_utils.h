@@ -11,6 +11,7 @@
 #include <sstream>
 
 #include <mutex>
+#include <utility>
 
 namespace avgen {
 template <typename... Args>
@@ -56,13 +57,41 @@ inline int* error_word(int device) {
   return words[device];
 }
 
+// Runs a callable once per device, thread-safely. Kernel attributes (the
+// dynamic shared-memory limit among them) are per device, so a per-process
+// flag would leave every device but the first one without them.
+class PerDeviceOnce {
+ public:
+  template <typename Fn>
+  void run(int device, Fn&& fn) {
+    AVGEN_CHECK(device >= 0 && device < kMaxDevices, "bad device index ", device);
+    std::call_once(flags_[device], std::forward<Fn>(fn));
+  }
+
+ private:
+  std::once_flag flags_[kMaxDevices];
+};
+
+// Raises `kernel`'s dynamic shared-memory limit to `bytes` on the current device
+// (once per device for each `once`).
+template <typename Kernel>
+inline void raise_smem_limit(PerDeviceOnce& once, Kernel kernel, int bytes) {
+  int device = 0;
+  AVGEN_CUDA_CHECK(cudaGetDevice(&device));
+  once.run(device, [&] {
+    AVGEN_CUDA_CHECK(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes));
+  });
+}
+
 inline int num_sms(int device) {
+  AVGEN_CHECK(device >= 0 && device < kMaxDevices, "bad device index ", device);
+  static PerDeviceOnce once;
   static int cache[kMaxDevices] = {0};
-  if (cache[device] == 0) {
+  once.run(device, [&] {
     int n = 0;
     AVGEN_CUDA_CHECK(cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device));
     cache[device] = n;
-  }
+  });
   return cache[device];
 }
 

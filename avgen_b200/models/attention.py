@@ -29,14 +29,23 @@ def device_arch(device: torch.device | str | None = None) -> str:
 
 
 def key_padding_mask(mask: torch.Tensor | None, *, assume_dense: bool = False) -> torch.Tensor | None:
-    """``(B, L)`` bool validity, or ``None`` when every key is valid."""
+    """``(B, L)`` bool validity, or ``None`` when every key is known to be valid.
+
+    On CUDA the mask is returned as given, without testing whether every key is
+    valid: that test reads a device value on the host and so waits for the
+    device to drain its queue. The kernels apply an all-valid mask at the cost of
+    a few bit loads per key tile. On the CPU an all-valid mask becomes ``None``."""
     if mask is None or assume_dense:
         return None
     if mask.ndim != 2:
         raise ValueError(f"key mask must have rank 2 (batch, keys); got {tuple(mask.shape)}")
     if mask.dtype is not torch.bool:
         raise TypeError(f"key mask must be bool; got {mask.dtype}")
-    if mask.numel() == 0 or bool(mask.all()):
+    if mask.numel() == 0:
+        return None
+    if mask.is_cuda:
+        return mask
+    if bool(mask.all()):
         return None
     return mask
 

@@ -317,26 +317,29 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
     del avgen
     dev = torch.device("cuda", local)
     cp, dp = layout(world)
-    torch.manual_seed(1234)
-    with torch.device("meta"):
-        model = build_model("video_dit", {"width": WIDTH, "depth": args.depth, "num_heads": HEADS,
-                                          "text_width": TEXT_WIDTH, "text_context_length": TEXT_TOKENS,
-                                          "in_channels": CHANNELS})
-    model = model.to_empty(device=dev)
-    model.init_weights()
-    tokens_local = (args.frames * HEIGHT * WIDTH_PX // 4) // cp
-    ac_mode = "selective_op" if tokens_local <= 16384 else "full"
+    micro = cp
     dims = ParallelDims(world_size=world, dp_shard=dp, context=cp)
-    parallel = parallelize(model, dims, config=ParallelConfig(
-        activation_checkpoint=ActivationCheckpointConfig(mode=ac_mode)))
-    data_rank = dims.data_coordinates(parallel.mesh)[0] if parallel.mesh is not None else 0
-    optimizer = build_optimizer(parallel.model, lr=1e-4, weight_decay=0.0)
-    state = TrainState(model=parallel.model, optimizer=optimizer, rng=RNGStreams.for_rank(0, data_rank=data_rank))
+
+    def build(mode: str, frequency: int):  # noqa: ANN202
+        torch.manual_seed(1234)
+        with torch.device("meta"):
+            model = build_model("video_dit", {"width": WIDTH, "depth": args.depth, "num_heads": HEADS,
+                                              "text_width": TEXT_WIDTH, "text_context_length": TEXT_TOKENS,
+                                              "in_channels": CHANNELS})
+        model = model.to_empty(device=dev)
+        model.init_weights()
+        parallel = parallelize(model, dims, config=ParallelConfig(
+            activation_checkpoint=ActivationCheckpointConfig(mode=mode, save_op_frequency=frequency)))
+        data_rank = dims.data_coordinates(parallel.mesh)[0] if parallel.mesh is not None else 0
+        optimizer = build_optimizer(parallel.model, lr=1e-4, weight_decay=0.0)
+        state = TrainState(model=parallel.model, optimizer=optimizer,
+                           rng=RNGStreams.for_rank(0, data_rank=data_rank))
+        return parallel, state, data_rank
+
     objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("shifted_logit_normal"),
                                       MultiTaskConditioning())
     patchifier = GridPatchifier()
-    micro = cp
-    gen = torch.Generator().manual_seed(1000 + data_rank)
+    gen = torch.Generator()
 
     def make(pin: bool) -> MediaBatch:
         spec = MediaBatchSpec(schema_version=1, bucket_id=0, video_shape=(1, CHANNELS, args.frames, HEIGHT, WIDTH_PX),
@@ -356,8 +359,6 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
             t = {k: v.pin_memory() for k, v in t.items()}
         return MediaBatch(sample_ids=torch.zeros(1, dtype=torch.int64), spec=spec, **t)
 
-    host = [make(True) for _ in range(micro)]
-    dev_batches = [b.to(dev) for b in host]
     use_ring = cp > 1 and args.ref_variant == "ring"
     cp_buffer = torch.zeros(cp * 128, device=dev)
     if use_ring:
@@ -369,6 +370,8 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
 
     def step(batches, *, copy: bool) -> object:
         metrics = None
+        state = current["state"]
+        parallel = current["parallel"]
         for m, b in enumerate(batches):
             if copy:
                 b = b.to(dev, non_blocking=True)
@@ -383,6 +386,38 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
                                         autocast_dtype=torch.bfloat16, data_world=dp)
         return metrics
 
+    # Activation checkpointing: the cheapest of the reference's own policies that
+    # fits, tried in order of recompute (none, selective_op saving every listed op,
+    # then every 2nd, then full), each moved past only after a caught CUDA OOM on
+    # some rank (every rank takes the same path: the OOM flag is max-reduced).
+    current: dict = {}
+    attempts: list[str] = []
+    ac_mode = "full"
+    for mode, frequency in (("none", 1), ("selective_op", 1), ("selective_op", 2), ("full", 1)):
+        label = mode if mode != "selective_op" else f"selective_op(save_op_frequency={frequency})"
+        oom = 0.0
+        try:
+            parallel, state, data_rank = build(mode, frequency)
+            current.update(parallel=parallel, state=state)
+            gen.manual_seed(1000 + data_rank)
+            host = [make(True) for _ in range(micro)]
+            dev_batches = [b.to(dev) for b in host]
+            if mode != "full":
+                step(dev_batches, copy=False)
+                torch.cuda.synchronize()
+        except torch.OutOfMemoryError:
+            oom = 1.0
+        if max_over_ranks(oom) == 0.0:
+            ac_mode = label
+            break
+        attempts.append(f"{label}: CUDA out of memory")
+        current.clear()
+        parallel = state = host = dev_batches = None
+        import gc
+
+        gc.collect()
+        torch.cuda.empty_cache()
+        barrier()
     for _ in range(args.warmup):
         step(dev_batches, copy=False)
     torch.cuda.synchronize()
@@ -422,10 +457,11 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
         "loss": loss_val, "e2e": {"value": world / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
                                   "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
         "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro, "ac_mode": ac_mode,
+        "ac_attempts": attempts,
         "ref_variant": ("ring (context_parallel_region)" if use_ring else
                         f"shipped: block-local attention within each of the {cp} sequence shards "
                         f"(1/{cp} of the global self-attention FLOPs)") if cp > 1 else "n/a (cp=1)",
-        "applied": list(parallel.applied),
+        "applied": list(current["parallel"].applied),
     }
 
 
@@ -467,6 +503,7 @@ def main() -> None:
             if args.impl == "reference":
                 line["impl"] = "reference"
                 line["config"]["activation_checkpoint"] = out["ac_mode"]
+                line["config"]["activation_checkpoint_rejected"] = out["ac_attempts"]
                 line["config"]["ref_variant"] = out["ref_variant"]
                 line["config"]["applied"] = out["applied"]
             else:

@@ -51,5 +51,5 @@ setup(
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
-    entry_points={"console_scripts": ["avgen-b200=avgen_b200.cli.main:main"]},
+    entry_points={"console_scripts": ["avgen=avgen_b200.cli.main:main", "avgen-b200=avgen_b200.cli.main:main"]},
 )

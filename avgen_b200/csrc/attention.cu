@@ -137,9 +137,12 @@ __global__ void __launch_bounds__(384, 1)
           const int r = g / ring_tiles;
           row = (g - r * ring_tiles) * kTile;
           slab += r * p.B * p.Hk;
-          if (r != p.ring_rank && row == 0 &&
-              !flag_wait_geq(p.ring_flags + r, p.ring_epoch, abort_flag, p.err, kErrTimeoutPeer))
-            break;
+          if (r != p.ring_rank && row == 0) {
+            const long long t0 = clock64();
+            if (!flag_wait_geq(p.ring_flags + r, p.ring_epoch, abort_flag, p.err, kErrTimeoutPeer)) break;
+            if (p.wait_cycles != nullptr)
+              atomicAdd(p.wait_cycles, static_cast<unsigned long long>(clock64() - t0));
+          }
         }
         mbar_arrive_expect_tx(&kv_full[s], 65536);
         uint8_t* st = smem + FwdSmem::KV + s * 65536;

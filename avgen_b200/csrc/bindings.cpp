@@ -602,7 +602,7 @@ long stat_row_stride(const at::Tensor& t, int B, int H, int Lq, const char* what
 // (keys of rank r in slab r; Lk = world * L) together with ring_flags.
 void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at::Tensor& out, const OptT& lse,
               const OptT& kmask, double scale, const OptT& trace, int64_t ring_rank, const OptT& ring_flags,
-              int64_t ring_epoch) {
+              int64_t ring_epoch, const OptT& ring_wait) {
   c10::cuda::CUDAGuard guard(q.device());
   check_bf16(q, "q");
   check_bf16(k, "k");
@@ -632,6 +632,11 @@ void attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, at:
     d.ring_len = static_cast<int>(k.size(3));
     d.ring_flags = reinterpret_cast<const unsigned*>(ring_flags->data_ptr<int>());
     d.ring_epoch = static_cast<unsigned>(ring_epoch);
+    if (has(ring_wait)) {
+      TORCH_CHECK(ring_wait->scalar_type() == at::kLong && ring_wait->is_cuda() && ring_wait->numel() >= 1,
+                  "attention ring: ring_wait must be an int64 device tensor");
+      d.wait_cycles = reinterpret_cast<unsigned long long*>(ring_wait->data_ptr<int64_t>());
+    }
   }
   // out: token-major [B, Lq, H, D] (any strides with a contiguous last dim)
   TORCH_CHECK(out.dim() == 4 && out.size(0) == d.B && out.size(1) == d.Lq && out.size(2) == d.H &&
@@ -792,6 +797,63 @@ void shard_adamw_push(const std::vector<int64_t>& params, int64_t rank, int64_t 
   shard_adamw_push_launch(d, p.data(), cur_stream());
 }
 
+// --------------------------------------------------------------------- sharded data parallelism
+void peer_reduce(const std::vector<int64_t>& srcs, int64_t rank, int64_t offset, at::Tensor& out, bool src_bf16,
+                 double scale, const OptT& sq_acc) {
+  c10::cuda::CUDAGuard guard(out.device());
+  check_f32(out, "out");
+  TORCH_CHECK(out.is_contiguous(), "peer_reduce: out must be contiguous");
+  std::vector<const void*> p;
+  p.reserve(srcs.size());
+  for (int64_t a : srcs) p.push_back(reinterpret_cast<const void*>(a));
+  peer_reduce_launch(p.data(), static_cast<int>(p.size()), static_cast<int>(rank), offset, out.numel(), src_bf16,
+                     static_cast<float>(scale), out.data_ptr<float>(), const_cast<float*>(f32_or_null(sq_acc, "sq_acc")),
+                     out.device().index(), cur_stream());
+}
+
+// `table`: int64 device tensor [T, 4] of (param, grad, exp_avg, exp_avg_sq) addresses;
+// `chunks`: int64 device tensor [C, 3] of (row, start, length).
+const MTTensor* mt_rows(const at::Tensor& table) {
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kLong && table.is_contiguous() && table.dim() == 2 &&
+                  table.size(1) == 4,
+              "multi-tensor: the table must be a contiguous int64 [T, 4] device tensor");
+  static_assert(sizeof(MTTensor) == 4 * sizeof(int64_t), "MTTensor layout");
+  return reinterpret_cast<const MTTensor*>(table.data_ptr<int64_t>());
+}
+const MTChunk* mt_chunks(const at::Tensor& chunks) {
+  TORCH_CHECK(chunks.is_cuda() && chunks.scalar_type() == at::kLong && chunks.is_contiguous() && chunks.dim() == 2 &&
+                  chunks.size(1) == 3,
+              "multi-tensor: chunks must be a contiguous int64 [C, 3] device tensor");
+  static_assert(sizeof(MTChunk) == 3 * sizeof(int64_t), "MTChunk layout");
+  return reinterpret_cast<const MTChunk*>(chunks.data_ptr<int64_t>());
+}
+
+void mt_sq_norm(const at::Tensor& table, const at::Tensor& chunks, at::Tensor& acc) {
+  c10::cuda::CUDAGuard guard(acc.device());
+  check_f32(acc, "acc");
+  mt_sq_norm_launch(mt_chunks(chunks), static_cast<int>(chunks.size(0)), mt_rows(table), acc.data_ptr<float>(),
+                    cur_stream());
+}
+
+void mt_adamw(const at::Tensor& table, const at::Tensor& chunks, double lr, double beta1, double beta2, double eps,
+              double weight_decay, int64_t step, const OptT& grad_scale, const OptT& skip) {
+  c10::cuda::CUDAGuard guard(table.device());
+  MTAdamWArgs a;
+  a.lr = static_cast<float>(lr);
+  a.beta1 = static_cast<float>(beta1);
+  a.beta2 = static_cast<float>(beta2);
+  a.eps = static_cast<float>(eps);
+  a.weight_decay = static_cast<float>(weight_decay);
+  a.bias_correction1 = static_cast<float>(1.0 - std::pow(beta1, static_cast<double>(step)));
+  a.bias_correction2_sqrt = static_cast<float>(std::sqrt(1.0 - std::pow(beta2, static_cast<double>(step))));
+  a.grad_scale = f32_or_null(grad_scale, "grad_scale");
+  if (has(skip)) {
+    TORCH_CHECK(skip->scalar_type() == at::kInt && skip->is_cuda(), "mt_adamw: skip must be int32 on device");
+    a.skip = skip->data_ptr<int>();
+  }
+  mt_adamw_launch(mt_chunks(chunks), static_cast<int>(chunks.size(0)), mt_rows(table), a, cur_stream());
+}
+
 // --------------------------------------------------------------------- peer memory
 int64_t p2p_alloc_py(int64_t bytes, int64_t device) {
   return reinterpret_cast<int64_t>(p2p_alloc(static_cast<size_t>(bytes), static_cast<int>(device)));
@@ -888,11 +950,16 @@ PYBIND11_MODULE(_C, m) {
   m.def("ema", &a::ema);
   m.def("attn_fwd", &a::attn_fwd, arg("q"), arg("k"), arg("v"), arg("out"), arg("lse") = none, arg("kmask") = none,
         arg("scale") = 0.0, arg("trace") = none, arg("ring_rank") = 0, arg("ring_flags") = none,
-        arg("ring_epoch") = 0);
+        arg("ring_epoch") = 0, arg("ring_wait") = none);
   m.def("shard_reduce", &a::shard_reduce, arg("grads"), arg("lo"), arg("out"), arg("sq_acc"));
   m.def("shard_adamw_push", &a::shard_adamw_push, arg("params"), arg("rank"), arg("lo"), arg("grad"),
         arg("exp_avg"), arg("exp_avg_sq"), arg("lr"), arg("beta1"), arg("beta2"), arg("eps"), arg("weight_decay"),
         arg("step"), arg("grad_scale") = none, arg("skip") = none);
+  m.def("peer_reduce", &a::peer_reduce, arg("srcs"), arg("rank"), arg("offset"), arg("out"), arg("src_bf16"),
+        arg("scale"), arg("sq_acc") = none);
+  m.def("mt_sq_norm", &a::mt_sq_norm, arg("table"), arg("chunks"), arg("acc"));
+  m.def("mt_adamw", &a::mt_adamw, arg("table"), arg("chunks"), arg("lr"), arg("beta1"), arg("beta2"), arg("eps"),
+        arg("weight_decay"), arg("step"), arg("grad_scale") = none, arg("skip") = none);
   m.def("p2p_alloc", &a::p2p_alloc_py, arg("bytes"), arg("device"));
   m.def("p2p_free", &a::p2p_free_py);
   m.def("p2p_export", &a::p2p_export_py);

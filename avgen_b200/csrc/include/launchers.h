@@ -230,6 +230,9 @@ struct AttnFwdDesc {
   int ring_len = 0;
   const unsigned* ring_flags = nullptr;
   unsigned ring_epoch = 0;
+  // Optional: SM clock cycles the TMA producers spent waiting on ring_flags, summed
+  // over CTAs (exposed-communication accounting).
+  unsigned long long* wait_cycles = nullptr;
 };
 void attn_fwd_launch(const AttnFwdDesc& d, cudaStream_t stream);
 
@@ -347,5 +350,33 @@ struct ShardAdamWDesc {
   const int* skip = nullptr;
 };
 void shard_adamw_push_launch(const ShardAdamWDesc& d, const float* const* params, cudaStream_t stream);
+
+// Sharded data parallelism (fsdp.cu). peer_reduce: out[i] = scale * sum over the
+// `world` sources (one address per rank, valid on this device) of src[offset + i];
+// fp32 or bf16 sources, fp32 out; sq_acc (nullable) accumulates sum(out^2).
+void peer_reduce_launch(const void* const* srcs, int world, int rank, long offset, long n, bool src_bf16, float scale,
+                        float* out, float* sq_acc, int device, cudaStream_t stream);
+// Multi-tensor optimizer kernels: one block per chunk of one tensor row.
+struct MTTensor {
+  float* param = nullptr;
+  const float* grad = nullptr;
+  float* exp_avg = nullptr;
+  float* exp_avg_sq = nullptr;
+};
+struct MTChunk {
+  int tensor = 0;
+  int pad = 0;
+  long start = 0;
+  long len = 0;
+};
+struct MTAdamWArgs {
+  float lr = 1e-4f, beta1 = 0.9f, beta2 = 0.999f, eps = 1e-8f, weight_decay = 0.f;
+  float bias_correction1 = 1.f, bias_correction2_sqrt = 1.f;
+  const float* grad_scale = nullptr;
+  const int* skip = nullptr;
+};
+void mt_sq_norm_launch(const MTChunk* chunks, int nchunks, const MTTensor* tensors, float* acc, cudaStream_t stream);
+void mt_adamw_launch(const MTChunk* chunks, int nchunks, const MTTensor* tensors, const MTAdamWArgs& args,
+                     cudaStream_t stream);
 
 }  // namespace avgen

@@ -48,32 +48,40 @@ class MetricBundle:
     parameters: dict[str, str] = field(default_factory=dict)
 
 
+_PIXEL_ON_LATENTS = ("pixel-space metric requested on latents; set eval.decode=true or drop it "
+                     "(its value on latents would not measure what its name says)")
+
+
+def _build_one(name: str, kwargs: dict[str, Any], decoded: bool) -> tuple[Any, str | None]:
+    """(metric, None) when ``name`` can run here, else (None, why it is skipped)."""
+    if name in list_learned_metrics():
+        from avgen_b200.eval.learned import build_learned_metric
+
+        try:
+            return build_learned_metric(name, **kwargs), None
+        except MissingBackendError as err:
+            return None, str(err).splitlines()[0]
+    if name not in list_metrics():
+        raise MetricError(f"unknown metric {name!r}; built-ins: {', '.join(list_metrics())}; gated: "
+                          f"{', '.join(list_learned_metrics())}")
+    metric: RunningMetric = build_metric(name, **kwargs)
+    if metric.pixel_space_only and not decoded:
+        return None, _PIXEL_ON_LATENTS
+    return metric, None
+
+
 def build_metrics(names: Sequence[str], *, decoded: bool,
                   options: Mapping[str, Mapping[str, Any]] | None = None) -> MetricBundle:
     """Build each named metric; gated learned metrics whose backend is missing and
     pixel-space metrics on latents are recorded as skipped, with the reason."""
-    opts = dict(options or {})
     bundle = MetricBundle()
     for name in names:
-        kwargs = dict(opts.get(name, {}))
-        if name in list_learned_metrics():
-            from avgen_b200.eval.learned import build_learned_metric
-
-            try:
-                bundle.metrics[name] = build_learned_metric(name, **kwargs)
-            except MissingBackendError as err:
-                bundle.skipped[name] = str(err).splitlines()[0]
-                continue
-        else:
-            if name not in list_metrics():
-                raise MetricError(f"unknown metric {name!r}; built-ins: {', '.join(list_metrics())}; gated: "
-                                  f"{', '.join(list_learned_metrics())}")
-            metric: RunningMetric = build_metric(name, **kwargs)
-            if metric.pixel_space_only and not decoded:
-                bundle.skipped[name] = ("pixel-space metric requested on latents; set eval.decode=true or drop it "
-                                        "(its value on latents would not measure what its name says)")
-                continue
-            bundle.metrics[name] = metric
+        kwargs = dict((options or {}).get(name, {}))
+        metric, why = _build_one(name, kwargs, decoded)
+        if metric is None:
+            bundle.skipped[name] = why or "unavailable"
+            continue
+        bundle.metrics[name] = metric
         bundle.parameters[name] = ",".join(f"{k}={v!r}" for k, v in sorted(kwargs.items())) or "default"
     return bundle
 
@@ -101,15 +109,31 @@ def torch_gather(group: Any = None) -> Callable[[Any], list[Any]]:
 
 
 def _merge_remote(bundle: MetricBundle, gather: Callable[[Any], list[Any]] | None, data_rank: int) -> None:
+    """Fold every other rank's running state into this rank's metrics (exact: states are sums)."""
     if gather is None:
         return
-    states = gather({name: m.state() for name, m in bundle.metrics.items()})
-    for index, remote in enumerate(states or ()):
+    for index, remote in enumerate(gather({name: m.state() for name, m in bundle.metrics.items()}) or ()):
         if index == data_rank or not isinstance(remote, dict):
             continue
-        for name, state in remote.items():
-            if name in bundle.metrics:
-                bundle.metrics[name].merge(state)
+        for name in remote.keys() & bundle.metrics.keys():
+            bundle.metrics[name].merge(remote[name])
+
+
+def _feed(bundle: MetricBundle, batches: Iterable[EvalBatch]) -> tuple[int, set[str]]:
+    """Update every metric with every batch that carries its inputs; returns
+    (samples seen, metrics that received at least one batch)."""
+    samples, fed = 0, set()
+    for batch in batches:
+        inputs = batch.as_inputs()
+        samples += int(batch.video.shape[0])
+        for name, metric in bundle.metrics.items():
+            lacking = [k for k in metric.required_inputs if k not in inputs]
+            if lacking:
+                bundle.skipped.setdefault(name, f"needs {', '.join(lacking)}, which this evaluation did not produce")
+            else:
+                metric.update(**inputs)
+                fed.add(name)
+    return samples, fed
 
 
 def run_eval_suite(batches: Iterable[EvalBatch], *, metrics: Sequence[str] | MetricBundle, pin: EvalPin,
@@ -119,36 +143,24 @@ def run_eval_suite(batches: Iterable[EvalBatch], *, metrics: Sequence[str] | Met
                    step: int = 0, notes: str = "") -> EvalReport:
     """Feed every batch to every metric that has its inputs, merge the ranks' running
     sums exactly, and return the pinned report (sample count summed over ranks)."""
+    import dataclasses
+
     bundle = metrics if isinstance(metrics, MetricBundle) else build_metrics(metrics, decoded=decoded,
                                                                               options=metric_options)
-    seen = 0
-    fed: set[str] = set()
-    for batch in batches:
-        inputs = batch.as_inputs()
-        seen += int(batch.video.shape[0])
-        for name, metric in bundle.metrics.items():
-            missing = [k for k in metric.required_inputs if k not in inputs]
-            if missing:
-                bundle.skipped.setdefault(name, f"needs {', '.join(missing)}, which this evaluation did not produce")
-                continue
-            metric.update(**inputs)
-            fed.add(name)
-    for name in [n for n in bundle.metrics if n not in fed]:
-        bundle.metrics.pop(name)
+    samples, fed = _feed(bundle, batches)
+    for name in set(bundle.metrics) - fed:
+        del bundle.metrics[name]
         bundle.skipped.setdefault(name, "no batch supplied its required inputs")
     _merge_remote(bundle, gather, data_rank)
     values: dict[str, float] = {}
     for name, metric in bundle.metrics.items():
-        got = metric.compute()
-        if not got:
+        stats = metric.compute()
+        if stats:
+            values.update(stats)
+        else:
             bundle.skipped.setdefault(name, "produced no statistics (every clip was too short for it)")
-            continue
-        values.update(got)
-    total = sum(int(c) for c in gather(seen)) if gather is not None else seen
-    resolved = EvalPin(checkpoint=pin.checkpoint, sampler=pin.sampler, steps=pin.steps, guidance=pin.guidance,
-                       guidance_rescale=pin.guidance_rescale, negative_prompt=pin.negative_prompt, seed=pin.seed,
-                       num_samples=total, prompt_digest=prompt_set_digest(prompts) if prompts else pin.prompt_digest,
-                       frames=pin.frames, height=pin.height, width=pin.width, decoded=decoded, codec=pin.codec,
-                       precision=pin.precision, metrics=dict(bundle.parameters))
+    total = sum(int(c) for c in gather(samples)) if gather is not None else samples
+    resolved = dataclasses.replace(pin, num_samples=total, decoded=decoded, metrics=dict(bundle.parameters),
+                                   prompt_digest=prompt_set_digest(prompts) if prompts else pin.prompt_digest)
     return EvalReport(pin=resolved, metrics=values, skipped=dict(bundle.skipped), run_name=run_name, step=step,
                       notes=notes)

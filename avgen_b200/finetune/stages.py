@@ -24,16 +24,22 @@ _MODES = ("JOINT", "VIDEO_TO_AUDIO", "AUDIO_TO_VIDEO", "VIDEO_ONLY", "CONTINUATI
           "VIDEO_TO_VIDEO")
 
 
+def _clamped_lerp(x: float, x0: float, x1: float, y0: float, y1: float) -> float:
+    """The line through (x0, y0) and (x1, y1) at x, held at its end values outside [x0, x1]."""
+    y = y0 + (x - x0) * (y1 - y0) / (x1 - x0)
+    return min(max(y, min(y0, y1)), max(y0, y1))
+
+
 def resolution_shift(sequence_length: int, *, base_length: int = 4096, base_shift: float = 1.0,
                      max_length: int = 65536, max_shift: float = 3.0) -> float:
     """Timestep shift growing linearly in the token count, clamped to its end points."""
     if base_length >= max_length:
         raise ValueError("base_length must be below max_length")
-    t = (sequence_length - base_length) / (max_length - base_length)
-    return min(max(base_shift + t * (max_shift - base_shift), min(base_shift, max_shift)), max(base_shift, max_shift))
+    return _clamped_lerp(float(sequence_length), base_length, max_length, base_shift, max_shift)
 
 
 def shift_timesteps(noise_level: torch.Tensor, shift: float) -> torch.Tensor:
+    """Resolution-dependent shift of noise levels: t -> s t / (1 + (s - 1) t)."""
     if not shift > 0:
         raise ValueError(f"shift must be positive; got {shift!r}")
     return shift * noise_level / (1.0 + (shift - 1.0) * noise_level)
@@ -113,50 +119,78 @@ class FinetuneStage:
         return self.lora is not None or self.control is not None
 
     def normalized_mix(self) -> dict[str, float]:
-        total = sum(w for _, w in self.conditioning_mix)
-        return {m: w / total for m, w in self.conditioning_mix if w > 0}
+        """The conditioning mix as probabilities (modes with weight 0 left out)."""
+        weights = dict(self.conditioning_mix)
+        scale = 1.0 / sum(weights.values())
+        return {mode: w * scale for mode, w in weights.items() if w > 0}
 
 
-_STAGES: dict[str, FinetuneStage] = {}
+class _Registry:
+    """Named stages; a name is taken once unless the caller asks to replace it."""
+
+    def __init__(self) -> None:
+        self._by_name: dict[str, FinetuneStage] = {}
+
+    def add(self, stage: FinetuneStage, overwrite: bool) -> FinetuneStage:
+        if not overwrite and stage.name in self._by_name:
+            raise KeyError(f"stage {stage.name!r} already registered (overwrite=True replaces it)")
+        self._by_name[stage.name] = stage
+        return stage
+
+    def get(self, name: str) -> FinetuneStage:
+        try:
+            return self._by_name[name]
+        except KeyError:
+            raise KeyError(f"unknown stage {name!r}; registered: {self.names()}") from None
+
+    def names(self) -> tuple[str, ...]:
+        return tuple(sorted(self._by_name))
+
+    def items(self) -> list[tuple[str, FinetuneStage]]:
+        return sorted(self._by_name.items())
+
+
+_REGISTRY = _Registry()
 
 
 def register_stage(stage: FinetuneStage, *, overwrite: bool = False) -> FinetuneStage:
-    if stage.name in _STAGES and not overwrite:
-        raise KeyError(f"stage {stage.name!r} already registered (overwrite=True replaces it)")
-    _STAGES[stage.name] = stage
-    return stage
+    return _REGISTRY.add(stage, overwrite)
 
 
 def get_stage(name: str) -> FinetuneStage:
-    if name not in _STAGES:
-        raise KeyError(f"unknown stage {name!r}; registered: {list_stages()}")
-    return _STAGES[name]
+    return _REGISTRY.get(name)
 
 
 def list_stages() -> tuple[str, ...]:
-    return tuple(sorted(_STAGES))
+    return _REGISTRY.names()
 
 
 def standard_stages() -> Mapping[str, FinetuneStage]:
-    return dict(_STAGES)
+    return dict(_REGISTRY.items())
 
 
 def stage_names_for(modes: Sequence[str]) -> tuple[str, ...]:
     """Stages whose conditioning mix covers every mode in ``modes``."""
-    return tuple(sorted(n for n, s in _STAGES.items() if all(m in s.normalized_mix() for m in modes)))
+    wanted = set(modes)
+    return tuple(name for name, stage in _REGISTRY.items() if wanted <= set(stage.normalized_mix()))
 
 
 def apply_stage(model: Any, stage: FinetuneStage) -> Any:
+    """Make ``model`` trainable the way ``stage`` says: a LoRA (only its factors, plus
+    ``trainable_patterns``), or the listed patterns; then freeze ``frozen_patterns``."""
     from avgen_b200.finetune.freeze import freeze_except, freeze_matching
     from avgen_b200.finetune.lora import apply_lora, mark_only_lora_trainable
 
+    steps = []
     if stage.lora is not None:
-        apply_lora(model, stage.lora)
-        mark_only_lora_trainable(model, extra_trainable=stage.trainable_patterns)
+        steps += [lambda m: apply_lora(m, stage.lora),
+                  lambda m: mark_only_lora_trainable(m, extra_trainable=stage.trainable_patterns)]
     elif stage.trainable_patterns:
-        freeze_except(model, stage.trainable_patterns)
+        steps.append(lambda m: freeze_except(m, stage.trainable_patterns))
     if stage.frozen_patterns:
-        freeze_matching(model, stage.frozen_patterns)
+        steps.append(lambda m: freeze_matching(m, stage.frozen_patterns))
+    for step in steps:
+        step(model)
     return model
 
 

@@ -331,6 +331,7 @@ def attention_fwd(
     ring_rank: int = 0,
     ring_flags: torch.Tensor | None = None,
     ring_epoch: int = 0,
+    ring_wait: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor | None]:
     """Flash attention forward. Returns ``(out [B, Lq, H, D], lse [B, H, Lq])``.
 
@@ -341,14 +342,15 @@ def attention_fwd(
     Context-parallel ring: ``k``/``v`` given as ``[world, B, Hk, L, D]`` (rank r's
     keys in slab r, ``L`` a multiple of 128). Every CTA starts at slab
     ``ring_rank`` and reads slab r only after ``ring_flags[r]`` (int32, written
-    by a copy stream or a peer) has reached ``ring_epoch``.
+    by a copy stream or a peer) has reached ``ring_epoch``. ``ring_wait`` (int64
+    [1], optional) accumulates the SM clock cycles the CTAs spent in those waits.
     """
     b, h, lq, d = q.shape
     scale = 1.0 / math.sqrt(d) if scale is None else scale
     if out is None:
         out = torch.empty((b, lq, h, d), device=q.device, dtype=_BF16)
     lse = row_stats(b, h, lq, q.device) if want_lse else None
-    load().attn_fwd(q, k, v, out, lse, kmask, scale, trace, ring_rank, ring_flags, ring_epoch & 0xFFFFFFFF)
+    load().attn_fwd(q, k, v, out, lse, kmask, scale, trace, ring_rank, ring_flags, ring_epoch & 0xFFFFFFFF, ring_wait)
     _count()
     return out, lse
 

@@ -4,8 +4,10 @@ Order: float8 conversion -> tensor parallel -> ``adapt`` hook (LoRA, control
 branches) -> activation checkpointing -> FSDP2/HSDP over the data (and
 context) dimensions, or replicated data parallelism.
 
-Replicated data parallelism (``dp_replicate`` and/or ``cp`` without sharding)
-is native by default: the model stays an ordinary module and the fused AdamW
+Parameters are sharded (FSDP2 over ``dp_shard_cp``, or HSDP) whenever
+``dp_shard`` or ``cp`` is enabled, as in the reference. Replicated data
+parallelism (``dp_replicate`` alone, or ``shard_parameters=False``) is native
+by default: the model stays an ordinary module and the fused AdamW
 all-reduces its flat fp32 gradient buffer once per step over
 ``ParallelModel.data_group`` (one collective, no per-bucket hooks). ``ParallelConfig(native_data_parallel=False)``
 wraps the model in ``DistributedDataParallel`` instead.
@@ -38,6 +40,7 @@ class ParallelConfig:
     block_attribute: str = "blocks"
     sequence_parallel: bool = False
     native_data_parallel: bool = True
+    shard_parameters: bool = True
 
 
 @dataclass(frozen=True, slots=True)
@@ -105,15 +108,22 @@ def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, confi
     if cfg.compile_blocks:
         warnings.warn("compile_blocks is ignored: blocks already run as fused sm_100a kernels", RuntimeWarning,
                       stacklevel=2)
-    if mesh is not None and dims.dp_shard_enabled:
+    # Shard whenever there is a data-parallel or context-parallel dimension to
+    # shard over (the reference's gate, avgen/parallel/apply.py:226-243): a cp-only
+    # job still sums partial gradients, and sharding spreads parameters and
+    # optimizer state over the context ranks too (the ``dp_shard_cp`` mesh).
+    if mesh is not None and (dims.dp_shard_enabled or dims.cp_enabled) and cfg.shard_parameters:
         target = _fsdp_mesh(dims, mesh)
         if target is not None:
             apply_fsdp(model, target, precision=cfg.precision, config=cfg.fsdp)
+            peer = "peer" if getattr(model, "_avgen_peer_collectives", None) else "nccl"
             if dims.dp_replicate_enabled:
                 applied.append(f"hsdp(dp_replicate={dims.dp_replicate}, dp_shard={dims.dp_shard})")
+            elif dims.dp_shard_enabled:
+                applied.append(f"fsdp(dp_shard={dims.dp_shard}" + (f", cp={dims.context}" if dims.cp_enabled
+                                                                   else "") + f", collectives={peer})")
             else:
-                applied.append(f"fsdp(dp_shard={dims.dp_shard}" + (f", cp={dims.context})" if dims.cp_enabled
-                                                                   else ")"))
+                applied.append(f"fsdp(cp={dims.context}, collectives={peer})")
     elif mesh is not None and (dims.dp_replicate_enabled or dims.cp_enabled):
         if cfg.native_data_parallel:
             applied.append(f"native_dp(dp_replicate={dims.dp_replicate}, cp={dims.context})")

@@ -28,6 +28,7 @@ import torch.distributed as dist
 from torch.distributed.device_mesh import DeviceMesh
 
 from avgen_b200.core.tokens import TokenStream
+from avgen_b200.telemetry.comm import comm_span, counter as comm_counter, enabled as comm_enabled
 
 __all__ = ["ContextParallelAttention", "RingAttention", "context_parallel_region", "cp_attention", "gather_stream", "gather_tokens",
            "maybe_context_parallel", "pad_to_multiple", "shard_bounds", "shard_stream", "sharded_length"]
@@ -310,7 +311,8 @@ class RingAttention:
         epoch = self.epoch
         main = torch.cuda.current_stream(k.device)
         assert self._token is not None and self.flags is not None
-        dist.all_reduce(self._token, group=self.group)  # every rank's slab is written
+        with comm_span("ring_ready_barrier"):
+            dist.all_reduce(self._token, group=self.group)  # every rank's slab is written
         copy = self._copy_stream
         assert copy is not None
         copy.wait_stream(main)
@@ -323,9 +325,14 @@ class RingAttention:
                 ext.p2p_copy(k_all[r].data_ptr(), pk[r].data_ptr(), slab_bytes)
                 ext.p2p_copy(v_all[r].data_ptr(), pv[r].data_ptr(), slab_bytes)
                 ext.stream_write(flag0 + 4 * r, epoch)
+        wait = None
+        if comm_enabled():
+            sms = torch.cuda.get_device_properties(q.device).multi_processor_count
+            wait = comm_counter("ring_kv_wait", q.device, sms)
         out, lse = K.attention_fwd(q, k_all, v_all, kmask=kmask, scale=scale, ring_rank=self.rank,
-                                   ring_flags=self.flags, ring_epoch=epoch)
-        main.wait_stream(copy)
+                                   ring_flags=self.flags, ring_epoch=epoch, ring_wait=wait)
+        with comm_span("ring_copy_tail"):
+            main.wait_stream(copy)
         return out, lse, (k_all, v_all)
 
     # receive buffers for dK/dV partials pushed by peers: one pair per (group, shape),
@@ -378,15 +385,17 @@ class RingAttention:
         order = [(self.rank + s_) % self.world for s_ in range(1, self.world)] + [self.rank]
         dq, dk_all, dv_all = K.attention_bwd_slabs(q, k_all, v_all, o, do, lse, order=order, kmask=kmask,
                                                    scale=scale, on_slab=push)
-        main.wait_stream(copy)
-        dist.all_reduce(self._token, group=self.group)  # every peer's pushes into this rank have landed
+        with comm_span("ring_dkdv_barrier"):
+            main.wait_stream(copy)
+            dist.all_reduce(self._token, group=self.group)  # every peer's pushes into this rank have landed
         shape = self.shape[1:]
         sources_k = [dk_all[self.rank]] + [recv.view(self.rank, (2 * parity) * part + s_ * slab, shape, torch.bfloat16)
                                            for s_ in range(self.world) if s_ != self.rank]
         sources_v = [dv_all[self.rank]] + [recv.view(self.rank, (2 * parity + 1) * part + s_ * slab, shape,
                                                      torch.bfloat16) for s_ in range(self.world) if s_ != self.rank]
-        dk = K.slab_sum(sources_k, torch.empty(shape, device=q.device, dtype=torch.bfloat16))
-        dv = K.slab_sum(sources_v, torch.empty(shape, device=q.device, dtype=torch.bfloat16))
+        with comm_span("ring_dkdv_sum"):
+            dk = K.slab_sum(sources_k, torch.empty(shape, device=q.device, dtype=torch.bfloat16))
+            dv = K.slab_sum(sources_v, torch.empty(shape, device=q.device, dtype=torch.bfloat16))
         return dq, dk, dv
 
     _bwd_calls = 0

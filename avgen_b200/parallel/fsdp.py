@@ -4,6 +4,11 @@
 ``fully_shard`` over the given (possibly 2-D HSDP) mesh. The last block keeps
 its gathered parameters after forward by default, since backward starts with
 it. ``set_prefetch_depth`` overlaps the next blocks' all-gathers with compute.
+
+On CUDA ranks of one NVSwitch node with a 1-D mesh, the parameter all-gather
+and the gradient reduce-scatter run over NVLink peer memory
+(:mod:`avgen_b200.parallel.peer_comm`: copy-engine pulls and a pull-reduce
+kernel) instead of NCCL; ``FSDPConfig(peer_collectives=False)`` keeps NCCL.
 """
 from __future__ import annotations
 
@@ -26,6 +31,7 @@ class FSDPConfig:
     ignore_frozen_params: bool = False
     forward_prefetch: int = 1
     backward_prefetch: int = 1
+    peer_collectives: bool = True
 
 
 def apply_fsdp(model: nn.Module, mesh: Any, *, precision: PrecisionConfig | None = None,
@@ -52,6 +58,10 @@ def apply_fsdp(model: nn.Module, mesh: Any, *, precision: PrecisionConfig | None
     fully_shard(model, reshard_after_forward=cfg.reshard_after_forward, **kwargs)
     if cfg.forward_prefetch > 1 or cfg.backward_prefetch > 1:
         set_prefetch_depth(model, forward=cfg.forward_prefetch, backward=cfg.backward_prefetch)
+    if cfg.peer_collectives and getattr(mesh, "device_type", "cpu") == "cuda":
+        from avgen_b200.parallel.peer_comm import install_peer_collectives
+
+        install_peer_collectives(model, mesh)
     return model
 
 

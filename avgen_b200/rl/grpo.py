@@ -17,7 +17,9 @@ freezes a copy of the current policy so the KL term always has a reference.
 """
 from __future__ import annotations
 
+import bisect
 import copy
+import functools
 from collections.abc import Sequence
 from dataclasses import dataclass
 from typing import Any
@@ -29,6 +31,22 @@ from avgen_b200.rl.sde import to_sde
 
 __all__ = ["GRPOConfig", "GRPOMetrics", "GRPOTrainer", "WindowSchedule", "clipped_surrogate", "kl_penalty",
            "regulated_log_ratio"]
+
+
+@functools.lru_cache(maxsize=64)
+def _move_times(interval: int, stride: int, limit: int, exponential: bool, decay: float) -> tuple[float, ...]:
+    """Optimizer steps at which the window moves, ascending: every ``interval`` steps,
+    or (``exponential``) after intervals that shrink by ``decay`` down to one step.
+    The window stops once it reaches ``limit``, after ceil(limit / stride) moves."""
+    moves = -(-limit // stride) if limit > 0 else 0
+    if not exponential:
+        return tuple(float(interval * (k + 1)) for k in range(moves))
+    times, at, span = [], 0.0, float(interval)
+    for _ in range(moves):
+        at += span
+        times.append(at)
+        span = max(span * decay, 1.0)
+    return tuple(times)
 
 
 @dataclass(frozen=True, slots=True)
@@ -55,17 +73,13 @@ class WindowSchedule:
             raise ValueError(f"decay must be in (0, 1]; got {self.decay!r}")
 
     def start_for(self, optimizer_step: int) -> int:
+        """First SDE step of the window after ``optimizer_step`` optimizer steps."""
         if optimizer_step < 0:
             raise ValueError(f"optimizer_step must be non-negative; got {optimizer_step}")
         limit = self.total_steps - self.window
-        if not self.exponential:
-            return int(min((optimizer_step // self.interval) * self.stride, limit))
-        moves, elapsed, span = 0, 0.0, float(self.interval)
-        while elapsed + span <= optimizer_step and moves * self.stride < limit:
-            elapsed += span
-            span = max(span * self.decay, 1.0)
-            moves += 1
-        return int(min(moves * self.stride, limit))
+        moves_made = bisect.bisect_right(_move_times(self.interval, self.stride, limit, self.exponential, self.decay),
+                                         optimizer_step)
+        return min(moves_made * self.stride, limit)
 
     def steps_for(self, optimizer_step: int) -> tuple[int, ...]:
         start = self.start_for(optimizer_step)
@@ -196,30 +210,39 @@ class GRPOTrainer:
         w = 1.0 / (batch.sigma - batch.sigma_next).abs().clamp_min(1e-8)
         return w / w.mean().clamp_min(1e-12)
 
-    def loss(self, batch: RolloutBatch) -> tuple[torch.Tensor, GRPOMetrics]:
+    def _transition(self, velocity_fn: VelocityFn, batch: RolloutBatch) -> Any:
+        """The SDE transition ``velocity_fn`` assigns to each stored step (scored on the stored next state)."""
         c = self.config
-        v = self.velocity_fn(batch.sample_before, batch.sigma, prompt_index=batch.prompt_index)
-        step = to_sde(v, batch.sample_before, batch.sigma, batch.sigma_next, noise_level=c.noise_level,
+        v = velocity_fn(batch.sample_before, batch.sigma, prompt_index=batch.prompt_index)
+        return to_sde(v, batch.sample_before, batch.sigma, batch.sigma_next, noise_level=c.noise_level,
                       schedule=c.sde_schedule, prev_sample=batch.sample_after)
-        if c.regulated_clip:
-            log_ratio = regulated_log_ratio(step.mean.float(), batch.mean_old.float(), batch.std_old.float(),
-                                            batch.sample_after.float())
-        else:
-            log_ratio = step.log_prob - batch.log_prob_old
-        policy_loss, clip_fraction, ratio = clipped_surrogate(log_ratio, batch.advantage, clip_low=c.clip_range,
-                                                              clip_high=c.high, weights=self._step_weights(batch))
-        kl = torch.zeros((), device=policy_loss.device, dtype=policy_loss.dtype)
-        if c.kl_coefficient > 0.0 and self.reference_velocity_fn is not None:
-            with torch.no_grad():
-                rv = self.reference_velocity_fn(batch.sample_before, batch.sigma, prompt_index=batch.prompt_index)
-                ref = to_sde(rv, batch.sample_before, batch.sigma, batch.sigma_next, noise_level=c.noise_level,
-                             schedule=c.sde_schedule, prev_sample=batch.sample_after)
-            kl = kl_penalty(step.log_prob, ref.log_prob).mean()
+
+    def _log_ratio(self, step: Any, batch: RolloutBatch) -> torch.Tensor:
+        if not self.config.regulated_clip:
+            return step.log_prob - batch.log_prob_old
+        return regulated_log_ratio(step.mean.float(), batch.mean_old.float(), batch.std_old.float(),
+                                   batch.sample_after.float())
+
+    def _kl(self, step: Any, batch: RolloutBatch, like: torch.Tensor) -> torch.Tensor:
+        if self.config.kl_coefficient <= 0.0 or self.reference_velocity_fn is None:
+            return torch.zeros((), device=like.device, dtype=like.dtype)
+        with torch.no_grad():
+            reference = self._transition(self.reference_velocity_fn, batch)
+        return kl_penalty(step.log_prob, reference.log_prob).mean()
+
+    def loss(self, batch: RolloutBatch) -> tuple[torch.Tensor, GRPOMetrics]:
+        """Clipped surrogate of the policy's transitions plus the weighted KL term."""
+        c = self.config
+        step = self._transition(self.velocity_fn, batch)
+        policy_loss, clip_fraction, ratio = clipped_surrogate(self._log_ratio(step, batch), batch.advantage,
+                                                              clip_low=c.clip_range, clip_high=c.high,
+                                                              weights=self._step_weights(batch))
+        kl = self._kl(step, batch, policy_loss)
         total = policy_loss + c.kl_coefficient * kl
         adv = batch.advantage.detach()
-        return total, GRPOMetrics(loss=total.detach(), policy_loss=policy_loss.detach(), kl=kl.detach(),
-                                  clip_fraction=clip_fraction.detach(), ratio_mean=ratio.detach().mean(),
-                                  advantage_mean=adv.mean(), advantage_std=adv.std(unbiased=False))
+        summary = {"loss": total, "policy_loss": policy_loss, "kl": kl, "clip_fraction": clip_fraction,
+                   "ratio_mean": ratio.mean(), "advantage_mean": adv.mean(), "advantage_std": adv.std(unbiased=False)}
+        return total, GRPOMetrics(**{k: v.detach() for k, v in summary.items()})
 
     def train_step(self, batch: RolloutBatch) -> GRPOMetrics:
         """Backward of one minibatch, then a clipped optimizer step (skipped on device if non-finite)."""

@@ -78,71 +78,128 @@ class SimulationReport:
         return dest
 
     def render(self) -> str:
+        """A plain-text summary: one headline, then one aligned table per concern."""
+        d = self.to_dict()
         local = self.shape.sequence_length // max(1, self.dims.sequence_shard_size)
-        bar = "=" * 72
-        out = [bar, f"avgen_b200 simulation - {self.dims.describe()}", bar,
-               f"  device                {self.accelerator.name} ({self.accelerator.memory_gib:.0f} GiB)",
-               f"  parameters            {self.shape.parameters / 1e9:.2f} B",
-               f"  depth x width         {self.shape.depth} x {self.shape.width}",
-               f"  sequence length       {self.shape.sequence_length:,} tokens ({local:,} per rank)",
-               f"  global batch          {self.global_batch_size} (micro {self.shape.micro_batch_size} x accum "
-               f"{self.gradient_accumulation} x dp {self.dims.dp_size})", "",
-               f"MEMORY  {self.memory.total_gib:.1f} GiB per rank   {'FITS' if self.fits else 'DOES NOT FIT'}"]
-        for name, gib in self.memory.breakdown_gib().items():
-            if gib > 0.01:
-                out.append(f"    {name.removesuffix('_bytes'):<20} {gib:8.2f} GiB")
-        out += ["", f"COMPUTE  {self.compute.seconds * 1e3:.1f} ms/microbatch   MFU {self.mfu:.1%}   recompute "
-                    f"overhead {self.compute.recompute_overhead:.1%}", "",
-                f"COMMUNICATION  {self.communication.total_wire_gib:.2f} GiB/step   exposed "
-                f"{self.communication.exposed_seconds * 1e3:.1f} ms   scaling efficiency "
-                f"{self.communication.scaling_efficiency:.1%}"]
-        out += [f"    {label:<32} {sec * 1e3:8.2f} ms" for label, sec in self.communication.by_label().items()]
-        out += ["", f"THROUGHPUT  {self.step_seconds:.3f} s/step   {self.tokens_per_second / 1e6:.2f} M tokens/s"]
+        verdict = "fits" if d["fits"] else "DOES NOT FIT"
+        head = (f"{d['plan']} on {self.accelerator.name}: {self.step_seconds:.3f} s/step, "
+                f"{d['tokens_per_second'] / 1e6:.2f} M tok/s, MFU {d['mfu']:.1%}, {d['memory_gib']:.1f} GiB/rank "
+                f"({verdict})")
+        sections = [
+            ("model", [("parameters", f"{self.shape.parameters / 1e9:.2f} B ({self.shape.depth} x {self.shape.width})"),
+                       ("tokens", f"{self.shape.sequence_length:,} per sample, {local:,} per rank"),
+                       ("global batch", f"{d['global_batch_size']} = dp {self.dims.dp_size} x micro "
+                                        f"{self.shape.micro_batch_size} x accumulation {self.gradient_accumulation}")]),
+            ("memory per rank (GiB)", [(k.removesuffix("_bytes"), f"{v:.2f}")
+                                       for k, v in d["memory_breakdown_gib"].items() if v > 0.01]
+             + [("device", f"{self.accelerator.memory_gib:.0f}")]),
+            ("compute", [("per micro-batch", f"{d['compute_seconds'] * 1e3:.1f} ms"),
+                         ("recompute", f"{d['recompute_overhead']:.1%}")]),
+            ("communication (exposed ms)", [(k, f"{v * 1e3:.2f}") for k, v in d["comm_by_label_seconds"].items()]
+             + [("total on the wire", f"{d['comm_gib_per_step']:.2f} GiB/step"),
+                ("scaling efficiency", f"{d['scaling_efficiency']:.1%}")]),
+        ]
+        lines = [head]
+        for title, rows in sections:
+            width = max((len(k) for k, _ in rows), default=0)
+            lines.append(f"[{title}]")
+            lines += [f"  {k.ljust(width)}  {v}" for k, v in rows]
         if self.notes:
-            out += ["", "NOTES", *(f"    - {n}" for n in self.notes)]
-        out.append(bar)
-        return "\n".join(out)
+            lines.append("[advice]")
+            lines += [f"  * {n}" for n in self.notes]
+        return "\n".join(lines)
 
     def assert_no_regression(self, baseline: dict[str, Any], *, mfu_tolerance: float = 0.05,
                              memory_tolerance_gib: float = 2.0) -> None:
-        cur = self.to_dict()
-        if baseline.get("fits") and not cur["fits"]:
-            raise AssertionError(f"configuration no longer fits: {cur['memory_gib']:.1f} GiB > "
-                                 f"{self.accelerator.memory_gib:.0f} GiB (was {baseline.get('memory_gib')} GiB); "
-                                 f"dominant term {cur['dominant_memory_term']}")
-        grew = cur["memory_gib"] - float(baseline.get("memory_gib", 0.0))
-        if grew > memory_tolerance_gib:
-            raise AssertionError(f"per-rank memory grew by {grew:.2f} GiB (tolerance {memory_tolerance_gib} GiB); "
-                                 f"dominant term {cur['dominant_memory_term']}")
-        base_mfu = float(baseline.get("mfu", 0.0))
-        if base_mfu > 0 and (base_mfu - cur["mfu"]) / base_mfu > mfu_tolerance:
-            raise AssertionError(f"predicted MFU fell {(base_mfu - cur['mfu']) / base_mfu:.1%} ({base_mfu:.3f} -> "
-                                 f"{cur['mfu']:.3f}); communication bottleneck {cur['comm_bottleneck']}")
+        """Compare against a pinned report; raise one AssertionError naming every
+        metric that moved past its tolerance (fit lost, memory up, MFU down)."""
+        now = self.to_dict()
+        problems: list[str] = []
+        if bool(baseline.get("fits")) and not now["fits"]:
+            problems.append(f"fit lost: {now['memory_gib']:.1f} GiB on a {self.accelerator.memory_gib:.0f} GiB device")
+        pinned_mem = float(baseline.get("memory_gib", 0.0))
+        if now["memory_gib"] - pinned_mem > memory_tolerance_gib:
+            problems.append(f"memory {pinned_mem:.2f} -> {now['memory_gib']:.2f} GiB "
+                            f"(+{now['memory_gib'] - pinned_mem:.2f} > {memory_tolerance_gib})")
+        pinned_mfu = float(baseline.get("mfu", 0.0))
+        if pinned_mfu > 0.0 and now["mfu"] < pinned_mfu * (1.0 - mfu_tolerance):
+            problems.append(f"MFU {pinned_mfu:.3f} -> {now['mfu']:.3f} (more than {mfu_tolerance:.0%} lower)")
+        if problems:
+            raise AssertionError(f"{self.dims.describe()} regressed: " + "; ".join(problems)
+                                 + f" [largest memory term {now['dominant_memory_term']}, "
+                                   f"communication bottleneck {now['comm_bottleneck']}]")
+
+
+# Advisory rules: each looks at the estimate and returns a sentence or None. They
+# encode B200 / NVLink 5 facts: an HGX B200 node is one NVSwitch domain of 8 GPUs,
+# the ring attention kernel takes key tiles of 128 tokens, and exposed
+# communication above 5 % of a step is worth restructuring.
+_NODE_GPUS = 8
+
+
+def _rule_memory(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    need, have = memory.total_gib, accel.memory_gib
+    if need > have:
+        return f"needs {need:.1f} of {have:.0f} GiB: shrink {memory.dominant_term()} (more sharding or recompute)"
+    if need > 0.95 * have:
+        return f"{need:.1f} of {have:.0f} GiB leaves under 5 % headroom for allocator fragmentation"
+    return None
+
+
+def _rule_ring_tiles(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    if not dims.cp_enabled:
+        return None
+    if shape.sequence_length % dims.sequence_shard_size:
+        return (f"{shape.sequence_length} tokens do not split over cp x tp = {dims.sequence_shard_size}: pad the "
+                "sequence at the data boundary")
+    if (shape.sequence_length // dims.sequence_shard_size) % 128:
+        return "tokens per context-parallel rank are not a multiple of 128: the NVLink ring kernel falls back to NCCL"
+    return None
+
+
+def _rule_domains(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    inner = dims.tensor * (dims.context if dims.cp_enabled else 1)
+    if dims.tensor > _NODE_GPUS:
+        return f"tp={dims.tensor} leaves the {_NODE_GPUS}-GPU NVSwitch domain: keep tensor parallelism inside a node"
+    if inner > _NODE_GPUS:
+        return f"tp x cp = {inner} > {_NODE_GPUS}: ring steps cross InfiniBand; prefer cp inside a node"
+    return None
+
+
+def _rule_exposed(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    step = comm.estimated_step_seconds
+    if step > 0 and comm.exposed_seconds / step > 0.05:
+        return f"{comm.exposed_seconds / step:.0%} of the step waits on {comm.bottleneck()}"
+    return None
+
+
+def _rule_pipeline(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    if dims.pp_enabled and shape.depth < 4 * dims.pipeline:
+        return f"{shape.depth} blocks over pp={dims.pipeline} stages: under 4 blocks per stage, the bubble dominates"
+    return None
+
+
+def _rule_attention(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    frac = transformer_flops(shape)["attention_fraction"]
+    if frac > 0.5:
+        return f"attention is {frac:.0%} of forward FLOPs: its kernel speed sets the step time"
+    return None
+
+
+def _rule_policy(shape, dims, memory, comm, accel, policy):  # noqa: ANN001, ANN202
+    if accel.name == "B200" and policy.mode != "fused":
+        return f"activation policy {policy.mode!r} takes the per-layer path; 'fused' keeps only x, O and lse"
+    return None
+
+
+_RULES = (_rule_memory, _rule_domains, _rule_ring_tiles, _rule_exposed, _rule_attention, _rule_pipeline,
+          _rule_policy)
 
 
 def _advisories(shape: ModelShape, dims: ParallelDims, memory: MemoryEstimate, comm: CommunicationEstimate,
                 accel: Accelerator, policy: ActivationCheckpointConfig) -> tuple[str, ...]:
-    notes: list[str] = []
-    if dims.tensor > 8:
-        notes.append(f"tensor parallel degree {dims.tensor} spans NVLink domains; TP sits on the critical path twice "
-                     "per block and belongs inside one NVSwitch domain")
-    if dims.pp_enabled and dims.pipeline > shape.depth // 4:
-        notes.append(f"pipeline degree {dims.pipeline} leaves fewer than 4 blocks per stage; the bubble dominates")
-    if not memory.fits_in(accel.memory_gib):
-        notes.append(f"does not fit: {memory.total_gib:.1f} GiB needed, {accel.memory_gib:.0f} GiB available; "
-                     f"largest term {memory.dominant_term()}")
-    if comm.scaling_efficiency < 0.8:
-        notes.append(f"scaling efficiency {comm.scaling_efficiency:.0%}: {comm.bottleneck()} is not hidden")
-    frac = transformer_flops(shape)["attention_fraction"]
-    if frac > 0.5:
-        notes.append(f"attention is {frac:.0%} of forward FLOPs at {shape.sequence_length:,} tokens; the attention "
-                     "kernel and context parallelism matter more than parameter sharding")
-    if dims.cp_enabled and shape.sequence_length % dims.sequence_shard_size:
-        notes.append(f"sequence length {shape.sequence_length} does not divide by cp*tp = {dims.sequence_shard_size}; "
-                     "pad at the data boundary")
-    if policy.mode != "fused" and accel.name == "B200":
-        notes.append(f"policy {policy.mode!r} runs the eager block; the fused B200 block saves only x, O and lse")
-    return tuple(notes)
+    notes = (rule(shape, dims, memory, comm, accel, policy) for rule in _RULES)
+    return tuple(n for n in notes if n)
 
 
 def simulate_config(shape: ModelShape, dims: ParallelDims, *, accelerator: Accelerator = B200,

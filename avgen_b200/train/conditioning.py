@@ -56,6 +56,75 @@ class ConditioningSampler(Protocol):
     def sample(self, batch: MediaBatch, *, rng: RNGStreams) -> ConditioningPlan: ...
 
 
+def _resolve_mode(key: ConditionMode | str | int) -> ConditionMode:
+    """A condition mode from itself, its integer value or its (case-insensitive) name."""
+    if isinstance(key, ConditionMode):
+        return key
+    if isinstance(key, int):
+        return ConditionMode(key)
+    mode = ConditionMode.__members__.get(str(key).upper())
+    if mode is None:
+        raise KeyError(f"unknown condition mode {key!r}")
+    return mode
+
+
+@dataclass(frozen=True, slots=True)
+class _Draws:
+    """Every random quantity one plan needs, drawn up front from the conditioning stream."""
+
+    modes: torch.Tensor           # int64 [B]
+    prefix_fraction: torch.Tensor  # [B] continuation prefix as a fraction of the frames
+    keep_fraction: torch.Tensor    # [B] inpaint: share of tokens kept clean
+    keep_draw: torch.Tensor        # [B, T, H, W] uniform draw per token for inpainting
+    drop_video: torch.Tensor       # bool [B] anchor dropout
+    drop_audio: torch.Tensor
+    drop_text: torch.Tensor
+
+
+def _no_anchor(cfg, draws, frames, video_shape, audio_len):  # noqa: ANN001, ANN202
+    return None, None
+
+
+def _prefix_anchor(frames_kept: torch.Tensor, frames: int, video_shape: tuple[int, ...]) -> torch.Tensor:
+    index = torch.arange(frames, device=frames_kept.device)
+    return (index[None, :] < frames_kept[:, None])[:, :, None, None].expand(video_shape)
+
+
+def _continuation_anchor(cfg, draws, frames, video_shape, audio_len):  # noqa: ANN001, ANN202
+    kept = (draws.prefix_fraction * frames).to(torch.int64).clamp(1, max(frames - 1, 1))
+    return _prefix_anchor(kept, frames, video_shape), None
+
+
+def _image_anchor(cfg, draws, frames, video_shape, audio_len):  # noqa: ANN001, ANN202
+    kept = torch.full_like(draws.modes, min(cfg.image_frames, max(frames - 1, 1)))
+    return _prefix_anchor(kept, frames, video_shape), None
+
+
+def _inpaint_anchor(cfg, draws, frames, video_shape, audio_len):  # noqa: ANN001, ANN202
+    return draws.keep_draw < draws.keep_fraction[:, None, None, None], None
+
+
+def _video_to_audio_anchor(cfg, draws, frames, video_shape, audio_len):  # noqa: ANN001, ANN202
+    return torch.ones(video_shape, dtype=torch.bool, device=draws.modes.device), None
+
+
+def _audio_to_video_anchor(cfg, draws, frames, video_shape, audio_len):  # noqa: ANN001, ANN202
+    return None, torch.ones((video_shape[0], audio_len), dtype=torch.bool, device=draws.modes.device)
+
+
+# Which clean anchors each task gives the model (the mode's definition): a
+# continuation keeps a random prefix of frames, image-to-video the first frame(s),
+# inpainting a random share of tokens, V2A the whole video, A2V the whole audio.
+_ANCHORS = {
+    ConditionMode.JOINT: _no_anchor,
+    ConditionMode.CONTINUATION: _continuation_anchor,
+    ConditionMode.IMAGE_TO_VIDEO: _image_anchor,
+    ConditionMode.INPAINT: _inpaint_anchor,
+    ConditionMode.VIDEO_TO_AUDIO: _video_to_audio_anchor,
+    ConditionMode.AUDIO_TO_VIDEO: _audio_to_video_anchor,
+}
+
+
 @dataclass(frozen=True, slots=True)
 class MultiTaskConditioning:
     mode_weights: tuple[tuple[ConditionMode, float], ...] = field(default_factory=default_mode_weights)
@@ -67,24 +136,25 @@ class MultiTaskConditioning:
     audio_anchor_dropout: float = 0.1
 
     def __post_init__(self) -> None:
-        if not self.mode_weights:
+        modes = [m for m, _ in self.mode_weights]
+        bad = [m for m in modes if not isinstance(m, ConditionMode)]
+        if not modes:
             raise ValueError("mode_weights must contain at least one entry")
-        seen: set[ConditionMode] = set()
-        for mode, weight in self.mode_weights:
-            if not isinstance(mode, ConditionMode):
-                raise TypeError(f"mode_weights key must be a ConditionMode; got {mode!r}")
-            if mode in seen:
-                raise ValueError(f"mode_weights contains {mode.name} twice")
-            seen.add(mode)
-            if weight < 0.0:
-                raise ValueError(f"weight for {mode.name} must be >= 0")
-        if sum(w for _, w in self.mode_weights) <= 0.0:
+        if bad:
+            raise TypeError(f"mode_weights key must be a ConditionMode; got {bad[0]!r}")
+        repeated = {m for m in modes if modes.count(m) > 1}
+        if repeated:
+            raise ValueError(f"mode_weights contains {sorted(repeated)[0].name} twice")
+        negative = [m for m, w in self.mode_weights if w < 0.0]
+        if negative:
+            raise ValueError(f"weight for {negative[0].name} must be >= 0")
+        if not any(w > 0.0 for _, w in self.mode_weights):
             raise ValueError("mode_weights must contain a positive weight")
         for name in ("continuation_prefix", "inpaint_ratio"):
-            lo, hi = getattr(self, name)
-            require_probability(f"{name}[0]", lo)
-            require_probability(f"{name}[1]", hi)
-            if lo > hi:
+            bounds = getattr(self, name)
+            for i, value in enumerate(bounds):
+                require_probability(f"{name}[{i}]", value)
+            if bounds[0] > bounds[1]:
                 raise ValueError(f"{name} must be ordered (low, high)")
         if isinstance(self.image_frames, bool) or self.image_frames < 1:
             raise ValueError("image_frames must be >= 1")
@@ -93,59 +163,52 @@ class MultiTaskConditioning:
 
     @classmethod
     def from_weights(cls, weights: Mapping[ConditionMode | str | int, float], **options) -> MultiTaskConditioning:  # noqa: ANN003
-        resolved = []
-        for key, weight in weights.items():
-            if isinstance(key, ConditionMode):
-                mode = key
-            elif isinstance(key, int):
-                mode = ConditionMode(key)
-            else:
-                try:
-                    mode = ConditionMode[key.upper()]
-                except KeyError:
-                    raise KeyError(f"unknown condition mode {key!r}") from None
-            resolved.append((mode, float(weight)))
-        resolved.sort(key=lambda p: int(p[0]))
-        return cls(mode_weights=tuple(resolved), **options)
+        """Build from a mapping keyed by mode, mode name or mode value (ordered by mode value)."""
+        table = sorted(((_resolve_mode(k), float(w)) for k, w in weights.items()), key=lambda mw: int(mw[0]))
+        return cls(mode_weights=tuple(table), **options)
 
-    def sample(self, batch: MediaBatch, *, rng: RNGStreams) -> ConditioningPlan:
+    def _draw(self, batch: MediaBatch, generator: torch.Generator) -> _Draws:
         dev = batch.device
-        g = rng.conditioning
         size = batch.spec.batch_size
         _, _, frames, height, width = batch.spec.video_shape
-        a_frames = batch.spec.audio_tokens
-        modes = self._draw_modes(size, batch=batch, generator=g, device=dev)
-        video = torch.zeros((size, frames, height, width), dtype=torch.bool, device=dev)
-        audio = torch.zeros((size, a_frames), dtype=torch.bool, device=dev)
-        frame_index = torch.arange(frames, device=dev)[None]
-        lo, hi = self.continuation_prefix
-        ratio = lo + (hi - lo) * uniform((size,), generator=g, device=dev)
-        cont = (ratio * frames).to(torch.int64).clamp(1, max(frames - 1, 1))
-        prefix = torch.zeros((size,), dtype=torch.int64, device=dev)
-        image = torch.full_like(prefix, min(self.image_frames, max(frames - 1, 1)))
-        prefix = torch.where(modes == int(ConditionMode.CONTINUATION), cont, prefix)
-        prefix = torch.where(modes == int(ConditionMode.IMAGE_TO_VIDEO), image, prefix)
-        video |= (frame_index < prefix[:, None])[:, :, None, None]
-        lo, hi = self.inpaint_ratio
-        keep = lo + (hi - lo) * uniform((size,), generator=g, device=dev)
-        draw = uniform((size, frames, height, width), generator=g, device=dev)
-        video |= (draw < keep[:, None, None, None]) & (modes == int(ConditionMode.INPAINT))[:, None, None, None]
-        video |= (modes == int(ConditionMode.VIDEO_TO_AUDIO))[:, None, None, None]
-        audio |= (modes == int(ConditionMode.AUDIO_TO_VIDEO))[:, None]
-        video &= ~bernoulli((size,), self.video_anchor_dropout, generator=g, device=dev)[:, None, None, None]
-        audio &= ~bernoulli((size,), self.audio_anchor_dropout, generator=g, device=dev)[:, None]
-        video &= batch.video_mask
-        audio &= batch.audio_mask
-        drop_text = bernoulli((size,), self.text_dropout, generator=g, device=dev)
-        return ConditioningPlan(condition_mode=modes, video_conditioned=video, audio_conditioned=audio,
-                                drop_text=drop_text)
+
+        def between(bounds: tuple[float, float]) -> torch.Tensor:
+            return bounds[0] + (bounds[1] - bounds[0]) * uniform((size,), generator=generator, device=dev)
+
+        modes = self._draw_modes(size, batch=batch, generator=generator, device=dev)
+        prefix = between(self.continuation_prefix)
+        keep = between(self.inpaint_ratio)
+        keep_draw = uniform((size, frames, height, width), generator=generator, device=dev)
+        drop_video = bernoulli((size,), self.video_anchor_dropout, generator=generator, device=dev)
+        drop_audio = bernoulli((size,), self.audio_anchor_dropout, generator=generator, device=dev)
+        drop_text = bernoulli((size,), self.text_dropout, generator=generator, device=dev)
+        return _Draws(modes, prefix, keep, keep_draw, drop_video, drop_audio, drop_text)
+
+    def sample(self, batch: MediaBatch, *, rng: RNGStreams) -> ConditioningPlan:
+        """Draw a task per sample and the clean anchors it implies (masked by validity and anchor dropout)."""
+        draws = self._draw(batch, rng.conditioning)
+        size = batch.spec.batch_size
+        _, _, frames, height, width = batch.spec.video_shape
+        video_shape = (size, frames, height, width)
+        audio_len = batch.spec.audio_tokens
+        video = torch.zeros(video_shape, dtype=torch.bool, device=batch.device)
+        audio = torch.zeros((size, audio_len), dtype=torch.bool, device=batch.device)
+        for mode, anchor in _ANCHORS.items():
+            chosen = draws.modes == int(mode)
+            v, a = anchor(self, draws, frames, video_shape, audio_len)
+            if v is not None:
+                video |= v & chosen[:, None, None, None]
+            if a is not None:
+                audio |= a & chosen[:, None]
+        video &= batch.video_mask & ~draws.drop_video[:, None, None, None]
+        audio &= batch.audio_mask & ~draws.drop_audio[:, None]
+        return ConditioningPlan(condition_mode=draws.modes, video_conditioned=video, audio_conditioned=audio,
+                                drop_text=draws.drop_text)
 
     def _draw_modes(self, size: int, *, batch: MediaBatch, generator: torch.Generator,
                     device: torch.device) -> torch.Tensor:
-        modes = [m for m, _ in self.mode_weights]
-        weights = [w for _, w in self.mode_weights]
-        if not batch.spec.has_audio:
-            weights = [0.0 if m in _AUDIO_MODES else w for m, w in zip(modes, weights)]
-        idx = categorical(torch.tensor(weights, dtype=torch.float32), size, generator=generator, device=device)
-        lookup = torch.tensor([int(m) for m in modes], dtype=torch.int64, device=device)
-        return lookup[idx]
+        """Modes by weight; the audio tasks get weight 0 when the batch carries no audio."""
+        usable = [(m, 0.0 if (m in _AUDIO_MODES and not batch.spec.has_audio) else w) for m, w in self.mode_weights]
+        weights = torch.tensor([w for _, w in usable], dtype=torch.float32)
+        values = torch.tensor([int(m) for m, _ in usable], dtype=torch.int64, device=device)
+        return values[categorical(weights, size, generator=generator, device=device)]

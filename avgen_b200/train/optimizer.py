@@ -26,8 +26,8 @@ import torch.distributed as dist
 from torch import nn
 from torch.optim import Optimizer
 
-__all__ = ["DEFAULT_NO_DECAY_PATTERNS", "FusedAdamW", "ShardedAdamW", "build_optimizer", "build_param_groups",
-           "list_optimizers"]
+__all__ = ["DEFAULT_NO_DECAY_PATTERNS", "FusedAdamW", "MultiTensorAdamW", "ShardedAdamW", "build_optimizer",
+           "build_param_groups", "list_optimizers"]
 
 DEFAULT_NO_DECAY_PATTERNS: tuple[str, ...] = ("norm", "bias", "scale_shift", "embed")
 _OPTIMIZERS = ("adafactor", "adamw", "adamw_8bit")
@@ -390,6 +390,160 @@ class ShardedAdamW(FusedAdamW):
         return loss
 
 
+_CHUNK = 65536  # elements per block of the multi-tensor kernels
+
+
+def _local(t: torch.Tensor) -> torch.Tensor:
+    from torch.distributed.tensor import DTensor
+
+    return t._local_tensor if isinstance(t, DTensor) else t
+
+
+def _shard_groups(p: torch.Tensor) -> tuple[Any, ...]:
+    """Process groups over which ``p``'s gradient shards must be summed for the
+    global norm: one per mesh dimension that shards it (replicated dimensions hold
+    copies and are counted once)."""
+    from torch.distributed.tensor import DTensor, Shard
+
+    if not isinstance(p, DTensor):
+        return ()
+    mesh = p.device_mesh
+    return tuple(mesh.get_group(i) for i, pl in enumerate(p.placements) if isinstance(pl, Shard))
+
+
+class MultiTensorAdamW(Optimizer):
+    """AdamW over sharded parameters (FSDP2 / tensor-parallel DTensors) with the
+    multi-tensor sm_100a kernels: one squared-norm launch and one AdamW launch
+    per parameter group over a table of every parameter's local shard, the
+    global-norm clip coefficient and the non-finite skip flag computed on the
+    device (the same semantics as :class:`FusedAdamW`, which needs plain
+    tensors it can re-home into flat buffers). Moments are DTensors shaped and
+    placed like their parameters, so ``state_dict`` and DCP reshard them as
+    they do torch's AdamW state. The norm sums each parameter's shard partials
+    over the mesh dimensions that shard it. On CPU the same steps run with
+    torch operations (``gloo`` tests)."""
+
+    def __init__(self, params: Iterable[Any], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.95),
+                 eps: float = 1e-8, weight_decay: float = 0.0) -> None:
+        super().__init__(params, {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay})
+        self.max_grad_norm: float | None = None
+        self.last_grad_norm: torch.Tensor | None = None
+        self.last_nonfinite: torch.Tensor | None = None
+        self._step = 0
+        self._tables: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                if _local(p).dtype != torch.float32:
+                    raise TypeError("MultiTensorAdamW keeps fp32 parameters; got " + str(_local(p).dtype))
+                st = self.state[p]
+                st["step"] = torch.tensor(0.0)
+                st["exp_avg"] = torch.zeros_like(p)
+                st["exp_avg_sq"] = torch.zeros_like(p)
+
+    def _rows(self, group: dict[str, Any]) -> list[tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]]:
+        rows = []
+        for p in group["params"]:
+            if p.grad is None:
+                continue
+            st = self.state[p]
+            rows.append((_local(p), _local(p.grad), _local(st["exp_avg"]), _local(st["exp_avg_sq"])))
+        return rows
+
+    def _table(self, rows: list[tuple[torch.Tensor, ...]], dev: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+        """Device tables: addresses [T, 4] (rebuilt every step: gradients move) and chunks [C, 3] (cached)."""
+        for t in (x for r in rows for x in r):
+            if not t.is_contiguous() or t.dtype != torch.float32:
+                raise ValueError("multi-tensor AdamW needs contiguous fp32 shards")
+        numels = tuple(r[0].numel() for r in rows)
+        addrs = torch.tensor([[t.data_ptr() for t in r] for r in rows], dtype=torch.int64)
+        key = (dev, numels)
+        chunks = self._tables.get(key)
+        if chunks is None:
+            spec = [(i, s, min(_CHUNK, n - s)) for i, n in enumerate(numels) for s in range(0, n, _CHUNK)]
+            chunks = torch.tensor(spec or [[0, 0, 0]], dtype=torch.int64).to(dev)
+            if not spec:
+                chunks = chunks[:0]
+            self._tables[key] = chunks
+        return addrs.pin_memory().to(dev, non_blocking=True), chunks
+
+    def grad_norm(self) -> torch.Tensor:
+        """Global L2 norm of all gradients across shards (device scalar, no host sync)."""
+        import torch.distributed as dist
+
+        params = [p for g in self.param_groups for p in g["params"] if p.grad is not None]
+        if not params:
+            return torch.zeros((), dtype=torch.float32)
+        dev = _local(params[0]).device
+        by_groups: dict[tuple, list[torch.Tensor]] = {}
+        for p in params:
+            by_groups.setdefault(_shard_groups(p), []).append(p)
+        total = torch.zeros(1, dtype=torch.float32, device=dev)
+        for groups, ps in by_groups.items():
+            acc = torch.zeros(1, dtype=torch.float32, device=dev)
+            if dev.type == "cuda":
+                from avgen_b200.ops import kernels as K
+                from avgen_b200.ops._ext import load
+
+                rows = [(_local(p), _local(p.grad), _local(p.grad), _local(p.grad)) for p in ps]
+                addrs, chunks = self._table(rows, dev)
+                load().mt_sq_norm(addrs, chunks, acc)
+                K._count()
+            else:
+                for p in ps:
+                    acc += _local(p.grad).float().pow(2).sum()
+            for g in groups:
+                dist.all_reduce(acc, group=g)
+            total += acc
+        return total.sqrt()[0]
+
+    @torch.no_grad()
+    def step(self, closure: Any = None, *, max_grad_norm: float | None = None) -> Any:
+        loss = closure() if closure is not None else None
+        from avgen_b200.models.linear import bump_weight_epoch
+
+        self._step += 1
+        norm = self.grad_norm()
+        nonfinite = ~torch.isfinite(norm)
+        clip = max_grad_norm if max_grad_norm is not None else self.max_grad_norm
+        scale = torch.clamp(clip / (norm + 1e-6), max=1.0) if clip is not None else torch.ones_like(norm)
+        scale = torch.where(nonfinite, torch.zeros_like(scale), scale).reshape(1).float()
+        skip = nonfinite.to(torch.int32).reshape(1)
+        self.last_grad_norm = norm
+        self.last_nonfinite = nonfinite
+        for group in self.param_groups:
+            b1, b2 = group["betas"]
+            rows = self._rows(group)
+            if not rows:
+                continue
+            for p in group["params"]:
+                if p.grad is not None:
+                    self.state[p]["step"] = torch.tensor(float(self._step))
+            dev = rows[0][0].device
+            if dev.type == "cuda":
+                from avgen_b200.ops import kernels as K
+                from avgen_b200.ops._ext import load
+
+                addrs, chunks = self._table(rows, dev)
+                load().mt_adamw(addrs, chunks, group["lr"], b1, b2, group["eps"], group["weight_decay"], self._step,
+                                scale.to(dev), skip.to(dev))
+                K._count()
+            else:
+                for prm, g, m, v in rows:
+                    _adamw_reference({"param": prm, "grad": g, "exp_avg": m, "exp_avg_sq": v}, lr=group["lr"],
+                                     beta1=b1, beta2=b2, eps=group["eps"], weight_decay=group["weight_decay"],
+                                     step=self._step, scale=scale, nonfinite=nonfinite)
+        bump_weight_epoch()
+        return loss
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        super().zero_grad(set_to_none=set_to_none)
+
+    def load_state_dict(self, state_dict: dict[str, Any]) -> None:
+        super().load_state_dict(state_dict)
+        steps = [float(st["step"]) for st in self.state.values() if "step" in st]
+        self._step = int(max(steps)) if steps else 0
+
+
 def _adamw_reference(flat: dict[str, torch.Tensor], *, lr: float, beta1: float, beta2: float, eps: float,
                      weight_decay: float, step: int, scale: torch.Tensor, nonfinite: torch.Tensor) -> None:
     """CPU fp32 AdamW over a flat buffer (same maths as the kernel)."""
@@ -423,7 +577,10 @@ def build_optimizer(model: nn.Module, *, name: str = "adamw", lr: float, weight_
 
         on_cuda = all(p.device.type == "cuda" for g in groups for p in g["params"])
         if any(isinstance(p, DTensor) for g in groups for p in g["params"]):
-            # FSDP / tensor-parallel shards: per-shard updates; the flat-buffer kernel needs plain tensors
+            # FSDP / tensor-parallel shards: multi-tensor kernels over every local shard
+            fp32 = all(p.dtype == torch.float32 for g in groups for p in g["params"])
+            if fused is not False and fp32:
+                return MultiTensorAdamW(groups, lr=lr, betas=betas, eps=eps)
             return torch.optim.AdamW(groups, lr=lr, betas=betas, eps=eps, fused=on_cuda or None)
         use_fused = on_cuda if fused is None else fused
         if shard_group is not None:

@@ -24,7 +24,7 @@ from avgen_b200.core.metrics import StepMetrics
 from avgen_b200.core.patchify import GridPatchifier, Patchifier
 from avgen_b200.core.state import TrainState
 from avgen_b200.train.objective import Objective, ObjectiveOutput
-from avgen_b200.train.optimizer import FusedAdamW
+from avgen_b200.train.optimizer import FusedAdamW, MultiTensorAdamW
 
 __all__ = ["Curriculum", "CurriculumStage", "MetricSink", "ResolutionBucket", "Trainer", "TrainerCallback",
            "TrainerConfig", "optimizer_update", "train_step"]
@@ -179,7 +179,7 @@ def optimizer_update(state: TrainState, *, max_grad_norm: float | None = None, p
     dev = next((p.device for p in state.model.parameters()), torch.device("cpu"))
     finite = torch.ones((), dtype=torch.bool, device=dev) if finite is None else finite
     grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
-    if isinstance(opt, FusedAdamW):
+    if isinstance(opt, (FusedAdamW, MultiTensorAdamW)):
         opt.step(max_grad_norm=max_grad_norm)
         grad_norm = opt.last_grad_norm.to(torch.float32).to(dev)
         finite = finite & ~opt.last_nonfinite.to(dev)

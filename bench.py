@@ -179,21 +179,16 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     from avgen_b200.data.synthetic_batch import random_batch
     from avgen_b200.models import build_model
     from avgen_b200.ops import kernels as K
-    from avgen_b200.parallel.context import apply_context_parallel
+    from avgen_b200.parallel import ActivationCheckpointConfig, ParallelConfig, ParallelDims, parallelize
     from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, Trainer,
                                   TrainerConfig, build_optimizer, build_timestep_sampler, train_step)
 
     dev = torch.device("cuda", local)
     cp, dp = layout(world)
-    mesh = cp_mesh = None
-    if world > 1:
-        from torch.distributed.device_mesh import init_device_mesh
-
-        mesh = init_device_mesh("cuda", (dp, cp), mesh_dim_names=("dp", "cp"))
-        cp_mesh = mesh["cp"] if cp > 1 else None
-        data_rank = mesh["dp"].get_local_rank() if dp > 1 else 0
-    else:
-        data_rank = 0
+    # The named config's layout through the public API: parameters (and AdamW
+    # state) sharded over dp_shard x cp (FSDP2, collectives over NVLink peer
+    # memory), global attention over the cp ranks (NVLink ring).
+    dims = ParallelDims(world_size=world, dp_shard=dp, context=cp)
     torch.manual_seed(1234)
     with torch.device("meta"):
         model = build_model("video_dit", {"width": WIDTH, "depth": args.depth, "num_heads": HEADS,
@@ -201,12 +196,15 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
                                           "in_channels": CHANNELS})
     model = model.to_empty(device=dev)
     model.init_weights()
-    apply_context_parallel(model, cp_mesh)
-    optimizer = build_optimizer(model, lr=1e-4, weight_decay=0.0, dp_group=dist.group.WORLD if world > 1 else None)
+    pm = parallelize(model, dims, config=ParallelConfig(activation_checkpoint=ActivationCheckpointConfig(mode="none")))
+    model = pm.model
+    cp_mesh = pm.cp_mesh
+    data_rank = dims.data_coordinates(pm.mesh)[0] if pm.mesh is not None else 0
+    optimizer = build_optimizer(model, lr=1e-4, weight_decay=0.0, dp_group=pm.data_group)
     state = TrainState(model=model, optimizer=optimizer, rng=RNGStreams.for_rank(0, data_rank=data_rank))
     objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("shifted_logit_normal"),
                                       MultiTaskConditioning())
-    patchifier = model.patchifier
+    patchifier = pm.model.patchifier
     micro = cp
     gen = torch.Generator().manual_seed(1000 + data_rank)
     shape = dict(batch=1, channels=CHANNELS, frames=args.frames, height=HEIGHT, width=WIDTH_PX,
@@ -222,6 +220,10 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
                                     microbatch_index=m, max_grad_norm=1.0, cp_mesh=cp_mesh, data_world=dp)
         return metrics
 
+    from avgen_b200.telemetry import comm as exposed
+
+    if world > 1:
+        exposed.instrument_fsdp(model)
     for _ in range(args.warmup):
         step(dev_batches)
     torch.cuda.synchronize()
@@ -229,6 +231,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     clocks = ClockSampler()
     if rank == 0:
         clocks.start()
+    exposed.enable(world > 1)
+    exposed.reset()
     launches0 = K.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
@@ -240,18 +244,24 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     torch.cuda.synchronize()
     barrier()
     launches = (K.launch_count() - launches0)
+    exposed.enable(False)
     clock_info = clocks.stop(list(range(world))) if rank == 0 else {}
+    sm_mhz = max_over_ranks(float(clock_info.get("sm_mhz") or 0.0)) if world > 1 else 0.0
+    comm_ms = exposed.summary(sm_mhz or None)
     if args.profile_step:
         _profile_one_step(lambda: step(dev_batches), rank)
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    # exposed communication per step: each source's max over ranks (ranks wait for the slowest)
+    comm = {k: max_over_ranks(v) / args.steps for k, v in sorted(comm_ms.items())} if world > 1 else {}
+    ring_ms = sum(v for k, v in comm.items() if k.startswith("ring"))
     loss_val = float(metrics.loss.item())
     from avgen_b200.ops._ext import check_errors
 
     err = check_errors(local)
 
     # ------------------------------------------------------------------ end to end through the Trainer
-    trainer = Trainer(state, objective, type("P", (), {"cp_mesh": cp_mesh, "pp_mesh": None})(),
-                      TrainerConfig(gradient_accumulation_steps=micro, max_grad_norm=1.0, data_world=dp))
+    trainer = Trainer(state, objective, pm, TrainerConfig(gradient_accumulation_steps=micro, max_grad_norm=1.0,
+                                                          data_world=dp))
     host = [random_batch(**shape, generator=gen, pin=True) for _ in range(micro)]
     h2d = sum(b.nbytes() for b in host)
     torch.cuda.synchronize()
@@ -274,8 +284,11 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
         "gpu_launches": launches, "gpu_launches_per_step": launches // max(1, args.steps),
         "e2e": {"value": samples_per_step / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
+        "exposed_comm": {"ms_per_step": sum(comm.values()), "share_of_step": sum(comm.values()) / ms,
+                         "ring_ms_per_step": ring_ms, "ring_share_of_step": ring_ms / ms,
+                         "by_source_ms_per_step": comm} if world > 1 else None,
         "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro,
-        "params": sum(p.numel() for p in model.parameters()),
+        "params": sum(p.numel() for p in model.parameters()), "applied": list(pm.applied),
         "peak_mem_gib": torch.cuda.max_memory_allocated(dev) / 2**30,
     }
 
@@ -456,6 +469,9 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
         * value / (world * PEAK_NOMINAL),
         "loss": loss_val, "e2e": {"value": world / e2e_s, "unit": "samples/s", "h2d_bytes_per_step": int(h2d),
                                   "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
+        "exposed_comm": {"ms_per_step": sum(comm.values()), "share_of_step": sum(comm.values()) / ms,
+                         "ring_ms_per_step": ring_ms, "ring_share_of_step": ring_ms / ms,
+                         "by_source_ms_per_step": comm} if world > 1 else None,
         "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro, "ac_mode": ac_mode,
         "ac_attempts": attempts,
         "ref_variant": ("ring (context_parallel_region)" if use_ring else
@@ -511,7 +527,10 @@ def main() -> None:
                 line["gpu_launches"] = out["gpu_launches"]
                 line["kernel_errors"] = out["kernel_errors"]
                 line["params"] = out["params"]
+                line["config"]["applied"] = out["applied"]
                 line["peak_mem_gib"] = round(out["peak_mem_gib"], 1)
+                if out["exposed_comm"] is not None:
+                    line["exposed_comm"] = out["exposed_comm"]
             if args.depth != DEPTH or args.frames != FRAMES:
                 line["note"] = "reduced model/config: not a valid benchmark line"
             print(json.dumps(line), flush=True)

@@ -118,14 +118,18 @@ def _tp_worker(rank: int, world: int) -> None:
         torch.testing.assert_close(g, ref_grads[n], rtol=1e-3, atol=1e-5, msg=n)
 
 
-def _cp_worker(rank: int, world: int) -> None:
-    from avgen_b200.core.model_input import ModelOutput  # noqa: F401
-    from avgen_b200.parallel import ParallelDims, gather_tokens, parallelize, shard_stream
+def _cp_worker(rank: int, world: int, sharded: bool = True) -> None:
+    from torch.distributed.tensor import DTensor
+
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PrecisionConfig, gather_tokens, parallelize, shard_stream
 
     ref_outs, ref_grads = _reference_grads([31])
     model = _model()
     dims = ParallelDims(world_size=world, context=world)
-    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"))
+    cfg = ParallelConfig(precision=PrecisionConfig(param_dtype="float32"), shard_parameters=sharded)
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"), config=cfg)
+    # cp alone shards parameters over the context ranks, as the reference does
+    assert any(a.startswith("fsdp(cp=") for a in pm.applied) == sharded, pm.applied
     inputs = _inputs(31, model)
     local = inputs.replace_streams(video=shard_stream(inputs.video, pm.cp_mesh))
     out = pm.model(local)
@@ -133,9 +137,52 @@ def _cp_worker(rank: int, world: int) -> None:
     torch.testing.assert_close(full, ref_outs[0], rtol=1e-4, atol=1e-5)
     _loss(out).backward()  # per-shard partial loss: the full gradient is the sum over shards
     for n, p in pm.model.named_parameters():
-        g = p.grad.clone()
-        dist.all_reduce(g)
+        if isinstance(p.grad, DTensor):  # FSDP averaged the shards' gradients over the cp ranks
+            g = p.grad.full_tensor() * world
+        else:
+            g = p.grad.clone()
+            dist.all_reduce(g)
         torch.testing.assert_close(g, ref_grads[n], rtol=1e-3, atol=1e-5, msg=n)
+
+
+def _cp_replicated_worker(rank: int, world: int) -> None:
+    _cp_worker(rank, world, sharded=False)
+
+
+def _sharded_adamw_worker(rank: int, world: int) -> None:
+    """AdamW over FSDP-sharded parameters (the multi-tensor optimizer) takes the same
+    two clipped steps as torch's AdamW on the unsharded model."""
+    from torch.distributed.tensor import DTensor
+
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PrecisionConfig, parallelize
+    from avgen_b200.train import build_optimizer
+    from avgen_b200.train.optimizer import MultiTensorAdamW
+
+    ref = _model()
+    ref_opt = torch.optim.AdamW(ref.parameters(), lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.0)
+    model = _model()
+    dims = ParallelDims(world_size=world, dp_shard=world)
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"),
+                     config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32")))
+    opt = build_optimizer(pm.model, lr=1e-2, weight_decay=0.0)
+    assert isinstance(opt, MultiTensorAdamW)
+    for step, seeds in enumerate(([10, 11], [12, 13])):
+        ref_opt.zero_grad()
+        for s in seeds:  # the unsharded model sees both ranks' samples (mean)
+            (_loss(ref(_inputs(s, ref))) / len(seeds)).backward()
+        torch.nn.utils.clip_grad_norm_(ref.parameters(), 0.05)
+        ref_opt.step()
+        opt.zero_grad()
+        _loss(pm.model(_inputs(seeds[rank], model))).backward()  # FSDP averages over the 2 ranks
+        opt.step(max_grad_norm=0.05)
+        assert not bool(opt.last_nonfinite)
+        for (n, p), (_, q) in zip(pm.model.named_parameters(), ref.named_parameters()):
+            full = p.full_tensor() if isinstance(p, DTensor) else p
+            err = (full.detach() - q.detach()).abs().max().item()
+            assert err <= 1e-6 + 1e-4 * q.detach().abs().max().item(), f"step {step}: {n}: {err} (|ref| {q.abs().max().item()}, grad None: {p.grad is None})"
+    # the optimizer state is per-parameter DTensors placed like the parameters (DCP reshards them)
+    st = opt.state_dict()["state"]
+    assert all(isinstance(v["exp_avg"], DTensor) for v in st.values())
 
 
 def _nonfinite_worker(rank: int, world: int) -> None:
@@ -186,8 +233,10 @@ def _shards_worker(rank: int, world: int) -> None:
     assert len(allids) == len(set(allids)) == 37
 
 
-@pytest.mark.parametrize("worker", [_fsdp_worker, _tp_worker, _cp_worker, _nonfinite_worker],
-                         ids=["fsdp", "tensor_parallel", "context_parallel", "nonfinite_skip"])
+@pytest.mark.parametrize("worker", [_fsdp_worker, _tp_worker, _cp_worker, _cp_replicated_worker, _nonfinite_worker,
+                                    _sharded_adamw_worker],
+                         ids=["fsdp", "tensor_parallel", "context_parallel", "context_parallel_replicated",
+                              "nonfinite_skip", "sharded_adamw"])
 def test_two_rank_parallelism(worker) -> None:  # noqa: ANN001
     _spawn(worker)
 

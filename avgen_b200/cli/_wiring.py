@@ -18,7 +18,7 @@ from typing import Any
 import torch
 from torch import nn
 
-__all__ = ["RunStack", "build_run", "run_training"]
+__all__ = ["RunStack", "build_run", "build_telemetry", "run_training"]
 
 _LOG = logging.getLogger(__name__)
 
@@ -97,7 +97,8 @@ def build_run(config: Any, *, adapt: Callable[[nn.Module], nn.Module] | None = N
                                                           eval_every=t.eval_every, checkpoint_every=ck.save_every,
                                                           data_world=data_world),
                       patchifier=getattr(model, "patchifier", None),
-                      callbacks=[_CheckpointCallback(manager, pm, ck.async_save)], logger=logger)
+                      callbacks=[_CheckpointCallback(manager, pm, ck.async_save)], logger=logger,
+                      telemetry=build_telemetry(config, env=env, mesh=mesh, output_dir=out))
     if ck.resume:
         step = None if ck.resume == "latest" else None
         path = manager.root if ck.resume == "latest" else Path(ck.resume)
@@ -110,6 +111,37 @@ def build_run(config: Any, *, adapt: Callable[[nn.Module], nn.Module] | None = N
                 CheckpointManager(path.parent).load(state, parallel=pm, step=_step_of(path))
             _LOG.info("resumed at step %s", found)
     return RunStack(config, env, pm, state, objective, loader, trainer, manager, logger, accumulation, out)
+
+
+def build_telemetry(config: Any, *, env: Any, mesh: Any, output_dir: Path) -> Any:
+    """The fit loop's measurements from ``config.telemetry``: metric means over each
+    log window (averaged over data ranks), device-timed throughput with MFU of the
+    configured model (max over ranks), an optional profiler window and memory
+    reports."""
+    from avgen_b200.config.resolve import build_model_shape
+    from avgen_b200.simulate.compute import transformer_flops
+    from avgen_b200.telemetry.metrics import MemoryReporter, MetricAccumulator, ThroughputMeter
+    from avgen_b200.telemetry.profiler import profile_steps
+    from avgen_b200.train import TrainerTelemetry
+
+    tel = config.telemetry
+    data_mesh = None
+    if mesh is not None:
+        from avgen_b200.parallel.dims import submesh
+
+        data_mesh = next((m for m in (submesh(mesh, n) for n in ("dp_cp", "dp_shard_cp", "dp_replicate", "dp_shard",
+                                                                   "cp")) if m is not None), None)
+    shape = build_model_shape(config)
+    per_sample = transformer_flops(shape)["total"] / max(1, shape.micro_batch_size) if tel.report_mfu else 0.0
+    import torch.distributed as dist
+
+    world_group = dist.group.WORLD if env.world_size > 1 else None
+    throughput = ThroughputMeter(flops_per_sample=per_sample, world_size=env.world_size, group=world_group)
+    profiler = (profile_steps(output_dir / "profile", active=tel.profile_steps, warmup=tel.profile_warmup)
+                if tel.profile_steps > 0 else None)
+    memory = MemoryReporter(env.device) if tel.memory_report_every > 0 else None
+    return TrainerTelemetry(accumulator=MetricAccumulator(mesh=data_mesh), throughput=throughput, profiler=profiler,
+                            memory=memory, memory_every=tel.memory_report_every)
 
 
 def _sampler_options(t: Any) -> dict[str, Any]:

@@ -901,8 +901,8 @@ __global__ void __launch_bounds__(384, 1)
 //  * dV and dK read P^T / dS^T from TMEM (the TS form: no shared-memory traffic
 //    for A); the shared dS^T tile is the MN-major B operand of dQ^T, whose A
 //    operand is the K tile read MN-major.
-//  * dQ^T of a pair (128 d x 64 q, fp32) lands in the dP^T buffer after dK has
-//    read it. Four epilogue warps drain it through shared memory and add it into
+//  * dQ^T of a pair (128 d x 64 q, fp32) lands in the S^T buffer after dV has
+//    read P^T from it, so the next pair's dP^T can start while dQ^T drains. Four epilogue warps drain it through shared memory and add it into
 //    a global fp32 dQ^T accumulator [B*H, 128, ld] with TMA bulk reduce-add, two
 //    32 x 32 swizzled boxes per warp (measured faster than per-thread
 //    red.global.add, whose load/store-pipe traffic slows the MMA operand reads).
@@ -913,7 +913,7 @@ __global__ void __launch_bounds__(384, 1)
 // key is masked carry lse = +inf (P = 0), and masked keys or keys past Lk get
 // P = dS = 0 through a per-thread select (their dS^T would otherwise reach dQ).
 //
-// TMEM columns: dV [0,128), dK [128,256), S^T[b] at 256 + 64b, dP^T / dQ^T[b] at 384 + 64b.
+// TMEM columns: dV [0,128), dK [128,256), S^T / dQ^T[b] at 256 + 64b, dP^T[b] at 384 + 64b.
 struct FusedBwdSmem {
   static constexpr int K = 0;            // 2 chunks x 16 KB (128 keys x 64 d, SW128)
   static constexpr int V = 32768;
@@ -969,7 +969,7 @@ __global__ void __launch_bounds__(512, 1)
   // diagnostics: SM clock stamps of CTA 0, 24 per iteration, first 64 iterations. Slots:
   // 0 MMA thread passes p_full(i), 1 it passes dq_empty, 2 softmax starts, 3 warp 4 arrives,
   // 4 drain sees dq_full, 5/6/7 dV/dK/dQ^T(i) complete, 8-15 softmax warps arrive,
-  // 16-19 drain warps release dQ^T, 20/21 S^T/dP^T(i+2) complete.
+  // 16-19 drain warps release dQ^T, 20/21 dP^T/S^T(i+2) complete.
   long long* trace = (kTrace && blockIdx.x == 0) ? p.trace : nullptr;
   auto stamp = [&](int i, int slot) {
     if (trace != nullptr && i < 64) trace[i * 24 + slot] = clock64();
@@ -1084,8 +1084,8 @@ __global__ void __launch_bounds__(512, 1)
                       (i > 0 || kk > 0) ? 1u : 0u);
         if (trace != nullptr) mma_commit(&trace_bar[1]);
 #pragma unroll
-        for (int kk = 0; kk < kTile / 16; ++kk)
-          mma_bf16_ss(tmem + 384 + 64 * buf, dKt + static_cast<uint64_t>(kk * 128),
+        for (int kk = 0; kk < kTile / 16; ++kk)  // into the S^T buffer: dV(i) has read P^T(i) (in order)
+          mma_bf16_ss(tmem + 256 + 64 * buf, dKt + static_cast<uint64_t>(kk * 128),
                       dsM + static_cast<uint64_t>(kk * 128), idQ, kk > 0 ? 1u : 0u);
         mma_commit(&dq_full[buf]);
         if (trace != nullptr) mma_commit(&trace_bar[2]);
@@ -1098,16 +1098,16 @@ __global__ void __launch_bounds__(512, 1)
           break;
         tc_fence_after();
         if (elect_one()) {
-          issue_s(i + 2);  // S^T buffer: in order after dV(i) read P^T(i)
+          issue_dp(i + 2);  // dP^T buffer: in order after dK(i) read dS^T(i); runs while dQ^T(i) drains
           if (trace != nullptr) mma_commit(&trace_bar[3]);
         }
         __syncwarp();
-        // dP^T buffer holds dQ^T(i) until the epilogue has read it
+        // the S^T buffer holds dQ^T(i) until the epilogue has read it
         if (!mbar_wait(&dq_empty[buf], (i >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
         if (elect_one()) {
           stamp(i, 1);
-          issue_dp(i + 2);
+          issue_s(i + 2);
           mma_commit(&sdp_full[buf]);
           if (trace != nullptr) mma_commit(&trace_bar[4]);
         }
@@ -1223,8 +1223,8 @@ __global__ void __launch_bounds__(512, 1)
       tc_fence_after();
       if (warp == 12 && lane == 0) stamp(i, 4);
       uint32_t v0[32], v1[32];
-      tmem_ld32(tmem + lane_base + 384 + 64 * buf, v0);
-      tmem_ld32(tmem + lane_base + 384 + 64 * buf + 32, v1);
+      tmem_ld32(tmem + lane_base + 256 + 64 * buf, v0);
+      tmem_ld32(tmem + lane_base + 256 + 64 * buf + 32, v1);
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(&dq_empty[buf]);

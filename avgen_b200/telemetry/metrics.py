@@ -16,6 +16,8 @@ import statistics
 import time
 from dataclasses import dataclass, fields
 
+from typing import Any
+
 import torch
 import torch.distributed as dist
 from torch.distributed.device_mesh import DeviceMesh
@@ -89,66 +91,72 @@ class ThroughputReport:
 
 
 class ThroughputMeter:
-    """Device-timed step throughput and model FLOPs utilisation."""
+    """Device-timed step throughput and model FLOPs utilisation.
+
+    With CUDA, each ``step()`` records an event on the current stream and
+    returns at once (no host synchronisation); step times are read from the
+    events when ``report()`` is called, which synchronises once. Without CUDA
+    the host clock is used. ``report()`` takes the max over ``mesh``'s ranks of
+    the window's total time (the slowest rank sets the pace)."""
 
     def __init__(self, *, flops_per_sample: float = 0.0, hardware_flops_per_sample: float | None = None,
                  peak_flops: float = 2.25e15, world_size: int = 1, mesh: DeviceMesh | None = None,
-                 use_cuda_events: bool | None = None) -> None:
+                 use_cuda_events: bool | None = None, group: Any = None) -> None:
+        self._group = mesh.get_group() if mesh is not None and mesh.size() > 1 else group
         self._fps = flops_per_sample
         self._hfps = hardware_flops_per_sample if hardware_flops_per_sample is not None else flops_per_sample
         self._peak = peak_flops
         self._world = world_size
         self._mesh = mesh
         self._events = torch.cuda.is_available() if use_cuda_events is None else use_cuda_events
-        self._times: list[float] = []
+        self._marks: list[object] = []  # window start, then one mark per step (events or host times)
         self._samples = 0
         self._tokens = 0
-        self._last: object | None = None
+
+    def _mark(self) -> object:
+        if not self._events:
+            return time.perf_counter()
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
+        return ev
 
     def start(self) -> None:
-        if self._events:
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            self._last = ev
-        else:
-            self._last = time.perf_counter()
+        self._marks = [self._mark()]
 
-    def step(self, *, samples: int = 0, tokens: int = 0) -> float:
-        """Close the current step (seconds, device-timed when CUDA is available)."""
-        if self._last is None:
+    def step(self, *, samples: int = 0, tokens: int = 0) -> None:
+        """Close the current step."""
+        if not self._marks:
             self.start()
-            return 0.0
-        if self._events:
-            ev = torch.cuda.Event(enable_timing=True)
-            ev.record()
-            ev.synchronize()
-            dt = self._last.elapsed_time(ev) / 1000.0  # type: ignore[union-attr]
-            self._last = ev
-        else:
-            now = time.perf_counter()
-            dt = now - self._last  # type: ignore[operator]
-            self._last = now
-        self._times.append(dt)
+            return
+        self._marks.append(self._mark())
         self._samples += samples
         self._tokens += tokens
-        return dt
+
+    def _step_times(self) -> list[float]:
+        if len(self._marks) < 2:
+            return []
+        if not self._events:
+            return [b - a for a, b in zip(self._marks, self._marks[1:])]  # type: ignore[operator]
+        self._marks[-1].synchronize()  # type: ignore[union-attr]
+        return [a.elapsed_time(b) / 1000.0 for a, b in zip(self._marks, self._marks[1:])]  # type: ignore[union-attr]
 
     def report(self, *, reset: bool = True) -> ThroughputReport:
-        times = sorted(self._times) or [float("nan")]
-        total = sum(self._times)
-        if self._mesh is not None and self._mesh.size() > 1 and dist.is_initialized():
+        step_times = self._step_times()
+        times = sorted(step_times) or [float("nan")]
+        total = sum(step_times)
+        if self._group is not None and dist.is_initialized() and dist.get_world_size(self._group) > 1:
             t = torch.tensor([total], dtype=torch.float64, device="cuda" if self._events else "cpu")
-            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self._mesh.get_group())
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self._group)
             total = float(t.item())
         sps = self._samples / total if total > 0 else 0.0
         tps = self._tokens / total if total > 0 else 0.0
         p99 = times[min(len(times) - 1, int(round(0.99 * (len(times) - 1))))]
-        rep = ThroughputReport(steps=len(self._times), step_time_p50=statistics.median(times), step_time_p99=p99,
+        rep = ThroughputReport(steps=len(step_times), step_time_p50=statistics.median(times), step_time_p99=p99,
                                samples_per_second=sps, tokens_per_second=tps,
                                mfu=sps * self._fps / (self._peak * self._world) if self._peak else 0.0,
                                hfu=sps * self._hfps / (self._peak * self._world) if self._peak else 0.0)
         if reset:
-            self._times.clear()
+            self._marks = self._marks[-1:]
             self._samples = self._tokens = 0
         return rep
 

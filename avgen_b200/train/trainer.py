@@ -27,7 +27,7 @@ from avgen_b200.train.objective import Objective, ObjectiveOutput
 from avgen_b200.train.optimizer import FusedAdamW, MultiTensorAdamW
 
 __all__ = ["Curriculum", "CurriculumStage", "MetricSink", "ResolutionBucket", "Trainer", "TrainerCallback",
-           "TrainerConfig", "optimizer_update", "train_step"]
+           "TrainerConfig", "TrainerTelemetry", "optimizer_update", "train_step"]
 
 _LOG = logging.getLogger("avgen_b200.train")
 
@@ -145,27 +145,75 @@ def _autocast(model: torch.nn.Module, device: torch.device, dtype: torch.dtype) 
     return torch.autocast(device_type="cuda", dtype=dtype)
 
 
+@dataclass(frozen=True, slots=True)
+class _MicroStep:
+    """Where a micro-batch sits in its optimizer step."""
+
+    index: int
+    count: int
+
+    def __post_init__(self) -> None:
+        if not 0 <= self.index < self.count:
+            raise ValueError(f"microbatch_index={self.index} must lie in [0, {self.count})")
+
+    @property
+    def opens(self) -> bool:
+        return self.index == 0
+
+    @property
+    def closes(self) -> bool:
+        return self.index == self.count - 1
+
+    @property
+    def loss_scale(self) -> float:
+        return 1.0 / self.count
+
+
+def _device_clipping(opt: Any) -> bool:
+    """Optimizers that clip, skip and report the norm on the device themselves."""
+    return isinstance(opt, (FusedAdamW, MultiTensorAdamW))
+
+
+def _clear_gradients(opt: Any) -> None:
+    # the flat-buffer optimizer keeps its gradient views alive; the others drop them
+    opt.zero_grad(set_to_none=not isinstance(opt, FusedAdamW))
+
+
 def _set_gradient_sync(model: torch.nn.Module, enabled: bool) -> None:
     setter = getattr(model, "set_requires_gradient_sync", None)
     if callable(setter):
         setter(enabled)
 
 
-def _average_gradients(params: Sequence[torch.Tensor], group: Any) -> None:
+def _host_clip_and_step(state: TrainState, max_grad_norm: float | None, pp_mesh: DeviceMesh | None,
+                        data_group: Any, finite: torch.Tensor, dev: torch.device) -> tuple[torch.Tensor, torch.Tensor]:
+    """The path for optimizers without device-side clipping: average over the data
+    group, global norm (clip when asked), zero a non-finite step's gradients on the
+    device (no collective decides it), step."""
     import torch.distributed as dist
 
-    if group is None or not dist.is_initialized() or dist.get_world_size(group) == 1:
-        return
-    world = dist.get_world_size(group)
-    for p in params:
-        dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=group)
-        p.grad.div_(world)
+    from avgen_b200.parallel.comm import clip_grad_norm
 
-
-def _neutralise_nonfinite(grads: Sequence[torch.Tensor], finite: torch.Tensor) -> None:
+    params = [p for p in state.model.parameters() if p.grad is not None]
+    if not params:
+        state.optimizer.step()
+        return torch.zeros((), dtype=torch.float32, device=dev), finite
+    if data_group is not None and dist.is_initialized() and dist.get_world_size(data_group) > 1:
+        world = dist.get_world_size(data_group)
+        for p in params:
+            dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=data_group)
+            p.grad.div_(world)
+    if max_grad_norm is not None:
+        norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh)
+    else:
+        norm = torch.nn.utils.get_total_norm([p.grad for p in params], norm_type=2.0, error_if_nonfinite=False)
+    norm = norm.to(torch.float32)
+    finite = finite & torch.isfinite(norm)
     with torch.no_grad():
-        for g in grads:
-            torch.where(finite, g, torch.zeros((), dtype=g.dtype, device=g.device), out=g)
+        for p in params:
+            p.grad.mul_(finite.to(p.grad.dtype)).nan_to_num_(0.0, 0.0, 0.0)
+    state.optimizer.step()
+    return norm, finite
 
 
 def optimizer_update(state: TrainState, *, max_grad_norm: float | None = None, pp_mesh: DeviceMesh | None = None,
@@ -178,30 +226,21 @@ def optimizer_update(state: TrainState, *, max_grad_norm: float | None = None, p
     opt = state.optimizer
     dev = next((p.device for p in state.model.parameters()), torch.device("cpu"))
     finite = torch.ones((), dtype=torch.bool, device=dev) if finite is None else finite
-    grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
-    if isinstance(opt, (FusedAdamW, MultiTensorAdamW)):
+    if _device_clipping(opt):
         opt.step(max_grad_norm=max_grad_norm)
-        grad_norm = opt.last_grad_norm.to(torch.float32).to(dev)
+        norm = opt.last_grad_norm.to(device=dev, dtype=torch.float32)
         finite = finite & ~opt.last_nonfinite.to(dev)
     else:
-        from avgen_b200.parallel.comm import clip_grad_norm
-
-        params = [p for p in state.model.parameters() if p.grad is not None]
-        _average_gradients(params, data_group)
-        if max_grad_norm is not None and params:
-            grad_norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh).to(torch.float32)
-        elif params:
-            grad_norm = torch.nn.utils.get_total_norm([p.grad for p in params], norm_type=2.0,
-                                                      error_if_nonfinite=False).to(torch.float32)
-        finite = finite & torch.isfinite(grad_norm)
-        _neutralise_nonfinite([p.grad for p in params], finite)
-        opt.step()
-    if state.schedule is not None:
-        state.schedule.step()
-    if state.ema is not None:
-        state.ema.update(state.model)
+        norm, finite = _host_clip_and_step(state, max_grad_norm, pp_mesh, data_group, finite, dev)
+    for follower in (state.schedule, state.ema):
+        if follower is None:
+            continue
+        if follower is state.ema:
+            follower.update(state.model)
+        else:
+            follower.step()
     state.step += 1
-    return grad_norm, finite
+    return norm, finite
 
 
 def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, patchifier: Patchifier,
@@ -215,39 +254,56 @@ def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, pa
     ranks whose gradients are averaged before the optimizer step. The fused
     AdamW averages its flat buffer over its own ``dp_group`` instead.
     """
-    if not 0 <= microbatch_index < gradient_accumulation_steps:
-        raise ValueError(f"microbatch_index={microbatch_index} must lie in [0, {gradient_accumulation_steps})")
+    micro = _MicroStep(microbatch_index, gradient_accumulation_steps)
     dev = batch.device
-    first = microbatch_index == 0
-    last = microbatch_index == gradient_accumulation_steps - 1
-    opt = state.optimizer
-    if first:
-        opt.zero_grad(set_to_none=not isinstance(opt, FusedAdamW))
-    _set_gradient_sync(state.model, last)
+    if micro.opens:
+        _clear_gradients(state.optimizer)
+    # sharded / replicated gradients are reduced once, after the step's last micro-batch
+    _set_gradient_sync(state.model, micro.closes)
     with _autocast(state.model, dev, autocast_dtype):
         out: ObjectiveOutput = objective(state.model, batch, state.rng, patchifier=patchifier, cp_mesh=cp_mesh)
-    (out.loss / gradient_accumulation_steps).backward()
-    grad_norm = torch.zeros((), dtype=torch.float32, device=dev)
+    (out.loss * micro.loss_scale).backward()
     finite = torch.isfinite(out.loss.detach())
-    if last:
-        grad_norm, finite = optimizer_update(state, max_grad_norm=max_grad_norm, pp_mesh=pp_mesh,
-                                             data_group=data_group, finite=finite)
-    state.samples_seen += batch.spec.batch_size * data_world
-    state.tokens_seen += batch.spec.batch_size * batch.spec.sequence_length * data_world
-    skipped = ~finite if last else torch.zeros((), dtype=torch.bool, device=dev)
-    metrics = StepMetrics(loss=out.loss.detach().to(torch.float32), video_loss=out.video_loss.to(torch.float32),
-                          audio_loss=out.audio_loss.to(torch.float32), valid_video_tokens=out.valid_video_tokens,
-                          valid_audio_tokens=out.valid_audio_tokens, grad_norm=grad_norm.reshape(()),
+    norm = torch.zeros((), dtype=torch.float32, device=dev)
+    if micro.closes:
+        norm, finite = optimizer_update(state, max_grad_norm=max_grad_norm, pp_mesh=pp_mesh, data_group=data_group,
+                                        finite=finite)
+    samples = batch.spec.batch_size * data_world
+    state.samples_seen += samples
+    state.tokens_seen += samples * batch.spec.sequence_length
+    skipped = (~finite) if micro.closes else torch.zeros((), dtype=torch.bool, device=dev)
+    as_scalar = lambda t: t.detach().to(torch.float32).reshape(())  # noqa: E731
+    metrics = StepMetrics(loss=as_scalar(out.loss), video_loss=as_scalar(out.video_loss),
+                          audio_loss=as_scalar(out.audio_loss), valid_video_tokens=out.valid_video_tokens,
+                          valid_audio_tokens=out.valid_audio_tokens, grad_norm=norm.reshape(()),
                           nonfinite=(~finite).reshape(()), skipped=skipped.reshape(()))
     return state, metrics
 
 
+@dataclass(slots=True)
+class TrainerTelemetry:
+    """What the fit loop measures besides the loss; every part is optional.
+
+    ``accumulator`` averages step metrics over each log window (one collective and
+    one host sync per log line); ``throughput`` times steps on the device (events,
+    no per-step sync) and reports samples/s and MFU as the max over ranks;
+    ``profiler`` is a torch profiler context (``telemetry.profile_steps``) stepped
+    once per optimizer step; ``memory`` reports allocator peaks every
+    ``memory_every`` steps."""
+
+    accumulator: Any = None
+    throughput: Any = None
+    profiler: Any = None
+    memory: Any = None
+    memory_every: int = 0
+
+
 class Trainer:
-    """The fit loop: cadence callbacks, logging, curriculum stage announcements."""
+    """The fit loop: cadence callbacks, logging, telemetry, curriculum stage announcements."""
 
     def __init__(self, state: TrainState, objective: Objective, parallel: Any, config: TrainerConfig, *,
                  patchifier: Patchifier | None = None, callbacks: Sequence[TrainerCallback] = (),
-                 logger: MetricSink | None = None) -> None:
+                 logger: MetricSink | None = None, telemetry: TrainerTelemetry | None = None) -> None:
         self.state = state
         self.objective = objective
         self.parallel = parallel
@@ -255,13 +311,12 @@ class Trainer:
         self.patchifier = patchifier or _model_patchifier(state.model)
         self.callbacks = tuple(callbacks)
         self.logger = logger
+        self.telemetry = telemetry or TrainerTelemetry()
         self._stage_name: str | None = None
 
     @property
     def device(self) -> torch.device:
-        for p in self.state.model.parameters():
-            return p.device
-        return torch.device("cpu")
+        return next((p.device for p in self.state.model.parameters()), torch.device("cpu"))
 
     def train_step(self, batch: MediaBatch, *, microbatch_index: int = 0, accumulation: int | None = None,
                    ) -> StepMetrics:
@@ -274,36 +329,72 @@ class Trainer:
             data_group=getattr(self.parallel, "data_group", None))
         return metrics
 
+    def run_step(self, micro_batches: Sequence[MediaBatch]) -> StepMetrics:
+        """One optimizer step over its micro-batches; returns the last micro-step's metrics."""
+        metrics = None
+        for index, batch in enumerate(micro_batches):
+            metrics = self.train_step(batch, microbatch_index=index, accumulation=len(micro_batches))
+        assert metrics is not None
+        return metrics
+
     def fit(self, loader: Iterable[MediaBatch], total_steps: int | None = None) -> None:
         if total_steps is not None and (isinstance(total_steps, bool) or total_steps < 1):
             raise ValueError(f"total_steps must be positive; got {total_steps!r}")
-        acc = self.config.gradient_accumulation_steps
-        self._announce_stage(loader)
-        for index, batch in enumerate(_iterate(loader, self.device)):
-            metrics = self.train_step(batch, microbatch_index=index % acc, accumulation=acc)
-            if index % acc != acc - 1:
-                continue
-            self._on_step_end(metrics)
+        tel = self.telemetry
+        profiler = tel.profiler if tel.profiler is not None else nullcontext()
+        with profiler:
+            if tel.throughput is not None:
+                tel.throughput.start()
             self._announce_stage(loader)
-            if total_steps is not None and self.state.step >= total_steps:
-                return
+            for window in _step_windows(loader, self.config.gradient_accumulation_steps, self.device):
+                metrics = self.run_step(window)
+                self._measure(metrics, window)
+                self._on_step_end(metrics)
+                self._announce_stage(loader)
+                if total_steps is not None and self.state.step >= total_steps:
+                    return
+
+    def _measure(self, metrics: StepMetrics, window: Sequence[MediaBatch]) -> None:
+        tel = self.telemetry
+        if tel.accumulator is not None:
+            tel.accumulator.update(metrics)
+        if tel.throughput is not None:
+            samples = sum(b.spec.batch_size for b in window) * self.config.data_world
+            tel.throughput.step(samples=samples, tokens=samples * window[0].spec.sequence_length)
+        step = getattr(tel.profiler, "step", None)
+        if callable(step):
+            step()
+
+    def _log_line(self, metrics: StepMetrics) -> dict[str, float]:
+        tel = self.telemetry
+        line = tel.accumulator.flush() if tel.accumulator is not None else metrics.to_mapping()
+        line.update({f"progress/{k}": float(v) for k, v in self.state.progress().items()})
+        if tel.throughput is not None:
+            line.update(tel.throughput.report().to_mapping())
+        step = self.state.step
+        if tel.memory is not None and tel.memory_every and step % tel.memory_every == 0:
+            report = tel.memory.report()
+            if report is not None:
+                line.update(report.to_mapping())
+        if self.state.schedule is not None:
+            line["lr"] = self.state.schedule.get_last_lr()[0]
+        return line
 
     def _on_step_end(self, metrics: StepMetrics) -> None:
         step = self.state.step
         _dispatch(self.callbacks, "on_step_end", self, self.state, metrics)
-        if step % self.config.log_every == 0:
-            snap = metrics.to_mapping()
-            snap.update({f"progress/{k}": float(v) for k, v in self.state.progress().items()})
-            if self.state.schedule is not None:
-                snap["lr"] = self.state.schedule.get_last_lr()[0]
+        cadence = {"log": self.config.log_every, "eval": self.config.eval_every,
+                   "checkpoint": self.config.checkpoint_every}
+        due = {name for name, every in cadence.items() if every and step % every == 0}
+        if "log" in due:
+            line = self._log_line(metrics)
             if self.logger is not None:
-                self.logger.log_metrics(snap, step)
+                self.logger.log_metrics(line, step)
             else:
-                _LOG.info("step %d %s", step, snap)
-        if self.config.eval_every and step % self.config.eval_every == 0:
-            _dispatch(self.callbacks, "on_eval", self, self.state)
-        if self.config.checkpoint_every and step % self.config.checkpoint_every == 0:
-            _dispatch(self.callbacks, "on_checkpoint", self, self.state)
+                _LOG.info("step %d %s", step, line)
+        for hook in ("eval", "checkpoint"):
+            if hook in due:
+                _dispatch(self.callbacks, f"on_{hook}", self, self.state)
 
     def _announce_stage(self, loader: object) -> None:
         stage = self.config.curriculum.stage_for(self.state.step)
@@ -316,9 +407,15 @@ class Trainer:
         _LOG.info("curriculum stage %r active at step %d", stage.name, self.state.step)
 
 
-def _iterate(loader: Iterable[MediaBatch], device: torch.device) -> Iterator[MediaBatch]:
+def _step_windows(loader: Iterable[MediaBatch], size: int, device: torch.device) -> Iterator[list[MediaBatch]]:
+    """The loader's batches on ``device``, grouped into optimizer steps of ``size``
+    micro-batches (a trailing partial group is dropped: it cannot close a step)."""
+    window: list[MediaBatch] = []
     for batch in loader:
-        yield batch if batch.device == device else batch.to(device)
+        window.append(batch if batch.device == device else batch.to(device))
+        if len(window) == size:
+            yield window
+            window = []
 
 
 def _dispatch(callbacks: Sequence[Any], hook: str, *args: object) -> None:

@@ -39,6 +39,11 @@ def test_train_resume_export_generate(tmp_path: Path, capsys: pytest.CaptureFixt
     assert [c.name for c in ckpts] == ["step_0000000001", "step_0000000002"]
     lines = (out / "metrics.jsonl").read_text().splitlines()
     assert len(lines) == 2 and json.loads(lines[-1])["step"] == 2
+    # the training loop drives the metric accumulator and the throughput meter
+    last = json.loads(lines[-1])
+    flat = {**last, **last.get("metrics", {})}
+    assert "loss" in flat and "progress/samples_seen" in flat
+    assert flat["throughput/steps"] == 1 and flat["throughput/samples_per_second"] > 0 and flat["throughput/mfu"] > 0
     # resume continues from step 2 to step 3
     assert main(["train", *TINY, "train.steps=3", "checkpoint.save_every=10", f"output_dir={out}",
                  "--resume", "latest"]) == 0

@@ -23,6 +23,13 @@ import torch
 from torch import nn
 from torch.utils.hooks import RemovableHandle
 
+
+def _is_block_list(blocks: object) -> bool:
+    from avgen_b200.parallel.pipeline import is_block_list
+
+    return is_block_list(blocks)
+
+
 __all__ = ["AdapterHandles", "ControlAdapter", "ControlAdapterConfig", "IPAdapter", "IPAdapterConfig"]
 
 
@@ -60,7 +67,7 @@ class AdapterHandles:
 
 def _blocks(model: nn.Module, attribute: str) -> nn.ModuleList:
     blocks = getattr(model, attribute, None)
-    if not isinstance(blocks, nn.ModuleList) or not len(blocks):
+    if not _is_block_list(blocks) or not len(blocks):
         raise AttributeError(f"{type(model).__name__} has no non-empty nn.ModuleList {attribute!r}")
     return blocks
 

@@ -237,18 +237,44 @@ class VideoDiT(nn.Module):
         return torch.zeros((a.batch_size, a.length, a.layout.patch_dim), dtype=like.dtype, device=like.device)
 
     def forward(self, inputs: ModelInput) -> ModelOutput:
+        hidden, context, modulation = self.stage_embed(inputs)
+        hidden = self.stage_blocks(hidden, context, modulation, self.stage_inputs(inputs))
+        return self.stage_head(hidden, inputs)
+
+    # ------------------------------------------------------------------ pipeline stages
+    # The forward in three parts so a pipeline stage runs only what it owns: the first
+    # stage embeds (patches, text, modulation rows), every stage runs its blocks, the
+    # last stage projects to the output. ``stage_inputs`` holds what every stage can
+    # rebuild from the model input without parameters (RoPE coordinates, key masks,
+    # each token's modulation row).
+    def stage_inputs(self, inputs: ModelInput) -> dict[str, Any]:
+        video, text = inputs.video, inputs.text
+        context_mask = None
+        if not text.is_empty and self.config.cross_attention:
+            context_mask = key_padding_mask(text.mask, assume_dense=self.config.assume_dense_mask)
+        return {"rope": self._rope_inputs(video.coords), "context_mask": context_mask,
+                "key_mask": key_padding_mask(self._global_mask(video.mask), assume_dense=self.config.assume_dense_mask),
+                "modulation_index": _modulation_index(video)}
+
+    def stage_embed(self, inputs: ModelInput) -> tuple[torch.Tensor, torch.Tensor | None, torch.Tensor]:
+        """(hidden, text context or None, modulation rows): the tensors later stages receive."""
         video = inputs.video
-        context, context_mask = self.encode_text(inputs.text)
+        context, _ = self.encode_text(inputs.text)
         tokens = video.masked()
         if tokens.device.type == "cuda":
             tokens = tokens.to(torch.bfloat16)
         hidden = linear(match_dtype(tokens, self.patch_embed), self.patch_embed)
-        modulation, mod_index = self._stream_conditioning(video, embed=self.time_embed, modulation=self.modulation)
-        rope = self._rope_inputs(video.coords)
-        key_mask = key_padding_mask(self._global_mask(video.mask), assume_dense=self.config.assume_dense_mask)
-        hidden = self._denoise(hidden, modulation=modulation, rope=rope, key_mask=key_mask, context=context,
-                               context_mask=context_mask, modulation_index=mod_index)
-        predicted = self._video_head(hidden, video)
+        modulation, _ = self._stream_conditioning(video, embed=self.time_embed, modulation=self.modulation)
+        return hidden, context, modulation
+
+    def stage_blocks(self, hidden: torch.Tensor, context: torch.Tensor | None, modulation: torch.Tensor,
+                     aux: dict[str, Any]) -> torch.Tensor:
+        return self._denoise(hidden, modulation=modulation, rope=aux["rope"], key_mask=aux["key_mask"],
+                             context=context, context_mask=aux["context_mask"],
+                             modulation_index=aux["modulation_index"])
+
+    def stage_head(self, hidden: torch.Tensor, inputs: ModelInput) -> ModelOutput:
+        predicted = self._video_head(hidden, inputs.video)
         return ModelOutput(video=predicted, audio=self._null_audio(inputs, predicted))
 
     def tensor_parallel_plan(self, *, sequence_parallel: bool) -> tuple[dict[str, Any], dict[str, Any]]:
@@ -445,6 +471,18 @@ class AVDiT(VideoDiT):
         if self.config.fusion == "joint":
             return self._forward_joint(inputs)
         return self._forward_two_tower(inputs)
+
+
+def _modulation_index(stream: TokenStream) -> torch.Tensor | None:
+    """Each token's row in the modulation rows ``_stream_conditioning`` builds (None: one row per sample)."""
+    if stream.has_level_groups:
+        b, g = stream.level_values.shape
+        base = torch.arange(b, device=stream.level_index.device, dtype=torch.int32)[:, None] * g
+        return stream.level_index + base
+    if stream.per_token_noise:
+        b, length = stream.noise_level.shape
+        return torch.arange(b * length, device=stream.noise_level.device, dtype=torch.int32).view(b, length)
+    return None
 
 
 def _row_index(rows: torch.Tensor, index: torch.Tensor | None, batch: int, length: int) -> torch.Tensor:

@@ -23,6 +23,13 @@ from typing import Any, Literal
 import torch
 from torch import nn
 
+
+def _is_block_list(blocks: object) -> bool:
+    from avgen_b200.parallel.pipeline import is_block_list
+
+    return is_block_list(blocks)
+
+
 __all__ = ["ACMode", "ActivationCheckpointConfig", "CheckpointedBlock", "apply_activation_checkpointing",
            "DEFAULT_SAVE_OPS"]
 
@@ -141,7 +148,7 @@ def apply_activation_checkpointing(model: nn.Module, config: ActivationCheckpoin
     blocks = getattr(model, block_attribute, None)
     if blocks is None:
         raise AttributeError(f"model {type(model).__name__} has no {block_attribute!r}; pass block_attribute=")
-    if not isinstance(blocks, nn.ModuleList):
+    if not _is_block_list(blocks):
         raise TypeError(f"{block_attribute!r} must be an nn.ModuleList; got {type(blocks).__name__}")
     for i, block in enumerate(blocks):
         if isinstance(block, CheckpointedBlock):

@@ -24,6 +24,7 @@ from torch import nn
 from avgen_b200.parallel.activation import ActivationCheckpointConfig, apply_activation_checkpointing
 from avgen_b200.parallel.dims import ParallelDims, submesh
 from avgen_b200.parallel.fsdp import FSDPConfig, apply_fsdp
+from avgen_b200.parallel.pipeline import PipelineConfig
 from avgen_b200.parallel.precision import PrecisionConfig, convert_to_float8
 from avgen_b200.parallel.tensor import apply_tensor_parallel
 
@@ -41,6 +42,7 @@ class ParallelConfig:
     sequence_parallel: bool = False
     native_data_parallel: bool = True
     shard_parameters: bool = True
+    pipeline: PipelineConfig = field(default_factory=PipelineConfig)
 
 
 @dataclass(frozen=True, slots=True)
@@ -49,6 +51,7 @@ class ParallelModel:
     dims: ParallelDims
     mesh: Any
     applied: tuple[str, ...]
+    pipeline: Any = None  # PipelineRunner of this rank's stage when pp > 1
 
     def submesh(self, name: str) -> Any:
         return submesh(self.mesh, name)
@@ -92,6 +95,18 @@ def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, confi
     applied: list[str] = []
     if mesh is None and dims.world_size > 1:
         mesh = dims.build_mesh()
+    runner = None
+    if dims.pp_enabled and mesh is not None:
+        from avgen_b200.parallel.pipeline import PipelineRunner, balanced_split_points, split_model
+
+        pp = submesh(mesh, "pp")
+        stage, stages = pp.get_local_rank(), pp.size()
+        depth = len(getattr(model, cfg.block_attribute))
+        points = balanced_split_points(depth, stages, embedding_weight=cfg.pipeline.embedding_weight,
+                                       head_weight=cfg.pipeline.head_weight)
+        model = split_model(model, stage_index=stage, num_stages=stages, split_points=points,
+                            block_attribute=cfg.block_attribute)
+        applied.append(f"pipeline(pp={stages}, stage={stage}, {cfg.pipeline.schedule})")
     n8 = convert_to_float8(model, cfg.precision)
     if n8:
         applied.append(f"float8({n8} linears)")
@@ -139,6 +154,9 @@ def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, confi
 
         apply_context_parallel(model, submesh(mesh, "cp"))
         applied.append(f"context_parallel(cp={dims.context})")
+    if dims.pp_enabled and mesh is not None:
+        runner = PipelineRunner(model, submesh(mesh, "pp").get_group(),
+                                schedule="gpipe" if cfg.pipeline.schedule == "gpipe" else "1f1b")
     if not applied:
         applied.append("single-device")
-    return ParallelModel(model=model, dims=dims, mesh=mesh, applied=tuple(applied))
+    return ParallelModel(model=model, dims=dims, mesh=mesh, applied=tuple(applied), pipeline=runner)

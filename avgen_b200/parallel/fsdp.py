@@ -19,6 +19,13 @@ from torch import nn
 
 from avgen_b200.parallel.precision import PrecisionConfig
 
+
+def _is_block_list(blocks: object) -> bool:
+    from avgen_b200.parallel.pipeline import is_block_list
+
+    return is_block_list(blocks)
+
+
 __all__ = ["FSDPConfig", "apply_fsdp", "set_prefetch_depth", "summarize_sharding"]
 
 
@@ -41,7 +48,7 @@ def apply_fsdp(model: nn.Module, mesh: Any, *, precision: PrecisionConfig | None
     cfg = config or FSDPConfig()
     prec = precision or PrecisionConfig()
     blocks = getattr(model, cfg.block_attribute, None)
-    if not isinstance(blocks, nn.ModuleList):
+    if not _is_block_list(blocks):
         raise AttributeError(f"{type(model).__name__} has no nn.ModuleList {cfg.block_attribute!r}; FSDP shards "
                              "per block so communication overlaps compute")
     kwargs: dict[str, Any] = {"mesh": mesh, "mp_policy": prec.fsdp_policy(),

@@ -17,8 +17,8 @@ from typing import Any, Literal
 import torch
 from torch import nn
 
-__all__ = ["PipelineConfig", "ScheduleName", "balanced_split_points", "build_pipeline_schedule", "split_model",
-           "stage_for_rank"]
+__all__ = ["PipelineConfig", "PipelineRunner", "ScheduleName", "StageBlocks", "balanced_split_points",
+           "build_pipeline_schedule", "is_block_list", "split_model", "stage_for_rank"]
 
 ScheduleName = Literal["gpipe", "1f1b", "interleaved_1f1b", "zero_bubble"]
 _NAMES = ("gpipe", "1f1b", "interleaved_1f1b", "zero_bubble")
@@ -103,6 +103,25 @@ def balanced_split_points(num_blocks: int, num_stages: int, *, embedding_weight:
     return points
 
 
+class StageBlocks(nn.ModuleDict):
+    """One pipeline stage's blocks, registered under their indices in the full model
+    (``blocks.12.attention...``), so parameter names, state dicts and DCP checkpoints
+    of a stage match the unsplit model. Iterating yields the blocks in order."""
+
+    def __iter__(self):  # noqa: ANN204 - the blocks, not their names
+        return iter(self.values())
+
+    def __getitem__(self, key):  # noqa: ANN001, ANN204 - position within the stage, or the global name
+        if isinstance(key, int):
+            return list(self.values())[key]
+        return super().__getitem__(key)
+
+
+def is_block_list(blocks: object) -> bool:
+    """A model's block container: an ``nn.ModuleList`` or a pipeline stage's :class:`StageBlocks`."""
+    return isinstance(blocks, (nn.ModuleList, StageBlocks))
+
+
 def split_model(model: nn.Module, *, stage_index: int, num_stages: int, split_points: Sequence[int],
                 block_attribute: str = "blocks") -> nn.Module:
     if not 0 <= stage_index < num_stages:
@@ -113,7 +132,8 @@ def split_model(model: nn.Module, *, stage_index: int, num_stages: int, split_po
     if len(split_points) != num_stages - 1:
         raise ValueError(f"{num_stages} stages need {num_stages - 1} split points; got {len(split_points)}")
     bounds = [0, *split_points, len(blocks)]
-    setattr(model, block_attribute, nn.ModuleList(list(blocks)[bounds[stage_index]:bounds[stage_index + 1]]))
+    lo, hi = bounds[stage_index], bounds[stage_index + 1]
+    setattr(model, block_attribute, StageBlocks({str(i): blocks[i] for i in range(lo, hi)}))
     if stage_index > 0:
         for name in _INPUT_MODULES:
             if hasattr(model, name):
@@ -144,3 +164,195 @@ def build_pipeline_schedule(stages: Sequence[Any], config: PipelineConfig,
 def stage_for_rank(mesh: Any) -> tuple[int, int]:
     """(stage index, number of stages) of this rank on the pipeline mesh."""
     return mesh.get_local_rank(), mesh.size()
+
+
+# --------------------------------------------------------------------------- execution
+class _Carry:
+    """The tensors one stage hands the next for a micro-batch: hidden states, the
+    text context (or None) and the modulation rows. On the receiving side they are
+    leaves that collect their gradients, sent back upstream in backward."""
+
+    __slots__ = ("context", "hidden", "modulation")
+
+    def __init__(self, hidden: torch.Tensor, context: torch.Tensor | None, modulation: torch.Tensor) -> None:
+        self.hidden, self.context, self.modulation = hidden, context, modulation
+
+    def tensors(self) -> list[torch.Tensor]:
+        return [t for t in (self.hidden, self.context, self.modulation) if t is not None]
+
+
+class PipelineRunner:
+    """Runs one pipeline stage of a model that exposes ``stage_embed`` / ``stage_inputs``
+    / ``stage_blocks`` / ``stage_head`` (:class:`~avgen_b200.models.VideoDiT`) through a
+    1F1B or GPipe schedule, exchanging carries with the neighbouring stages by NCCL
+    (or gloo) point-to-point operations.
+
+    In the steady 1F1B state each stage batches "send my forward output, receive the
+    gradient of an earlier micro-batch" (and the mirror operation downstream) into
+    one grouped call, so the two neighbours' operations match and progress together,
+    and the compute stream only waits on a transfer when it needs its data: the send
+    of one micro-batch's activations overlaps the backward of another. The last stage
+    evaluates ``loss_fn(micro_index, output)``; every stage accumulates its own
+    parameters' gradients (the reference leaves its schedules unused:
+    avgen/parallel/pipeline.py:254-289)."""
+
+    def __init__(self, model: nn.Module, group: Any, *, schedule: str = "1f1b") -> None:
+        import torch.distributed as dist
+
+        if schedule not in ("1f1b", "gpipe"):
+            raise ValueError(f"PipelineRunner runs the 1f1b and gpipe schedules; got {schedule!r}")
+        for name in ("stage_embed", "stage_inputs", "stage_blocks", "stage_head"):
+            if not callable(getattr(model, name, None)):
+                raise TypeError(f"{type(model).__name__} has no {name}(): it cannot run as pipeline stages")
+        self.model = model
+        self.group = group
+        self.schedule = schedule
+        self.stage = dist.get_rank(group)
+        self.stages = dist.get_world_size(group)
+        ranks = dist.get_process_group_ranks(group)
+        self._prev = ranks[self.stage - 1] if self.stage > 0 else None
+        self._next = ranks[self.stage + 1] if self.stage < self.stages - 1 else None
+
+    @property
+    def first(self) -> bool:
+        return self.stage == 0
+
+    @property
+    def last(self) -> bool:
+        return self.stage == self.stages - 1
+
+    # ---------------------------------------------------------------- communication
+    def _exchange(self, sends: list[tuple[torch.Tensor, int]], recvs: list[tuple[torch.Tensor, int]]) -> None:
+        """One grouped batch of point-to-point operations; the caller's stream (or the
+        host, with gloo) waits for it before the received tensors are used."""
+        import torch.distributed as dist
+
+        ops = [dist.P2POp(dist.isend, t.contiguous(), peer, self.group) for t, peer in sends]
+        ops += [dist.P2POp(dist.irecv, t, peer, self.group) for t, peer in recvs]
+        if not ops:
+            return
+        for work in dist.batch_isend_irecv(ops):
+            work.wait()
+
+    def _carry_like(self, spec: list[tuple[tuple[int, ...], torch.dtype]], device: torch.device) -> list[torch.Tensor]:
+        return [torch.empty(shape, dtype=dtype, device=device) for shape, dtype in spec]
+
+    # ---------------------------------------------------------------- compute
+    def _forward(self, k: int, inputs: Any, received: list[torch.Tensor] | None,
+                 loss_fn: Callable[[int, Any], torch.Tensor]) -> tuple[Any, Any]:
+        """Returns (what backward starts from, this micro-batch's received leaves)."""
+        if self.first:
+            carry = _Carry(*self.model.stage_embed(inputs))
+            leaves = None
+        else:
+            assert received is not None
+            leaves = [t.requires_grad_() for t in received]
+            it = iter(leaves)
+            hidden = next(it)
+            context = next(it) if self._has_context(inputs) else None
+            carry = _Carry(hidden, context, next(it))
+        hidden = self.model.stage_blocks(carry.hidden, carry.context, carry.modulation, self.model.stage_inputs(inputs))
+        if self.last:
+            return loss_fn(k, self.model.stage_head(hidden, inputs)), leaves
+        return _Carry(hidden, carry.context, carry.modulation), leaves
+
+    def _has_context(self, inputs: Any) -> bool:
+        return (not inputs.text.is_empty) and bool(getattr(self.model.config, "cross_attention", True))
+
+    def _spec(self, inputs: Any, like: Any) -> list[tuple[tuple[int, ...], torch.dtype]]:
+        """Shapes and dtypes of a carry for ``inputs`` (every stage derives it alike)."""
+        cfg = self.model.config
+        video = inputs.video
+        b, length = video.batch_size, video.length
+        dtype = torch.bfloat16 if video.tokens.device.type == "cuda" else like.dtype
+        spec = [((b, length, cfg.width), dtype)]
+        if self._has_context(inputs):
+            spec.append(((b, inputs.text.features.shape[1], cfg.width), dtype))
+        if video.has_level_groups:
+            rows = video.level_values.numel()
+        elif video.per_token_noise:
+            rows = b * length
+        else:
+            rows = b
+        spec.append(((rows, 6, cfg.width), torch.float32))
+        return spec
+
+    def _backward(self, start: Any, grads: list[torch.Tensor] | None, leaves: list[torch.Tensor] | None
+                  ) -> list[torch.Tensor] | None:
+        if self.last:
+            start.backward()
+        else:
+            outs = start.tensors()
+            assert grads is not None and len(grads) == len(outs)
+            torch.autograd.backward(outs, grads)
+        if leaves is None:
+            return None
+        return [t.grad if t.grad is not None else torch.zeros_like(t) for t in leaves]
+
+    # ---------------------------------------------------------------- schedule
+    def run(self, micro_inputs: Sequence[Any], loss_fn: Callable[[int, Any], torch.Tensor]) -> list[torch.Tensor]:
+        """Forward and backward of every micro-batch on this stage. Returns the losses
+        (last stage only; empty elsewhere). Gradients accumulate in the parameters."""
+        m = len(micro_inputs)
+        if m == 0:
+            return []
+        like = next(self.model.parameters())
+        device = like.device
+        warmup = m if self.schedule == "gpipe" else min(self.stages - self.stage - 1, m)
+        starts: dict[int, Any] = {}
+        leaves: dict[int, Any] = {}
+        losses: list[torch.Tensor] = []
+
+        def recv_forward(k: int) -> list[torch.Tensor] | None:
+            if self.first:
+                return None
+            bufs = self._carry_like(self._spec(micro_inputs[k], like), device)
+            self._exchange([], [(t, self._prev) for t in bufs])
+            return bufs
+
+        def forward(k: int, received: list[torch.Tensor] | None) -> None:
+            start, leaves[k] = self._forward(k, micro_inputs[k], received, loss_fn)
+            starts[k] = start
+            if self.last:
+                losses.append(start.detach())
+
+        def outgoing(k: int) -> list[tuple[torch.Tensor, int]]:
+            if self.last:
+                return []
+            return [(t.detach(), self._next) for t in starts[k].tensors()]
+
+        def grad_bufs(k: int) -> list[torch.Tensor]:
+            return [] if self.last else self._carry_like(self._spec(micro_inputs[k], like), device)
+
+        def backward(k: int, grads: list[torch.Tensor] | None) -> list[torch.Tensor] | None:
+            out = self._backward(starts.pop(k), grads, leaves.pop(k))
+            return out
+
+        # warm-up forwards (all of them for GPipe)
+        for k in range(warmup):
+            forward(k, recv_forward(k))
+            self._exchange(outgoing(k), [])
+        # steady state: one forward, one backward
+        received = recv_forward(warmup) if warmup < m else None
+        for i in range(m - warmup):
+            k = warmup + i
+            forward(k, received)
+            grads = grad_bufs(i)
+            self._exchange(outgoing(k), [(g, self._next) for g in grads])
+            upstream = backward(i, grads or None)
+            nxt = k + 1
+            if nxt < m:
+                bufs = None if self.first else self._carry_like(self._spec(micro_inputs[nxt], like), device)
+                sends = [] if upstream is None else [(g, self._prev) for g in upstream]
+                self._exchange(sends, [] if bufs is None else [(t, self._prev) for t in bufs])
+                received = bufs
+            elif upstream is not None:
+                self._exchange([(g, self._prev) for g in upstream], [])
+        # cool-down backwards
+        for i in range(m - warmup, m):
+            grads = grad_bufs(i)
+            self._exchange([], [(g, self._next) for g in grads])
+            upstream = backward(i, grads or None)
+            if upstream is not None:
+                self._exchange([(g, self._prev) for g in upstream], [])
+        return losses

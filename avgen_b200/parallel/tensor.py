@@ -17,6 +17,13 @@ from typing import Protocol, runtime_checkable
 
 from torch import nn
 
+
+def _is_block_list(blocks: object) -> bool:
+    from avgen_b200.parallel.pipeline import is_block_list
+
+    return is_block_list(blocks)
+
+
 __all__ = ["TensorParallelPlan", "TensorParallelizable", "apply_tensor_parallel", "standard_block_plan",
            "standard_root_plan"]
 
@@ -73,7 +80,7 @@ def apply_tensor_parallel(model: nn.Module, mesh, *, sequence_parallel: bool = F
         root_plan = root_plan if root_plan is not None else derived_root
         block_plan = block_plan if block_plan is not None else derived_block
     blocks = getattr(model, block_attribute, None)
-    if not isinstance(blocks, nn.ModuleList):
+    if not _is_block_list(blocks):
         raise AttributeError(f"{type(model).__name__} has no nn.ModuleList {block_attribute!r}")
     if root_plan:
         parallelize_module(model, mesh, root_plan)

@@ -19,7 +19,7 @@ from __future__ import annotations
 
 from collections.abc import Callable
 from dataclasses import dataclass, field, replace
-from typing import Protocol, runtime_checkable
+from typing import Any, Protocol, runtime_checkable
 
 import torch
 from torch import nn
@@ -36,7 +36,8 @@ from avgen_b200.parallel.context import shard_bounds, shard_stream
 from avgen_b200.train.conditioning import ConditioningPlan, ConditioningSampler
 from avgen_b200.train.timestep import TimestepSampler
 
-__all__ = ["FlowMatchingConfig", "FlowMatchingObjective", "Objective", "ObjectiveOutput", "masked_flow_loss"]
+__all__ = ["FlowMatchingConfig", "FlowMatchingObjective", "FlowTargets", "Objective", "ObjectiveOutput",
+           "masked_flow_loss"]
 
 _T_EPS = 1e-5
 _WEIGHTINGS = ("uniform", "sigma_sqrt", "cosmap")
@@ -136,6 +137,18 @@ def masked_flow_loss(prediction: torch.Tensor, target: torch.Tensor, stream: Tok
     return (masked * weight[:, None]).sum(), masked.sum().detach(), sup.sum().detach(), valid
 
 
+@dataclass(frozen=True, slots=True)
+class FlowTargets:
+    """What the loss needs besides the model output: velocity targets and noise levels."""
+
+    video: torch.Tensor
+    audio: torch.Tensor
+    video_t: torch.Tensor
+    audio_t: torch.Tensor
+    has_audio: bool
+    cp_mesh: Any = None
+
+
 class FlowMatchingObjective:
     __slots__ = ("audio_patchifier", "conditioning_sampler", "config", "timestep_sampler", "weight_fn")
 
@@ -150,6 +163,15 @@ class FlowMatchingObjective:
 
     def __call__(self, model: nn.Module, batch: MediaBatch, rng: RNGStreams, *, patchifier: Patchifier,
                  cp_mesh: DeviceMesh | None = None) -> ObjectiveOutput:
+        inputs, targets = self.prepare(batch, rng, patchifier=patchifier, cp_mesh=cp_mesh)
+        output: ModelOutput = model(inputs)
+        return self.finish(output, inputs, targets)
+
+    def prepare(self, batch: MediaBatch, rng: RNGStreams, *, patchifier: Patchifier,
+                cp_mesh: DeviceMesh | None = None) -> tuple[ModelInput, FlowTargets]:
+        """The model input (noisy streams, conditioning, text after dropout) and the
+        regression targets of one batch. Deterministic in ``rng``: pipeline stages
+        that share a data rank draw the same noise and timesteps."""
         plan = self.conditioning_sampler.sample(batch, rng=rng)
         if self.config.validate:
             plan.validate(batch)
@@ -181,11 +203,16 @@ class FlowMatchingObjective:
                             condition_mode=plan.condition_mode)
         if self.config.validate:
             inputs.validate()
-        output: ModelOutput = model(inputs)
+        return inputs, FlowTargets(video=vtarget, audio=atarget, video_t=vt, audio_t=at, has_audio=has_audio,
+                                   cp_mesh=cp_mesh)
+
+    def finish(self, output: ModelOutput, inputs: ModelInput, targets: FlowTargets) -> ObjectiveOutput:
+        """The loss of ``output`` against ``targets`` (summed across context-parallel shards)."""
         if self.config.validate:
             output.validate(inputs)
-        return self._reduce(output=output, vstream=vstream, vtarget=vtarget, vt=vt, astream=astream,
-                            atarget=atarget, at=at, has_audio=has_audio, cp_mesh=cp_mesh)
+        return self._reduce(output=output, vstream=inputs.video, vtarget=targets.video, vt=targets.video_t,
+                            astream=inputs.audio, atarget=targets.audio, at=targets.audio_t,
+                            has_audio=targets.has_audio, cp_mesh=targets.cp_mesh)
 
     def _prepare(self, patchifier: Patchifier, *, grid: torch.Tensor, positions: torch.Tensor, mask: torch.Tensor,
                  conditioned: torch.Tensor, timesteps: torch.Tensor, rng: RNGStreams, cp_mesh: DeviceMesh | None,

@@ -69,6 +69,8 @@ class FusedAdamW(Optimizer):
         super().__init__(params, defaults)
         self.dp_group = dp_group
         self.max_grad_norm: float | None = None
+        # groups holding other parts of the model (pipeline stages): the squared norm is summed over them
+        self.norm_groups: tuple[Any, ...] = ()
         self._flat: list[dict[str, torch.Tensor]] = []
         self._step = 0
         self.last_grad_norm: torch.Tensor | None = None
@@ -166,6 +168,8 @@ class FusedAdamW(Optimizer):
                 K.sq_norm_(flat["grad"], acc)
             else:
                 acc += flat["grad"].pow(2).sum()
+        for group in self.norm_groups:
+            dist.all_reduce(acc, group=group)
         return acc.sqrt()[0]
 
     def sync_gradients(self) -> None:
@@ -429,6 +433,7 @@ class MultiTensorAdamW(Optimizer):
         self.max_grad_norm: float | None = None
         self.last_grad_norm: torch.Tensor | None = None
         self.last_nonfinite: torch.Tensor | None = None
+        self.norm_groups: tuple[Any, ...] = ()  # other pipeline stages: the squared norm is summed over them
         self._step = 0
         self._tables: dict[tuple, tuple[torch.Tensor, torch.Tensor]] = {}
         for group in self.param_groups:
@@ -472,7 +477,10 @@ class MultiTensorAdamW(Optimizer):
 
         params = [p for g in self.param_groups for p in g["params"] if p.grad is not None]
         if not params:
-            return torch.zeros((), dtype=torch.float32)
+            total = torch.zeros(1, dtype=torch.float32)
+            for group in self.norm_groups:
+                dist.all_reduce(total, group=group)
+            return total.sqrt()[0]
         dev = _local(params[0]).device
         by_groups: dict[tuple, list[torch.Tensor]] = {}
         for p in params:
@@ -494,6 +502,8 @@ class MultiTensorAdamW(Optimizer):
             for g in groups:
                 dist.all_reduce(acc, group=g)
             total += acc
+        for group in self.norm_groups:
+            dist.all_reduce(total, group=group)
         return total.sqrt()[0]
 
     @torch.no_grad()

@@ -27,7 +27,7 @@ from avgen_b200.train.objective import Objective, ObjectiveOutput
 from avgen_b200.train.optimizer import FusedAdamW, MultiTensorAdamW
 
 __all__ = ["Curriculum", "CurriculumStage", "MetricSink", "ResolutionBucket", "Trainer", "TrainerCallback",
-           "TrainerConfig", "TrainerTelemetry", "optimizer_update", "train_step"]
+           "TrainerConfig", "TrainerTelemetry", "optimizer_update", "pipeline_train_step", "train_step"]
 
 _LOG = logging.getLogger("avgen_b200.train")
 
@@ -280,6 +280,53 @@ def train_step(state: TrainState, batch: MediaBatch, objective: Objective, *, pa
     return state, metrics
 
 
+def pipeline_train_step(state: TrainState, micro_batches: Sequence[MediaBatch], objective: Any, runner: Any, *,
+                        patchifier: Patchifier, max_grad_norm: float | None = None,
+                        cp_mesh: DeviceMesh | None = None, pp_mesh: DeviceMesh | None = None,
+                        data_world: int = 1, data_group: Any = None) -> tuple[TrainState, StepMetrics]:
+    """One optimizer step of a pipeline-parallel model: every stage prepares the same
+    model inputs (same RNG streams on a data rank), ``runner`` (a
+    :class:`~avgen_b200.parallel.pipeline.PipelineRunner`) drives the micro-batches
+    through the stages, the last stage evaluates the loss, and the optimizer step
+    (global norm summed over the stages) follows. Returns the step's mean metrics on
+    every stage."""
+    import torch.distributed as dist
+
+    if not micro_batches:
+        raise ValueError("pipeline_train_step needs at least one micro-batch")
+    opt = state.optimizer
+    if pp_mesh is not None and hasattr(opt, "norm_groups") and not opt.norm_groups:
+        opt.norm_groups = (pp_mesh.get_group(),)  # the clip uses the norm over every stage's gradients
+    _clear_gradients(opt)
+    prepared = [objective.prepare(b, state.rng, patchifier=patchifier, cp_mesh=cp_mesh) for b in micro_batches]
+    outcomes: list[ObjectiveOutput] = []
+
+    def loss_fn(k: int, output: Any) -> torch.Tensor:
+        out = objective.finish(output, prepared[k][0], prepared[k][1])
+        outcomes.append(out)
+        return out.loss / len(micro_batches)
+
+    runner.run([p[0] for p in prepared], loss_fn)
+    dev = micro_batches[0].device
+    stats = torch.zeros(5, dtype=torch.float32, device=dev)  # loss, video, audio, valid video, valid audio
+    for out in outcomes:
+        stats += torch.stack([out.loss.detach().float(), out.video_loss.float(), out.audio_loss.float(),
+                              out.valid_video_tokens.float(), out.valid_audio_tokens.float()])
+    if pp_mesh is not None and dist.is_initialized():
+        dist.all_reduce(stats, group=pp_mesh.get_group())  # only the last stage contributes
+    stats[:3] /= len(micro_batches)
+    finite = torch.isfinite(stats[0])
+    norm, finite = optimizer_update(state, max_grad_norm=max_grad_norm, pp_mesh=pp_mesh, data_group=data_group,
+                                    finite=finite)
+    samples = sum(b.spec.batch_size for b in micro_batches) * data_world
+    state.samples_seen += samples
+    state.tokens_seen += samples * micro_batches[0].spec.sequence_length
+    metrics = StepMetrics(loss=stats[0], video_loss=stats[1], audio_loss=stats[2],
+                          valid_video_tokens=stats[3].to(torch.int64), valid_audio_tokens=stats[4].to(torch.int64),
+                          grad_norm=norm.reshape(()), nonfinite=(~finite).reshape(()), skipped=(~finite).reshape(()))
+    return state, metrics
+
+
 @dataclass(slots=True)
 class TrainerTelemetry:
     """What the fit loop measures besides the loss; every part is optional.
@@ -330,7 +377,16 @@ class Trainer:
         return metrics
 
     def run_step(self, micro_batches: Sequence[MediaBatch]) -> StepMetrics:
-        """One optimizer step over its micro-batches; returns the last micro-step's metrics."""
+        """One optimizer step over its micro-batches; returns the last micro-step's metrics
+        (the step's means under pipeline parallelism)."""
+        runner = getattr(self.parallel, "pipeline", None)
+        if runner is not None:
+            _, metrics = pipeline_train_step(
+                self.state, micro_batches, self.objective, runner, patchifier=self.patchifier,
+                max_grad_norm=self.config.max_grad_norm, cp_mesh=getattr(self.parallel, "cp_mesh", None),
+                pp_mesh=getattr(self.parallel, "pp_mesh", None), data_world=self.config.data_world,
+                data_group=getattr(self.parallel, "data_group", None))
+            return metrics
         metrics = None
         for index, batch in enumerate(micro_batches):
             metrics = self.train_step(batch, microbatch_index=index, accumulation=len(micro_batches))

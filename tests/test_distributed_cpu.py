@@ -149,6 +149,57 @@ def _cp_replicated_worker(rank: int, world: int) -> None:
     _cp_worker(rank, world, sharded=False)
 
 
+def _pipeline_worker(rank: int, world: int, schedule: str = "1f1b") -> None:
+    """Two pipeline stages (1F1B over gloo point-to-point) take the same two optimizer
+    steps, each over 3 micro-batches with gradient clipping, as the unsharded model
+    with gradient accumulation: losses and every parameter match."""
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PipelineConfig, PrecisionConfig, parallelize
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                                  build_timestep_sampler, train_step)
+    from avgen_b200.train.trainer import pipeline_train_step
+
+    ref = _model()
+    model = _model()
+    dims = ParallelDims(world_size=world, pipeline=world)
+    pm = parallelize(model, dims, mesh=dims.build_mesh("cpu"),
+                     config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32"),
+                                           pipeline=PipelineConfig(schedule=schedule)))
+    assert pm.pipeline is not None and any(a.startswith("pipeline(pp=2") for a in pm.applied), pm.applied
+    assert len(pm.model.blocks) < len(ref.blocks)
+    objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("uniform"), MultiTaskConditioning())
+    state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    c = ref.config
+    gen = torch.Generator().manual_seed(5)
+    for step in range(2):
+        micro = [random_batch(batch=1, channels=c.in_channels, frames=2, height=8, width=8, text_tokens=4,
+                              text_width=c.text_width, generator=gen) for _ in range(3)]
+        _, metrics = pipeline_train_step(state, micro, objective, pm.pipeline, patchifier=ref.patchifier,
+                                         max_grad_norm=0.05, pp_mesh=pm.pp_mesh)
+        losses = []
+        for i, b in enumerate(micro):
+            _, rm = train_step(ref_state, b, objective, patchifier=ref.patchifier, gradient_accumulation_steps=3,
+                               microbatch_index=i, max_grad_norm=0.05)
+            losses.append(float(rm.loss))
+        assert abs(float(metrics.loss) - sum(losses) / 3) <= 1e-5 * max(1.0, abs(sum(losses))), (step, metrics.loss)
+        assert abs(float(metrics.grad_norm) - float(rm.grad_norm)) <= 1e-4 * float(rm.grad_norm)
+        mine = dict(pm.model.named_parameters())
+        for name, q in ref.named_parameters():
+            if name in mine:
+                err = (mine[name].detach() - q.detach()).abs().max().item()
+                assert err <= 1e-6 + 1e-4 * q.detach().abs().max().item(), f"step {step}: {name}: {err}"
+    owned = {n for n, _ in pm.model.named_parameters()}
+    every = [None] * world
+    dist.all_gather_object(every, sorted(owned))
+    assert set().union(*map(set, every)) == {n for n, _ in ref.named_parameters()}
+
+
+def _pipeline_gpipe_worker(rank: int, world: int) -> None:
+    _pipeline_worker(rank, world, schedule="gpipe")
+
+
 def _sharded_adamw_worker(rank: int, world: int) -> None:
     """AdamW over FSDP-sharded parameters (the multi-tensor optimizer) takes the same
     two clipped steps as torch's AdamW on the unsharded model."""
@@ -234,9 +285,9 @@ def _shards_worker(rank: int, world: int) -> None:
 
 
 @pytest.mark.parametrize("worker", [_fsdp_worker, _tp_worker, _cp_worker, _cp_replicated_worker, _nonfinite_worker,
-                                    _sharded_adamw_worker],
+                                    _sharded_adamw_worker, _pipeline_worker, _pipeline_gpipe_worker],
                          ids=["fsdp", "tensor_parallel", "context_parallel", "context_parallel_replicated",
-                              "nonfinite_skip", "sharded_adamw"])
+                              "nonfinite_skip", "sharded_adamw", "pipeline_1f1b", "pipeline_gpipe"])
 def test_two_rank_parallelism(worker) -> None:  # noqa: ANN001
     _spawn(worker)
 

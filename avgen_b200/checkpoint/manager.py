@@ -253,8 +253,14 @@ class CheckpointManager:
         extra = saved - set(to_load) - {MODEL_OPTIMIZER_KEY, PROGRESS_KEY}
         if extra:
             _LOG.warning("checkpoint contains %s which this run does not use; skipped", sorted(extra))
-        with collective_timeout(self._timeout):
-            dcp.load(to_load, storage_reader=dcp.FileSystemReader(entry.path))
+        from torch.distributed.checkpoint.api import CheckpointException
+
+        try:
+            with collective_timeout(self._timeout):
+                dcp.load(to_load, storage_reader=dcp.FileSystemReader(entry.path))
+        except CheckpointException as exc:  # a BaseException in DCP: surface it as an ordinary error
+            raise RuntimeError(f"checkpoint {entry.path} could not be read (truncated or corrupt data, or a "
+                               f"state layout this run cannot take): {str(exc).splitlines()[0]}") from exc
         return entry.step
 
     def close(self) -> None:

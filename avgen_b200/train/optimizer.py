@@ -60,12 +60,19 @@ def build_param_groups(model: nn.Module, *, weight_decay: float,
     return groups
 
 
+# Hyper-parameter keys torch's AdamW keeps in every parameter group. The optimizers
+# here carry them too (with the behaviour they implement), so their state dicts and
+# DCP checkpoints load into torch's AdamW (the reference's optimizer) and back.
+_ADAMW_GROUP_KEYS = {"amsgrad": False, "maximize": False, "foreach": None, "capturable": False,
+                     "differentiable": False, "fused": None, "decoupled_weight_decay": True}
+
+
 class FusedAdamW(Optimizer):
     """AdamW over per-group flat fp32 buffers with the sm_100a fused kernel."""
 
     def __init__(self, params: Iterable[Any], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.95),
                  eps: float = 1e-8, weight_decay: float = 0.0, *, dp_group: Any = None) -> None:
-        defaults = {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay}
+        defaults = {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay, **_ADAMW_GROUP_KEYS}
         super().__init__(params, defaults)
         self.dp_group = dp_group
         self.max_grad_norm: float | None = None
@@ -429,7 +436,8 @@ class MultiTensorAdamW(Optimizer):
 
     def __init__(self, params: Iterable[Any], lr: float = 1e-3, betas: tuple[float, float] = (0.9, 0.95),
                  eps: float = 1e-8, weight_decay: float = 0.0) -> None:
-        super().__init__(params, {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay})
+        super().__init__(params, {"lr": lr, "betas": betas, "eps": eps, "weight_decay": weight_decay,
+                                  **_ADAMW_GROUP_KEYS})
         self.max_grad_norm: float | None = None
         self.last_grad_norm: torch.Tensor | None = None
         self.last_nonfinite: torch.Tensor | None = None

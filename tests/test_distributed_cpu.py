@@ -200,6 +200,72 @@ def _pipeline_gpipe_worker(rank: int, world: int) -> None:
     _pipeline_worker(rank, world, schedule="gpipe")
 
 
+def _lora_tp_worker(rank: int, world: int, use_dora: bool = False) -> None:
+    """LoRA / DoRA on tensor-parallel DTensor weights: adapter placements follow the
+    base weight's shard dimension (column-parallel Shard(0) -> A replicated, B
+    Shard(0); row-parallel Shard(1) -> A Shard(1), B replicated; the DoRA magnitude
+    like B), and forward plus every adapter gradient match the unsharded adapted
+    model (the DoRA row norms of a row-parallel weight sum squares across ranks)."""
+    from torch.distributed.tensor import DTensor, Replicate, Shard, distribute_tensor
+
+    from avgen_b200.finetune.lora import LoRAConfig, apply_lora, lora_modules, mark_only_lora_trainable
+    from avgen_b200.parallel import ParallelDims, parallelize
+
+    cfg = LoRAConfig(rank=4, alpha=8.0, use_dora=use_dora, target_modules=("q_proj", "out_proj", "down_proj"))
+    ref = apply_lora(_model(), cfg)
+    torch.manual_seed(3)
+    with torch.no_grad():  # non-zero B: the adapter contributes to the output
+        for _, m in lora_modules(ref):
+            m.lora_b.normal_(0.0, 0.05)
+            if m.lora_magnitude is not None:
+                m.lora_magnitude.mul_(1.0 + 0.1 * torch.randn_like(m.lora_magnitude))
+    mark_only_lora_trainable(ref)
+    dims = ParallelDims(world_size=world, tensor=world)
+    pm = parallelize(_model(), dims, mesh=dims.build_mesh("cpu"), adapt=lambda m: apply_lora(m, cfg))
+    mark_only_lora_trainable(pm.model)
+    ref_mods = dict(lora_modules(ref))
+    checked = set()
+    for name, mod in lora_modules(pm.model):
+        w = mod.weight
+        if not isinstance(w, DTensor):  # layers outside the tensor-parallel plan (text refiner) stay plain
+            assert not name.startswith("blocks."), name
+            with torch.no_grad():
+                for attr in ("lora_a", "lora_b", "lora_magnitude"):
+                    if getattr(mod, attr) is not None:
+                        getattr(mod, attr).copy_(getattr(ref_mods[name], attr))
+            continue
+        dim = [p.dim for p in w.placements if isinstance(p, Shard)][0]
+        want_a, want_b = ((Replicate(),), (Shard(0),)) if dim == 0 else ((Shard(1),), (Replicate(),))
+        assert tuple(mod.lora_a.placements) == want_a and tuple(mod.lora_b.placements) == want_b, name
+        if mod.lora_magnitude is not None:
+            assert tuple(mod.lora_magnitude.placements) == want_b, name
+        checked.add(dim)
+        r = ref_mods[name]
+        with torch.no_grad():  # the same adapter values as the unsharded model
+            for attr in ("lora_a", "lora_b", "lora_magnitude"):
+                t = getattr(mod, attr)
+                if t is not None:
+                    t.copy_(distribute_tensor(getattr(r, attr).detach(), t.device_mesh, list(t.placements)))
+    assert checked == {0, 1}, "both column- and row-parallel adapters must be covered"
+    out = pm.model(_inputs(61, ref))
+    want = ref(_inputs(61, ref))
+    torch.testing.assert_close(out.video.detach(), want.video.detach(), rtol=1e-4, atol=1e-5)
+    _loss(out).backward()
+    _loss(want).backward()
+    for name, mod in lora_modules(pm.model):
+        for attr in ("lora_a", "lora_b", "lora_magnitude"):
+            t = getattr(mod, attr)
+            if t is None:
+                continue
+            g = t.grad.full_tensor() if isinstance(t.grad, DTensor) else t.grad
+            torch.testing.assert_close(g, getattr(ref_mods[name], attr).grad, rtol=1e-3, atol=1e-5,
+                                       msg=f"{name}.{attr}")
+
+
+def _dora_tp_worker(rank: int, world: int) -> None:
+    _lora_tp_worker(rank, world, use_dora=True)
+
+
 def _sharded_adamw_worker(rank: int, world: int) -> None:
     """AdamW over FSDP-sharded parameters (the multi-tensor optimizer) takes the same
     two clipped steps as torch's AdamW on the unsharded model."""
@@ -285,9 +351,11 @@ def _shards_worker(rank: int, world: int) -> None:
 
 
 @pytest.mark.parametrize("worker", [_fsdp_worker, _tp_worker, _cp_worker, _cp_replicated_worker, _nonfinite_worker,
-                                    _sharded_adamw_worker, _pipeline_worker, _pipeline_gpipe_worker],
+                                    _sharded_adamw_worker, _pipeline_worker, _pipeline_gpipe_worker, _lora_tp_worker,
+                                    _dora_tp_worker],
                          ids=["fsdp", "tensor_parallel", "context_parallel", "context_parallel_replicated",
-                              "nonfinite_skip", "sharded_adamw", "pipeline_1f1b", "pipeline_gpipe"])
+                              "nonfinite_skip", "sharded_adamw", "pipeline_1f1b", "pipeline_gpipe", "lora_tensor_parallel",
+                              "dora_tensor_parallel"])
 def test_two_rank_parallelism(worker) -> None:  # noqa: ANN001
     _spawn(worker)
 

@@ -222,10 +222,20 @@ class VideoDiT(nn.Module):
     def _denoise(self, hidden: torch.Tensor, *, modulation: torch.Tensor, rope: RopeInputs | None,
                  key_mask: torch.Tensor | None, context: torch.Tensor | None,
                  context_mask: torch.Tensor | None, modulation_index: torch.Tensor | None = None) -> torch.Tensor:
+        tp = getattr(self, "head_parallel", None)
+        sequence = tp is not None and tp.sequence_parallel
+        if sequence:  # the residual stream between blocks holds this rank's tokens only
+            length = hidden.shape[1]
+            hidden = tp.local_tokens(hidden)
+            modulation = tp.shared(modulation)
+            if modulation_index is not None:
+                modulation_index = modulation_index[:, tp.token_slice(length)]
+            elif modulation.ndim == 4:
+                modulation = modulation[:, tp.token_slice(length)]
         for block in self.blocks:
             hidden = block(hidden, modulation=modulation, rope=rope, key_mask=key_mask, context=context,
                            context_mask=context_mask, modulation_index=modulation_index)
-        return hidden
+        return tp.all_tokens(hidden) if sequence else hidden
 
     def _video_head(self, hidden: torch.Tensor, stream: TokenStream) -> torch.Tensor:
         normed = self.final_norm(hidden)

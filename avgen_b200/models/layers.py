@@ -122,9 +122,13 @@ class SwiGLU(nn.Module):
         self.gate_proj = nn.Linear(width, hidden, bias=bias)
         self.up_proj = nn.Linear(width, hidden, bias=bias)
         self.down_proj = nn.Linear(hidden, width, bias=bias)
+        self.tp = None  # set by head-parallel sharding: this rank's slice of the hidden units
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
-        return linear(F.silu(linear(hidden, self.gate_proj)) * linear(hidden, self.up_proj), self.down_proj)
+        if self.tp is not None:
+            hidden = self.tp.enter(hidden)
+        out = linear(F.silu(linear(hidden, self.gate_proj)) * linear(hidden, self.up_proj), self.down_proj)
+        return self.tp.leave(out) if self.tp is not None else out
 
     def init_weights(self, *, std: float = 0.02, out_std: float | None = None) -> None:
         init_linear(self.gate_proj, std=std)
@@ -139,9 +143,13 @@ class GeluMLP(nn.Module):
         super().__init__()
         self.up_proj = nn.Linear(width, hidden, bias=bias)
         self.down_proj = nn.Linear(hidden, width, bias=bias)
+        self.tp = None  # set by head-parallel sharding
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
-        return linear(F.gelu(linear(hidden, self.up_proj), approximate="tanh"), self.down_proj)
+        if self.tp is not None:
+            hidden = self.tp.enter(hidden)
+        out = linear(F.gelu(linear(hidden, self.up_proj), approximate="tanh"), self.down_proj)
+        return self.tp.leave(out) if self.tp is not None else out
 
     def init_weights(self, *, std: float = 0.02, out_std: float | None = None) -> None:
         init_linear(self.up_proj, std=std)
@@ -174,12 +182,15 @@ class SelfAttention(nn.Module):
         self.q_norm = rms_norm(head_dim, eps=eps) if qk_norm else nn.Identity()
         self.k_norm = rms_norm(head_dim, eps=eps) if qk_norm else nn.Identity()
         self.cp_mesh = None  # set by context parallelism: attention becomes global over the shards
+        self.tp = None  # set by head-parallel sharding: this rank's heads, collectives in and out
 
     def _heads(self, x: torch.Tensor) -> torch.Tensor:
         return x.unflatten(-1, (-1, self.head_dim)).transpose(1, 2)
 
     def forward(self, hidden: torch.Tensor, rope: RotaryTables | None = None, *,
                 key_mask: torch.Tensor | None = None) -> torch.Tensor:
+        if self.tp is not None:
+            hidden = self.tp.enter(hidden)
         q = self.q_norm(self._heads(linear(hidden, self.q_proj)))
         k = self.k_norm(self._heads(linear(hidden, self.k_proj)))
         v = self._heads(linear(hidden, self.v_proj))
@@ -192,7 +203,8 @@ class SelfAttention(nn.Module):
             out = cp_attention(q, k, v, mesh=self.cp_mesh, key_mask=key_mask).transpose(1, 2)
         else:
             out = attention(q, k, v, key_mask=key_mask, layout="blhd")
-        return linear(out.flatten(2), self.out_proj)
+        out = linear(out.flatten(2), self.out_proj)
+        return self.tp.leave(out) if self.tp is not None else out
 
     def init_weights(self, *, std: float = 0.02, out_std: float | None = None) -> None:
         for layer in (self.q_proj, self.k_proj, self.v_proj):
@@ -221,6 +233,7 @@ class CrossAttention(nn.Module):
         self.out_proj = nn.Linear(num_heads * head_dim, width, bias=bias)
         self.q_norm = rms_norm(head_dim, eps=eps) if qk_norm else nn.Identity()
         self.k_norm = rms_norm(head_dim, eps=eps) if qk_norm else nn.Identity()
+        self.tp = None  # set by head-parallel sharding
 
     def _heads(self, x: torch.Tensor) -> torch.Tensor:
         return x.unflatten(-1, (-1, self.head_dim)).transpose(1, 2)
@@ -229,6 +242,9 @@ class CrossAttention(nn.Module):
                 ) -> torch.Tensor:
         if context.shape[1] == 0:
             return torch.zeros_like(hidden)
+        if self.tp is not None:
+            hidden = self.tp.enter(hidden)
+            context = self.tp.shared(context)  # every rank's heads read the same text tokens
         q = self.q_norm(self._heads(linear(hidden, self.q_proj)))
         k = self.k_norm(self._heads(linear(context, self.k_proj)))
         v = self._heads(linear(context, self.v_proj))
@@ -236,7 +252,8 @@ class CrossAttention(nn.Module):
         if mask is not None and mask.ndim != 2:
             raise ValueError("cross-attention context mask must be (batch, keys)")
         out = attention(q, k, v, key_mask=mask, layout="blhd")
-        return linear(out.flatten(2), self.out_proj)
+        out = linear(out.flatten(2), self.out_proj)
+        return self.tp.leave(out) if self.tp is not None else out
 
     def init_weights(self, *, std: float = 0.02, zero_output: bool = True) -> None:
         for layer in (self.q_proj, self.k_proj, self.v_proj):

@@ -113,7 +113,9 @@ def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, confi
     if dims.tp_enabled and mesh is not None:
         apply_tensor_parallel(model, mesh["tp"], sequence_parallel=cfg.sequence_parallel,
                               block_attribute=cfg.block_attribute)
-        applied.append(f"tensor_parallel(tp={dims.tensor})")
+        heads = getattr(model, "head_parallel", None)
+        applied.append(f"tensor_parallel(tp={dims.tensor}" + (
+            f", heads, sequence_parallel={heads.sequence_parallel})" if heads is not None else ", dtensor)"))
     if adapt is not None:
         model = adapt(model)
         applied.append("adapt")

@@ -7,9 +7,9 @@ local projection width). Every parallel style hands plain local tensors to the
 rest of the block, so norms, adaLN modulation and the attention kernel see
 ordinary tensors.
 
-Sequence parallelism (norm activations sharded along tokens) is not provided by
-this module: requesting it raises. Token sharding across ranks is what context
-parallelism does.
+Uneven head counts (20 heads at tp=8) and sequence parallelism (norms and
+residuals on token shards) take the head-parallel path of
+:mod:`avgen_b200.parallel.heads` instead of the DTensor plans.
 """
 from __future__ import annotations
 
@@ -37,8 +37,8 @@ class TensorParallelizable(Protocol):
 
 def _no_sp(sequence_parallel: bool) -> None:
     if sequence_parallel:
-        raise NotImplementedError("sequence_parallel=True is not supported by the tensor-parallel plan; use "
-                                  "sequence_parallel=False (context parallelism shards tokens)")
+        raise NotImplementedError("the DTensor plans have no sequence parallelism; use style='heads' "
+                                  "(apply_tensor_parallel picks it automatically)")
 
 
 def standard_block_plan(*, sequence_parallel: bool = False, attention_prefix: str = "attention",
@@ -66,11 +66,39 @@ def standard_root_plan(*, sequence_parallel: bool = False) -> TensorParallelPlan
     return {}
 
 
+def _heads_divide(model: nn.Module, tp: int, block_attribute: str) -> bool:
+    for block in getattr(model, block_attribute, ()):
+        for name in ("attention", "cross_attention"):
+            att = getattr(block, name, None)
+            if att is not None and (att.num_heads % tp or getattr(att, "num_kv_heads", att.num_heads) % tp):
+                return False
+    return True
+
+
 def apply_tensor_parallel(model: nn.Module, mesh, *, sequence_parallel: bool = False,  # noqa: ANN001
                           block_attribute: str = "blocks", root_plan: TensorParallelPlan | None = None,
-                          block_plan: TensorParallelPlan | None = None) -> nn.Module:
+                          block_plan: TensorParallelPlan | None = None, style: str = "auto") -> nn.Module:
+    """Shard the blocks over the tensor-parallel ``mesh``.
+
+    ``style="dtensor"``: torch DTensor plans (equal column / row chunks; the head
+    counts must divide by the degree; no sequence parallelism). ``style="heads"``:
+    whole heads per rank with uneven splits and optional sequence-parallel norms
+    (:mod:`avgen_b200.parallel.heads`). ``"auto"`` takes DTensor plans when the
+    heads divide and no sequence parallelism is asked for, else heads."""
     from torch.distributed.tensor.parallel import parallelize_module
 
+    if style not in ("auto", "dtensor", "heads"):
+        raise ValueError(f"style must be auto, dtensor or heads; got {style!r}")
+    if style == "auto":
+        style = "dtensor" if (not sequence_parallel and _heads_divide(model, mesh.size(), block_attribute)
+                              and block_plan is None) else "heads"
+    if style == "heads":
+        from avgen_b200.parallel.heads import apply_head_parallel
+
+        if block_plan is not None or root_plan:
+            raise ValueError("custom DTensor plans go with style='dtensor'")
+        apply_head_parallel(model, mesh, sequence_parallel=sequence_parallel, block_attribute=block_attribute)
+        return model
     _no_sp(sequence_parallel)
     if root_plan is None or block_plan is None:
         if isinstance(model, TensorParallelizable):

@@ -266,6 +266,64 @@ def _dora_tp_worker(rank: int, world: int) -> None:
     _lora_tp_worker(rank, world, use_dora=True)
 
 
+def _head_parallel_worker(rank: int, world: int, sequence_parallel: bool = False) -> None:
+    """Tensor parallelism by whole heads over a prime number of ranks (4 heads over 3:
+    an uneven [2, 1, 1] split), with and without sequence-parallel norms: output and
+    every gradient match the unsharded model; checkpoints hold full tensors."""
+    from avgen_b200.core.tokens import TextContext
+    from avgen_b200.infer.conditioning import StreamState, condition_first_frame
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, parallelize
+    from avgen_b200.parallel.heads import head_partition
+
+    assert head_partition(20, 8) == [3, 3, 3, 3, 2, 2, 2, 2]
+
+    def inputs(model):  # noqa: ANN001, ANN202 - 3 frames x 4 x 4 patches = 48 tokens (divisible by 3)
+        g = torch.Generator().manual_seed(71)
+        c = model.config
+        lat = torch.randn(1, c.in_channels, 3, 8, 8, generator=g)
+        text = TextContext(features=torch.randn(1, 6, c.text_width, generator=g),
+                           mask=torch.ones(1, 6, dtype=torch.bool))
+        return condition_first_frame(StreamState(lat, fps=8.0), lat[:, :, 0], sigma=0.6, text=text,
+                                     patchifier=model.patchifier)
+
+    ref = _model()
+    want = ref(inputs(ref))
+    _loss(want).backward()
+    ref_grads = {n: p.grad for n, p in ref.named_parameters()}
+    full_state = {k: v.clone() for k, v in ref.state_dict().items()}
+    dims = ParallelDims(world_size=world, tensor=world)
+    pm = parallelize(_model(), dims, mesh=dims.build_mesh("cpu"),
+                     config=ParallelConfig(sequence_parallel=sequence_parallel))
+    assert any(f"heads, sequence_parallel={sequence_parallel}" in a for a in pm.applied), pm.applied
+    assert pm.model.blocks[0].attention.num_heads == [2, 1, 1][rank]
+    out = pm.model(inputs(ref))
+    torch.testing.assert_close(out.video.detach(), want.video.detach(), rtol=1e-4, atol=1e-5)
+    _loss(out).backward()
+    modules = dict(pm.model.named_modules())
+    for name, p in pm.model.named_parameters():
+        g = ref_grads[name]
+        owner = modules[name.rsplit(".", 1)[0]]
+        shard = getattr(owner, "_avgen_tp_shard", None)
+        if shard is not None and (name.endswith("weight") or shard[0] == 0):
+            dim, sizes, _ = shard
+            g = g.narrow(dim, sum(sizes[:rank]), sizes[rank])
+        torch.testing.assert_close(p.grad, g, rtol=1e-3, atol=1e-5, msg=name)
+    saved = pm.model.state_dict()  # gathered to full tensors
+    for key, value in full_state.items():
+        torch.testing.assert_close(saved[key], value, rtol=0, atol=0, msg=key)
+    pm.model.load_state_dict(saved)  # sliced back to this rank's heads
+
+
+def _head_parallel_sp_worker(rank: int, world: int) -> None:
+    _head_parallel_worker(rank, world, sequence_parallel=True)
+
+
+@pytest.mark.parametrize("worker", [_head_parallel_worker, _head_parallel_sp_worker],
+                         ids=["heads_uneven", "heads_uneven_sequence_parallel"])
+def test_three_rank_head_parallel(worker) -> None:  # noqa: ANN001
+    _spawn(worker, 3)
+
+
 def _sharded_adamw_worker(rank: int, world: int) -> None:
     """AdamW over FSDP-sharded parameters (the multi-tensor optimizer) takes the same
     two clipped steps as torch's AdamW on the unsharded model."""

@@ -71,9 +71,15 @@ def _worker(rank: int, world: int, port: int) -> None:
                                         MultiTaskConditioning())
             g = torch.Generator().manual_seed(50 + rank)
             norms = []
+            grads = {}
             for step in range(2):
                 batch = random_batch(batch=1, channels=4, frames=4, height=16, width=32, text_tokens=16,
                                      text_width=128, generator=g, device=dev)
+                if step == 0:  # the reduced gradient shards themselves, before any optimizer step
+                    opt.zero_grad()
+                    loss = obj(pm.model, batch, RNGStreams.for_rank(9, data_rank=rank), patchifier=pm.model.patchifier)
+                    loss.loss.backward()
+                    grads = {n: p.grad.full_tensor().clone() for n, p in pm.model.named_parameters()}
                 _, metrics = train_step(state, batch, obj, patchifier=pm.model.patchifier,
                                         max_grad_norm=0.5 if step else None)
                 norms.append(metrics.grad_norm)
@@ -81,17 +87,24 @@ def _worker(rank: int, world: int, port: int) -> None:
             params = {n: (p.full_tensor() if isinstance(p, DTensor) else p).detach().clone()
                       for n, p in pm.model.named_parameters()}
             moments = {n: opt.state[p]["exp_avg"].full_tensor().clone() for n, p in pm.model.named_parameters()}
-            runs[peer] = (params, torch.stack([torch.as_tensor(x, device=dev).float() for x in norms]), moments)
+            runs[peer] = (params, torch.stack([torch.as_tensor(x, device=dev).float() for x in norms]), moments,
+                          grads)
             if peer:
                 gather, reduce = pm.model._avgen_peer_collectives
                 assert gather.calls > 0 and reduce.calls > 0
                 assert not gather.slots.buf.check_guards() and not reduce.slots.buf.check_guards()
         assert check_errors(dev) == 0
-        (p_peer, n_peer, m_peer), (p_nccl, n_nccl, m_nccl) = runs[True], runs[False]
+        (p_peer, n_peer, m_peer, g_peer), (p_nccl, n_nccl, m_nccl, g_nccl) = runs[True], runs[False]
+        for name in g_nccl:  # the reduce-scatter: the same fp32 sums (up to summation order)
+            err = (g_peer[name] - g_nccl[name]).abs().max().item()
+            assert err <= 1e-6 + 1e-5 * g_nccl[name].abs().max().item(), f"grad {name}: {err}"
         torch.testing.assert_close(n_peer, n_nccl, rtol=1e-4, atol=1e-6)
         for name in p_nccl:
-            torch.testing.assert_close(p_peer[name], p_nccl[name], rtol=1e-4, atol=1e-6, msg=name)
-            torch.testing.assert_close(m_peer[name], m_nccl[name], rtol=1e-3, atol=1e-7, msg=name)
+            # AdamW divides by sqrt(v): rounding-level gradient differences on near-zero entries
+            # can move a parameter by up to ~lr per step, so compare at that scale
+            err = (p_peer[name] - p_nccl[name]).abs().max().item()
+            assert err <= 2.5e-3, f"param {name}: {err}"
+            torch.testing.assert_close(m_peer[name], m_nccl[name], rtol=1e-3, atol=1e-6, msg=name)
     finally:
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()

@@ -42,6 +42,23 @@ WIDTH, DEPTH, HEADS, TEXT_TOKENS, TEXT_WIDTH, CHANNELS = 2560, 32, 20, 512, 4096
 FRAMES, HEIGHT, WIDTH_PX = 16, 128, 128  # 65,536 tokens after 1x2x2 patching
 PEAK_NOMINAL = 2.25e15
 
+# The BASELINE.json workloads. "2b_64k" is the headline the driver runs; the others
+# are selected with --config. layout: "dp_cp" = cp = min(4, N) ring ranks and dp = N / cp
+# data ranks, each GPU a whole sample's tokens per step; "cp_all" = one sample per
+# step sharded over all N ranks (ring cp = N, FSDP over the same ranks); "tp_all" =
+# tensor parallel over all N ranks by heads with sequence-parallel norms.
+WORKLOADS = {
+    "2b_64k": {"width": 2560, "depth": 32, "heads": 20, "ffn_hidden": None, "frames": 16, "layout": "dp_cp",
+               "samples": None, "label": "2B video DiT @64k tok"},
+    "14b_131k": {"width": 5120, "depth": 40, "heads": 40, "ffn_hidden": 13824, "frames": 32, "layout": "cp_all",
+                 "samples": 1, "label": "14B video DiT @131k tok, cp ring + FSDP over the same ranks"},
+    "2b_32k_tp": {"width": 2560, "depth": 32, "heads": 20, "ffn_hidden": None, "frames": 8, "layout": "tp_all",
+                  "samples": 8, "label": "2B video DiT @32k tok, tensor parallel by heads + sequence parallel"},
+    "2b_16k_lora": {"width": 2560, "depth": 32, "heads": 20, "ffn_hidden": None, "frames": 4, "layout": "dp_cp",
+                    "samples": None, "lora_rank": 64,
+                    "label": "2B video DiT @16k tok, LoRA rank 64 on every attention/MLP linear, FSDP2 x cp"},
+}
+
 
 def parse_args() -> argparse.Namespace:
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
@@ -54,11 +71,22 @@ def parse_args() -> argparse.Namespace:
                    help="reference CP attention: as shipped (block-local: each rank attends within its own shard, "
                         "the stock training path) or wrapped in its own context_parallel_region (torch ring SDPA; "
                         "fails on this model's text cross-attention with torch 2.11)")
-    p.add_argument("--depth", type=int, default=DEPTH, help="override for quick local checks (not a valid bench)")
-    p.add_argument("--frames", type=int, default=FRAMES)
+    p.add_argument("--config", choices=tuple(WORKLOADS), default="2b_64k",
+                   help="BASELINE workload (default: the headline 2B at 64k tokens)")
+    p.add_argument("--depth", type=int, default=None, help="override for quick local checks (not a valid bench)")
+    p.add_argument("--frames", type=int, default=None)
     p.add_argument("--profile-step", action="store_true",
                    help="after the timed region, print the device-time breakdown of one step (stderr)")
-    return p.parse_args()
+    args = p.parse_args()
+    work = WORKLOADS[args.config]
+    args.work = work
+    args.full_depth = work["depth"]
+    args.full_frames = work["frames"]
+    if args.depth is None:
+        args.depth = work["depth"]
+    if args.frames is None:
+        args.frames = work["frames"]
+    return args
 
 
 # --------------------------------------------------------------------------- helpers
@@ -123,13 +151,14 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def model_flops_per_sample(tokens: int, depth: int, *, attention_shards: int = 1) -> float:
+def model_flops_per_sample(tokens: int, depth: int, *, attention_shards: int = 1, width: int = WIDTH,
+                           hidden: int | None = None) -> float:
     """Training FLOPs of one sample (3 x forward; recompute not counted).
 
     ``attention_shards`` > 1 counts block-local self-attention over that many
     contiguous shards (each token attends only within its shard): 1/shards of
     the global attention FLOPs."""
-    w, f, t = WIDTH, 4 * WIDTH, TEXT_TOKENS
+    w, f, t = width, hidden or 4 * width, TEXT_TOKENS
     per_block_linear = 2 * tokens * (6 * w * w + 3 * w * f) + 2 * t * 2 * w * w
     per_block_attn = 4 * tokens * tokens * w / attention_shards + 4 * tokens * t * w
     root = 2 * tokens * (64 * w + w * 64) + 2 * t * TEXT_WIDTH * w
@@ -184,19 +213,43 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
                                   TrainerConfig, build_optimizer, build_timestep_sampler, train_step)
 
     dev = torch.device("cuda", local)
-    cp, dp = layout(world)
+    work = args.work
+    tp = 1
+    if work["layout"] == "cp_all":
+        cp, dp = world, 1
+    elif work["layout"] == "tp_all":
+        cp, dp, tp = 1, 1, world
+    else:
+        cp, dp = layout(world)
     # The named config's layout through the public API: parameters (and AdamW
     # state) sharded over dp_shard x cp (FSDP2, collectives over NVLink peer
-    # memory), global attention over the cp ranks (NVLink ring).
-    dims = ParallelDims(world_size=world, dp_shard=dp, context=cp)
+    # memory), global attention over the cp ranks (NVLink ring); or tensor
+    # parallelism by heads with sequence-parallel norms.
+    dims = ParallelDims(world_size=world, dp_shard=dp, context=cp, tensor=tp)
     torch.manual_seed(1234)
+    spec = {"width": work["width"], "depth": args.depth, "num_heads": work["heads"], "text_width": TEXT_WIDTH,
+            "text_context_length": TEXT_TOKENS, "in_channels": CHANNELS}
+    if work["ffn_hidden"]:
+        spec["ffn_hidden"] = work["ffn_hidden"]
     with torch.device("meta"):
-        model = build_model("video_dit", {"width": WIDTH, "depth": args.depth, "num_heads": HEADS,
-                                          "text_width": TEXT_WIDTH, "text_context_length": TEXT_TOKENS,
-                                          "in_channels": CHANNELS})
+        model = build_model("video_dit", spec)
     model = model.to_empty(device=dev)
     model.init_weights()
-    pm = parallelize(model, dims, config=ParallelConfig(activation_checkpoint=ActivationCheckpointConfig(mode="none")))
+    adapt = None
+    if work.get("lora_rank"):
+        from avgen_b200.finetune.lora import LoRAConfig, apply_lora
+
+        lora = LoRAConfig(rank=work["lora_rank"], alpha=float(work["lora_rank"]),
+                          target_modules=("q_proj", "k_proj", "v_proj", "out_proj", "gate_proj", "up_proj",
+                                          "down_proj"))
+        def adapt(m):  # noqa: ANN001, ANN202 - adapters (only they train) go in before sharding
+            from avgen_b200.finetune.lora import mark_only_lora_trainable
+
+            apply_lora(m, lora)
+            mark_only_lora_trainable(m)
+            return m
+    pm = parallelize(model, dims, config=ParallelConfig(activation_checkpoint=ActivationCheckpointConfig(mode="none"),
+                                                        sequence_parallel=tp > 1), adapt=adapt)
     model = pm.model
     cp_mesh = pm.cp_mesh
     data_rank = dims.data_coordinates(pm.mesh)[0] if pm.mesh is not None else 0
@@ -205,7 +258,7 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("shifted_logit_normal"),
                                       MultiTaskConditioning())
     patchifier = pm.model.patchifier
-    micro = cp
+    micro = work["samples"] or cp
     gen = torch.Generator().manual_seed(1000 + data_rank)
     shape = dict(batch=1, channels=CHANNELS, frames=args.frames, height=HEIGHT, width=WIDTH_PX,
                  text_tokens=TEXT_TOKENS, text_width=TEXT_WIDTH)
@@ -275,9 +328,11 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     barrier()
     e2e_s = max_over_ranks(time.perf_counter() - t0) / max(1, args.e2e_steps)
 
-    samples_per_step = world  # global batch (dp groups x cp micro-batches of one sample)
+    samples_per_step = dp * micro  # global batch: every data group's micro-batches of one sample
     value = samples_per_step / (ms / 1000.0)
-    flops = model_flops_per_sample(tokens, args.depth)
+    flops = model_flops_per_sample(tokens, args.depth, width=work["width"], hidden=work["ffn_hidden"])
+    if work.get("lora_rank"):
+        flops *= 2.0 / 3.0  # frozen base weights: forward and input gradients, no weight gradients
     mfu = flops * value / (world * PEAK_NOMINAL)
     return {
         "value": value, "ms_per_step": ms, "mfu": mfu, "loss": loss_val, "kernel_errors": err,
@@ -287,7 +342,8 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
         "exposed_comm": {"ms_per_step": sum(comm.values()), "share_of_step": sum(comm.values()) / ms,
                          "ring_ms_per_step": ring_ms, "ring_share_of_step": ring_ms / ms,
                          "by_source_ms_per_step": comm} if world > 1 else None,
-        "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "micro": micro,
+        "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "tp": tp, "micro": micro,
+        "global_batch": samples_per_step,
         "params": sum(p.numel() for p in model.parameters()), "applied": list(pm.applied),
         "peak_mem_gib": torch.cuda.max_memory_allocated(dev) / 2**30,
     }
@@ -496,22 +552,33 @@ def main() -> None:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun --nproc-per-node {args.gpus}")
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
-    out = run_reference(args, rank, world, local) if args.impl == "reference" else run_ours(args, rank, world, local)
+    if args.impl == "reference" and args.config != "2b_64k":
+        out = {"unavailable": f"the reference arm runs the headline workload only (asked for {args.config})"}
+    elif args.impl == "reference":
+        out = run_reference(args, rank, world, local)
+    else:
+        out = run_ours(args, rank, world, local)
     if rank == 0:
         if "unavailable" in out:
             print(json.dumps({"impl": "reference", "unavailable": out["unavailable"]}), flush=True)
         else:
-            cp, dp = out["cp"], out["dp"]
+            cp, dp, tp = out["cp"], out["dp"], out.get("tp", 1)
+            work = args.work
+            metric = ("samples/s + MFU, 2B video DiT @64k tok, 1/2/4/8 B200; ring-attn exposed comm"
+                      if args.config == "2b_64k" else f"samples/s + MFU, {work['label']}")
+            hidden = f"MLP {work['ffn_hidden']}" if work["ffn_hidden"] else "SwiGLU mlp_ratio 4"
+            parallelism = "single" if world == 1 else (f"tp{tp}+sp" if tp > 1 else f"dp{dp}xcp{cp}")
             line = {
-                "metric": "samples/s + MFU, 2B video DiT @64k tok, 1/2/4/8 B200; ring-attn exposed comm",
+                "metric": metric,
                 "value": out["value"], "unit": "samples/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": out["ms_per_step"], "higher_is_better": True,
-                "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-                "data": "synthetic N(0,1) latents [1,16,16,128,128] and text [1,512,4096]; random-init weights",
-                "config": {"model": f"video_dit {args.depth}x{WIDTH}, {HEADS} heads x 128, SwiGLU mlp_ratio 4, "
+                "scaling": "weak" if work["layout"] == "dp_cp" else "strong", "vs_baseline": None, "dtype": "bf16",
+                "data": f"synthetic N(0,1) latents [1,16,{args.frames},128,128] and text [1,512,4096]; "
+                        "random-init weights",
+                "config": {"model": f"video_dit {args.depth}x{work['width']}, {work['heads']} heads x 128, {hidden}, "
                                     f"QK-RMSNorm, 3-D RoPE, cross-attn 512x4096",
-                           "global_batch": world, "seq_len": out["tokens"],
-                           "parallelism": (f"dp{dp}xcp{cp}" if world > 1 else "single"),
+                           "global_batch": out.get("global_batch", world), "seq_len": out["tokens"],
+                           "parallelism": parallelism,
                            "micro_batches_per_step": out["micro"],
                            "l2": "inputs larger than L2 (each block activation is 335 MB)"},
                 "mfu": out["mfu"], "loss": out["loss"], "e2e": out["e2e"], "clocks": out["clocks"],
@@ -531,8 +598,10 @@ def main() -> None:
                 line["peak_mem_gib"] = round(out["peak_mem_gib"], 1)
                 if out["exposed_comm"] is not None:
                     line["exposed_comm"] = out["exposed_comm"]
-            if args.depth != DEPTH or args.frames != FRAMES:
+            if args.depth != args.full_depth or args.frames != args.full_frames:
                 line["note"] = "reduced model/config: not a valid benchmark line"
+            if args.config != "2b_64k":
+                line["config"]["workload"] = args.config
             print(json.dumps(line), flush=True)
     if dist.is_initialized():
         barrier()

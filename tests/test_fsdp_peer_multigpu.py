@@ -95,9 +95,12 @@ def _worker(rank: int, world: int, port: int) -> None:
                 assert not gather.slots.buf.check_guards() and not reduce.slots.buf.check_guards()
         assert check_errors(dev) == 0
         (p_peer, n_peer, m_peer, g_peer), (p_nccl, n_nccl, m_nccl, g_nccl) = runs[True], runs[False]
-        for name in g_nccl:  # the reduce-scatter: the same fp32 sums (up to summation order)
+        for name in g_nccl:
+            # the same fp32 sums of each rank's gradient; those gradients are bf16 (FSDP's parameter dtype)
+            # and come from GEMMs with fp32 atomic split-K, so two runs may differ by one bf16 rounding
+            # step (2^-8 relative); a misplaced shard or offset would differ by the gradient's own size
             err = (g_peer[name] - g_nccl[name]).abs().max().item()
-            assert err <= 1e-6 + 1e-5 * g_nccl[name].abs().max().item(), f"grad {name}: {err}"
+            assert err <= 1e-6 + 8e-3 * g_nccl[name].abs().max().item(), f"grad {name}: {err}"
         torch.testing.assert_close(n_peer, n_nccl, rtol=1e-4, atol=1e-6)
         for name in p_nccl:
             # AdamW divides by sqrt(v): rounding-level gradient differences on near-zero entries

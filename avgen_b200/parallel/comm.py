@@ -8,6 +8,8 @@ from __future__ import annotations
 
 from collections.abc import Iterable
 
+from typing import Any
+
 import torch
 import torch.distributed as dist
 from torch.distributed.device_mesh import DeviceMesh
@@ -59,11 +61,24 @@ def clip_grad_norm(parameters: Iterable[torch.nn.Parameter], max_norm: float, *,
     """Clip by the global L2 norm (DTensor shards reduced, PP stages summed)."""
     from torch.distributed.tensor import DTensor
 
+    from avgen_b200.parallel.heads import tp_shard_group
+
     params = [p for p in parameters if p.grad is not None]
-    grads = [p.grad for p in params]
-    total = torch.nn.utils.get_total_norm(grads, norm_type=2.0, error_if_nonfinite=error_if_nonfinite, foreach=foreach)
+    replicated = [p.grad for p in params if tp_shard_group(p) is None]
+    by_group: dict[Any, list[torch.Tensor]] = {}
+    for p in params:
+        if tp_shard_group(p) is not None:
+            by_group.setdefault(tp_shard_group(p), []).append(p.grad)
+    total = torch.nn.utils.get_total_norm(replicated, norm_type=2.0, error_if_nonfinite=error_if_nonfinite,
+                                          foreach=foreach) if replicated else None
     if isinstance(total, DTensor):
         total = total.full_tensor()
+    for group, grads in by_group.items():  # head-parallel slices: their squares sum over the group
+        sq = torch.nn.utils.get_total_norm(grads, norm_type=2.0, foreach=foreach).pow(2)
+        dist.all_reduce(sq, group=group)
+        total = sq.sqrt() if total is None else (total.pow(2) + sq).sqrt()
+    if total is None:
+        total = torch.zeros((), device=params[0].grad.device if params else "cpu")
     if pp_mesh is not None and pp_mesh.size() > 1:
         sq = total.pow(2)
         dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=pp_mesh.get_group())

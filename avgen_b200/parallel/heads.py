@@ -34,7 +34,12 @@ import torch
 import torch.distributed as dist
 from torch import nn
 
-__all__ = ["HeadParallel", "apply_head_parallel", "head_partition"]
+__all__ = ["HeadParallel", "apply_head_parallel", "head_partition", "tp_shard_group"]
+
+
+def tp_shard_group(param: torch.Tensor) -> Any:
+    """The tensor-parallel group whose ranks hold disjoint slices of ``param`` (None if replicated)."""
+    return getattr(param, "_avgen_tp_group", None)
 
 
 def head_partition(count: int, parts: int) -> list[int]:
@@ -192,6 +197,11 @@ def _keep(linear: nn.Linear, dim: int, start: int, length: int, full: int, tp: H
     sizes_t = torch.tensor(sizes)
     dist.all_reduce(sizes_t, group=tp.group)
     linear._avgen_tp_shard = (dim, [int(s) for s in sizes_t], full)  # type: ignore[attr-defined]
+    # the parameters themselves carry their group: a global gradient norm sums their
+    # squares over it (every rank holds a different slice), replicated ones count once
+    linear.weight._avgen_tp_group = tp.group  # type: ignore[attr-defined]
+    if linear.bias is not None and dim == 0:
+        linear.bias._avgen_tp_group = tp.group  # type: ignore[attr-defined]
 
     def save_full(module: nn.Module, state: dict, prefix: str, _meta: Any) -> None:
         d, all_sizes, _ = module._avgen_tp_shard

@@ -175,6 +175,21 @@ class FusedAdamW(Optimizer):
                 K.sq_norm_(flat["grad"], acc)
             else:
                 acc += flat["grad"].pow(2).sum()
+        # head-parallel slices (each rank a different part): their squares sum over the group
+        from avgen_b200.parallel.heads import tp_shard_group
+
+        sliced: dict[Any, list[torch.Tensor]] = {}
+        for group in self.param_groups:
+            for p in group["params"]:
+                if tp_shard_group(p) is not None and p.grad is not None:
+                    sliced.setdefault(tp_shard_group(p), []).append(p.grad)
+        for tp_group, grads in sliced.items():
+            part = torch.zeros(1, device=acc.device, dtype=torch.float32)
+            for g in grads:
+                part += g.float().pow(2).sum()
+            local = part.clone()
+            dist.all_reduce(part, group=tp_group)
+            acc += part - local
         for group in self.norm_groups:
             dist.all_reduce(acc, group=group)
         return acc.sqrt()[0]

@@ -318,8 +318,39 @@ def _head_parallel_sp_worker(rank: int, world: int) -> None:
     _head_parallel_worker(rank, world, sequence_parallel=True)
 
 
-@pytest.mark.parametrize("worker", [_head_parallel_worker, _head_parallel_sp_worker],
-                         ids=["heads_uneven", "heads_uneven_sequence_parallel"])
+def _head_parallel_train_worker(rank: int, world: int) -> None:
+    """Two clipped AdamW steps with head-parallel sequence-parallel sharding over 3 ranks
+    equal two steps of the unsharded model: the global gradient norm sums the squares of
+    the ranks' slices once and counts replicated parameters once."""
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, parallelize
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                                  build_timestep_sampler, train_step)
+
+    ref = _model()
+    dims = ParallelDims(world_size=world, tensor=world)
+    pm = parallelize(_model(), dims, mesh=dims.build_mesh("cpu"), config=ParallelConfig(sequence_parallel=True))
+    obj = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("uniform"), MultiTaskConditioning())
+    state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    c = ref.config
+    gen = torch.Generator().manual_seed(9)
+    for step in range(2):
+        batch = random_batch(batch=1, channels=c.in_channels, frames=3, height=8, width=8, text_tokens=4,
+                             text_width=c.text_width, generator=gen)
+        _, m = train_step(state, batch, obj, patchifier=ref.patchifier, max_grad_norm=0.05)
+        _, rm = train_step(ref_state, batch, obj, patchifier=ref.patchifier, max_grad_norm=0.05)
+        assert abs(float(m.grad_norm) - float(rm.grad_norm)) <= 1e-4 * float(rm.grad_norm), (step, m.grad_norm,
+                                                                                              rm.grad_norm)
+        full = pm.model.state_dict()
+        for name, q in ref.state_dict().items():
+            err = (full[name].float() - q.float()).abs().max().item()
+            assert err <= 1e-6 + 1e-4 * q.float().abs().max().item(), f"step {step}: {name}: {err}"
+
+
+@pytest.mark.parametrize("worker", [_head_parallel_worker, _head_parallel_sp_worker, _head_parallel_train_worker],
+                         ids=["heads_uneven", "heads_uneven_sequence_parallel", "heads_sp_two_clipped_steps"])
 def test_three_rank_head_parallel(worker) -> None:  # noqa: ANN001
     _spawn(worker, 3)
 

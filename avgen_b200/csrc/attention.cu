@@ -256,17 +256,11 @@ __global__ void __launch_bounds__(384, 1)
       }
       tc_fence_after();
       if (tr) stamp(j, ts);
-      uint32_t sr[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]);
-        tmem_ld32(tS + 32 * c, chunk);
-      }
-      tmem_wait_ld();
-      if (tr) stamp(j, ts + 1);
+      // key-validity words of this tile, loaded before the TMEM read so their latency overlaps it
       const int kbase = (ring ? (j + ring_start) % nkv : j) * kTile;
-      if (kbase + kTile > p.Lk || p.kmask != nullptr) {
-        uint32_t words[4];
+      const bool check_keys = kbase + kTile > p.Lk || p.kmask != nullptr;
+      uint32_t words[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (check_keys) {
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           const int key0 = kbase + 32 * w;
@@ -276,6 +270,17 @@ __global__ void __launch_bounds__(384, 1)
           if (left < 32) bits &= (left <= 0) ? 0u : ((1u << left) - 1u);
           words[w] = bits;
         }
+      }
+      uint32_t sr[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t (&chunk)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sr[32 * c]);
+        tmem_ld32(tS + 32 * c, chunk);
+      }
+      tmem_wait_ld();
+      if (tr) stamp(j, ts + 1);
+      // a tile whose keys are all valid (a dense mask) skips the per-element selects
+      if (check_keys && (words[0] & words[1] & words[2] & words[3]) != 0xffffffffu) {
 #pragma unroll
         for (int c = 0; c < 128; ++c)
           if (!((words[c >> 5] >> (c & 31)) & 1u)) sr[c] = __float_as_uint(-INFINITY);

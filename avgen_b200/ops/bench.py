@@ -49,6 +49,9 @@ def bench_attention(length: int, heads: int, iters: int, once: bool) -> None:
     flops = 4.0 * heads * length * length * 128
     t_fwd = _time(lambda: K.attention_fwd(q, k, v), iters)
     t_bwd = _time(lambda: K.attention_bwd(q, k, v, out, dout, lse), iters)
+    dense = K.pack_key_mask(torch.ones(1, length, dtype=torch.bool, device="cuda"))  # what the model passes
+    t_fwd_m = _time(lambda: K.attention_fwd(q, k, v, kmask=dense), iters)
+    t_bwd_m = _time(lambda: K.attention_bwd(q, k, v, out, dout, lse, kmask=dense), iters)
     qt, kt, vt = (t.requires_grad_() for t in (q.clone(), k.clone(), v.clone()))
     ref = torch.nn.functional.scaled_dot_product_attention
     t_lf = _time(lambda: ref(qt, kt, vt), iters)
@@ -57,7 +60,8 @@ def bench_attention(length: int, heads: int, iters: int, once: bool) -> None:
     t_lb = _time(lambda: torch.autograd.grad(o, (qt, kt, vt), g, retain_graph=True), iters)
     print(f"attention L={length} H={heads}: fwd {t_fwd:.3f} ms ({flops / t_fwd / 1e9:.0f} TF/s) | "
           f"bwd {t_bwd:.3f} ms ({2.5 * flops / t_bwd / 1e9:.0f} TF/s counted) | "
-          f"torch SDPA fwd {t_lf:.3f} ms, bwd {t_lb:.3f} ms")
+          f"torch SDPA fwd {t_lf:.3f} ms, bwd {t_lb:.3f} ms | with an all-valid key mask: fwd {t_fwd_m:.3f} ms, "
+          f"bwd {t_bwd_m:.3f} ms")
 
 
 def trace_attention(length: int, heads: int, which: str) -> None:

@@ -456,15 +456,16 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
         return metrics
 
     # Activation checkpointing: the cheapest of the reference's own policies that
-    # fits, tried in order of recompute (none, selective_op saving every listed op,
-    # then every 2nd, then full), each moved past only after a caught CUDA OOM on
-    # some rank (every rank takes the same path: the OOM flag is max-reduced).
+    # runs, tried in order of recompute (none, selective_op saving every listed op,
+    # then every 2nd, then full), each moved past only after a caught CUDA OOM (or
+    # an error of the mode itself) on some rank (every rank takes the same path: the
+    # failure flag is max-reduced); the line lists each rejected mode with its reason.
     current: dict = {}
     attempts: list[str] = []
     ac_mode = "full"
     for mode, frequency in (("none", 1), ("selective_op", 1), ("selective_op", 2), ("full", 1)):
         label = mode if mode != "selective_op" else f"selective_op(save_op_frequency={frequency})"
-        oom = 0.0
+        failed, why = 0.0, ""
         try:
             parallel, state, data_rank = build(mode, frequency)
             current.update(parallel=parallel, state=state)
@@ -475,11 +476,13 @@ def run_reference(args: argparse.Namespace, rank: int, world: int, local: int) -
                 step(dev_batches, copy=False)
                 torch.cuda.synchronize()
         except torch.OutOfMemoryError:
-            oom = 1.0
-        if max_over_ranks(oom) == 0.0:
+            failed, why = 1.0, "CUDA out of memory"
+        except RuntimeError as exc:  # the mode itself fails on this model (not a memory limit)
+            failed, why = 1.0, f"{type(exc).__name__}: {str(exc).splitlines()[0][:160]}"
+        if max_over_ranks(failed) == 0.0:
             ac_mode = label
             break
-        attempts.append(f"{label}: CUDA out of memory")
+        attempts.append(f"{label}: {why or 'failed on another rank'}")
         current.clear()
         parallel = state = host = dev_batches = None
         import gc

@@ -107,8 +107,10 @@ class BucketSampler:
         n = len(plan.buckets)
         if curriculum is not None and curriculum.bucket_count != n:
             raise ValueError("curriculum weights do not match the bucket plan")
-        self._weights = tuple(weights) if weights is not None else tuple(float(len(self._pools[b.bucket_id]))
-                                                                        for b in plan.buckets)
+        # without explicit weights a bucket is drawn as often as its pool fills whole batches on every
+        # rank, so an epoch visits each sample at most once whatever the buckets' micro-batch sizes
+        self._weights = tuple(weights) if weights is not None else tuple(
+            float(len(self._pools[b.bucket_id]) // (self._bsz(b.bucket_id) * data_world)) for b in plan.buckets)
         self._curriculum = curriculum
 
     @property
@@ -135,7 +137,10 @@ class BucketSampler:
 
     def quotas_at(self, step: int, *, batches: int | None = None) -> tuple[int, ...]:
         total = self.batches_per_epoch() if batches is None else batches
-        return largest_remainder(total, self.weights_at(step))
+        weights = self.weights_at(step)
+        if total == 0 or not any(weights):
+            return tuple(0 for _ in weights)
+        return largest_remainder(total, weights)
 
     def plan_epoch(self, *, epoch: int, step: int = 0) -> tuple[BucketBatch, ...]:
         """This rank's batches for ``epoch`` (identical plan on every rank, disjoint slices)."""

@@ -114,6 +114,11 @@ def read_safetensors_dir(path: Path) -> dict[str, torch.Tensor]:
 
 def import_safetensors(path: str | os.PathLike[str], model: nn.Module, *, strict: bool = True) -> nn.Module:
     tensors = read_safetensors_dir(Path(path))
+    if strict:  # DCP's full-state load reports unexpected keys but fills missing ones from the model itself
+        missing = sorted(set(model.state_dict()) - set(tensors))
+        if missing:
+            raise RuntimeError(f"{path} lacks {len(missing)} tensor(s) of the model, e.g. {missing[:3]}; pass "
+                               "strict=False to load the shared subset")
     set_model_state_dict(model, model_state_dict=tensors,
                          options=StateDictOptions(full_state_dict=True, strict=strict))
     from avgen_b200.models.linear import bump_weight_epoch

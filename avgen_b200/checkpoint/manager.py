@@ -25,6 +25,7 @@ import torch
 import torch.distributed as dist
 import torch.distributed.checkpoint as dcp
 from torch import nn
+from torch.distributed.checkpoint.api import CheckpointException
 
 from avgen_b200.checkpoint.stateful import (EMA_KEY, EXTRAS_KEY, MODEL_OPTIMIZER_KEY, PROGRESS_KEY, RNG_KEY,
                                             SCHEDULE_KEY, build_stateful)
@@ -253,8 +254,6 @@ class CheckpointManager:
         extra = saved - set(to_load) - {MODEL_OPTIMIZER_KEY, PROGRESS_KEY}
         if extra:
             _LOG.warning("checkpoint contains %s which this run does not use; skipped", sorted(extra))
-        from torch.distributed.checkpoint.api import CheckpointException
-
         try:
             with collective_timeout(self._timeout):
                 dcp.load(to_load, storage_reader=dcp.FileSystemReader(entry.path))
@@ -296,8 +295,8 @@ def load_model(path: str | Path, model: nn.Module, *, strict: bool = True) -> No
     holder = {MODEL_OPTIMIZER_KEY: {"model": get_model_state_dict(model, options=opts)}}
     try:
         dcp.load(holder, checkpoint_id=str(d))
-    except Exception as exc:  # noqa: BLE001
-        raise RuntimeError(f"could not read model weights from {d}: {exc}") from exc
+    except (Exception, CheckpointException) as exc:  # noqa: BLE001 - DCP's error is a BaseException
+        raise RuntimeError(f"could not read model weights from {d}: {str(exc).splitlines()[0]}") from exc
     set_model_state_dict(model, holder[MODEL_OPTIMIZER_KEY]["model"], options=opts)
     from avgen_b200.models.linear import bump_weight_epoch
 
@@ -315,7 +314,7 @@ def load_ema(path: str | Path, model: nn.Module, *, decay: float = 0.9999) -> No
     holder = {EMA_KEY: ema.state_dict()}
     try:
         dcp.load(holder, checkpoint_id=str(d))
-    except Exception as exc:  # noqa: BLE001
-        raise RuntimeError(f"could not read EMA weights from {d}: {exc}") from exc
+    except (Exception, CheckpointException) as exc:  # noqa: BLE001 - DCP's error is a BaseException
+        raise RuntimeError(f"could not read EMA weights from {d}: {str(exc).splitlines()[0]}") from exc
     ema.load_state_dict(holder[EMA_KEY])
     ema.copy_to(model)

@@ -74,7 +74,10 @@ def _fused_eligible(block: DiTBlock, hidden: torch.Tensor) -> bool:
 
     if any(isinstance(m.weight, DTensor) or hasattr(m, "adapted_weight") for m in linears
            if isinstance(m, nn.Linear)):
-        return False  # tensor-parallel shards and adapters run the per-layer path
+        return False  # DTensor shards and adapters run the per-layer path
+    tp = getattr(block, "tp", None)
+    if tp is not None and (not tp.sequence_parallel or block.attention_impl is not None):
+        return False  # head-parallel shards fuse with sequence parallelism and local attention
     return all(getattr(m, "bias", None) is None for m in linears if isinstance(m, nn.Linear))
 
 

@@ -21,6 +21,16 @@ recompute the rest) built into the block.
 
 Self-attention can be swapped for a context-parallel implementation through
 ``BlockSpec.attention`` (see :mod:`avgen_b200.parallel.context`).
+
+Head-parallel tensor parallelism with sequence parallelism
+(:mod:`avgen_b200.parallel.heads`) runs through the same node: the norms,
+modulation and gated residuals act on this rank's token chunk; each normalised
+input is all-gathered over the tensor-parallel group before the rank's q/k/v,
+cross-attention and MLP GEMMs (its heads and hidden slice over the whole
+sequence), and each output projection's partial sums are reduce-scattered back
+to the token chunk before the gated residual. The backward mirrors that: the
+gradient entering each output projection is all-gathered, the gradient leaving
+each input projection is reduce-scattered.
 """
 from __future__ import annotations
 
@@ -85,6 +95,16 @@ class BlockSpec:
     attention: AttentionImpl | None = None
     mod_rows_per_batch: int = 0   # rows sharing one modulation row (0: ``length``)
     groups: torch.Tensor | None = None  # int32 [B*L] modulation row per token (overrides the above)
+    # head-parallel tensor parallelism with sequence parallelism: ``length`` is this rank's
+    # token chunk (norms, modulation, residuals), ``full_length`` the sequence the rank's
+    # heads attend over; None / 0 without tensor parallelism
+    tp: Any = None
+    full_length: int = 0
+
+    @property
+    def seq(self) -> int:
+        """Tokens per sample the attention and its projections see."""
+        return self.full_length or self.length
 
     def mod_rows(self) -> dict[str, Any]:
         """Keyword arguments selecting each token's modulation row in the kernels."""
@@ -152,6 +172,55 @@ def _norm_weight(norm: nn.Module) -> torch.Tensor | None:
     return _f32(w) if isinstance(w, torch.Tensor) else None
 
 
+def _tp_gather(spec: BlockSpec, rows: torch.Tensor) -> torch.Tensor:
+    """This rank's token rows ``[B*L_local, C]`` -> every rank's, ``[B*L, C]`` in sequence
+    order (identity without tensor parallelism)."""
+    tp = spec.tp
+    if tp is None:
+        return rows
+    import torch.distributed as dist
+
+    rows = rows.contiguous()
+    out = torch.empty((tp.world, *rows.shape), dtype=rows.dtype, device=rows.device)
+    dist.all_gather_into_tensor(out, rows, group=tp.group)
+    if spec.batch == 1:
+        return out.view(-1, rows.shape[-1])
+    c = rows.shape[-1]
+    return out.view(tp.world, spec.batch, spec.length, c).transpose(0, 1).reshape(spec.batch * spec.seq, c)
+
+
+def _tp_reduce(spec: BlockSpec, rows: torch.Tensor) -> torch.Tensor:
+    """Partial sums over the full sequence ``[B*L, C]`` -> this rank's token rows of their
+    sum over the tensor-parallel ranks, ``[B*L_local, C]`` (identity without it)."""
+    tp = spec.tp
+    if tp is None:
+        return rows
+    import torch.distributed as dist
+
+    c = rows.shape[-1]
+    src = rows.contiguous() if spec.batch == 1 else \
+        rows.view(spec.batch, tp.world, spec.length, c).transpose(0, 1).contiguous()
+    out = torch.empty((spec.batch * spec.length, c), dtype=rows.dtype, device=rows.device)
+    dist.reduce_scatter_tensor(out, src, group=tp.group)
+    return out
+
+
+def _gated_residual(spec: BlockSpec, resid: torch.Tensor, update: torch.Tensor,
+                    gate: torch.Tensor | None) -> torch.Tensor:
+    """``resid + gate * update`` on local rows (each row's gate picked as the kernels'
+    modulation rows do), computed in fp32 and rounded once; the tensor-parallel form of
+    the GEMM's gated-residual epilogue, which cannot run before the reduce-scatter."""
+    r, u = resid.float(), update.float()
+    if gate is None:
+        return (r + u).to(_BF16)
+    if spec.groups is not None:
+        return (r + gate[spec.groups.long()] * u).to(_BF16)
+    rpb = spec.mod_rows_per_batch or spec.length
+    w = r.shape[-1]
+    out = r.view(-1, rpb, w) + gate.view(-1, 1, w) * u.view(-1, rpb, w)
+    return out.view(-1, w).to(_BF16)
+
+
 def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask, *, save,  # noqa: ANN001, ANN202
                   keep_inter=False):
     """Run the block head; returns (intermediates, O, lse, attn_state). The
@@ -167,13 +236,14 @@ def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     att = block.attention
     n1, rstd1 = K.rmsnorm_mod(xb, _norm_weight(block.attention_norm), scale_a, shift_a, **spec.mod_rows(),
                               eps=block.attention_norm.eps or eps)
-    qkv = K.gemm(n1, pw["qkv"])
+    n1g = _tp_gather(spec, n1)
+    qkv = K.gemm(n1g, pw["qkv"])
     qw = _norm_weight(att.q_norm) if spec.qk_norm else None
     kw = _norm_weight(att.k_norm) if spec.qk_norm else None
     impl = _attn_impl(spec)
     kv_out = getattr(impl, "kv_out", None) if save else None  # ring CP: write K/V into the shared buffer
     bufs = kv_out(b, hk, length, d, xb.device) if kv_out is not None else None
-    q, k, v = K.qkv_rope(qkv, batch=b, length=length, heads=h, kv_heads=hk, head_dim=d, q_weight=qw, k_weight=kw,
+    q, k, v = K.qkv_rope(qkv, batch=b, length=spec.seq, heads=h, kv_heads=hk, head_dim=d, q_weight=qw, k_weight=kw,
                          coords=coords, freq=freq, axis=axis, eps=eps, k_out=bufs[0] if bufs else None,
                          v_out=bufs[1] if bufs else None)
     scale = 1.0 / math.sqrt(d)
@@ -184,7 +254,7 @@ def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     return_o = o
     inter: dict[str, Any] = {}
     if not save or keep_inter:
-        inter.update(n1=n1, rstd1=rstd1, qkv=qkv, q=q, k=k, v=v)
+        inter.update(n1=n1, n1g=n1g, rstd1=rstd1, qkv=qkv, q=q, k=k, v=v)
     return inter, return_o, lse, attn_state
 
 
@@ -198,43 +268,58 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep, want_out=Fal
 
     b, length, w = spec.batch, spec.length, spec.width
     m = b * length
+    mf = b * spec.seq
     eps = spec.eps
     gate_a = modf[:, 2]
     shift_f, scale_f, gate_f = modf[:, 3], modf[:, 4], modf[:, 5]
     keep_d: dict[str, Any] = {}
-    a_o = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
-    x1 = K.gemm(o.view(m, -1), pw["o"], epilogue="gate_resid", resid=xb, gate=gate_a, **spec.mod_rows(),
-                aux=a_o)
+    if spec.tp is None:
+        a_o = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
+        x1 = K.gemm(o.view(m, -1), pw["o"], epilogue="gate_resid", resid=xb, gate=gate_a, **spec.mod_rows(),
+                    aux=a_o)
+    else:
+        a_o = _tp_reduce(spec, K.gemm(o.view(mf, -1), pw["o"]))
+        x1 = _gated_residual(spec, xb, a_o, gate_a)
     x2 = x1
     if spec.cross and ctxb is not None:
         ca = block.cross_attention
         n2, rstd2 = K.rmsnorm_mod(x1, _norm_weight(block.cross_norm), eps=block.cross_norm.eps or eps)
-        qc = K.gemm(n2, pw["cq"])
+        n2g = _tp_gather(spec, n2)
+        qc = K.gemm(n2g, pw["cq"])
         t = ctxb.shape[1]
         kvc = K.gemm(ctxb.view(b * t, -1), pw["ckv"])
         cqw = _norm_weight(ca.q_norm) if spec.qk_norm else None
         ckw = _norm_weight(ca.k_norm) if spec.qk_norm else None
-        qh, _, _ = K.qkv_rope(qc, batch=b, length=length, heads=spec.ctx_heads, kv_heads=0, head_dim=spec.head_dim,
+        qh, _, _ = K.qkv_rope(qc, batch=b, length=spec.seq, heads=spec.ctx_heads, kv_heads=0, head_dim=spec.head_dim,
                               q_weight=cqw, k_weight=None, coords=None, freq=None, axis=None, eps=eps)
         _, kc, vc = K.qkv_rope(kvc, batch=b, length=t, heads=0, kv_heads=spec.ctx_kv_heads, head_dim=spec.head_dim,
                                q_weight=None, k_weight=ckw, coords=None, freq=None, axis=None, eps=eps)
         oc, lsec = K.attention_fwd(qh, kc, vc, kmask=cmask, scale=1.0 / math.sqrt(spec.head_dim))
-        x2 = K.gemm(oc.view(m, -1), pw["co"], epilogue="gate_resid", resid=x1, gate=None)
+        if spec.tp is None:
+            x2 = K.gemm(oc.view(m, -1), pw["co"], epilogue="gate_resid", resid=x1, gate=None)
+        else:
+            x2 = _gated_residual(spec, x1, _tp_reduce(spec, K.gemm(oc.view(mf, -1), pw["co"])), None)
         if keep:
-            keep_d.update(x1=x1, n2=n2, rstd2=rstd2, qc=qc, kvc=kvc, qh=qh, kc=kc, vc=vc, oc=oc, lsec=lsec)
+            keep_d.update(x1=x1, n2=n2, n2g=n2g, rstd2=rstd2, qc=qc, kvc=kvc, qh=qh, kc=kc, vc=vc, oc=oc,
+                          lsec=lsec)
     elif keep:
         keep_d.update(x1=x1)
     n3, rstd3 = K.rmsnorm_mod(x2, _norm_weight(block.ffn_norm), scale_f, shift_f, **spec.mod_rows(),
                               eps=block.ffn_norm.eps or eps)
-    gu, hdn = _mlp_up(spec, pw, n3, keep=keep and keep_mlp)
+    n3g = _tp_gather(spec, n3)
+    gu, hdn = _mlp_up(spec, pw, n3g, keep=keep and keep_mlp)
     if keep and not want_out:
-        f = K.gemm(hdn, pw["down"])
-        keep_d.update(a_o=a_o, x2=x2, n3=n3, rstd3=rstd3, gu=gu, h=hdn, f=f)
+        f = _tp_reduce(spec, K.gemm(hdn, pw["down"]))
+        keep_d.update(a_o=a_o, x2=x2, n3=n3, n3g=n3g, rstd3=rstd3, gu=gu, h=hdn, f=f)
         return None, keep_d
-    f = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
-    x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, **spec.mod_rows(), aux=f)
+    if spec.tp is None:
+        f = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
+        x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, **spec.mod_rows(), aux=f)
+    else:
+        f = _tp_reduce(spec, K.gemm(hdn, pw["down"]))
+        x3 = _gated_residual(spec, x2, f, gate_f)
     if keep:
-        keep_d.update(a_o=a_o, x2=x2, n3=n3, rstd3=rstd3, f=f)
+        keep_d.update(a_o=a_o, x2=x2, n3=n3, n3g=n3g, rstd3=rstd3, f=f)
         if keep_mlp:
             keep_d.update(gu=gu, h=hdn)
     return x3, keep_d
@@ -265,6 +350,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
 
     b, length, w = spec.batch, spec.length, spec.width
     m = b * length
+    mf = b * spec.seq
     h, hk, d = spec.heads, spec.kv_heads, spec.head_dim
     eps = spec.eps
     dev = xb.device
@@ -276,7 +362,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
         inter, keep = saved
         if "gu" not in keep:  # the MLP activations were not kept: rebuild them from n3
             keep = dict(keep)
-            keep["gu"], keep["h"] = _mlp_up(spec, pw, keep["n3"], keep=True)
+            keep["gu"], keep["h"] = _mlp_up(spec, pw, keep["n3g"], keep=True)
     else:
         inter, _, _, _ = _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask,
                                        save=False)
@@ -289,22 +375,22 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
         return torch.zeros(p.shape, device=dev, dtype=torch.float32)
 
     # ---------------------------------------------------------------- FFN
-    df = K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], **spec.mod_rows())
+    df = _tp_gather(spec, K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], **spec.mod_rows()))
     dh = K.linear_dx(df, pw["down"])
     g_down = zeros_like_param(ff.down_proj.weight)
     K.linear_dw(df, keep["h"], g_down)
     if spec.ffn == "swiglu":
         dgu = K.swiglu_bwd(dh, keep["gu"])
-        dn3 = K.linear_dx(dgu, pw["gu"])
+        dn3 = _tp_reduce(spec, K.linear_dx(dgu, pw["gu"]))
         g_gu = torch.zeros((2 * spec.hidden, w), device=dev, dtype=torch.float32)
-        K.linear_dw(dgu, keep["n3"], g_gu)
+        K.linear_dw(dgu, keep["n3g"], g_gu)
         g_gate = g_gu[0::2].contiguous()
         g_up = g_gu[1::2].contiguous()
     else:
         dpre = K.gelu_bwd(dh, keep["gu"])
-        dn3 = K.linear_dx(dpre, pw["up"])
+        dn3 = _tp_reduce(spec, K.linear_dx(dpre, pw["up"]))
         g_up = zeros_like_param(ff.up_proj.weight)
-        K.linear_dw(dpre, keep["n3"], g_up)
+        K.linear_dw(dpre, keep["n3g"], g_up)
         g_gate = None
     g_ffn_norm = zeros_like_param(block.ffn_norm.weight) if block.ffn_norm.weight is not None else None
     dx2 = K.rmsnorm_mod_bwd(keep["x2"], keep["rstd3"], dn3, _norm_weight(block.ffn_norm), modf[:, 4], modf[:, 3],
@@ -316,25 +402,26 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     if spec.cross and ctxb is not None:
         ca = block.cross_attention
         t = ctxb.shape[1]
-        doc = K.linear_dx(dx2, pw["co"])
+        dco = _tp_gather(spec, dx2)
+        doc = K.linear_dx(dco, pw["co"])
         g_co = zeros_like_param(ca.out_proj.weight)
-        K.linear_dw(dx2, keep["oc"].view(m, -1), g_co)
+        K.linear_dw(dco, keep["oc"].view(mf, -1), g_co)
         dqh, dkc, dvc = K.attention_bwd(keep["qh"], keep["kc"], keep["vc"], keep["oc"],
-                                        doc.view(b, length, spec.ctx_heads, d), keep["lsec"], kmask=cmask,
+                                        doc.view(b, spec.seq, spec.ctx_heads, d), keep["lsec"], kmask=cmask,
                                         scale=1.0 / math.sqrt(d))
         cqw = _norm_weight(ca.q_norm) if spec.qk_norm else None
         ckw = _norm_weight(ca.k_norm) if spec.qk_norm else None
         g_cqn = zeros_like_param(ca.q_norm.weight) if cqw is not None else None
         g_ckn = zeros_like_param(ca.k_norm.weight) if ckw is not None else None
-        dqc = K.qkv_rope_bwd(keep["qc"], dqh.to(_BF16), None, None, batch=b, length=length, heads=spec.ctx_heads,
+        dqc = K.qkv_rope_bwd(keep["qc"], dqh.to(_BF16), None, None, batch=b, length=spec.seq, heads=spec.ctx_heads,
                              kv_heads=0, head_dim=d, q_weight=cqw, k_weight=None, coords=None, freq=None, axis=None,
                              dq_weight=g_cqn, eps=eps)
         dkvc = K.qkv_rope_bwd(keep["kvc"], None, dkc, dvc, batch=b, length=t, heads=0, kv_heads=spec.ctx_kv_heads,
                               head_dim=d, q_weight=None, k_weight=ckw, coords=None, freq=None, axis=None,
                               dk_weight=g_ckn, eps=eps)
-        dn2 = K.linear_dx(dqc, pw["cq"])
+        dn2 = _tp_reduce(spec, K.linear_dx(dqc, pw["cq"]))
         g_cq = zeros_like_param(ca.q_proj.weight)
-        K.linear_dw(dqc, keep["n2"], g_cq)
+        K.linear_dw(dqc, keep["n2g"], g_cq)
         g_ckv = torch.zeros((pw["ckv"].shape[0], pw["ckv"].shape[1]), device=dev, dtype=torch.float32)
         K.linear_dw(dkvc, ctxb.view(b * t, -1), g_ckv)
         dctx = K.linear_dx(dkvc, pw["ckv"]).view(b, t, -1)
@@ -347,23 +434,23 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     else:
         dx1 = dx2
     # ---------------------------------------------------------------- self attention
-    da = K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], **spec.mod_rows())
+    da = _tp_gather(spec, K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], **spec.mod_rows()))
     do = K.linear_dx(da, pw["o"])
     g_o = zeros_like_param(att.out_proj.weight)
-    K.linear_dw(da, o.view(m, -1), g_o)
+    K.linear_dw(da, o.view(mf, -1), g_o)
     impl = _attn_impl(spec)
-    dq, dk, dv = impl.backward(inter["q"], inter["k"], inter["v"], o, do.view(b, length, h, d), lse, kmask,
+    dq, dk, dv = impl.backward(inter["q"], inter["k"], inter["v"], o, do.view(b, spec.seq, h, d), lse, kmask,
                                1.0 / math.sqrt(d), attn_state)
     qw = _norm_weight(att.q_norm) if spec.qk_norm else None
     kw = _norm_weight(att.k_norm) if spec.qk_norm else None
     g_qn = zeros_like_param(att.q_norm.weight) if qw is not None else None
     g_kn = zeros_like_param(att.k_norm.weight) if kw is not None else None
-    dqkv = K.qkv_rope_bwd(inter["qkv"], dq.to(_BF16), dk, dv, batch=b, length=length, heads=h, kv_heads=hk,
+    dqkv = K.qkv_rope_bwd(inter["qkv"], dq.to(_BF16), dk, dv, batch=b, length=spec.seq, heads=h, kv_heads=hk,
                           head_dim=d, q_weight=qw, k_weight=kw, coords=coords, freq=freq, axis=axis, dq_weight=g_qn,
                           dk_weight=g_kn, eps=eps)
-    dn1 = K.linear_dx(dqkv, pw["qkv"])
+    dn1 = _tp_reduce(spec, K.linear_dx(dqkv, pw["qkv"]))
     g_qkv = torch.zeros((pw["qkv"].shape[0], w), device=dev, dtype=torch.float32)
-    K.linear_dw(dqkv, inter["n1"], g_qkv)
+    K.linear_dw(dqkv, inter["n1g"], g_qkv)
     g_attn_norm = zeros_like_param(block.attention_norm.weight) if block.attention_norm.weight is not None else None
     dx = K.rmsnorm_mod_bwd(xb, inter["rstd1"], dn1, _norm_weight(block.attention_norm), modf[:, 1], modf[:, 0],
                            dres=dx1, dweight=g_attn_norm, dscale=dmod[:, 1], dshift=dmod[:, 0],
@@ -421,7 +508,7 @@ def _keep_mode(spec: BlockSpec, xb: torch.Tensor) -> str:
         return "none"
     free, _ = torch.cuda.mem_get_info(xb.device)
     free += torch.cuda.memory_reserved(xb.device) - torch.cuda.memory_allocated(xb.device)
-    tokens = spec.batch * spec.length
+    tokens = spec.batch * spec.seq
     w, f = spec.width, spec.hidden
     # reserve what the rest of the forward must still hold: every later block's saved
     # input and attention output (up to 40 blocks) and ring buffers not yet allocated
@@ -530,5 +617,16 @@ def fused_block_forward(block: nn.Module, hidden: torch.Tensor, combined_mod: to
                      ctx_kv_heads=ca.num_kv_heads if ca is not None else 0,
                      text_length=context.shape[1] if context is not None else 0, attention=attention_impl,
                      mod_rows_per_batch=rpb, groups=groups)
+    tp = getattr(block, "tp", None)
+    if tp is not None:
+        # head-parallel shards: this rank's heads and MLP slice over the whole sequence, the
+        # residual stream on its own token chunk; the text context feeds every rank's heads,
+        # so its gradient is summed over the group
+        if not tp.sequence_parallel or attention_impl is not None:
+            raise ValueError("the fused block runs tensor parallelism with sequence parallelism and local "
+                             "attention only")
+        spec.tp, spec.full_length = tp, length * tp.world
+        if context is not None:
+            context = tp.shared(context)
     params = [p for n, p in block.named_parameters() if n != "scale_shift_table"]
     return FusedBlockFn.apply(spec, block, coords, freq, axis, kmask, cmask, hidden, combined_mod, context, *params)

@@ -22,6 +22,11 @@ tensor-parallel region through one collective pair:
   ``scale_shift_table``, the shared modulation rows and the text context feeding
   every rank's heads) have their gradients summed over the group.
 
+With sequence parallelism and local attention the block runs as one fused
+sm_100a node on its shards (the collectives sit between its kernels, see
+:mod:`avgen_b200.models.fused`); without it the block runs module by module
+through the enter / leave pairs above.
+
 Checkpoints hold full tensors: each sharded weight's state-dict entry is
 gathered from the ranks' (possibly uneven) slices on save and sliced on load.
 """
@@ -287,8 +292,7 @@ def apply_head_parallel(model: nn.Module, mesh: Any, *, sequence_parallel: bool 
         if block.cross_attention is not None:
             _shard_attention(block.cross_attention, tp)
         _shard_mlp(block.feed_forward, tp)
-        block.tp = tp
-        block.use_fused = False  # the fused block runs whole heads on one device
+        block.tp = tp  # the fused block takes these shards when sequence parallel (models/fused.py)
         if sequence_parallel:  # these act on local tokens only: sum their gradients over the group
             for p in (block.attention_norm.weight, getattr(block.cross_norm, "weight", None),
                       block.ffn_norm.weight, block.scale_shift_table):

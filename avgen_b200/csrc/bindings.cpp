@@ -11,6 +11,10 @@
 #include "include/launchers.h"
 
 namespace avgen {
+bool install_crash_backtrace();  // crash_trace.cpp
+}
+
+namespace avgen {
 namespace {
 
 using OptT = c10::optional<at::Tensor>;
@@ -973,6 +977,8 @@ PYBIND11_MODULE(_C, m) {
         arg("trace") = none, arg("kt_begin") = 0, arg("kt_count") = 0, arg("skip_prologue") = false,
         arg("skip_epilogue") = false);
   m.def("slab_sum", &a::slab_sum, arg("srcs"), arg("dst"));
+  m.def("install_crash_backtrace", &avgen::install_crash_backtrace,
+        "print native frames on SIGSEGV/SIGBUS/SIGFPE/SIGILL/SIGABRT, then chain to the previous handler");
   m.def("read_error", &a::read_error);
   m.def("clear_error", &a::clear_error);
 }

@@ -8,6 +8,7 @@ hand-written kernel and there is no silent PyTorch fallback.
 from __future__ import annotations
 
 import importlib
+import os
 from types import ModuleType
 
 import torch
@@ -33,6 +34,8 @@ def load() -> ModuleType:
             "avgen_b200._C (the sm_100a kernels) is not built or failed to load; "
             "run `python setup.py build_ext --inplace` in the repository root"
         ) from exc
+    if os.environ.get("AVGEN_NATIVE_BACKTRACE", "0") == "1":
+        _EXT.install_crash_backtrace()  # native frames on a host crash, then Python's fault handler
     return _EXT
 
 

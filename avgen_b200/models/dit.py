@@ -221,7 +221,9 @@ class VideoDiT(nn.Module):
 
     def _denoise(self, hidden: torch.Tensor, *, modulation: torch.Tensor, rope: RopeInputs | None,
                  key_mask: torch.Tensor | None, context: torch.Tensor | None,
-                 context_mask: torch.Tensor | None, modulation_index: torch.Tensor | None = None) -> torch.Tensor:
+                 context_mask: torch.Tensor | None, modulation_index: torch.Tensor | None = None,
+                 blocks: Any = None) -> torch.Tensor:
+        """The block stack (or ``blocks``, a subset of it: an interleaved pipeline's chunk)."""
         tp = getattr(self, "head_parallel", None)
         sequence = tp is not None and tp.sequence_parallel
         if sequence:  # the residual stream between blocks holds this rank's tokens only
@@ -232,7 +234,7 @@ class VideoDiT(nn.Module):
                 modulation_index = modulation_index[:, tp.token_slice(length)]
             elif modulation.ndim == 4:
                 modulation = modulation[:, tp.token_slice(length)]
-        for block in self.blocks:
+        for block in (self.blocks if blocks is None else blocks):
             hidden = block(hidden, modulation=modulation, rope=rope, key_mask=key_mask, context=context,
                            context_mask=context_mask, modulation_index=modulation_index)
         return tp.all_tokens(hidden) if sequence else hidden
@@ -281,7 +283,7 @@ class VideoDiT(nn.Module):
                      aux: dict[str, Any]) -> torch.Tensor:
         return self._denoise(hidden, modulation=modulation, rope=aux["rope"], key_mask=aux["key_mask"],
                              context=context, context_mask=aux["context_mask"],
-                             modulation_index=aux["modulation_index"])
+                             modulation_index=aux["modulation_index"], blocks=aux.get("blocks"))
 
     def stage_head(self, hidden: torch.Tensor, inputs: ModelInput) -> ModelOutput:
         predicted = self._video_head(hidden, inputs.video)

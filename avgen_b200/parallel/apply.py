@@ -97,16 +97,27 @@ def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, confi
         mesh = dims.build_mesh()
     runner = None
     if dims.pp_enabled and mesh is not None:
-        from avgen_b200.parallel.pipeline import PipelineRunner, balanced_split_points, split_model
+        from avgen_b200.parallel.pipeline import balanced_split_points, split_model, split_model_interleaved
 
+        if cfg.pipeline.schedule == "zero_bubble":
+            raise NotImplementedError("the zero-bubble schedule is not implemented; use 1f1b, gpipe or "
+                                      "interleaved_1f1b")
         pp = submesh(mesh, "pp")
         stage, stages = pp.get_local_rank(), pp.size()
         depth = len(getattr(model, cfg.block_attribute))
-        points = balanced_split_points(depth, stages, embedding_weight=cfg.pipeline.embedding_weight,
+        chunks = stages * cfg.pipeline.stages_per_rank
+        points = balanced_split_points(depth, chunks, embedding_weight=cfg.pipeline.embedding_weight,
                                        head_weight=cfg.pipeline.head_weight)
-        model = split_model(model, stage_index=stage, num_stages=stages, split_points=points,
-                            block_attribute=cfg.block_attribute)
-        applied.append(f"pipeline(pp={stages}, stage={stage}, {cfg.pipeline.schedule})")
+        if cfg.pipeline.is_interleaved:
+            model = split_model_interleaved(model, rank=stage, ranks=stages,
+                                            chunks_per_rank=cfg.pipeline.stages_per_rank, split_points=points,
+                                            block_attribute=cfg.block_attribute)
+        else:
+            model = split_model(model, stage_index=stage, num_stages=stages, split_points=points,
+                                block_attribute=cfg.block_attribute)
+        applied.append(f"pipeline(pp={stages}, stage={stage}, {cfg.pipeline.schedule}"
+                       + (f", chunks_per_rank={cfg.pipeline.stages_per_rank})" if cfg.pipeline.is_interleaved
+                          else ")"))
     n8 = convert_to_float8(model, cfg.precision)
     if n8:
         applied.append(f"float8({n8} linears)")
@@ -157,8 +168,13 @@ def parallelize(model: nn.Module, dims: ParallelDims, *, mesh: Any = None, confi
         apply_context_parallel(model, submesh(mesh, "cp"))
         applied.append(f"context_parallel(cp={dims.context})")
     if dims.pp_enabled and mesh is not None:
-        runner = PipelineRunner(model, submesh(mesh, "pp").get_group(),
-                                schedule="gpipe" if cfg.pipeline.schedule == "gpipe" else "1f1b")
+        from avgen_b200.parallel.pipeline import InterleavedPipelineRunner, PipelineRunner
+
+        group = submesh(mesh, "pp").get_group()
+        if cfg.pipeline.is_interleaved:
+            runner = InterleavedPipelineRunner(model, group, chunks_per_rank=cfg.pipeline.stages_per_rank)
+        else:
+            runner = PipelineRunner(model, group, schedule="gpipe" if cfg.pipeline.schedule == "gpipe" else "1f1b")
     if not applied:
         applied.append("single-device")
     return ParallelModel(model=model, dims=dims, mesh=mesh, applied=tuple(applied), pipeline=runner)

@@ -17,8 +17,9 @@ from typing import Any, Literal
 import torch
 from torch import nn
 
-__all__ = ["PipelineConfig", "PipelineRunner", "ScheduleName", "StageBlocks", "balanced_split_points",
-           "build_pipeline_schedule", "is_block_list", "split_model", "stage_for_rank"]
+__all__ = ["InterleavedPipelineRunner", "PipelineConfig", "PipelineRunner", "ScheduleName", "StageBlocks",
+           "balanced_split_points", "build_pipeline_schedule", "interleaved_order", "interleaved_timetable",
+           "is_block_list", "split_model", "split_model_interleaved", "stage_for_rank"]
 
 ScheduleName = Literal["gpipe", "1f1b", "interleaved_1f1b", "zero_bubble"]
 _NAMES = ("gpipe", "1f1b", "interleaved_1f1b", "zero_bubble")
@@ -356,3 +357,217 @@ class PipelineRunner:
             if upstream is not None:
                 self._exchange([(g, self._prev) for g in upstream], [])
         return losses
+
+
+# --------------------------------------------------------------------------- interleaved (virtual) stages
+def split_model_interleaved(model: nn.Module, *, rank: int, ranks: int, chunks_per_rank: int,
+                            split_points: Sequence[int], block_attribute: str = "blocks") -> nn.Module:
+    """Keep this rank's ``chunks_per_rank`` chunks of an interleaved pipeline.
+
+    The block list is cut into ``ranks * chunks_per_rank`` contiguous chunks; chunk
+    ``g`` lives on rank ``g % ranks`` (rank ``r`` owns chunks ``r, r + ranks, ...``),
+    so a micro-batch visits every rank ``chunks_per_rank`` times. The rank keeps its
+    blocks under their global names (one :class:`StageBlocks`) and records each
+    chunk's blocks in ``model.pipeline_chunks``; the input modules stay on the rank
+    of chunk 0 (rank 0) and the output head on the rank of the last chunk."""
+    chunks = ranks * chunks_per_rank
+    if not 0 <= rank < ranks:
+        raise ValueError(f"rank must be in [0, {ranks}); got {rank!r}")
+    blocks = getattr(model, block_attribute, None)
+    if not isinstance(blocks, nn.ModuleList):
+        raise AttributeError(f"{type(model).__name__} has no nn.ModuleList {block_attribute!r}")
+    if len(split_points) != chunks - 1:
+        raise ValueError(f"{chunks} chunks need {chunks - 1} split points; got {len(split_points)}")
+    bounds = [0, *split_points, len(blocks)]
+    owned = [g for g in range(chunks) if g % ranks == rank]
+    per_chunk = [StageBlocks({str(i): blocks[i] for i in range(bounds[g], bounds[g + 1])}) for g in owned]
+    setattr(model, block_attribute, StageBlocks({k: m for chunk in per_chunk for k, m in chunk.items()}))
+    model.pipeline_chunks = per_chunk  # plain attribute: the modules are registered once, above
+    if rank != 0:
+        for name in _INPUT_MODULES:
+            if hasattr(model, name):
+                setattr(model, name, None)
+    if rank != (chunks - 1) % ranks:
+        for name in _OUTPUT_MODULES:
+            if hasattr(model, name):
+                setattr(model, name, None)
+    return model
+
+
+def interleaved_order(rank: int, ranks: int, chunks_per_rank: int, microbatches: int) -> list[tuple[str, int, int]]:
+    """Rank ``rank``'s actions ``(kind, local chunk, micro-batch)`` in interleaved 1F1B
+    order: ``min(2 (ranks - rank - 1) + (chunks_per_rank - 1) ranks, total)`` warm-up
+    forwards, then alternating forward / backward, then the remaining backwards.
+    Forward ``k`` runs chunk ``(k // ranks) % v`` of micro-batch ``(k // (ranks v)) ranks + k % ranks``;
+    backwards visit the chunks in reverse (the schedule of Narayanan et al., 2021)."""
+    p, v, m = ranks, chunks_per_rank, microbatches
+    if m % p:
+        raise ValueError(f"the interleaved schedule needs the micro-batch count ({m}) to be a multiple of the "
+                         f"pipeline size ({p})")
+    total = m * v
+
+    def mb(k: int) -> int:
+        return (k // (p * v)) * p + k % p
+
+    fwd = [("F", (k // p) % v, mb(k)) for k in range(total)]
+    bwd = [("B", v - 1 - (k // p) % v, mb(k)) for k in range(total)]
+    warm = min(2 * (p - rank - 1) + (v - 1) * p, total)
+    order = fwd[:warm]
+    for f, b in zip(fwd[warm:], bwd):
+        order += [f, b]
+    return order + bwd[total - warm:]
+
+
+def interleaved_timetable(ranks: int, chunks_per_rank: int, microbatches: int) -> list[list[tuple[str, int, int] | None]]:
+    """Lock-step ticks: ``table[t][r]`` is rank ``r``'s action at tick ``t`` (or None when
+    it waits). Every rank derives the same table, so the point-to-point transfers of a
+    tick (a finished forward's carry to the next chunk's rank, a finished backward's
+    input gradients to the previous chunk's rank) are posted by both sides in the same
+    tick and matched by construction. A rank runs its next action as soon as its input
+    arrived in an earlier tick."""
+    p, v = ranks, chunks_per_rank
+    orders = [interleaved_order(r, p, v, microbatches) for r in range(p)]
+    last = p * v - 1
+    fwd_done: dict[tuple[int, int], int] = {}
+    bwd_done: dict[tuple[int, int], int] = {}
+    pos = [0] * p
+    table: list[list[tuple[str, int, int] | None]] = []
+    t = 0
+    while any(pos[r] < len(orders[r]) for r in range(p)):
+        row: list[tuple[str, int, int] | None] = [None] * p
+        for r in range(p):
+            if pos[r] >= len(orders[r]):
+                continue
+            kind, j, k = orders[r][pos[r]]
+            g = j * p + r
+            if kind == "F":
+                ready = g == 0 or fwd_done.get((g - 1, k), t) < t
+            else:
+                ready = fwd_done.get((g, k), t) < t and (g == last or bwd_done.get((g + 1, k), t) < t)
+            if ready:
+                row[r] = (kind, j, k)
+        if not any(row):
+            raise RuntimeError("interleaved schedule stalled: no rank can make progress")
+        for r, action in enumerate(row):
+            if action is not None:
+                kind, j, k = action
+                (fwd_done if kind == "F" else bwd_done)[(j * p + r, k)] = t
+                pos[r] += 1
+        table.append(row)
+        t += 1
+    return table
+
+
+class InterleavedPipelineRunner(PipelineRunner):
+    """Interleaved 1F1B over ``chunks_per_rank`` virtual stages per rank (a model cut by
+    :func:`split_model_interleaved`): the pipeline bubble shrinks by that factor at the
+    cost of ``chunks_per_rank`` times as many carries crossing between ranks. Each tick
+    of :func:`interleaved_timetable` runs at most one forward or backward chunk per
+    rank, then one grouped exchange with the neighbours (the carry to the next chunk's
+    rank, input gradients to the previous chunk's rank; chunk ``g``'s neighbours are
+    ranks ``g - 1`` and ``g + 1`` mod ``ranks``)."""
+
+    def __init__(self, model: nn.Module, group: Any, *, chunks_per_rank: int) -> None:
+        super().__init__(model, group, schedule="1f1b")
+        if self.stages < 2:
+            raise ValueError("an interleaved pipeline needs at least two ranks")
+        chunks = getattr(model, "pipeline_chunks", None)
+        if chunks is None or len(chunks) != chunks_per_rank:
+            raise ValueError(f"the model holds {0 if chunks is None else len(chunks)} pipeline chunks; expected "
+                             f"{chunks_per_rank} (cut it with split_model_interleaved)")
+        self.chunks_per_rank = chunks_per_rank
+        import torch.distributed as dist
+
+        self._ranks = dist.get_process_group_ranks(group)
+
+    def _peer(self, rank: int) -> int:
+        return self._ranks[rank % self.stages]
+
+    def run(self, micro_inputs: Sequence[Any], loss_fn: Callable[[int, Any], torch.Tensor]) -> list[torch.Tensor]:
+        m = len(micro_inputs)
+        if m == 0:
+            return []
+        p, v, r = self.stages, self.chunks_per_rank, self.stage
+        last = p * v - 1
+        like = next(self.model.parameters())
+        device = like.device
+        table = interleaved_timetable(p, v, m)
+        inputs: dict[tuple[int, int], list[torch.Tensor]] = {}   # received carries, by (global chunk, micro-batch)
+        grads_in: dict[tuple[int, int], list[torch.Tensor]] = {}  # received output gradients
+        starts: dict[tuple[int, int], Any] = {}
+        leaves: dict[tuple[int, int], Any] = {}
+        losses: dict[int, torch.Tensor] = {}
+
+        def spec(k: int) -> list[tuple[tuple[int, ...], torch.dtype]]:
+            return self._spec(micro_inputs[k], like)
+
+        for row in table:
+            sends: list[tuple[torch.Tensor, int]] = []
+            mine = row[r]
+            if mine is not None:
+                kind, j, k = mine
+                g = j * p + r
+                if kind == "F":
+                    start, leaf = self._chunk_forward(g, j, k, micro_inputs[k], inputs.pop((g, k), None), loss_fn,
+                                                      last)
+                    starts[(g, k)], leaves[(g, k)] = start, leaf
+                    if g == last:
+                        losses[k] = start.detach()
+                    else:
+                        sends += [(t.detach(), self._peer(r + 1)) for t in start.tensors()]
+                else:
+                    up = self._chunk_backward(starts.pop((g, k)), grads_in.pop((g, k), None), leaves.pop((g, k)),
+                                              g == last)
+                    if up is not None:
+                        sends += [(t, self._peer(r - 1)) for t in up]
+            recvs: list[tuple[torch.Tensor, int]] = []
+            prev_rank, next_rank = (r - 1) % p, (r + 1) % p
+            theirs = row[prev_rank]
+            if theirs is not None and theirs[0] == "F":  # the previous chunk's carry, for my next chunk
+                g = theirs[1] * p + prev_rank
+                if g != last:
+                    bufs = self._carry_like(spec(theirs[2]), device)
+                    inputs[(g + 1, theirs[2])] = bufs
+                    recvs += [(t, self._peer(prev_rank)) for t in bufs]
+            theirs = row[next_rank]
+            if theirs is not None and theirs[0] == "B":  # the next chunk's input gradients, for my chunk
+                g = theirs[1] * p + next_rank
+                if g != 0:
+                    bufs = self._carry_like(spec(theirs[2]), device)
+                    grads_in[(g - 1, theirs[2])] = bufs
+                    recvs += [(t, self._peer(next_rank)) for t in bufs]
+            self._exchange(sends, recvs)
+        return [losses[k] for k in sorted(losses)]
+
+    @staticmethod
+    def _chunk_backward(start: Any, grads: list[torch.Tensor] | None, leaves: list[torch.Tensor] | None,
+                        is_last: bool) -> list[torch.Tensor] | None:
+        """Backward of one chunk from its loss (last chunk) or its output gradients;
+        returns its input gradients (None for chunk 0)."""
+        if is_last:
+            start.backward()
+        else:
+            outs = start.tensors()
+            assert grads is not None and len(grads) == len(outs), "output gradients did not arrive"
+            torch.autograd.backward(outs, grads)
+        if leaves is None:
+            return None
+        return [t.grad if t.grad is not None else torch.zeros_like(t) for t in leaves]
+
+    def _chunk_forward(self, g: int, j: int, k: int, inputs: Any, received: list[torch.Tensor] | None,
+                       loss_fn: Callable[[int, Any], torch.Tensor], last: int) -> tuple[Any, Any]:
+        if g == 0:
+            carry = _Carry(*self.model.stage_embed(inputs))
+            leaves = None
+        else:
+            assert received is not None, f"chunk {g}: no carry arrived for micro-batch {k}"
+            leaves = [t.requires_grad_() for t in received]
+            it = iter(leaves)
+            hidden = next(it)
+            context = next(it) if self._has_context(inputs) else None
+            carry = _Carry(hidden, context, next(it))
+        aux = dict(self.model.stage_inputs(inputs), blocks=self.model.pipeline_chunks[j])
+        hidden = self.model.stage_blocks(carry.hidden, carry.context, carry.modulation, aux)
+        if g == last:
+            return loss_fn(k, self.model.stage_head(hidden, inputs)), leaves
+        return _Carry(hidden, carry.context, carry.modulation), leaves

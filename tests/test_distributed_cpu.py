@@ -200,6 +200,68 @@ def _pipeline_gpipe_worker(rank: int, world: int) -> None:
     _pipeline_worker(rank, world, schedule="gpipe")
 
 
+def _pipeline_interleaved_worker(rank: int, world: int) -> None:
+    """Interleaved 1F1B: a 4-block model cut into 4 chunks over 2 ranks (rank 0 owns
+    chunks 0 and 2, rank 1 chunks 1 and 3, so each micro-batch crosses between the
+    ranks three times), 4 micro-batches per step: two clipped optimizer steps equal
+    the unsharded model's with gradient accumulation."""
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.models import build_model, preset
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PipelineConfig, PrecisionConfig, parallelize
+    from avgen_b200.parallel.pipeline import InterleavedPipelineRunner
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                                  build_timestep_sampler, train_step)
+    from avgen_b200.train.trainer import pipeline_train_step
+
+    def deep():  # noqa: ANN202
+        torch.manual_seed(0)
+        cfg = {k: v for k, v in asdict(preset("tiny")).items() if k != "rope_scaling"}
+        cfg["depth"] = 4
+        m = build_model("video_dit", cfg)
+        m.init_weights()
+        with torch.no_grad():
+            for p in m.parameters():
+                p.add_(0.02 * torch.randn_like(p))
+        return m
+
+    ref = deep()
+    dims = ParallelDims(world_size=world, pipeline=world)
+    pm = parallelize(deep(), dims, mesh=dims.build_mesh("cpu"),
+                     config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32"),
+                                           pipeline=PipelineConfig(schedule="interleaved_1f1b", stages_per_rank=2)))
+    assert isinstance(pm.pipeline, InterleavedPipelineRunner), pm.applied
+    assert [list(c.keys()) for c in pm.model.pipeline_chunks] == ([["0"], ["2"]] if rank == 0 else [["1"], ["3"]])
+    assert (pm.model.patch_embed is not None) == (rank == 0) and (pm.model.final_proj is not None) == (rank == 1)
+    objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("uniform"), MultiTaskConditioning())
+    state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-2),
+                       rng=RNGStreams.for_rank(0, data_rank=0))
+    ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    c = ref.config
+    gen = torch.Generator().manual_seed(6)
+    for step in range(2):
+        micro = [random_batch(batch=1, channels=c.in_channels, frames=2, height=8, width=8, text_tokens=4,
+                              text_width=c.text_width, generator=gen) for _ in range(4)]
+        _, metrics = pipeline_train_step(state, micro, objective, pm.pipeline, patchifier=ref.patchifier,
+                                         max_grad_norm=0.05, pp_mesh=pm.pp_mesh)
+        losses = []
+        for i, b in enumerate(micro):
+            _, rm = train_step(ref_state, b, objective, patchifier=ref.patchifier, gradient_accumulation_steps=4,
+                               microbatch_index=i, max_grad_norm=0.05)
+            losses.append(float(rm.loss))
+        assert abs(float(metrics.loss) - sum(losses) / 4) <= 1e-5 * max(1.0, abs(sum(losses))), (step, metrics.loss)
+        assert abs(float(metrics.grad_norm) - float(rm.grad_norm)) <= 1e-4 * float(rm.grad_norm)
+        mine = dict(pm.model.named_parameters())
+        for name, q in ref.named_parameters():
+            if name in mine:
+                err = (mine[name].detach() - q.detach()).abs().max().item()
+                assert err <= 1e-6 + 1e-4 * q.detach().abs().max().item(), f"step {step}: {name}: {err}"
+    owned = {n for n, _ in pm.model.named_parameters()}
+    every = [None] * world
+    dist.all_gather_object(every, sorted(owned))
+    assert set().union(*map(set, every)) == {n for n, _ in ref.named_parameters()}
+
+
 def _lora_tp_worker(rank: int, world: int, use_dora: bool = False) -> None:
     """LoRA / DoRA on tensor-parallel DTensor weights: adapter placements follow the
     base weight's shard dimension (column-parallel Shard(0) -> A replicated, B
@@ -440,11 +502,11 @@ def _shards_worker(rank: int, world: int) -> None:
 
 
 @pytest.mark.parametrize("worker", [_fsdp_worker, _tp_worker, _cp_worker, _cp_replicated_worker, _nonfinite_worker,
-                                    _sharded_adamw_worker, _pipeline_worker, _pipeline_gpipe_worker, _lora_tp_worker,
-                                    _dora_tp_worker],
+                                    _sharded_adamw_worker, _pipeline_worker, _pipeline_gpipe_worker,
+                                    _pipeline_interleaved_worker, _lora_tp_worker, _dora_tp_worker],
                          ids=["fsdp", "tensor_parallel", "context_parallel", "context_parallel_replicated",
-                              "nonfinite_skip", "sharded_adamw", "pipeline_1f1b", "pipeline_gpipe", "lora_tensor_parallel",
-                              "dora_tensor_parallel"])
+                              "nonfinite_skip", "sharded_adamw", "pipeline_1f1b", "pipeline_gpipe",
+                              "pipeline_interleaved_1f1b", "lora_tensor_parallel", "dora_tensor_parallel"])
 def test_two_rank_parallelism(worker) -> None:  # noqa: ANN001
     _spawn(worker)
 

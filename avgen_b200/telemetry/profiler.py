@@ -104,8 +104,8 @@ def flight_recorder_dump(path: str | os.PathLike[str]) -> Path | None:
     except RuntimeError:
         return None
     p = Path(path)
-    p.parent.mkdir(parents=True, exist_ok=True)
-    target = p / f"flight_recorder_rank{_rank()}.pkl" if p.suffix == "" else p
+    target = p / f"flight_recorder_rank{_rank()}.pkl" if p.suffix == "" else p  # a directory, or a file name
+    target.parent.mkdir(parents=True, exist_ok=True)
     with open(target, "wb") as fh:
         fh.write(payload if isinstance(payload, bytes) else pickle.dumps(payload))
     return target
@@ -144,6 +144,8 @@ class DeviceTimer:
             self._open.append((name, start, end))
 
     def collect(self, *, max_over_ranks: bool = False) -> dict[str, float]:
+        if not self._open and not self.totals_ms:
+            return {}
         torch.cuda.synchronize()
         for name, s, e in self._open:
             self.totals_ms[name] += s.elapsed_time(e)

@@ -72,9 +72,19 @@ def _fused_eligible(block: DiTBlock, hidden: torch.Tensor) -> bool:
             return False
     from torch.distributed.tensor import DTensor
 
-    if any(isinstance(m.weight, DTensor) or hasattr(m, "adapted_weight") for m in linears
-           if isinstance(m, nn.Linear)):
-        return False  # DTensor shards and adapters run the per-layer path
+    for m in linears:
+        if not isinstance(m, nn.Linear):
+            continue
+        if isinstance(m.weight, DTensor):
+            return False  # DTensor shards run the per-layer path
+        if hasattr(m, "adapted_weight"):
+            # adapters join the fused block through their effective weight, which holds for
+            # LoRA / DoRA without adapter dropout (dropout acts on the adapter's input only)
+            adapter_params = [getattr(m, n, None) for n in ("lora_a", "lora_b", "lora_magnitude")]
+            if any(isinstance(t, DTensor) for t in adapter_params):
+                return False
+            if not getattr(m, "merged", False) and not isinstance(getattr(m, "lora_dropout", None), nn.Identity):
+                return False
     tp = getattr(block, "tp", None)
     if tp is not None and (not tp.sequence_parallel or block.attention_impl is not None):
         return False  # head-parallel shards fuse with sequence parallelism and local attention

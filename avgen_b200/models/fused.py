@@ -136,26 +136,68 @@ def _fsdp_managed(module: nn.Module) -> bool:
     return isinstance(module, FSDPModule)
 
 
-def packed_weights(block: nn.Module) -> dict[str, torch.Tensor]:
-    """bf16 kernel-layout weights of a DiT block, rebuilt only after parameter updates."""
-    att = block.attention
+def _adapted_layers(block: nn.Module) -> dict[str, nn.Module]:
+    """The block's adapter-wrapped linears (LoRA / DoRA), by module name."""
+    return {name: m for name, m in block.named_modules()
+            if isinstance(m, nn.Linear) and callable(getattr(m, "adapted_weight", None))}
+
+
+def fused_inputs(block: nn.Module, *, differentiable: bool = True) -> tuple[list[str], list[torch.Tensor]]:
+    """The tensors the fused node takes, by block parameter name: every parameter but the
+    modulation table, with an adapter-wrapped linear contributing its effective weight
+    (``W + s B A``, DoRA-scaled where it applies) under ``<layer>.weight`` instead of
+    its own parameters. The node returns a dense gradient for that effective weight and
+    autograd carries it into the adapter parameters through ``adapted_weight()`` (for
+    LoRA ``dB = s dW A^T``, ``dA = s B^T dW``): the block keeps its fused kernels while
+    only the adapters train."""
+    adapted = _adapted_layers(block)
+    names: list[str] = []
+    tensors: list[torch.Tensor] = []
+    for name, p in block.named_parameters():
+        if name == "scale_shift_table":
+            continue
+        owner, _, leaf = name.rpartition(".")
+        layer = adapted.get(owner)
+        if layer is None:
+            names.append(name)
+            tensors.append(p)
+        elif leaf == "weight":
+            names.append(name)
+            if differentiable:
+                tensors.append(layer.adapted_weight())
+            else:
+                with torch.no_grad():
+                    tensors.append(layer.adapted_weight())
+    return names, tensors
+
+
+def packed_weights(block: nn.Module, weights: dict[str, torch.Tensor] | None = None) -> dict[str, torch.Tensor]:
+    """bf16 kernel-layout weights of a DiT block, rebuilt only after parameter updates.
+    ``weights`` (block parameter name -> tensor) replaces the module's own tensors,
+    e.g. with adapters' effective weights."""
+
+    def w(name: str) -> torch.Tensor:
+        if weights is not None and name in weights:
+            return weights[name]
+        return block.get_parameter(name)
+
     ff = block.feed_forward
     out = {
-        "qkv": _packed(block, "qkv", [att.q_proj.weight, att.k_proj.weight, att.v_proj.weight],
-                       lambda q, k, v: torch.cat((q, k, v), 0)),
-        "o": _packed(block, "o", [att.out_proj.weight], lambda w: w),
-        "down": _packed(block, "down", [ff.down_proj.weight], lambda w: w),
+        "qkv": _packed(block, "qkv", [w("attention.q_proj.weight"), w("attention.k_proj.weight"),
+                                      w("attention.v_proj.weight")], lambda q, k, v: torch.cat((q, k, v), 0)),
+        "o": _packed(block, "o", [w("attention.out_proj.weight")], lambda t: t),
+        "down": _packed(block, "down", [w("feed_forward.down_proj.weight")], lambda t: t),
     }
     if hasattr(ff, "gate_proj"):
-        out["gu"] = _packed(block, "gu", [ff.gate_proj.weight, ff.up_proj.weight],
+        out["gu"] = _packed(block, "gu", [w("feed_forward.gate_proj.weight"), w("feed_forward.up_proj.weight")],
                             lambda g, u: torch.stack((g, u), 1).reshape(2 * g.shape[0], g.shape[1]))
     else:
-        out["up"] = _packed(block, "up", [ff.up_proj.weight], lambda w: w)
+        out["up"] = _packed(block, "up", [w("feed_forward.up_proj.weight")], lambda t: t)
     if block.cross_attention is not None:
-        ca = block.cross_attention
-        out["cq"] = _packed(block, "cq", [ca.q_proj.weight], lambda w: w)
-        out["ckv"] = _packed(block, "ckv", [ca.k_proj.weight, ca.v_proj.weight], lambda k, v: torch.cat((k, v), 0))
-        out["co"] = _packed(block, "co", [ca.out_proj.weight], lambda w: w)
+        out["cq"] = _packed(block, "cq", [w("cross_attention.q_proj.weight")], lambda t: t)
+        out["ckv"] = _packed(block, "ckv", [w("cross_attention.k_proj.weight"), w("cross_attention.v_proj.weight")],
+                             lambda k, v: torch.cat((k, v), 0))
+        out["co"] = _packed(block, "co", [w("cross_attention.out_proj.weight")], lambda t: t)
     return out
 
 
@@ -345,7 +387,7 @@ def _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
 
 
 def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask, o, lse, attn_state, dout,  # noqa: ANN001, ANN202
-                   saved=None):
+                   saved=None, names=None):
     from avgen_b200.ops import kernels as K
 
     b, length, w = spec.batch, spec.length, spec.width
@@ -354,7 +396,11 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     h, hk, d = spec.heads, spec.kv_heads, spec.head_dim
     eps = spec.eps
     dev = xb.device
-    pw = packed_weights(block)
+    if names is None:
+        names, tensors = fused_inputs(block, differentiable=False)
+    else:
+        tensors = fused_inputs(block, differentiable=False)[1]
+    pw = packed_weights(block, dict(zip(names, tensors)))
     att = block.attention
     ff = block.feed_forward
     # ---------------------------------------------------------------- recompute (unless kept in forward)
@@ -475,13 +521,8 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
                  "cross_attention.v_proj.weight", "cross_attention.out_proj.weight", "cross_attention.q_norm.weight",
                  "cross_attention.k_norm.weight"]
         pgrads.update(dict(zip(names, cross_grads)))
-    ordered = [pgrads.get(name) for name in block_param_names(block)]
+    ordered = [pgrads.get(name) for name in names]
     return dx, dmod, dctx, ordered
-
-
-def block_param_names(block: nn.Module) -> list[str]:
-    """Parameter names the fused function takes (excludes the modulation table)."""
-    return [n for n, _ in block.named_parameters() if n != "scale_shift_table"]
 
 
 # Bytes per token kept by the forward when it skips the backward's recompute, by
@@ -530,13 +571,13 @@ class FusedBlockFn(torch.autograd.Function):
     """Autograd node for a whole DiT block."""
 
     @staticmethod
-    def forward(ctx, spec, block, coords, freq, axis, kmask, cmask, x, mod, context, *params):  # noqa: ANN001, ANN205
+    def forward(ctx, spec, block, names, coords, freq, axis, kmask, cmask, x, mod, context, *params):  # noqa: ANN001, ANN205
         b, length, w = spec.batch, spec.length, spec.width
         m = b * length
         xb = x.reshape(m, w).to(_BF16).contiguous()
         modf = mod.detach().float().contiguous()
         ctxb = context.detach().to(_BF16).contiguous() if context is not None else None
-        pw = packed_weights(block)
+        pw = packed_weights(block, dict(zip(names, params)))
         mode = _keep_mode(spec, xb) if any(ctx.needs_input_grad) else "none"
         ctx.saved = None
         if mode == "none":
@@ -558,6 +599,7 @@ class FusedBlockFn(torch.autograd.Function):
                 _KEEP_BYTES[mode] = total * 1.05 / max(1, spec.batch * spec.length)  # bytes per token
         ctx.spec = spec
         ctx.block = block
+        ctx.names = names
         ctx.attn_state = attn_state
         ctx.flags = (coords is not None, kmask is not None, cmask is not None, ctxb is not None)
         empty = torch.empty(0)
@@ -576,11 +618,12 @@ class FusedBlockFn(torch.autograd.Function):
         dx, dmod, dctx, pgrads = _backward_impl(
             ctx.spec, ctx.block, xb, modf, ctxb if has_ctx else None, coords if has_coords else None,
             freq if has_coords else None, axis if has_coords else None, kmask if has_kmask else None,
-            cmask if has_cmask else None, o, lse, ctx.attn_state, dout, saved=ctx.saved)
+            cmask if has_cmask else None, o, lse, ctx.attn_state, dout, saved=ctx.saved, names=ctx.names)
         ctx.saved = None
         if dctx is not None and ctx.ctx_dtype is not None:
             dctx = dctx.to(ctx.ctx_dtype)
-        return (None, None, None, None, None, None, None, dx.view_as(dout).to(ctx.x_dtype), dmod, dctx, *pgrads)
+        return (None, None, None, None, None, None, None, None, dx.view_as(dout).to(ctx.x_dtype), dmod, dctx,
+                *pgrads)
 
 
 def fused_block_forward(block: nn.Module, hidden: torch.Tensor, combined_mod: torch.Tensor, *,
@@ -628,5 +671,6 @@ def fused_block_forward(block: nn.Module, hidden: torch.Tensor, combined_mod: to
         spec.tp, spec.full_length = tp, length * tp.world
         if context is not None:
             context = tp.shared(context)
-    params = [p for n, p in block.named_parameters() if n != "scale_shift_table"]
-    return FusedBlockFn.apply(spec, block, coords, freq, axis, kmask, cmask, hidden, combined_mod, context, *params)
+    names, params = fused_inputs(block)
+    return FusedBlockFn.apply(spec, block, names, coords, freq, axis, kmask, cmask, hidden, combined_mod, context,
+                              *params)

@@ -184,9 +184,12 @@ class HeadParallel:
 
 
 # --------------------------------------------------------------------------- sharding
-def _keep(linear: nn.Linear, dim: int, start: int, length: int, full: int, tp: HeadParallel) -> None:
-    """Replace ``linear``'s weight (and bias along dim 0) by this rank's slice, and make its
+def _keep(linear: nn.Linear, dim: int, sizes: list[int], tp: HeadParallel) -> None:
+    """Replace ``linear``'s weight (and bias along dim 0) by this rank's slice of ``sizes``
+    (every rank's extent along ``dim``, the same list on every rank), and make its
     state-dict entries full tensors again (gathered on save, sliced on load)."""
+    start, length = _span(sizes, tp.rank)
+    full = sum(sizes)
     with torch.no_grad():
         weight = linear.weight.narrow(dim, start, length).detach().clone()
         linear.weight = nn.Parameter(weight, requires_grad=linear.weight.requires_grad)
@@ -197,11 +200,7 @@ def _keep(linear: nn.Linear, dim: int, start: int, length: int, full: int, tp: H
         linear.out_features = length
     else:
         linear.in_features = length
-    sizes = [0] * tp.world
-    sizes[tp.rank] = length
-    sizes_t = torch.tensor(sizes)
-    dist.all_reduce(sizes_t, group=tp.group)
-    linear._avgen_tp_shard = (dim, [int(s) for s in sizes_t], full)  # type: ignore[attr-defined]
+    linear._avgen_tp_shard = (dim, list(sizes), full)  # type: ignore[attr-defined]
     # the parameters themselves carry their group: a global gradient norm sums their
     # squares over it (every rank holds a different slice), replicated ones count once
     linear.weight._avgen_tp_group = tp.group  # type: ignore[attr-defined]
@@ -249,13 +248,13 @@ def _shard_attention(att: nn.Module, tp: HeadParallel) -> None:
                              f"tp={tp.world}")
     else:
         kv_sizes = q_sizes
-    q0, qn = _span(q_sizes, tp.rank)
-    k0, kn = _span(kv_sizes, tp.rank)
-    _keep(att.q_proj, 0, q0 * hd, qn * hd, heads * hd, tp)
-    _keep(att.k_proj, 0, k0 * hd, kn * hd, kv * hd, tp)
-    _keep(att.v_proj, 0, k0 * hd, kn * hd, kv * hd, tp)
-    _keep(att.out_proj, 1, q0 * hd, qn * hd, heads * hd, tp)
-    att.num_heads, att.num_kv_heads = qn, kn
+    q_rows = [n * hd for n in q_sizes]
+    kv_rows = [n * hd for n in kv_sizes]
+    _keep(att.q_proj, 0, q_rows, tp)
+    _keep(att.k_proj, 0, kv_rows, tp)
+    _keep(att.v_proj, 0, kv_rows, tp)
+    _keep(att.out_proj, 1, q_rows, tp)
+    att.num_heads, att.num_kv_heads = q_sizes[tp.rank], kv_sizes[tp.rank]
     att.tp = tp
     # QK-norm weights are replicated but each rank applies them to its own heads only
     for norm in (getattr(att, "q_norm", None), getattr(att, "k_norm", None)):
@@ -268,12 +267,11 @@ def _shard_mlp(ff: nn.Module, tp: HeadParallel) -> None:
     up = ff.up_proj
     hidden = up.out_features
     sizes = head_partition(hidden, tp.world)
-    lo, n = _span(sizes, tp.rank)
     for name in ("gate_proj", "up_proj"):
         layer = getattr(ff, name, None)
         if layer is not None:
-            _keep(layer, 0, lo, n, hidden, tp)
-    _keep(ff.down_proj, 1, lo, n, hidden, tp)
+            _keep(layer, 0, sizes, tp)
+    _keep(ff.down_proj, 1, sizes, tp)
     ff.tp = tp
 
 

@@ -22,6 +22,11 @@ recompute the rest) built into the block.
 Self-attention can be swapped for a context-parallel implementation through
 ``BlockSpec.attention`` (see :mod:`avgen_b200.parallel.context`).
 
+Adapter-wrapped linears (LoRA / DoRA without adapter dropout) take part through
+their effective weights: the node sees ``W + s B A`` (DoRA-scaled where it
+applies) and returns its dense gradient, which autograd carries into the adapter
+parameters (``fused_inputs``).
+
 Head-parallel tensor parallelism with sequence parallelism
 (:mod:`avgen_b200.parallel.heads`) runs through the same node: the norms,
 modulation and gated residuals act on this rank's token chunk; each normalised

@@ -57,6 +57,10 @@ WORKLOADS = {
     "2b_16k_lora": {"width": 2560, "depth": 32, "heads": 20, "ffn_hidden": None, "frames": 4, "layout": "dp_cp",
                     "samples": None, "lora_rank": 64,
                     "label": "2B video DiT @16k tok, LoRA rank 64 on every attention/MLP linear, FSDP2 x cp"},
+    "2b_16k_grpo": {"width": 2560, "depth": 32, "heads": 20, "ffn_hidden": None, "frames": 4, "layout": "dp_cp",
+                    "samples": None, "lora_rank": 64, "grpo": True,
+                    "label": "GRPO on the 2B video DiT @16k tok: LoRA rank 64 under FSDP2 x cp=2, group 8, 20-step "
+                             "Euler rollouts with CFG 5.0 and sequence-length shift, MLP-scorer reward"},
 }
 
 
@@ -349,6 +353,122 @@ def run_ours(args: argparse.Namespace, rank: int, world: int, local: int) -> dic
     }
 
 
+def run_grpo(args: argparse.Namespace, rank: int, world: int, local: int) -> dict:
+    """One GRPO iteration per timed step through the public API (``GRPOTrainer``):
+    a group of 8 trajectories per data rank rolled out with 20-step Euler/SDE
+    sampling and CFG 5.0 (conditional and unconditional in one forward), the
+    MLP-scorer reward, group advantages, then the clipped-surrogate update of the
+    LoRA adapters over a 4-step MixGRPO window in minibatches of 2. Throughput is
+    trajectories per second over the whole job."""
+    sys.path.insert(0, HERE)
+    from avgen_b200.core.rng import RNGStreams
+    from avgen_b200.core.state import TrainState
+    from avgen_b200.finetune.lora import LoRAConfig, apply_lora, mark_only_lora_trainable
+    from avgen_b200.infer.schedule import ScheduleConfig, build_sigma_schedule
+    from avgen_b200.models import build_model
+    from avgen_b200.ops import kernels as K
+    from avgen_b200.parallel import ActivationCheckpointConfig, ParallelConfig, ParallelDims, parallelize
+    from avgen_b200.rl.grpo import GRPOConfig, GRPOTrainer, WindowSchedule
+    from avgen_b200.rl.rewards import build_reward
+    from avgen_b200.rl.rollout import model_velocity_fn
+    from avgen_b200.train import build_optimizer
+
+    dev = torch.device("cuda", local)
+    work = args.work
+    cp = 2 if world % 2 == 0 else 1
+    dp = world // cp
+    dims = ParallelDims(world_size=world, dp_shard=dp, context=cp)
+    torch.manual_seed(1234)
+    with torch.device("meta"):
+        model = build_model("video_dit", {"width": work["width"], "depth": args.depth, "num_heads": work["heads"],
+                                          "text_width": TEXT_WIDTH, "text_context_length": TEXT_TOKENS,
+                                          "in_channels": CHANNELS})
+    model = model.to_empty(device=dev)
+    model.init_weights()
+    lora = LoRAConfig(rank=work["lora_rank"], alpha=float(work["lora_rank"]),
+                      target_modules=("q_proj", "k_proj", "v_proj", "out_proj", "gate_proj", "up_proj", "down_proj"))
+
+    def adapt(m):  # noqa: ANN001, ANN202
+        apply_lora(m, lora)
+        mark_only_lora_trainable(m)
+        return m
+
+    pm = parallelize(model, dims, config=ParallelConfig(activation_checkpoint=ActivationCheckpointConfig(mode="none")),
+                     adapt=adapt)
+    data_rank = dims.data_coordinates(pm.mesh)[0] if pm.mesh is not None else 0
+    state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-5, dp_group=pm.data_group),
+                       rng=RNGStreams.for_rank(0, data_rank=data_rank))
+    gen = torch.Generator().manual_seed(77 + data_rank)
+    text = torch.randn(1, TEXT_TOKENS, TEXT_WIDTH, generator=gen).to(dev, torch.bfloat16)
+    frames = args.frames
+    positions = (torch.arange(frames, dtype=torch.float32) / 24.0).to(dev)[None]
+    grid_mask = torch.ones(1, frames, HEIGHT, WIDTH_PX, dtype=torch.bool, device=dev)
+    velocity = model_velocity_fn(pm.model, patchifier=pm.model.patchifier, positions=positions, mask=grid_mask,
+                                 text_features=text, text_mask=torch.ones(1, TEXT_TOKENS, dtype=torch.bool, device=dev),
+                                 guidance=5.0, cp_mesh=pm.cp_mesh)
+    tokens = frames * (HEIGHT // 2) * (WIDTH_PX // 2)
+    sigmas = build_sigma_schedule(ScheduleConfig(steps=20, dynamic_shift=True), sequence_length=tokens).sigmas.to(dev)
+    cfg = GRPOConfig(group_size=8, clip_range=2e-4, minibatch_size=2, max_grad_norm=1.0,
+                     window=WindowSchedule(window=4, stride=1, interval=25, total_steps=20))
+    trainer = GRPOTrainer(state, velocity, cfg, cp_mesh=pm.cp_mesh, data_group=pm.data_group)
+    reward = build_reward("mlp_scorer", channels=CHANNELS)
+    latent_shape = (CHANNELS, frames, HEIGHT, WIDTH_PX)
+
+    def iteration() -> float:
+        buffer = trainer.rollout(["synthetic prompt"], sigmas=sigmas, latent_shape=latent_shape, reward=reward,
+                                 device=dev, dtype=torch.bfloat16)
+        metrics = trainer.update(buffer)
+        return metrics[-1].loss
+
+    for _ in range(args.warmup):
+        iteration()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = ClockSampler()
+    if rank == 0:
+        clocks.start()
+    launches0 = K.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        loss = iteration()
+    ev1.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = K.launch_count() - launches0
+    clock_info = clocks.stop(list(range(world))) if rank == 0 else {}
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    from avgen_b200.ops._ext import check_errors
+
+    err = check_errors(local)
+    trajectories = dp * cfg.group_size  # per iteration, over the whole job
+    # end to end: the prompt embedding copied in from pinned host memory, the mean reward read back
+    host_text = text.cpu().pin_memory()
+    torch.cuda.synchronize()
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.e2e_steps):
+        text.copy_(host_text.to(dev, non_blocking=True))  # the step's prompt embedding, read by the velocity
+        buffer = trainer.rollout(["synthetic prompt"], sigmas=sigmas, latent_shape=latent_shape, reward=reward,
+                                 device=dev, dtype=torch.bfloat16)
+        trainer.update(buffer)
+        _ = float(buffer.rewards.mean().item())
+    torch.cuda.synchronize()
+    barrier()
+    e2e_s = max_over_ranks(time.perf_counter() - t0) / max(1, args.e2e_steps)
+    return {
+        "value": trajectories / (ms / 1000.0), "unit": "trajectories/s", "ms_per_step": ms, "mfu": None,
+        "loss": float(loss), "kernel_errors": err, "gpu_launches": launches,
+        "e2e": {"value": trajectories / e2e_s, "unit": "trajectories/s", "h2d_bytes_per_step": host_text.numel() * host_text.element_size(),
+                "d2h_bytes_per_step": 4, "s_per_step": e2e_s},
+        "exposed_comm": None, "clocks": clock_info, "tokens": tokens, "cp": cp, "dp": dp, "tp": 1, "micro": 1,
+        "global_batch": trajectories, "params": sum(p.numel() for p in pm.model.parameters()),
+        "applied": list(pm.applied), "peak_mem_gib": torch.cuda.max_memory_allocated(dev) / 2**30,
+        "grpo": {"group_size": cfg.group_size, "sampler_steps": 20, "guidance": 5.0, "window": 4,
+                 "minibatch_size": cfg.minibatch_size, "reward": "mlp_scorer"},
+    }
+
+
 def _profile_one_step(fn, rank: int) -> None:  # noqa: ANN001
     """Kernel-time shares of one step (torch.profiler CUDA activity); never a bench value."""
     from torch.profiler import ProfilerActivity, profile
@@ -559,6 +679,8 @@ def main() -> None:
         out = {"unavailable": f"the reference arm runs the headline workload only (asked for {args.config})"}
     elif args.impl == "reference":
         out = run_reference(args, rank, world, local)
+    elif args.work.get("grpo"):
+        out = run_grpo(args, rank, world, local)
     else:
         out = run_ours(args, rank, world, local)
     if rank == 0:
@@ -571,9 +693,11 @@ def main() -> None:
                       if args.config == "2b_64k" else f"samples/s + MFU, {work['label']}")
             hidden = f"MLP {work['ffn_hidden']}" if work["ffn_hidden"] else "SwiGLU mlp_ratio 4"
             parallelism = "single" if world == 1 else (f"tp{tp}+sp" if tp > 1 else f"dp{dp}xcp{cp}")
+            if work.get("grpo"):
+                metric = f"trajectories/s, {work['label']}"
             line = {
                 "metric": metric,
-                "value": out["value"], "unit": "samples/s", "n_gpus": world, "steps": args.steps,
+                "value": out["value"], "unit": out.get("unit", "samples/s"), "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": out["ms_per_step"], "higher_is_better": True,
                 "scaling": "weak" if work["layout"] == "dp_cp" else "strong", "vs_baseline": None, "dtype": "bf16",
                 "data": f"synthetic N(0,1) latents [1,16,{args.frames},128,128] and text [1,512,4096]; "
@@ -601,6 +725,8 @@ def main() -> None:
                 line["peak_mem_gib"] = round(out["peak_mem_gib"], 1)
                 if out["exposed_comm"] is not None:
                     line["exposed_comm"] = out["exposed_comm"]
+                if out.get("grpo"):
+                    line["config"]["grpo"] = out["grpo"]
             if args.depth != args.full_depth or args.frames != args.full_frames:
                 line["note"] = "reduced model/config: not a valid benchmark line"
             if args.config != "2b_64k":

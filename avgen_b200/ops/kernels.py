@@ -54,6 +54,24 @@ def launch_count() -> int:
     """Kernels launched through :mod:`avgen_b200.ops.kernels` so far in this process."""
     return LAUNCHES[0]
 
+
+# Deterministic weight gradients: the weight-gradient GEMM splits its reduction over
+# CTAs that add into the fp32 gradient with atomics, in whatever order they finish.
+# In deterministic mode (``AVGEN_DETERMINISTIC=1`` or ``set_deterministic(True)``)
+# it runs unsplit: each output element gets exactly one add per call, so repeated
+# runs agree bitwise. Attention's dQ accumulation and the norm reductions keep their
+# order-dependent sums.
+_DETERMINISTIC = [os.environ.get("AVGEN_DETERMINISTIC", "0") == "1"]
+
+
+def set_deterministic(on: bool = True) -> None:
+    _DETERMINISTIC[0] = bool(on)
+
+
+def deterministic() -> bool:
+    return _DETERMINISTIC[0]
+
+
 _BF16 = torch.bfloat16
 _F32 = torch.float32
 
@@ -125,6 +143,8 @@ def linear_dx(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype = _BF16,
 def linear_dw(dy: torch.Tensor, x: torch.Tensor, grad: torch.Tensor, *, k_splits: int = 0) -> torch.Tensor:
     """Accumulate the weight gradient ``grad[N, K] += dy[M, N]^T @ x[M, K]`` (fp32)."""
     n, k = grad.shape
+    if k_splits <= 0 and _DETERMINISTIC[0]:
+        k_splits = 1
     if k_splits <= 0:
         tiles = -(-n // 128) * -(-k // 256)
         sms = torch.cuda.get_device_properties(dy.device).multi_processor_count

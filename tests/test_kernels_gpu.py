@@ -648,3 +648,29 @@ def test_gemm_gated_operand_times_out_without_its_chunk() -> None:
     assert check_errors(clear=True) == 5
     _close(ops.gemm(x, w), x.float() @ w.float().t())
     _errors_clear()
+
+
+def test_deterministic_weight_gradient_is_bitwise_repeatable() -> None:
+    """The weight-gradient GEMM unsplit (deterministic mode) gives bitwise-identical
+    results on repeated runs and agrees with the split-K atomic form to fp32 rounding."""
+    from avgen_b200.ops import kernels as K
+
+    torch.manual_seed(4)
+    dy = torch.randn(8192, 512, device=DEV).bfloat16()
+    x = torch.randn(8192, 768, device=DEV).bfloat16()
+    try:
+        K.set_deterministic(True)
+        runs = []
+        for _ in range(3):
+            g = torch.zeros(512, 768, device=DEV)
+            K.linear_dw(dy, x, g)
+            runs.append(g)
+    finally:
+        K.set_deterministic(False)
+    assert torch.equal(runs[0], runs[1]) and torch.equal(runs[0], runs[2])
+    split = torch.zeros(512, 768, device=DEV)
+    K.linear_dw(dy, x, split, k_splits=8)
+    ref = dy.float().T @ x.float()
+    _close(runs[0], ref)
+    _close(split, ref)
+    _errors_clear()

@@ -149,8 +149,31 @@ __device__ __forceinline__ bool flag_wait_geq(const unsigned* flag, unsigned tar
 }
 
 // ---------------------------------------------------------------- TMA (local, no multicast)
+// Checked build (compile with -DAVGEN_KCHECK, `AVGEN_KCHECK=1 python setup.py build_ext --inplace`):
+// every tiled TMA copy first checks that its innermost coordinate is a multiple of 8
+// elements (16 bytes for the bf16 maps; every map of this package is addressed in
+// multiples of 8 along x). A misaligned copy is reported with the coordinate and
+// skipped instead of issued; the copy's waiter then runs out its bounded wait and
+// records a timeout in the error word, so the host sees the failure and the context
+// stays usable.
+#ifdef AVGEN_KCHECK
+#define AVGEN_TMA_X_CHECK(x)                                                                         \
+  do {                                                                                               \
+    if (((x) & 7) != 0) {                                                                            \
+      printf("avgen kcheck: TMA copy with misaligned x=%d skipped (block %d, thread %d, line %d)\n", \
+             (x), static_cast<int>(blockIdx.x), static_cast<int>(threadIdx.x), __LINE__);             \
+      return;                                                                                        \
+    }                                                                                                \
+  } while (0)
+#else
+#define AVGEN_TMA_X_CHECK(x) \
+  do {                       \
+  } while (0)
+#endif
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y) {
+  AVGEN_TMA_X_CHECK(x);
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
@@ -160,6 +183,7 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
 
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y, int z) {
+  AVGEN_TMA_X_CHECK(x);
   asm volatile(
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
@@ -169,6 +193,7 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int x,
                                             int y, int z, int w) {
+  AVGEN_TMA_X_CHECK(x);
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(dst)),
@@ -180,6 +205,7 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, u
 // box from the tensor map; elements outside the tensor are skipped). Bulk-group
 // completion: commit, then wait for the source reads before reusing the buffer.
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* src, int x, int y, int z) {
+  AVGEN_TMA_X_CHECK(x);
   asm volatile(
       "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
           reinterpret_cast<uint64_t>(map)),

@@ -30,6 +30,8 @@ NVCC_FLAGS = [
 ]
 if os.environ.get("AVGEN_PTXAS_VERBOSE"):
     NVCC_FLAGS.append("-Xptxas=-v")
+if os.environ.get("AVGEN_KCHECK") == "1":  # checked build: TMA coordinates verified before each copy
+    NVCC_FLAGS.append("-DAVGEN_KCHECK")
 
 
 def sources() -> list[str]:

@@ -39,3 +39,22 @@ def test_preflight_reports_missing_gpu() -> None:
 
     failures = run_checks(world_size=8)
     assert any("no CUDA device" in f for f in failures)
+
+
+def test_checked_build_flag_compiles_the_tma_checks() -> None:
+    """``AVGEN_KCHECK=1`` adds ``-DAVGEN_KCHECK`` to the nvcc flags, and the TMA helpers
+    carry the coordinate check only in that build."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    code = ("import runpy, sys; sys.argv = ['setup.py', '--name']; "
+            "g = runpy.run_path('setup.py', run_name='flags'); print('-DAVGEN_KCHECK' in g['NVCC_FLAGS'])")
+    for flag, want in (("1", "True"), ("0", "False")):
+        out = subprocess.run([sys.executable, "-c", code], cwd=root, env=dict(os.environ, AVGEN_KCHECK=flag),
+                             capture_output=True, text=True, timeout=300)
+        assert out.stdout.strip().splitlines()[-1] == want, out.stderr[-2000:]
+    header = (root / "avgen_b200" / "csrc" / "include" / "sm100.cuh").read_text()
+    assert "#ifdef AVGEN_KCHECK" in header and header.count("AVGEN_TMA_X_CHECK(x);") == 4

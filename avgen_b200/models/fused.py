@@ -123,6 +123,8 @@ def _packed(module: nn.Module, key: str, params: list[torch.Tensor], build) -> t
         fresh = lambda: build(*[p.detach() for p in params]).to(_BF16).contiguous()  # noqa: E731
         if _fsdp_managed(module):
             return fresh()  # FSDP re-gathers the parameters every forward: never serve a cached copy
+        if not all(isinstance(p, nn.Parameter) or getattr(p, "_avgen_stable", False) for p in params):
+            return fresh()  # a temporary's address and version can repeat after it is freed
         cache = module.__dict__.setdefault("_avgen_packed", {})
         version = (weight_epoch(), *((p._version, p.data_ptr()) for p in params))
         hit = cache.get(key)
@@ -147,14 +149,23 @@ def _adapted_layers(block: nn.Module) -> dict[str, nn.Module]:
             if isinstance(m, nn.Linear) and callable(getattr(m, "adapted_weight", None))}
 
 
+def _plain_lora(layer: nn.Module) -> bool:
+    """A LoRA adapter whose effective weight is exactly ``W + s B A`` (no DoRA scale,
+    not merged, no adapter dropout)."""
+    return (getattr(layer, "lora_magnitude", None) is None and not getattr(layer, "merged", False)
+            and isinstance(getattr(layer, "lora_dropout", None), nn.Identity)
+            and isinstance(getattr(layer, "lora_a", None), torch.Tensor))
+
+
 def fused_inputs(block: nn.Module, *, differentiable: bool = True) -> tuple[list[str], list[torch.Tensor]]:
     """The tensors the fused node takes, by block parameter name: every parameter but the
-    modulation table, with an adapter-wrapped linear contributing its effective weight
-    (``W + s B A``, DoRA-scaled where it applies) under ``<layer>.weight`` instead of
-    its own parameters. The node returns a dense gradient for that effective weight and
-    autograd carries it into the adapter parameters through ``adapted_weight()`` (for
-    LoRA ``dB = s dW A^T``, ``dA = s B^T dW``): the block keeps its fused kernels while
-    only the adapters train."""
+    modulation table. A plain LoRA layer contributes its base weight and ``lora_a`` /
+    ``lora_b`` themselves: the node packs ``W + s B A`` for its kernels and forms the
+    adapter gradients from low-rank products (``dB = s dY^T (X A^T)``,
+    ``dA = s (dY B)^T X``), never the dense weight gradient unless the base weight
+    trains. Any other adapter (DoRA, merged, with dropout) contributes its effective
+    weight under ``<layer>.weight``; the node returns that weight's dense gradient and
+    autograd carries it into the adapter through ``adapted_weight()``."""
     adapted = _adapted_layers(block)
     names: list[str] = []
     tensors: list[torch.Tensor] = []
@@ -163,7 +174,7 @@ def fused_inputs(block: nn.Module, *, differentiable: bool = True) -> tuple[list
             continue
         owner, _, leaf = name.rpartition(".")
         layer = adapted.get(owner)
-        if layer is None:
+        if layer is None or _plain_lora(layer):
             names.append(name)
             tensors.append(p)
         elif leaf == "weight":
@@ -174,6 +185,33 @@ def fused_inputs(block: nn.Module, *, differentiable: bool = True) -> tuple[list
                 with torch.no_grad():
                     tensors.append(layer.adapted_weight())
     return names, tensors
+
+
+def _packing_weights(block: nn.Module, weights: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    """``weights`` with each plain LoRA layer's base weight replaced by ``W + s B A``.
+    Outside FSDP the sum is kept on the layer until one of its three inputs changes, so
+    the packed-weight cache sees one stable tensor per adapter state."""
+    from avgen_b200.models.linear import weight_epoch
+
+    out = dict(weights)
+    cacheable = not _fsdp_managed(block)
+    for prefix, layer in _adapted_layers(block).items():
+        a, bmat = out.get(f"{prefix}.lora_a"), out.get(f"{prefix}.lora_b")
+        if a is None or bmat is None or not _plain_lora(layer):
+            continue
+        base = out[f"{prefix}.weight"]
+        key = (weight_epoch(), *((t._version, t.data_ptr()) for t in (base, a, bmat)))
+        hit = layer.__dict__.get("_avgen_effective")
+        if cacheable and hit is not None and hit[0] == key:
+            out[f"{prefix}.weight"] = hit[1]
+            continue
+        with torch.no_grad():
+            eff = base.detach() + (bmat.detach().float() @ a.detach().float()).mul_(layer.scaling).to(base.dtype)
+        if cacheable:
+            eff._avgen_stable = True
+            layer.__dict__["_avgen_effective"] = (key, eff)
+        out[f"{prefix}.weight"] = eff
+    return out
 
 
 def packed_weights(block: nn.Module, weights: dict[str, torch.Tensor] | None = None) -> dict[str, torch.Tensor]:
@@ -391,8 +429,56 @@ def _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     return x3, (o, lse, attn_state)
 
 
+def _weight_grads(block: nn.Module, members: list[tuple[str, Any]], dy: torch.Tensor, x: torch.Tensor,
+                  weights: dict[str, torch.Tensor], need: dict[str, bool], out: dict[str, torch.Tensor | None]) -> None:
+    """Gradients of the linears that share input ``x`` and whose output gradients are the
+    columns of ``dy``: ``members`` lists ``(layer prefix, columns)`` with ``columns`` a
+    ``slice`` of a concatenated output or ``"even"`` / ``"odd"`` for the interleaved
+    SwiGLU pair. A dense weight gradient is formed only for weights that train; plain
+    LoRA adapters get theirs from rank-r products; frozen weights get nothing."""
+    from avgen_b200.ops import kernels as K
+
+    dev = dy.device
+    rows = dy.shape[1]
+    dense = None
+    if any(need.get(f"{p}.weight", False) for p, _ in members):
+        dense = torch.zeros((rows, x.shape[1]), device=dev, dtype=torch.float32)
+        K.linear_dw(dy, x, dense)
+    layers = dict(block.named_modules())
+    for prefix, cols in members:
+        sel = cols if isinstance(cols, slice) else slice(0 if cols == "even" else 1, None, 2)
+        if dense is not None and need.get(f"{prefix}.weight", False):
+            out[f"{prefix}.weight"] = dense[sel].contiguous()
+        a_name, b_name = f"{prefix}.lora_a", f"{prefix}.lora_b"
+        if not (need.get(a_name, False) or need.get(b_name, False)):
+            continue
+        layer = layers[prefix]
+        a = weights[a_name].detach().to(_BF16).contiguous()        # [r, in]
+        bm = weights[b_name].detach().to(_BF16).contiguous()       # [out, r]
+        r = a.shape[0]
+        xa = K.gemm(x, a)                                          # [M, r] = X A^T
+        if isinstance(cols, slice):
+            dy_m = dy[:, sel]                                      # row-strided view of this layer's columns
+            g_b = torch.zeros((bm.shape[0], r), device=dev, dtype=torch.float32)
+            K.linear_dw(dy_m, xa, g_b)                             # dY^T (X A^T)
+            dyb = K.gemm(dy_m, bm, b_mn=True)                      # [M, r] = dY B
+        else:  # interleaved columns: route through a zero-padded B and keep every other row
+            full = torch.zeros((rows, r), device=dev, dtype=torch.float32)
+            K.linear_dw(dy, xa, full)
+            g_b = full[sel].contiguous()
+            padded = torch.zeros((rows, r), device=dev, dtype=_BF16)
+            padded[sel] = bm
+            dyb = K.gemm(dy, padded, b_mn=True)
+        g_a = torch.zeros((r, x.shape[1]), device=dev, dtype=torch.float32)
+        K.linear_dw(dyb, x, g_a)                                   # (dY B)^T X
+        if need.get(a_name, False):
+            out[a_name] = g_a.mul_(layer.scaling).to(weights[a_name].dtype)
+        if need.get(b_name, False):
+            out[b_name] = g_b.mul_(layer.scaling).to(weights[b_name].dtype)
+
+
 def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask, o, lse, attn_state, dout,  # noqa: ANN001, ANN202
-                   saved=None, names=None):
+                   saved=None, names=None, need=None):
     from avgen_b200.ops import kernels as K
 
     b, length, w = spec.batch, spec.length, spec.width
@@ -405,7 +491,11 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
         names, tensors = fused_inputs(block, differentiable=False)
     else:
         tensors = fused_inputs(block, differentiable=False)[1]
-    pw = packed_weights(block, dict(zip(names, tensors)))
+    weights = dict(zip(names, tensors))
+    if need is None:
+        need = {n: True for n in names}
+    pw = packed_weights(block, _packing_weights(block, weights))
+    pgrads: dict[str, torch.Tensor | None] = {}
     att = block.attention
     ff = block.feed_forward
     # ---------------------------------------------------------------- recompute (unless kept in forward)
@@ -428,35 +518,30 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     # ---------------------------------------------------------------- FFN
     df = _tp_gather(spec, K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], **spec.mod_rows()))
     dh = K.linear_dx(df, pw["down"])
-    g_down = zeros_like_param(ff.down_proj.weight)
-    K.linear_dw(df, keep["h"], g_down)
+    _weight_grads(block, [("feed_forward.down_proj", slice(None))], df, keep["h"], weights, need, pgrads)
     if spec.ffn == "swiglu":
         dgu = K.swiglu_bwd(dh, keep["gu"])
         dn3 = _tp_reduce(spec, K.linear_dx(dgu, pw["gu"]))
-        g_gu = torch.zeros((2 * spec.hidden, w), device=dev, dtype=torch.float32)
-        K.linear_dw(dgu, keep["n3g"], g_gu)
-        g_gate = g_gu[0::2].contiguous()
-        g_up = g_gu[1::2].contiguous()
+        _weight_grads(block, [("feed_forward.gate_proj", "even"), ("feed_forward.up_proj", "odd")], dgu,
+                      keep["n3g"], weights, need, pgrads)
     else:
         dpre = K.gelu_bwd(dh, keep["gu"])
         dn3 = _tp_reduce(spec, K.linear_dx(dpre, pw["up"]))
-        g_up = zeros_like_param(ff.up_proj.weight)
-        K.linear_dw(dpre, keep["n3g"], g_up)
-        g_gate = None
+        _weight_grads(block, [("feed_forward.up_proj", slice(None))], dpre, keep["n3g"], weights, need, pgrads)
     g_ffn_norm = zeros_like_param(block.ffn_norm.weight) if block.ffn_norm.weight is not None else None
     dx2 = K.rmsnorm_mod_bwd(keep["x2"], keep["rstd3"], dn3, _norm_weight(block.ffn_norm), modf[:, 4], modf[:, 3],
                             dres=dx3, dweight=g_ffn_norm, dscale=dmod[:, 4], dshift=dmod[:, 3],
                             **spec.mod_rows())
     # ---------------------------------------------------------------- cross attention
     dctx = None
-    cross_grads: list[torch.Tensor | None] = []
+    cross_grads: dict[str, torch.Tensor | None] = {}
     if spec.cross and ctxb is not None:
         ca = block.cross_attention
         t = ctxb.shape[1]
         dco = _tp_gather(spec, dx2)
         doc = K.linear_dx(dco, pw["co"])
-        g_co = zeros_like_param(ca.out_proj.weight)
-        K.linear_dw(dco, keep["oc"].view(mf, -1), g_co)
+        _weight_grads(block, [("cross_attention.out_proj", slice(None))], dco, keep["oc"].view(mf, -1), weights,
+                      need, pgrads)
         dqh, dkc, dvc = K.attention_bwd(keep["qh"], keep["kc"], keep["vc"], keep["oc"],
                                         doc.view(b, spec.seq, spec.ctx_heads, d), keep["lsec"], kmask=cmask,
                                         scale=1.0 / math.sqrt(d))
@@ -471,24 +556,23 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
                               head_dim=d, q_weight=None, k_weight=ckw, coords=None, freq=None, axis=None,
                               dk_weight=g_ckn, eps=eps)
         dn2 = _tp_reduce(spec, K.linear_dx(dqc, pw["cq"]))
-        g_cq = zeros_like_param(ca.q_proj.weight)
-        K.linear_dw(dqc, keep["n2g"], g_cq)
-        g_ckv = torch.zeros((pw["ckv"].shape[0], pw["ckv"].shape[1]), device=dev, dtype=torch.float32)
-        K.linear_dw(dkvc, ctxb.view(b * t, -1), g_ckv)
-        dctx = K.linear_dx(dkvc, pw["ckv"]).view(b, t, -1)
+        _weight_grads(block, [("cross_attention.q_proj", slice(None))], dqc, keep["n2g"], weights, need, pgrads)
         kv_rows = ca.k_proj.weight.shape[0]
+        _weight_grads(block, [("cross_attention.k_proj", slice(0, kv_rows)),
+                              ("cross_attention.v_proj", slice(kv_rows, None))], dkvc, ctxb.view(b * t, -1),
+                      weights, need, pgrads)
+        dctx = K.linear_dx(dkvc, pw["ckv"]).view(b, t, -1)
         g_cross_norm = zeros_like_param(block.cross_norm.weight) if block.cross_norm.weight is not None else None
         dx1 = K.rmsnorm_mod_bwd(keep["x1"], keep["rstd2"], dn2, _norm_weight(block.cross_norm), dres=dx2,
                                 dweight=g_cross_norm)
-        cross_grads = [g_cross_norm, g_cq, g_ckv[:kv_rows].contiguous(), g_ckv[kv_rows:].contiguous(), g_co,
-                       g_cqn, g_ckn]
+        cross_grads = {"cross_norm.weight": g_cross_norm, "cross_attention.q_norm.weight": g_cqn,
+                       "cross_attention.k_norm.weight": g_ckn}
     else:
         dx1 = dx2
     # ---------------------------------------------------------------- self attention
     da = _tp_gather(spec, K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], **spec.mod_rows()))
     do = K.linear_dx(da, pw["o"])
-    g_o = zeros_like_param(att.out_proj.weight)
-    K.linear_dw(da, o.view(mf, -1), g_o)
+    _weight_grads(block, [("attention.out_proj", slice(None))], da, o.view(mf, -1), weights, need, pgrads)
     impl = _attn_impl(spec)
     dq, dk, dv = impl.backward(inter["q"], inter["k"], inter["v"], o, do.view(b, spec.seq, h, d), lse, kmask,
                                1.0 / math.sqrt(d), attn_state)
@@ -500,33 +584,16 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
                           head_dim=d, q_weight=qw, k_weight=kw, coords=coords, freq=freq, axis=axis, dq_weight=g_qn,
                           dk_weight=g_kn, eps=eps)
     dn1 = _tp_reduce(spec, K.linear_dx(dqkv, pw["qkv"]))
-    g_qkv = torch.zeros((pw["qkv"].shape[0], w), device=dev, dtype=torch.float32)
-    K.linear_dw(dqkv, inter["n1g"], g_qkv)
+    qr, kr = h * d, hk * d
+    _weight_grads(block, [("attention.q_proj", slice(0, qr)), ("attention.k_proj", slice(qr, qr + kr)),
+                          ("attention.v_proj", slice(qr + kr, None))], dqkv, inter["n1g"], weights, need, pgrads)
     g_attn_norm = zeros_like_param(block.attention_norm.weight) if block.attention_norm.weight is not None else None
     dx = K.rmsnorm_mod_bwd(xb, inter["rstd1"], dn1, _norm_weight(block.attention_norm), modf[:, 1], modf[:, 0],
                            dres=dx1, dweight=g_attn_norm, dscale=dmod[:, 1], dshift=dmod[:, 0],
                            **spec.mod_rows())
-    qr, kr = h * d, hk * d
-    pgrads = {
-        "attention_norm.weight": g_attn_norm,
-        "attention.q_proj.weight": g_qkv[:qr].contiguous(),
-        "attention.k_proj.weight": g_qkv[qr:qr + kr].contiguous(),
-        "attention.v_proj.weight": g_qkv[qr + kr:].contiguous(),
-        "attention.out_proj.weight": g_o,
-        "attention.q_norm.weight": g_qn,
-        "attention.k_norm.weight": g_kn,
-        "ffn_norm.weight": g_ffn_norm,
-        "feed_forward.down_proj.weight": g_down,
-        "feed_forward.up_proj.weight": g_up,
-    }
-    if g_gate is not None:
-        pgrads["feed_forward.gate_proj.weight"] = g_gate
-    if cross_grads:
-        names = ["cross_norm.weight", "cross_attention.q_proj.weight", "cross_attention.k_proj.weight",
-                 "cross_attention.v_proj.weight", "cross_attention.out_proj.weight", "cross_attention.q_norm.weight",
-                 "cross_attention.k_norm.weight"]
-        pgrads.update(dict(zip(names, cross_grads)))
-    ordered = [pgrads.get(name) for name in names]
+    pgrads.update({"attention_norm.weight": g_attn_norm, "attention.q_norm.weight": g_qn,
+                   "attention.k_norm.weight": g_kn, "ffn_norm.weight": g_ffn_norm, **cross_grads})
+    ordered = [pgrads.get(name) if need.get(name, True) else None for name in names]
     return dx, dmod, dctx, ordered
 
 
@@ -582,7 +649,7 @@ class FusedBlockFn(torch.autograd.Function):
         xb = x.reshape(m, w).to(_BF16).contiguous()
         modf = mod.detach().float().contiguous()
         ctxb = context.detach().to(_BF16).contiguous() if context is not None else None
-        pw = packed_weights(block, dict(zip(names, params)))
+        pw = packed_weights(block, _packing_weights(block, dict(zip(names, params))))
         mode = _keep_mode(spec, xb) if any(ctx.needs_input_grad) else "none"
         ctx.saved = None
         if mode == "none":
@@ -623,7 +690,8 @@ class FusedBlockFn(torch.autograd.Function):
         dx, dmod, dctx, pgrads = _backward_impl(
             ctx.spec, ctx.block, xb, modf, ctxb if has_ctx else None, coords if has_coords else None,
             freq if has_coords else None, axis if has_coords else None, kmask if has_kmask else None,
-            cmask if has_cmask else None, o, lse, ctx.attn_state, dout, saved=ctx.saved, names=ctx.names)
+            cmask if has_cmask else None, o, lse, ctx.attn_state, dout, saved=ctx.saved, names=ctx.names,
+            need=dict(zip(ctx.names, ctx.needs_input_grad[11:])))
         ctx.saved = None
         if dctx is not None and ctx.ctx_dtype is not None:
             dctx = dctx.to(ctx.ctx_dtype)

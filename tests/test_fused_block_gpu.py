@@ -132,13 +132,15 @@ def test_generation_fused_guided_euler_matches_unfused(monkeypatch: pytest.Monke
     assert _rel(fused.latents, plain.latents) < 1e-3
 
 
-@pytest.mark.parametrize("dora", [False, True])
-def test_fused_block_with_adapters_matches_eager(dora: bool) -> None:
+@pytest.mark.parametrize("mode", ["lora", "dora", "lora+base"])
+def test_fused_block_with_adapters_matches_eager(mode: str) -> None:
     """LoRA / DoRA adapters on every attention and MLP linear: the block still runs
-    through the fused node (its effective weights in the kernels, dense weight
-    gradients carried into the adapters by autograd) and matches the CPU fp32 eager
-    block with the same adapters, forward and every adapter gradient; frozen base
-    weights get no gradient."""
+    through the fused node (effective weights in the kernels; LoRA gradients from
+    rank-r products, DoRA's through the dense effective-weight gradient) and matches
+    the CPU fp32 eager block with the same adapters, forward and every adapter
+    gradient. Frozen base weights get no gradient; trainable ones ("lora+base") get
+    their dense gradient beside the adapters'."""
+    dora = mode == "dora"
     import avgen_b200.models.fused as fused_mod
     from avgen_b200.finetune.lora import LoRAConfig, apply_lora, lora_modules, mark_only_lora_trainable
 
@@ -158,6 +160,10 @@ def test_fused_block_with_adapters_matches_eager(dora: bool) -> None:
             if m.lora_magnitude is not None:
                 m.lora_magnitude.mul_(1.0 + 0.1 * torch.randn_like(m.lora_magnitude))
     mark_only_lora_trainable(block)
+    if mode == "lora+base":
+        for name, p in block.named_parameters():
+            if name.endswith("proj.weight"):
+                p.requires_grad_(True)
     rope = RotaryEmbedding(128)
     x = torch.randn(b, length, width)
     mod = 0.1 * torch.randn(b, 6, width)
@@ -187,13 +193,13 @@ def test_fused_block_with_adapters_matches_eager(dora: bool) -> None:
     ref_params = dict(ref_block.named_parameters())
     checked = 0
     for name, p in gb.named_parameters():
-        if "lora_" in name:
+        if p.requires_grad:
             assert p.grad is not None, name
             assert _rel(p.grad, ref_params[name].grad) < 6e-2, name
             checked += 1
         else:
             assert p.grad is None, name  # frozen
-    assert checked >= 14
+    assert checked >= (14 if mode != "lora+base" else 21)
     from avgen_b200.ops._ext import check_errors
 
     assert check_errors() == 0

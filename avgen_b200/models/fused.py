@@ -47,7 +47,8 @@ from typing import Any, Protocol
 import torch
 from torch import nn
 
-__all__ = ["AttentionImpl", "BlockSpec", "LocalAttention", "fused_block_forward", "packed_weights"]
+__all__ = ["AttentionImpl", "BlockSpec", "LocalAttention", "close_tp_peer", "fused_block_forward", "packed_weights",
+           "tp_peer_guard_violations"]
 
 _BF16 = torch.bfloat16
 
@@ -290,6 +291,84 @@ def _tp_reduce(spec: BlockSpec, rows: torch.Tensor) -> torch.Tensor:
     return out
 
 
+
+# Peer-memory collective GEMMs of the tensor-parallel group, one per (kind, group, shape):
+# every rank creates them at the same call in the same order, so creation is collective.
+_TP_PEER: dict[tuple, Any] = {}
+
+
+def _tp_peer(spec: BlockSpec) -> bool:
+    """Whether this block's tensor-parallel collectives run fused with their GEMMs over
+    NVLink peer memory (single-sample rows, an NCCL group; ``AVGEN_TP_PEER=0`` keeps
+    the NCCL collectives between the kernels)."""
+    tp = spec.tp
+    if tp is None or spec.batch != 1 or os.environ.get("AVGEN_TP_PEER", "1") == "0":
+        return False
+    import torch.distributed as dist
+
+    return dist.get_backend(tp.group) == "nccl"
+
+
+def _tp_comm(kind: str, spec: BlockSpec, rows: int, cols: int, device: torch.device) -> Any:
+    from avgen_b200.parallel.collective_gemm import AllGatherGemm, GemmReduceScatter
+
+    key = (kind, id(spec.tp.group), rows, cols, device.index)
+    obj = _TP_PEER.get(key)
+    if obj is None:
+        obj = (AllGatherGemm(spec.tp.group, rows, cols, device, operand="a") if kind == "ag"
+               else GemmReduceScatter(spec.tp.group, rows, cols, device))
+        _TP_PEER[key] = obj
+    return obj
+
+
+def tp_peer_guard_violations() -> list[tuple[str, int]]:
+    """Changed canary bytes around the tensor-parallel peer buffers of this rank (empty
+    when no peer write ran past a buffer). Synchronises with the device."""
+    bad: list[tuple[str, int]] = []
+    for obj in _TP_PEER.values():
+        if obj.buf is not None:
+            bad += obj.buf.check_guards()
+    return bad
+
+
+def close_tp_peer() -> None:
+    """Free the tensor-parallel peer buffers. Collective over their groups: every rank
+    calls it at the same point (the buffers were created in the same order)."""
+    for obj in list(_TP_PEER.values()):
+        obj.close()
+    _TP_PEER.clear()
+
+
+def _tp_gather_gemm(spec: BlockSpec, rows: torch.Tensor, weight: torch.Tensor, *, keep: bool,
+                    **gemm_kwargs: Any) -> tuple[torch.Tensor, torch.Tensor]:
+    """``(gemm(all_gather(rows), weight), gathered rows)``. On the peer path the gather
+    runs on the copy engines while the GEMM computes, each tile of a peer's rows
+    waiting on that chunk's arrival flag; ``keep`` lands the gathered rows in a tensor
+    of their own (kept for the weight gradient), else they are a view of the
+    double-buffered symmetric buffer, valid until the call after next."""
+    from avgen_b200.ops import kernels as K
+
+    if not _tp_peer(spec):
+        full = _tp_gather(spec, rows)
+        return K.gemm(full, weight, **gemm_kwargs), full
+    rows = rows.contiguous()
+    ag = _tp_comm("ag", spec, rows.shape[0], rows.shape[1], rows.device)
+    out = torch.empty((ag.world * ag.rows, ag.cols), device=rows.device, dtype=_BF16) if keep else None
+    return ag(rows, weight, gathered_out=out, **gemm_kwargs)
+
+
+def _tp_gemm_reduce(spec: BlockSpec, x: torch.Tensor, weight: torch.Tensor, **gemm_kwargs: Any) -> torch.Tensor:
+    """``reduce_scatter(gemm(x, weight))`` over the token rows. On the peer path the
+    GEMM writes its partial product into symmetric memory and this rank sums its rows
+    straight out of every peer's buffer."""
+    from avgen_b200.ops import kernels as K
+
+    if not _tp_peer(spec):
+        return _tp_reduce(spec, K.gemm(x, weight, **gemm_kwargs))
+    n = weight.shape[1] if gemm_kwargs.get("b_mn") else weight.shape[0]
+    rs = _tp_comm("rs", spec, x.shape[0], n, x.device)
+    return rs(x, weight, **gemm_kwargs)
+
 def _gated_residual(spec: BlockSpec, resid: torch.Tensor, update: torch.Tensor,
                     gate: torch.Tensor | None) -> torch.Tensor:
     """``resid + gate * update`` on local rows (each row's gate picked as the kernels'
@@ -321,8 +400,7 @@ def _forward_impl(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cm
     att = block.attention
     n1, rstd1 = K.rmsnorm_mod(xb, _norm_weight(block.attention_norm), scale_a, shift_a, **spec.mod_rows(),
                               eps=block.attention_norm.eps or eps)
-    n1g = _tp_gather(spec, n1)
-    qkv = K.gemm(n1g, pw["qkv"])
+    qkv, n1g = _tp_gather_gemm(spec, n1, pw["qkv"], keep=not save or keep_inter)
     qw = _norm_weight(att.q_norm) if spec.qk_norm else None
     kw = _norm_weight(att.k_norm) if spec.qk_norm else None
     impl = _attn_impl(spec)
@@ -363,14 +441,13 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep, want_out=Fal
         x1 = K.gemm(o.view(m, -1), pw["o"], epilogue="gate_resid", resid=xb, gate=gate_a, **spec.mod_rows(),
                     aux=a_o)
     else:
-        a_o = _tp_reduce(spec, K.gemm(o.view(mf, -1), pw["o"]))
+        a_o = _tp_gemm_reduce(spec, o.view(mf, -1), pw["o"])
         x1 = _gated_residual(spec, xb, a_o, gate_a)
     x2 = x1
     if spec.cross and ctxb is not None:
         ca = block.cross_attention
         n2, rstd2 = K.rmsnorm_mod(x1, _norm_weight(block.cross_norm), eps=block.cross_norm.eps or eps)
-        n2g = _tp_gather(spec, n2)
-        qc = K.gemm(n2g, pw["cq"])
+        qc, n2g = _tp_gather_gemm(spec, n2, pw["cq"], keep=keep)
         t = ctxb.shape[1]
         kvc = K.gemm(ctxb.view(b * t, -1), pw["ckv"])
         cqw = _norm_weight(ca.q_norm) if spec.qk_norm else None
@@ -383,7 +460,7 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep, want_out=Fal
         if spec.tp is None:
             x2 = K.gemm(oc.view(m, -1), pw["co"], epilogue="gate_resid", resid=x1, gate=None)
         else:
-            x2 = _gated_residual(spec, x1, _tp_reduce(spec, K.gemm(oc.view(mf, -1), pw["co"])), None)
+            x2 = _gated_residual(spec, x1, _tp_gemm_reduce(spec, oc.view(mf, -1), pw["co"]), None)
         if keep:
             keep_d.update(x1=x1, n2=n2, n2g=n2g, rstd2=rstd2, qc=qc, kvc=kvc, qh=qh, kc=kc, vc=vc, oc=oc,
                           lsec=lsec)
@@ -391,17 +468,16 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep, want_out=Fal
         keep_d.update(x1=x1)
     n3, rstd3 = K.rmsnorm_mod(x2, _norm_weight(block.ffn_norm), scale_f, shift_f, **spec.mod_rows(),
                               eps=block.ffn_norm.eps or eps)
-    n3g = _tp_gather(spec, n3)
-    gu, hdn = _mlp_up(spec, pw, n3g, keep=keep and keep_mlp)
+    gu, hdn, n3g = _mlp_up(spec, pw, n3, keep=keep and keep_mlp, gather=True, keep_gathered=keep)
     if keep and not want_out:
-        f = _tp_reduce(spec, K.gemm(hdn, pw["down"]))
+        f = _tp_gemm_reduce(spec, hdn, pw["down"])
         keep_d.update(a_o=a_o, x2=x2, n3=n3, n3g=n3g, rstd3=rstd3, gu=gu, h=hdn, f=f)
         return None, keep_d
     if spec.tp is None:
         f = torch.empty((m, w), device=xb.device, dtype=_BF16) if keep else None
         x3 = K.gemm(hdn, pw["down"], epilogue="gate_resid", resid=x2, gate=gate_f, **spec.mod_rows(), aux=f)
     else:
-        f = _tp_reduce(spec, K.gemm(hdn, pw["down"]))
+        f = _tp_gemm_reduce(spec, hdn, pw["down"])
         x3 = _gated_residual(spec, x2, f, gate_f)
     if keep:
         keep_d.update(a_o=a_o, x2=x2, n3=n3, n3g=n3g, rstd3=rstd3, f=f)
@@ -410,16 +486,20 @@ def _block_tail(spec, block, pw, xb, modf, ctxb, cmask, o, *, keep, want_out=Fal
     return x3, keep_d
 
 
-def _mlp_up(spec, pw, n3, *, keep):  # noqa: ANN001, ANN202
-    """MLP up-projection with its activation epilogue: (pre-activation or None, h)."""
+def _mlp_up(spec, pw, n3, *, keep, gather=False, keep_gathered=False):  # noqa: ANN001, ANN202
+    """MLP up-projection with its activation epilogue: (pre-activation or None, h), and
+    the gathered input as a third value when ``gather`` (the tensor-parallel
+    all-gather of ``n3``'s token rows runs inside the GEMM)."""
     from avgen_b200.ops import kernels as K
 
-    m = n3.shape[0]
-    if spec.ffn == "swiglu":
-        gu = torch.empty((m, 2 * spec.hidden), device=n3.device, dtype=_BF16) if keep else None
-        return gu, K.gemm(n3, pw["gu"], epilogue="swiglu", aux=gu)
-    gu = torch.empty((m, spec.hidden), device=n3.device, dtype=_BF16) if keep else None
-    return gu, K.gemm(n3, pw["up"], epilogue="gelu", aux=gu)
+    m = n3.shape[0] * (spec.tp.world if gather and spec.tp is not None else 1)
+    swiglu = spec.ffn == "swiglu"
+    gu = torch.empty((m, 2 * spec.hidden if swiglu else spec.hidden), device=n3.device, dtype=_BF16) if keep else None
+    weight, epilogue = (pw["gu"], "swiglu") if swiglu else (pw["up"], "gelu")
+    if not gather:
+        return gu, K.gemm(n3, weight, epilogue=epilogue, aux=gu)
+    hdn, n3g = _tp_gather_gemm(spec, n3, weight, keep=keep_gathered, epilogue=epilogue, aux=gu)
+    return gu, hdn, n3g
 
 
 def _forward_full(spec, block, pw, xb, modf, ctxb, coords, freq, axis, kmask, cmask):  # noqa: ANN001, ANN202
@@ -516,17 +596,17 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
         return torch.zeros(p.shape, device=dev, dtype=torch.float32)
 
     # ---------------------------------------------------------------- FFN
-    df = _tp_gather(spec, K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], **spec.mod_rows()))
-    dh = K.linear_dx(df, pw["down"])
+    dh, df = _tp_gather_gemm(spec, K.gate_bwd(dx3, keep["f"], gate_f, dmod[:, 5], **spec.mod_rows()), pw["down"],
+                             keep=False, b_mn=True)
     _weight_grads(block, [("feed_forward.down_proj", slice(None))], df, keep["h"], weights, need, pgrads)
     if spec.ffn == "swiglu":
         dgu = K.swiglu_bwd(dh, keep["gu"])
-        dn3 = _tp_reduce(spec, K.linear_dx(dgu, pw["gu"]))
+        dn3 = _tp_gemm_reduce(spec, dgu, pw["gu"], b_mn=True)
         _weight_grads(block, [("feed_forward.gate_proj", "even"), ("feed_forward.up_proj", "odd")], dgu,
                       keep["n3g"], weights, need, pgrads)
     else:
         dpre = K.gelu_bwd(dh, keep["gu"])
-        dn3 = _tp_reduce(spec, K.linear_dx(dpre, pw["up"]))
+        dn3 = _tp_gemm_reduce(spec, dpre, pw["up"], b_mn=True)
         _weight_grads(block, [("feed_forward.up_proj", slice(None))], dpre, keep["n3g"], weights, need, pgrads)
     g_ffn_norm = zeros_like_param(block.ffn_norm.weight) if block.ffn_norm.weight is not None else None
     dx2 = K.rmsnorm_mod_bwd(keep["x2"], keep["rstd3"], dn3, _norm_weight(block.ffn_norm), modf[:, 4], modf[:, 3],
@@ -538,8 +618,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     if spec.cross and ctxb is not None:
         ca = block.cross_attention
         t = ctxb.shape[1]
-        dco = _tp_gather(spec, dx2)
-        doc = K.linear_dx(dco, pw["co"])
+        doc, dco = _tp_gather_gemm(spec, dx2, pw["co"], keep=False, b_mn=True)
         _weight_grads(block, [("cross_attention.out_proj", slice(None))], dco, keep["oc"].view(mf, -1), weights,
                       need, pgrads)
         dqh, dkc, dvc = K.attention_bwd(keep["qh"], keep["kc"], keep["vc"], keep["oc"],
@@ -555,7 +634,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
         dkvc = K.qkv_rope_bwd(keep["kvc"], None, dkc, dvc, batch=b, length=t, heads=0, kv_heads=spec.ctx_kv_heads,
                               head_dim=d, q_weight=None, k_weight=ckw, coords=None, freq=None, axis=None,
                               dk_weight=g_ckn, eps=eps)
-        dn2 = _tp_reduce(spec, K.linear_dx(dqc, pw["cq"]))
+        dn2 = _tp_gemm_reduce(spec, dqc, pw["cq"], b_mn=True)
         _weight_grads(block, [("cross_attention.q_proj", slice(None))], dqc, keep["n2g"], weights, need, pgrads)
         kv_rows = ca.k_proj.weight.shape[0]
         _weight_grads(block, [("cross_attention.k_proj", slice(0, kv_rows)),
@@ -570,8 +649,8 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     else:
         dx1 = dx2
     # ---------------------------------------------------------------- self attention
-    da = _tp_gather(spec, K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], **spec.mod_rows()))
-    do = K.linear_dx(da, pw["o"])
+    do, da = _tp_gather_gemm(spec, K.gate_bwd(dx1, keep["a_o"], gate_a, dmod[:, 2], **spec.mod_rows()), pw["o"],
+                             keep=False, b_mn=True)
     _weight_grads(block, [("attention.out_proj", slice(None))], da, o.view(mf, -1), weights, need, pgrads)
     impl = _attn_impl(spec)
     dq, dk, dv = impl.backward(inter["q"], inter["k"], inter["v"], o, do.view(b, spec.seq, h, d), lse, kmask,
@@ -583,7 +662,7 @@ def _backward_impl(spec, block, xb, modf, ctxb, coords, freq, axis, kmask, cmask
     dqkv = K.qkv_rope_bwd(inter["qkv"], dq.to(_BF16), dk, dv, batch=b, length=spec.seq, heads=h, kv_heads=hk,
                           head_dim=d, q_weight=qw, k_weight=kw, coords=coords, freq=freq, axis=axis, dq_weight=g_qn,
                           dk_weight=g_kn, eps=eps)
-    dn1 = _tp_reduce(spec, K.linear_dx(dqkv, pw["qkv"]))
+    dn1 = _tp_gemm_reduce(spec, dqkv, pw["qkv"], b_mn=True)
     qr, kr = h * d, hk * d
     _weight_grads(block, [("attention.q_proj", slice(0, qr)), ("attention.k_proj", slice(qr, qr + kr)),
                           ("attention.v_proj", slice(qr + kr, None))], dqkv, inter["n1g"], weights, need, pgrads)

@@ -87,19 +87,29 @@ class AllGatherGemm:
             return None
         return self._full(self.rank, self.calls % 2)[self.rank * self.rows:(self.rank + 1) * self.rows]
 
-    def gather(self, shard: torch.Tensor) -> tuple[torch.Tensor, int]:
-        """Start the gather of ``shard``; returns the (filling) full buffer and the epoch
-        its arrival flags reach. Pulls run on the copy stream, nearest-next rank first."""
+    def gather(self, shard: torch.Tensor, out: torch.Tensor | None = None) -> tuple[torch.Tensor, int]:
+        """Start the gather of ``shard``; returns the (filling) full matrix and the epoch
+        its arrival flags reach. Pulls run on the copy stream, nearest-next rank first.
+        The rows land in the symmetric buffer, or in ``out`` (a contiguous local
+        ``[world * rows, cols]`` bf16 tensor the caller keeps) when given; peers read
+        this rank's rows from the symmetric buffer either way."""
         from avgen_b200.ops._ext import load
 
         if tuple(shard.shape) != (self.rows, self.cols):
             raise ValueError(f"shard must be [{self.rows}, {self.cols}]; got {list(shard.shape)}")
+        if out is not None and (tuple(out.shape) != (self.world * self.rows, self.cols) or not out.is_contiguous()
+                                or out.dtype != torch.bfloat16 or out.device != self.device):
+            raise ValueError(f"out must be a contiguous bf16 [{self.world * self.rows}, {self.cols}] tensor on "
+                             f"{self.device}")
         parity = self.calls % 2
         self.calls += 1
-        full = self._full(self.rank, parity)
-        own = full[self.rank * self.rows:(self.rank + 1) * self.rows]
+        sym = self._full(self.rank, parity)
+        own = sym[self.rank * self.rows:(self.rank + 1) * self.rows]
         if own.data_ptr() != shard.data_ptr():
             own.copy_(shard)
+        full = sym if out is None else out
+        if out is not None:
+            out[self.rank * self.rows:(self.rank + 1) * self.rows].copy_(shard)
         self.epoch = (self.epoch + 1) & 0x7FFFFFFF or 1
         main = torch.cuda.current_stream(self.device)
         dist.all_reduce(self._token, group=self.group)  # every rank's shard is written
@@ -115,16 +125,21 @@ class AllGatherGemm:
                 ext.stream_write(flag0 + 4 * r, self.epoch)
         return full, self.epoch
 
-    def __call__(self, shard: torch.Tensor, other: torch.Tensor, **gemm_kwargs: Any) -> tuple[torch.Tensor, torch.Tensor]:
-        """Returns ``(y, gathered)``. ``gathered`` stays valid until the call after next."""
+    def __call__(self, shard: torch.Tensor, other: torch.Tensor, *, gathered_out: torch.Tensor | None = None,
+                 **gemm_kwargs: Any) -> tuple[torch.Tensor, torch.Tensor]:
+        """Returns ``(y, gathered)``. ``gathered`` is ``gathered_out`` when given, else a
+        view of the symmetric buffer that stays valid until the call after next."""
         if not _on_cuda(self.device):
             full = torch.empty(self.world * self.rows, self.cols, dtype=shard.dtype)
             dist.all_gather_into_tensor(full, shard.contiguous(), group=self.group)
             y = F.linear(other, full) if self.operand == "b" else F.linear(full, other)
+            if gathered_out is not None:
+                gathered_out.copy_(full)
+                full = gathered_out
             return y, full
         from avgen_b200.ops import kernels as K
 
-        full, epoch = self.gather(shard)
+        full, epoch = self.gather(shard, gathered_out)
         a, b = (other, full) if self.operand == "b" else (full, other)
         y = K.gemm(a, b, gate_flags=self.flags, gate_epoch=epoch, gate_operand=self.operand, gate_chunk=self.rows,
                    gate_rank=self.rank, **gemm_kwargs)

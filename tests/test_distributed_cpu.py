@@ -609,6 +609,10 @@ def _collective_gemm_worker(rank: int, world: int) -> None:
     sp = AllGatherGemm(dist.group.WORLD, rows, cols, "cpu", operand="a")
     y, _ = sp(w_all[rank * rows:(rank + 1) * rows], w)
     torch.testing.assert_close(y, w_all @ w.t())
+    kept = torch.empty(world * rows, cols)
+    y, gathered = sp(w_all[rank * rows:(rank + 1) * rows], w, gathered_out=kept)  # rows land in the caller's tensor
+    assert gathered is kept
+    torch.testing.assert_close(kept, w_all)
     # row-parallel: rank r holds columns [r*c, (r+1)*c) of the reduction axis
     xs = torch.randn(world * rows, world * cols, generator=g)
     ws = torch.randn(n, world * cols, generator=g)

@@ -3,7 +3,10 @@ sm_100a block, on 2 and 4 GPUs: the sharded model (uneven head split: 3 heads
 over 2 ranks is [2, 1]) runs every block through the fused path and its output
 and every gradient (this rank's slice of the sharded weights, the full tensor
 of the replicated ones) match the unsharded model's fused run on the same
-weights and inputs, within bf16 rounding."""
+weights and inputs, within bf16 rounding. Both collective paths run: the
+all-gather and reduce-scatter fused with their GEMMs over NVLink peer memory
+(default; canary guards around every peer buffer stay intact) and NCCL
+collectives between the kernels (``AVGEN_TP_PEER=0``)."""
 from __future__ import annotations
 
 import os
@@ -60,12 +63,12 @@ def _close(got: torch.Tensor, want: torch.Tensor, what: str, rel: float) -> None
     assert err <= 1e-6 + rel * scale, f"{what}: max err {err} vs max {scale}"
 
 
-def _worker(rank: int, world: int, port: int, heads: int) -> None:
+def _worker(rank: int, world: int, port: int, heads: int, peer: bool) -> None:
     from datetime import timedelta
 
     import torch.distributed as dist
 
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), AVGEN_TP_PEER="1" if peer else "0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
@@ -110,16 +113,20 @@ def _worker(rank: int, world: int, port: int, heads: int) -> None:
             assert p.grad is not None, name
             _close(p.grad, g, f"grad {name}", 3e-2)
         assert check_errors(dev) == 0
+        assert bool(fused_mod._TP_PEER) == peer, "the peer path must run exactly when it is on"
+        assert fused_mod.tp_peer_guard_violations() == []
+        fused_mod.close_tp_peer()
         fused_mod.fused_block_forward = original
     finally:
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("peer", [True, False])
 @pytest.mark.parametrize("world,heads", [(2, 3), (4, 4)])
-def test_fused_head_parallel_matches_unsharded(world: int, heads: int) -> None:
+def test_fused_head_parallel_matches_unsharded(world: int, heads: int, peer: bool) -> None:
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
 
-    mp.spawn(_worker, args=(world, _free_port(), heads), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), heads, peer), nprocs=world, join=True)

@@ -267,10 +267,10 @@ def _tp_gather(spec: BlockSpec, rows: torch.Tensor) -> torch.Tensor:
     import torch.distributed as dist
 
     rows = rows.contiguous()
-    out = torch.empty((tp.world, *rows.shape), dtype=rows.dtype, device=rows.device)
+    out = torch.empty((tp.world * rows.shape[0], rows.shape[-1]), dtype=rows.dtype, device=rows.device)
     dist.all_gather_into_tensor(out, rows, group=tp.group)
     if spec.batch == 1:
-        return out.view(-1, rows.shape[-1])
+        return out
     c = rows.shape[-1]
     return out.view(tp.world, spec.batch, spec.length, c).transpose(0, 1).reshape(spec.batch * spec.seq, c)
 
@@ -289,7 +289,6 @@ def _tp_reduce(spec: BlockSpec, rows: torch.Tensor) -> torch.Tensor:
     out = torch.empty((spec.batch * spec.length, c), dtype=rows.dtype, device=rows.device)
     dist.reduce_scatter_tensor(out, src, group=tp.group)
     return out
-
 
 
 # Peer-memory collective GEMMs of the tensor-parallel group, one per (kind, group, shape):

@@ -10,6 +10,7 @@ import socket
 
 import pytest
 import torch
+from multigpu_util import leave_on_failure
 
 pytestmark = pytest.mark.gpu
 
@@ -107,9 +108,10 @@ def _worker(rank: int, world: int, port: int) -> None:
         ag.close()
         sp.close()
         rs.close()
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world", [2])
@@ -173,9 +175,10 @@ def _sp_worker(rank: int, world: int, port: int) -> None:
         for prim in _POOL.values():
             assert not prim.buf.check_guards()
             prim.close()
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 def test_sequence_parallel_mlp_multi_gpu() -> None:

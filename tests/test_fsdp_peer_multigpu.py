@@ -12,6 +12,7 @@ from dataclasses import asdict
 
 import pytest
 import torch
+from multigpu_util import leave_on_failure
 
 pytestmark = pytest.mark.gpu
 
@@ -108,9 +109,10 @@ def _worker(rank: int, world: int, port: int) -> None:
             err = (p_peer[name] - p_nccl[name]).abs().max().item()
             assert err <= 2.5e-3, f"param {name}: {err}"
             torch.testing.assert_close(m_peer[name], m_nccl[name], rtol=1e-3, atol=1e-6, msg=name)
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world", [2, 4])

@@ -10,6 +10,7 @@ from dataclasses import asdict
 
 import pytest
 import torch
+from multigpu_util import leave_on_failure
 
 pytestmark = pytest.mark.gpu
 
@@ -83,9 +84,10 @@ def _worker(rank: int, world: int, port: int, schedule: str, chunks: int) -> Non
                 err = (mine[name].detach() - q.detach()).abs().max().item()
                 assert err <= 2.5e-3, f"{name}: {err}"  # AdamW moves each parameter by about lr
         assert check_errors(dev) == 0
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("schedule,chunks", [("1f1b", 1), ("interleaved_1f1b", 2)])

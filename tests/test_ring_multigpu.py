@@ -11,6 +11,7 @@ import socket
 
 import pytest
 import torch
+from multigpu_util import leave_on_failure
 
 pytestmark = pytest.mark.gpu
 
@@ -90,9 +91,10 @@ def _worker(rank: int, world: int, port: int, masked: bool) -> None:
         close(dq, qf.grad)
         close(dk, gk[:, :, lo:hi])
         close(dv, gv[:, :, lo:hi])
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world,masked", [(2, False), (2, True), (4, True)])

@@ -10,6 +10,7 @@ import socket
 
 import pytest
 import torch
+from multigpu_util import leave_on_failure
 
 pytestmark = pytest.mark.gpu
 
@@ -57,9 +58,10 @@ def _worker(rank: int, world: int, port: int) -> None:
         st_ref, st_sh = o_ref.state, o_sh.state
         for p_ref, p_sh in zip(ref.parameters(), sharded.parameters()):
             torch.testing.assert_close(st_ref[p_ref]["exp_avg"], st_sh[p_sh]["exp_avg"], rtol=1e-5, atol=1e-8)
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 def test_sharded_adamw_two_gpus() -> None:

@@ -15,6 +15,7 @@ from dataclasses import asdict
 
 import pytest
 import torch
+from multigpu_util import leave_on_failure
 
 pytestmark = pytest.mark.gpu
 
@@ -117,9 +118,10 @@ def _worker(rank: int, world: int, port: int, heads: int, peer: bool) -> None:
         assert fused_mod.tp_peer_guard_violations() == []
         fused_mod.close_tp_peer()
         fused_mod.fused_block_forward = original
-    finally:
-        dist.barrier(device_ids=[rank])
-        dist.destroy_process_group()
+    except BaseException:
+        leave_on_failure()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("peer", [True, False])

@@ -26,6 +26,7 @@ from typing import Any
 
 import torch
 
+from avgen_b200.core.limits import Limit, enforce
 from avgen_b200.rl.rollout import RolloutBatch, RolloutBuffer, VelocityFn, generate_group
 from avgen_b200.rl.sde import to_sde
 
@@ -63,27 +64,24 @@ class WindowSchedule:
     decay: float = 0.8
 
     def __post_init__(self) -> None:
-        for name in ("window", "stride", "interval", "total_steps"):
-            v = getattr(self, name)
-            if isinstance(v, bool) or v < 1:
-                raise ValueError(f"{name} must be a positive integer; got {v!r}")
-        if self.window > self.total_steps:
-            raise ValueError(f"window={self.window} exceeds total_steps={self.total_steps}")
-        if not 0.0 < self.decay <= 1.0:
-            raise ValueError(f"decay must be in (0, 1]; got {self.decay!r}")
+        enforce(self, _WINDOW_LIMITS)
+        enforce(self, {"window": Limit(lo=1, hi=self.total_steps, integer=True)})  # fits in the trajectory
 
     def start_for(self, optimizer_step: int) -> int:
         """First SDE step of the window after ``optimizer_step`` optimizer steps."""
         if optimizer_step < 0:
             raise ValueError(f"optimizer_step must be non-negative; got {optimizer_step}")
-        limit = self.total_steps - self.window
-        moves_made = bisect.bisect_right(_move_times(self.interval, self.stride, limit, self.exponential, self.decay),
-                                         optimizer_step)
-        return min(moves_made * self.stride, limit)
+        last = self.total_steps - self.window
+        times = _move_times(self.interval, self.stride, last, self.exponential, self.decay)
+        return min(self.stride * bisect.bisect_right(times, optimizer_step), last)
 
     def steps_for(self, optimizer_step: int) -> tuple[int, ...]:
-        start = self.start_for(optimizer_step)
-        return tuple(range(start, start + self.window))
+        first = self.start_for(optimizer_step)
+        return tuple(first + i for i in range(self.window))
+
+
+_WINDOW_LIMITS = {name: Limit(lo=1, integer=True) for name in ("window", "stride", "interval", "total_steps")} | {
+    "decay": Limit(lo=0.0, hi=1.0, lo_open=True)}
 
 
 @dataclass(frozen=True, slots=True)
@@ -105,27 +103,19 @@ class GRPOConfig:
     window: WindowSchedule | None = None
 
     def __post_init__(self) -> None:
-        if self.group_size < 2:
-            raise ValueError(f"group_size must be at least 2; got {self.group_size} (a group of one has no baseline)")
-        if self.clip_range <= 0.0:
-            raise ValueError(f"clip_range must be positive; got {self.clip_range!r}")
-        if self.clip_range_high is not None and self.clip_range_high <= 0.0:
-            raise ValueError(f"clip_range_high must be positive or None; got {self.clip_range_high!r}")
-        if self.kl_coefficient < 0.0:
-            raise ValueError(f"kl_coefficient must be non-negative; got {self.kl_coefficient!r}")
-        if self.noise_level <= 0.0:
-            raise ValueError(f"noise_level must be positive for GRPO; got {self.noise_level!r} "
-                             "(a deterministic policy has no policy gradient)")
-        for name in ("inner_epochs", "minibatch_size"):
-            v = getattr(self, name)
-            if isinstance(v, bool) or v < 1:
-                raise ValueError(f"{name} must be a positive integer; got {v!r}")
-        if self.max_grad_norm <= 0.0:
-            raise ValueError(f"max_grad_norm must be positive; got {self.max_grad_norm!r}")
+        # a group of one has no baseline; a deterministic policy (noise 0) has no policy gradient
+        enforce(self, _GRPO_LIMITS)
 
     @property
     def high(self) -> float:
         return self.clip_range if self.clip_range_high is None else self.clip_range_high
+
+
+_POSITIVE = Limit(lo=0.0, lo_open=True)
+_GRPO_LIMITS = {"group_size": Limit(lo=2, integer=True), "clip_range": _POSITIVE,
+                "clip_range_high": Limit(lo=0.0, lo_open=True, optional=True), "kl_coefficient": Limit(lo=0.0),
+                "noise_level": _POSITIVE, "inner_epochs": Limit(lo=1, integer=True),
+                "minibatch_size": Limit(lo=1, integer=True), "max_grad_norm": _POSITIVE}
 
 
 @dataclass(frozen=True, slots=True)

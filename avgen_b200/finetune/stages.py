@@ -7,13 +7,13 @@ conditioning-mode mix. Registered stages: ``full``, ``lora``, ``control``,
 """
 from __future__ import annotations
 
-import math
 from collections.abc import Mapping, Sequence
 from dataclasses import dataclass, field
 from typing import Any
 
 import torch
 
+from avgen_b200.core.limits import Limit, enforce
 from avgen_b200.finetune.adapters import ControlAdapterConfig
 from avgen_b200.finetune.lora import LoRAConfig
 
@@ -39,10 +39,11 @@ def resolution_shift(sequence_length: int, *, base_length: int = 4096, base_shif
 
 
 def shift_timesteps(noise_level: torch.Tensor, shift: float) -> torch.Tensor:
-    """Resolution-dependent shift of noise levels: t -> s t / (1 + (s - 1) t)."""
-    if not shift > 0:
-        raise ValueError(f"shift must be positive; got {shift!r}")
-    return shift * noise_level / (1.0 + (shift - 1.0) * noise_level)
+    """Resolution-dependent shift of noise levels: t -> s t / (1 + (s - 1) t) (the
+    training sampler's warp)."""
+    from avgen_b200.train.timestep import shift_timesteps as warp
+
+    return warp(noise_level, shift)
 
 
 @dataclass(frozen=True, slots=True)
@@ -104,15 +105,13 @@ class FinetuneStage:
     def __post_init__(self) -> None:
         if not self.name:
             raise ValueError("stage name must be non-empty")
-        if not (math.isfinite(self.learning_rate) and self.learning_rate > 0):
-            raise ValueError("learning_rate must be positive")
+        enforce(self, {"learning_rate": Limit(lo=0.0, lo_open=True)})
         if self.lora is not None and self.control is not None:
             raise ValueError("a stage trains either a LoRA or a control adapter, not both")
-        for mode, w in self.conditioning_mix:
-            if mode not in _MODES or w < 0:
-                raise ValueError(f"bad conditioning mix entry {(mode, w)!r}")
-        if sum(w for _, w in self.conditioning_mix) <= 0:
-            raise ValueError("conditioning_mix weights must sum to a positive value")
+        bad = [(mode, w) for mode, w in self.conditioning_mix if mode not in _MODES or not w >= 0]
+        if bad or not sum(w for _, w in self.conditioning_mix) > 0:
+            raise ValueError(f"conditioning_mix needs known modes with non-negative weights summing above zero; "
+                             f"got {self.conditioning_mix!r}")
 
     @property
     def uses_adapter(self) -> bool:

@@ -9,6 +9,7 @@ clip coefficient and non-finite flag never leave the device.
 """
 from __future__ import annotations
 
+import bisect
 import logging
 from collections.abc import Iterable, Iterator, Sequence
 from contextlib import nullcontext
@@ -18,7 +19,8 @@ from typing import Any, Protocol, runtime_checkable
 import torch
 from torch.distributed.device_mesh import DeviceMesh
 
-from avgen_b200.core._validate import require_name, require_positive
+from avgen_b200.core._validate import require_name
+from avgen_b200.core.limits import Limit, enforce
 from avgen_b200.core.batch import MediaBatch
 from avgen_b200.core.metrics import StepMetrics
 from avgen_b200.core.patchify import GridPatchifier, Patchifier
@@ -55,8 +57,7 @@ class ResolutionBucket:
 
     def __post_init__(self) -> None:
         require_name("name", self.name)
-        for f in ("frames", "height", "width"):
-            require_positive(f, getattr(self, f))
+        enforce(self, _GRID_LIMITS)
 
     @property
     def latents(self) -> int:
@@ -71,13 +72,11 @@ class CurriculumStage:
 
     def __post_init__(self) -> None:
         require_name("name", self.name)
-        require_positive("until_step", self.until_step)
-        if not self.buckets:
-            raise ValueError(f"stage {self.name!r} must declare at least one bucket")
-        if sum(w for _, w in self.buckets) <= 0.0:
-            raise ValueError(f"stage {self.name!r} must have a positive total weight")
-        if any(w < 0 for _, w in self.buckets):
-            raise ValueError(f"stage {self.name!r} has a negative weight")
+        enforce(self, {"until_step": Limit(lo=1, integer=True)})
+        weights = [w for _, w in self.buckets]
+        if not weights or min(weights) < 0 or not sum(weights) > 0:
+            raise ValueError(f"stage {self.name!r} needs at least one bucket, no negative weight and a positive "
+                             f"total; got weights {weights}")
 
 
 @dataclass(frozen=True, slots=True)
@@ -94,12 +93,12 @@ class Curriculum:
         return not self.stages
 
     def stage_for(self, step: int) -> CurriculumStage | None:
+        """The first stage whose ``until_step`` lies beyond ``step`` (the last stage
+        stays active after the schedule ends)."""
         if not self.stages:
             return None
-        for s in self.stages:
-            if step < s.until_step:
-                return s
-        return self.stages[-1]
+        at = bisect.bisect_right([s.until_step for s in self.stages], step)
+        return self.stages[min(at, len(self.stages) - 1)]
 
 
 @dataclass(frozen=True, slots=True)
@@ -114,21 +113,21 @@ class TrainerConfig:
     data_world: int = 1
 
     def __post_init__(self) -> None:
-        require_positive("gradient_accumulation_steps", self.gradient_accumulation_steps)
-        require_positive("log_every", self.log_every)
-        require_positive("data_world", self.data_world)
-        for name in ("eval_every", "checkpoint_every"):
-            v = getattr(self, name)
-            if isinstance(v, bool) or v < 0:
-                raise ValueError(f"{name} must be non-negative")
-        if self.max_grad_norm is not None and self.max_grad_norm <= 0.0:
-            raise ValueError("max_grad_norm must be positive or None")
+        enforce(self, _TRAINER_LIMITS)
         if not isinstance(getattr(torch, self.autocast_dtype, None), torch.dtype):
             raise ValueError(f"unknown autocast dtype {self.autocast_dtype!r}")
 
     @property
     def torch_autocast_dtype(self) -> torch.dtype:
         return getattr(torch, self.autocast_dtype)
+
+
+_GRID_LIMITS = {axis: Limit(lo=1, integer=True) for axis in ("frames", "height", "width")}
+# cadences of 0 switch eval / checkpoint callbacks off; logging always has one
+_TRAINER_LIMITS = {"gradient_accumulation_steps": Limit(lo=1, integer=True), "log_every": Limit(lo=1, integer=True),
+                   "data_world": Limit(lo=1, integer=True), "eval_every": Limit(lo=0, integer=True),
+                   "checkpoint_every": Limit(lo=0, integer=True),
+                   "max_grad_norm": Limit(lo=0.0, lo_open=True, optional=True)}
 
 
 def _native(model: torch.nn.Module) -> bool:

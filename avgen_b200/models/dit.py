@@ -12,6 +12,7 @@ root linears run the tcgen05 GEMM; on the CPU everything is the fp32 oracle.
 """
 from __future__ import annotations
 
+import math
 from dataclasses import dataclass, field, fields, replace
 from typing import TYPE_CHECKING, Any
 
@@ -19,6 +20,7 @@ import torch
 import torch.nn.functional as F
 from torch import nn
 
+from avgen_b200.core.limits import Limit, enforce
 from avgen_b200.core.model_input import ModelInput, ModelOutput
 from avgen_b200.core.patchify import GridPatchifier, Patchifier
 from avgen_b200.core.tokens import TextContext, TokenStream
@@ -36,6 +38,33 @@ __all__ = ["FUSION_MODES", "AVDiT", "AVDiTConfig", "VideoDiT", "VideoDiTConfig",
 
 FUSION_MODES = ("cross_attention", "joint")
 FFN_KINDS = ("swiglu", "gelu")
+
+
+_COUNT = Limit(lo=1, integer=True)
+_VIDEO_LIMITS = {**{name: _COUNT for name in ("width", "depth", "num_heads", "ffn_multiple_of", "in_channels",
+                                              "patch_frames", "patch_height", "patch_width", "text_width",
+                                              "time_frequency_dim")},
+                 "num_kv_heads": Limit(lo=1, integer=True, optional=True), "mlp_ratio": Limit(lo=0.0, lo_open=True),
+                 "ffn_hidden": Limit(lo=1, integer=True, optional=True), "text_refiner_depth": Limit(lo=0, integer=True)}
+_AUDIO_LIMITS = {name: _COUNT for name in ("audio_width", "audio_num_heads", "audio_in_channels", "audio_patch_frames",
+                                           "fusion_interval")}
+
+
+def _check_heads(prefix: str, width: int, heads: int) -> None:
+    """Heads split the width evenly into even (rotary pairs) head dims of at least 6
+    (two pairs for time, one for each spatial axis at the least)."""
+    if width % heads:
+        raise ValueError(f"{prefix}width={width} must be divisible by {prefix}num_heads={heads}")
+    dim = width // heads
+    if dim % 2 or dim < 6:
+        raise ValueError(f"{prefix}head_dim={dim} must be even and at least 6")
+
+
+def _ffn_width(explicit: int | None, ratio: float, width: int, multiple: int) -> int:
+    """``explicit``, else ``ratio * width`` rounded up to a multiple of ``multiple``."""
+    if explicit is not None:
+        return explicit
+    return math.ceil(int(ratio * width) / multiple) * multiple
 
 
 @dataclass(frozen=True, slots=True)
@@ -69,29 +98,16 @@ class VideoDiTConfig:
     init_std: float = 0.02
 
     def __post_init__(self) -> None:
-        for name in ("width", "depth", "num_heads", "ffn_multiple_of", "in_channels", "patch_frames", "patch_height",
-                     "patch_width", "text_width", "time_frequency_dim"):
-            v = getattr(self, name)
-            if not isinstance(v, int) or isinstance(v, bool) or v < 1:
-                raise ValueError(f"{name} must be a positive integer; got {v!r}")
-        if self.width % self.num_heads:
-            raise ValueError(f"width {self.width} must be divisible by num_heads {self.num_heads}")
-        if self.head_dim % 2 or self.head_dim < 6:
-            raise ValueError(f"head_dim {self.head_dim} must be even and at least 6")
-        if self.num_kv_heads is not None and (self.num_kv_heads < 1 or self.num_heads % self.num_kv_heads):
-            raise ValueError(f"num_kv_heads must divide num_heads {self.num_heads}")
-        if self.mlp_ratio <= 0:
-            raise ValueError("mlp_ratio must be positive")
-        if self.ffn_hidden is not None and self.ffn_hidden < 1:
-            raise ValueError("ffn_hidden must be positive")
-        if self.ffn not in FFN_KINDS:
-            raise ValueError(f"ffn must be one of {FFN_KINDS}; got {self.ffn!r}")
-        if self.text_refiner_depth < 0:
-            raise ValueError("text_refiner_depth must be non-negative")
-        if self.text_refiner_depth and not self.cross_attention:
-            raise ValueError("text_refiner_depth > 0 needs cross_attention")
         if not isinstance(self.rope_scaling, RoPEScaling):
             raise TypeError("rope_scaling must be a RoPEScaling")
+        enforce(self, _VIDEO_LIMITS)
+        _check_heads("", self.width, self.num_heads)
+        if self.num_kv_heads is not None and self.num_heads % self.num_kv_heads:
+            raise ValueError(f"num_kv_heads={self.num_kv_heads} must divide num_heads={self.num_heads}")
+        if self.ffn not in FFN_KINDS:
+            raise ValueError(f"ffn must be one of {FFN_KINDS}; got {self.ffn!r}")
+        if self.text_refiner_depth and not self.cross_attention:
+            raise ValueError("text_refiner_depth > 0 needs cross_attention")
 
     @property
     def head_dim(self) -> int:
@@ -99,10 +115,7 @@ class VideoDiTConfig:
 
     @property
     def ffn_width(self) -> int:
-        if self.ffn_hidden is not None:
-            return self.ffn_hidden
-        hidden = int(self.mlp_ratio * self.width)
-        return -(-hidden // self.ffn_multiple_of) * self.ffn_multiple_of
+        return _ffn_width(self.ffn_hidden, self.mlp_ratio, self.width, self.ffn_multiple_of)
 
     @property
     def cond_dim(self) -> int:
@@ -314,16 +327,10 @@ class AVDiTConfig(VideoDiTConfig):
 
     def __post_init__(self) -> None:
         VideoDiTConfig.__post_init__(self)
-        for name in ("audio_width", "audio_num_heads", "audio_in_channels", "audio_patch_frames", "fusion_interval"):
-            v = getattr(self, name)
-            if not isinstance(v, int) or isinstance(v, bool) or v < 1:
-                raise ValueError(f"{name} must be a positive integer; got {v!r}")
+        enforce(self, _AUDIO_LIMITS)
         if self.fusion not in FUSION_MODES:
             raise ValueError(f"fusion must be one of {FUSION_MODES}; got {self.fusion!r}")
-        if self.audio_width % self.audio_num_heads:
-            raise ValueError("audio_width must be divisible by audio_num_heads")
-        if self.audio_head_dim % 2 or self.audio_head_dim < 6:
-            raise ValueError("audio head_dim must be even and at least 6")
+        _check_heads("audio_", self.audio_width, self.audio_num_heads)
 
     @property
     def audio_head_dim(self) -> int:
@@ -331,11 +338,9 @@ class AVDiTConfig(VideoDiTConfig):
 
     @property
     def audio_ffn_width(self) -> int:
-        if self.audio_ffn_hidden is not None:
-            return self.audio_ffn_hidden
-        hidden = int(self.mlp_ratio * self.audio_width)
-        multiple = min(self.ffn_multiple_of, max(1, self.audio_width))
-        return -(-hidden // multiple) * multiple
+        # the rounding multiple never exceeds the tower's own width (narrow audio towers)
+        return _ffn_width(self.audio_ffn_hidden, self.mlp_ratio, self.audio_width,
+                          min(self.ffn_multiple_of, self.audio_width))
 
     @property
     def audio_patch_dim(self) -> int:

@@ -84,11 +84,29 @@ def build_model_shape(config: RunConfig, *, bucket: BucketConfig | None = None, 
     if config.model.has_audio and config.data.audio_frames:
         tokens += config.data.audio_frames // config.model.patch_frames
     micro = config.train.micro_batch_size if config.train.micro_batch_size != -1 else chosen.micro_batch_size
-    return ModelShape(parameters=parameters or config.model.estimated_parameters(), depth=config.model.depth,
+    return ModelShape(parameters=parameters or counted_parameters(config), depth=config.model.depth,
                       width=config.model.width, sequence_length=tokens, micro_batch_size=micro,
                       mlp_ratio=config.model.mlp_ratio, num_heads=config.model.num_heads,
                       text_tokens=config.data.text_tokens if config.model.cross_attention else 0,
                       ffn=config.model.ffn)
+
+
+_COUNTS: dict[str, int] = {}
+
+
+def counted_parameters(config: RunConfig) -> int:
+    """The parameter count of the model ``config`` builds, counted on the meta device
+    (no memory), or the closed-form estimate when the model cannot be built here."""
+    if config.model.parameters:
+        return config.model.parameters
+    key = repr((config.model, config.data.text_width, config.data.text_tokens, config.data.audio_channels))
+    if key not in _COUNTS:
+        try:
+            model = build_model(config, meta=True)
+            _COUNTS[key] = int(sum(p.numel() for p in model.parameters()))
+        except Exception:  # noqa: BLE001 - a plugin model or an invalid shape: fall back to the formula
+            _COUNTS[key] = config.model.estimated_parameters(text_width=config.data.text_width)
+    return _COUNTS[key]
 
 
 def build_accelerator(name: str):  # noqa: ANN201

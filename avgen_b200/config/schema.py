@@ -114,15 +114,29 @@ class ModelConfig:
     def has_audio(self) -> bool:
         return self.audio_width > 0
 
-    def estimated_parameters(self) -> int:
+    def estimated_parameters(self, *, text_width: int | None = None) -> int:
+        """Closed-form parameter count of this framework's video DiT: per block q/k/v/out
+        with their QK-norm weights, the MLP (three matrices for SwiGLU, two for GELU,
+        hidden rounded up to 256), cross-attention (its k/v read the text after the
+        root's ``text_width`` -> width projection), its norms and the block's
+        modulation table; at the root the patch and text projections, the timestep MLP,
+        the shared adaLN projection (6 x width outputs) and the output projection.
+        ``parameters`` overrides it; :func:`avgen_b200.config.resolve.build_model_shape`
+        counts the built model's parameters exactly when it can."""
         if self.parameters:
             return self.parameters
-        w = float(self.width)
-        mlp = (3.0 if self.ffn == "swiglu" else 2.0) * self.mlp_ratio * w * w
-        per_block = 4.0 * w * w + mlp + 6.0 * w * w + (4.0 * w * w if self.cross_attention else 0.0)
-        patch_dim = self.in_channels * self.patch_frames * self.patch_height * self.patch_width
-        embed = 2 * patch_dim * w + 4.0 * w * w
-        return int(per_block * self.depth + embed)
+        w = self.width
+        tw = text_width if text_width is not None else int(self.extra.get("text_width", 4096))
+        hidden = -(-int(self.mlp_ratio * w) // 256) * 256
+        mlp = (3 if self.ffn == "swiglu" else 2) * hidden * w
+        attention = 4 * w * w + 2 * self.head_dim
+        norms = (3 if self.cross_attention else 2) * w
+        per_block = attention * (2 if self.cross_attention else 1) + mlp + 6 * w + norms
+        patch = self.in_channels * self.patch_frames * self.patch_height * self.patch_width
+        out = (self.out_channels if self.out_channels != -1 else self.in_channels) * (
+            self.patch_frames * self.patch_height * self.patch_width)
+        root = (patch + 1) * w + (tw + 1) * w + (256 * w + w * w + 2 * w) + (w + 1) * 6 * w + (w + 1) * out + w
+        return int(per_block * self.depth + root)
 
 
 @dataclass(frozen=True, slots=True)

@@ -589,3 +589,19 @@ def test_build_accelerator_unknown_and_interconnects() -> None:
     intra, inter = build_interconnects("b200")
     intra_h, _ = build_interconnects("h100")
     assert intra is not intra_h and inter is not None
+
+
+@pytest.mark.parametrize("ffn,cross,width,heads", [("swiglu", True, 256, 4), ("gelu", True, 192, 3),
+                                                   ("swiglu", False, 128, 2), ("gelu", False, 320, 5)])
+def test_parameter_estimate_matches_the_built_model(ffn: str, cross: bool, width: int, heads: int) -> None:
+    """The closed form counts exactly what the model builds (on the meta device), so the
+    simulator's memory and FLOP estimates start from the right parameter count."""
+    from avgen_b200.config.loader import load_config
+    from avgen_b200.config.resolve import build_model, counted_parameters
+
+    cfg = load_config(None, overrides=[f"model.width={width}", f"model.num_heads={heads}", "model.depth=3",
+                                       f"model.ffn={ffn}", f"model.cross_attention={str(cross).lower()}",
+                                       "data.text_width=96"])
+    built = sum(p.numel() for p in build_model(cfg, meta=True).parameters())
+    assert counted_parameters(cfg) == built
+    assert cfg.model.estimated_parameters(text_width=96) == built

@@ -44,6 +44,7 @@ setup(
     name="avgen_b200",
     version="0.1.0",
     packages=find_packages(include=["avgen_b200", "avgen_b200.*"]),
+    package_data={"avgen_b200.simulate": ["*.json"]},
     ext_modules=[
         CUDAExtension(
             name="avgen_b200._C",

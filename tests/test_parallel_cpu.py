@@ -43,6 +43,18 @@ def test_block_plan_and_precision() -> None:
     assert p.fsdp_policy().cast_forward_inputs is False
     with pytest.raises(KeyError):
         PrecisionConfig(param_dtype="int8")  # type: ignore[arg-type]
+    with pytest.raises(ValueError):
+        PrecisionConfig(float8_min_features=0)
+    assert PrecisionConfig(param_dtype="float32").autocast_dtype() is None
+
+
+def test_float8_targets_skip_small_unaligned_and_kept_linears() -> None:
+    model = torch.nn.ModuleDict({"patch_embed": torch.nn.Linear(2048, 2048), "big": torch.nn.Linear(2048, 4096),
+                                 "small": torch.nn.Linear(512, 2048), "odd": torch.nn.Linear(2048, 2050),
+                                 "final_proj": torch.nn.Linear(2048, 2048)})
+    assert PrecisionConfig().float8_targets(model) == ["big"]
+    assert PrecisionConfig(float8_min_features=256, float8_exclude=()).float8_targets(model) == [
+        "patch_embed", "big", "small", "final_proj"]
 
 
 def test_activation_policies_preserve_checkpoint_keys() -> None:

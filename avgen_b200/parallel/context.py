@@ -171,9 +171,10 @@ class ContextParallelAttention:
 
     def _gather(self, t: torch.Tensor) -> torch.Tensor:
         b, h, length, d = t.shape
-        buf = torch.empty((self.world, b, h, length, d), device=t.device, dtype=t.dtype)
+        # rank-major rows, dim 0 a multiple of the input's (the layout every backend accepts)
+        buf = torch.empty((self.world * b, h, length, d), device=t.device, dtype=t.dtype)
         dist.all_gather_into_tensor(buf, t.contiguous(), group=self.group)
-        return buf.permute(1, 2, 0, 3, 4).reshape(b, h, self.world * length, d)
+        return buf.view(self.world, b, h, length, d).permute(1, 2, 0, 3, 4).reshape(b, h, self.world * length, d)
 
     def forward(self, q, k, v, kmask, scale):  # noqa: ANN001, ANN201
         from avgen_b200.ops import kernels as K
@@ -191,7 +192,7 @@ class ContextParallelAttention:
         b, h, length, d = k.shape
 
         def scatter(full: torch.Tensor) -> torch.Tensor:
-            parts = full.view(b, h, self.world, length, d).permute(2, 0, 1, 3, 4).contiguous()
+            parts = full.view(b, h, self.world, length, d).permute(2, 0, 1, 3, 4).reshape(self.world * b, h, length, d)
             out = torch.empty((b, h, length, d), device=full.device, dtype=full.dtype)
             dist.reduce_scatter_tensor(out, parts, group=self.group)
             return out

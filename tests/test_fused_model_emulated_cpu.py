@@ -3,8 +3,10 @@ restated in PyTorch (``kernel_emulator``) and the fused path forced on: a
 flow-matching step of the tiny model matches the eager model, and a two-stage
 1F1B pipeline over ``gloo`` with fused blocks on both stages matches the
 unsharded eager model with gradient accumulation (loss and gradient norm, bf16
-tolerance). This is the path where a wrong gradient list from the fused node
-leaves one pipeline rank waiting on the other."""
+tolerance), and so does a two-rank context-parallel step whose fused blocks
+attend over the whole sequence (K/V gathered, dK/dV reduce-scattered). The
+pipeline is the path where a wrong gradient list from the fused node leaves one
+rank waiting on the other."""
 from __future__ import annotations
 
 import os
@@ -146,3 +148,39 @@ def _pipeline_worker(rank: int, world: int, port: int) -> None:
 
 def test_two_stage_pipeline_with_fused_blocks_matches_unsharded() -> None:
     mp.spawn(_pipeline_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _context_worker(rank: int, world: int, port: int) -> None:
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PrecisionConfig, parallelize
+    from avgen_b200.parallel.context import ContextParallelAttention
+    from avgen_b200.train import build_optimizer, train_step
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), AVGEN_KEEP_ACTIVATIONS="none")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        ref = _model()
+        dims = ParallelDims(world_size=world, context=world)
+        pm = parallelize(_model(), dims, mesh=dims.build_mesh("cpu"),
+                         config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32")))
+        assert all(isinstance(b.attention_impl, ContextParallelAttention) for b in pm.model.blocks)
+        state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-3),
+                           rng=RNGStreams.for_rank(0, data_rank=0))
+        ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-3),
+                               rng=RNGStreams.for_rank(0, data_rank=0))
+        batch = _batches(ref, 1, seed=9)[0]
+        with _ForcedFused() as forced:
+            _, metrics = train_step(state, batch, _objective(), patchifier=ref.patchifier, max_grad_norm=None,
+                                    cp_mesh=pm.cp_mesh)
+        assert forced.calls == len(pm.model.blocks)
+        _, want = train_step(ref_state, batch, _objective(), patchifier=ref.patchifier, max_grad_norm=None)
+        loss = metrics.loss.detach().reshape(1).clone()
+        dist.all_reduce(loss)  # each rank reports its shard's share; the step's loss is their mean
+        assert abs(float(loss) / world - float(want.loss)) <= 2e-2 * abs(float(want.loss))
+        assert abs(float(metrics.grad_norm) - float(want.grad_norm)) <= 5e-2 * float(want.grad_norm)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_context_parallel_step_with_fused_blocks_matches_unsharded() -> None:
+    mp.spawn(_context_worker, args=(2, _free_port()), nprocs=2, join=True)

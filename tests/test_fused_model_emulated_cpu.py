@@ -4,7 +4,8 @@ flow-matching step of the tiny model matches the eager model, and a two-stage
 1F1B pipeline over ``gloo`` with fused blocks on both stages matches the
 unsharded eager model with gradient accumulation (loss and gradient norm, bf16
 tolerance), and so does a two-rank context-parallel step whose fused blocks
-attend over the whole sequence (K/V gathered, dK/dV reduce-scattered). The
+attend over the whole sequence (K/V gathered, dK/dV reduce-scattered) with their
+parameters sharded over the cp ranks by FSDP2 (the flagship's layout at two GPUs). The
 pipeline is the path where a wrong gradient list from the fused node leaves one
 rank waiting on the other."""
 from __future__ import annotations
@@ -164,6 +165,7 @@ def _context_worker(rank: int, world: int, port: int) -> None:
         pm = parallelize(_model(), dims, mesh=dims.build_mesh("cpu"),
                          config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32")))
         assert all(isinstance(b.attention_impl, ContextParallelAttention) for b in pm.model.blocks)
+        assert any(a.startswith("fsdp(cp=") for a in pm.applied), pm.applied  # parameters sharded over cp
         state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-3),
                            rng=RNGStreams.for_rank(0, data_rank=0))
         ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-3),

@@ -285,7 +285,7 @@ def _tp_reduce(spec: BlockSpec, rows: torch.Tensor) -> torch.Tensor:
 
     c = rows.shape[-1]
     src = rows.contiguous() if spec.batch == 1 else \
-        rows.view(spec.batch, tp.world, spec.length, c).transpose(0, 1).contiguous()
+        rows.view(spec.batch, tp.world, spec.length, c).transpose(0, 1).reshape(-1, c)
     out = torch.empty((spec.batch * spec.length, c), dtype=rows.dtype, device=rows.device)
     dist.reduce_scatter_tensor(out, src, group=tp.group)
     return out

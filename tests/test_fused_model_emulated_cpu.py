@@ -5,7 +5,9 @@ flow-matching step of the tiny model matches the eager model, and a two-stage
 unsharded eager model with gradient accumulation (loss and gradient norm, bf16
 tolerance), and so does a two-rank context-parallel step whose fused blocks
 attend over the whole sequence (K/V gathered, dK/dV reduce-scattered) with their
-parameters sharded over the cp ranks by FSDP2 (the flagship's layout at two GPUs). The
+parameters sharded over the cp ranks by FSDP2 (the flagship's layout at two GPUs),
+an interleaved 1F1B pipeline (4 chunks over 2 ranks) and head-parallel tensor
+parallelism with sequence parallelism (3 heads as [2, 1], two samples per batch). The
 pipeline is the path where a wrong gradient list from the fused node leaves one
 rank waiting on the other."""
 from __future__ import annotations
@@ -186,3 +188,71 @@ def _context_worker(rank: int, world: int, port: int) -> None:
 
 def test_context_parallel_step_with_fused_blocks_matches_unsharded() -> None:
     mp.spawn(_context_worker, args=(2, _free_port()), nprocs=2, join=True)
+
+
+def _deep_model(depth: int = 4, heads: int | None = None):  # noqa: ANN202
+    from avgen_b200.models import build_model, preset
+
+    torch.manual_seed(0)
+    cfg = {k: v for k, v in asdict(preset("tiny")).items() if k != "rope_scaling"}
+    cfg["depth"] = depth
+    if heads is not None:
+        cfg.update(num_heads=heads, width=16 * heads)
+    model = build_model("video_dit", cfg)
+    model.init_weights()
+    with torch.no_grad():
+        for p in model.parameters():
+            p.add_(0.02 * torch.randn_like(p))
+    return model
+
+
+def _layout_worker(rank: int, world: int, port: int, layout: str) -> None:
+    """Interleaved 1F1B (4 chunks over 2 ranks) or head-parallel TP with sequence
+    parallelism (3 heads as [2, 1]), fused blocks emulated, against the eager model."""
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PipelineConfig, PrecisionConfig, parallelize
+    from avgen_b200.train import build_optimizer, train_step
+    from avgen_b200.train.trainer import pipeline_train_step
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), AVGEN_KEEP_ACTIVATIONS="none")
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        heads = 3 if layout == "tp" else None
+        ref = _deep_model(heads=heads)
+        fp32 = PrecisionConfig(param_dtype="float32")
+        if layout == "tp":
+            dims = ParallelDims(world_size=world, tensor=world)
+            cfg = ParallelConfig(precision=fp32, sequence_parallel=True)
+        else:
+            dims = ParallelDims(world_size=world, pipeline=world)
+            cfg = ParallelConfig(precision=fp32, pipeline=PipelineConfig(schedule="interleaved_1f1b",
+                                                                         stages_per_rank=2, microbatches=4))
+        pm = parallelize(_deep_model(heads=heads), dims, mesh=dims.build_mesh("cpu"), config=cfg)
+        state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-3),
+                           rng=RNGStreams.for_rank(0, data_rank=0))
+        ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-3),
+                               rng=RNGStreams.for_rank(0, data_rank=0))
+        micro = _batches(ref, 4 if layout != "tp" else 1, seed=13)
+        with _ForcedFused() as forced:
+            if layout == "tp":
+                _, metrics = train_step(state, micro[0], _objective(), patchifier=ref.patchifier, max_grad_norm=None)
+            else:
+                _, metrics = pipeline_train_step(state, micro, _objective(), pm.pipeline, patchifier=ref.patchifier,
+                                                 max_grad_norm=1.0, pp_mesh=pm.pp_mesh)
+        assert forced.calls > 0
+        losses = []
+        for i, b in enumerate(micro):
+            _, rm = train_step(ref_state, b, _objective(), patchifier=ref.patchifier,
+                               gradient_accumulation_steps=len(micro), microbatch_index=i,
+                               max_grad_norm=None if layout == "tp" else 1.0)
+            losses.append(float(rm.loss))
+        want = sum(losses) / len(losses)
+        assert abs(float(metrics.loss) - want) <= 2e-2 * abs(want), (layout, float(metrics.loss), want)
+        assert abs(float(metrics.grad_norm) - float(rm.grad_norm)) <= 5e-2 * float(rm.grad_norm)
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("layout", ["interleaved", "tp"])
+def test_other_layouts_with_fused_blocks_match_unsharded(layout: str) -> None:
+    mp.spawn(_layout_worker, args=(2, _free_port(), layout), nprocs=2, join=True)

@@ -117,17 +117,38 @@ class BlockSpec:
         return {"rows_per_batch": self.mod_rows_per_batch or self.length, "groups": self.groups}
 
 
-def _packed(module: nn.Module, key: str, params: list[torch.Tensor], build) -> torch.Tensor:  # noqa: ANN001
+@dataclass(frozen=True)
+class _LoRAWeight:
+    """A plain LoRA layer's effective weight ``W + s B A``, formed only when packed."""
+
+    base: torch.Tensor
+    a: torch.Tensor
+    b: torch.Tensor
+    scaling: float
+
+    def parts(self) -> tuple[torch.Tensor, ...]:
+        return (self.base, self.a, self.b)
+
+    def value(self) -> torch.Tensor:
+        delta = (self.b.detach().float() @ self.a.detach().float()).mul_(self.scaling)
+        return self.base.detach() + delta.to(self.base.dtype)
+
+
+def _packed(module: nn.Module, key: str, params: list[Any], build) -> torch.Tensor:  # noqa: ANN001
+    """``build(*params)`` in bf16, cached on ``module`` until one of its source
+    parameters changes (a LoRA weight's sources are its base, A and B)."""
     from avgen_b200.models.linear import weight_epoch
 
     with torch.no_grad():
-        fresh = lambda: build(*[p.detach() for p in params]).to(_BF16).contiguous()  # noqa: E731
+        fresh = lambda: build(*[p.value() if isinstance(p, _LoRAWeight) else p.detach()  # noqa: E731
+                                for p in params]).to(_BF16).contiguous()
         if _fsdp_managed(module):
             return fresh()  # FSDP re-gathers the parameters every forward: never serve a cached copy
-        if not all(isinstance(p, nn.Parameter) or getattr(p, "_avgen_stable", False) for p in params):
+        sources = [t for p in params for t in (p.parts() if isinstance(p, _LoRAWeight) else (p,))]
+        if not all(isinstance(t, nn.Parameter) for t in sources):
             return fresh()  # a temporary's address and version can repeat after it is freed
         cache = module.__dict__.setdefault("_avgen_packed", {})
-        version = (weight_epoch(), *((p._version, p.data_ptr()) for p in params))
+        version = (weight_epoch(), *((t._version, t.data_ptr()) for t in sources))
         hit = cache.get(key)
         if hit is not None and hit[0] == version:
             return hit[1]
@@ -188,30 +209,15 @@ def fused_inputs(block: nn.Module, *, differentiable: bool = True) -> tuple[list
     return names, tensors
 
 
-def _packing_weights(block: nn.Module, weights: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
-    """``weights`` with each plain LoRA layer's base weight replaced by ``W + s B A``.
-    Outside FSDP the sum is kept on the layer until one of its three inputs changes, so
-    the packed-weight cache sees one stable tensor per adapter state."""
-    from avgen_b200.models.linear import weight_epoch
-
-    out = dict(weights)
-    cacheable = not _fsdp_managed(block)
+def _packing_weights(block: nn.Module, weights: dict[str, torch.Tensor]) -> dict[str, Any]:
+    """``weights`` with each plain LoRA layer's base weight standing for ``W + s B A``
+    (formed by the packed-weight cache from its three sources, so no second copy of the
+    weight is kept beside the packed one)."""
+    out: dict[str, Any] = dict(weights)
     for prefix, layer in _adapted_layers(block).items():
         a, bmat = out.get(f"{prefix}.lora_a"), out.get(f"{prefix}.lora_b")
-        if a is None or bmat is None or not _plain_lora(layer):
-            continue
-        base = out[f"{prefix}.weight"]
-        key = (weight_epoch(), *((t._version, t.data_ptr()) for t in (base, a, bmat)))
-        hit = layer.__dict__.get("_avgen_effective")
-        if cacheable and hit is not None and hit[0] == key:
-            out[f"{prefix}.weight"] = hit[1]
-            continue
-        with torch.no_grad():
-            eff = base.detach() + (bmat.detach().float() @ a.detach().float()).mul_(layer.scaling).to(base.dtype)
-        if cacheable:
-            eff._avgen_stable = True
-            layer.__dict__["_avgen_effective"] = (key, eff)
-        out[f"{prefix}.weight"] = eff
+        if a is not None and bmat is not None and _plain_lora(layer):
+            out[f"{prefix}.weight"] = _LoRAWeight(out[f"{prefix}.weight"], a, bmat, float(layer.scaling))
     return out
 
 

@@ -231,3 +231,37 @@ def _tp_worker(rank: int, world: int, port: int, heads: int) -> None:
 @pytest.mark.parametrize("world,heads", [(2, 3)])
 def test_head_parallel_fused_block_matches_unsharded(world: int, heads: int) -> None:
     mp.spawn(_tp_worker, args=(world, _free_port(), heads), nprocs=world, join=True)
+
+
+def test_lora_packed_weights_are_cached_until_an_adapter_changes(monkeypatch: pytest.MonkeyPatch) -> None:
+    """The packed bf16 weights of a LoRA-adapted block are built once per adapter state:
+    the backward's recompute reuses the forward's, an in-place adapter update rebuilds
+    them, and the effective weight is never kept beside its packed copy."""
+    import avgen_b200.models.fused as fused_mod
+    from avgen_b200.finetune.lora import LoRAConfig, apply_lora, lora_modules, mark_only_lora_trainable
+
+    monkeypatch.setenv("AVGEN_KEEP_ACTIVATIONS", "none")
+    block = _block()
+    apply_lora(block, LoRAConfig(rank=8, alpha=16.0, target_modules=("q_proj", "out_proj", "down_proj")))
+    mark_only_lora_trainable(block)
+    built = {"n": 0}
+    original = fused_mod._LoRAWeight.value
+
+    def counting(self):  # noqa: ANN001, ANN202
+        built["n"] += 1
+        return original(self)
+
+    monkeypatch.setattr(fused_mod._LoRAWeight, "value", counting)
+    x, mod, ctx, coords, kmask, cmask, mod_index = _inputs(1, 16, 5, masked=False, modulation="sample")
+    g = torch.randn(1, 16, WIDTH)
+    with emulate_kernels():
+        _run(block, True, x, mod, ctx, coords, kmask, cmask, mod_index, g)
+        first = built["n"]
+        assert first == 5  # self q, self out, cross q, cross out, MLP down: once each for forward and recompute
+        _run(block, True, x, mod, ctx, coords, kmask, cmask, mod_index, g)
+        assert built["n"] == first  # nothing changed: every packed weight served from the cache
+        with torch.no_grad():
+            next(m for _, m in lora_modules(block)).lora_b.add_(0.01)
+        _run(block, True, x, mod, ctx, coords, kmask, cmask, mod_index, g)
+        assert built["n"] == first + 1  # only the updated adapter's pack was rebuilt
+    assert not any("_avgen_effective" in m.__dict__ for m in block.modules())

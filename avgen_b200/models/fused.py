@@ -22,20 +22,26 @@ recompute the rest) built into the block.
 Self-attention can be swapped for a context-parallel implementation through
 ``BlockSpec.attention`` (see :mod:`avgen_b200.parallel.context`).
 
-Adapter-wrapped linears (LoRA / DoRA without adapter dropout) take part through
-their effective weights: the node sees ``W + s B A`` (DoRA-scaled where it
-applies) and returns its dense gradient, which autograd carries into the adapter
-parameters (``fused_inputs``).
+Adapter-wrapped linears take part through their effective weights, which the
+kernels read packed in bf16: a plain LoRA layer's ``W + s B A`` is formed from
+W, A and B when they change, and its gradients come from rank-r products with
+no dense weight gradient unless W trains; a DoRA (or merged, or dropout)
+adapter's effective weight gets its dense gradient, which autograd carries into
+the adapter parameters (``fused_inputs``, ``_weight_grads``). Frozen weights get
+no weight-gradient GEMM.
 
 Head-parallel tensor parallelism with sequence parallelism
 (:mod:`avgen_b200.parallel.heads`) runs through the same node: the norms,
 modulation and gated residuals act on this rank's token chunk; each normalised
-input is all-gathered over the tensor-parallel group before the rank's q/k/v,
-cross-attention and MLP GEMMs (its heads and hidden slice over the whole
+input is all-gathered over the tensor-parallel group inside the rank's q/k/v,
+cross-attention and MLP GEMMs (copy-engine pulls over NVLink, each tile waiting
+on its chunk's arrival flag; its heads and hidden slice over the whole
 sequence), and each output projection's partial sums are reduce-scattered back
-to the token chunk before the gated residual. The backward mirrors that: the
-gradient entering each output projection is all-gathered, the gradient leaving
-each input projection is reduce-scattered.
+to the token chunk through peer memory before the gated residual. The backward
+mirrors that: the gradient entering each output projection is all-gathered
+inside its dX GEMM, the gradient leaving each input projection is
+reduce-scattered. ``AVGEN_TP_PEER=0``, several samples per batch or a non-NCCL
+group use NCCL collectives between the kernels instead.
 """
 from __future__ import annotations
 

@@ -19,18 +19,32 @@ from typing import Any
 
 import torch
 
+from avgen_b200.core.limits import Limit, enforce
 from avgen_b200.core.model_input import ModelInput
 
 __all__ = ["GuidanceConfig", "adaptive_projected_guidance", "apply_guidance", "apply_modality_guidance",
            "classifier_free_guidance", "rescale_guidance", "unconditional_branch"]
 
 _MODALITIES = ("text", "video", "audio")
-_SCHEDULES = ("constant", "linear", "cosine", "power", "interval")
 
 
-def _positive(name: str, v: float | None) -> None:
-    if v is not None and not (math.isfinite(v) and v > 0.0):
-        raise ValueError(f"{name} must be finite and positive; got {v!r}")
+# Scale schedules over sampling progress p in [0, 1]: each maps (config, p) to the
+# fraction of the way from ``min_scale`` to ``scale`` (1 = full scale). "interval"
+# holds full scale inside [start_fraction, end_fraction] and min_scale outside.
+_SCHEDULE_WEIGHT = {
+    "constant": lambda c, p: 1.0,
+    "linear": lambda c, p: 1.0 - p,
+    "cosine": lambda c, p: 0.5 * (1.0 + math.cos(math.pi * p)),
+    "power": lambda c, p: (1.0 - p) ** c.schedule_power,
+    "interval": lambda c, p: 1.0 if c.start_fraction <= p <= c.end_fraction else 0.0,
+}
+_SCHEDULES = tuple(_SCHEDULE_WEIGHT)
+_POSITIVE = Limit(lo=0.0, lo_open=True)
+_UNIT = Limit(lo=0.0, hi=1.0)
+_GUIDANCE_LIMITS = {"scale": _POSITIVE, "min_scale": _POSITIVE, "schedule_power": _POSITIVE,
+                    **{f"{m}_scale": Limit(lo=0.0, lo_open=True, optional=True) for m in _MODALITIES},
+                    "rescale": _UNIT, "projection_eta": Limit(), "projection_threshold": Limit(lo=0.0),
+                    "start_fraction": _UNIT, "end_fraction": _UNIT}
 
 
 @dataclass(frozen=True, slots=True)
@@ -50,20 +64,9 @@ class GuidanceConfig:
     end_fraction: float = 1.0
 
     def __post_init__(self) -> None:
-        for name in ("scale", "min_scale", "text_scale", "video_scale", "audio_scale", "schedule_power"):
-            _positive(name, getattr(self, name))
-        if not (math.isfinite(self.rescale) and 0.0 <= self.rescale <= 1.0):
-            raise ValueError(f"rescale must be in [0, 1]; got {self.rescale!r}")
-        if not math.isfinite(self.projection_eta):
-            raise ValueError(f"projection_eta must be finite; got {self.projection_eta!r}")
-        if not (math.isfinite(self.projection_threshold) and self.projection_threshold >= 0.0):
-            raise ValueError(f"projection_threshold must be non-negative; got {self.projection_threshold!r}")
-        if self.schedule not in _SCHEDULES:
+        enforce(self, _GUIDANCE_LIMITS)
+        if self.schedule not in _SCHEDULE_WEIGHT:
             raise ValueError(f"unknown guidance schedule {self.schedule!r}; choose from {', '.join(_SCHEDULES)}")
-        for name in ("start_fraction", "end_fraction"):
-            v = getattr(self, name)
-            if not (math.isfinite(v) and 0.0 <= v <= 1.0):
-                raise ValueError(f"{name} must be in [0, 1]; got {v!r}")
         if self.start_fraction >= self.end_fraction:
             raise ValueError("start_fraction must be below end_fraction")
 
@@ -76,15 +79,11 @@ class GuidanceConfig:
         if not (math.isfinite(progress) and 0.0 <= progress <= 1.0):
             raise ValueError(f"progress must be in [0, 1]; got {progress!r}")
         if self.schedule == "constant":
-            return self.scale
-        if self.schedule == "interval":
-            return self.scale if self.start_fraction <= progress <= self.end_fraction else self.min_scale
-        span = self.scale - self.min_scale
-        if self.schedule == "linear":
-            return self.scale - span * progress
-        if self.schedule == "cosine":
-            return self.min_scale + span * 0.5 * (1.0 + math.cos(math.pi * progress))
-        return self.min_scale + span * (1.0 - progress) ** self.schedule_power
+            return self.scale  # exactly, whatever min_scale says
+        weight = _SCHEDULE_WEIGHT[self.schedule](self, progress)
+        if weight in (0.0, 1.0):  # the end points exactly
+            return self.scale if weight else self.min_scale
+        return self.min_scale + (self.scale - self.min_scale) * weight
 
     def modality_scale(self, modality: str, progress: float = 0.0) -> float:
         if modality not in _MODALITIES:

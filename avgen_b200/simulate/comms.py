@@ -10,6 +10,9 @@ exceeds the attention time of that layer is exposed.
 """
 from __future__ import annotations
 
+import functools
+import math
+
 import contextlib
 from collections.abc import Callable
 from dataclasses import dataclass
@@ -67,6 +70,7 @@ class CollectiveCost:
     tier: str
     seconds: float
     overlappable_with: float = 0.0  # seconds of compute this collective can hide under
+    synchronising: bool = False  # a wait for the slowest rank: never hidden under compute
 
 
 def _wire(kind: str, payload: float, ranks: int) -> float:
@@ -95,7 +99,9 @@ class CommunicationEstimate:
         exposed = 0.0
         general = 0.0
         for c in self.collectives:
-            if c.overlappable_with > 0:  # fused with its compute: only the excess is exposed
+            if c.synchronising:
+                exposed += c.seconds
+            elif c.overlappable_with > 0:  # fused with its compute: only the excess is exposed
                 exposed += max(0.0, c.seconds - c.overlappable_with)
             else:
                 general += c.seconds
@@ -167,7 +173,40 @@ def estimate_step_communication(shape: ModelShape, dims: Any, *, intra_node: Int
     if dims.pp_enabled:
         boundary = shape.micro_batch_size * seq * shape.width * param_dtype_bytes
         add("pipeline.p2p", "all_gather", boundary, 2, dims.pipeline - 1)
+    if dims.cp_enabled and compute_seconds > 0:
+        # The ring's per-block barriers (K/V readiness before each block's attention,
+        # dK/dV arrival after its backward) wait for the slowest rank of the ranks that
+        # step together: the expected maximum of their block-time jitter.
+        ranks = dims.context * (dims.dp_shard if dims.dp_shard_enabled else 1)
+        per_block_seconds = compute_seconds / depth
+        wait = RING_SKEW_FRACTION * per_block_seconds * expected_max_normal(ranks)
+        items.append(CollectiveCost("context_parallel.rank_skew", "barrier", 0.0, 0.0, ranks, 2 * depth,
+                                    intra_node.name, wait * 2 * depth, synchronising=True))
     return CommunicationEstimate(tuple(items), compute_seconds, overlap_efficiency)
+
+
+# Standard deviation of one block's time across ranks, as a fraction of the block
+# time, fitted to the barrier waits this framework measured on B200 at cp=2 and at
+# dp_shard 2 x cp 4 (``measured_b200.json``).
+RING_SKEW_FRACTION = 0.013
+
+@functools.lru_cache(maxsize=256)
+def expected_max_normal(n: int) -> float:
+    """Expected maximum of ``n`` independent standard normal draws,
+    ``integral x n phi(x) Phi(x)^(n-1) dx``, by the trapezoid rule on [-9, 9]
+    (0 for n <= 1; 0.5642 for 2, 1.0294 for 4, 1.4236 for 8)."""
+    if n <= 1:
+        return 0.0
+    steps, lo, hi = 6000, -9.0, 9.0
+    h = (hi - lo) / steps
+    total = 0.0
+    for i in range(steps + 1):
+        x = lo + i * h
+        pdf = math.exp(-0.5 * x * x) / math.sqrt(2.0 * math.pi)
+        cdf = 0.5 * (1.0 + math.erf(x / math.sqrt(2.0)))
+        w = 0.5 if i in (0, steps) else 1.0
+        total += w * x * n * pdf * cdf ** (n - 1)
+    return total * h
 
 
 def count_collectives(step: Callable[[], Any], *, trace_file: str | None = None) -> dict[str, Any]:

@@ -1,8 +1,9 @@
 """The analytic simulator against this framework's measured B200 step times for the
 flagship model (1, 2 and 8 GPUs): the predicted step stays within 15 % of the
-measurement, and the predicted exposed communication stays below the measured one
-(the model counts wire time, not rank skew), so a cost-model change that drifts
-away from the hardware fails here."""
+measurement and the predicted exposed communication (wire time the overlap does
+not hide plus the ring barriers' wait for the slowest rank) within a factor of
+two of the measured one, so a cost-model change that drifts away from the
+hardware fails here."""
 from __future__ import annotations
 
 import json
@@ -26,4 +27,12 @@ def test_simulated_step_tracks_the_measured_step(run: dict) -> None:
     predicted_ms = report.step_seconds * 1e3
     assert abs(predicted_ms / run["ms_per_step"] - 1.0) < 0.15, (predicted_ms, run["ms_per_step"])
     exposed_ms = report.communication.exposed_seconds * 1e3 * accumulation
-    assert exposed_ms <= run["exposed_comm_ms"] + 1.0, (exposed_ms, run["exposed_comm_ms"])
+    measured = run["exposed_comm_ms"]
+    assert measured / 2 - 1.0 <= exposed_ms <= 2 * measured + 1.0, (exposed_ms, measured)
+
+
+@pytest.mark.parametrize("n,want", [(1, 0.0), (2, 0.5642), (3, 0.8463), (4, 1.0294), (8, 1.4236), (16, 1.7660)])
+def test_expected_normal_maximum(n: int, want: float) -> None:
+    from avgen_b200.simulate.comms import expected_max_normal
+
+    assert expected_max_normal(n) == pytest.approx(want, abs=2e-4)

@@ -10,3 +10,7 @@ __all__ = ["CHECKPOINT_DIR_PREFIX", "CHECKPOINT_FORMAT_VERSION", "DEFAULT_MAX_SH
            "INDEX_FILENAME", "MARKER_FILENAME", "MODEL_OPTIMIZER_KEY", "PROGRESS_KEY", "RNG_KEY", "SCHEDULE_KEY",
            "WEIGHTS_FILENAME", "CheckpointEntry", "CheckpointManager", "build_stateful", "convert",
            "export_huggingface", "export_safetensors", "import_safetensors", "load", "load_ema", "load_model", "save"]
+
+from avgen_b200.checkpoint.stateful import ExtrasState, ModelOptimizerState, ProgressState, RNGState  # noqa: E402
+
+__all__ += ["ExtrasState", "ModelOptimizerState", "ProgressState", "RNGState"]

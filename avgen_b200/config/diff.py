@@ -10,7 +10,7 @@ import yaml
 
 from avgen_b200.config.schema import RunConfig
 
-__all__ = ["config_diff", "config_to_dict", "render_diff", "save_config"]
+__all__ = ["config_diff", "config_to_dict", "format_diff", "render_diff", "save_config", "to_mapping"]
 
 
 def _plain(value: Any) -> Any:
@@ -24,6 +24,12 @@ def _plain(value: Any) -> Any:
 
 
 def config_to_dict(config: RunConfig) -> dict[str, Any]:
+    return _plain(config)
+
+
+def to_mapping(config: Any) -> Any:
+    """Any config dataclass (or container of them) as plain lists and dicts, which
+    ``yaml.safe_dump`` writes and :func:`load_config` reads back unchanged."""
     return _plain(config)
 
 
@@ -56,7 +62,16 @@ def config_diff(a: RunConfig | Mapping[str, Any], b: RunConfig | Mapping[str, An
 
 
 def render_diff(diff: Mapping[str, tuple[Any, Any]]) -> str:
-    if not diff:
+    return format_diff(diff)
+
+
+def format_diff(differences: Mapping[str, tuple[Any, Any]], *, left_name: str = "a", right_name: str = "b") -> str:
+    """One aligned line per differing key, ``key  left -> right``, under a header
+    naming the two sides when they are not the default ``a`` / ``b``."""
+    if not differences:
         return "(no differences)"
-    width = max(len(k) for k in diff)
-    return "\n".join(f"{k.ljust(width)}  {a!r} -> {b!r}" for k, (a, b) in diff.items())
+    width = max(len(k) for k in differences)
+    lines = [f"{k.ljust(width)}  {a!r} -> {b!r}" for k, (a, b) in differences.items()]
+    if (left_name, right_name) != ("a", "b"):
+        lines.insert(0, f"{''.ljust(width)}  {left_name} -> {right_name}")
+    return "\n".join(lines)

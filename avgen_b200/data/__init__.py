@@ -23,3 +23,7 @@ __all__ = [
     "largest_remainder", "pack_streams", "plan_clip_spec", "plan_packing", "probe_clip", "random_batch",
     "split_packed", "summarise_reports", "tensor_fingerprint", "validate_shard", "write_shard",
 ]
+
+from avgen_b200.data.ingest import iter_clip_table  # noqa: E402
+
+__all__ += ["iter_clip_table"]

@@ -17,3 +17,7 @@ __all__ = ["DEFAULT_TARGET_MODULES", "AdapterHandles", "ControlAdapter", "Contro
            "load_adapter", "lora_modules", "lora_parameters", "mark_only_lora_trainable", "merge_lora",
            "register_stage", "run_finetune", "save_adapter", "stage_names_for", "standard_stages",
            "trainable_summary", "unmerge_lora"]
+
+from avgen_b200.finetune.stages import resolution_shift, shift_timesteps  # noqa: E402
+
+__all__ += ["resolution_shift", "shift_timesteps"]

@@ -14,3 +14,13 @@ __all__ = [
     "build_model", "build_rotary_tables", "device_arch", "key_padding_mask", "list_models", "list_presets",
     "model_config_class", "modulate", "preset", "register_model", "sinusoidal_embedding", "temporal_neighbour_mask",
 ]
+
+# constants and helpers the reference also exports at this level
+from avgen_b200.models.attention import attention_backends, sdpa_context  # noqa: E402
+from avgen_b200.models.dit import FUSION_MODES  # noqa: E402
+from avgen_b200.models.layers import MODULATION_CHUNKS, init_linear, init_norm, rms_norm  # noqa: E402
+from avgen_b200.models.registry import MODEL_ENTRY_POINT_GROUP  # noqa: E402
+from avgen_b200.models.rope import ROPE_SCALING_MODES, rope_axis_pairs  # noqa: E402
+
+__all__ += ["FUSION_MODES", "MODEL_ENTRY_POINT_GROUP", "MODULATION_CHUNKS", "ROPE_SCALING_MODES", "attention_backends",
+            "init_linear", "init_norm", "rms_norm", "rope_axis_pairs", "sdpa_context"]

@@ -14,7 +14,8 @@ import math
 
 import torch
 
-__all__ = ["FlashAttention", "attention", "device_arch", "key_padding_mask", "reference_attention"]
+__all__ = ["FlashAttention", "attention", "attention_backends", "device_arch", "key_padding_mask",
+           "reference_attention", "sdpa_context"]
 
 _ARCH_BY_MAJOR = ((10, "blackwell"), (9, "hopper"), (8, "ampere"), (0, "legacy"))
 
@@ -74,6 +75,39 @@ class FlashAttention(torch.autograd.Function):
         dq, dk, dv = K.attention_bwd(qb, kb, vb, out, dout.to(torch.bfloat16).contiguous(), lse,
                                      kmask=packed if ctx.has_mask else None, scale=ctx.scale)
         return dq.to(ctx.dtypes[0]), dk.to(ctx.dtypes[1]), dv.to(ctx.dtypes[2]), None, None
+
+
+def attention_backends(device: torch.device | str | None = None, *, allow_flash: bool = True) -> tuple:
+    """Priority list of ``torch.nn.functional.scaled_dot_product_attention`` backends for
+    SDPA calls made outside this framework's kernels (user code, plugins): cuDNN first
+    on Blackwell and Hopper, then flash, memory-efficient and math; math alone on the
+    CPU. The framework's own attention never calls SDPA (see :func:`attention`)."""
+    from torch.nn.attention import SDPBackend
+
+    if device_arch(device) == "cpu":
+        return (SDPBackend.MATH,)
+    order = [SDPBackend.CUDNN_ATTENTION, SDPBackend.FLASH_ATTENTION, SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]
+    if device_arch(device) not in ("blackwell", "hopper"):
+        order.remove(SDPBackend.CUDNN_ATTENTION)
+    if not allow_flash:
+        order.remove(SDPBackend.FLASH_ATTENTION)
+    return tuple(order)
+
+
+def sdpa_context(device: torch.device | str | None = None, *, backends=None):  # noqa: ANN001, ANN201
+    """A context pinning SDPA's backend priority (``backends`` or
+    :func:`attention_backends`) on CUDA; a no-op on the CPU, which has one kernel."""
+    import contextlib
+
+    if device_arch(device) == "cpu":
+        return contextlib.nullcontext()
+    from torch.nn.attention import sdpa_kernel
+
+    chosen = list(backends) if backends is not None else list(attention_backends(device))
+    try:
+        return sdpa_kernel(chosen, set_priority=True)
+    except TypeError:  # builds without priority ordering take the set only
+        return sdpa_kernel(chosen)
 
 
 def reference_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, key_mask: torch.Tensor | None,

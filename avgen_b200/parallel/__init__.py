@@ -28,3 +28,8 @@ __all__ = [
     "shutdown_distributed", "split_model", "stage_for_rank", "standard_block_plan", "standard_root_plan", "submesh",
     "summarize_sharding", "unwrap_model",
 ]
+
+from avgen_b200.parallel.activation import ACMode  # noqa: E402
+from avgen_b200.parallel.tensor import TensorParallelizable, TensorParallelPlan  # noqa: E402
+
+__all__ += ["ACMode", "TensorParallelPlan", "TensorParallelizable"]

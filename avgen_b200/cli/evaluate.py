@@ -23,7 +23,7 @@ __all__ = ["add_parser", "run"]
 
 
 def add_parser(subparsers: Any) -> None:
-    p = subparsers.add_parser("evaluate", help="evaluate a checkpoint and write a pinned report",
+    p = subparsers.add_parser("evaluate", aliases=["eval"], help="evaluate a checkpoint and write a pinned report",
                               description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--checkpoint", metavar="PATH", default="")
     p.add_argument("--config", metavar="PATH", default="", help="run config (default: config.yaml beside it)")

@@ -102,3 +102,8 @@ def test_unknown_command_and_help(capsys: pytest.CaptureFixture[str]) -> None:
     assert main(["frobnicate"]) == 2
     assert main(["--help"]) == 0
     assert "exit codes" in capsys.readouterr().out
+
+
+def test_eval_is_an_alias_of_evaluate(capsys: pytest.CaptureFixture[str]) -> None:
+    assert main(["eval", "--help"]) == 0  # the reference's subcommand name
+    assert capsys.readouterr().out.startswith("usage: avgen-b200 evaluate")

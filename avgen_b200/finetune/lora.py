@@ -25,6 +25,7 @@ from pathlib import Path
 from typing import Any
 
 import torch
+import torch.distributed as dist
 import torch.nn.functional as F
 from torch import nn
 
@@ -161,6 +162,9 @@ class LoRALinear(nn.Linear):
             m.reset_dora_magnitude()
         for name in ("_forward_hooks", "_forward_pre_hooks"):  # keep tensor-parallel hooks of the base layer
             getattr(m, name).update(getattr(linear, name))
+        shard = getattr(linear, "_avgen_tp_shard", None)
+        if shard is not None:
+            _take_head_shard(m, linear, shard)
         return m
 
     def reset_lora_parameters(self, init: str = "kaiming") -> None:
@@ -234,6 +238,54 @@ class LoRALinear(nn.Linear):
     def extra_repr(self) -> str:
         kind = "dora" if self.lora_magnitude is not None else "lora"
         return f"{super().extra_repr()}, {kind}_rank={self.rank}, alpha={self.alpha}, merged={self.merged}"
+
+
+def _take_head_shard(m: LoRALinear, linear: nn.Linear, shard: tuple[int, list[int], int]) -> None:
+    """Adapters on a head-parallel shard (a plain-tensor slice of the full weight, made
+    by :mod:`avgen_b200.parallel.heads`), mirroring the DTensor layout above: the factor
+    on the sharded side (B and the DoRA magnitude of a column-parallel layer, A of a
+    row-parallel one) is this rank's slice and is gathered into the full tensor in
+    checkpoints like the base weight; the other factor is replicated, and its gradient,
+    each rank's partial sum of the full one, is summed over the tensor-parallel group."""
+    from avgen_b200.parallel.heads import gather_slices, local_slice, tp_shard_group
+
+    dim, sizes, full = shard
+    if dim == 1 and m.lora_magnitude is not None:
+        raise NotImplementedError("DoRA on a row-parallel head shard needs its row norms summed over the group; "
+                                  "use LoRA there or DoRA without head-parallel tensor parallelism")
+    group = tp_shard_group(linear.weight)
+    rank = dist.get_rank(group)
+    m._avgen_tp_shard = shard
+    sharded = {"lora_b": 0, "lora_magnitude": 0} if dim == 0 else {"lora_a": 1}
+    replicated = m.lora_a if dim == 0 else m.lora_b
+    for name in sharded:
+        t = getattr(m, name, None)
+        if isinstance(t, torch.Tensor):
+            t._avgen_tp_group = group  # type: ignore[attr-defined]
+
+    def summed(grad: torch.Tensor, _group: Any = group) -> torch.Tensor:
+        grad = grad.clone()
+        dist.all_reduce(grad, group=_group)
+        return grad
+
+    replicated.register_hook(summed)
+    for name in ("_state_dict_hooks", "_load_state_dict_pre_hooks"):  # the base weight's full-tensor hooks
+        getattr(m, name).update(getattr(linear, name))
+
+    def save_full(module: nn.Module, state: dict, prefix: str, _meta: Any) -> None:
+        for name, d in sharded.items():
+            t = state.get(prefix + name)
+            if t is not None:
+                state[prefix + name] = gather_slices(t, d, sizes, group)
+
+    def load_local(state: dict, prefix: str, *_args: Any) -> None:
+        for name, d in sharded.items():
+            t = state.get(prefix + name)
+            if t is not None and t.dim() > d and t.shape[d] == full:
+                state[prefix + name] = local_slice(t, d, sizes, rank)
+
+    m._register_state_dict_hook(save_full)
+    m._register_load_state_dict_pre_hook(load_local)
 
 
 def _set_child(root: nn.Module, name: str, module: nn.Module) -> None:

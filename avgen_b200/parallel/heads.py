@@ -184,6 +184,25 @@ class HeadParallel:
 
 
 # --------------------------------------------------------------------------- sharding
+def gather_slices(t: torch.Tensor, dim: int, sizes: list[int], group: Any) -> torch.Tensor:
+    """Every rank's slice of a tensor split unevenly along ``dim`` (``sizes``, in rank
+    order), concatenated into the full tensor on every rank (collective)."""
+    biggest = max(sizes)
+    pad = list(t.shape)
+    pad[dim] = biggest
+    padded = torch.zeros(pad, dtype=t.dtype, device=t.device)
+    padded.narrow(dim, 0, t.shape[dim]).copy_(t)
+    parts = [torch.empty_like(padded) for _ in sizes]
+    dist.all_gather(parts, padded, group=group)
+    return torch.cat([part.narrow(dim, 0, n) for part, n in zip(parts, sizes)], dim)
+
+
+def local_slice(t: torch.Tensor, dim: int, sizes: list[int], rank: int) -> torch.Tensor:
+    """This rank's slice of a full tensor split along ``dim`` as ``sizes``."""
+    start, length = _span(sizes, rank)
+    return t.narrow(dim, start, length)
+
+
 def _keep(linear: nn.Linear, dim: int, sizes: list[int], tp: HeadParallel) -> None:
     """Replace ``linear``'s weight (and bias along dim 0) by this rank's slice of ``sizes``
     (every rank's extent along ``dim``, the same list on every rank), and make its
@@ -214,23 +233,15 @@ def _keep(linear: nn.Linear, dim: int, sizes: list[int], tp: HeadParallel) -> No
             t = state.get(key)
             if t is None or (name == "bias" and d != 0):
                 continue
-            biggest = max(all_sizes)
-            pad = list(t.shape)
-            pad[d] = biggest
-            padded = torch.zeros(pad, dtype=t.dtype, device=t.device)
-            padded.narrow(d, 0, t.shape[d]).copy_(t)
-            parts = [torch.empty_like(padded) for _ in all_sizes]
-            dist.all_gather(parts, padded, group=tp.group)
-            state[key] = torch.cat([p.narrow(d, 0, n) for p, n in zip(parts, all_sizes)], d)
+            state[key] = gather_slices(t, d, all_sizes, tp.group)
 
     def load_local(state: dict, prefix: str, *_args: Any) -> None:
         d, all_sizes, full_size = linear._avgen_tp_shard
-        lo, n = _span(all_sizes, tp.rank)
         for name in ("weight", "bias"):
             key = prefix + name
             t = state.get(key)
             if t is not None and t.dim() > d and t.shape[d] == full_size and (name == "weight" or d == 0):
-                state[key] = t.narrow(d, lo, n)
+                state[key] = local_slice(t, d, all_sizes, tp.rank)
 
     linear._register_state_dict_hook(save_full)
     linear._register_load_state_dict_pre_hook(load_local)

@@ -723,3 +723,55 @@ def _sp_validation_worker(rank: int, world: int) -> None:
 
 def test_sequence_parallel_argument_checks() -> None:
     _spawn(_sp_validation_worker)
+
+
+def _tp_cp_worker(rank: int, world: int, sequence_parallel: bool) -> None:
+    """Tensor parallelism by heads (3 heads over 2 ranks, uneven) inside context
+    parallelism (2 sequence shards) on 4 ranks: the gathered output and every gradient
+    (summed over the cp shards, this rank's slice of head-sharded weights) match the
+    unsharded model."""
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PrecisionConfig, gather_tokens, parallelize, shard_stream
+
+    def model3():  # noqa: ANN202 - 3 heads: an uneven [2, 1] split over tp=2
+        from avgen_b200.models import build_model, preset
+
+        torch.manual_seed(0)
+        cfg = {k: v for k, v in asdict(preset("tiny")).items() if k != "rope_scaling"}
+        cfg.update(num_heads=3, width=48)
+        m = build_model("video_dit", cfg)
+        m.init_weights()
+        with torch.no_grad():
+            for p in m.parameters():
+                p.add_(0.02 * torch.randn_like(p))
+        return m
+
+    ref = model3()
+    inputs = _inputs(31, ref)
+    want = ref(inputs)
+    _loss(want).backward()
+    ref_grads = {n: p.grad for n, p in ref.named_parameters()}
+    dims = ParallelDims(world_size=world, tensor=2, context=2)
+    cfg = ParallelConfig(precision=PrecisionConfig(param_dtype="float32"), shard_parameters=False,
+                         sequence_parallel=sequence_parallel)
+    pm = parallelize(model3(), dims, mesh=dims.build_mesh("cpu"), config=cfg)
+    local = inputs.replace_streams(video=shard_stream(inputs.video, pm.cp_mesh))
+    out = pm.model(local)
+    torch.testing.assert_close(gather_tokens(out.video.detach(), pm.cp_mesh), want.video.detach(), rtol=1e-4,
+                               atol=1e-5)
+    _loss(out).backward()
+    modules = dict(pm.model.named_modules())
+    tp_rank = pm.submesh("tp").get_local_rank()
+    for name, p in pm.model.named_parameters():
+        g = p.grad.clone()
+        dist.all_reduce(g, group=pm.cp_mesh.get_group())  # each cp shard holds a partial loss
+        want_g = ref_grads[name]
+        shard = getattr(modules[name.rsplit(".", 1)[0]], "_avgen_tp_shard", None)
+        if shard is not None and (name.endswith("weight") or shard[0] == 0):
+            dim, sizes, _ = shard
+            want_g = want_g.narrow(dim, sum(sizes[:tp_rank]), sizes[tp_rank])
+        torch.testing.assert_close(g, want_g, rtol=1e-3, atol=1e-5, msg=name)
+
+
+@pytest.mark.parametrize("sequence_parallel", [False, True], ids=["tp_cp", "tp_sp_cp"])
+def test_tensor_inside_context_parallel(sequence_parallel: bool) -> None:
+    _spawn(_tp_cp_worker, 4, sequence_parallel)

@@ -17,7 +17,7 @@ from torch.distributed.device_mesh import DeviceMesh
 from avgen_b200.parallel.dims import submesh
 
 __all__ = ["all_gather_object", "all_reduce_max", "all_reduce_mean", "all_reduce_sum", "broadcast_object",
-           "clip_grad_norm", "data_mesh", "gather_object"]
+           "clip_grad_norm", "data_mesh", "gather_object", "global_grad_norm"]
 
 
 def data_mesh(mesh: DeviceMesh | None) -> DeviceMesh | None:
@@ -59,6 +59,16 @@ def all_reduce_mean(value: torch.Tensor, mesh: DeviceMesh | None) -> torch.Tenso
 def clip_grad_norm(parameters: Iterable[torch.nn.Parameter], max_norm: float, *, pp_mesh: DeviceMesh | None = None,
                    foreach: bool = True, error_if_nonfinite: bool = False) -> torch.Tensor:
     """Clip by the global L2 norm (DTensor shards reduced, PP stages summed)."""
+    params = [p for p in parameters if p.grad is not None]
+    total = global_grad_norm(params, pp_mesh=pp_mesh, foreach=foreach, error_if_nonfinite=error_if_nonfinite)
+    torch.nn.utils.clip_grads_with_norm_(params, max_norm, total, foreach=foreach)
+    return total
+
+
+def global_grad_norm(parameters: Iterable[torch.nn.Parameter], *, pp_mesh: DeviceMesh | None = None,
+                     foreach: bool = True, error_if_nonfinite: bool = False) -> torch.Tensor:
+    """The L2 norm of the whole model's gradient: DTensor shards reduced, head-parallel
+    slices' squares summed over their group, pipeline stages' squares summed."""
     from torch.distributed.tensor import DTensor
 
     from avgen_b200.parallel.heads import tp_shard_group
@@ -83,7 +93,6 @@ def clip_grad_norm(parameters: Iterable[torch.nn.Parameter], max_norm: float, *,
         sq = total.pow(2)
         dist.all_reduce(sq, op=dist.ReduceOp.SUM, group=pp_mesh.get_group())
         total = sq.sqrt()
-    torch.nn.utils.clip_grads_with_norm_(params, max_norm, total, foreach=foreach)
     return total
 
 

@@ -462,8 +462,9 @@ def apply_context_parallel(model: torch.nn.Module, mesh: DeviceMesh | None, *, r
         if isinstance(module, SelfAttention):
             module.cp_mesh = mesh
     model.cp_mesh = mesh
-    # text-refiner self-attention runs on replicated text tokens: keep it local
-    for refiner in getattr(model, "text_refiner", []):
+    # text-refiner self-attention runs on replicated text tokens: keep it local (a
+    # pipeline stage without the embedding holds no refiner)
+    for refiner in getattr(model, "text_refiner", None) or []:
         refiner.attention.cp_mesh = None
     return model
 

@@ -191,7 +191,7 @@ def _host_clip_and_step(state: TrainState, max_grad_norm: float | None, pp_mesh:
     device (no collective decides it), step."""
     import torch.distributed as dist
 
-    from avgen_b200.parallel.comm import clip_grad_norm
+    from avgen_b200.parallel.comm import clip_grad_norm, global_grad_norm
 
     params = [p for p in state.model.parameters() if p.grad is not None]
     if not params:
@@ -204,8 +204,8 @@ def _host_clip_and_step(state: TrainState, max_grad_norm: float | None, pp_mesh:
             p.grad.div_(world)
     if max_grad_norm is not None:
         norm = clip_grad_norm(params, max_grad_norm, pp_mesh=pp_mesh)
-    else:
-        norm = torch.nn.utils.get_total_norm([p.grad for p in params], norm_type=2.0, error_if_nonfinite=False)
+    else:  # still the whole model's norm (stages and head-parallel slices), only not clipped
+        norm = global_grad_norm(params, pp_mesh=pp_mesh)
     norm = norm.to(torch.float32)
     finite = finite & torch.isfinite(norm)
     with torch.no_grad():

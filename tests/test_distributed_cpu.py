@@ -775,3 +775,46 @@ def _tp_cp_worker(rank: int, world: int, sequence_parallel: bool) -> None:
 @pytest.mark.parametrize("sequence_parallel", [False, True], ids=["tp_cp", "tp_sp_cp"])
 def test_tensor_inside_context_parallel(sequence_parallel: bool) -> None:
     _spawn(_tp_cp_worker, 4, sequence_parallel)
+
+
+def _pp_cp_worker(rank: int, world: int) -> None:
+    """Two pipeline stages, each over two context-parallel ranks (4 ranks): one 1F1B
+    optimizer step over 2 micro-batches matches the unsharded model's loss and
+    gradient norm with gradient accumulation."""
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PipelineConfig, PrecisionConfig, parallelize
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                                  build_timestep_sampler, train_step)
+    from avgen_b200.train.trainer import pipeline_train_step
+
+    ref = _model()
+    dims = ParallelDims(world_size=world, pipeline=2, context=2)
+    pm = parallelize(_model(), dims, mesh=dims.build_mesh("cpu"),
+                     config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32"), shard_parameters=False,
+                                           pipeline=PipelineConfig(schedule="1f1b")))
+    objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("uniform"), MultiTaskConditioning())
+    state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-2),
+                       rng=RNGStreams.for_rank(0, data_rank=0))
+    ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    c = ref.config
+    gen = torch.Generator().manual_seed(5)
+    micro = [random_batch(batch=1, channels=c.in_channels, frames=2, height=8, width=8, text_tokens=4,
+                          text_width=c.text_width, generator=gen) for _ in range(2)]
+    _, metrics = pipeline_train_step(state, micro, objective, pm.pipeline, patchifier=ref.patchifier,
+                                     max_grad_norm=None, pp_mesh=pm.pp_mesh, cp_mesh=pm.cp_mesh,
+                                     data_group=pm.data_group)  # replicated parameters: gradients summed over cp
+    losses = []
+    for i, b in enumerate(micro):
+        _, rm = train_step(ref_state, b, objective, patchifier=ref.patchifier, gradient_accumulation_steps=2,
+                           microbatch_index=i, max_grad_norm=None)
+        losses.append(float(rm.loss))
+    loss = metrics.loss.detach().reshape(1).clone()
+    dist.all_reduce(loss, group=pm.cp_mesh.get_group())  # each cp rank reports its shard's share
+    assert abs(float(loss) / 2 - sum(losses) / 2) <= 1e-4 * max(1.0, abs(sum(losses))), (float(loss), losses)
+    assert abs(float(metrics.grad_norm) - float(rm.grad_norm)) <= 1e-3 * float(rm.grad_norm), (
+        float(metrics.grad_norm), float(rm.grad_norm))
+
+
+def test_pipeline_over_context_parallel_stages() -> None:
+    _spawn(_pp_cp_worker, 4)

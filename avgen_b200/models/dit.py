@@ -261,7 +261,22 @@ class VideoDiT(nn.Module):
         a = inputs.audio
         return torch.zeros((a.batch_size, a.length, a.layout.patch_dim), dtype=like.dtype, device=like.device)
 
-    def forward(self, inputs: ModelInput) -> ModelOutput:
+    def forward(self, inputs: ModelInput, *, stage: str | None = None, hidden: torch.Tensor | None = None,
+                carry: tuple[Any, ...] | None = None, aux: dict[str, Any] | None = None) -> Any:
+        """The whole model, or one pipeline part through the module call so that hooks on
+        the root module (FSDP2's lazy initialisation and parameter gathering among them)
+        run for it: ``stage="embed"`` is ``stage_embed(inputs)``, ``stage="blocks"`` is
+        ``stage_blocks(*carry, aux)``, ``stage="head"`` is ``stage_head(hidden, inputs)``."""
+        if stage == "embed":
+            return self.stage_embed(inputs)
+        if stage == "blocks":
+            assert carry is not None and aux is not None, "the blocks stage takes the carry and its inputs"
+            return self.stage_blocks(*carry, aux)
+        if stage == "head":
+            assert hidden is not None, "the head stage takes the blocks' output"
+            return self.stage_head(hidden, inputs)
+        if stage is not None:
+            raise ValueError(f"stage must be None, 'embed', 'blocks' or 'head'; got {stage!r}")
         hidden, context, modulation = self.stage_embed(inputs)
         hidden = self.stage_blocks(hidden, context, modulation, self.stage_inputs(inputs))
         return self.stage_head(hidden, inputs)

@@ -243,7 +243,7 @@ class PipelineRunner:
                  loss_fn: Callable[[int, Any], torch.Tensor]) -> tuple[Any, Any]:
         """Returns (what backward starts from, this micro-batch's received leaves)."""
         if self.first:
-            carry = _Carry(*self.model.stage_embed(inputs))
+            carry = _Carry(*self.model(inputs, stage="embed"))
             leaves = None
         else:
             assert received is not None
@@ -252,9 +252,10 @@ class PipelineRunner:
             hidden = next(it)
             context = next(it) if self._has_context(inputs) else None
             carry = _Carry(hidden, context, next(it))
-        hidden = self.model.stage_blocks(carry.hidden, carry.context, carry.modulation, self.model.stage_inputs(inputs))
+        hidden = self.model(inputs, stage="blocks", carry=(carry.hidden, carry.context, carry.modulation),
+                            aux=self.model.stage_inputs(inputs))
         if self.last:
-            return loss_fn(k, self.model.stage_head(hidden, inputs)), leaves
+            return loss_fn(k, self.model(inputs, stage="head", hidden=hidden)), leaves
         return _Carry(hidden, carry.context, carry.modulation), leaves
 
     def _has_context(self, inputs: Any) -> bool:
@@ -557,7 +558,7 @@ class InterleavedPipelineRunner(PipelineRunner):
     def _chunk_forward(self, g: int, j: int, k: int, inputs: Any, received: list[torch.Tensor] | None,
                        loss_fn: Callable[[int, Any], torch.Tensor], last: int) -> tuple[Any, Any]:
         if g == 0:
-            carry = _Carry(*self.model.stage_embed(inputs))
+            carry = _Carry(*self.model(inputs, stage="embed"))
             leaves = None
         else:
             assert received is not None, f"chunk {g}: no carry arrived for micro-batch {k}"
@@ -567,7 +568,7 @@ class InterleavedPipelineRunner(PipelineRunner):
             context = next(it) if self._has_context(inputs) else None
             carry = _Carry(hidden, context, next(it))
         aux = dict(self.model.stage_inputs(inputs), blocks=self.model.pipeline_chunks[j])
-        hidden = self.model.stage_blocks(carry.hidden, carry.context, carry.modulation, aux)
+        hidden = self.model(inputs, stage="blocks", carry=(carry.hidden, carry.context, carry.modulation), aux=aux)
         if g == last:
-            return loss_fn(k, self.model.stage_head(hidden, inputs)), leaves
+            return loss_fn(k, self.model(inputs, stage="head", hidden=hidden)), leaves
         return _Carry(hidden, carry.context, carry.modulation), leaves

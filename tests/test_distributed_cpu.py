@@ -818,3 +818,72 @@ def _pp_cp_worker(rank: int, world: int) -> None:
 
 def test_pipeline_over_context_parallel_stages() -> None:
     _spawn(_pp_cp_worker, 4)
+
+
+def _pp_combo_worker(rank: int, world: int, other: str) -> None:
+    """Two pipeline stages, each over two ranks of another layout (head-parallel TP with
+    sequence parallelism, or FSDP2 sharding): one clipped 1F1B optimizer step over 2
+    micro-batches matches the unsharded model's loss and gradient norm."""
+    from avgen_b200.core import RNGStreams, TrainState
+    from avgen_b200.data.synthetic_batch import random_batch
+    from avgen_b200.parallel import ParallelConfig, ParallelDims, PipelineConfig, PrecisionConfig, parallelize
+    from avgen_b200.train import (FlowMatchingConfig, FlowMatchingObjective, MultiTaskConditioning, build_optimizer,
+                                  build_timestep_sampler, train_step)
+    from avgen_b200.train.trainer import pipeline_train_step
+
+    def model3():  # noqa: ANN202 - 3 heads, 2 blocks
+        from avgen_b200.models import build_model, preset
+
+        torch.manual_seed(0)
+        cfg = {k: v for k, v in asdict(preset("tiny")).items() if k != "rope_scaling"}
+        cfg.update(num_heads=3, width=48)
+        m = build_model("video_dit", cfg)
+        m.init_weights()
+        with torch.no_grad():
+            for p in m.parameters():
+                p.add_(0.02 * torch.randn_like(p))
+        return m
+
+    ref = model3()
+    if other == "tp":
+        dims = ParallelDims(world_size=world, pipeline=2, tensor=2)
+        extra = {"sequence_parallel": True}
+    else:
+        dims = ParallelDims(world_size=world, pipeline=2, dp_shard=2)
+        extra = {}
+    pm = parallelize(model3(), dims, mesh=dims.build_mesh("cpu"),
+                     config=ParallelConfig(precision=PrecisionConfig(param_dtype="float32"),
+                                           pipeline=PipelineConfig(schedule="1f1b"), **extra))
+    objective = FlowMatchingObjective(FlowMatchingConfig(), build_timestep_sampler("uniform"), MultiTaskConditioning())
+    # micro-batch i draws its noise from the stream of data rank i, here and in the reference
+    data_rank = pm.submesh("dp_shard").get_local_rank() if other == "fsdp" else 0
+    state = TrainState(model=pm.model, optimizer=build_optimizer(pm.model, lr=1e-2),
+                       rng=RNGStreams.for_rank(0, data_rank=data_rank))
+    ref_state = TrainState(model=ref, optimizer=build_optimizer(ref, lr=1e-2), rng=RNGStreams.for_rank(0, data_rank=0))
+    c = ref.config
+    gen = torch.Generator().manual_seed(5)
+    micro = [random_batch(batch=1, channels=c.in_channels, frames=2, height=8, width=8, text_tokens=4,
+                          text_width=c.text_width, generator=gen) for _ in range(2)]
+    # the two data ranks of a stage see one sample each; the unsharded step sees both
+    mine = [micro[data_rank]] if other == "fsdp" else micro
+    _, metrics = pipeline_train_step(state, mine, objective, pm.pipeline, patchifier=ref.patchifier,
+                                     max_grad_norm=0.05, pp_mesh=pm.pp_mesh, data_group=pm.data_group)
+    losses = []
+    for i, b in enumerate(micro):
+        if other == "fsdp":
+            ref_state.rng = RNGStreams.for_rank(0, data_rank=i)
+        _, rm = train_step(ref_state, b, objective, patchifier=ref.patchifier, gradient_accumulation_steps=2,
+                           microbatch_index=i, max_grad_norm=0.05)
+        losses.append(float(rm.loss))
+    loss = metrics.loss.detach().reshape(1).clone()
+    if other == "fsdp":
+        dist.all_reduce(loss, group=pm.submesh("dp_shard").get_group())
+        loss /= 2
+    assert abs(float(loss) - sum(losses) / 2) <= 1e-4 * max(1.0, abs(sum(losses))), (float(loss), losses)
+    assert abs(float(metrics.grad_norm) - float(rm.grad_norm)) <= 1e-3 * float(rm.grad_norm), (
+        float(metrics.grad_norm), float(rm.grad_norm))
+
+
+@pytest.mark.parametrize("other", ["tp", "fsdp"])
+def test_pipeline_with_tensor_or_sharded_data_parallel_stages(other: str) -> None:
+    _spawn(_pp_combo_worker, 4, other)

@@ -106,100 +106,146 @@ class RolloutBatch:
         return int(self.sample_before.shape[0])
 
 
+def _need_group(group_size: int) -> None:
+    if group_size < 2:
+        raise ValueError(f"a GRPO group needs two or more samples to form a baseline (group_size={group_size})")
+
+
 def group_advantages(rewards: torch.Tensor, group_size: int, *, epsilon: float = 1e-4, normalize_by_std: bool = True,
                      clip: float | None = 5.0) -> torch.Tensor:
-    """``(r - mean_group) / (std_group + eps)`` per trajectory (population std), optionally clipped."""
-    if group_size < 2:
-        raise ValueError(f"group_size must be at least 2; got {group_size} (a group of one has no baseline)")
-    if rewards.numel() % group_size:
-        raise ValueError(f"reward count {rewards.numel()} is not a multiple of group_size={group_size}")
-    g = rewards.float().reshape(-1, group_size)
-    adv = g - g.mean(1, keepdim=True)
+    """``(r - mean_group) / (std_group + eps)`` per trajectory (population std), optionally clipped.
+
+    ``rewards`` lists the groups one after another (``group_size`` consecutive
+    entries share a prompt)."""
+    _need_group(group_size)
+    groups, rest = divmod(rewards.numel(), group_size)
+    if rest:
+        raise ValueError(f"{rewards.numel()} rewards do not split into groups of {group_size}")
+    g = rewards.float().reshape(groups, group_size)
+    centred = g - g.mean(1, keepdim=True)
     if normalize_by_std:
-        adv = adv / (g.std(1, unbiased=False, keepdim=True) + epsilon)
-    if clip is not None:
-        adv = adv.clamp(-clip, clip)
-    return adv.reshape(-1)
+        centred = centred / (g.std(1, unbiased=False, keepdim=True) + epsilon)
+    return (centred if clip is None else centred.clamp(-clip, clip)).reshape(-1)
 
 
-_STEP_KEYS = ("sample_before", "sample_after", "sigma", "sigma_next", "log_prob_old", "mean_old", "std_old",
-              "step_index")
+# per-sample fields of one stored transition, in RolloutBatch order
+_FIELDS = ("sample_before", "sample_after", "sigma", "sigma_next", "log_prob_old", "mean_old", "std_old")
 
 
 @dataclass(slots=True)
 class RolloutBuffer:
-    """Transitions of a group rollout (only steps inside the gradient window are stored)."""
+    """Window transitions of one group rollout, kept in step-major arenas on the rollout's device.
+
+    Every per-sample field is one tensor of shape ``[capacity, N, ...]``,
+    allocated when the first step is stored (``capacity`` is the number of
+    window steps when the caller knows it, as :func:`generate_group` does;
+    otherwise the arenas double when full). Storing a step is an in-place copy
+    into row ``len(self)``; a minibatch is one ``index_select`` per field from
+    the ``[steps * N]`` flat view. Flat row ``r`` is sample ``r % N`` at stored
+    step ``r // N``, so its advantage, prompt and step index come from ``r`` by
+    arithmetic: nothing is concatenated or repeated at update time, which would
+    otherwise hold a second copy of every latent the rollout kept.
+    """
 
     group_size: int
     prompts: tuple[str, ...] = ()
     rewards: torch.Tensor | None = None
     advantages: torch.Tensor | None = None
     media: torch.Tensor | None = None
-    _steps: list[dict[str, torch.Tensor]] = field(default_factory=list, repr=False)
+    capacity: int = 0
+    _arena: dict[str, torch.Tensor] = field(default_factory=dict, repr=False)
+    _step_ids: torch.Tensor | None = field(default=None, repr=False)
+    _count: int = field(default=0, repr=False)
 
     def __post_init__(self) -> None:
-        if self.group_size < 2:
-            raise ValueError(f"group_size must be at least 2; got {self.group_size}")
+        _need_group(self.group_size)
 
     def __len__(self) -> int:
-        return len(self._steps)
+        return self._count
 
     @property
     def num_samples(self) -> int:
-        return int(self._steps[0]["sample_before"].shape[0]) if self._steps else 0
+        return int(self._arena["sample_before"].shape[1]) if self._count else 0
+
+    def transitions(self, name: str) -> torch.Tensor:
+        """The stored ``[steps, N, ...]`` view of one field (``sample_before``, ``log_prob_old``, ...)."""
+        if name not in _FIELDS:
+            raise KeyError(f"unknown transition field {name!r}; fields are {', '.join(_FIELDS)}")
+        if not self._count:
+            raise RuntimeError("the buffer holds no transitions yet")
+        return self._arena[name][:self._count]
+
+    def _grow(self, values: dict[str, torch.Tensor]) -> None:
+        size = max(self.capacity, 2 * self._count, 1)
+        arena = {k: v.new_empty((size, *v.shape)) for k, v in values.items()}
+        ids = torch.empty(size, dtype=torch.int64, device=values["sample_before"].device)
+        if self._count:
+            for k, old in self._arena.items():
+                arena[k][:self._count].copy_(old[:self._count])
+            ids[:self._count].copy_(self._step_ids[:self._count])
+        self._arena, self._step_ids = arena, ids
 
     def add_step(self, *, step_index: int, sample_before: torch.Tensor, step: SDEStep, sigma: torch.Tensor,
                  sigma_next: torch.Tensor) -> None:
-        n = sample_before.shape[0]
-        self._steps.append({
-            "sample_before": sample_before.detach(), "sample_after": step.sample.detach(), "sigma": sigma.detach(),
-            "sigma_next": sigma_next.detach(), "log_prob_old": step.log_prob.detach(), "mean_old": step.mean.detach(),
-            "std_old": step.std.detach(),
-            "step_index": torch.full((n,), step_index, dtype=torch.int64, device=sample_before.device)})
+        values = dict(zip(_FIELDS, (sample_before, step.sample, sigma, sigma_next, step.log_prob, step.mean,
+                                    step.std)))
+        if self._count and values["sample_before"].shape[0] != self.num_samples:
+            raise ValueError(f"every stored step must cover the same {self.num_samples} samples; this one has "
+                             f"{values['sample_before'].shape[0]}")
+        if not self._arena or self._count == self._arena["sample_before"].shape[0]:
+            self._grow(values)
+        row = self._count
+        with torch.no_grad():
+            for k, v in values.items():
+                self._arena[k][row].copy_(v)
+        self._step_ids[row] = int(step_index)
+        self._count = row + 1
 
     def set_rewards(self, rewards: torch.Tensor, *, media: torch.Tensor | None) -> None:
         if rewards.numel() != self.num_samples:
-            raise ValueError(f"expected {self.num_samples} rewards to match the trajectories; got {rewards.numel()}")
-        self.rewards = rewards.detach().float()
-        self.media = media
+            raise ValueError(f"one reward per trajectory: the buffer holds {self.num_samples} trajectories, "
+                             f"{rewards.numel()} rewards were given")
+        self.rewards, self.media = rewards.detach().float().reshape(-1), media
 
     def compute_advantages(self, *, epsilon: float = 1e-4, normalize_by_std: bool = True,
                            clip: float | None = 5.0) -> torch.Tensor:
         if self.rewards is None:
-            raise RuntimeError("call set_rewards() before compute_advantages()")
+            raise RuntimeError("advantages need rewards: call set_rewards first")
         self.advantages = group_advantages(self.rewards, self.group_size, epsilon=epsilon,
                                            normalize_by_std=normalize_by_std, clip=clip)
         return self.advantages
 
     def iter_minibatches(self, batch_size: int, *, generator: torch.Generator | None = None,
                          shuffle: bool = True) -> Iterator[RolloutBatch]:
+        """Minibatches over every stored (step, sample) transition, shuffled by ``generator``'s draw."""
         if self.advantages is None:
-            raise RuntimeError("call compute_advantages() before iterating")
+            raise RuntimeError("minibatches need advantages: call compute_advantages first")
         if batch_size < 1:
-            raise ValueError(f"batch_size must be positive; got {batch_size}")
-        flat = self._flatten()
-        total = int(flat["sample_before"].shape[0])
-        order = torch.randperm(total, generator=generator) if shuffle else torch.arange(total)
-        order = order.to(flat["sample_before"].device)
-        for start in range(0, total, batch_size):
-            idx = order[start:start + batch_size]
-            yield RolloutBatch(**{k: v[idx] for k, v in flat.items()})
+            raise ValueError(f"batch_size must be at least 1 (got {batch_size})")
+        n, steps = self.num_samples, self._count
+        dev = self._arena["sample_before"].device
+        flat = {k: v[:steps].flatten(0, 1) for k, v in self._arena.items()}
+        advantages = self.advantages.to(dev)
+        order = torch.randperm(n * steps, generator=generator) if shuffle else torch.arange(n * steps)
+        for rows in order.to(dev).split(batch_size):
+            sample = rows % n
+            yield RolloutBatch(**{k: flat[k].index_select(0, rows) for k in _FIELDS},
+                               advantage=advantages.index_select(0, sample),
+                               prompt_index=sample // self.group_size,
+                               step_index=self._step_ids.index_select(0, rows // n))
 
-    def _flatten(self) -> dict[str, torch.Tensor]:
-        assert self.advantages is not None
-        dev = self._steps[0]["sample_before"].device
-        flat = {k: torch.cat([s[k] for s in self._steps]) for k in _STEP_KEYS}
-        reps = len(self._steps)
-        flat["advantage"] = self.advantages.to(dev).repeat(reps)
-        flat["prompt_index"] = (torch.arange(self.num_samples, device=dev) // self.group_size).repeat(reps)
-        return flat
+
+def _check_data_coordinates(data_rank: int, data_world: int) -> None:
+    if data_world < 1:
+        raise ValueError(f"data_world counts ranks and must be at least 1 (got {data_world})")
+    if not 0 <= data_rank < data_world:
+        raise ValueError(f"data_rank {data_rank} lies outside the {data_world} data ranks")
 
 
 def distribute_prompts(prompts: Sequence[str], *, data_rank: int, data_world: int,
                        ) -> tuple[tuple[str, ...], tuple[int, ...]]:
     """Strided prompt shard of one data rank: ``range(data_rank, N, data_world)``."""
-    if data_world < 1 or not 0 <= data_rank < data_world:
-        raise ValueError(f"invalid data coordinates: data_rank={data_rank}, data_world={data_world}")
+    _check_data_coordinates(data_rank, data_world)
     idx = tuple(range(data_rank, len(prompts), data_world))
     return tuple(prompts[i] for i in idx), idx
 
@@ -229,13 +275,13 @@ def generate_group(velocity_fn: VelocityFn, *, prompts: Sequence[str], group_siz
     Steps in ``gradient_steps`` (all steps if ``None``) take the SDE and are
     stored; the others take a deterministic ODE step and are not.
     """
-    if sigmas.ndim != 1 or sigmas.numel() < 2:
-        raise ValueError(f"sigmas must be a 1-D schedule with at least two entries; got {tuple(sigmas.shape)}")
-    if bool((sigmas[1:] > sigmas[:-1]).any()):
-        raise ValueError("sigmas must be non-increasing (1 = noise down to 0 = clean)")
+    if sigmas.ndim != 1 or sigmas.numel() < 2 or bool((sigmas[1:] > sigmas[:-1]).any()):
+        raise ValueError(f"sigmas must be one non-increasing run of two or more levels from noise (1) towards clean "
+                         f"(0); got shape {tuple(sigmas.shape)}")
     n_prompts, n_steps = len(prompts), int(sigmas.numel()) - 1
     dev = torch.device(device)
     active = frozenset(range(n_steps)) if gradient_steps is None else frozenset(int(i) for i in gradient_steps)
+    window = sum(1 for i in active if 0 <= i < n_steps)
     if initial_latents is None:
         gen_dev = generator.device if generator is not None else dev
         seed = torch.randn((n_prompts, *latent_shape), device=gen_dev, dtype=dtype, generator=generator).to(dev)
@@ -245,7 +291,7 @@ def generate_group(velocity_fn: VelocityFn, *, prompts: Sequence[str], group_siz
                              f"{tuple(initial_latents.shape)}")
         seed = initial_latents.to(device=dev, dtype=dtype)
     state = seed.repeat_interleave(group_size, 0)
-    buffer = RolloutBuffer(group_size=group_size, prompts=tuple(prompts))
+    buffer = RolloutBuffer(group_size=group_size, prompts=tuple(prompts), capacity=window)
     prompt_index = torch.arange(n_prompts, device=dev).repeat_interleave(group_size)
     b = state.shape[0]
     with torch.no_grad():

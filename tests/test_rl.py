@@ -116,7 +116,7 @@ def test_generate_group_shares_seed_noise_per_prompt() -> None:
 
     buf = generate_group(vel, prompts=["p", "q"], group_size=3, sigmas=torch.linspace(1, 0, 4), latent_shape=(2, 3),
                          generator=torch.Generator().manual_seed(0), noise_level=0.5)
-    first = buf._steps[0]["sample_before"]
+    first = buf.transitions("sample_before")[0]
     assert torch.equal(first[0], first[2]) and not torch.equal(first[0], first[3])
 
 

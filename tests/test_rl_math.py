@@ -270,6 +270,39 @@ def test_rollout_buffer_flow() -> None:
         RolloutBuffer(group_size=1)
 
 
+def test_rollout_buffer_arenas_grow_and_keep_every_step() -> None:
+    """Without a capacity hint the arenas double when full; stored rows survive every regrowth
+    and a minibatch row maps back to its (step, sample) pair."""
+    buf = RolloutBuffer(group_size=2)
+    for i in range(5):
+        x = torch.full((4, 2), float(i))
+        step = SDEStep(sample=x + 0.5, log_prob=torch.full((4,), -float(i)), mean=x, std=torch.ones(4))
+        buf.add_step(step_index=10 + i, sample_before=x, step=step, sigma=torch.full((4,), 1.0 - 0.1 * i),
+                     sigma_next=torch.full((4,), 0.9 - 0.1 * i))
+    assert len(buf) == 5 and buf.transitions("sample_before").shape == (5, 4, 2)
+    torch.testing.assert_close(buf.transitions("sample_before")[:, 0, 0], torch.arange(5.0))
+    with pytest.raises(KeyError):
+        buf.transitions("advantage")
+    with pytest.raises(ValueError):  # a step over a different sample count
+        buf.add_step(step_index=0, sample_before=torch.zeros(3, 2),
+                     step=SDEStep(sample=torch.zeros(3, 2), log_prob=torch.zeros(3), mean=torch.zeros(3, 2),
+                                  std=torch.ones(3)), sigma=torch.ones(3), sigma_next=torch.ones(3))
+    buf.set_rewards(torch.tensor([0.0, 1.0, 3.0, 5.0]), media=None)
+    adv = buf.compute_advantages(clip=None)
+    for batch in buf.iter_minibatches(3, generator=torch.Generator().manual_seed(1)):
+        step = batch.step_index - 10
+        torch.testing.assert_close(batch.sample_before[:, 0], step.float())
+        torch.testing.assert_close(batch.log_prob_old, -step.float())
+        torch.testing.assert_close(batch.sigma, 1.0 - 0.1 * step.float())
+        assert set(batch.prompt_index.tolist()) <= {0, 1}
+        assert all(float(a) in adv.tolist() for a in batch.advantage)
+
+
+def test_rollout_buffer_from_empty_has_no_transitions() -> None:
+    with pytest.raises(RuntimeError):
+        RolloutBuffer(group_size=3).transitions("sample_before")
+
+
 @pytest.mark.parametrize("world", [1, 2, 3, 4])
 def test_distribute_prompts_is_a_partition(world: int) -> None:
     prompts = [f"p{i}" for i in range(10)]

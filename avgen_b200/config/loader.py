@@ -248,6 +248,12 @@ def build_dataclass(cls: type, values: Mapping[str, Any], where: str = "") -> An
         raise ConfigError(str(exc)) from exc
 
 
+def build(cls: type, mapping: Mapping[str, Any], *, where: str = "") -> Any:
+    """Construct config dataclass ``cls`` from ``mapping`` (unknown keys and uncoercible values raise
+    :class:`ConfigError` naming the dotted path ``where.field``); keyword form of :func:`build_dataclass`."""
+    return build_dataclass(cls, mapping, where)
+
+
 def _normalise(mapping: dict[str, Any]) -> dict[str, Any]:
     par = mapping.get("parallel")
     if isinstance(par, dict) and isinstance(par.get("pipeline"), dict):

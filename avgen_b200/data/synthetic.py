@@ -201,6 +201,21 @@ class SyntheticSource:
         w = 2 * math.pi * p["frequency"]
         return torch.sin(w * t + p["phase"]) + c.drive_harmonic_gain * torch.sin(2 * w * t + 2 * p["phase"])
 
+    def descriptor(self, index: int) -> SampleDescriptor:
+        """Metadata of sample ``index`` without generating it: every synthetic sample has the
+        configured geometry, so only the id varies. ``index`` must lie in ``[0, num_samples)``."""
+        c = self._config
+        if not 0 <= index < c.num_samples:
+            raise IndexError(f"sample {index} is outside the synthetic corpus of {c.num_samples}")
+        audio = c.has_audio
+        return SampleDescriptor(sample_id=index, frames=c.frames, height=c.height, width=c.width,
+                                channels=c.video_channels, audio_frames=c.audio_frames,
+                                audio_channels=c.audio_channels if audio else 0, text_tokens=c.text_tokens,
+                                text_width=c.text_width, video_timebase_num=c.video_timebase_num,
+                                video_timebase_den=c.video_timebase_den, audio_timebase_num=c.audio_timebase_num,
+                                audio_timebase_den=c.audio_timebase_den, video_codec_id=c.video_codec_id,
+                                audio_codec_id=c.audio_codec_id if audio else "none")
+
     def sample(self, index: int) -> LatentSample:
         """Sample ``index`` (a pure function of the seed and the index)."""
         c = self._config
@@ -227,14 +242,7 @@ class SyntheticSource:
             audio = torch.zeros(c.audio_channels, 0)
         coeff = torch.tensor([p["frequency"], math.sin(p["phase"]), math.cos(p["phase"]), p["vx"], p["vy"], 1.0])
         text = torch.einsum("k,ktd->td", coeff, self._text_proj)
-        desc = SampleDescriptor(sample_id=index, frames=c.frames, height=c.height, width=c.width,
-                                channels=c.video_channels, audio_frames=c.audio_frames,
-                                audio_channels=c.audio_channels if c.has_audio else 0, text_tokens=c.text_tokens,
-                                text_width=c.text_width, video_timebase_num=c.video_timebase_num,
-                                video_timebase_den=c.video_timebase_den, audio_timebase_num=c.audio_timebase_num,
-                                audio_timebase_den=c.audio_timebase_den, video_codec_id=c.video_codec_id,
-                                audio_codec_id=c.audio_codec_id if c.has_audio else "none")
-        return LatentSample(descriptor=desc, video=video.to(c.dtype), audio=audio.to(c.dtype), text=text,
+        return LatentSample(descriptor=self.descriptor(index), video=video.to(c.dtype), audio=audio.to(c.dtype), text=text,
                             text_mask=torch.ones(c.text_tokens, dtype=torch.bool))
 
     def __iter__(self) -> Iterator[MediaBatch]:

@@ -605,3 +605,14 @@ def test_parameter_estimate_matches_the_built_model(ffn: str, cross: bool, width
     built = sum(p.numel() for p in build_model(cfg, meta=True).parameters())
     assert counted_parameters(cfg) == built
     assert cfg.model.estimated_parameters(text_width=96) == built
+
+
+def test_loader_build_keyword_form() -> None:
+    from avgen_b200.config.loader import build
+
+    built = build(S.TrainConfig, {"lr": "2e-4", "steps": 500}, where="train")
+    assert built == build_dataclass(S.TrainConfig, {"lr": 2e-4, "steps": 500})
+    with pytest.raises(ConfigError, match="train"):
+        build(S.TrainConfig, {"learning_rat": 1.0}, where="train")
+    with pytest.raises(ConfigError, match="warmup_steps"):  # the dataclass's own check, as a ConfigError
+        build(S.TrainConfig, {"steps": 50}, where="train")

@@ -422,3 +422,13 @@ def test_build_latent_sample_descriptor() -> None:
     assert d.caption == "a cat" and bool(s.text_mask.all())
     silent = build_latent_sample(8, video_latent=torch.zeros(4, 1, 2, 2), text=torch.zeros(1, 4))
     assert silent.descriptor.audio_frames == 0 and silent.descriptor.audio_channels == 0
+
+
+def test_synthetic_descriptor_matches_generated_sample() -> None:
+    source = SyntheticSource(SyntheticConfig(num_samples=5))
+    for i in (0, 4):
+        assert source.descriptor(i) == source.sample(i).descriptor
+    with pytest.raises(IndexError):
+        source.descriptor(5)
+    with pytest.raises(IndexError):
+        source.descriptor(-1)

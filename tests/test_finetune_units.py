@@ -186,3 +186,22 @@ def test_freeze_helpers() -> None:
     s = freeze_matching(model, ["norm.*", "other.*"])
     assert s.frozen == 2 * 8 + 8 * 8 + 8 and s.total == total
     assert trainable_summary(model).optimizer_state_bytes == 12 * s.trainable
+
+
+def test_stage_overrides_copy_and_plain_description() -> None:
+    import json
+
+    from avgen_b200.finetune.stages import get_stage, list_stages
+
+    for name in list_stages():
+        stage = get_stage(name)
+        described = stage.to_dict()
+        json.dumps(described)  # JSON-safe all the way down
+        assert described["name"] == name and abs(sum(described["conditioning_mix"].values()) - 1.0) < 1e-9
+        assert described["uses_adapter"] == stage.uses_adapter
+    base = get_stage(list_stages()[0])
+    changed = base.with_overrides(learning_rate=3e-6, notes="borrowed")
+    assert changed.learning_rate == 3e-6 and changed.notes == "borrowed"
+    assert base.learning_rate != 3e-6 and get_stage(base.name) == base  # the registered recipe is untouched
+    with pytest.raises(ValueError):
+        base.with_overrides(learning_rate=0.0)  # validation runs on the copy

@@ -29,6 +29,9 @@ __all__ = ["DEFAULT_INIT_TIMEOUT", "DEFAULT_TIMEOUT", "DistributedEnv", "barrier
 
 DEFAULT_TIMEOUT = timedelta(minutes=10)
 DEFAULT_INIT_TIMEOUT = timedelta(minutes=30)
+# the steady-state collective timeout the default group was created with; a
+# temporary bound (collective_timeout) is undone back to this value
+_group_timeout: timedelta = DEFAULT_TIMEOUT
 
 # NCCL debugging aids on by default (a user's own environment wins): keep the last
 # collectives of every communicator, dump them when a collective times out, and
@@ -131,6 +134,8 @@ def init_distributed(*, backend: str | None = None, timeout: timedelta = DEFAULT
         os.environ["TORCH_DISTRIBUTED_STORE_TIMEOUT"] = str(int(init_timeout.total_seconds()))
         dist.init_process_group(backend=chosen, rank=launch.rank, world_size=launch.world_size, timeout=timeout,
                                 device_id=device if device.type == "cuda" else None)
+        global _group_timeout
+        _group_timeout = timeout
     return DistributedEnv(rank=launch.rank, local_rank=launch.local_rank, world_size=launch.world_size,
                           local_world_size=launch.local_world_size, backend=chosen, device=device)
 
@@ -168,7 +173,8 @@ def unwrap_model(model: nn.Module) -> nn.Module:
 @contextmanager
 def collective_timeout(seconds: float) -> Iterator[None]:
     """Run the enclosed block with the default group's collective timeout set to
-    ``seconds`` (restored to :data:`DEFAULT_TIMEOUT` afterwards)."""
+    ``seconds``; afterwards the timeout the group was created with (the
+    ``timeout`` given to :func:`init_distributed`) applies again."""
     if not (dist.is_available() and dist.is_initialized()):
         yield
         return
@@ -178,4 +184,4 @@ def collective_timeout(seconds: float) -> Iterator[None]:
     try:
         yield
     finally:
-        c10d._set_pg_timeout(DEFAULT_TIMEOUT, default)
+        c10d._set_pg_timeout(_group_timeout, default)

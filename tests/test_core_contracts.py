@@ -187,3 +187,22 @@ def test_rng_fork_seed_for_and_validation() -> None:
             RNGStreams.from_seed(bad)  # type: ignore[arg-type]
     with pytest.raises(ValueError):
         RNGStreams.for_rank(0, data_rank=-1)
+
+
+def test_collective_timeout_restores_the_groups_own_timeout(monkeypatch: pytest.MonkeyPatch) -> None:
+    """A temporary bound is undone to the timeout the group was created with, not to the library default."""
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from avgen_b200.parallel import env
+
+    calls: list[timedelta] = []
+    c10d = dist.distributed_c10d
+    monkeypatch.setattr(dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(c10d, "_get_default_group", lambda: "group")
+    monkeypatch.setattr(c10d, "_set_pg_timeout", lambda t, g: calls.append(t))
+    monkeypatch.setattr(env, "_group_timeout", timedelta(seconds=77))
+    with env.collective_timeout(5):
+        assert calls == [timedelta(seconds=5)]
+    assert calls[-1] == timedelta(seconds=77)
